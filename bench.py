@@ -1,0 +1,491 @@
+#!/usr/bin/env python
+"""Benchmark of the jero-kernels-rvv quantized-matmul hot path on B200 (sm_100a).
+
+Default workload: the Llama-3-8B decode GEMV set at batch 1 --
+Q4_K_M q/o 4096->4096, k/v 4096->1024, gate/up 4096->14336, down 14336->4096 and the Q6_K
+lm_head 4096->128256, each fed by its own Q8_K-quantized activation. One step quantizes the
+five activation vectors and runs the eight GEMVs through the C ABI (jkb200). Weights are
+synthetic N(0, 0.02) rows quantized by this file's numpy quantizers (a seeded pool of rows
+tiled to full size; GEMV time does not depend on the values), activations N(0, 1).
+
+Metric: algorithmic bytes per step (GGUF weight blocks + Q8_K activation blocks + f32 outputs,
+the BASELINE.md table) / step time, in GB/s. The seven layer matrices exist in two copies used
+on alternate steps and the lm_head is 431 MB, so every step streams 554 MB (> 4x the 126 MB L2).
+
+With --gpus N (torchrun, one rank per GPU) every matrix is sharded by output rows; each rank
+runs its slices and one NCCL all-gather per step collects the output slices on every rank
+(strong scaling: the same total work at every N).
+
+`--impl reference` times the CPU restatement of the reference's scalar path (oracle/) on all
+host cores over the same workload (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "jero-kernels-rvv_b200"))
+
+Q4_K, Q6_K, Q8_0 = 12, 14, 8
+BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), Q8_0: (32, 34)}
+
+# (name, quant, rows, cols, activation stream)
+DECODE_8B = [
+    ("attn_q", Q4_K, 4096, 4096, "x"), ("attn_k", Q4_K, 1024, 4096, "x"),
+    ("attn_v", Q4_K, 1024, 4096, "x"), ("attn_o", Q4_K, 4096, 4096, "attn"),
+    ("ffn_gate", Q4_K, 14336, 4096, "h"), ("ffn_up", Q4_K, 14336, 4096, "h"),
+    ("ffn_down", Q4_K, 4096, 14336, "a"), ("lm_head", Q6_K, 128256, 4096, "f"),
+]
+ACTS = {"x": 4096, "attn": 4096, "h": 4096, "a": 14336, "f": 4096}
+LAYER_COPIES = 2
+POOL_ROWS = 512
+
+
+# ----------------------------------------------------------------------------- synthetic data
+
+def _f16(x):
+    return np.asarray(x, np.float32).astype(np.float16)
+
+
+def _rnd(x):
+    """Round half away from zero (C roundf / Rust f32::round), evaluated exactly in f64."""
+    x = np.asarray(x, np.float64)
+    return np.sign(x) * np.floor(np.abs(x) + 0.5)
+
+
+def quantize_q4_k(w: np.ndarray) -> np.ndarray:
+    """Q4_K blocks from f32 rows: per 32-element sub-block an affine (scale, min) pair
+    re-quantized to 6 bits against f16 super-block d / dmin (same rule as the oracle's own
+    quantizer, written with numpy)."""
+    R, K = w.shape
+    x = w.reshape(R, K // 256, 8, 32)
+    lo = np.minimum(x.min(-1), 0.0)
+    hi = x.max(-1)
+    scale = (hi - lo) / np.float32(15.0)
+    minv = -lo
+    d = _f16(scale.max(-1) / np.float32(63.0)).astype(np.float32)
+    dmin = _f16(minv.max(-1) / np.float32(63.0)).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        sc = np.where(d[..., None] > 0, _rnd(scale / d[..., None]), 0).clip(0, 63).astype(np.uint8)
+        m = np.where(dmin[..., None] > 0, _rnd(minv / dmin[..., None]), 0).clip(0, 63).astype(np.uint8)
+        ds = d[..., None] * sc.astype(np.float32)
+        dm = dmin[..., None] * m.astype(np.float32)
+        q = np.where(ds[..., None] > 0, _rnd((x + dm[..., None]) / ds[..., None]), 0)
+    q = q.clip(0, 15).astype(np.uint8).reshape(R, K // 256, 4, 2, 32)
+    out = np.zeros((R, K // 256, 144), np.uint8)
+    out[..., 0:2] = _f16(d).view(np.uint8).reshape(R, K // 256, 2)
+    out[..., 2:4] = _f16(dmin).view(np.uint8).reshape(R, K // 256, 2)
+    s = out[..., 4:16]
+    s[..., 0:4] = (sc[..., 0:4] & 63) | ((sc[..., 4:8] >> 4) << 6)
+    s[..., 4:8] = (m[..., 0:4] & 63) | ((m[..., 4:8] >> 4) << 6)
+    s[..., 8:12] = (sc[..., 4:8] & 15) | ((m[..., 4:8] & 15) << 4)
+    out[..., 16:] = (q[..., 0, :] | (q[..., 1, :] << 4)).reshape(R, K // 256, 128)
+    return out.reshape(-1)
+
+
+def quantize_q6_k(w: np.ndarray) -> np.ndarray:
+    """Q6_K blocks from f32 rows: 16-element sub-block scales absmax/31 as i8 against an f16
+    super-block d, values q+32 packed into ql/qh."""
+    R, K = w.shape
+    x = w.reshape(R, K // 256, 16, 16)
+    s = np.abs(x).max(-1) / np.float32(31.0)
+    d = _f16(s.max(-1) / np.float32(127.0)).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        sc = np.where(d[..., None] > 0, _rnd(s / d[..., None]), 0).clip(-128, 127).astype(np.int8)
+        ds = d[..., None] * sc.astype(np.float32)
+        q = np.where(ds[..., None] != 0, _rnd(x / ds[..., None]), 0)
+    u = (q.clip(-32, 31) + 32).astype(np.uint8).reshape(R, K // 256, 2, 4, 32)
+    out = np.zeros((R, K // 256, 210), np.uint8)
+    for h in range(2):
+        ql = out[..., 64 * h:64 * h + 64]
+        ql[..., 0:32] = (u[..., h, 0, :] & 15) | ((u[..., h, 2, :] & 15) << 4)
+        ql[..., 32:64] = (u[..., h, 1, :] & 15) | ((u[..., h, 3, :] & 15) << 4)
+        out[..., 128 + 32 * h:160 + 32 * h] = ((u[..., h, 0, :] >> 4) | ((u[..., h, 1, :] >> 4) << 2)
+                                               | ((u[..., h, 2, :] >> 4) << 4)
+                                               | ((u[..., h, 3, :] >> 4) << 6))
+    out[..., 192:208] = sc.view(np.uint8)
+    out[..., 208:210] = _f16(d).view(np.uint8).reshape(R, K // 256, 2)
+    return out.reshape(-1)
+
+
+def quantize_q8_0(w: np.ndarray) -> np.ndarray:
+    R, K = w.shape
+    x = w.reshape(R, K // 32, 32)
+    d = np.abs(x).max(-1) / np.float32(127.0)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        inv = np.where(d > 0, np.float32(1.0) / d, np.float32(0.0)).astype(np.float32)
+        q = _rnd(x * inv[..., None]).clip(-127, 127).astype(np.int8)
+    out = np.zeros((R, K // 32, 34), np.uint8)
+    out[..., 0:2] = _f16(d).view(np.uint8).reshape(R, K // 32, 2)
+    out[..., 2:] = q.view(np.uint8)
+    return out.reshape(-1)
+
+
+QUANTIZERS = {Q4_K: quantize_q4_k, Q6_K: quantize_q6_k, Q8_0: quantize_q8_0}
+
+
+def synth_matrix(quant, rows, cols, seed, row_begin=0, row_end=None):
+    """GGUF bytes of rows [row_begin, row_end) of a seeded N(0, 0.02) matrix: a pool of
+    POOL_ROWS quantized rows tiled over the matrix."""
+    row_end = rows if row_end is None else row_end
+    rng = np.random.default_rng(seed)
+    pool = rng.standard_normal((min(POOL_ROWS, rows), cols), dtype=np.float32) * np.float32(0.02)
+    qp = QUANTIZERS[quant](pool).reshape(pool.shape[0], -1)
+    idx = np.arange(row_begin, row_end) % pool.shape[0]
+    return np.ascontiguousarray(qp[idx]).reshape(-1)
+
+
+def algorithmic_bytes(quant, rows, cols):
+    be, bb = BLOCK[quant]
+    act = cols // 256 * 292 if quant in (Q4_K, Q6_K) else cols // 32 * 36
+    return rows * (cols // be) * bb + act + 4 * rows
+
+
+# ----------------------------------------------------------------------------- helpers
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(kernel_key):
+    """dram bytes per launch recorded from an ncu capture in profiles/<kernel_key>.txt
+    ("traffic_bytes_per_launch: N" line), or None."""
+    p = os.path.join(ROOT, "profiles", f"{kernel_key}.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+def cpu_oracle_step(O, mats, xq, nthreads):
+    for name, quant, rows, cols, stream, w in mats:
+        O.gemv_mt(quant, w, rows, cols, xq[stream], nthreads)
+
+
+def cpu_workload(O, frac_rows=1.0):
+    """The decode workload restricted to the first frac of each matrix's rows (CPU arms)."""
+    mats = []
+    for i, (name, quant, rows, cols, stream) in enumerate(DECODE_8B):
+        r = max(4, int(rows * frac_rows) // 4 * 4)
+        mats.append((name, quant, r, cols, stream, synth_matrix(quant, rows, cols, 1000 + i, 0, r)))
+    rng = np.random.default_rng(7)
+    xq = {s: O.quantize_row_q8_k(rng.standard_normal(n, dtype=np.float32)) for s, n in ACTS.items()}
+    nbytes = sum(algorithmic_bytes(q, r, c) for _, q, r, c, _, _ in mats)
+    return mats, xq, nbytes
+
+
+def run_reference(args):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as O
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    frac = 0.125
+    mats, xq, nbytes = cpu_workload(O, frac)
+    for _ in range(args.warmup):
+        cpu_oracle_step(O, mats, xq, cores)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_oracle_step(O, mats, xq, cores)
+    dt = (time.perf_counter() - t0) / args.steps
+    gbs = nbytes / dt / 1e9
+    sample = (f"each step: rows [0, {frac:g} * N) of every GEMV of the decode set "
+              f"({nbytes / 1e6:.1f} MB), oracle scalar port, row-range split over {cores} threads")
+    print(json.dumps({
+        "impl": "reference", "metric": "quant GEMV weight GB/s", "value": round(gbs, 3),
+        "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8 dot / f32 scale", "data": "synthetic",
+        "config": {"workload": "llama3-8b-decode-gemv-set (sampled rows)", "batch": 1},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def cpu_baseline_single():
+    """Oracle port on one host core over a bounded sample of the decode workload, repeated for
+    about 10 s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as O
+
+    frac = 1 / 16
+    mats, xq, nbytes = cpu_workload(O, frac)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        cpu_oracle_step(O, mats, xq, 1)
+        n += 1
+        if time.perf_counter() - t0 > 10.0:
+            break
+    dt = (time.perf_counter() - t0) / n
+    return {"value": round(nbytes / dt / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{n} passes over rows [0, N/16) of each decode GEMV "
+                      f"({nbytes / 1e6:.1f} MB per pass), single thread"}
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    import jkb200 as jkb
+
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    # --- weights: this rank's row shard of every matrix (layer matrices in two copies)
+    shards, weights, total_bytes = [], {}, 0
+    for i, (name, quant, rows, cols, s) in enumerate(DECODE_8B):
+        per = rows // world
+        r0, r1 = rank * per, (rank + 1) * per
+        total_bytes += algorithmic_bytes(quant, rows, cols)
+        copies = 1 if name == "lm_head" else LAYER_COPIES
+        for c in range(copies):
+            raw = synth_matrix(quant, rows, cols, 1000 + i + 97 * c, r0, r1)
+            weights[(name, c)] = jkb.Weight(jkb.TensorView(f"{name}.{c}", quant, [per, cols], raw),
+                                            per, cols)
+        shards.append((name, quant, per, cols, s, copies))
+    g = torch.Generator(device="cpu").manual_seed(7)
+    xs = {s: torch.randn(n, generator=g).cuda() for s, n in ACTS.items()}
+    xq = {s: jkb.empty_q8_k_blocks(n // 256) for s, n in ACTS.items()}
+    out_len = sum(per for _, _, per, _, _, _ in shards)
+    out = torch.empty(out_len, dtype=torch.float32, device="cuda")
+    gathered = torch.empty(out_len * world, dtype=torch.float32, device="cuda") if world > 1 else None
+    offs, o = {}, 0
+    for name, _, per, _, _, _ in shards:
+        offs[name] = (o, o + per)
+        o += per
+    fns = {Q4_K: jkb.gemv_q4_k_q8_k, Q6_K: jkb.gemv_q6_k_q8_k}
+
+    def layer_part(copy):
+        for s in ACTS:
+            jkb.quantize_row_q8_k(xs[s], xq[s])
+        for name, quant, per, cols, s, copies in shards:
+            if name == "lm_head":
+                continue
+            a, b = offs[name]
+            fns[quant](out[a:b], weights[(name, copy)], xq[s])
+
+    def lm_head():
+        a, b = offs["lm_head"]
+        fns[Q6_K](out[a:b], weights[("lm_head", 0)], xq["f"])
+
+    # warm once eagerly (sets kernel attributes), then capture the layer part per copy
+    layer_part(0)
+    lm_head()
+    torch.cuda.synchronize()
+    graphs = []
+    for c in range(LAYER_COPIES):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            layer_part(c)
+        graphs.append(gr)
+    n_ev = args.steps
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+
+    def step(i, timed):
+        graphs[i % LAYER_COPIES].replay()
+        if timed:
+            ev_a[i].record(stream)
+        lm_head()
+        if timed:
+            ev_b[i].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+
+    for i in range(args.warmup):
+        step(i, False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        step(i, True)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = t_start.elapsed_time(t_end)
+    lm_ms = sum(a.elapsed_time(b) for a, b in zip(ev_a, ev_b)) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = total_bytes / (ms_step * 1e-3) / 1e9
+
+    # --- e2e: the public API with host buffers (pinned f32 inputs in, f32 outputs out)
+    host_in = {s: xs[s].cpu().pin_memory() for s in ACTS}
+    host_out = torch.empty(out_len, dtype=torch.float32).pin_memory()
+    h2d = sum(v.numel() * 4 for v in host_in.values())
+    d2h = out_len * 4
+
+    def e2e_step(i):
+        for s in ACTS:
+            xs[s].copy_(host_in[s], non_blocking=True)
+        for s in ACTS:
+            jkb.quantize_row_q8_k(xs[s], xq[s])
+        for name, quant, per, cols, s, copies in shards:
+            a, b = offs[name]
+            fns[quant](out[a:b], weights[(name, i % copies)], xq[s])
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+        host_out.copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        lm_q, lm_rows, lm_cols = Q6_K, DECODE_8B[-1][2], DECODE_8B[-1][3]
+        lm_bytes = algorithmic_bytes(lm_q, lm_rows, lm_cols) / world
+        achieved = lm_bytes / (lm_ms * 1e-3) / 1e9
+        traffic = profile_traffic("gemv_q6_k_lm_head_4096x128256")
+        res = {
+            "metric": "quant GEMV weight GB/s", "value": round(value, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8 dot / f32 scale", "data": "synthetic",
+            "config": {"workload": "llama3-8b-decode-gemv-set (BASELINE configs[1])",
+                       "batch": 1, "weights": "Q4_K_M layers + Q6_K lm_head",
+                       "bytes_per_step": total_bytes,
+                       "l2": "inputs larger than L2 (554 MB per step, layer weights in 2 "
+                             "alternating copies)",
+                       "parallelism": f"row-shard x{world}" + (" + NCCL all-gather" if world > 1 else "")},
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<FQ6_K> lm_head 4096->128256",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "traffic": traffic, "algorithmic_bytes": lm_bytes,
+                         "avg_ms": round(lm_ms, 5)},
+            "gpu_launches": args.steps * (len(ACTS) + len(DECODE_8B)),
+            "clocks": clocks,
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline_single()
+        print(json.dumps(res), flush=True)
+    for gr in graphs:
+        del gr
+    graphs.clear()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="jkb", choices=["jkb", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

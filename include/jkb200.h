@@ -1,0 +1,286 @@
+/*
+ * jkb200.h -- C ABI of the B200 (sm_100a) quantized-matmul hot path of jero-kernels-rvv.
+ *
+ * Every entry point below replaces one public Rust function of the jero-kernels-rvv crate
+ * (path:line inside that crate is cited beside it) and keeps its argument meaning, validation
+ * order and error kinds. The differences are the ones a GPU boundary forces:
+ *   - slices become (pointer, element count) pairs; activation, output and scratch pointers are
+ *     device pointers unless a comment says otherwise;
+ *   - `&TensorView` weights become a `jkb_weight*` handle, created once at load time (validate,
+ *     upload, relayout), the analogue of RepackedWeight::from_tensor (repack.rs:2288);
+ *   - `Result<_, K3Error>` becomes an int status (jkb_status) plus a thread-local error record
+ *     with the K3Error::TensorBoundsError fields (tensor_name, offset, byte_len, buffer_len,
+ *     reason);
+ *   - every call takes a CUDA stream (`void*` holding a cudaStream_t, NULL = legacy default
+ *     stream) and is asynchronous on it; nothing is launched when validation fails, and no call
+ *     allocates device memory (all buffers live in handles created at load time).
+ *
+ * All structs are plain C, little-endian, with the same layout as the reference #[repr(C)]
+ * block structs.
+ */
+#ifndef JKB200_H
+#define JKB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; everything declared here is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define JKB_ABI_VERSION 1
+
+/* ---- status codes: K3Error variants plus device-side failures ---- */
+typedef enum {
+    JKB_OK = 0,
+    JKB_E_BOUNDS = 1,     /* K3Error::TensorBoundsError */
+    JKB_E_CAPABILITY = 2, /* K3Error::CapabilityMismatch (unsupported_tensor_quant) */
+    JKB_E_CUDA = 3,       /* CUDA runtime / launch failure */
+    JKB_E_NCCL = 4,       /* collective failure (sharded calls) */
+    JKB_E_TIMEOUT = 5,    /* a bounded wait expired (sharded calls) */
+    JKB_E_INVALID = 6     /* null pointer or destroyed handle */
+} jkb_status;
+
+/* QuantType codes (GGML type ids; I2_S is BitNet.cpp's 36). Q4_K_M is the crate's name for
+ * GGML Q4_K (lib.rs:129-132). */
+typedef enum {
+    JKB_F32 = 0,
+    JKB_F16 = 1,
+    JKB_Q4_0 = 2,
+    JKB_Q8_0 = 8,
+    JKB_Q4_K_M = 12,
+    JKB_Q6_K = 14,
+    JKB_BF16 = 30,
+    JKB_TQ1_0 = 34,
+    JKB_TQ2_0 = 35,
+    JKB_I2_S = 36
+} jkb_quant;
+
+/* BlockQ8_0 (quant_q8.rs:37-44): 36 bytes. */
+typedef struct {
+    float d;
+    int8_t qs[32];
+} jkb_block_q8_0;
+
+/* BlockQ8K (quant_q8.rs:62-71): 292 bytes. */
+typedef struct {
+    float d;
+    int8_t qs[256];
+    int16_t bsums[16];
+} jkb_block_q8_k;
+
+/* jero_core::TensorView: name, quant, shape ([rows, cols], GGUF [cols, rows] or 1-D), offset
+ * of the tensor in its file (reported in errors only), and the raw GGUF block bytes. `data`
+ * may be host or device memory (data_on_device). */
+typedef struct {
+    const char *name;
+    int32_t quant;
+    uint32_t ndim;
+    size_t shape[4];
+    size_t offset;
+    const void *data;
+    size_t byte_len;
+    int32_t data_on_device;
+} jkb_tensor_view;
+
+/* K3Error::TensorBoundsError fields of the last failure on this thread. */
+typedef struct {
+    int32_t status;
+    char tensor_name[64];
+    size_t offset;
+    size_t byte_len;
+    size_t buffer_len;
+    char reason[256];
+} jkb_error_info;
+
+typedef struct jkb_weight jkb_weight;                   /* GEMV / BitLinear weight */
+typedef struct jkb_repacked_weight jkb_repacked_weight; /* RepackedWeight (GEMM)    */
+typedef struct jkb_act_q8 jkb_act_q8;                   /* QuantizedActQ8           */
+
+/* ---- library / errors ---- */
+int jkb_abi_version(void);
+const char *jkb_last_error(void);
+int jkb_last_error_info(jkb_error_info *out);
+void jkb_clear_error(void);
+
+/* ---- activation quantizers ---- */
+/* quant_q8.rs:395 quantize_row_q8_0 (alias of quantize_row_q8_0_f32, :370). */
+int jkb_quantize_row_q8_0(const float *x, size_t x_len, jkb_block_q8_0 *out, size_t out_len,
+                          void *stream);
+/* quant_q8.rs:370 quantize_row_q8_0_f32 */
+int jkb_quantize_row_q8_0_f32(const float *x, size_t x_len, jkb_block_q8_0 *out, size_t out_len,
+                              void *stream);
+/* quant_q8.rs:576 quantize_row_q8_k */
+int jkb_quantize_row_q8_k(const float *x, size_t x_len, jkb_block_q8_k *out, size_t out_len,
+                          void *stream);
+/* M rows of quantize_row_q8_0 / _q8_k in one launch (x is [m][k], out is [m][k/32] or
+ * [m][k/256]); each row is exactly one reference call. */
+int jkb_quantize_rows_q8_0(const float *x, size_t m, size_t k, jkb_block_q8_0 *out,
+                           size_t out_len, void *stream);
+int jkb_quantize_rows_q8_k(const float *x, size_t m, size_t k, jkb_block_q8_k *out,
+                           size_t out_len, void *stream);
+/* lib.rs:1042 subln_quantize_absmax_i8; the returned scale is written to *scale_out (device). */
+int jkb_subln_quantize_absmax_i8(int8_t *out_i8, size_t out_len, const float *input,
+                                 size_t in_len, const float *norm_weight, size_t w_len, float eps,
+                                 float *scale_out, void *stream);
+/* M independent rows of subln_quantize_absmax_i8 (input [m][len], out [m][len], scales [m]). */
+int jkb_subln_quantize_absmax_i8_rows(int8_t *out_i8, const float *input,
+                                      const float *norm_weight, size_t m, size_t len, float eps,
+                                      float *scales_out, void *stream);
+
+/* ---- QuantizedActQ8 (repack.rs:461-724) ---- */
+/* Allocates device buffers for up to m_capacity rows of k elements (load time). */
+int jkb_act_q8_create(size_t m_capacity, size_t k, jkb_act_q8 **out);
+int jkb_act_q8_destroy(jkb_act_q8 *act);
+/* repack.rs:522 QuantizedActQ8::quantize / :542 quantize_into: act is [m][k] f32 (device). */
+int jkb_act_q8_quantize(jkb_act_q8 *act, const float *input, size_t in_len, size_t m, size_t k,
+                        void *stream);
+/* Device views of the quantized batch (row-major): q [m][k_pad] i8, x_scales and x_sums
+ * [m][k_pad/32], x_sums_16 [m][k_pad/16], super_scales [m][ceil(k/256)]. Any out-pointer may
+ * be NULL. */
+int jkb_act_q8_buffers(const jkb_act_q8 *act, size_t *m, size_t *k, size_t *k_padded,
+                       int8_t **q, float **x_scales, float **x_sums, float **x_sums_16,
+                       float **super_scales);
+
+/* ---- weights (GEMV / BitLinear layout) ---- */
+/* Validates the view like the reference validators, uploads and relayouts into the GPU layout
+ * for an explicit [rows, cols] interpretation (RepackedWeight::from_tensor, repack.rs:2288). */
+int jkb_weight_upload(const jkb_tensor_view *view, size_t rows, size_t cols, void *stream,
+                      jkb_weight **out);
+/* Infers (rows, cols) from a 2-D shape the way RepackedWeight::repack does (repack.rs:2255). */
+int jkb_weight_upload_infer(const jkb_tensor_view *view, void *stream, jkb_weight **out);
+int jkb_weight_destroy(jkb_weight *w);
+int jkb_weight_info(const jkb_weight *w, size_t *rows, size_t *cols, int32_t *quant,
+                    size_t *device_bytes, size_t *gguf_bytes);
+
+/* ---- direct-integer single-row block dots (raw GGUF row bytes on the device) ---- */
+/* quant_q8.rs:1463 vec_dot_q4_0_q8_0 -> *result (device f32) */
+int jkb_vec_dot_q4_0_q8_0(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_0 *x,
+                          size_t x_len, float *result, void *stream);
+/* quant_q8.rs:1493 vec_dot_q8_0_q8_0 */
+int jkb_vec_dot_q8_0_q8_0(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_0 *x,
+                          size_t x_len, float *result, void *stream);
+/* quant_q8.rs:3019 vec_dot_q4_k_q8_k */
+int jkb_vec_dot_q4_k_q8_k(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_k *x,
+                          size_t x_len, float *result, void *stream);
+/* quant_q8.rs:3056 vec_dot_q6_k_q8_k */
+int jkb_vec_dot_q6_k_q8_k(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_k *x,
+                          size_t x_len, float *result, void *stream);
+/* quant_q8.rs:3071 vec_dot_tq1_0_q8_k */
+int jkb_vec_dot_tq1_0_q8_k(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_k *x,
+                           size_t x_len, float *result, void *stream);
+/* quant_q8.rs:3086 vec_dot_tq2_0_q8_k */
+int jkb_vec_dot_tq2_0_q8_k(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_k *x,
+                           size_t x_len, float *result, void *stream);
+
+/* ---- M = 1 decode GEMV over pre-quantized activations (output fully overwritten) ---- */
+/* quant_q8.rs:1586 gemv_q4_0_q8_0 (and :1612 gemv_q4_0_q8_0_4x) */
+int jkb_gemv_q4_0_q8_0(float *out, size_t out_len, const jkb_weight *w, const jkb_block_q8_0 *x,
+                       size_t x_len, void *stream);
+int jkb_gemv_q4_0_q8_0_4x(float *out, size_t out_len, const jkb_weight *w,
+                          const jkb_block_q8_0 *x, size_t x_len, void *stream);
+/* quant_q8.rs:1670 gemv_q8_0_q8_0 (and :1696 gemv_q8_0_q8_0_4x) */
+int jkb_gemv_q8_0_q8_0(float *out, size_t out_len, const jkb_weight *w, const jkb_block_q8_0 *x,
+                       size_t x_len, void *stream);
+int jkb_gemv_q8_0_q8_0_4x(float *out, size_t out_len, const jkb_weight *w,
+                          const jkb_block_q8_0 *x, size_t x_len, void *stream);
+/* quant_q8.rs:3101 gemv_q4_k_q8_k */
+int jkb_gemv_q4_k_q8_k(float *out, size_t out_len, const jkb_weight *w, const jkb_block_q8_k *x,
+                       size_t x_len, void *stream);
+/* quant_q8.rs:3189 gemv_q6_k_q8_k */
+int jkb_gemv_q6_k_q8_k(float *out, size_t out_len, const jkb_weight *w, const jkb_block_q8_k *x,
+                       size_t x_len, void *stream);
+/* quant_q8.rs:3221 gemv_tq1_0_q8_k */
+int jkb_gemv_tq1_0_q8_k(float *out, size_t out_len, const jkb_weight *w,
+                        const jkb_block_q8_k *x, size_t x_len, void *stream);
+/* quant_q8.rs:3250 gemv_tq2_0_q8_k */
+int jkb_gemv_tq2_0_q8_k(float *out, size_t out_len, const jkb_weight *w,
+                        const jkb_block_q8_k *x, size_t x_len, void *stream);
+/* Row-sliced form of the gemv_* calls above (the analogue of gemv_repacked_rows,
+ * repack.rs:4014): writes out[0 .. row_end - row_begin] for weight rows [row_begin, row_end).
+ * x points at BlockQ8_0 (Q4_0, Q8_0 weights) or BlockQ8K (Q4_K_M, Q6_K, TQ1_0, TQ2_0). */
+int jkb_gemv_rows(float *out, size_t out_len, const jkb_weight *w, const void *x, size_t x_len,
+                  size_t row_begin, size_t row_end, void *stream);
+/* Diagnostic with no reference counterpart: the per-(row, block) integer sums (sumi and, for
+ * Q4_K_M, summins) and the f32 block values the GEMV kernels form before summing a row.
+ * Arrays are [rows][blocks_per_row]; summins may be NULL. */
+int jkb_gemv_block_dots(const jkb_weight *w, const void *x, size_t x_len, int32_t *sumi,
+                        int32_t *summins, float *block_values, void *stream);
+
+/* ---- f32-activation VectorKernel entries (dequantize -> f32 dot, lib.rs:135-199) ---- */
+/* lib.rs:157 VectorKernel::vec_dot_q4_k_m (host path vec_dot_q4_k_m_scalar lib.rs:1268) */
+int jkb_vec_dot_q4_k_m(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                       size_t in_len, void *stream);
+/* quant.rs:1069 vec_dot_q8_0 (scalar :899) */
+int jkb_vec_dot_q8_0(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                     size_t in_len, void *stream);
+/* quant.rs:1089 vec_dot_q6_k (scalar :1012) */
+int jkb_vec_dot_q6_k(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                     size_t in_len, void *stream);
+/* quant.rs:1458 vec_dot_q4_0 (scalar :1401) */
+int jkb_vec_dot_q4_0(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                     size_t in_len, void *stream);
+/* quant.rs:2199 vec_dot_i2_s */
+int jkb_vec_dot_i2_s(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                     size_t in_len, void *stream);
+
+/* ---- ternary BitLinear (ime.rs) ---- */
+/* ime.rs:882 bitlinear_i8_rvv / :1005 bitlinear_i8_ime (bit-identical pair): TQ1_0, TQ2_0,
+ * Q8_0 or I2_S weights, i8 activation (device) and its per-tensor scale. */
+int jkb_bitlinear_i8(float *out, size_t out_len, const jkb_weight *w, const int8_t *act_i8,
+                     size_t act_len, float act_scale, void *stream);
+int jkb_bitlinear_i8_rvv(float *out, size_t out_len, const jkb_weight *w, const int8_t *act_i8,
+                         size_t act_len, float act_scale, void *stream);
+int jkb_bitlinear_i8_ime(float *out, size_t out_len, const jkb_weight *w, const int8_t *act_i8,
+                         size_t act_len, float act_scale, void *stream);
+/* M tokens of bitlinear_i8 in one launch: act [m][cols] i8, act_scales [m] f32 (device),
+ * out [m][rows]; each token is exactly one reference call. */
+int jkb_bitlinear_i8_batch(float *out, size_t out_len, const jkb_weight *w, const int8_t *act_i8,
+                           size_t act_len, const float *act_scales, size_t m, void *stream);
+
+/* ---- RepackedWeight + GEMM (repack.rs) ---- */
+/* repack.rs:2288 RepackedWeight::from_tensor (explicit [rows, cols]) */
+int jkb_repacked_weight_from_tensor(const jkb_tensor_view *view, size_t rows, size_t cols,
+                                    void *stream, jkb_repacked_weight **out);
+/* repack.rs:2255 RepackedWeight::repack (orientation inferred) */
+int jkb_repacked_weight_repack(const jkb_tensor_view *view, void *stream,
+                               jkb_repacked_weight **out);
+int jkb_repacked_weight_destroy(jkb_repacked_weight *w);
+/* Device views: q [rows][k_pad] i8, scales and mins [rows][scale_groups] f32 (mins NULL
+ * unless Q4_K_M). */
+int jkb_repacked_weight_buffers(const jkb_repacked_weight *w, size_t *rows, size_t *cols,
+                                int32_t *quant, size_t *scale_groups, int8_t **q,
+                                float **scales, float **mins);
+/* repack.rs:4073 gemm_repacked: out [act.m][rows] */
+int jkb_gemm_repacked(float *out, size_t out_len, const jkb_repacked_weight *w,
+                      const jkb_act_q8 *act, void *stream);
+/* repack.rs:4087 gemm_repacked_rows: out [act.m][row_end - row_begin] */
+int jkb_gemm_repacked_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
+                           const jkb_act_q8 *act, size_t row_begin, size_t row_end,
+                           void *stream);
+/* repack.rs:3999 gemv_repacked (act.m must be 1) */
+int jkb_gemv_repacked(float *out, size_t out_len, const jkb_repacked_weight *w,
+                      const jkb_act_q8 *act, void *stream);
+/* repack.rs:4014 gemv_repacked_rows */
+int jkb_gemv_repacked_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
+                           const jkb_act_q8 *act, size_t row_begin, size_t row_end,
+                           void *stream);
+/* repack.rs:4129 gemm_repacked_f32: quantizes input [m][cols] into the caller's act handle
+ * (the reference allocates a QuantizedActQ8 here; this ABI never allocates), then GEMMs. */
+int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight *w,
+                          const float *input, size_t in_len, size_t m, jkb_act_q8 *scratch,
+                          void *stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* JKB200_H */

@@ -1,0 +1,190 @@
+// Repacked block-scaled GEMM (repack.rs:2718-3093) over jkb_repacked_weight (i8 [rows][k_pad]
+// plus per-group f32 scales / mins) and jkb_act_q8 (i8 [m][k_pad] plus per-32 scales / sums).
+//
+// Semantics per output (m, n), bit-exact with accumulate_scaled_tile_scalar
+// (repack.rs:3045-3093): acc = 0.0; for each scale group g in K order:
+//     c = sum_{k in g} xq[m][k] * wq[n][k]            (exact i32)
+//     acc += (f32)c * (xs[m][b] * ws[n][g])  [- xsum[m][.] * wm[n][g]]
+// with b = g for 32-element groups and g/2 for Q6_K's 16-element groups.
+//
+// gemm_tc.cu holds the tcgen05 tensor-core kernel used for 32-element groups; this file holds
+// the dp4a tile kernel used for the other cases (16-element groups, mins, small M) and the
+// ABI entry points.
+#include <cstring>
+
+#include "jkb_internal.h"
+
+namespace jkb {
+
+int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out,
+                   size_t row_begin, size_t row_end, cudaStream_t st, bool *used);
+
+namespace {
+
+constexpr int TM = 64, TN = 64, TG = 32;  // tile M, tile N, K elements staged per step
+
+// 256 threads; thread (ty, tx) owns outputs m = ty*4 + i, n = tx*4 + j (i, j < 4).
+__global__ void __launch_bounds__(256) gemm_dp4a_kernel(
+    const int8_t *__restrict__ xq, const float *__restrict__ xs, const float *__restrict__ xsum,
+    const float *__restrict__ xs16, size_t m, size_t kp, const int8_t *__restrict__ wq,
+    const float *__restrict__ ws, const float *__restrict__ wm, size_t groups, int gsz,
+    size_t row_begin, size_t row_end, float *__restrict__ out) {
+    __shared__ __align__(16) int8_t sa[TM][TG + 4];
+    __shared__ __align__(16) int8_t sb[TN][TG + 4];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const size_t m0 = (size_t)blockIdx.y * TM, n0 = row_begin + (size_t)blockIdx.x * TN;
+    const size_t kb = kp / 32, kc = kp / 16;
+    const size_t sub_n = row_end - row_begin;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0f;
+    const int per_step = TG / gsz;  // scale groups per staged step (1 or 2)
+    const size_t steps = kp / TG;
+    for (size_t st = 0; st < steps; st++) {
+        // stage 64 x 32 bytes of A and B (one 8-byte word per thread each)
+        {
+            int r = threadIdx.x >> 2, c = (threadIdx.x & 3) * 8;
+            size_t gm = m0 + r, gn = n0 + r;
+            uint2 va = make_uint2(0, 0), vb = make_uint2(0, 0);
+            if (gm < m) va = *reinterpret_cast<const uint2 *>(xq + gm * kp + st * TG + c);
+            if (gn < row_end) vb = *reinterpret_cast<const uint2 *>(wq + gn * kp + st * TG + c);
+            *reinterpret_cast<uint2 *>(&sa[r][c]) = va;
+            *reinterpret_cast<uint2 *>(&sb[r][c]) = vb;
+        }
+        __syncthreads();
+        for (int gg = 0; gg < per_step; gg++) {
+            const size_t g = st * per_step + gg;
+            const int k0 = gg * gsz;
+            int c[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) c[i][j] = 0;
+            for (int k = k0; k < k0 + gsz; k += 4) {
+                int a4[4], b4[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) a4[i] = *reinterpret_cast<const int *>(&sa[ty * 4 + i][k]);
+#pragma unroll
+                for (int j = 0; j < 4; j++) b4[j] = *reinterpret_cast<const int *>(&sb[tx * 4 + j][k]);
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) c[i][j] = __dp4a(a4[i], b4[j], c[i][j]);
+            }
+            const size_t b32 = gsz == 32 ? g : g / 2;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                size_t gm = m0 + ty * 4 + i;
+                if (gm >= m) continue;
+                float x_sc = xs[gm * kb + b32];
+                float x_sm = 0.0f;
+                if (wm) x_sm = gsz == 32 ? xsum[gm * kb + b32] : xs16[gm * kc + g];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    size_t gn = n0 + tx * 4 + j;
+                    if (gn >= row_end) continue;
+                    float t = __fmul_rn((float)c[i][j], __fmul_rn(x_sc, ws[gn * groups + g]));
+                    if (wm) t = __fsub_rn(t, __fmul_rn(x_sm, wm[gn * groups + g]));
+                    acc[i][j] = __fadd_rn(acc[i][j], t);
+                }
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        size_t gm = m0 + ty * 4 + i;
+        if (gm >= m) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            size_t gn = n0 + tx * 4 + j;
+            if (gn < row_end) out[gm * sub_n + (gn - row_begin)] = acc[i][j];
+        }
+    }
+}
+
+}  // namespace
+
+// execute_gemm_repacked_rows validation (repack.rs:2725-2779).
+static int gemm_rows(const char *fn, float *out, size_t out_len, const jkb_repacked_weight *w,
+                     const jkb_act_q8 *act, size_t row_begin, size_t row_end, bool gemv_only,
+                     cudaStream_t st) {
+    if (!w || w->magic != REPACKED_MAGIC)
+        return fail(JKB_E_INVALID, fn, 0, 0, 0, "null or destroyed repacked weight");
+    if (!act || act->magic != ACT_MAGIC)
+        return fail(JKB_E_INVALID, fn, 0, 0, 0, "null or destroyed activation handle");
+    if (gemv_only && act->m != 1)
+        return fail(JKB_E_BOUNDS, "gemv_repacked", 0, out_len * 4, w->device_bytes,
+                    "gemv_repacked requires act.m() == 1, got %zu", act->m);
+    if (act->k != w->cols)
+        return fail(JKB_E_BOUNDS, "gemm_repacked", 0, out_len * 4, w->device_bytes,
+                    "activation k %zu != weight cols %zu", act->k, w->cols);
+    if (row_begin > row_end || row_end > w->rows)
+        return fail(JKB_E_BOUNDS, "gemm_repacked", row_begin, row_end - row_begin, w->rows,
+                    "row_range %zu..%zu out of bounds for %zu rows", row_begin, row_end, w->rows);
+    size_t sub_n = row_end - row_begin;
+    if (out_len != act->m * sub_n)
+        return fail(JKB_E_BOUNDS, "gemm_repacked", 0, out_len * 4, act->m * sub_n * 4,
+                    "output length %zu != m * row_range.len() = %zu", out_len, act->m * sub_n);
+    if (sub_n == 0 || act->m == 0) return JKB_OK;
+    if (!out) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null output");
+    bool used = false;
+    int rc = gemm_tc_launch(w, act, out, row_begin, row_end, st, &used);
+    if (rc || used) return rc;
+    dim3 grid((unsigned)((sub_n + TN - 1) / TN), (unsigned)((act->m + TM - 1) / TM));
+    gemm_dp4a_kernel<<<grid, 256, 0, st>>>(act->q, act->x_scales, act->x_sums, act->x_sums_16,
+                                          act->m, act->k_pad, w->q, w->scales, w->mins,
+                                          w->scale_groups, (int)w->group_elems, row_begin,
+                                          row_end, out);
+    return check_launch("gemm_dp4a_kernel");
+}
+
+}  // namespace jkb
+
+using namespace jkb;
+
+extern "C" {
+
+int jkb_gemm_repacked(float *out, size_t out_len, const jkb_repacked_weight *w,
+                      const jkb_act_q8 *act, void *stream) {
+    size_t rows = (w && w->magic == REPACKED_MAGIC) ? w->rows : 0;
+    return gemm_rows("gemm_repacked", out, out_len, w, act, 0, rows, false, as_stream(stream));
+}
+
+int jkb_gemm_repacked_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
+                           const jkb_act_q8 *act, size_t row_begin, size_t row_end,
+                           void *stream) {
+    return gemm_rows("gemm_repacked_rows", out, out_len, w, act, row_begin, row_end, false,
+                     as_stream(stream));
+}
+
+int jkb_gemv_repacked(float *out, size_t out_len, const jkb_repacked_weight *w,
+                      const jkb_act_q8 *act, void *stream) {
+    size_t rows = (w && w->magic == REPACKED_MAGIC) ? w->rows : 0;
+    return gemm_rows("gemv_repacked", out, out_len, w, act, 0, rows, true, as_stream(stream));
+}
+
+int jkb_gemv_repacked_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
+                           const jkb_act_q8 *act, size_t row_begin, size_t row_end,
+                           void *stream) {
+    return gemm_rows("gemv_repacked_rows", out, out_len, w, act, row_begin, row_end, true,
+                     as_stream(stream));
+}
+
+int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight *w,
+                          const float *input, size_t in_len, size_t m, jkb_act_q8 *scratch,
+                          void *stream) {
+    if (!w || w->magic != REPACKED_MAGIC)
+        return fail(JKB_E_INVALID, "gemm_repacked_f32", 0, 0, 0, "null or destroyed weight");
+    // gemm_repacked_f32_rows validation (repack.rs:4147-4161)
+    if (m == 0 || w->cols == 0 || in_len != m * w->cols)
+        return fail(JKB_E_BOUNDS, "gemm_repacked_f32", 0, in_len * 4, m * w->cols * 4,
+                    "input length %zu != m (%zu) * cols (%zu)", in_len, m, w->cols);
+    int rc = jkb_act_q8_quantize(scratch, input, in_len, m, w->cols, stream);
+    if (rc) return rc;
+    return jkb_gemm_repacked(out, out_len, w, scratch, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,141 @@
+// Internal host-side declarations shared by the .cu files of libjkb200.so.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+
+#include "jkb200.h"
+
+namespace jkb {
+
+// ---- errors (errors.cu) ----
+// Records a K3Error::TensorBoundsError-shaped failure for this thread and returns `status`.
+int fail(int status, const char *tensor, size_t offset, size_t byte_len, size_t buffer_len,
+         const char *fmt, ...) __attribute__((format(printf, 6, 7)));
+int fail_cuda(cudaError_t e, const char *where);
+// Checks cudaGetLastError after a launch.
+int check_launch(const char *where);
+void clear_error();
+
+// ---- quant format table ----
+struct Fmt {
+    int quant;
+    const char *name;
+    int block_elems;
+    int block_bytes;
+    int trailer_bytes;
+};
+const Fmt *fmt_of(int quant);  // nullptr for formats the hot path does not cover
+const char *quant_name(int quant);
+
+// Bytes of `n` logical elements in GGUF storage (QuantType::storage_bytes incl. trailer).
+inline size_t storage_bytes(const Fmt *f, size_t n) {
+    return n / (size_t)f->block_elems * (size_t)f->block_bytes + (size_t)f->trailer_bytes;
+}
+
+// ---- device buffers ----
+// One cudaMalloc per handle; planes are carved at 256-byte boundaries.
+struct Arena {
+    uint8_t *base = nullptr;
+    size_t used = 0, cap = 0;
+    static size_t round(size_t n) { return (n + 255) & ~(size_t)255; }
+    uint8_t *take(size_t n) {
+        uint8_t *p = base + used;
+        used += round(n);
+        return p;
+    }
+};
+
+// GPU layout of one weight matrix (see weights.cu for the per-format plane contents).
+struct WeightPlanes {
+    const uint8_t *qs = nullptr;  // quant plane, row pitch qs_row bytes
+    size_t qs_row = 0;
+    const uint8_t *sc = nullptr;  // 16-byte-per-block scale plane (Q4_K_M, Q6_K)
+    size_t sc_row = 0;
+    const uint16_t *d = nullptr;  // f16 block scales [rows][nb] (Q4_0, Q8_0, Q6_K, TQ*)
+    float i2s_scale = 0.0f;       // I2_S per-tensor trailer scale (non-finite -> 0)
+};
+
+}  // namespace jkb
+
+struct jkb_weight {
+    uint32_t magic;
+    int quant;       // source QuantType
+    int gpu_format;  // kernel format (TQ1_0 is stored in the TQ2_0 GPU layout)
+    size_t rows, cols, nb;
+    uint32_t ndim;
+    size_t shape[4];
+    char name[64];
+    size_t offset, byte_len, gguf_bytes;
+    uint8_t *base;
+    size_t device_bytes;
+    jkb::WeightPlanes p;
+};
+
+struct jkb_repacked_weight {
+    uint32_t magic;
+    int quant;
+    size_t rows, cols, k_pad, scale_groups, group_elems;
+    char name[64];
+    uint8_t *base;
+    size_t device_bytes;
+    int8_t *q;       // [rows][k_pad]
+    float *scales;   // [rows][scale_groups]
+    float *mins;     // [rows][scale_groups] or nullptr
+};
+
+struct jkb_act_q8 {
+    uint32_t magic;
+    size_t m_cap, k, k_pad, m;
+    uint8_t *base;
+    int8_t *q;            // [m_cap][k_pad]
+    float *x_scales;      // [m_cap][k_pad/32]
+    float *x_sums;        // [m_cap][k_pad/32]
+    float *x_sums_16;     // [m_cap][k_pad/16]
+    float *super_scales;  // [m_cap][ceil(k/256)]
+};
+
+namespace jkb {
+constexpr uint32_t WEIGHT_MAGIC = 0x4A4B5731u;    // "JKW1"
+constexpr uint32_t REPACKED_MAGIC = 0x4A4B5231u;  // "JKR1"
+constexpr uint32_t ACT_MAGIC = 0x4A4B4131u;       // "JKA1"
+
+int num_sms();
+inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Reference validators over a stored 2-D/1-D shape (quant.rs:1810-1894 and its per-format
+// twins quant.rs:762-892, :1315-1394, lib.rs:1195-1260): accepts [rows, cols] or GGUF
+// [cols, rows]; writes the (rows, cols) interpretation.
+int validate_matvec_shape(const char *tensor, size_t offset, size_t byte_len, size_t buffer_len,
+                          int quant, const size_t *shape, uint32_t ndim, size_t output_len,
+                          size_t input_len, size_t *rows, size_t *cols);
+// Handle-level wrapper: runs the validator on the handle's shape and checks that the
+// interpretation matches the orientation the handle was uploaded with.
+int validate_weight_call(const char *fn, const jkb_weight *w, int expected_quant,
+                         size_t output_len, size_t input_len);
+int check_weight(const jkb_weight *w);
+
+// gemv.cu entry used by bitlinear.cu and the sharded paths.
+enum GpuFormat { GF_Q4_0, GF_Q8_0, GF_Q4_K, GF_Q6_K, GF_TQ2_0, GF_I2_S };
+enum ActKind { ACT_Q8_0 = 0, ACT_Q8_K = 1, ACT_I8 = 2 };
+struct GemvLaunch {
+    const jkb_weight *w;
+    const void *x;           // activation rows (AoS blocks or i8)
+    size_t x_row_stride;     // bytes between tokens (batch)
+    int act_kind;
+    const float *act_scales; // per-token scale (i8 activations, device) or nullptr
+    float act_scale;         // per-tensor scale when act_scales == nullptr
+    float *out;
+    size_t out_ld;           // floats between tokens
+    size_t row_begin, row_end;
+    size_t m;                // tokens
+    int32_t *dbg_sumi, *dbg_mins;
+    float *dbg_val;
+};
+int launch_gemv(const GemvLaunch &L, cudaStream_t st);
+
+}  // namespace jkb

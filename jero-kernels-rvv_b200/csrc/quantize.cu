@@ -1,0 +1,464 @@
+// Activation quantizers: BlockQ8_0 / BlockQ8K rows (quant_q8.rs), QuantizedActQ8 per-32 blocks
+// (repack.rs) and the BitNet SubLN absmax quantizer (lib.rs). All are bit-exact restatements:
+// IEEE division (__fdiv_rn), round-half-away-from-zero (roundf), separately rounded multiplies
+// and adds where the reference sums in f32.
+#include <cstring>
+
+#include "jkb_internal.h"
+
+namespace jkb {
+
+__device__ __forceinline__ bool finite_f(float v) { return isfinite(v); }
+
+// round_scaled_to_i8 (quant_q8.rs:102-108)
+__device__ __forceinline__ int round_scaled(float v, float inv) {
+    if (!finite_f(v)) return 0;
+    float r = roundf(__fmul_rn(v, inv));
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    return (int)r;
+}
+
+// quantize_block_q8_0_scalar (quant_q8.rs:203-219): 8 lanes per 32-element block, 4 values per
+// lane. absmax over finite values (a max is order independent), amax == 0 -> ZERO block.
+template <bool VEC>
+__global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float *__restrict__ x,
+                                                            size_t nblocks,
+                                                            uint8_t *__restrict__ out) {
+    size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    size_t blk = gid >> 3;
+    int sub = (int)(gid & 7);
+    bool valid = blk < nblocks;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (valid) {
+        const float *p = x + blk * 32 + 4 * sub;
+        if (VEC) {
+            float4 t = __ldg(reinterpret_cast<const float4 *>(p));
+            v[0] = t.x;
+            v[1] = t.y;
+            v[2] = t.z;
+            v[3] = t.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; i++) v[i] = __ldg(p + i);
+        }
+    }
+    float a = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        if (finite_f(v[i])) a = fmaxf(a, fabsf(v[i]));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
+    if (!valid) return;
+    uint8_t *ob = out + blk * 36;
+    float d = 0.0f;
+    uint32_t packed = 0;
+    if (a != 0.0f) {
+        d = __fdiv_rn(a, 127.0f);
+        float inv = __fdiv_rn(127.0f, a);
+#pragma unroll
+        for (int i = 0; i < 4; i++) packed |= ((uint32_t)(round_scaled(v[i], inv) & 0xFF)) << (8 * i);
+    }
+    if (sub == 0) *reinterpret_cast<float *>(ob) = d;
+    *reinterpret_cast<uint32_t *>(ob + 4 + 4 * sub) = packed;
+}
+
+// quantize_block_q8_k_scalar (quant_q8.rs:447-475): one warp per 256-element block, 8 values per
+// lane; bsums[j] = sum of the 16 quantized values of lanes 2j and 2j+1.
+template <bool VEC>
+__global__ void __launch_bounds__(256) quantize_q8_k_kernel(const float *__restrict__ x,
+                                                            size_t nblocks,
+                                                            uint8_t *__restrict__ out) {
+    size_t blk = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    bool valid = blk < nblocks;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = 0.0f;
+    if (valid) {
+        const float *p = x + blk * 256 + 8 * lane;
+        if (VEC) {
+            float4 t0 = __ldg(reinterpret_cast<const float4 *>(p));
+            float4 t1 = __ldg(reinterpret_cast<const float4 *>(p + 4));
+            v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w;
+            v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = __ldg(p + i);
+        }
+    }
+    float a = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+        if (finite_f(v[i])) a = fmaxf(a, fabsf(v[i]));
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, m));
+    float d = 0.0f, inv = 0.0f;
+    if (a != 0.0f) {
+        d = __fdiv_rn(a, 127.0f);
+        inv = __fdiv_rn(127.0f, a);
+    }
+    uint32_t p0 = 0, p1 = 0;
+    int s = 0;
+    if (a != 0.0f) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            int q = round_scaled(v[i], inv);
+            s += q;
+            if (i < 4)
+                p0 |= ((uint32_t)(q & 0xFF)) << (8 * i);
+            else
+                p1 |= ((uint32_t)(q & 0xFF)) << (8 * (i - 4));
+        }
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    if (!valid) return;
+    uint8_t *ob = out + blk * 292;
+    if (lane == 0) *reinterpret_cast<float *>(ob) = d;
+    *reinterpret_cast<uint32_t *>(ob + 4 + 8 * lane) = p0;
+    *reinterpret_cast<uint32_t *>(ob + 8 + 8 * lane) = p1;
+    if ((lane & 1) == 0) *reinterpret_cast<int16_t *>(ob + 260 + lane) = (int16_t)s;
+}
+
+// QuantizedActQ8::quantize_into (repack.rs:542-650) with quantize_block32_scalar
+// (repack.rs:175-204): one thread per 32-element block, so the f32 sums run sequentially in
+// element order exactly as in the reference (x_sums from 0.0, x_sums_16 from -0.0).
+__global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ act, size_t m,
+                                                     size_t k, size_t kp,
+                                                     int8_t *__restrict__ q,
+                                                     float *__restrict__ xs,
+                                                     float *__restrict__ xsum,
+                                                     float *__restrict__ xs16) {
+    size_t kb = kp / 32;
+    size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= m * kb) return;
+    size_t r = gid / kb, b = gid % kb;
+    const float *src = act + r * k;
+    float c[32];
+    float absmax = 0.0f, s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        size_t idx = b * 32 + i;
+        float v = idx < k ? __ldg(src + idx) : 0.0f;
+        v = finite_f(v) ? v : 0.0f;
+        c[i] = v;
+        s = __fadd_rn(s, v);
+        float av = fabsf(v);
+        if (av > absmax) absmax = av;
+    }
+    float h0 = -0.0f, h1 = -0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) h0 = __fadd_rn(h0, c[i]);
+#pragma unroll
+    for (int i = 16; i < 32; i++) h1 = __fadd_rn(h1, c[i]);
+    uint32_t words[8];
+    float d = 0.0f;
+    if (absmax < 1e-30f) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) words[i] = 0;
+    } else {
+        d = __fdiv_rn(absmax, 127.0f);
+        float inv = __fdiv_rn(127.0f, absmax);
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            uint32_t pk = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float t = roundf(__fmul_rn(c[4 * w + j], inv));
+                t = fminf(fmaxf(t, -127.0f), 127.0f);
+                pk |= ((uint32_t)((int)t & 0xFF)) << (8 * j);
+            }
+            words[w] = pk;
+        }
+    }
+    uint4 *qo = reinterpret_cast<uint4 *>(q + r * kp + b * 32);
+    qo[0] = make_uint4(words[0], words[1], words[2], words[3]);
+    qo[1] = make_uint4(words[4], words[5], words[6], words[7]);
+    xs[r * kb + b] = d;
+    xsum[r * kb + b] = s;
+    xs16[r * (kp / 16) + 2 * b] = h0;
+    xs16[r * (kp / 16) + 2 * b + 1] = h1;
+}
+
+// super_scales_256 (repack.rs:623-630): slot starts at 0.0, `if sc > slot { slot = sc }` over
+// the 32-blocks of each 256 span.
+__global__ void act_super_kernel(const float *__restrict__ xs, size_t m, size_t kb, size_t nsb,
+                                 float *__restrict__ sup) {
+    size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= m * nsb) return;
+    size_t r = gid / nsb, s = gid % nsb;
+    float v = 0.0f;
+    for (size_t b = 8 * s; b < 8 * s + 8 && b < kb; b++) {
+        float sc = xs[r * kb + b];
+        if (sc > v) v = sc;
+    }
+    sup[gid] = v;
+}
+
+// subln_quantize_absmax_i8 (lib.rs:1042-1101), one CTA per row. The sum of squares is the
+// reference's sequential f32 dot (lib.rs:770-777), so one thread walks it in element order;
+// the absmax and the quantization are elementwise and run on all threads.
+__global__ void __launch_bounds__(256) subln_kernel(const float *__restrict__ in,
+                                                    const float *__restrict__ w, size_t len,
+                                                    float eps, int8_t *__restrict__ out,
+                                                    float *__restrict__ scales) {
+    extern __shared__ float sx[];
+    __shared__ float s_inv_rms, s_red[8];
+    const float *x = in + (size_t)blockIdx.x * len;
+    int8_t *o = out + (size_t)blockIdx.x * len;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) {
+        float v = __ldg(x + i);
+        sx[i] = __fmul_rn(v, v);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s0 = 0.0f;
+        for (size_t i = 0; i < len; i++) s0 = __fadd_rn(s0, sx[i]);
+        float mean_sq = __fdiv_rn(s0, (float)len);
+        s_inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean_sq, eps)));
+    }
+    __syncthreads();
+    float inv_rms = s_inv_rms;
+    float mx = 0.0f;
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) {
+        float xn = __fmul_rn(__fmul_rn(__ldg(x + i), inv_rms), __ldg(w + i));
+        float av = fabsf(xn);
+        sx[i] = xn;
+        if (av > mx) mx = av;
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+        float t = __shfl_xor_sync(0xffffffffu, mx, m);
+        if (t > mx) mx = t;
+    }
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float v = 0.0f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++)
+            if (s_red[i] > v) v = s_red[i];
+        s_red[0] = v;
+    }
+    __syncthreads();
+    float max_val = s_red[0];
+    if (isnan(max_val) || max_val < 1e-12f) {
+        for (size_t i = threadIdx.x; i < len; i += blockDim.x) o[i] = 0;
+        if (threadIdx.x == 0) scales[blockIdx.x] = __fdiv_rn(1.0f, 127.0f);
+        return;
+    }
+    float scale = __fdiv_rn(max_val, 127.0f);
+    for (size_t i = threadIdx.x; i < len; i += blockDim.x) {
+        float q = roundf(__fdiv_rn(sx[i], scale));
+        int qi = 0;
+        if (!isnan(q)) qi = (int)fminf(fmaxf(q, -128.0f), 127.0f);
+        o[i] = (int8_t)qi;
+    }
+    if (threadIdx.x == 0) scales[blockIdx.x] = scale;
+}
+
+// validate_activation_input / validate_activation_quant_slice (quant_q8.rs:111-149)
+static int validate_act(const char *name, size_t x_len, size_t out_len, size_t be) {
+    if (x_len == 0 || x_len % be != 0)
+        return fail(JKB_E_BOUNDS, name, 0, x_len * 4, out_len,
+                    "%s: input length %zu must be a positive multiple of %zu", name, x_len, be);
+    if (out_len != x_len / be)
+        return fail(JKB_E_BOUNDS, name, 0, x_len * 4, out_len,
+                    "%s: output block count %zu != expected %zu", name, out_len, x_len / be);
+    return JKB_OK;
+}
+
+static int launch_q8_0(const float *x, size_t nblocks, void *out, cudaStream_t st) {
+    size_t threads = nblocks * 8;
+    unsigned grid = (unsigned)((threads + 255) / 256);
+    bool vec = ((uintptr_t)x & 15) == 0;
+    if (vec)
+        quantize_q8_0_kernel<true><<<grid, 256, 0, st>>>(x, nblocks, (uint8_t *)out);
+    else
+        quantize_q8_0_kernel<false><<<grid, 256, 0, st>>>(x, nblocks, (uint8_t *)out);
+    return check_launch("quantize_q8_0_kernel");
+}
+
+static int launch_q8_k(const float *x, size_t nblocks, void *out, cudaStream_t st) {
+    size_t threads = nblocks * 32;
+    unsigned grid = (unsigned)((threads + 255) / 256);
+    bool vec = ((uintptr_t)x & 15) == 0;
+    if (vec)
+        quantize_q8_k_kernel<true><<<grid, 256, 0, st>>>(x, nblocks, (uint8_t *)out);
+    else
+        quantize_q8_k_kernel<false><<<grid, 256, 0, st>>>(x, nblocks, (uint8_t *)out);
+    return check_launch("quantize_q8_k_kernel");
+}
+
+static bool check_act(const jkb_act_q8 *a) { return a && a->magic == ACT_MAGIC; }
+
+}  // namespace jkb
+
+using namespace jkb;
+
+extern "C" {
+
+int jkb_quantize_row_q8_0_f32(const float *x, size_t x_len, jkb_block_q8_0 *out, size_t out_len,
+                              void *stream) {
+    int rc = validate_act("quantize_row_q8_0_f32", x_len, out_len, 32);
+    if (rc) return rc;
+    if (!x || !out) return fail(JKB_E_INVALID, "quantize_row_q8_0_f32", 0, 0, 0, "null pointer");
+    return launch_q8_0(x, out_len, out, as_stream(stream));
+}
+
+int jkb_quantize_row_q8_0(const float *x, size_t x_len, jkb_block_q8_0 *out, size_t out_len,
+                          void *stream) {
+    return jkb_quantize_row_q8_0_f32(x, x_len, out, out_len, stream);
+}
+
+int jkb_quantize_row_q8_k(const float *x, size_t x_len, jkb_block_q8_k *out, size_t out_len,
+                          void *stream) {
+    int rc = validate_act("quantize_row_q8_k", x_len, out_len, 256);
+    if (rc) return rc;
+    if (!x || !out) return fail(JKB_E_INVALID, "quantize_row_q8_k", 0, 0, 0, "null pointer");
+    return launch_q8_k(x, out_len, out, as_stream(stream));
+}
+
+int jkb_quantize_rows_q8_0(const float *x, size_t m, size_t k, jkb_block_q8_0 *out,
+                           size_t out_len, void *stream) {
+    if (m == 0) return fail(JKB_E_BOUNDS, "quantize_rows_q8_0", 0, 0, out_len, "m must be > 0");
+    int rc = validate_act("quantize_row_q8_0_f32", k, out_len / m, 32);
+    if (rc) return rc;
+    if (out_len != m * (k / 32))
+        return fail(JKB_E_BOUNDS, "quantize_rows_q8_0", 0, m * k * 4, out_len,
+                    "output block count %zu != expected %zu", out_len, m * (k / 32));
+    if (!x || !out) return fail(JKB_E_INVALID, "quantize_rows_q8_0", 0, 0, 0, "null pointer");
+    return launch_q8_0(x, out_len, out, as_stream(stream));
+}
+
+int jkb_quantize_rows_q8_k(const float *x, size_t m, size_t k, jkb_block_q8_k *out,
+                           size_t out_len, void *stream) {
+    if (m == 0) return fail(JKB_E_BOUNDS, "quantize_rows_q8_k", 0, 0, out_len, "m must be > 0");
+    int rc = validate_act("quantize_row_q8_k", k, out_len / m, 256);
+    if (rc) return rc;
+    if (out_len != m * (k / 256))
+        return fail(JKB_E_BOUNDS, "quantize_rows_q8_k", 0, m * k * 4, out_len,
+                    "output block count %zu != expected %zu", out_len, m * (k / 256));
+    if (!x || !out) return fail(JKB_E_INVALID, "quantize_rows_q8_k", 0, 0, 0, "null pointer");
+    return launch_q8_k(x, out_len, out, as_stream(stream));
+}
+
+int jkb_subln_quantize_absmax_i8_rows(int8_t *out_i8, const float *input,
+                                      const float *norm_weight, size_t m, size_t len, float eps,
+                                      float *scales_out, void *stream) {
+    if (len == 0 || m == 0)
+        return fail(JKB_E_BOUNDS, "subln", 0, 0, len * 4,
+                    "dimension mismatch: input=%zu, rows=%zu", len, m);
+    if (!out_i8 || !input || !norm_weight || !scales_out)
+        return fail(JKB_E_INVALID, "subln", 0, 0, 0, "null pointer");
+    size_t smem = len * sizeof(float);
+    if (smem > 200 * 1024)
+        return fail(JKB_E_BOUNDS, "subln", 0, len, 200 * 1024 / 4,
+                    "row length %zu exceeds the %d-element limit of the GPU kernel", len,
+                    200 * 1024 / 4);
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(subln_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024);
+        attr = true;
+    }
+    subln_kernel<<<(unsigned)m, 256, smem, as_stream(stream)>>>(input, norm_weight, len, eps,
+                                                                out_i8, scales_out);
+    return check_launch("subln_kernel");
+}
+
+int jkb_subln_quantize_absmax_i8(int8_t *out_i8, size_t out_len, const float *input,
+                                 size_t in_len, const float *norm_weight, size_t w_len, float eps,
+                                 float *scale_out, void *stream) {
+    if (in_len == 0 || out_len != in_len || w_len != in_len)
+        return fail(JKB_E_BOUNDS, "subln", 0, out_len, in_len * 4,
+                    "dimension mismatch: input=%zu, out_i8=%zu, norm_weight=%zu", in_len,
+                    out_len, w_len);
+    return jkb_subln_quantize_absmax_i8_rows(out_i8, input, norm_weight, 1, in_len, eps,
+                                             scale_out, stream);
+}
+
+int jkb_act_q8_create(size_t m_capacity, size_t k, jkb_act_q8 **out) {
+    if (!out) return fail(JKB_E_INVALID, "QuantizedActQ8", 0, 0, 0, "null out");
+    *out = nullptr;
+    if (m_capacity == 0 || k == 0)
+        return fail(JKB_E_BOUNDS, "QuantizedActQ8", 0, 0, 0,
+                    "capacity must be non-zero, got m=%zu k=%zu", m_capacity, k);
+    jkb_act_q8 *a = new jkb_act_q8();
+    memset(a, 0, sizeof(*a));
+    a->magic = ACT_MAGIC;
+    a->m_cap = m_capacity;
+    a->k = k;
+    a->k_pad = (k + 31) / 32 * 32;
+    size_t kb = a->k_pad / 32, kc = a->k_pad / 16, nsb = (k + 255) / 256;
+    Arena ar;
+    size_t qb = m_capacity * a->k_pad, fb = m_capacity * kb * 4, f16b = m_capacity * kc * 4,
+           sb = m_capacity * nsb * 4;
+    ar.cap = Arena::round(qb) + 2 * Arena::round(fb) + Arena::round(f16b) + Arena::round(sb);
+    cudaError_t e = cudaMalloc(&ar.base, ar.cap);
+    if (e != cudaSuccess) {
+        delete a;
+        return fail_cuda(e, "jkb_act_q8_create");
+    }
+    a->base = ar.base;
+    a->q = (int8_t *)ar.take(qb);
+    a->x_scales = (float *)ar.take(fb);
+    a->x_sums = (float *)ar.take(fb);
+    a->x_sums_16 = (float *)ar.take(f16b);
+    a->super_scales = (float *)ar.take(sb);
+    *out = a;
+    return JKB_OK;
+}
+
+int jkb_act_q8_destroy(jkb_act_q8 *a) {
+    if (!check_act(a)) return fail(JKB_E_INVALID, "QuantizedActQ8", 0, 0, 0, "null or destroyed");
+    a->magic = 0;
+    cudaFree(a->base);
+    delete a;
+    return JKB_OK;
+}
+
+int jkb_act_q8_quantize(jkb_act_q8 *a, const float *input, size_t in_len, size_t m, size_t k,
+                        void *stream) {
+    if (!check_act(a)) return fail(JKB_E_INVALID, "QuantizedActQ8", 0, 0, 0, "null or destroyed");
+    // QuantizedActQ8::quantize_into validation (repack.rs:547-560)
+    if (m == 0 || k == 0 || in_len != m * k)
+        return fail(JKB_E_BOUNDS, "QuantizedActQ8", 0, in_len * 4, m * k * 4,
+                    "activation length %zu does not match m (%zu) * k (%zu)", in_len, m, k);
+    if (k != a->k || m > a->m_cap)
+        return fail(JKB_E_BOUNDS, "QuantizedActQ8", 0, in_len * 4, a->m_cap * a->k * 4,
+                    "batch [%zu, %zu] exceeds the handle capacity [%zu, %zu]", m, k, a->m_cap,
+                    a->k);
+    if (!input) return fail(JKB_E_INVALID, "QuantizedActQ8", 0, 0, 0, "null input");
+    cudaStream_t st = as_stream(stream);
+    size_t kb = a->k_pad / 32, nsb = (k + 255) / 256;
+    size_t n = m * kb;
+    act_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(input, m, k, a->k_pad, a->q,
+                                                               a->x_scales, a->x_sums,
+                                                               a->x_sums_16);
+    int rc = check_launch("act_q8_kernel");
+    if (rc) return rc;
+    size_t ns = m * nsb;
+    act_super_kernel<<<(unsigned)((ns + 255) / 256), 256, 0, st>>>(a->x_scales, m, kb, nsb,
+                                                                   a->super_scales);
+    rc = check_launch("act_super_kernel");
+    if (rc) return rc;
+    a->m = m;
+    return JKB_OK;
+}
+
+int jkb_act_q8_buffers(const jkb_act_q8 *a, size_t *m, size_t *k, size_t *k_padded, int8_t **q,
+                       float **x_scales, float **x_sums, float **x_sums_16,
+                       float **super_scales) {
+    if (!check_act(a)) return fail(JKB_E_INVALID, "QuantizedActQ8", 0, 0, 0, "null or destroyed");
+    if (m) *m = a->m;
+    if (k) *k = a->k;
+    if (k_padded) *k_padded = a->k_pad;
+    if (q) *q = a->q;
+    if (x_scales) *x_scales = a->x_scales;
+    if (x_sums) *x_sums = a->x_sums;
+    if (x_sums_16) *x_sums_16 = a->x_sums_16;
+    if (super_scales) *super_scales = a->super_scales;
+    return JKB_OK;
+}
+
+}  // extern "C"

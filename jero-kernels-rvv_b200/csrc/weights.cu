@@ -1,0 +1,543 @@
+// Load-time weight handles: validation (repack.rs:1208-1284), upload and relayout into the
+// GPU layouts used by the GEMV / BitLinear kernels (jkb_weight) and by the GEMM
+// (jkb_repacked_weight, the i8-expanded RepackedWeight of repack.rs:1092-1133).
+//
+// jkb_weight planes (every row contiguous, rows back to back, block order kept):
+//   Q4_0   qs: 16 B/block, the GGUF nibble bytes        d: f16 per block
+//   Q8_0   qs: 32 B/block, the GGUF i8 quants           d: f16 per block
+//   Q4_K_M qs: 128 B/block, GGUF qs bytes               sc: 16 B/block = d, dmin, scales[12]
+//   Q6_K   qs: 192 B/block, ql/qh regrouped per lane    sc: 16 B/block i8 scales, d: f16
+//          (item t = 2h+i owns A = ql[64h+16i..+16], B = ql[64h+32+16i..+16],
+//           H = qh[32h+16i..+16]; stored as A0..A3 | B0..B3 | H0..H3)
+//   TQ2_0  qs: 64 B/block, 2-bit codes re-ordered so that word W, bit pair j, byte b holds
+//          element 16W+4j+b of the 64-element chunk   d: f16 per block
+//   TQ1_0  decoded at load into the TQ2_0 GPU layout (same codes 0..2)
+//   I2_S   qs: 32 B/block, GGUF bytes unchanged; the trailer scale is kept on the host
+// Byte counts equal the GGUF payload (except TQ1_0, whose base-3 bytes grow from 54 to 66).
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "jkb_internal.h"
+
+namespace jkb {
+
+__device__ __forceinline__ uint16_t rd16(const uint8_t *p) {
+    return (uint16_t)(p[0] | (p[1] << 8));
+}
+
+__global__ void relayout_kernel(int quant, const uint8_t *__restrict__ raw, size_t rows,
+                                size_t nb, size_t raw_row, int bb, uint8_t *__restrict__ qs,
+                                size_t qs_row, uint8_t *__restrict__ sc, size_t sc_row,
+                                uint16_t *__restrict__ d) {
+    size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= rows * nb) return;
+    size_t r = idx / nb, b = idx % nb;
+    const uint8_t *blk = raw + r * raw_row + b * (size_t)bb;
+    switch (quant) {
+    case JKB_Q4_0: {
+        d[idx] = rd16(blk);
+        uint8_t *o = qs + r * qs_row + 16 * b;
+        for (int i = 0; i < 16; i++) o[i] = blk[2 + i];
+        break;
+    }
+    case JKB_Q8_0: {
+        d[idx] = rd16(blk);
+        uint8_t *o = qs + r * qs_row + 32 * b;
+        for (int i = 0; i < 32; i++) o[i] = blk[2 + i];
+        break;
+    }
+    case JKB_Q4_K_M: {
+        uint8_t *s = sc + r * sc_row + 16 * b;
+        for (int i = 0; i < 16; i++) s[i] = blk[i];
+        uint8_t *o = qs + r * qs_row + 128 * b;
+        for (int i = 0; i < 128; i++) o[i] = blk[16 + i];
+        break;
+    }
+    case JKB_Q6_K: {
+        uint8_t *s = sc + r * sc_row + 16 * b;
+        for (int i = 0; i < 16; i++) s[i] = blk[192 + i];
+        d[idx] = rd16(blk + 208);
+        uint8_t *o = qs + r * qs_row + 192 * b;
+        for (int t = 0; t < 4; t++) {
+            int h = t >> 1, i = t & 1;
+            for (int j = 0; j < 16; j++) {
+                o[16 * t + j] = blk[64 * h + 16 * i + j];
+                o[64 + 16 * t + j] = blk[64 * h + 32 + 16 * i + j];
+                o[128 + 16 * t + j] = blk[128 + 32 * h + 16 * i + j];
+            }
+        }
+        break;
+    }
+    case JKB_TQ2_0:
+    case JKB_TQ1_0: {
+        d[idx] = rd16(blk);
+        uint8_t codes[256];
+        if (quant == JKB_TQ2_0) {
+            for (int e = 0; e < 256; e++) codes[e] = (blk[2 + e / 4] >> (2 * (e % 4))) & 3;
+        } else {
+            for (int i = 0; i < 51; i++) {
+                unsigned v = blk[2 + i];
+                for (int j = 0; j < 5; j++) {
+                    codes[5 * i + j] = (uint8_t)(v % 3);
+                    v /= 3;
+                }
+            }
+            codes[255] = (uint8_t)(blk[53] % 3);
+        }
+        uint8_t *o = qs + r * qs_row + 64 * b;
+        for (int i = 0; i < 64; i++) o[i] = 0;
+        for (int e = 0; e < 256; e++) {
+            int p = e >> 6, W = (e & 63) >> 4, j = (e & 15) >> 2, bq = e & 3;
+            o[16 * p + 4 * W + bq] |= (uint8_t)(codes[e] << (2 * j));
+        }
+        break;
+    }
+    case JKB_I2_S: {
+        uint8_t *o = qs + r * qs_row + 32 * b;
+        for (int i = 0; i < 32; i++) o[i] = blk[i];
+        break;
+    }
+    default: break;
+    }
+}
+
+__device__ __forceinline__ float f16_finite_dev(uint16_t bits) {
+    float v = __half2float(__ushort_as_half(bits));
+    return ((bits >> 10) & 0x1F) == 0x1F ? 0.0f : v;
+}
+
+// repack_block_scaled_range_into_i8 (repack.rs:1724-2103) for the covered formats, one thread
+// per (row, block): i8 values row-major [rows][k_pad], f32 scales [rows][groups].
+__global__ void repack_i8_kernel(int quant, const uint8_t *__restrict__ raw, size_t rows,
+                                 size_t nb, size_t raw_row, int bb, float i2s, int8_t *q,
+                                 size_t k_pad, float *scales, float *mins, size_t groups) {
+    size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= rows * nb) return;
+    size_t r = idx / nb, b = idx % nb;
+    const uint8_t *blk = raw + r * raw_row + b * (size_t)bb;
+    int8_t *qr = q + r * k_pad;
+    float *sr = scales + r * groups;
+    float *mr = mins ? mins + r * groups : nullptr;
+    switch (quant) {
+    case JKB_Q8_0: {
+        float dd = f16_finite_dev(rd16(blk));
+        sr[b] = dd;
+        for (int i = 0; i < 32; i++) qr[32 * b + i] = dd != 0.0f ? (int8_t)blk[2 + i] : 0;
+        break;
+    }
+    case JKB_Q4_0: {
+        float dd = f16_finite_dev(rd16(blk));
+        sr[b] = dd;
+        for (int i = 0; i < 16; i++) {
+            qr[32 * b + i] = dd != 0.0f ? (int8_t)((blk[2 + i] & 0x0F) - 8) : 0;
+            qr[32 * b + 16 + i] = dd != 0.0f ? (int8_t)(((blk[2 + i] >> 4) & 0x0F) - 8) : 0;
+        }
+        break;
+    }
+    case JKB_Q4_K_M: {
+        float dd = f16_finite_dev(rd16(blk)), dmin = f16_finite_dev(rd16(blk + 2));
+        const uint8_t *s = blk + 4;
+        uint8_t scv[8], mv[8];
+        for (int j = 0; j < 4; j++) {
+            scv[j] = s[j] & 0x3F;
+            mv[j] = s[j + 4] & 0x3F;
+        }
+        for (int j = 4; j < 8; j++) {
+            scv[j] = (uint8_t)((s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4));
+            mv[j] = (uint8_t)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+        }
+        for (int c = 0; c < 4; c++) {
+            size_t g0 = b * 8 + 2 * c;
+            sr[g0] = __fmul_rn(dd, (float)scv[2 * c]);
+            mr[g0] = __fmul_rn(dmin, (float)mv[2 * c]);
+            sr[g0 + 1] = __fmul_rn(dd, (float)scv[2 * c + 1]);
+            mr[g0 + 1] = __fmul_rn(dmin, (float)mv[2 * c + 1]);
+            for (int l = 0; l < 32; l++) {
+                qr[256 * b + 64 * c + l] = (int8_t)(blk[16 + 32 * c + l] & 0x0F);
+                qr[256 * b + 64 * c + 32 + l] = (int8_t)((blk[16 + 32 * c + l] >> 4) & 0x0F);
+            }
+        }
+        break;
+    }
+    case JKB_Q6_K: {
+        float dd = f16_finite_dev(rd16(blk + 208));
+        for (int s = 0; s < 16; s++) sr[b * 16 + s] = __fmul_rn(dd, (float)(int8_t)blk[192 + s]);
+        const uint8_t *ql = blk, *qh = blk + 128;
+        for (int h = 0; h < 2; h++)
+            for (int l = 0; l < 32; l++) {
+                int lb = 64 * h, hb = 32 * h, n = 256 * (int)b + 128 * h;
+                int q1 = (int)((ql[lb + l] & 0x0F) | ((qh[hb + l] & 3) << 4)) - 32;
+                int q2 = (int)((ql[lb + l + 32] & 0x0F) | (((qh[hb + l] >> 2) & 3) << 4)) - 32;
+                int q3 = (int)(((ql[lb + l] >> 4) & 0x0F) | (((qh[hb + l] >> 4) & 3) << 4)) - 32;
+                int q4 = (int)(((ql[lb + l + 32] >> 4) & 0x0F) | (((qh[hb + l] >> 6) & 3) << 4)) - 32;
+                bool z = dd == 0.0f;
+                qr[n + l] = z ? 0 : (int8_t)q1;
+                qr[n + l + 32] = z ? 0 : (int8_t)q2;
+                qr[n + l + 64] = z ? 0 : (int8_t)q3;
+                qr[n + l + 96] = z ? 0 : (int8_t)q4;
+            }
+        break;
+    }
+    case JKB_TQ2_0:
+    case JKB_TQ1_0: {
+        float dd = f16_finite_dev(rd16(blk));
+        for (int s = 0; s < 8; s++) sr[b * 8 + s] = dd;
+        if (quant == JKB_TQ2_0) {
+            for (int e = 0; e < 256; e++)
+                qr[256 * b + e] = (int8_t)(((blk[2 + e / 4] >> (2 * (e % 4))) & 3) - 1);
+        } else {
+            for (int i = 0; i < 51; i++) {
+                unsigned v = blk[2 + i];
+                for (int j = 0; j < 5; j++) {
+                    qr[256 * b + 5 * i + j] = (int8_t)((int)(v % 3) - 1);
+                    v /= 3;
+                }
+            }
+            qr[256 * b + 255] = (int8_t)((int)(blk[53] % 3) - 1);
+        }
+        break;
+    }
+    case JKB_I2_S: {
+        for (int s = 0; s < 4; s++) sr[b * 4 + s] = i2s;
+        for (int g = 0; g < 32; g++) {
+            uint8_t v = blk[g];
+            bool z = i2s == 0.0f;
+            qr[128 * b + g] = z ? 0 : (int8_t)(((v >> 6) & 3) - 1);
+            qr[128 * b + 32 + g] = z ? 0 : (int8_t)(((v >> 4) & 3) - 1);
+            qr[128 * b + 64 + g] = z ? 0 : (int8_t)(((v >> 2) & 3) - 1);
+            qr[128 * b + 96 + g] = z ? 0 : (int8_t)((v & 3) - 1);
+        }
+        break;
+    }
+    default: break;
+    }
+}
+
+// validate_matrix_shape + validate_matrix_view (repack.rs:1151-1284).
+static int validate_matrix_view(const jkb_tensor_view *v, const Fmt *f, size_t rows,
+                                size_t cols) {
+    const char *nm = v->name ? v->name : "";
+    if (rows == 0 || cols == 0)
+        return fail(JKB_E_BOUNDS, nm, v->offset, v->byte_len, v->byte_len,
+                    "repack dimensions must be non-zero, got [%zu, %zu]", rows, cols);
+    if (cols % (size_t)f->block_elems != 0)
+        return fail(JKB_E_BOUNDS, nm, v->offset, v->byte_len, v->byte_len,
+                    "columns (%zu) must be a multiple of %s block size (%d)", cols, f->name,
+                    f->block_elems);
+    if (v->ndim == 1) {
+        if (rows * cols != v->shape[0])
+            return fail(JKB_E_BOUNDS, nm, v->offset, v->byte_len, v->byte_len,
+                        "1D tensor length %zu does not match rows (%zu) * cols (%zu)",
+                        v->shape[0], rows, cols);
+    } else if (v->ndim == 2) {
+        size_t d0 = v->shape[0], d1 = v->shape[1];
+        if (!((d0 == rows && d1 == cols) || (d0 == cols && d1 == rows)))
+            return fail(JKB_E_BOUNDS, nm, v->offset, v->byte_len, v->byte_len,
+                        "tensor shape [%zu, %zu] does not match requested rows=%zu, cols=%zu",
+                        d0, d1, rows, cols);
+    } else {
+        return fail(JKB_E_BOUNDS, nm, v->offset, v->byte_len, v->byte_len,
+                    "expected 1D or 2D weight tensor, got %uD", v->ndim);
+    }
+    size_t need = storage_bytes(f, rows * cols);
+    if (v->byte_len < need)
+        return fail(JKB_E_BOUNDS, nm, v->offset, v->byte_len, v->byte_len,
+                    "backing bytes %zu < required %zu", v->byte_len, need);
+    return JKB_OK;
+}
+
+// RepackedWeight::repack orientation rule (repack.rs:2255-2282).
+static int infer_rows_cols(const jkb_tensor_view *v, const Fmt *f, size_t *rows, size_t *cols) {
+    if (v->ndim != 2)
+        return fail(JKB_E_BOUNDS, v->name ? v->name : "", v->offset, v->byte_len, v->byte_len,
+                    "RepackedWeight::repack requires a 2D tensor, got %uD", v->ndim);
+    size_t d0 = v->shape[0], d1 = v->shape[1], be = (size_t)f->block_elems;
+    if (d0 % be == 0 && d1 % be != 0) {
+        *rows = d1;
+        *cols = d0;
+    } else if (d1 % be == 0 && d0 % be != 0) {
+        *rows = d0;
+        *cols = d1;
+    } else {
+        *rows = d1;
+        *cols = d0;
+    }
+    return JKB_OK;
+}
+
+// Stages the raw GGUF bytes on the device (a load-time temporary) and reads the I2_S trailer.
+static int stage_raw(const jkb_tensor_view *v, size_t need, cudaStream_t st, uint8_t **dev,
+                     bool *owned) {
+    if (v->data_on_device) {
+        *dev = (uint8_t *)v->data;
+        *owned = false;
+        return JKB_OK;
+    }
+    cudaError_t e = cudaMalloc(dev, need);
+    if (e != cudaSuccess) return fail_cuda(e, "weight upload (staging)");
+    *owned = true;
+    e = cudaMemcpyAsync(*dev, v->data, need, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) {
+        cudaFree(*dev);
+        return fail_cuda(e, "weight upload (copy)");
+    }
+    return JKB_OK;
+}
+
+static float read_i2s_trailer(const jkb_tensor_view *v, size_t payload) {
+    float s = 0.0f;
+    if (v->data_on_device)
+        cudaMemcpy(&s, (const uint8_t *)v->data + payload, 4, cudaMemcpyDeviceToHost);
+    else
+        memcpy(&s, (const uint8_t *)v->data + payload, 4);
+    // read_i2_s_trailer_scale (quant.rs:360-366): non-finite -> 0.0
+    uint32_t u;
+    memcpy(&u, &s, 4);
+    return ((u >> 23) & 0xFF) == 0xFF ? 0.0f : s;
+}
+
+static int weight_upload(const jkb_tensor_view *v, size_t rows, size_t cols, cudaStream_t st,
+                         jkb_weight **out) {
+    if (!v || !out) return fail(JKB_E_INVALID, "jkb_weight_upload", 0, 0, 0, "null argument");
+    *out = nullptr;
+    const Fmt *f = fmt_of(v->quant);
+    const char *nm = v->name ? v->name : "";
+    if (!f)
+        return fail(JKB_E_CAPABILITY, nm, v->offset, v->byte_len, v->byte_len,
+                    "unsupported tensor quant %s for the GEMV layout", quant_name(v->quant));
+    if (!v->data) return fail(JKB_E_INVALID, nm, v->offset, 0, 0, "null tensor data");
+    int rc = validate_matrix_view(v, f, rows, cols);
+    if (rc) return rc;
+
+    jkb_weight *w = new jkb_weight();
+    memset(w, 0, sizeof(*w));
+    w->magic = WEIGHT_MAGIC;
+    w->quant = v->quant;
+    w->rows = rows;
+    w->cols = cols;
+    w->nb = cols / (size_t)f->block_elems;
+    w->ndim = v->ndim;
+    for (uint32_t i = 0; i < v->ndim && i < 4; i++) w->shape[i] = v->shape[i];
+    snprintf(w->name, sizeof(w->name), "%s", nm);
+    w->offset = v->offset;
+    w->byte_len = v->byte_len;
+    w->gguf_bytes = storage_bytes(f, rows * cols);
+
+    size_t qp = 0, scp = 0;
+    bool has_d = false;
+    switch (v->quant) {
+    case JKB_Q4_0: qp = 16; has_d = true; w->gpu_format = GF_Q4_0; break;
+    case JKB_Q8_0: qp = 32; has_d = true; w->gpu_format = GF_Q8_0; break;
+    case JKB_Q4_K_M: qp = 128; scp = 16; w->gpu_format = GF_Q4_K; break;
+    case JKB_Q6_K: qp = 192; scp = 16; has_d = true; w->gpu_format = GF_Q6_K; break;
+    case JKB_TQ1_0:
+    case JKB_TQ2_0: qp = 64; has_d = true; w->gpu_format = GF_TQ2_0; break;
+    case JKB_I2_S: qp = 32; w->gpu_format = GF_I2_S; break;
+    }
+    Arena a;
+    size_t qs_bytes = rows * w->nb * qp, sc_bytes = rows * w->nb * scp,
+           d_bytes = has_d ? rows * w->nb * 2 : 0;
+    a.cap = Arena::round(qs_bytes) + Arena::round(sc_bytes) + Arena::round(d_bytes);
+    cudaError_t e = cudaMalloc(&a.base, a.cap);
+    if (e != cudaSuccess) {
+        delete w;
+        return fail_cuda(e, "jkb_weight_upload (device planes)");
+    }
+    w->base = a.base;
+    w->device_bytes = a.cap;
+    uint8_t *qs = a.take(qs_bytes);
+    uint8_t *sc = scp ? a.take(sc_bytes) : nullptr;
+    uint16_t *d = has_d ? (uint16_t *)a.take(d_bytes) : nullptr;
+    w->p.qs = qs;
+    w->p.qs_row = w->nb * qp;
+    w->p.sc = sc;
+    w->p.sc_row = w->nb * scp;
+    w->p.d = d;
+    size_t payload = rows * w->nb * (size_t)f->block_bytes;
+    if (v->quant == JKB_I2_S) w->p.i2s_scale = read_i2s_trailer(v, payload);
+
+    uint8_t *raw = nullptr;
+    bool owned = false;
+    rc = stage_raw(v, payload, st, &raw, &owned);
+    if (rc) {
+        cudaFree(a.base);
+        delete w;
+        return rc;
+    }
+    size_t n = rows * w->nb;
+    relayout_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+        v->quant, raw, rows, w->nb, w->nb * (size_t)f->block_bytes, f->block_bytes, qs,
+        w->p.qs_row, sc, w->p.sc_row, d);
+    rc = check_launch("relayout_kernel");
+    if (owned) {
+        cudaStreamSynchronize(st);
+        cudaFree(raw);
+    }
+    if (rc) {
+        cudaFree(a.base);
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return JKB_OK;
+}
+
+static int repacked_upload(const jkb_tensor_view *v, size_t rows, size_t cols, cudaStream_t st,
+                           jkb_repacked_weight **out) {
+    if (!v || !out)
+        return fail(JKB_E_INVALID, "jkb_repacked_weight", 0, 0, 0, "null argument");
+    *out = nullptr;
+    const char *nm = v->name ? v->name : "";
+    const Fmt *f = fmt_of(v->quant);
+    if (!f)
+        // Dense F32/F16/BF16 storage (RepackedStorage::DenseF32/DenseHalf) and the formats
+        // outside the hot path are not built on the GPU.
+        return fail(JKB_E_CAPABILITY, nm, v->offset, v->byte_len, v->byte_len,
+                    "unsupported tensor quant %s for repack", quant_name(v->quant));
+    if (!v->data) return fail(JKB_E_INVALID, nm, v->offset, 0, 0, "null tensor data");
+    int rc = validate_matrix_view(v, f, rows, cols);
+    if (rc) return rc;
+    jkb_repacked_weight *w = new jkb_repacked_weight();
+    memset(w, 0, sizeof(*w));
+    w->magic = REPACKED_MAGIC;
+    w->quant = v->quant;
+    w->rows = rows;
+    w->cols = cols;
+    w->k_pad = (cols + 31) / 32 * 32;
+    w->group_elems = v->quant == JKB_Q6_K ? 16 : 32;
+    w->scale_groups = w->k_pad / w->group_elems;
+    snprintf(w->name, sizeof(w->name), "%s", nm);
+    bool mins = v->quant == JKB_Q4_K_M;
+    Arena a;
+    size_t qb = rows * w->k_pad, sb = rows * w->scale_groups * 4;
+    a.cap = Arena::round(qb) + Arena::round(sb) * (mins ? 2 : 1);
+    cudaError_t e = cudaMalloc(&a.base, a.cap);
+    if (e != cudaSuccess) {
+        delete w;
+        return fail_cuda(e, "jkb_repacked_weight (device buffers)");
+    }
+    w->base = a.base;
+    w->device_bytes = a.cap;
+    w->q = (int8_t *)a.take(qb);
+    w->scales = (float *)a.take(sb);
+    w->mins = mins ? (float *)a.take(sb) : nullptr;
+    size_t nb = cols / (size_t)f->block_elems;
+    size_t payload = rows * nb * (size_t)f->block_bytes;
+    float i2s = v->quant == JKB_I2_S ? read_i2s_trailer(v, payload) : 0.0f;
+    uint8_t *raw = nullptr;
+    bool owned = false;
+    rc = stage_raw(v, payload, st, &raw, &owned);
+    if (rc) {
+        cudaFree(a.base);
+        delete w;
+        return rc;
+    }
+    cudaMemsetAsync(w->q, 0, qb, st);
+    size_t n = rows * nb;
+    repack_i8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+        v->quant, raw, rows, nb, nb * (size_t)f->block_bytes, f->block_bytes, i2s, w->q,
+        w->k_pad, w->scales, w->mins, w->scale_groups);
+    rc = check_launch("repack_i8_kernel");
+    if (owned) {
+        cudaStreamSynchronize(st);
+        cudaFree(raw);
+    }
+    if (rc) {
+        cudaFree(a.base);
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return JKB_OK;
+}
+
+}  // namespace jkb
+
+using namespace jkb;
+
+extern "C" {
+
+int jkb_weight_upload(const jkb_tensor_view *view, size_t rows, size_t cols, void *stream,
+                      jkb_weight **out) {
+    return weight_upload(view, rows, cols, as_stream(stream), out);
+}
+
+int jkb_weight_upload_infer(const jkb_tensor_view *view, void *stream, jkb_weight **out) {
+    if (!view || !out) return fail(JKB_E_INVALID, "jkb_weight_upload_infer", 0, 0, 0, "null");
+    const Fmt *f = fmt_of(view->quant);
+    if (!f)
+        return fail(JKB_E_CAPABILITY, view->name ? view->name : "", view->offset,
+                    view->byte_len, view->byte_len, "unsupported tensor quant %s",
+                    quant_name(view->quant));
+    size_t r = 0, c = 0;
+    int rc = infer_rows_cols(view, f, &r, &c);
+    if (rc) return rc;
+    return weight_upload(view, r, c, as_stream(stream), out);
+}
+
+int jkb_weight_destroy(jkb_weight *w) {
+    int rc = check_weight(w);
+    if (rc) return rc;
+    w->magic = 0;
+    cudaFree(w->base);
+    delete w;
+    return JKB_OK;
+}
+
+int jkb_weight_info(const jkb_weight *w, size_t *rows, size_t *cols, int32_t *quant,
+                    size_t *device_bytes, size_t *gguf_bytes) {
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (rows) *rows = w->rows;
+    if (cols) *cols = w->cols;
+    if (quant) *quant = w->quant;
+    if (device_bytes) *device_bytes = w->device_bytes;
+    if (gguf_bytes) *gguf_bytes = w->gguf_bytes;
+    return JKB_OK;
+}
+
+int jkb_repacked_weight_from_tensor(const jkb_tensor_view *view, size_t rows, size_t cols,
+                                    void *stream, jkb_repacked_weight **out) {
+    return repacked_upload(view, rows, cols, as_stream(stream), out);
+}
+
+int jkb_repacked_weight_repack(const jkb_tensor_view *view, void *stream,
+                               jkb_repacked_weight **out) {
+    if (!view || !out) return fail(JKB_E_INVALID, "jkb_repacked_weight_repack", 0, 0, 0, "null");
+    const Fmt *f = fmt_of(view->quant);
+    if (!f)
+        return fail(JKB_E_CAPABILITY, view->name ? view->name : "", view->offset,
+                    view->byte_len, view->byte_len, "unsupported tensor quant %s for repack",
+                    quant_name(view->quant));
+    size_t r = 0, c = 0;
+    int rc = infer_rows_cols(view, f, &r, &c);
+    if (rc) return rc;
+    return repacked_upload(view, r, c, as_stream(stream), out);
+}
+
+int jkb_repacked_weight_destroy(jkb_repacked_weight *w) {
+    if (!w || w->magic != REPACKED_MAGIC)
+        return fail(JKB_E_INVALID, "jkb_repacked_weight", 0, 0, 0, "null or destroyed handle");
+    w->magic = 0;
+    cudaFree(w->base);
+    delete w;
+    return JKB_OK;
+}
+
+int jkb_repacked_weight_buffers(const jkb_repacked_weight *w, size_t *rows, size_t *cols,
+                                int32_t *quant, size_t *scale_groups, int8_t **q,
+                                float **scales, float **mins) {
+    if (!w || w->magic != REPACKED_MAGIC)
+        return fail(JKB_E_INVALID, "jkb_repacked_weight", 0, 0, 0, "null or destroyed handle");
+    if (rows) *rows = w->rows;
+    if (cols) *cols = w->cols;
+    if (quant) *quant = w->quant;
+    if (scale_groups) *scale_groups = w->scale_groups;
+    if (q) *q = w->q;
+    if (scales) *scales = w->scales;
+    if (mins) *mins = w->mins;
+    return JKB_OK;
+}
+
+}  // extern "C"

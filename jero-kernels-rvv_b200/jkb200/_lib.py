@@ -1,0 +1,125 @@
+"""Loads libjkb200.so (the C ABI of include/jkb200.h) and declares its signatures.
+
+The shared object is built in-tree by ``jero-kernels-rvv_b200/Makefile`` (nvcc, sm_100a only).
+There is no fallback: if the library is missing, importing the package raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+ROOT_DIR = os.path.dirname(PKG_DIR)
+LIB_PATH = os.path.join(ROOT_DIR, "libjkb200.so")
+
+
+class jkb_tensor_view(C.Structure):
+    _fields_ = [
+        ("name", C.c_char_p),
+        ("quant", C.c_int32),
+        ("ndim", C.c_uint32),
+        ("shape", C.c_size_t * 4),
+        ("offset", C.c_size_t),
+        ("data", C.c_void_p),
+        ("byte_len", C.c_size_t),
+        ("data_on_device", C.c_int32),
+    ]
+
+
+class jkb_error_info(C.Structure):
+    _fields_ = [
+        ("status", C.c_int32),
+        ("tensor_name", C.c_char * 64),
+        ("offset", C.c_size_t),
+        ("byte_len", C.c_size_t),
+        ("buffer_len", C.c_size_t),
+        ("reason", C.c_char * 256),
+    ]
+
+
+P, S, I, F = C.c_void_p, C.c_size_t, C.c_int, C.c_float
+PP = C.POINTER(C.c_void_p)
+PS = C.POINTER(C.c_size_t)
+PI32 = C.POINTER(C.c_int32)
+
+# name -> argument types (every entry point returns int status unless listed in _RESTYPE)
+SIGNATURES = {
+    "jkb_abi_version": [],
+    "jkb_last_error": [],
+    "jkb_last_error_info": [C.POINTER(jkb_error_info)],
+    "jkb_clear_error": [],
+    "jkb_quantize_row_q8_0": [P, S, P, S, P],
+    "jkb_quantize_row_q8_0_f32": [P, S, P, S, P],
+    "jkb_quantize_row_q8_k": [P, S, P, S, P],
+    "jkb_quantize_rows_q8_0": [P, S, S, P, S, P],
+    "jkb_quantize_rows_q8_k": [P, S, S, P, S, P],
+    "jkb_subln_quantize_absmax_i8": [P, S, P, S, P, S, F, P, P],
+    "jkb_subln_quantize_absmax_i8_rows": [P, P, P, S, S, F, P, P],
+    "jkb_act_q8_create": [S, S, PP],
+    "jkb_act_q8_destroy": [P],
+    "jkb_act_q8_quantize": [P, P, S, S, S, P],
+    "jkb_act_q8_buffers": [P, PS, PS, PS, PP, PP, PP, PP, PP],
+    "jkb_weight_upload": [C.POINTER(jkb_tensor_view), S, S, P, PP],
+    "jkb_weight_upload_infer": [C.POINTER(jkb_tensor_view), P, PP],
+    "jkb_weight_destroy": [P],
+    "jkb_weight_info": [P, PS, PS, PI32, PS, PS],
+    "jkb_vec_dot_q4_0_q8_0": [P, S, P, S, P, P],
+    "jkb_vec_dot_q8_0_q8_0": [P, S, P, S, P, P],
+    "jkb_vec_dot_q4_k_q8_k": [P, S, P, S, P, P],
+    "jkb_vec_dot_q6_k_q8_k": [P, S, P, S, P, P],
+    "jkb_vec_dot_tq1_0_q8_k": [P, S, P, S, P, P],
+    "jkb_vec_dot_tq2_0_q8_k": [P, S, P, S, P, P],
+    "jkb_gemv_q4_0_q8_0": [P, S, P, P, S, P],
+    "jkb_gemv_q4_0_q8_0_4x": [P, S, P, P, S, P],
+    "jkb_gemv_q8_0_q8_0": [P, S, P, P, S, P],
+    "jkb_gemv_q8_0_q8_0_4x": [P, S, P, P, S, P],
+    "jkb_gemv_q4_k_q8_k": [P, S, P, P, S, P],
+    "jkb_gemv_q6_k_q8_k": [P, S, P, P, S, P],
+    "jkb_gemv_tq1_0_q8_k": [P, S, P, P, S, P],
+    "jkb_gemv_tq2_0_q8_k": [P, S, P, P, S, P],
+    "jkb_gemv_rows": [P, S, P, P, S, S, S, P],
+    "jkb_gemv_block_dots": [P, P, S, P, P, P, P],
+    "jkb_vec_dot_q4_k_m": [P, S, P, P, S, P],
+    "jkb_vec_dot_q8_0": [P, S, P, P, S, P],
+    "jkb_vec_dot_q6_k": [P, S, P, P, S, P],
+    "jkb_vec_dot_q4_0": [P, S, P, P, S, P],
+    "jkb_vec_dot_i2_s": [P, S, P, P, S, P],
+    "jkb_bitlinear_i8": [P, S, P, P, S, F, P],
+    "jkb_bitlinear_i8_rvv": [P, S, P, P, S, F, P],
+    "jkb_bitlinear_i8_ime": [P, S, P, P, S, F, P],
+    "jkb_bitlinear_i8_batch": [P, S, P, P, S, P, S, P],
+    "jkb_repacked_weight_from_tensor": [C.POINTER(jkb_tensor_view), S, S, P, PP],
+    "jkb_repacked_weight_repack": [C.POINTER(jkb_tensor_view), P, PP],
+    "jkb_repacked_weight_destroy": [P],
+    "jkb_repacked_weight_buffers": [P, PS, PS, PI32, PS, PP, PP, PP],
+    "jkb_gemm_repacked": [P, S, P, P, P],
+    "jkb_gemm_repacked_rows": [P, S, P, P, S, S, P],
+    "jkb_gemv_repacked": [P, S, P, P, P],
+    "jkb_gemv_repacked_rows": [P, S, P, P, S, S, P],
+    "jkb_gemm_repacked_f32": [P, S, P, P, S, S, P, P],
+}
+_RESTYPE = {"jkb_last_error": C.c_char_p, "jkb_clear_error": None}
+
+_lib = None
+
+
+def load() -> C.CDLL:
+    """Return the loaded ABI library; raise ImportError (no fallback) when it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `make -C {ROOT_DIR}` (nvcc, sm_100a). "
+            "jkb200 has no CPU fallback.")
+    lib = C.CDLL(LIB_PATH)
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RESTYPE.get(name, C.c_int)
+    _lib = lib
+    return lib
+
+
+def declared_symbols():
+    return list(SIGNATURES)

@@ -1,0 +1,575 @@
+"""Python mirror of the jero-kernels-rvv public API over the jkb200 C ABI.
+
+Names, argument meaning and error behaviour follow the Rust crate (file:line in each
+docstring). Device arguments are torch CUDA tensors; block activations are uint8 tensors
+holding packed BlockQ8_0 (36 B) / BlockQ8K (292 B) structs. Errors raise K3Error subclasses
+carrying the TensorBoundsError fields; nothing is launched when validation fails.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+
+import numpy as np
+import torch
+
+from . import _lib
+
+__all__ = [
+    "QuantType", "BLOCK", "BLOCK_Q8_0_BYTES", "BLOCK_Q8_K_BYTES", "K3Error", "TensorBoundsError",
+    "CapabilityMismatch", "CudaError", "InvalidHandle", "TensorView", "Weight", "RepackedWeight",
+    "QuantizedActQ8", "abi_version", "quantize_row_q8_0", "quantize_row_q8_0_f32",
+    "quantize_row_q8_k", "quantize_rows_q8_0", "quantize_rows_q8_k", "subln_quantize_absmax_i8",
+    "subln_quantize_absmax_i8_rows", "vec_dot_q4_0_q8_0", "vec_dot_q8_0_q8_0",
+    "vec_dot_q4_k_q8_k", "vec_dot_q6_k_q8_k", "vec_dot_tq1_0_q8_k", "vec_dot_tq2_0_q8_k",
+    "gemv_q4_0_q8_0", "gemv_q4_0_q8_0_4x", "gemv_q8_0_q8_0", "gemv_q8_0_q8_0_4x",
+    "gemv_q4_k_q8_k", "gemv_q6_k_q8_k", "gemv_tq1_0_q8_k", "gemv_tq2_0_q8_k", "gemv_rows",
+    "gemv_block_dots", "vec_dot_q4_k_m", "vec_dot_q8_0", "vec_dot_q6_k", "vec_dot_q4_0",
+    "vec_dot_i2_s", "bitlinear_i8", "bitlinear_i8_rvv", "bitlinear_i8_ime",
+    "bitlinear_i8_batch", "gemm_repacked", "gemm_repacked_rows", "gemv_repacked",
+    "gemv_repacked_rows", "gemm_repacked_f32", "empty_q8_0_blocks", "empty_q8_k_blocks",
+    "device_view",
+]
+
+
+class QuantType(enum.IntEnum):
+    """jero_core::QuantType codes used at the boundary (GGML type ids)."""
+    F32 = 0
+    F16 = 1
+    Q4_0 = 2
+    Q8_0 = 8
+    Q4_K_M = 12
+    Q6_K = 14
+    BF16 = 30
+    TQ1_0 = 34
+    TQ2_0 = 35
+    I2_S = 36
+
+
+# (block elements, block bytes) -- quant.rs:20-91, ime.rs:28-37, lib.rs:129-132
+BLOCK = {
+    QuantType.Q4_0: (32, 18), QuantType.Q8_0: (32, 34), QuantType.Q4_K_M: (256, 144),
+    QuantType.Q6_K: (256, 210), QuantType.TQ1_0: (256, 54), QuantType.TQ2_0: (256, 66),
+    QuantType.I2_S: (128, 32),
+}
+BLOCK_Q8_0_BYTES = 36
+BLOCK_Q8_K_BYTES = 292
+
+
+class K3Error(Exception):
+    """Mirror of jero_core::K3Error carrying the TensorBoundsError fields."""
+
+    def __init__(self, status, tensor_name, offset, byte_len, buffer_len, reason):
+        self.status = status
+        self.tensor_name = tensor_name
+        self.offset = offset
+        self.byte_len = byte_len
+        self.buffer_len = buffer_len
+        self.reason = reason
+        super().__init__(f"{type(self).__name__}{{tensor_name: {tensor_name!r}, offset: {offset}, "
+                         f"byte_len: {byte_len}, buffer_len: {buffer_len}, reason: {reason!r}}}")
+
+
+class TensorBoundsError(K3Error):
+    pass
+
+
+class CapabilityMismatch(K3Error):
+    pass
+
+
+class CudaError(K3Error):
+    pass
+
+
+class InvalidHandle(K3Error):
+    pass
+
+
+_STATUS = {1: TensorBoundsError, 2: CapabilityMismatch, 3: CudaError, 4: K3Error, 5: K3Error,
+           6: InvalidHandle}
+
+
+def _check(rc: int):
+    if rc == 0:
+        return
+    info = _lib.jkb_error_info()
+    L = _lib.load()
+    L.jkb_last_error_info(C.byref(info))
+    cls = _STATUS.get(rc, K3Error)
+    raise cls(rc, info.tensor_name.decode(errors="replace"), info.offset, info.byte_len,
+              info.buffer_len, info.reason.decode(errors="replace"))
+
+
+def _L():
+    return _lib.load()
+
+
+def abi_version() -> int:
+    return int(_L().jkb_abi_version())
+
+
+def _dptr(t):
+    """Device pointer of a CUDA tensor (must be contiguous)."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError("expected a CUDA torch.Tensor")
+    if not t.is_contiguous():
+        raise ValueError("tensor must be contiguous")
+    return t.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def _nblocks(t, block_bytes):
+    n = t.numel() * t.element_size()
+    if n % block_bytes:
+        raise ValueError(f"block buffer of {n} bytes is not a multiple of {block_bytes}")
+    return n // block_bytes
+
+
+class _CudaArray:
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 2,
+                                         "strides": None}
+
+
+def device_view(ptr: int, shape, dtype: str) -> torch.Tensor:
+    """Zero-copy torch view of library-owned device memory (handles' buffers)."""
+    return torch.as_tensor(_CudaArray(ptr, shape, np.dtype(dtype).str), device="cuda")
+
+
+def empty_q8_0_blocks(n: int, device="cuda") -> torch.Tensor:
+    return torch.empty(n * BLOCK_Q8_0_BYTES, dtype=torch.uint8, device=device)
+
+
+def empty_q8_k_blocks(n: int, device="cuda") -> torch.Tensor:
+    return torch.empty(n * BLOCK_Q8_K_BYTES, dtype=torch.uint8, device=device)
+
+
+# ------------------------------------------------------------------------------- TensorView
+
+class TensorView:
+    """jero_core::TensorView: name, quant, shape and the raw GGUF bytes (host or device)."""
+
+    def __init__(self, name: str, quant, shape, data, offset: int = 0):
+        self.name = name
+        self.quant = int(quant)
+        self.shape = tuple(int(s) for s in shape)
+        self.offset = int(offset)
+        if isinstance(data, torch.Tensor):
+            self._keep = data.contiguous()
+            self.on_device = self._keep.is_cuda
+            self.ptr = self._keep.data_ptr()
+            self.byte_len = self._keep.numel() * self._keep.element_size()
+        else:
+            self._keep = np.ascontiguousarray(data).view(np.uint8)
+            self.on_device = False
+            self.ptr = self._keep.ctypes.data
+            self.byte_len = self._keep.nbytes
+        self._name_b = name.encode()
+
+    def _c(self):
+        v = _lib.jkb_tensor_view()
+        v.name = self._name_b
+        v.quant = self.quant
+        v.ndim = len(self.shape)
+        for i, s in enumerate(self.shape[:4]):
+            v.shape[i] = s
+        v.offset = self.offset
+        v.data = self.ptr
+        v.byte_len = self.byte_len
+        v.data_on_device = 1 if self.on_device else 0
+        return v
+
+
+class Weight:
+    """Device-resident GEMV/BitLinear weight (validate + upload + relayout at load time).
+
+    ``Weight(view, rows, cols)`` follows RepackedWeight::from_tensor (repack.rs:2288);
+    ``Weight(view)`` infers the orientation like RepackedWeight::repack (repack.rs:2255).
+    """
+
+    def __init__(self, view: TensorView, rows=None, cols=None, stream=None):
+        h = C.c_void_p()
+        v = view._c()
+        if rows is None:
+            _check(_L().jkb_weight_upload_infer(C.byref(v), _stream(stream), C.byref(h)))
+        else:
+            _check(_L().jkb_weight_upload(C.byref(v), rows, cols, _stream(stream), C.byref(h)))
+        self._h = h.value
+        r, c, q = C.c_size_t(), C.c_size_t(), C.c_int32()
+        db, gb = C.c_size_t(), C.c_size_t()
+        _check(_L().jkb_weight_info(self._h, C.byref(r), C.byref(c), C.byref(q), C.byref(db),
+                                    C.byref(gb)))
+        self.rows, self.cols, self.quant = r.value, c.value, QuantType(q.value)
+        self.device_bytes, self.gguf_bytes = db.value, gb.value
+        self.name = view.name
+
+    @property
+    def handle(self):
+        if self._h is None:
+            raise InvalidHandle(6, self.name, 0, 0, 0, "weight destroyed")
+        return self._h
+
+    def destroy(self):
+        if getattr(self, "_h", None):
+            _L().jkb_weight_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+class QuantizedActQ8:
+    """Device QuantizedActQ8 (repack.rs:461-724) with a fixed capacity allocated up front."""
+
+    def __init__(self, m_capacity: int, k: int):
+        h = C.c_void_p()
+        _check(_L().jkb_act_q8_create(m_capacity, k, C.byref(h)))
+        self._h = h.value
+        self.m_capacity, self.k = m_capacity, k
+        self.k_padded = (k + 31) // 32 * 32
+
+    @classmethod
+    def quantize(cls, act: torch.Tensor, m: int, k: int, stream=None) -> "QuantizedActQ8":
+        """repack.rs:522 QuantizedActQ8::quantize."""
+        q = cls(max(m, 1), max(k, 1))
+        q.quantize_into(act, m, k, stream)
+        return q
+
+    def quantize_into(self, act: torch.Tensor, m: int, k: int, stream=None):
+        """repack.rs:542 QuantizedActQ8::quantize_into."""
+        _check(_L().jkb_act_q8_quantize(self._h, _dptr(act), act.numel(), m, k, _stream(stream)))
+
+    def buffers(self):
+        """Zero-copy device views: q, x_scales, x_sums, x_sums_16, super_scales (row-major)."""
+        m, k, kp = C.c_size_t(), C.c_size_t(), C.c_size_t()
+        ptrs = [C.c_void_p() for _ in range(5)]
+        _check(_L().jkb_act_q8_buffers(self._h, C.byref(m), C.byref(k), C.byref(kp),
+                                       *[C.byref(p) for p in ptrs]))
+        m, k, kp = m.value, k.value, kp.value
+        return (device_view(ptrs[0].value, (m, kp), "i1"),
+                device_view(ptrs[1].value, (m, kp // 32), "<f4"),
+                device_view(ptrs[2].value, (m, kp // 32), "<f4"),
+                device_view(ptrs[3].value, (m, kp // 16), "<f4"),
+                device_view(ptrs[4].value, (m, (k + 255) // 256), "<f4"))
+
+    def destroy(self):
+        if getattr(self, "_h", None):
+            _L().jkb_act_q8_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+class RepackedWeight:
+    """RepackedWeight (repack.rs:1124-1133): i8-expanded block-scaled weight for the GEMM."""
+
+    def __init__(self, handle, name):
+        self._h = handle
+        self.name = name
+        r, c, q, g = C.c_size_t(), C.c_size_t(), C.c_int32(), C.c_size_t()
+        _check(_L().jkb_repacked_weight_buffers(self._h, C.byref(r), C.byref(c), C.byref(q),
+                                                C.byref(g), None, None, None))
+        self.rows, self.cols, self.quant, self.scale_groups = r.value, c.value, QuantType(
+            q.value), g.value
+
+    @classmethod
+    def from_tensor(cls, view: TensorView, rows: int, cols: int, stream=None):
+        """repack.rs:2288 RepackedWeight::from_tensor."""
+        h = C.c_void_p()
+        v = view._c()
+        _check(_L().jkb_repacked_weight_from_tensor(C.byref(v), rows, cols, _stream(stream),
+                                                    C.byref(h)))
+        return cls(h.value, view.name)
+
+    @classmethod
+    def repack(cls, view: TensorView, stream=None):
+        """repack.rs:2255 RepackedWeight::repack."""
+        h = C.c_void_p()
+        v = view._c()
+        _check(_L().jkb_repacked_weight_repack(C.byref(v), _stream(stream), C.byref(h)))
+        return cls(h.value, view.name)
+
+    def buffers(self):
+        r, c, q, g = C.c_size_t(), C.c_size_t(), C.c_int32(), C.c_size_t()
+        pq, ps, pm = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        _check(_L().jkb_repacked_weight_buffers(self._h, C.byref(r), C.byref(c), C.byref(q),
+                                                C.byref(g), C.byref(pq), C.byref(ps),
+                                                C.byref(pm)))
+        kp = (c.value + 31) // 32 * 32
+        mins = device_view(pm.value, (r.value, g.value), "<f4") if pm.value else None
+        return (device_view(pq.value, (r.value, kp), "i1"),
+                device_view(ps.value, (r.value, g.value), "<f4"), mins)
+
+    def gemv(self, out, act, stream=None):
+        gemv_repacked(out, self, act, stream)
+
+    def gemv_rows(self, out, act, row_range, stream=None):
+        gemv_repacked_rows(out, self, act, row_range, stream)
+
+    def gemm(self, out, act, stream=None):
+        gemm_repacked(out, self, act, stream)
+
+    def gemm_rows(self, out, act, row_range, stream=None):
+        gemm_repacked_rows(out, self, act, row_range, stream)
+
+    def destroy(self):
+        if getattr(self, "_h", None):
+            _L().jkb_repacked_weight_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------------------- quantizers
+
+def quantize_row_q8_0(x, out, stream=None):
+    """quant_q8.rs:395 quantize_row_q8_0(x: &[f32], out: &mut [BlockQ8_0])."""
+    _check(_L().jkb_quantize_row_q8_0(_dptr(x), x.numel(), _dptr(out),
+                                      _nblocks(out, BLOCK_Q8_0_BYTES), _stream(stream)))
+
+
+def quantize_row_q8_0_f32(x, out, stream=None):
+    """quant_q8.rs:370 quantize_row_q8_0_f32."""
+    _check(_L().jkb_quantize_row_q8_0_f32(_dptr(x), x.numel(), _dptr(out),
+                                          _nblocks(out, BLOCK_Q8_0_BYTES), _stream(stream)))
+
+
+def quantize_row_q8_k(x, out, stream=None):
+    """quant_q8.rs:576 quantize_row_q8_k(x: &[f32], out: &mut [BlockQ8K])."""
+    _check(_L().jkb_quantize_row_q8_k(_dptr(x), x.numel(), _dptr(out),
+                                      _nblocks(out, BLOCK_Q8_K_BYTES), _stream(stream)))
+
+
+def quantize_rows_q8_0(x, m, k, out, stream=None):
+    _check(_L().jkb_quantize_rows_q8_0(_dptr(x), m, k, _dptr(out),
+                                       _nblocks(out, BLOCK_Q8_0_BYTES), _stream(stream)))
+
+
+def quantize_rows_q8_k(x, m, k, out, stream=None):
+    _check(_L().jkb_quantize_rows_q8_k(_dptr(x), m, k, _dptr(out),
+                                       _nblocks(out, BLOCK_Q8_K_BYTES), _stream(stream)))
+
+
+def subln_quantize_absmax_i8(out_i8, x, norm_weight, eps, scale_out, stream=None):
+    """lib.rs:1042 subln_quantize_absmax_i8 (the f32 scale lands in scale_out[0])."""
+    _check(_L().jkb_subln_quantize_absmax_i8(_dptr(out_i8), out_i8.numel(), _dptr(x), x.numel(),
+                                             _dptr(norm_weight), norm_weight.numel(), eps,
+                                             _dptr(scale_out), _stream(stream)))
+
+
+def subln_quantize_absmax_i8_rows(out_i8, x, norm_weight, m, length, eps, scales_out,
+                                  stream=None):
+    _check(_L().jkb_subln_quantize_absmax_i8_rows(_dptr(out_i8), _dptr(x), _dptr(norm_weight), m,
+                                                  length, eps, _dptr(scales_out),
+                                                  _stream(stream)))
+
+
+# ------------------------------------------------------------------------------- block dots
+
+def _vec_dot(fn, w_blocks, x_blocks, bb, result, stream):
+    _check(getattr(_L(), fn)(_dptr(w_blocks), w_blocks.numel() * w_blocks.element_size(),
+                             _dptr(x_blocks), _nblocks(x_blocks, bb), _dptr(result),
+                             _stream(stream)))
+
+
+def vec_dot_q4_0_q8_0(w_blocks, x_blocks, result, stream=None):
+    """quant_q8.rs:1463 (result: 1-element f32 device tensor)."""
+    _vec_dot("jkb_vec_dot_q4_0_q8_0", w_blocks, x_blocks, BLOCK_Q8_0_BYTES, result, stream)
+
+
+def vec_dot_q8_0_q8_0(w_blocks, x_blocks, result, stream=None):
+    """quant_q8.rs:1493."""
+    _vec_dot("jkb_vec_dot_q8_0_q8_0", w_blocks, x_blocks, BLOCK_Q8_0_BYTES, result, stream)
+
+
+def vec_dot_q4_k_q8_k(w_blocks, x_blocks, result, stream=None):
+    """quant_q8.rs:3019."""
+    _vec_dot("jkb_vec_dot_q4_k_q8_k", w_blocks, x_blocks, BLOCK_Q8_K_BYTES, result, stream)
+
+
+def vec_dot_q6_k_q8_k(w_blocks, x_blocks, result, stream=None):
+    """quant_q8.rs:3056."""
+    _vec_dot("jkb_vec_dot_q6_k_q8_k", w_blocks, x_blocks, BLOCK_Q8_K_BYTES, result, stream)
+
+
+def vec_dot_tq1_0_q8_k(w_blocks, x_blocks, result, stream=None):
+    """quant_q8.rs:3071."""
+    _vec_dot("jkb_vec_dot_tq1_0_q8_k", w_blocks, x_blocks, BLOCK_Q8_K_BYTES, result, stream)
+
+
+def vec_dot_tq2_0_q8_k(w_blocks, x_blocks, result, stream=None):
+    """quant_q8.rs:3086."""
+    _vec_dot("jkb_vec_dot_tq2_0_q8_k", w_blocks, x_blocks, BLOCK_Q8_K_BYTES, result, stream)
+
+
+# ------------------------------------------------------------------------------- GEMV
+
+def _gemv(fn, out, weights: Weight, x_blocks, bb, stream):
+    _check(getattr(_L(), fn)(_dptr(out), out.numel(), weights.handle, _dptr(x_blocks),
+                             _nblocks(x_blocks, bb), _stream(stream)))
+
+
+def gemv_q4_0_q8_0(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:1586 gemv_q4_0_q8_0(output, &TensorView, &[BlockQ8_0])."""
+    _gemv("jkb_gemv_q4_0_q8_0", out, weights, x_blocks, BLOCK_Q8_0_BYTES, stream)
+
+
+def gemv_q4_0_q8_0_4x(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:1612 alias."""
+    _gemv("jkb_gemv_q4_0_q8_0_4x", out, weights, x_blocks, BLOCK_Q8_0_BYTES, stream)
+
+
+def gemv_q8_0_q8_0(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:1670."""
+    _gemv("jkb_gemv_q8_0_q8_0", out, weights, x_blocks, BLOCK_Q8_0_BYTES, stream)
+
+
+def gemv_q8_0_q8_0_4x(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:1696 alias."""
+    _gemv("jkb_gemv_q8_0_q8_0_4x", out, weights, x_blocks, BLOCK_Q8_0_BYTES, stream)
+
+
+def gemv_q4_k_q8_k(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:3101."""
+    _gemv("jkb_gemv_q4_k_q8_k", out, weights, x_blocks, BLOCK_Q8_K_BYTES, stream)
+
+
+def gemv_q6_k_q8_k(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:3189."""
+    _gemv("jkb_gemv_q6_k_q8_k", out, weights, x_blocks, BLOCK_Q8_K_BYTES, stream)
+
+
+def gemv_tq1_0_q8_k(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:3221."""
+    _gemv("jkb_gemv_tq1_0_q8_k", out, weights, x_blocks, BLOCK_Q8_K_BYTES, stream)
+
+
+def gemv_tq2_0_q8_k(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:3250."""
+    _gemv("jkb_gemv_tq2_0_q8_k", out, weights, x_blocks, BLOCK_Q8_K_BYTES, stream)
+
+
+def _act_block_bytes(quant):
+    return BLOCK_Q8_0_BYTES if quant in (QuantType.Q4_0, QuantType.Q8_0) else BLOCK_Q8_K_BYTES
+
+
+def gemv_rows(out, weights: Weight, x_blocks, row_range, stream=None):
+    """Row-sliced GEMV (the gemv_repacked_rows split, repack.rs:4014)."""
+    r0, r1 = row_range.start, row_range.stop
+    _check(_L().jkb_gemv_rows(_dptr(out), out.numel(), weights.handle, _dptr(x_blocks),
+                              _nblocks(x_blocks, _act_block_bytes(weights.quant)), r0, r1,
+                              _stream(stream)))
+
+
+def gemv_block_dots(weights: Weight, x_blocks, stream=None):
+    """Per-(row, block) integer sums and f32 block values of the GEMV kernels."""
+    nb = weights.cols // BLOCK[weights.quant][0]
+    sumi = torch.empty((weights.rows, nb), dtype=torch.int32, device="cuda")
+    mins = torch.empty((weights.rows, nb), dtype=torch.int32, device="cuda")
+    vals = torch.empty((weights.rows, nb), dtype=torch.float32, device="cuda")
+    _check(_L().jkb_gemv_block_dots(weights.handle, _dptr(x_blocks),
+                                    _nblocks(x_blocks, _act_block_bytes(weights.quant)),
+                                    _dptr(sumi), _dptr(mins), _dptr(vals), _stream(stream)))
+    return sumi, mins, vals
+
+
+def _vk(fn, out, weights, x, stream):
+    _check(getattr(_L(), fn)(_dptr(out), out.numel(), weights.handle, _dptr(x), x.numel(),
+                             _stream(stream)))
+
+
+def vec_dot_q4_k_m(out, weights, x, stream=None):
+    """lib.rs:157 VectorKernel::vec_dot_q4_k_m (f32 activations)."""
+    _vk("jkb_vec_dot_q4_k_m", out, weights, x, stream)
+
+
+def vec_dot_q8_0(out, weights, x, stream=None):
+    """quant.rs:1069."""
+    _vk("jkb_vec_dot_q8_0", out, weights, x, stream)
+
+
+def vec_dot_q6_k(out, weights, x, stream=None):
+    """quant.rs:1089."""
+    _vk("jkb_vec_dot_q6_k", out, weights, x, stream)
+
+
+def vec_dot_q4_0(out, weights, x, stream=None):
+    """quant.rs:1458."""
+    _vk("jkb_vec_dot_q4_0", out, weights, x, stream)
+
+
+def vec_dot_i2_s(out, weights, x, stream=None):
+    """quant.rs:2199."""
+    _vk("jkb_vec_dot_i2_s", out, weights, x, stream)
+
+
+# ------------------------------------------------------------------------------- BitLinear
+
+def bitlinear_i8(out, weights, act_i8, act_scale: float, stream=None):
+    """ime.rs:882 bitlinear_i8_rvv / :1005 bitlinear_i8_ime."""
+    _check(_L().jkb_bitlinear_i8(_dptr(out), out.numel(), weights.handle, _dptr(act_i8),
+                                 act_i8.numel(), float(act_scale), _stream(stream)))
+
+
+bitlinear_i8_rvv = bitlinear_i8
+bitlinear_i8_ime = bitlinear_i8
+
+
+def bitlinear_i8_batch(out, weights, act_i8, act_scales, stream=None):
+    _check(_L().jkb_bitlinear_i8_batch(_dptr(out), out.numel(), weights.handle, _dptr(act_i8),
+                                       act_i8.numel(), _dptr(act_scales), act_scales.numel(),
+                                       _stream(stream)))
+
+
+# ------------------------------------------------------------------------------- GEMM
+
+def gemm_repacked(out, weights: RepackedWeight, act: QuantizedActQ8, stream=None):
+    """repack.rs:4073."""
+    _check(_L().jkb_gemm_repacked(_dptr(out), out.numel(), weights._h, act._h, _stream(stream)))
+
+
+def gemm_repacked_rows(out, weights, act, row_range, stream=None):
+    """repack.rs:4087."""
+    _check(_L().jkb_gemm_repacked_rows(_dptr(out), out.numel(), weights._h, act._h,
+                                       row_range.start, row_range.stop, _stream(stream)))
+
+
+def gemv_repacked(out, weights, act, stream=None):
+    """repack.rs:3999."""
+    _check(_L().jkb_gemv_repacked(_dptr(out), out.numel(), weights._h, act._h, _stream(stream)))
+
+
+def gemv_repacked_rows(out, weights, act, row_range, stream=None):
+    """repack.rs:4014."""
+    _check(_L().jkb_gemv_repacked_rows(_dptr(out), out.numel(), weights._h, act._h,
+                                       row_range.start, row_range.stop, _stream(stream)))
+
+
+def gemm_repacked_f32(out, weights, x, m, scratch: QuantizedActQ8, stream=None):
+    """repack.rs:4129 (the caller supplies the QuantizedActQ8 scratch handle)."""
+    _check(_L().jkb_gemm_repacked_f32(_dptr(out), out.numel(), weights._h, _dptr(x), x.numel(),
+                                      m, scratch._h, _stream(stream)))

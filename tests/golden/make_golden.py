@@ -1,0 +1,149 @@
+"""Generates the committed golden fixtures under tests/golden/.
+
+kats.json -- known-answer tests restated from the jero-kernels-rvv test suite. The Rust crate
+cannot be built in this environment (no cargo/rustc, its jero-core dependency is not vendored),
+so the expected values are the ones its tests assert, written here as data with the file:line
+of each assertion. Block bytes are hex strings.
+
+oracle_fixtures.npz -- small seeded cases (every covered format, ragged row counts) evaluated
+by the CPU oracle (oracle/jkb_oracle.c): weights, quantized activations, per-block integer
+sums, block values and row outputs. The GPU tests compare against these fixed arrays, and the
+CPU tests re-derive them from the live oracle so an oracle change cannot go unnoticed.
+
+Run: python tests/golden/make_golden.py
+"""
+import json
+import os
+import struct
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+
+def h16(v):
+    return struct.pack("<H", v)
+
+
+def kats():
+    out = {}
+    # quant.rs:2593-2629: Q8_0 d = 2.0 (0x4000), quants 1..=32, input ones -> 1056.
+    blk = h16(0x4000) + bytes(range(1, 33))
+    out["q8_0_vec_dot_f32"] = {"ref": "src/quant.rs:2593-2629", "quant": 8, "rows": 1,
+                               "cols": 32, "block_hex": blk.hex(), "input": [1.0] * 32,
+                               "expected": [1056.0], "abs_tol": 1e-4}
+    # quant.rs:2632-2663: Q6_K d = 1.0, scales 1, ql 0x22, qh 0 -> every element -30,
+    # dot with ones = -7680.
+    blk = bytes([0x22] * 128) + bytes(64) + bytes([1] * 16) + h16(0x3C00)
+    out["q6_k_vec_dot_f32"] = {"ref": "src/quant.rs:2632-2663", "quant": 14, "rows": 1,
+                               "cols": 256, "block_hex": blk.hex(), "input": [1.0] * 256,
+                               "expected": [-7680.0], "abs_tol": 1e-3,
+                               "dequant_each": -30.0}
+    # quant.rs:2727-2748: Q4_0 d = 0.5, nibbles lo 0xA (+2) hi 0x5 (-3), input 2s -> -16.
+    blk = h16(0x3800) + bytes([0x5A] * 16)
+    out["q4_0_vec_dot_f32"] = {"ref": "src/quant.rs:2727-2748", "quant": 2, "rows": 1,
+                               "cols": 32, "block_hex": blk.hex(), "input": [2.0] * 32,
+                               "expected": [-16.0], "abs_tol": 1e-4,
+                               "dequant_lo": 1.0, "dequant_hi": -1.5}
+    # lib.rs:1365-1396: two Q4_K_M blocks, d = 1.0, dmin = 0, scales[0..4] = 1, nibbles
+    # lo = blk+1, hi = blk+2, shape [256, 2]; the test asserts out[0] > 0 and out[1] > out[0].
+    # With sc[0..4] = 1 and sc[4..8] = 0 the exact values are 2*(32*1+32*2) = 192 and
+    # 2*(32*2+32*3) = 320.
+    raw = b""
+    for b in range(2):
+        blk = h16(0x3C00) + h16(0x0000) + bytes([1, 1, 1, 1]) + bytes(8)
+        blk += bytes([((b + 2) << 4) | (b + 1)] * 128)
+        raw += blk
+    out["q4_k_m_two_block"] = {"ref": "src/lib.rs:1365-1396", "quant": 12, "shape": [256, 2],
+                               "rows": 2, "cols": 256, "block_hex": raw.hex(),
+                               "input": [1.0] * 256, "expected": [192.0, 320.0],
+                               "abs_tol": 1e-4}
+    # tests/empirical_challenge_m3_bitnet.rs:512-575: trit KATs.
+    out["tq1_0_trits"] = {"ref": "tests/empirical_challenge_m3_bitnet.rs:512-556",
+                          "cases": [{"fill": 0, "last": 0, "value": -1},
+                                    {"fill": 121, "last": 1, "value": 0},
+                                    {"fill": 242, "last": 2, "value": 1}],
+                          "scale_hex": "003c", "scale": 1.0}
+    out["tq2_0_trits"] = {"ref": "tests/empirical_challenge_m3_bitnet.rs:558-575",
+                          "cases": [{"fill": 0x00, "value": -1}, {"fill": 0x55, "value": 0},
+                                    {"fill": 0xAA, "value": 1}],
+                          "scale_hex": "003c", "scale": 1.0}
+    # tests/empirical_challenge_m3_bitnet.rs:39-163: SubLN absmax quantizer edge cases.
+    out["subln"] = {
+        "ref": "tests/empirical_challenge_m3_bitnet.rs:39-163,165-201",
+        "len": 256, "eps": 1e-5,
+        "cases": [
+            {"name": "all_zero", "input": "zeros", "weight": "ones", "scale": 1.0 / 127.0,
+             "q": 0},
+            {"name": "zero_weight", "input": "iota1", "weight": "zeros", "scale": 1.0 / 127.0,
+             "q": 0},
+            {"name": "large_pos", "input": "const:1e6", "weight": "ones",
+             "scale_approx": 1.0 / 127.0, "q": 127},
+            {"name": "large_neg", "input": "const:-1e6", "weight": "ones",
+             "scale_approx": 1.0 / 127.0, "q": -127},
+            {"name": "alternating", "input": "alt:2.5", "weight": "ones",
+             "scale_approx": 1.0 / 127.0, "q_even": 127, "q_odd": -127},
+            {"name": "heterogeneous", "input": "ones", "weight": "alt_w:0.5:-2.0",
+             "scale_approx": 2.0 / 127.0, "q_even": 32, "q_odd": -127},
+            {"name": "nan", "input": "ones_nan13", "weight": "ones", "scale": 1.0 / 127.0,
+             "q": 0},
+            {"name": "inf", "input": "ones_inf42", "weight": "ones", "scale": 1.0 / 127.0,
+             "q": 0},
+            {"name": "tiny", "input": "const:1e-20", "weight": "ones", "q": 0},
+        ]}
+    # quant_q8.rs:3414-3482: quantizer sanitization on test_f32_row inputs.
+    out["q8_sanitize"] = {"ref": "src/quant_q8.rs:3388-3395,3414-3482"}
+    return out
+
+
+def test_f32_row(n, seed):
+    """quant_q8.rs:3388-3395 generator: ((i*37 + seed*13) % 29 - 14) * 0.125."""
+    return np.array([(((i * 37 + seed * 13) % 29) - 14) * 0.125 for i in range(n)], np.float32)
+
+
+def fixtures():
+    import pyoracle as O
+
+    data = {}
+    cases = [
+        ("q4_0", O.Q4_0, 5, 256), ("q4_0_b", O.Q4_0, 17, 1024),
+        ("q8_0", O.Q8_0, 5, 256), ("q8_0_b", O.Q8_0, 33, 512),
+        ("q4_k", O.Q4_K, 5, 512), ("q4_k_b", O.Q4_K, 19, 1024),
+        ("q6_k", O.Q6_K, 5, 512), ("q6_k_b", O.Q6_K, 21, 768),
+        ("tq2_0", O.TQ2_0, 7, 512),
+    ]
+    for name, q, rows, cols in cases:
+        seed = sum(map(ord, name))
+        if q == O.TQ2_0:
+            t = O.ternary(rows * cols, 0x5EED0000 + seed)
+            w = O.pack_ternary(q, t, rows, cols, 0.0125)
+        else:
+            W = O.normal(rows * cols, 0x5EED0000 + seed, 0.02)
+            w = O.quantize_weights(q, W, rows, cols)
+        x = O.normal(cols, 0xAC70000 + seed, 1.0)
+        xq = O.quantize_act(q, x)
+        sumi, summins, contrib = O.block_dots(q, w, rows, cols, xq)
+        y = O.gemv(q, w, rows, cols, xq)
+        data[f"{name}__meta"] = np.array([q, rows, cols], np.int64)
+        data[f"{name}__w"] = w
+        data[f"{name}__x"] = x
+        data[f"{name}__xq"] = xq.view(np.uint8).reshape(-1)
+        data[f"{name}__sumi"] = sumi
+        data[f"{name}__summins"] = summins
+        data[f"{name}__contrib"] = contrib
+        data[f"{name}__y"] = y
+    return data
+
+
+def main():
+    with open(os.path.join(HERE, "kats.json"), "w") as f:
+        json.dump(kats(), f, indent=1)
+    np.savez_compressed(os.path.join(HERE, "oracle_fixtures.npz"), **fixtures())
+    print("wrote kats.json and oracle_fixtures.npz")
+
+
+if __name__ == "__main__":
+    main()

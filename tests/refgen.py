@@ -1,0 +1,167 @@
+"""Input generators and metrics restated from the jero-kernels-rvv test suite.
+
+These are test data generators (not arithmetic under test); each cites the Rust test it
+restates so the parity tests here can apply the same properties as the crate's own tests.
+"""
+import numpy as np
+
+MASK64 = (1 << 64) - 1
+LCG_A = 6364136223846793005
+LCG_C = 1442695040888963407
+
+
+def lcg_seq(seed: int, n: int) -> np.ndarray:
+    """Successive states of lcg_next (tests/wave4_quant_gemv_and_argmax.rs:31-36):
+    s = s * 6364136223846793005 + 1442695040888963407 (mod 2^64), returned after each step.
+    Vectorised by leapfrogging blocks of B steps."""
+    B = 4096
+    first = np.empty(min(n, B), np.uint64)
+    s = seed & MASK64
+    for i in range(first.size):
+        s = (s * LCG_A + LCG_C) & MASK64
+        first[i] = s
+    if n <= B:
+        return first
+    # s_{k+B} = A s_k + C with A = a^B, C = c (a^{B-1} + ... + 1)
+    A, Cc = 1, 0
+    for _ in range(B):
+        A, Cc = (A * LCG_A) & MASK64, (Cc * LCG_A + LCG_C) & MASK64
+    out = np.empty(((n + B - 1) // B) * B, np.uint64)
+    out[:B] = first
+    A64, C64 = np.uint64(A), np.uint64(Cc)
+    with np.errstate(over="ignore"):
+        for k in range(1, out.size // B):
+            out[k * B:(k + 1) * B] = out[(k - 1) * B:k * B] * A64 + C64
+    return out[:n]
+
+
+def gen_activation(n: int, seed: int) -> np.ndarray:
+    """tests/wave4_quant_gemv_and_argmax.rs:38-48."""
+    s = lcg_seq(seed, n)
+    r = ((s >> np.uint64(32)).astype(np.uint32)).astype(np.float32) / np.float32(4294967295.0)
+    i = np.arange(n, dtype=np.float32)
+    return ((r - np.float32(0.35)) * np.float32(1.4) +
+            np.sin(i * np.float32(0.013)).astype(np.float32) * np.float32(0.2)).astype(np.float32)
+
+
+def test_f32_row(n: int, seed: int) -> np.ndarray:
+    """src/quant_q8.rs:3388-3395."""
+    i = np.arange(n)
+    return ((((i * 37 + seed * 13) % 29) - 14) * 0.125).astype(np.float32)
+
+
+def _hi32(s):
+    return (s >> np.uint64(32))
+
+
+def fill_q4_0_bytes(rows, cols, seed):
+    """tests/wave4_quant_gemv_and_argmax.rs:77-96."""
+    nb = cols // 32
+    s = lcg_seq(seed, rows * nb * 32).reshape(rows, nb, 16, 2)
+    lo = (_hi32(s[..., 0]) % np.uint64(16)).astype(np.uint8)
+    hi = ((s[..., 1] >> np.uint64(40)) % np.uint64(16)).astype(np.uint8)
+    scales = np.array([0x3000, 0x3200, 0x3400, 0x3600], np.uint16)
+    r = np.arange(rows)[:, None]
+    b = np.arange(nb)[None, :]
+    sc = scales[(r + b) % 4]
+    out = np.zeros((rows, nb, 18), np.uint8)
+    out[..., 0:2] = sc[..., None].view(np.uint8).reshape(rows, nb, 2)
+    out[..., 2:] = (hi << 4) | lo
+    return out.reshape(-1)
+
+
+def fill_q8_0_bytes(rows, cols, seed):
+    """tests/wave4_quant_gemv_and_argmax.rs:118-135."""
+    nb = cols // 32
+    s = lcg_seq(seed, rows * nb * 32).reshape(rows, nb, 32)
+    q = ((_hi32(s) % np.uint64(127)).astype(np.int16) - 63).astype(np.int8)
+    scales = np.array([0x2800, 0x2C00, 0x3000, 0x3200], np.uint16)
+    r = np.arange(rows)[:, None]
+    b = np.arange(nb)[None, :]
+    sc = scales[(r + b) % 4]
+    out = np.zeros((rows, nb, 34), np.uint8)
+    out[..., 0:2] = sc[..., None].view(np.uint8).reshape(rows, nb, 2)
+    out[..., 2:] = q.view(np.uint8)
+    return out.reshape(-1)
+
+
+def fill_q4_k_m_bytes(rows, cols, seed):
+    """tests/wave4_quant_gemv_and_argmax.rs:137-154."""
+    nb = cols // 256
+    s = lcg_seq(seed, rows * nb * 140).reshape(rows, nb, 140)
+    out = np.zeros((rows, nb, 144), np.uint8)
+    out[..., 0:2] = np.frombuffer(np.uint16(0x3000).tobytes(), np.uint8)
+    out[..., 2:4] = np.frombuffer(np.uint16(0x2800).tobytes(), np.uint8)
+    out[..., 4:16] = (_hi32(s[..., :12]) % np.uint64(31) + np.uint64(1)).astype(np.uint8)
+    out[..., 16:] = (_hi32(s[..., 12:]) & np.uint64(0xFF)).astype(np.uint8)
+    return out.reshape(-1)
+
+
+def fill_q6_k_bytes(rows, cols, seed):
+    """tests/wave4_quant_gemv_and_argmax.rs:175-192."""
+    nb = cols // 256
+    s = lcg_seq(seed, rows * nb * 208).reshape(rows, nb, 208)
+    out = np.zeros((rows, nb, 210), np.uint8)
+    out[..., 0:192] = (_hi32(s[..., :192]) & np.uint64(0xFF)).astype(np.uint8)
+    out[..., 192:208] = ((_hi32(s[..., 192:]) % np.uint64(15)).astype(np.int16) - 7).astype(
+        np.int8).view(np.uint8)
+    out[..., 208:210] = np.frombuffer(np.uint16(0x3000).tobytes(), np.uint8)
+    return out.reshape(-1)
+
+
+def fill_tq1_0_bytes(rows, cols, seed):
+    """tests/wave4_quant_gemv_and_argmax.rs:194-209."""
+    nb = cols // 256
+    s = lcg_seq(seed, rows * nb * 52).reshape(rows, nb, 52)
+    out = np.zeros((rows, nb, 54), np.uint8)
+    out[..., 0:2] = np.frombuffer(np.uint16(0x3400).tobytes(), np.uint8)
+    out[..., 2:] = (_hi32(s) % np.uint64(243)).astype(np.uint8)
+    return out.reshape(-1)
+
+
+def fill_tq2_0_bytes(rows, cols, seed):
+    """tests/wave4_quant_gemv_and_argmax.rs:211-226."""
+    nb = cols // 256
+    s = lcg_seq(seed, rows * nb * 64).reshape(rows, nb, 64)
+    out = np.zeros((rows, nb, 66), np.uint8)
+    out[..., 0:2] = np.frombuffer(np.uint16(0x3400).tobytes(), np.uint8)
+    out[..., 2:] = (_hi32(s) & np.uint64(0xFF)).astype(np.uint8)
+    return out.reshape(-1)
+
+
+def cosine(a, b) -> float:
+    """tests/wave4_quant_gemv_and_argmax.rs:50-65 (f64 accumulation)."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(a @ b / (np.sqrt(a @ a) * np.sqrt(b @ b)))
+
+
+def l2_rel_err(got, ref) -> float:
+    """tests/wave4_quant_gemv_and_argmax.rs:67-75."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    return float(np.sqrt(((got - ref) ** 2).sum()) / np.sqrt((ref ** 2).sum()))
+
+
+def ref_matvec(oracle, quant, w, rows, cols, x) -> np.ndarray:
+    """ref_matvec_blocks (tests/wave4_quant_gemv_and_argmax.rs:228-251): f64 sum over the
+    dequantized blocks (the dequantizers are the oracle's restatement of quant.rs/lib.rs)."""
+    deq = oracle.dequantize_rows(quant, w, rows, cols).astype(np.float64)
+    return (deq @ np.asarray(x, np.float64)).astype(np.float32)
+
+
+def dequant_q8(xq) -> np.ndarray:
+    """dequantize_q8_k_row (tests/wave4_quant_gemv_and_argmax.rs:350-358) and its Q8_0 twin."""
+    return (xq["qs"].astype(np.float32) * xq["d"][:, None]).reshape(-1)
+
+
+def gemv_tolerance_ok(got, oracle_out, contrib, rel=1e-5):
+    """f32 outputs: the GPU sums a row's (bit-exact) block values in a different order than
+    the reference's sequential loop, so each output may differ by rounding only. Bound per
+    element: |got - ref| <= rel * sum_b |block value_b| (+ the smallest normal), and the
+    vector-level l2 relative error must stay under rel."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(oracle_out, np.float64)
+    bound = rel * np.abs(np.asarray(contrib, np.float64)).sum(axis=-1) + 1.2e-38
+    ok = np.abs(got - ref) <= bound
+    return bool(ok.all()), float(np.max(np.abs(got - ref) / bound))

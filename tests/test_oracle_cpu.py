@@ -1,0 +1,298 @@
+"""Pins the CPU oracle (oracle/jkb_oracle.c) to the jero-kernels-rvv test suite: its
+known-answer tests, exhaustive decode tests, sanitization cases and the tolerance contracts of
+its GEMV/GEMM tests, plus the committed golden fixtures. CPU only."""
+import json
+import os
+import struct
+
+import numpy as np
+import pytest
+
+import refgen as R
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+@pytest.fixture(scope="module")
+def kats():
+    with open(os.path.join(GOLDEN, "kats.json")) as f:
+        return json.load(f)
+
+
+def _u8(hexs):
+    return np.frombuffer(bytes.fromhex(hexs), np.uint8).copy()
+
+
+@pytest.mark.parametrize("name", ["q8_0_vec_dot_f32", "q6_k_vec_dot_f32", "q4_0_vec_dot_f32",
+                                  "q4_k_m_two_block"])
+def test_vec_dot_f32_kats(oracle, kats, name):
+    k = kats[name]
+    w = _u8(k["block_hex"])
+    out = oracle.vec_dot_f32(k["quant"], w, k["rows"], k["cols"], np.array(k["input"], np.float32))
+    assert np.allclose(out, k["expected"], atol=k["abs_tol"], rtol=0), (name, out)
+    if name == "q6_k_vec_dot_f32":
+        assert np.all(oracle.dequantize_block(14, w) == -30.0)
+    if name == "q4_0_vec_dot_f32":
+        d = oracle.dequantize_block(2, w)
+        assert np.all(d[:16] == 1.0) and np.all(d[16:] == -1.5)
+    if name == "q4_k_m_two_block":  # lib.rs:1393-1395
+        assert out[0] > 0.0 and out[1] > out[0]
+
+
+def test_zero_scale_block_dequantizes_to_zero(oracle):
+    """quant.rs:2614-2618: all-zero Q8_0 block (d = 0) dequantizes to 0."""
+    assert np.all(oracle.dequantize_block(8, np.zeros(34, np.uint8)) == 0.0)
+
+
+def test_tq_trit_kats(oracle, kats):
+    for c in kats["tq1_0_trits"]["cases"]:
+        blk = np.full(54, c["fill"], np.uint8)
+        blk[0:2] = [0x00, 0x3C]
+        blk[53] = c["last"]
+        assert np.all(oracle.dequantize_block(34, blk) == c["value"])
+    for c in kats["tq2_0_trits"]["cases"]:
+        blk = np.full(66, c["fill"], np.uint8)
+        blk[0:2] = [0x00, 0x3C]
+        assert np.all(oracle.dequantize_block(35, blk) == c["value"])
+    # out-of-range base-3 bytes stay in {-1, 0, 1} (bitnet.rs:544-556)
+    for bad in range(243, 256):
+        blk = np.full(54, bad, np.uint8)
+        blk[0:2] = [0x00, 0x3C]
+        assert set(np.unique(oracle.dequantize_block(34, blk))) <= {-1.0, 0.0, 1.0}
+
+
+def test_exhaustive_tq1_0_base3_decode(oracle):
+    """tests/empirical_challenge_m3_bitlinear.rs:65-135 (scale 1.0, one byte set at a time)."""
+    for val in range(256):
+        exp = []
+        b = val
+        for _ in range(5):
+            exp.append(b % 3 - 1)
+            b //= 3
+        for chunk in (0, 17, 50):
+            blk = np.zeros(54, np.uint8)
+            blk[0:2] = [0x00, 0x3C]
+            blk[2 + chunk] = val
+            out = oracle.dequantize_block(34, blk)
+            assert list(out[chunk * 5:chunk * 5 + 5]) == exp
+            mask = np.ones(256, bool)
+            mask[chunk * 5:chunk * 5 + 5] = False
+            assert np.all(out[mask] == -1.0)
+        blk = np.zeros(54, np.uint8)
+        blk[0:2] = [0x00, 0x3C]
+        blk[53] = val
+        assert oracle.dequantize_block(34, blk)[255] == val % 3 - 1
+
+
+def test_exhaustive_tq2_0_2bit_decode(oracle):
+    """tests/empirical_challenge_m3_bitlinear.rs:141-181 (scale 2.5)."""
+    for val in range(256):
+        exp = [((val >> (2 * j)) & 3) - 1 for j in range(4)]
+        for idx in (0, 31, 63):
+            blk = np.zeros(66, np.uint8)
+            blk[0:2] = [0x00, 0x41]
+            blk[2 + idx] = val
+            out = oracle.dequantize_block(35, blk) / 2.5
+            assert list(out[4 * idx:4 * idx + 4]) == exp
+            mask = np.ones(256, bool)
+            mask[4 * idx:4 * idx + 4] = False
+            assert np.all(out[mask] == -1.0)
+
+
+def test_f16_exhaustive(oracle):
+    """tests/wave1_rope_swiglu_fidelity.rs:186-246: every f16 bit pattern; finite values match
+    IEEE bit for bit, non-finite ones decode to Inf/NaN and clamp to +0.0 in the finite form."""
+    L = oracle.lib()
+    bits = np.arange(65536, dtype=np.uint16)
+    ieee = np.array([L.or_f16_to_f32_ieee(int(b)) for b in bits], np.float32)
+    fin = np.array([L.or_f16_to_f32_finite(int(b)) for b in bits], np.float32)
+    np_ref = bits.view(np.float16).astype(np.float32)
+    finite = np.isfinite(np_ref)
+    assert np.array_equal(ieee[finite].view(np.uint32), np_ref[finite].view(np.uint32))
+    assert np.array_equal(fin[finite].view(np.uint32), np_ref[finite].view(np.uint32))
+    assert np.all(fin[~finite].view(np.uint32) == 0)
+    inf = np.isinf(np_ref)
+    assert np.all(np.isinf(ieee[inf])) and np.all(np.isnan(ieee[np.isnan(np_ref)]))
+
+
+def test_q8_quantizer_sanitization(oracle):
+    """src/quant_q8.rs:3414-3482 restated on the oracle."""
+    with pytest.raises(ValueError):
+        oracle.quantize_row_q8_0(np.zeros(31, np.float32))
+    x96 = R.test_f32_row(96, 1)
+    x96[3] = np.nan
+    x96[11] = -np.nan
+    x96[32 + 7] = np.inf
+    x96[32 + 19] = -np.inf
+    x96[64:96] = np.nan
+    x96[64] = np.inf
+    x96[95] = 0.0
+    q = oracle.quantize_row_q8_0(x96)
+    assert q[0]["d"] > 0 and q[0]["qs"][3] == 0 and q[0]["qs"][11] == 0
+    assert np.any(q[0]["qs"] != 0)
+    assert q[1]["d"] > 0 and q[1]["qs"][7] == 0 and q[1]["qs"][19] == 0
+    assert q[2]["d"] == 0 and np.all(q[2]["qs"] == 0)
+    x768 = R.test_f32_row(768, 2)
+    x768[3] = np.nan
+    x768[16 + 9] = -np.nan
+    x768[256 + 5] = -np.inf
+    x768[256 + 37] = np.inf
+    x768[512:768] = np.nan
+    x768[512] = -np.inf
+    k = oracle.quantize_row_q8_k(x768)
+    assert k[0]["d"] > 0 and k[0]["qs"][3] == 0 and k[0]["qs"][25] == 0
+    assert k[1]["d"] > 0 and k[1]["qs"][5] == 0 and k[1]["qs"][37] == 0
+    assert k[2]["d"] == 0 and np.all(k[2]["qs"] == 0) and np.all(k[2]["bsums"] == 0)
+    for blk in k:
+        assert np.array_equal(blk["bsums"], blk["qs"].reshape(16, 16).astype(np.int32).sum(1))
+
+
+def _subln_input(spec, n):
+    if spec == "zeros":
+        return np.zeros(n, np.float32)
+    if spec == "ones":
+        return np.ones(n, np.float32)
+    if spec == "iota1":
+        return np.arange(1, n + 1, dtype=np.float32)
+    if spec.startswith("const:"):
+        return np.full(n, float(spec[6:]), np.float32)
+    if spec.startswith("alt:"):
+        v = float(spec[4:])
+        return np.array([v if i % 2 == 0 else -v for i in range(n)], np.float32)
+    if spec.startswith("alt_w:"):
+        _, a, b = spec.split(":")
+        return np.array([float(a) if i % 2 == 0 else float(b) for i in range(n)], np.float32)
+    if spec == "ones_nan13":
+        x = np.ones(n, np.float32)
+        x[13] = np.nan
+        return x
+    if spec == "ones_inf42":
+        x = np.ones(n, np.float32)
+        x[42] = np.inf
+        return x
+    raise ValueError(spec)
+
+
+def subln_case_check(case, q, scale):
+    if "scale" in case:
+        assert scale == np.float32(case["scale"]), (case["name"], scale)
+    if "scale_approx" in case:
+        assert abs(scale - case["scale_approx"]) < 1e-5, (case["name"], scale)
+    if "q" in case:
+        assert np.all(q == case["q"]), case["name"]
+    if "q_even" in case:
+        assert np.all(q[0::2] == case["q_even"]) and np.all(q[1::2] == case["q_odd"]), case["name"]
+
+
+def test_subln_kats(oracle, kats):
+    s = kats["subln"]
+    for c in s["cases"]:
+        x = _subln_input(c["input"], s["len"])
+        w = _subln_input(c["weight"], s["len"])
+        q, scale = oracle.subln_quantize_absmax_i8(x, w, s["eps"])
+        subln_case_check(c, q, scale)
+    with pytest.raises(ValueError):
+        oracle.subln_quantize_absmax_i8(np.zeros(0, np.float32), np.zeros(0, np.float32), 1e-5)
+
+
+@pytest.mark.parametrize("k", [128, 896, 2048])
+def test_wave4_q4_0_q8_0_gemv_cosine(oracle, k):
+    """tests/wave4_quant_gemv_and_argmax.rs:254-348 (Q4_0, Q8_0) on the oracle."""
+    x = R.gen_activation(k, 100 + k)
+    xq = oracle.quantize_row_q8_0(x)
+    for n in (1, 3, 4, 17):
+        for quant, fill, seed in ((2, R.fill_q4_0_bytes, 200), (8, R.fill_q8_0_bytes, 400)):
+            w = fill(n, k, seed + k + n)
+            o = oracle.gemv(quant, w, n, k, xq)
+            o_mt = oracle.gemv_mt(quant, w, n, k, xq, 3)
+            assert np.array_equal(np.abs(o), np.abs(o_mt))  # gemv == gemv_4x up to -0.0
+            of32 = oracle.vec_dot_f32(quant, w, n, k, x)
+            ref = R.ref_matvec(oracle, quant, w, n, k, x)
+            if n == 1:
+                assert abs(o[0] - ref[0]) <= abs(ref[0]) * 0.03 + 0.25
+            else:
+                assert R.cosine(o, of32) > 0.9995 and R.cosine(o, ref) > 0.9995
+
+
+@pytest.mark.parametrize("k", [256, 1536, 2048, 3584, 5120])
+def test_wave4_k_quants_ternary_rel_err(oracle, k):
+    """tests/wave4_quant_gemv_and_argmax.rs:361-542: l2_rel_err(gemv, f64 over the Q8_K-
+    dequantized input) < 1e-5 and cosine > 0.999 against the f64 product on the f32 input."""
+    rows = 5
+    x = R.gen_activation(k, 700 + k)
+    xq = oracle.quantize_row_q8_k(x)
+    xd = R.dequant_q8(xq)
+    for quant, fill, seed in ((12, R.fill_q4_k_m_bytes, 11), (14, R.fill_q6_k_bytes, 33),
+                              (34, R.fill_tq1_0_bytes, 44), (35, R.fill_tq2_0_bytes, 55)):
+        w = fill(rows, k, seed + k)
+        o = oracle.gemv(quant, w, rows, k, xq)
+        r = R.ref_matvec(oracle, quant, w, rows, k, x)
+        rq = R.ref_matvec(oracle, quant, w, rows, k, xd)
+        assert R.cosine(o, r) > 0.999, (quant, k)
+        assert R.l2_rel_err(o, rq) < 1e-5, (quant, k, R.l2_rel_err(o, rq))
+        assert R.l2_rel_err(o, r) < 1.5e-2, (quant, k)
+        if quant in (12, 14):
+            of32 = oracle.vec_dot_f32(quant, w, rows, k, x)
+            assert R.cosine(of32, r) > 0.999
+
+
+def test_golden_fixtures_match_live_oracle(oracle):
+    """The committed oracle fixtures are reproduced bit for bit by the current oracle."""
+    f = np.load(os.path.join(GOLDEN, "oracle_fixtures.npz"))
+    names = sorted({k.split("__")[0] for k in f.files})
+    assert len(names) >= 9
+    for name in names:
+        q, rows, cols = (int(v) for v in f[f"{name}__meta"])
+        w = f[f"{name}__w"]
+        dt = oracle.BLOCK_Q8_K if oracle.ACT_IS_Q8K[q] else oracle.BLOCK_Q8_0
+        xq = oracle.quantize_act(q, f[f"{name}__x"])
+        assert np.array_equal(xq.view(np.uint8).reshape(-1), f[f"{name}__xq"])
+        sumi, summins, contrib = oracle.block_dots(q, w, rows, cols, f[f"{name}__xq"].view(dt))
+        assert np.array_equal(sumi, f[f"{name}__sumi"])
+        assert np.array_equal(summins, f[f"{name}__summins"])
+        assert np.array_equal(contrib.view(np.uint32), f[f"{name}__contrib"].view(np.uint32))
+        y = oracle.gemv(q, w, rows, cols, xq)
+        assert np.array_equal(y.view(np.uint32), f[f"{name}__y"].view(np.uint32))
+
+
+def test_bitlinear_tq1_tq2_same_trits_bit_identical(oracle):
+    """tests/empirical_challenge_m3_bitnet.rs:414-505: the same ternary matrix packed as TQ1_0
+    and TQ2_0 gives bit-identical BitLinear outputs."""
+    rows, cols = 37, 1024
+    t = oracle.ternary(rows * cols, 7)
+    w1 = oracle.pack_ternary(34, t, rows, cols, 0.03125)
+    w2 = oracle.pack_ternary(35, t, rows, cols, 0.03125)
+    act = oracle.ternary(cols, 9) * 40
+    o1 = oracle.bitlinear_i8(34, w1, rows, cols, act.astype(np.int8), 0.0123)
+    o2 = oracle.bitlinear_i8(35, w2, rows, cols, act.astype(np.int8), 0.0123)
+    assert np.array_equal(o1.view(np.uint32), o2.view(np.uint32))
+    with pytest.raises(ValueError):
+        oracle.bitlinear_i8(12, np.zeros(144, np.uint8), 1, 256, np.zeros(256, np.int8), 1.0)
+
+
+@pytest.mark.parametrize("quant", [2, 8, 12, 14, 35, 36])
+def test_repack_lossless_and_gemm_rows_stitch(oracle, quant):
+    """tests/test_repack_gemv_gemm.rs:619-700 (repacked values reproduce the dequantizer) and
+    :805-826 (row-slice outputs stitch to the full GEMM)."""
+    rows, cols = 19, 512
+    if quant in (35, 36):
+        w = oracle.pack_ternary(quant, oracle.ternary(rows * cols, 3), rows, cols, 0.02)
+    else:
+        w = oracle.quantize_weights(quant, oracle.normal(rows * cols, 5, 0.02), rows, cols)
+    q, s, mn = oracle.repack_block_scaled(quant, w, rows, cols)
+    g = 16 if quant == 14 else 32
+    deq = q.astype(np.float32).reshape(rows, -1, g) * s[:, :, None]
+    if mn is not None:
+        deq = deq - mn[:, :, None]
+    assert np.allclose(deq.reshape(rows, -1), oracle.dequantize_rows(quant, w, rows, cols),
+                       rtol=1e-6, atol=1e-7)
+    m = 5
+    act = oracle.normal(m * cols, 11, 1.0)
+    xq, xs, xsum, xs16, _ = oracle.act_q8_quantize(act, m, cols)
+    full = oracle.gemm_repacked(quant, q, s, mn, rows, cols, xq, xs, xsum, xs16, m, nthreads=2)
+    parts = [oracle.gemm_repacked(quant, q, s, mn, rows, cols, xq, xs, xsum, xs16, m, a, b)
+             for a, b in ((0, 7), (7, 8), (8, 19))]
+    assert np.array_equal(np.concatenate(parts, axis=1), full)
+    ref = oracle.dequantize_rows(quant, w, rows, cols).astype(np.float64) @ \
+        act.reshape(m, cols).astype(np.float64).T
+    assert R.cosine(full.reshape(-1), ref.T.reshape(-1)) > 0.9995
