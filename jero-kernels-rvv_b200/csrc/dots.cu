@@ -129,6 +129,9 @@ static int vec_dot_raw(const char *fn, int quant, const uint8_t *w, size_t w_len
                     "%s: expected %zu weight bytes for %zu blocks, got %zu", fn,
                     x_len * (size_t)f->block_bytes, x_len, w_len);
     if (!w || !x || !result) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
+    int rc;
+    if ((rc = check_align(x, 4, fn, "x_blocks")) || (rc = check_align(result, 4, fn, "result")))
+        return rc;
     if (x_len > 16384)
         return fail(JKB_E_BOUNDS, fn, 0, x_len, 16384, "%s: %zu blocks exceed the 16384-block row "
                     "limit of the GPU kernel", fn, x_len);
@@ -274,6 +277,8 @@ static int vec_dot_f32_call(const char *fn, int quant, float *out, size_t out_le
     int rc = validate_weight_call(fn, w, quant, out_len, in_len);
     if (rc) return rc;
     if (!out || !input) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
+    if ((rc = check_align(out, 4, fn, "output")) || (rc = check_align(input, 4, fn, "input")))
+        return rc;
     DqArgs a;
     a.qs = w->p.qs;
     a.qs_row = w->p.qs_row;
@@ -372,6 +377,7 @@ int jkb_bitlinear_i8(float *out, size_t out_len, const jkb_weight *w, const int8
     int rc = validate_bitlinear(w, out_len, act_len);
     if (rc) return rc;
     if (!out || !act_i8) return fail(JKB_E_INVALID, "bitlinear_i8", 0, 0, 0, "null pointer");
+    if ((rc = check_align(out, 4, "bitlinear_i8", "output"))) return rc;
     GemvLaunch L{};
     L.w = w;
     L.x = act_i8;
@@ -406,6 +412,9 @@ int jkb_bitlinear_i8_batch(float *out, size_t out_len, const jkb_weight *w, cons
     if (rc) return rc;
     if (!out || !act_i8 || !act_scales)
         return fail(JKB_E_INVALID, "bitlinear_i8_batch", 0, 0, 0, "null pointer");
+    if ((rc = check_align(out, 4, "bitlinear_i8_batch", "output")) ||
+        (rc = check_align(act_scales, 4, "bitlinear_i8_batch", "act_scales")))
+        return rc;
     GemvLaunch L{};
     L.w = w;
     L.x = act_i8;

@@ -28,6 +28,12 @@ int fail_cuda(cudaError_t e, const char *where) {
                 cudaGetErrorString(e));
 }
 
+int check_align(const void *p, size_t align, const char *fn, const char *what) {
+    if (((uintptr_t)p) % align == 0) return JKB_OK;
+    return fail(JKB_E_BOUNDS, fn, (size_t)((uintptr_t)p % align), 0, align,
+                "%s: %s pointer %p is not %zu-byte aligned", fn, what, p, align);
+}
+
 int check_launch(const char *where) {
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? JKB_OK : fail_cuda(e, where);

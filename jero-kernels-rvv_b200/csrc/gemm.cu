@@ -29,8 +29,9 @@ __global__ void __launch_bounds__(256) gemm_dp4a_kernel(
     const float *__restrict__ xs16, size_t m, size_t kp, const int8_t *__restrict__ wq,
     const float *__restrict__ ws, const float *__restrict__ wm, size_t groups, int gsz,
     size_t row_begin, size_t row_end, float *__restrict__ out) {
-    __shared__ __align__(16) int8_t sa[TM][TG + 4];
-    __shared__ __align__(16) int8_t sb[TN][TG + 4];
+    // Row pitch TG + 8 keeps every 8-byte staging store aligned and spreads rows over banks.
+    __shared__ __align__(16) int8_t sa[TM][TG + 8];
+    __shared__ __align__(16) int8_t sb[TN][TG + 8];
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const size_t m0 = (size_t)blockIdx.y * TM, n0 = row_begin + (size_t)blockIdx.x * TN;
     const size_t kb = kp / 32, kc = kp / 16;
@@ -130,6 +131,8 @@ static int gemm_rows(const char *fn, float *out, size_t out_len, const jkb_repac
                     "output length %zu != m * row_range.len() = %zu", out_len, act->m * sub_n);
     if (sub_n == 0 || act->m == 0) return JKB_OK;
     if (!out) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null output");
+    int arc = check_align(out, 4, fn, "output");
+    if (arc) return arc;
     bool used = false;
     int rc = gemm_tc_launch(w, act, out, row_begin, row_end, st, &used);
     if (rc || used) return rc;

@@ -79,7 +79,7 @@ __device__ __forceinline__ int4 lds_v4(const int8_t *p) {
 // ---------------------------------------------------------------- activation staging
 
 struct ActQ8K {
-    static __device__ size_t bytes(int K) { return ((size_t)K + 15) / 16 * 16 + K / 256 * 4 + K / 16 * 2 + 16; }
+    static __host__ __device__ size_t bytes(int K) { return ((size_t)K + 15) / 16 * 16 + K / 256 * 4 + K / 16 * 2 + 16; }
     static __device__ __forceinline__ const int8_t *xq(const uint8_t *s) { return (const int8_t *)s; }
     static __device__ __forceinline__ const float *xd(const uint8_t *s, int K) {
         return (const float *)(s + (K + 15) / 16 * 16);
@@ -108,7 +108,7 @@ struct ActQ8K {
 };
 
 struct ActQ80 {
-    static __device__ size_t bytes(int K) { return ((size_t)K + 15) / 16 * 16 + K / 32 * 8 + 16; }
+    static __host__ __device__ size_t bytes(int K) { return ((size_t)K + 15) / 16 * 16 + K / 32 * 8 + 16; }
     static __device__ __forceinline__ const int8_t *xq(const uint8_t *s) { return (const int8_t *)s; }
     static __device__ __forceinline__ const float *xd(const uint8_t *s, int K) {
         return (const float *)(s + (K + 15) / 16 * 16);
@@ -142,7 +142,7 @@ struct ActQ80 {
 };
 
 struct ActI8 {
-    static __device__ size_t bytes(int K) { return ((size_t)K + 15) / 16 * 16 + K / 16 * 4 + 16; }
+    static __host__ __device__ size_t bytes(int K) { return ((size_t)K + 15) / 16 * 16 + K / 16 * 4 + 16; }
     static __device__ __forceinline__ const int8_t *xq(const uint8_t *s) { return (const int8_t *)s; }
     static __device__ __forceinline__ const int *g16(const uint8_t *s, int K) {
         return (const int *)(s + (K + 15) / 16 * 16);
@@ -638,6 +638,8 @@ static int gemv_call(const char *fn, int quant, float *out, size_t out_len, cons
         return fail(JKB_E_BOUNDS, w->name, w->offset, x_len, w->nb,
                     "%s: x_blocks len %zu != expected %zu", fn, x_len, w->nb);
     if (!out || !x) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
+    if ((rc = check_align(out, 4, fn, "output")) || (rc = check_align(x, 4, fn, "x_blocks")))
+        return rc;
     GemvLaunch L{};
     L.w = w;
     L.x = x;
@@ -706,6 +708,9 @@ int jkb_gemv_rows(float *out, size_t out_len, const jkb_weight *w, const void *x
         return fail(JKB_E_BOUNDS, "gemv_rows", 0, out_len * 4, (row_end - row_begin) * 4,
                     "output length %zu != row range length %zu", out_len, row_end - row_begin);
     if ((!out && out_len) || !x) return fail(JKB_E_INVALID, "gemv_rows", 0, 0, 0, "null pointer");
+    if ((rc = check_align(out, 4, "gemv_rows", "output")) ||
+        (rc = check_align(x, 4, "gemv_rows", "x_blocks")))
+        return rc;
     GemvLaunch L{};
     L.w = w;
     L.x = x;
@@ -728,6 +733,11 @@ int jkb_gemv_block_dots(const jkb_weight *w, const void *x, size_t x_len, int32_
                     "gemv_block_dots: x_blocks len %zu != expected %zu", x_len, w->nb);
     if (!x || !sumi || !block_values)
         return fail(JKB_E_INVALID, "gemv_block_dots", 0, 0, 0, "null pointer");
+    if ((rc = check_align(x, 4, "gemv_block_dots", "x_blocks")) ||
+        (rc = check_align(sumi, 4, "gemv_block_dots", "sumi")) ||
+        (rc = check_align(block_values, 4, "gemv_block_dots", "block_values")) ||
+        (summins && (rc = check_align(summins, 4, "gemv_block_dots", "summins"))))
+        return rc;
     GemvLaunch L{};
     L.w = w;
     L.x = x;

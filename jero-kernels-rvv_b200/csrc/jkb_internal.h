@@ -17,6 +17,9 @@ namespace jkb {
 int fail(int status, const char *tensor, size_t offset, size_t byte_len, size_t buffer_len,
          const char *fmt, ...) __attribute__((format(printf, 6, 7)));
 int fail_cuda(cudaError_t e, const char *where);
+// Rejects a device pointer that is not `align`-byte aligned (JKB_E_BOUNDS). Block activations
+// carry an f32 field (align 4, like the reference #[repr(C)] structs); outputs are f32.
+int check_align(const void *p, size_t align, const char *fn, const char *what);
 // Checks cudaGetLastError after a launch.
 int check_launch(const char *where);
 void clear_error();

@@ -268,6 +268,10 @@ static int validate_act(const char *name, size_t x_len, size_t out_len, size_t b
 }
 
 static int launch_q8_0(const float *x, size_t nblocks, void *out, cudaStream_t st) {
+    int rc;
+    if ((rc = check_align(x, 4, "quantize_row_q8_0", "x")) ||
+        (rc = check_align(out, 4, "quantize_row_q8_0", "output blocks")))
+        return rc;
     size_t threads = nblocks * 8;
     unsigned grid = (unsigned)((threads + 255) / 256);
     bool vec = ((uintptr_t)x & 15) == 0;
@@ -279,6 +283,10 @@ static int launch_q8_0(const float *x, size_t nblocks, void *out, cudaStream_t s
 }
 
 static int launch_q8_k(const float *x, size_t nblocks, void *out, cudaStream_t st) {
+    int rc;
+    if ((rc = check_align(x, 4, "quantize_row_q8_k", "x")) ||
+        (rc = check_align(out, 4, "quantize_row_q8_k", "output blocks")))
+        return rc;
     size_t threads = nblocks * 32;
     unsigned grid = (unsigned)((threads + 255) / 256);
     bool vec = ((uintptr_t)x & 15) == 0;
@@ -350,6 +358,11 @@ int jkb_subln_quantize_absmax_i8_rows(int8_t *out_i8, const float *input,
                     "dimension mismatch: input=%zu, rows=%zu", len, m);
     if (!out_i8 || !input || !norm_weight || !scales_out)
         return fail(JKB_E_INVALID, "subln", 0, 0, 0, "null pointer");
+    int rc;
+    if ((rc = check_align(input, 4, "subln", "input")) ||
+        (rc = check_align(norm_weight, 4, "subln", "norm_weight")) ||
+        (rc = check_align(scales_out, 4, "subln", "scale")))
+        return rc;
     size_t smem = len * sizeof(float);
     if (smem > 200 * 1024)
         return fail(JKB_E_BOUNDS, "subln", 0, len, 200 * 1024 / 4,
@@ -429,6 +442,8 @@ int jkb_act_q8_quantize(jkb_act_q8 *a, const float *input, size_t in_len, size_t
                     "batch [%zu, %zu] exceeds the handle capacity [%zu, %zu]", m, k, a->m_cap,
                     a->k);
     if (!input) return fail(JKB_E_INVALID, "QuantizedActQ8", 0, 0, 0, "null input");
+    int arc = check_align(input, 4, "QuantizedActQ8", "input");
+    if (arc) return arc;
     cudaStream_t st = as_stream(stream);
     size_t kb = a->k_pad / 32, nsb = (k + 255) / 256;
     size_t n = m * kb;

@@ -78,6 +78,19 @@ def test_quantize_row_validation_fails_closed(lib):
     assert lib.jkb_last_error() == b""
 
 
+def test_misaligned_pointers_rejected_before_launch(lib):
+    """Block activations and f32 buffers must be 4-byte aligned (align_of BlockQ8_0); a
+    misaligned pointer is a TensorBoundsError, never a device access."""
+    buf = (C.c_uint8 * 4096)()
+    base = C.addressof(buf)
+    rc = lib.jkb_quantize_row_q8_0(base + 1, 32, base + 64, 1, None)
+    assert rc == 1 and b"not 4-byte aligned" in _err(lib).reason
+    rc = lib.jkb_quantize_row_q8_k(base, 256, base + 2, 1, None)
+    assert rc == 1 and b"not 4-byte aligned" in _err(lib).reason
+    rc = lib.jkb_vec_dot_q8_0_q8_0(base, 34, base + 3, 1, base + 128, None)
+    assert rc == 1 and b"x_blocks" in _err(lib).reason
+
+
 def test_subln_dimension_mismatch(lib):
     """tests/empirical_challenge_m3_bitnet.rs:271-297."""
     buf = (C.c_float * 256)()

@@ -21,7 +21,7 @@ def edge_rows(oracle, k):
     rows = [oracle.normal(k, 0xAC70000 + k, 1.0), R.test_f32_row(k, 3), np.zeros(k, np.float32)]
     x = R.gen_activation(k, 99)
     x[5] = np.nan
-    x[40] = np.inf
+    x[min(k - 1, 40)] = np.inf
     x[min(k - 1, 300)] = -np.inf
     rows.append(x)
     rows.append(np.full(k, 1e-40, np.float32))  # subnormal absmax
