@@ -160,6 +160,6 @@ def test_gemm_validation(jkb, oracle):
         rw.gemm(torch.empty(rows, device="cuda"), a)
     with pytest.raises(jkb.TensorBoundsError):
         rw.gemm_rows(torch.empty(2 * 4, device="cuda"), a, range(14, 18))
-    b = jkb.QuantizedActQ8.quantize(dev(oracle.normal(512)), 1, 512)
+    b = jkb.QuantizedActQ8.quantize(dev(oracle.normal(512, 2)), 1, 512)
     with pytest.raises(jkb.TensorBoundsError):
         rw.gemm(torch.empty(rows, device="cuda"), b)
