@@ -275,6 +275,20 @@ int jkb_gemv_repacked_rows(float *out, size_t out_len, const jkb_repacked_weight
 int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight *w,
                           const float *input, size_t in_len, size_t m, jkb_act_q8 *scratch,
                           void *stream);
+/* No counterpart in the reference. The same computation as jkb_gemm_repacked_f32 for callers
+ * that cannot allocate device memory, and so cannot create the jkb_act_q8 scratch handle. Two
+ * examples: an engine that reserved all remaining HBM for its KV cache at start-up, and a host
+ * whose per-token loop forbids cudaMalloc because it may synchronize the device and stall the
+ * pipeline. The quantized activations go to a scratch array built into the library (3.25 MiB
+ * of device memory on every GPU that loads it, held until exit). The batch must satisfy
+ * m * round_up(cols, 32) <= 2097152 elements (e.g. 512 tokens x 4096); larger batches fail
+ * with JKB_E_BOUNDS. The call allocates nothing. The first call on each device looks up the
+ * scratch address (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture. All calls share the one array, so calls whose executions overlap
+ * on the GPU (different streams, or threads sharing a device) race; serialize them. Each call
+ * writes every scratch value it reads, so results never depend on an earlier call. */
+int jkb_gemm_repacked_f32_noalloc(float *out, size_t out_len, const jkb_repacked_weight *w,
+                                  const float *input, size_t in_len, size_t m, void *stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -11,6 +11,7 @@
 // the dp4a tile kernel used for the other cases (16-element groups, mins, small M) and the
 // ABI entry points.
 #include <cstring>
+#include <mutex>
 
 #include "jkb_internal.h"
 
@@ -144,11 +145,94 @@ static int gemm_rows(const char *fn, float *out, size_t out_len, const jkb_repac
     return check_launch("gemm_dp4a_kernel");
 }
 
+// ---------------------------------------------------------------- allocation-free variant
+// Scratch of jkb_gemm_repacked_f32_noalloc: the quantized activation batch lives in this
+// file-scope device array instead of a caller-created jkb_act_q8. It holds batches with
+// m * k_padded <= NOALLOC_MAX_ELEMS (2^21, e.g. 512 tokens x 4096). Every GPU that loads the
+// library keeps these 3.25 MiB until process exit, and all calls share them.
+constexpr size_t NOALLOC_MAX_ELEMS = size_t(1) << 21;
+constexpr size_t NOALLOC_Q_BYTES = NOALLOC_MAX_ELEMS;             // i8 values [m][k_pad]
+constexpr size_t NOALLOC_G32_BYTES = NOALLOC_MAX_ELEMS / 32 * 4;  // f32 per 32 elements
+constexpr size_t NOALLOC_G16_BYTES = NOALLOC_MAX_ELEMS / 16 * 4;  // f32 per 16 elements
+// regions, each 256-byte aligned: q | x_scales | x_sums | x_sums_16 | super_scales
+// (super_scales needs m * ceil(k/256) <= m * k_pad / 32 floats)
+constexpr size_t NOALLOC_BYTES = NOALLOC_Q_BYTES + 3 * NOALLOC_G32_BYTES + NOALLOC_G16_BYTES;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_BYTES];
+
+// Host code cannot use g_noalloc_scratch's name as a device address; the address comes from
+// cudaGetSymbolAddress, once per device with that device current, and is cached here.
+static uint8_t *noalloc_scratch(int *rc) {
+    static std::mutex mu;
+    static uint8_t *ptr_by_device[128] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *rc = fail_cuda(e, "gemm_repacked_f32_noalloc (cudaGetDevice)");
+        return nullptr;
+    }
+    if (dev < 0 || dev >= 128) {
+        *rc = fail(JKB_E_INVALID, "gemm_repacked_f32_noalloc", 0, 0, 0,
+                   "device ordinal %d outside the supported range", dev);
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptr_by_device[dev]) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) {
+            *rc = fail_cuda(e, "gemm_repacked_f32_noalloc (cudaGetSymbolAddress)");
+            return nullptr;
+        }
+        ptr_by_device[dev] = static_cast<uint8_t *>(p);
+    }
+    return ptr_by_device[dev];
+}
+
 }  // namespace jkb
 
 using namespace jkb;
 
 extern "C" {
+
+int jkb_gemm_repacked_f32_noalloc(float *out, size_t out_len, const jkb_repacked_weight *w,
+                                  const float *input, size_t in_len, size_t m, void *stream) {
+    if (!w || w->magic != REPACKED_MAGIC)
+        return fail(JKB_E_INVALID, "gemm_repacked_f32_noalloc", 0, 0, 0,
+                    "null or destroyed weight");
+    // gemm_repacked_f32_rows validation (repack.rs:4147-4161), then the scratch limit
+    if (m == 0 || w->cols == 0 || in_len != m * w->cols)
+        return fail(JKB_E_BOUNDS, "gemm_repacked_f32_noalloc", 0, in_len * 4, m * w->cols * 4,
+                    "input length %zu != m (%zu) * cols (%zu)", in_len, m, w->cols);
+    const size_t kp = (w->cols + 31) / 32 * 32;
+    if (m > NOALLOC_MAX_ELEMS / kp)
+        return fail(JKB_E_BOUNDS, "gemm_repacked_f32_noalloc", 0, in_len * 4,
+                    NOALLOC_MAX_ELEMS,
+                    "m (%zu) * k_padded (%zu) exceeds the %zu-element limit of the built-in "
+                    "scratch; use jkb_gemm_repacked_f32 with a jkb_act_q8 handle",
+                    m, kp, NOALLOC_MAX_ELEMS);
+    int rc = JKB_OK;
+    uint8_t *s = noalloc_scratch(&rc);
+    if (!s) return rc;
+    // A stack view over the static scratch, filled by the same quantizer and read by the same
+    // GEMM as the handle-based path. Every value the GEMM reads (rows 0..m-1 of each region)
+    // is written by this call's quantizer first, so nothing needs clearing.
+    jkb_act_q8 view;
+    memset(&view, 0, sizeof(view));
+    view.magic = ACT_MAGIC;
+    view.m_cap = NOALLOC_MAX_ELEMS / kp;
+    view.k = w->cols;
+    view.k_pad = kp;
+    view.q = reinterpret_cast<int8_t *>(s);
+    view.x_scales = reinterpret_cast<float *>(s + NOALLOC_Q_BYTES);
+    view.x_sums = reinterpret_cast<float *>(s + NOALLOC_Q_BYTES + NOALLOC_G32_BYTES);
+    view.x_sums_16 = reinterpret_cast<float *>(s + NOALLOC_Q_BYTES + 2 * NOALLOC_G32_BYTES);
+    view.super_scales = reinterpret_cast<float *>(s + NOALLOC_Q_BYTES + 2 * NOALLOC_G32_BYTES +
+                                                  NOALLOC_G16_BYTES);
+    rc = jkb_act_q8_quantize(&view, input, in_len, m, w->cols, stream);
+    if (rc) return rc;
+    return gemm_rows("gemm_repacked_f32_noalloc", out, out_len, w, &view, 0, w->rows, false,
+                     as_stream(stream));
+}
 
 int jkb_gemm_repacked(float *out, size_t out_len, const jkb_repacked_weight *w,
                       const jkb_act_q8 *act, void *stream) {

@@ -97,6 +97,7 @@ SIGNATURES = {
     "jkb_gemv_repacked": [P, S, P, P, P],
     "jkb_gemv_repacked_rows": [P, S, P, P, S, S, P],
     "jkb_gemm_repacked_f32": [P, S, P, P, S, S, P, P],
+    "jkb_gemm_repacked_f32_noalloc": [P, S, P, P, S, S, P],
 }
 _RESTYPE = {"jkb_last_error": C.c_char_p, "jkb_clear_error": None}
 

@@ -27,7 +27,8 @@ __all__ = [
     "gemv_block_dots", "vec_dot_q4_k_m", "vec_dot_q8_0", "vec_dot_q6_k", "vec_dot_q4_0",
     "vec_dot_i2_s", "bitlinear_i8", "bitlinear_i8_rvv", "bitlinear_i8_ime",
     "bitlinear_i8_batch", "gemm_repacked", "gemm_repacked_rows", "gemv_repacked",
-    "gemv_repacked_rows", "gemm_repacked_f32", "empty_q8_0_blocks", "empty_q8_k_blocks",
+    "gemv_repacked_rows", "gemm_repacked_f32", "gemm_repacked_f32_noalloc",
+    "empty_q8_0_blocks", "empty_q8_k_blocks",
     "device_view",
 ]
 
@@ -573,3 +574,12 @@ def gemm_repacked_f32(out, weights, x, m, scratch: QuantizedActQ8, stream=None):
     """repack.rs:4129 (the caller supplies the QuantizedActQ8 scratch handle)."""
     _check(_L().jkb_gemm_repacked_f32(_dptr(out), out.numel(), weights._h, _dptr(x), x.numel(),
                                       m, scratch._h, _stream(stream)))
+
+
+def gemm_repacked_f32_noalloc(out, weights, x, m, stream=None):
+    """gemm_repacked_f32 for callers that cannot allocate device memory (and so cannot create
+    a QuantizedActQ8 handle). It uses a scratch array built into the library, limited to
+    m * round_up(cols, 32) <= 2**21 elements. Calls that overlap on the GPU share that array
+    and race, so serialize them. No counterpart in the reference."""
+    _check(_L().jkb_gemm_repacked_f32_noalloc(_dptr(out), out.numel(), weights._h, _dptr(x),
+                                              x.numel(), m, _stream(stream)))
