@@ -471,6 +471,38 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
+def run_kernel_case(args):
+    """One GEMV shape launched `--launches` times (the small, single-kernel case that the ncu
+    captures in profiles/ use); prints the CUDA-event time per launch."""
+    import torch
+    import jkb200 as jkb
+
+    quant = {"q4_k": Q4_K, "q6_k": Q6_K, "q8_0": Q8_0}[args.kernel]
+    rows, cols = args.rows, args.cols
+    raw = synth_matrix(quant, rows, cols, 4242)
+    w = jkb.Weight(jkb.TensorView(args.kernel, quant, [rows, cols], raw), rows, cols)
+    x = torch.randn(cols, generator=torch.Generator().manual_seed(1)).cuda()
+    if quant == Q8_0:
+        xq = jkb.empty_q8_0_blocks(cols // 32)
+        jkb.quantize_row_q8_0(x, xq)
+        fn = jkb.gemv_q8_0_q8_0
+    else:
+        xq = jkb.empty_q8_k_blocks(cols // 256)
+        jkb.quantize_row_q8_k(x, xq)
+        fn = jkb.gemv_q4_k_q8_k if quant == Q4_K else jkb.gemv_q6_k_q8_k
+    out = torch.empty(rows, dtype=torch.float32, device="cuda")
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.launches + 1)]
+    ev[0].record()
+    for i in range(args.launches):
+        fn(out, w, xq)
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    nbytes = algorithmic_bytes(quant, rows, cols)
+    ts = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.launches)]
+    print(json.dumps({"kernel": args.kernel, "rows": rows, "cols": cols,
+                      "ms_per_launch": ts, "gbs": [nbytes / (t * 1e-3) / 1e9 for t in ts]}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -478,10 +510,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="jkb", choices=["jkb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0"],
+                    help="run one GEMV shape (profiling case) instead of the benchmark")
+    ap.add_argument("--rows", type=int, default=65536)
+    ap.add_argument("--cols", type=int, default=4096)
+    ap.add_argument("--launches", type=int, default=3)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.kernel:
+        run_kernel_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

@@ -2,6 +2,7 @@
 // VectorKernel entries (dequantize -> f32 dot) and the BitLinear ABI glue.
 #include <cstring>
 
+#include "gpu_layout.cuh"
 #include "jkb_internal.h"
 
 namespace jkb {
@@ -154,7 +155,7 @@ struct DqArgs {
     size_t sc_row;
     const uint16_t *d;
     float i2s;
-    int quant, nb, be;
+    int quant, gpu_format, nb, be;
     const float *x;
     float *out;
     size_t rows;
@@ -162,10 +163,17 @@ struct DqArgs {
 
 __device__ float block_dot_f32(const DqArgs &a, size_t r, int b) {
     const float *x = a.x + (size_t)b * a.be;
+    // the block's quant bytes in GGUF order (gathered from the lane-interleaved chunks)
+    uint8_t q[192];
+    const int qch = qs_chunks(a.gpu_format);
+    const uint8_t *rowp = a.qs + r * a.qs_row;
+    for (int j = 0; j < qch; j++) {
+        const uint8_t *c = rowp + qs_chunk_offset(a.nb, qch, b, j);
+        for (int i = 0; i < 16; i++) q[16 * j + i] = c[i];
+    }
     float s = 0.0f;
     switch (a.quant) {
     case JKB_Q4_0: {
-        const uint8_t *q = a.qs + r * a.qs_row + 16 * (size_t)b;
         float d = f16_fin(a.d[r * a.nb + b]);
         for (int i = 0; i < 32; i++) {
             int n = i < 16 ? (q[i] & 0x0F) : (q[i - 16] >> 4);
@@ -175,17 +183,15 @@ __device__ float block_dot_f32(const DqArgs &a, size_t r, int b) {
         return s;
     }
     case JKB_Q8_0: {
-        const int8_t *q = reinterpret_cast<const int8_t *>(a.qs + r * a.qs_row + 32 * (size_t)b);
         float d = f16_fin(a.d[r * a.nb + b]);
         for (int i = 0; i < 32; i++) {
-            float v = d == 0.0f ? 0.0f : __fmul_rn(d, (float)q[i]);
+            float v = d == 0.0f ? 0.0f : __fmul_rn(d, (float)(int8_t)q[i]);
             s = __fadd_rn(s, __fmul_rn(v, x[i]));
         }
         return s;
     }
     case JKB_Q4_K_M: {
         const uint8_t *sv = a.sc + r * a.sc_row + 16 * (size_t)b;
-        const uint8_t *q = a.qs + r * a.qs_row + 128 * (size_t)b;
         float d = f16_fin(rd16d(sv)), dmin = f16_fin(rd16d(sv + 2));
         const uint8_t *s6 = sv + 4;
         for (int c = 0; c < 4; c++) {
@@ -207,27 +213,23 @@ __device__ float block_dot_f32(const DqArgs &a, size_t r, int b) {
         }
         return s;
     }
-    case JKB_Q6_K: {
-        const uint8_t *base = a.qs + r * a.qs_row + 192 * (size_t)b;
+    case JKB_Q6_K: {  // dequantize_q6_k_block (quant.rs:594-648); q = ql[128] | qh[64]
         const int8_t *sc = reinterpret_cast<const int8_t *>(a.sc + r * a.sc_row + 16 * (size_t)b);
         float d = f16_fin(a.d[r * a.nb + b]);
+        const uint8_t *ql = q, *qh = q + 128;
         float vals[256];
-        for (int t = 0; t < 4; t++) {
-            int h = t >> 1, i = t & 1;
-            for (int j = 0; j < 16; j++) {
-                uint8_t A = base[16 * t + j], B = base[64 + 16 * t + j], H = base[128 + 16 * t + j];
-                int l = 16 * i + j, n = 128 * h;
-                int q1 = (int)((A & 0x0F) | ((H & 3) << 4)) - 32;
-                int q2 = (int)((B & 0x0F) | (((H >> 2) & 3) << 4)) - 32;
-                int q3 = (int)((A >> 4) | (((H >> 4) & 3) << 4)) - 32;
-                int q4 = (int)((B >> 4) | (((H >> 6) & 3) << 4)) - 32;
-                int is = l / 16, sb = 8 * h;
+        for (int h = 0; h < 2; h++)
+            for (int l = 0; l < 32; l++) {
+                int lb = 64 * h, hb = 32 * h, n = 128 * h, is = l / 16, sb = 8 * h;
+                int q1 = (int)((ql[lb + l] & 0x0F) | ((qh[hb + l] & 3) << 4)) - 32;
+                int q2 = (int)((ql[lb + l + 32] & 0x0F) | (((qh[hb + l] >> 2) & 3) << 4)) - 32;
+                int q3 = (int)((ql[lb + l] >> 4) | (((qh[hb + l] >> 4) & 3) << 4)) - 32;
+                int q4 = (int)((ql[lb + l + 32] >> 4) | (((qh[hb + l] >> 6) & 3) << 4)) - 32;
                 vals[n + l] = __fmul_rn(__fmul_rn(d, (float)sc[sb + is]), (float)q1);
                 vals[n + l + 32] = __fmul_rn(__fmul_rn(d, (float)sc[sb + is + 2]), (float)q2);
                 vals[n + l + 64] = __fmul_rn(__fmul_rn(d, (float)sc[sb + is + 4]), (float)q3);
                 vals[n + l + 96] = __fmul_rn(__fmul_rn(d, (float)sc[sb + is + 6]), (float)q4);
             }
-        }
         for (int e = 0; e < 256; e++) {
             float v = d == 0.0f ? 0.0f : vals[e];
             s = __fadd_rn(s, __fmul_rn(v, x[e]));
@@ -235,7 +237,6 @@ __device__ float block_dot_f32(const DqArgs &a, size_t r, int b) {
         return s;
     }
     case JKB_I2_S: {
-        const uint8_t *q = a.qs + r * a.qs_row + 32 * (size_t)b;
         float vals[128];
         for (int g = 0; g < 32; g++) {
             vals[g] = (float)((int)((q[g] >> 6) & 3) - 1);
@@ -287,6 +288,7 @@ static int vec_dot_f32_call(const char *fn, int quant, float *out, size_t out_le
     a.d = w->p.d;
     a.i2s = w->p.i2s_scale;
     a.quant = quant;
+    a.gpu_format = w->gpu_format;
     a.nb = (int)w->nb;
     a.be = fmt_of(quant)->block_elems;
     a.x = input;

@@ -1,20 +1,26 @@
 // Memory-bound decode GEMV / BitLinear kernels over the jkb_weight GPU layout.
 //
-// One warp per weight row (persistent CTAs of 8 warps stride over rows); lane l of the warp
-// owns the 16-byte quant chunks l, l+32, l+64, ... of the row, so every warp-wide load reads
-// 512 contiguous bytes. A block's chunks sit on CPB consecutive lanes; each lane forms exact
-// integer partial sums with dp4a against the activation staged in shared memory, the CPB lanes
-// add them with xor-shuffles (integer, so the per-block sums are the reference's bit for bit),
-// and the block's first lane applies the reference's f32 block formula with separately rounded
-// multiplies (__fmul_rn/__fsub_rn). Only the final f32 sum over a row's blocks runs in a
-// different order than the reference's sequential row loop.
+// Work split: one lane owns one whole block (32, 128 or 256 elements) of one weight row.
+// A row with nb blocks gets LPR = min(32, pow2ceil(nb)) lanes (so one warp covers 1, 2, 4 ...
+// rows at a time), and lane i of the row walks blocks i, i+LPR, ... Persistent CTAs of 8 warps
+// stride over rows. The quant planes are lane-interleaved (gpu_layout.cuh), so the lanes' j-th
+// 16-byte chunk loads form one contiguous span.
 //
-// Activation staging (shared memory, per CTA and token):
-//   BlockQ8K rows: xq i8[K] | xd f32[K/256] | bsums i16[K/16]
-//   BlockQ8_0 rows: xq i8[K] | xd f32[K/32] | block sums i32[K/32]
-//   i8 rows (BitLinear): xq i8[K] | 16-element sums i32[K/16]
+// Per block a lane forms the exact integer sums with dp4a against the activation staged in
+// shared memory, and applies the offsets as integer corrections: -8 for Q4_0 and -1 for
+// ternary codes through the block sum, -32 for Q6_K through the 16-element bsums. It then
+// evaluates the reference's f32 block formula with separately rounded __fmul_rn/__fsub_rn, so
+// integer sums and block values are bit-exact. Only the f32 sum of a row's block values runs in
+// a different order than the reference's sequential row loop: in-lane, then a shuffle tree.
+//
+// Activation staging (shared memory, per CTA and token; chunk = 16 bytes, XOR-swizzled inside
+// each block so that lanes reading the same chunk of different blocks hit different banks):
+//   BlockQ8K rows : xq[K] | bsums i16[16] per superblock | xd f32 | block totals i32
+//   BlockQ8_0 rows: xq[K] | xd f32 per block | block sums i32
+//   i8 rows       : xq[K] | block totals i32 (block = the weight format's block)
 #include <cstdio>
 
+#include "gpu_layout.cuh"
 #include "jkb_internal.h"
 
 namespace jkb {
@@ -35,6 +41,7 @@ struct KArgs {
     size_t row_begin, row_end;
     int nb;  // blocks per row
     int K;
+    int lpr_shift;  // log2(lanes per row)
     int32_t *dbg_sumi, *dbg_mins;
     float *dbg_val;
 };
@@ -45,13 +52,6 @@ __device__ __forceinline__ uint4 ldg_stream(const uint8_t *p) {
     uint4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
-}
-__device__ __forceinline__ uint2 ldg_stream2(const uint8_t *p) {
-    uint2 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
-                 : "=r"(r.x), "=r"(r.y)
                  : "l"(p));
     return r;
 }
@@ -72,400 +72,437 @@ __device__ __forceinline__ float f16_finite(uint32_t bits) {
     float v = __half2float(__ushort_as_half((unsigned short)bits));
     return ((bits >> 10) & 0x1F) == 0x1F ? 0.0f : v;
 }
-__device__ __forceinline__ int4 lds_v4(const int8_t *p) {
-    return *reinterpret_cast<const int4 *>(p);
-}
+__device__ __forceinline__ int4 lds4(const void *p) { return *reinterpret_cast<const int4 *>(p); }
+__device__ __forceinline__ int sbyte(uint32_t w, int k) { return (int)(int8_t)(w >> (8 * k)); }
 
 // ---------------------------------------------------------------- activation staging
 
+// BlockQ8K activations (quant_q8.rs:62-71). Superblock s: 256 i8 at s*256 with chunk j at
+// 16*(j ^ (s & 7)); its 16 bsums (two 16-byte halves, half h at 16*(h ^ ((s >> 2) & 1))).
 struct ActQ8K {
-    static __host__ __device__ size_t bytes(int K) { return ((size_t)K + 15) / 16 * 16 + K / 256 * 4 + K / 16 * 2 + 16; }
-    static __device__ __forceinline__ const int8_t *xq(const uint8_t *s) { return (const int8_t *)s; }
-    static __device__ __forceinline__ const float *xd(const uint8_t *s, int K) {
-        return (const float *)(s + (K + 15) / 16 * 16);
+    static __host__ __device__ size_t bytes(int K) {
+        return (size_t)K + (size_t)(K / 256) * 40 + 16;
     }
-    static __device__ __forceinline__ const int16_t *bs(const uint8_t *s, int K) {
-        return (const int16_t *)(s + (K + 15) / 16 * 16 + K / 256 * 4);
+    static __device__ __forceinline__ const int8_t *chunk(const uint8_t *s, int sb, int j) {
+        return (const int8_t *)(s + sb * 256 + 16 * (j ^ (sb & 7)));
+    }
+    static __device__ __forceinline__ int4 bsums_half(const uint8_t *s, int K, int sb, int h) {
+        return lds4(s + K + sb * 32 + 16 * (h ^ ((sb >> 2) & 1)));
+    }
+    static __device__ __forceinline__ float xd(const uint8_t *s, int K, int sb) {
+        return reinterpret_cast<const float *>(s + K + (K / 256) * 32)[sb];
+    }
+    static __device__ __forceinline__ int tot(const uint8_t *s, int K, int sb) {
+        return reinterpret_cast<const int *>(s + K + (K / 256) * 36)[sb];
     }
     static __device__ void stage(const KArgs &a, const uint8_t *x, uint8_t *s) {
-        const int nb = a.K / 256;
-        const int total = nb * 73;  // 292-byte BlockQ8K = 73 words
-        uint32_t *q = (uint32_t *)s;
-        float *xd_ = (float *)xd(s, a.K);
-        uint32_t *bs_ = (uint32_t *)bs(s, a.K);
+        const int nb = a.K / 256, total = nb * 73;  // 292-byte BlockQ8K = 73 words
+        float *xd_ = (float *)(s + a.K + nb * 32);
         for (int i = threadIdx.x; i < total; i += blockDim.x) {
-            int blk = i / 73, w = i - blk * 73;
-            uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(x + (size_t)blk * 292) + w);
-            if (w == 0)
+            const int blk = i / 73, w = i - blk * 73;
+            const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(x + (size_t)blk * 292) + w);
+            if (w == 0) {
                 xd_[blk] = __uint_as_float(v);
-            else if (w <= 64)
-                q[blk * 64 + (w - 1)] = v;
-            else
-                bs_[blk * 8 + (w - 65)] = v;
+            } else if (w <= 64) {
+                const int ww = w - 1, j = ww >> 2;
+                *(uint32_t *)(s + blk * 256 + 16 * (j ^ (blk & 7)) + 4 * (ww & 3)) = v;
+            } else {
+                const int ww = w - 65, h = ww >> 2;
+                *(uint32_t *)(s + a.K + blk * 32 + 16 * (h ^ ((blk >> 2) & 1)) + 4 * (ww & 3)) = v;
+            }
+        }
+        __syncthreads();
+        int *tot_ = (int *)(s + a.K + nb * 36);
+        for (int blk = threadIdx.x; blk < nb; blk += blockDim.x) {
+            const int16_t *b16 = (const int16_t *)(s + a.K + blk * 32);
+            int t = 0;
+            for (int k = 0; k < 16; k++) t += b16[k];
+            tot_[blk] = t;
         }
         __syncthreads();
     }
 };
 
+// BlockQ8_0 activations (quant_q8.rs:37-44). Block b: 32 i8 at b*32 with chunk j at
+// 16*(j ^ ((b >> 2) & 1)); f32 scale; integer sum of the 32 values.
 struct ActQ80 {
-    static __host__ __device__ size_t bytes(int K) { return ((size_t)K + 15) / 16 * 16 + K / 32 * 8 + 16; }
-    static __device__ __forceinline__ const int8_t *xq(const uint8_t *s) { return (const int8_t *)s; }
-    static __device__ __forceinline__ const float *xd(const uint8_t *s, int K) {
-        return (const float *)(s + (K + 15) / 16 * 16);
+    static __host__ __device__ size_t bytes(int K) {
+        return (size_t)K + (size_t)(K / 32) * 8 + 16;
     }
-    static __device__ __forceinline__ const int *xs(const uint8_t *s, int K) {
-        return (const int *)(s + (K + 15) / 16 * 16 + K / 32 * 4);
+    static __device__ __forceinline__ const int8_t *chunk(const uint8_t *s, int b, int j) {
+        return (const int8_t *)(s + b * 32 + 16 * (j ^ ((b >> 2) & 1)));
+    }
+    static __device__ __forceinline__ float xd(const uint8_t *s, int K, int b) {
+        return reinterpret_cast<const float *>(s + K)[b];
+    }
+    static __device__ __forceinline__ int tot(const uint8_t *s, int K, int b) {
+        return reinterpret_cast<const int *>(s + K + (K / 32) * 4)[b];
     }
     static __device__ void stage(const KArgs &a, const uint8_t *x, uint8_t *s) {
-        const int nb = a.K / 32;
-        const int total = nb * 9;  // 36-byte BlockQ8_0 = 9 words
-        uint32_t *q = (uint32_t *)s;
-        float *xd_ = (float *)xd(s, a.K);
+        const int nb = a.K / 32, total = nb * 9;  // 36-byte BlockQ8_0 = 9 words
+        float *xd_ = (float *)(s + a.K);
         for (int i = threadIdx.x; i < total; i += blockDim.x) {
-            int blk = i / 9, w = i - blk * 9;
-            uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(x + (size_t)blk * 36) + w);
-            if (w == 0)
+            const int blk = i / 9, w = i - blk * 9;
+            const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(x + (size_t)blk * 36) + w);
+            if (w == 0) {
                 xd_[blk] = __uint_as_float(v);
-            else
-                q[blk * 8 + (w - 1)] = v;
+            } else {
+                const int ww = w - 1, j = ww >> 2;
+                *(uint32_t *)(s + blk * 32 + 16 * (j ^ ((blk >> 2) & 1)) + 4 * (ww & 3)) = v;
+            }
         }
         __syncthreads();
-        int *xs_ = (int *)xs(s, a.K);
+        int *tot_ = (int *)(s + a.K + nb * 4);
         for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+            const int *q = (const int *)(s + b * 32);
             int t = 0;
 #pragma unroll
-            for (int w = 0; w < 8; w++) t = __dp4a((int)q[b * 8 + w], 0x01010101, t);
-            xs_[b] = t;
+            for (int w = 0; w < 8; w++) t = __dp4a(q[w], 0x01010101, t);
+            tot_[b] = t;
         }
         __syncthreads();
     }
 };
 
+// Plain i8 activations (BitLinear, ime.rs:882): blocks of the weight format's BE elements,
+// chunk j at 16*(j ^ swz(b)); integer total per block.
+template <int BE>
 struct ActI8 {
-    static __host__ __device__ size_t bytes(int K) { return ((size_t)K + 15) / 16 * 16 + K / 16 * 4 + 16; }
-    static __device__ __forceinline__ const int8_t *xq(const uint8_t *s) { return (const int8_t *)s; }
-    static __device__ __forceinline__ const int *g16(const uint8_t *s, int K) {
-        return (const int *)(s + (K + 15) / 16 * 16);
+    static __host__ __device__ size_t bytes(int K) {
+        return (size_t)K + (size_t)(K / BE) * 4 + 16;
+    }
+    static __device__ __forceinline__ int swz(int b) { return BE >= 128 ? (b & 7) : ((b >> 2) & 1); }
+    static __device__ __forceinline__ const int8_t *chunk(const uint8_t *s, int b, int j) {
+        return (const int8_t *)(s + b * BE + 16 * (j ^ swz(b)));
+    }
+    static __device__ __forceinline__ int tot(const uint8_t *s, int K, int b) {
+        return reinterpret_cast<const int *>(s + K)[b];
     }
     static __device__ void stage(const KArgs &a, const uint8_t *x, uint8_t *s) {
-        if ((((uintptr_t)x) & 15) == 0) {
-            const int nv = a.K / 16;
-            for (int i = threadIdx.x; i < nv; i += blockDim.x)
-                reinterpret_cast<uint4 *>(s)[i] = __ldg(reinterpret_cast<const uint4 *>(x) + i);
-        } else {
-            for (int i = threadIdx.x; i < a.K; i += blockDim.x) s[i] = x[i];
+        const int nw = a.K / 4;
+        const bool aligned = (((uintptr_t)x) & 3) == 0;
+        for (int i = threadIdx.x; i < nw; i += blockDim.x) {
+            uint32_t v;
+            if (aligned) {
+                v = __ldg(reinterpret_cast<const uint32_t *>(x) + i);
+            } else {
+                v = (uint32_t)x[4 * i] | ((uint32_t)x[4 * i + 1] << 8) |
+                    ((uint32_t)x[4 * i + 2] << 16) | ((uint32_t)x[4 * i + 3] << 24);
+            }
+            const int e = 4 * i, b = e / BE, off = e - b * BE, j = off >> 4;
+            *(uint32_t *)(s + b * BE + 16 * (j ^ swz(b)) + (off & 15)) = v;
         }
         __syncthreads();
-        int *g = (int *)g16(s, a.K);
-        const uint32_t *q = (const uint32_t *)s;
-        for (int j = threadIdx.x; j < a.K / 16; j += blockDim.x) {
+        int *tot_ = (int *)(s + a.K);
+        for (int b = threadIdx.x; b < a.K / BE; b += blockDim.x) {
+            const int *q = (const int *)(s + b * BE);
             int t = 0;
-#pragma unroll
-            for (int w = 0; w < 4; w++) t = __dp4a((int)q[j * 4 + w], 0x01010101, t);
-            g[j] = t;
+            for (int w = 0; w < BE / 4; w++) t = __dp4a(q[w], 0x01010101, t);
+            tot_[b] = t;
         }
         __syncthreads();
     }
 };
 
 // ---------------------------------------------------------------- formats
-// Each format: CPB lanes per block (16-byte chunks per block), MINS (second integer sum),
-// Ld (per-chunk registers), load(), dot() -> partial integer sums, finish() -> block value.
+// load(): the block's registers; value(): exact integer sums (iv) and the f32 block value.
 
-struct LdW {
-    uint4 w;
-    uint32_t d;
-};
+template <int QCH>
+__device__ __forceinline__ void load_chunks(const KArgs &a, size_t row, int b, uint4 (&q)[QCH]) {
+    const uint8_t *rp = a.qs + row * a.qs_row;
+#pragma unroll
+    for (int j = 0; j < QCH; j++) q[j] = ldg_stream(rp + qs_chunk_offset(a.nb, QCH, b, j));
+}
 
-// Q4_0 x Q8_0 (quant_q8.rs:672-684)
+// dot of the low (mask 0x0F) or in-place high (mask 0xF0, result x16) nibbles of 16 bytes
+__device__ __forceinline__ int dot_lo(uint4 w, int4 x, int acc) {
+    acc = dp4a_ss((int)(w.x & 0x0F0F0F0F), x.x, acc);
+    acc = dp4a_ss((int)(w.y & 0x0F0F0F0F), x.y, acc);
+    acc = dp4a_ss((int)(w.z & 0x0F0F0F0F), x.z, acc);
+    return dp4a_ss((int)(w.w & 0x0F0F0F0F), x.w, acc);
+}
+__device__ __forceinline__ int dot_hi16(uint4 w, int4 x, int acc) {
+    acc = dp4a_us(w.x & 0xF0F0F0F0u, x.x, acc);
+    acc = dp4a_us(w.y & 0xF0F0F0F0u, x.y, acc);
+    acc = dp4a_us(w.z & 0xF0F0F0F0u, x.z, acc);
+    return dp4a_us(w.w & 0xF0F0F0F0u, x.w, acc);
+}
+__device__ __forceinline__ int dot_i8(uint4 w, int4 x, int acc) {
+    acc = dp4a_ss((int)w.x, x.x, acc);
+    acc = dp4a_ss((int)w.y, x.y, acc);
+    acc = dp4a_ss((int)w.z, x.z, acc);
+    return dp4a_ss((int)w.w, x.w, acc);
+}
+
+// Q4_0 x Q8_0 (quant_q8.rs:672-684): low nibble of byte j -> element j, high -> j+16, minus 8.
 struct FQ4_0 {
-    static constexpr int CPB = 1;
-    static constexpr bool MINS = false;
+    static constexpr int BE = 32;
     using Act = ActQ80;
-    using Ld = LdW;
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int q) {
-        Ld l;
-        l.w = ldg_stream(a.qs + row * a.qs_row + 16 * (size_t)q);
-        l.d = ldg_u16(a.d + row * a.nb + q);
-        return l;
-    }
-    static __device__ __forceinline__ int2 dot(const KArgs &a, const uint8_t *s, const Ld &l, int q) {
-        const int8_t *x = Act::xq(s) + 32 * q;
-        int4 xl = lds_v4(x), xh = lds_v4(x + 16);
-        int lo = 0, hi = 0;
-        lo = dp4a_ss(l.w.x & 0x0F0F0F0F, xl.x, lo);
-        lo = dp4a_ss(l.w.y & 0x0F0F0F0F, xl.y, lo);
-        lo = dp4a_ss(l.w.z & 0x0F0F0F0F, xl.z, lo);
-        lo = dp4a_ss(l.w.w & 0x0F0F0F0F, xl.w, lo);
-        hi = dp4a_us(l.w.x & 0xF0F0F0F0u, xh.x, hi);
-        hi = dp4a_us(l.w.y & 0xF0F0F0F0u, xh.y, hi);
-        hi = dp4a_us(l.w.z & 0xF0F0F0F0u, xh.z, hi);
-        hi = dp4a_us(l.w.w & 0xF0F0F0F0u, xh.w, hi);
-        // sum (n - 8) * x = sum n * x - 8 * sum x; the high nibbles were kept in place (x16).
-        return make_int2(lo + (hi >> 4) - 8 * Act::xs(s, a.K)[q], 0);
-    }
-    static __device__ __forceinline__ float finish(const KArgs &a, const uint8_t *s, const Ld &l,
-                                                   int b, int2 v) {
-        float dw = f16_finite(l.d), xd = Act::xd(s, a.K)[b];
-        if (dw == 0.0f || xd == 0.0f) return 0.0f;
-        return __fmul_rn((float)v.x, __fmul_rn(dw, xd));
-    }
-};
-
-// Q8_0 x Q8_0 (quant_q8.rs:707-717); also the Q8_0 BitLinear weight (ime.rs:840-853).
-template <class A>
-struct FQ8_0 {
-    static constexpr int CPB = 2;
-    static constexpr bool MINS = false;
-    using Act = A;
-    using Ld = LdW;
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int q) {
-        Ld l;
-        l.w = ldg_stream(a.qs + row * a.qs_row + 16 * (size_t)q);
-        l.d = ldg_u16(a.d + row * a.nb + (q >> 1));
-        return l;
-    }
-    static __device__ __forceinline__ int2 dot(const KArgs &a, const uint8_t *s, const Ld &l, int q) {
-        int4 x = lds_v4(Act::xq(s) + 16 * q);
-        int t = 0;
-        t = dp4a_ss((int)l.w.x, x.x, t);
-        t = dp4a_ss((int)l.w.y, x.y, t);
-        t = dp4a_ss((int)l.w.z, x.z, t);
-        t = dp4a_ss((int)l.w.w, x.w, t);
-        return make_int2(t, 0);
-    }
-    static __device__ __forceinline__ float finish(const KArgs &a, const uint8_t *s, const Ld &l,
-                                                   int b, int2 v);
-};
-template <>
-__device__ __forceinline__ float FQ8_0<ActQ80>::finish(const KArgs &a, const uint8_t *s,
-                                                        const Ld &l, int b, int2 v) {
-    float dw = f16_finite(l.d), xd = ActQ80::xd(s, a.K)[b];
-    if (dw == 0.0f || xd == 0.0f) return 0.0f;
-    return __fmul_rn((float)v.x, __fmul_rn(dw, xd));
-}
-// BitLinear (ime.rs:918-929): (f32)dot * (block_scale * act_scale), no zero shortcut.
-template <>
-__device__ __forceinline__ float FQ8_0<ActI8>::finish(const KArgs &a, const uint8_t *s,
-                                                       const Ld &l, int b, int2 v) {
-    return __fmul_rn((float)v.x, __fmul_rn(f16_finite(l.d), a.act_scale));
-}
-
-// Q4_K x Q8_K (quant_q8.rs:1834-1862). Chunk q: superblock q/8, part p = q%8 covers
-// qs[16p..16p+16] of the superblock = chunk c = p/2, half h = p%2: low nibbles pair with
-// x[64c+16h..], high nibbles with x[64c+32+16h..]; sub-block scales 2c and 2c+1.
-struct FQ4_K {
-    static constexpr int CPB = 8;
-    static constexpr bool MINS = true;
-    using Act = ActQ8K;
     struct Ld {
-        uint4 w, s;
-    };
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int q) {
-        Ld l;
-        l.w = ldg_stream(a.qs + row * a.qs_row + 16 * (size_t)q);
-        l.s = __ldg(reinterpret_cast<const uint4 *>(a.sc + row * a.sc_row + 16 * (size_t)(q >> 3)));
-        return l;
-    }
-    static __device__ __forceinline__ int2 dot(const KArgs &a, const uint8_t *s, const Ld &l, int q) {
-        const int sb = q >> 3, p = q & 7, c = p >> 1, h = p & 1;
-        const int8_t *x = Act::xq(s) + 256 * sb + 64 * c + 16 * h;
-        int4 xl = lds_v4(x), xh = lds_v4(x + 32);
-        int lo = 0, hi = 0;
-        lo = dp4a_ss(l.w.x & 0x0F0F0F0F, xl.x, lo);
-        lo = dp4a_ss(l.w.y & 0x0F0F0F0F, xl.y, lo);
-        lo = dp4a_ss(l.w.z & 0x0F0F0F0F, xl.z, lo);
-        lo = dp4a_ss(l.w.w & 0x0F0F0F0F, xl.w, lo);
-        hi = dp4a_us(l.w.x & 0xF0F0F0F0u, xh.x, hi);
-        hi = dp4a_us(l.w.y & 0xF0F0F0F0u, xh.y, hi);
-        hi = dp4a_us(l.w.z & 0xF0F0F0F0u, xh.z, hi);
-        hi = dp4a_us(l.w.w & 0xF0F0F0F0u, xh.w, hi);
-        hi >>= 4;
-        // 6-bit scales/mins j = 2c, 2c+1 (unpack_q4_q5_k_scales_mins, quant_q8.rs:1817-1830)
-        const int sh = 16 * (c & 1);
-        uint32_t scp, mp;
-        if (c < 2) {
-            scp = (l.s.y >> sh) & 0x3F3F;
-            mp = (l.s.z >> sh) & 0x3F3F;
-        } else {
-            scp = ((l.s.w >> sh) & 0x0F0F) | (((l.s.y >> sh) >> 2) & 0x3030);
-            mp = (((l.s.w >> sh) >> 4) & 0x0F0F) | (((l.s.z >> sh) >> 2) & 0x3030);
-        }
-        const int16_t *bs = Act::bs(s, a.K) + 16 * sb + 4 * c + h;
-        int sumi = (int)(scp & 0xFF) * lo + (int)(scp >> 8) * hi;
-        int mins = (int)(mp & 0xFF) * (int)bs[0] + (int)(mp >> 8) * (int)bs[2];
-        return make_int2(sumi, mins);
-    }
-    static __device__ __forceinline__ float finish(const KArgs &a, const uint8_t *s, const Ld &l,
-                                                   int b, int2 v) {
-        float d = f16_finite(l.s.x & 0xFFFF), dmin = f16_finite(l.s.x >> 16);
-        float xd = Act::xd(s, a.K)[b];
-        if ((d == 0.0f && dmin == 0.0f) || xd == 0.0f) return 0.0f;
-        return __fsub_rn(__fmul_rn(__fmul_rn(d, xd), (float)v.x),
-                         __fmul_rn(__fmul_rn(dmin, xd), (float)v.y));
-    }
-};
-
-// Q6_K x Q8_K (quant_q8.rs:1903-1942). Chunk q: superblock q/4, item t = q%4 (h = t/2,
-// i = t%2) holds 16 l-values: A = ql[64h+16i..], B = ql[64h+32+16i..], H = qh[32h+16i..];
-// values (6-bit, unsigned) pair with x[128h+16i + 32*k] for k = 0..3 and scales
-// sc[8h+i+2k]; the -32 offset is applied as -32 * bsum of the same 16 elements.
-struct FQ6_K {
-    static constexpr int CPB = 4;
-    static constexpr bool MINS = false;
-    using Act = ActQ8K;
-    struct Ld {
-        uint4 A, B, H;
-        uint2 sc;
+        uint4 q[1];
         uint32_t d;
     };
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int q) {
-        const int sb = q >> 2, t = q & 3, h = t >> 1;
-        const uint8_t *base = a.qs + row * a.qs_row + 192 * (size_t)sb + 16 * t;
+    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
         Ld l;
-        l.A = ldg_stream(base);
-        l.B = ldg_stream(base + 64);
-        l.H = ldg_stream(base + 128);
-        l.sc = __ldg(reinterpret_cast<const uint2 *>(a.sc + row * a.sc_row + 16 * (size_t)sb + 8 * h));
-        l.d = ldg_u16(a.d + row * a.nb + sb);
+        load_chunks<1>(a, row, b, l.q);
+        l.d = ldg_u16(a.d + row * a.nb + b);
         return l;
     }
-    static __device__ __forceinline__ int dot16(uint4 A, uint4 B, uint4 H, const int8_t *x,
-                                                int4 &S) {
-        int4 x1 = lds_v4(x), x2 = lds_v4(x + 32), x3 = lds_v4(x + 64), x4 = lds_v4(x + 96);
-        const uint32_t a_[4] = {A.x, A.y, A.z, A.w}, b_[4] = {B.x, B.y, B.z, B.w},
-                       h_[4] = {H.x, H.y, H.z, H.w};
-        const int x1_[4] = {x1.x, x1.y, x1.z, x1.w}, x2_[4] = {x2.x, x2.y, x2.z, x2.w},
-                  x3_[4] = {x3.x, x3.y, x3.z, x3.w}, x4_[4] = {x4.x, x4.y, x4.z, x4.w};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            uint32_t u1 = (a_[j] & 0x0F0F0F0F) | ((h_[j] << 4) & 0x30303030);
-            uint32_t u2 = (b_[j] & 0x0F0F0F0F) | ((h_[j] << 2) & 0x30303030);
-            uint32_t u3 = ((a_[j] >> 4) & 0x0F0F0F0F) | (h_[j] & 0x30303030);
-            uint32_t u4 = ((b_[j] >> 4) & 0x0F0F0F0F) | ((h_[j] >> 2) & 0x30303030);
-            S.x = dp4a_ss((int)u1, x1_[j], S.x);
-            S.y = dp4a_ss((int)u2, x2_[j], S.y);
-            S.z = dp4a_ss((int)u3, x3_[j], S.z);
-            S.w = dp4a_ss((int)u4, x4_[j], S.w);
-        }
-        return 0;
-    }
-    static __device__ __forceinline__ int2 dot(const KArgs &a, const uint8_t *s, const Ld &l, int q) {
-        const int sb = q >> 2, t = q & 3, h = t >> 1, i = t & 1;
-        const int e0 = 256 * sb + 128 * h + 16 * i;
-        int4 S = make_int4(0, 0, 0, 0);
-        dot16(l.A, l.B, l.H, Act::xq(s) + e0, S);
-        const int16_t *bs = Act::bs(s, a.K) + (e0 >> 4);
-        const int sc0 = (int)(int8_t)(l.sc.x >> (8 * i)), sc1 = (int)(int8_t)(l.sc.x >> (8 * i + 16));
-        const int sc2 = (int)(int8_t)(l.sc.y >> (8 * i)), sc3 = (int)(int8_t)(l.sc.y >> (8 * i + 16));
-        int sumi = sc0 * (S.x - 32 * (int)bs[0]) + sc1 * (S.y - 32 * (int)bs[2]) +
-                   sc2 * (S.z - 32 * (int)bs[4]) + sc3 * (S.w - 32 * (int)bs[6]);
-        return make_int2(sumi, 0);
-    }
-    static __device__ __forceinline__ float finish(const KArgs &a, const uint8_t *s, const Ld &l,
-                                                   int b, int2 v) {
-        float d = f16_finite(l.d), xd = Act::xd(s, a.K)[b];
-        if (d == 0.0f || xd == 0.0f) return 0.0f;
-        return __fmul_rn(__fmul_rn(d, xd), (float)v.x);
+    static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
+                                                  int b, int2 &iv) {
+        const int lo = dot_lo(l.q[0], lds4(Act::chunk(s, b, 0)), 0);
+        const int hi = dot_hi16(l.q[0], lds4(Act::chunk(s, b, 1)), 0);
+        const int sumi = lo + (hi >> 4) - 8 * Act::tot(s, a.K, b);
+        iv = make_int2(sumi, 0);
+        const float dw = f16_finite(l.d), xd = Act::xd(s, a.K, b);
+        if (dw == 0.0f || xd == 0.0f) return 0.0f;
+        return __fmul_rn((float)sumi, __fmul_rn(dw, xd));
     }
 };
 
-// TQ2_0 x Q8_K (quant_q8.rs:1992-2003) and TQ2_0/TQ1_0 BitLinear (ime.rs:918-929). Chunk q
-// covers elements 64q..64q+63 of the row; in the GPU layout word W, bit pair j, byte b holds
-// the 2-bit code of element 64q + 16W + 4j + b, so (w >> 2j) & 0x03030303 lines up with four
-// consecutive activations. Codes are value + 1; the +1 is removed as -sum(x).
+// Q8_0 weights: x Q8_0 activations (quant_q8.rs:707-717) or i8 BitLinear activations
+// (ime.rs:840-853, :918-929).
 template <class A>
-struct FTQ2 {
-    static constexpr int CPB = 4;
-    static constexpr bool MINS = false;
+struct FQ8_0 {
+    static constexpr int BE = 32;
     using Act = A;
-    using Ld = LdW;
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int q) {
+    struct Ld {
+        uint4 q[2];
+        uint32_t d;
+    };
+    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
         Ld l;
-        l.w = ldg_stream(a.qs + row * a.qs_row + 16 * (size_t)q);
-        l.d = ldg_u16(a.d + row * a.nb + (q >> 2));
+        load_chunks<2>(a, row, b, l.q);
+        l.d = ldg_u16(a.d + row * a.nb + b);
         return l;
     }
-    static __device__ __forceinline__ int sum_codes(const Ld &l, const int8_t *x) {
-        const uint32_t w_[4] = {l.w.x, l.w.y, l.w.z, l.w.w};
+    static __device__ __forceinline__ int sum(const uint8_t *s, const Ld &l, int b) {
+        return dot_i8(l.q[1], lds4(A::chunk(s, b, 1)), dot_i8(l.q[0], lds4(A::chunk(s, b, 0)), 0));
+    }
+    static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
+                                                  int b, int2 &iv);
+};
+template <>
+__device__ __forceinline__ float FQ8_0<ActQ80>::value(const KArgs &a, const uint8_t *s,
+                                                       const Ld &l, int b, int2 &iv) {
+    const int sumi = sum(s, l, b);
+    iv = make_int2(sumi, 0);
+    const float dw = f16_finite(l.d), xd = ActQ80::xd(s, a.K, b);
+    if (dw == 0.0f || xd == 0.0f) return 0.0f;
+    return __fmul_rn((float)sumi, __fmul_rn(dw, xd));
+}
+template <>
+__device__ __forceinline__ float FQ8_0<ActI8<32>>::value(const KArgs &a, const uint8_t *s,
+                                                          const Ld &l, int b, int2 &iv) {
+    const int sumi = sum(s, l, b);
+    iv = make_int2(sumi, 0);
+    return __fmul_rn((float)sumi, __fmul_rn(f16_finite(l.d), a.act_scale));
+}
+
+// Q4_K x Q8_K (quant_q8.rs:1817-1862). Chunk pair (2c, 2c+1) holds qs[32c..32c+32]: low
+// nibbles pair with x[64c..64c+32] (activation chunks 4c, 4c+1), high nibbles with
+// x[64c+32..64c+64] (chunks 4c+2, 4c+3), scaled by the 6-bit sc[2c], sc[2c+1]; the min term
+// uses m[2c], m[2c+1] and the bsums of the same elements.
+struct FQ4_K {
+    static constexpr int BE = 256;
+    using Act = ActQ8K;
+    struct Ld {
+        uint4 q[8];
+        uint4 s;
+    };
+    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
+        Ld l;
+        load_chunks<8>(a, row, b, l.q);
+        l.s = __ldg(reinterpret_cast<const uint4 *>(a.sc + row * a.sc_row + 16 * (size_t)b));
+        return l;
+    }
+    static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
+                                                  int b, int2 &iv) {
+        // unpack_q4_q5_k_scales_mins: bytes of sc_lo/m_lo are sc[0..4]/m[0..4], of sc_hi/m_hi
+        // are sc[4..8]/m[4..8]
+        const uint32_t sc_lo = l.s.y & 0x3F3F3F3F, m_lo = l.s.z & 0x3F3F3F3F;
+        const uint32_t sc_hi = (l.s.w & 0x0F0F0F0F) | ((l.s.y >> 2) & 0x30303030);
+        const uint32_t m_hi = ((l.s.w >> 4) & 0x0F0F0F0F) | ((l.s.z >> 2) & 0x30303030);
+        const int4 b0 = ActQ8K::bsums_half(s, a.K, b, 0), b1 = ActQ8K::bsums_half(s, a.K, b, 1);
+        const int bs[16] = {(int)(int16_t)b0.x, b0.x >> 16, (int)(int16_t)b0.y, b0.y >> 16,
+                            (int)(int16_t)b0.z, b0.z >> 16, (int)(int16_t)b0.w, b0.w >> 16,
+                            (int)(int16_t)b1.x, b1.x >> 16, (int)(int16_t)b1.y, b1.y >> 16,
+                            (int)(int16_t)b1.z, b1.z >> 16, (int)(int16_t)b1.w, b1.w >> 16};
+        int sumi = 0, mins = 0;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint4 qa = l.q[2 * c], qb = l.q[2 * c + 1];
+            int slo = dot_lo(qa, lds4(ActQ8K::chunk(s, b, 4 * c)), 0);
+            slo = dot_lo(qb, lds4(ActQ8K::chunk(s, b, 4 * c + 1)), slo);
+            int shi = dot_hi16(qa, lds4(ActQ8K::chunk(s, b, 4 * c + 2)), 0);
+            shi = dot_hi16(qb, lds4(ActQ8K::chunk(s, b, 4 * c + 3)), shi) >> 4;
+            const uint32_t scw = c < 2 ? sc_lo : sc_hi, mw = c < 2 ? m_lo : m_hi;
+            const int k = 2 * (c & 1);
+            sumi += (int)((scw >> (8 * k)) & 0xFF) * slo + (int)((scw >> (8 * k + 8)) & 0xFF) * shi;
+            mins += (int)((mw >> (8 * k)) & 0xFF) * (bs[4 * c] + bs[4 * c + 1]) +
+                    (int)((mw >> (8 * k + 8)) & 0xFF) * (bs[4 * c + 2] + bs[4 * c + 3]);
+        }
+        iv = make_int2(sumi, mins);
+        const float d = f16_finite(l.s.x & 0xFFFF), dmin = f16_finite(l.s.x >> 16);
+        const float xd = ActQ8K::xd(s, a.K, b);
+        if ((d == 0.0f && dmin == 0.0f) || xd == 0.0f) return 0.0f;
+        return __fsub_rn(__fmul_rn(__fmul_rn(d, xd), (float)sumi),
+                         __fmul_rn(__fmul_rn(dmin, xd), (float)mins));
+    }
+};
+
+// Q6_K x Q8_K (quant_q8.rs:1903-1942). Chunks 0-7 are ql, 8-11 qh (GGUF order). For half h
+// and is = i: A = ql[64h+16i..] (chunk 4h+i), B = ql[64h+32+16i..] (4h+2+i),
+// H = qh[32h+16i..] (8+2h+i); the four 6-bit values pair with activation chunks 8h+i+{0,2,4,6}
+// and scales sc[8h+i+{0,2,4,6}]; -32 is applied through the matching bsums.
+struct FQ6_K {
+    static constexpr int BE = 256;
+    using Act = ActQ8K;
+    struct Ld {
+        uint4 q[12];
+        uint4 s;
+        uint32_t d;
+    };
+    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
+        Ld l;
+        load_chunks<12>(a, row, b, l.q);
+        l.s = __ldg(reinterpret_cast<const uint4 *>(a.sc + row * a.sc_row + 16 * (size_t)b));
+        l.d = ldg_u16(a.d + row * a.nb + b);
+        return l;
+    }
+    static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
+                                                  int b, int2 &iv) {
+        const int4 b0 = ActQ8K::bsums_half(s, a.K, b, 0), b1 = ActQ8K::bsums_half(s, a.K, b, 1);
+        const int bs[16] = {(int)(int16_t)b0.x, b0.x >> 16, (int)(int16_t)b0.y, b0.y >> 16,
+                            (int)(int16_t)b0.z, b0.z >> 16, (int)(int16_t)b0.w, b0.w >> 16,
+                            (int)(int16_t)b1.x, b1.x >> 16, (int)(int16_t)b1.y, b1.y >> 16,
+                            (int)(int16_t)b1.z, b1.z >> 16, (int)(int16_t)b1.w, b1.w >> 16};
+        const uint32_t scw[4] = {l.s.x, l.s.y, l.s.z, l.s.w};
+        int sumi = 0;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const uint4 A = l.q[4 * h + i], B = l.q[4 * h + 2 + i], H = l.q[8 + 2 * h + i];
+                const int c0 = 8 * h + i;
+                const int4 x1 = lds4(ActQ8K::chunk(s, b, c0)), x2 = lds4(ActQ8K::chunk(s, b, c0 + 2));
+                const int4 x3 = lds4(ActQ8K::chunk(s, b, c0 + 4)), x4 = lds4(ActQ8K::chunk(s, b, c0 + 6));
+                const uint32_t a_[4] = {A.x, A.y, A.z, A.w}, b_[4] = {B.x, B.y, B.z, B.w},
+                               h_[4] = {H.x, H.y, H.z, H.w};
+                const int x1_[4] = {x1.x, x1.y, x1.z, x1.w}, x2_[4] = {x2.x, x2.y, x2.z, x2.w},
+                          x3_[4] = {x3.x, x3.y, x3.z, x3.w}, x4_[4] = {x4.x, x4.y, x4.z, x4.w};
+                int S1 = 0, S2 = 0, S3 = 0, S4 = 0;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const uint32_t u1 = (a_[j] & 0x0F0F0F0F) | ((h_[j] << 4) & 0x30303030);
+                    const uint32_t u2 = (b_[j] & 0x0F0F0F0F) | ((h_[j] << 2) & 0x30303030);
+                    const uint32_t u3 = ((a_[j] >> 4) & 0x0F0F0F0F) | (h_[j] & 0x30303030);
+                    const uint32_t u4 = ((b_[j] >> 4) & 0x0F0F0F0F) | ((h_[j] >> 2) & 0x30303030);
+                    S1 = dp4a_ss((int)u1, x1_[j], S1);
+                    S2 = dp4a_ss((int)u2, x2_[j], S2);
+                    S3 = dp4a_ss((int)u3, x3_[j], S3);
+                    S4 = dp4a_ss((int)u4, x4_[j], S4);
+                }
+                // scales sc[c0 + {0,2,4,6}]: byte (c0 & 3) + {0, 2} of words c0/4 and c0/4 + 1
+                const uint32_t w0 = scw[c0 >> 2], w1 = scw[(c0 >> 2) + 1];
+                const int k = c0 & 3;
+                sumi += sbyte(w0, k) * (S1 - 32 * bs[c0]) + sbyte(w0, k + 2) * (S2 - 32 * bs[c0 + 2]) +
+                        sbyte(w1, k) * (S3 - 32 * bs[c0 + 4]) + sbyte(w1, k + 2) * (S4 - 32 * bs[c0 + 6]);
+            }
+        }
+        iv = make_int2(sumi, 0);
+        const float d = f16_finite(l.d), xd = ActQ8K::xd(s, a.K, b);
+        if (d == 0.0f || xd == 0.0f) return 0.0f;
+        return __fmul_rn(__fmul_rn(d, xd), (float)sumi);
+    }
+};
+
+// TQ2_0 / TQ1_0 x Q8_K (quant_q8.rs:1960-2003) and TQ2_0 / TQ1_0 BitLinear (ime.rs:918-929).
+// Chunk p, word W, bit pair j holds the codes (value + 1) of elements 64p+16W+4j+{0..3}, i.e.
+// word j of activation chunk 4p+W; the +1 is removed as -sum(x) over the block.
+template <class A>
+struct FTQ2 {
+    static constexpr int BE = 256;
+    using Act = A;
+    struct Ld {
+        uint4 q[4];
+        uint32_t d;
+    };
+    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
+        Ld l;
+        load_chunks<4>(a, row, b, l.q);
+        l.d = ldg_u16(a.d + row * a.nb + b);
+        return l;
+    }
+    static __device__ __forceinline__ int codes(const uint8_t *s, const Ld &l, int b) {
         int t = 0;
 #pragma unroll
-        for (int W = 0; W < 4; W++) {
-            int4 xv = lds_v4(x + 16 * W);
-            t = dp4a_ss((int)(w_[W] & 0x03030303), xv.x, t);
-            t = dp4a_ss((int)((w_[W] >> 2) & 0x03030303), xv.y, t);
-            t = dp4a_ss((int)((w_[W] >> 4) & 0x03030303), xv.z, t);
-            t = dp4a_ss((int)((w_[W] >> 6) & 0x03030303), xv.w, t);
+        for (int p = 0; p < 4; p++) {
+            const uint32_t w_[4] = {l.q[p].x, l.q[p].y, l.q[p].z, l.q[p].w};
+#pragma unroll
+            for (int W = 0; W < 4; W++) {
+                const int4 xv = lds4(A::chunk(s, b, 4 * p + W));
+                t = dp4a_ss((int)(w_[W] & 0x03030303), xv.x, t);
+                t = dp4a_ss((int)((w_[W] >> 2) & 0x03030303), xv.y, t);
+                t = dp4a_ss((int)((w_[W] >> 4) & 0x03030303), xv.z, t);
+                t = dp4a_ss((int)((w_[W] >> 6) & 0x03030303), xv.w, t);
+            }
         }
         return t;
     }
-    static __device__ __forceinline__ int2 dot(const KArgs &a, const uint8_t *s, const Ld &l, int q);
-    static __device__ __forceinline__ float finish(const KArgs &a, const uint8_t *s, const Ld &l,
-                                                   int b, int2 v);
+    static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
+                                                  int b, int2 &iv);
 };
 template <>
-__device__ __forceinline__ int2 FTQ2<ActQ8K>::dot(const KArgs &a, const uint8_t *s, const Ld &l,
-                                                  int q) {
-    int t = sum_codes(l, ActQ8K::xq(s) + 64 * q);
-    const int16_t *bs = ActQ8K::bs(s, a.K) + 4 * q;
-    return make_int2(t - ((int)bs[0] + (int)bs[1] + (int)bs[2] + (int)bs[3]), 0);
-}
-template <>
-__device__ __forceinline__ float FTQ2<ActQ8K>::finish(const KArgs &a, const uint8_t *s,
-                                                      const Ld &l, int b, int2 v) {
-    float xd = ActQ8K::xd(s, a.K)[b];
-    float dw = f16_finite(l.d);
+__device__ __forceinline__ float FTQ2<ActQ8K>::value(const KArgs &a, const uint8_t *s,
+                                                     const Ld &l, int b, int2 &iv) {
+    const int sumi = codes(s, l, b) - ActQ8K::tot(s, a.K, b);
+    iv = make_int2(sumi, 0);
+    const float xd = ActQ8K::xd(s, a.K, b);
+    const float dw = f16_finite(l.d);
     if (xd == 0.0f || dw == 0.0f) return 0.0f;
-    return __fmul_rn((float)v.x, __fmul_rn(dw, xd));
+    return __fmul_rn((float)sumi, __fmul_rn(dw, xd));
 }
 template <>
-__device__ __forceinline__ int2 FTQ2<ActI8>::dot(const KArgs &a, const uint8_t *s, const Ld &l,
-                                                 int q) {
-    int t = sum_codes(l, ActI8::xq(s) + 64 * q);
-    const int *g = ActI8::g16(s, a.K) + 4 * q;
-    return make_int2(t - (g[0] + g[1] + g[2] + g[3]), 0);
-}
-template <>
-__device__ __forceinline__ float FTQ2<ActI8>::finish(const KArgs &a, const uint8_t *s,
-                                                     const Ld &l, int b, int2 v) {
-    return __fmul_rn((float)v.x, __fmul_rn(f16_finite(l.d), a.act_scale));
+__device__ __forceinline__ float FTQ2<ActI8<256>>::value(const KArgs &a, const uint8_t *s,
+                                                         const Ld &l, int b, int2 &iv) {
+    const int sumi = codes(s, l, b) - ActI8<256>::tot(s, a.K, b);
+    iv = make_int2(sumi, 0);
+    return __fmul_rn((float)sumi, __fmul_rn(f16_finite(l.d), a.act_scale));
 }
 
-// I2_S BitLinear (quant.rs:370-377, ime.rs:918-929). Chunk q = half h of block q/2: byte g in
-// [16h, 16h+16) carries elements g, 32+g, 64+g, 96+g in bits [7:6], [5:4], [3:2], [1:0].
+// I2_S BitLinear (quant.rs:370-377, ime.rs:918-929). Chunk h holds bytes 16h..16h+16; byte g
+// carries elements g, 32+g, 64+g, 96+g in bits [7:6], [5:4], [3:2], [1:0], so plane j of
+// word W pairs with word W of activation chunk 2j+h.
 struct FI2S {
-    static constexpr int CPB = 2;
-    static constexpr bool MINS = false;
-    using Act = ActI8;
+    static constexpr int BE = 128;
+    using Act = ActI8<128>;
     struct Ld {
-        uint4 w;
+        uint4 q[2];
     };
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int q) {
+    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
         Ld l;
-        l.w = ldg_stream(a.qs + row * a.qs_row + 16 * (size_t)q);
+        load_chunks<2>(a, row, b, l.q);
         return l;
     }
-    static __device__ __forceinline__ int2 dot(const KArgs &a, const uint8_t *s, const Ld &l, int q) {
-        const int b = q >> 1, h = q & 1;
-        const int8_t *x = Act::xq(s) + 128 * b + 16 * h;
-        int4 x0 = lds_v4(x), x1 = lds_v4(x + 32), x2 = lds_v4(x + 64), x3 = lds_v4(x + 96);
-        const uint32_t w_[4] = {l.w.x, l.w.y, l.w.z, l.w.w};
-        const int x0_[4] = {x0.x, x0.y, x0.z, x0.w}, x1_[4] = {x1.x, x1.y, x1.z, x1.w},
-                  x2_[4] = {x2.x, x2.y, x2.z, x2.w}, x3_[4] = {x3.x, x3.y, x3.z, x3.w};
+    static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
+                                                  int b, int2 &iv) {
         int t = 0;
 #pragma unroll
-        for (int W = 0; W < 4; W++) {
-            t = dp4a_ss((int)((w_[W] >> 6) & 0x03030303), x0_[W], t);
-            t = dp4a_ss((int)((w_[W] >> 4) & 0x03030303), x1_[W], t);
-            t = dp4a_ss((int)((w_[W] >> 2) & 0x03030303), x2_[W], t);
-            t = dp4a_ss((int)(w_[W] & 0x03030303), x3_[W], t);
+        for (int h = 0; h < 2; h++) {
+            const uint32_t w_[4] = {l.q[h].x, l.q[h].y, l.q[h].z, l.q[h].w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int4 xv = lds4(Act::chunk(s, b, 2 * j + h));
+                const int x_[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int W = 0; W < 4; W++)
+                    t = dp4a_ss((int)((w_[W] >> (6 - 2 * j)) & 0x03030303), x_[W], t);
+            }
         }
-        const int *g = Act::g16(s, a.K) + 8 * b + h;
-        return make_int2(t - (g[0] + g[2] + g[4] + g[6]), 0);
-    }
-    static __device__ __forceinline__ float finish(const KArgs &a, const uint8_t *s, const Ld &l,
-                                                   int b, int2 v) {
-        return __fmul_rn((float)v.x, __fmul_rn(a.i2s_scale, a.act_scale));
+        const int sumi = t - Act::tot(s, a.K, b);
+        iv = make_int2(sumi, 0);
+        return __fmul_rn((float)sumi, __fmul_rn(a.i2s_scale, a.act_scale));
     }
 };
 
@@ -473,76 +510,67 @@ struct FI2S {
 
 constexpr int WARPS = 8;
 
-template <class F, int U, bool DIAG>
-__global__ void __launch_bounds__(WARPS * 32, 2) gemv_kernel(KArgs a) {
+template <class F, bool DIAG>
+__global__ void __launch_bounds__(WARPS * 32) gemv_kernel(KArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int tok = blockIdx.y;
     KArgs args = a;
     if (a.act_scales) args.act_scale = a.act_scales[tok];
     F::Act::stage(args, a.x + (size_t)tok * a.x_row_stride, smem);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nchunks = a.nb * F::CPB;
+    const int lane = threadIdx.x & 31;
+    const int lpr = 1 << a.lpr_shift, rpw = 32 >> a.lpr_shift;
+    const int li = lane & (lpr - 1), rsub = lane >> a.lpr_shift;
+    const size_t wid = (size_t)blockIdx.x * WARPS + (threadIdx.x >> 5);
+    const size_t nwarps = (size_t)gridDim.x * WARPS;
     float *out = a.out + (size_t)tok * a.out_ld;
-    for (size_t row = a.row_begin + (size_t)blockIdx.x * WARPS + warp; row < a.row_end;
-         row += (size_t)gridDim.x * WARPS) {
+    for (size_t r0 = a.row_begin + wid * rpw; r0 < a.row_end; r0 += nwarps * rpw) {
+        const size_t row = r0 + rsub;
+        const bool row_ok = row < a.row_end;
         float acc = 0.0f;
-        for (int base = 0; base < nchunks; base += 32 * U) {
-            typename F::Ld ld[U];
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                int q = base + 32 * u + lane;
-                if (q < nchunks) ld[u] = F::load(args, row, q);
-            }
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int q = base + 32 * u + lane;
-                const bool valid = q < nchunks;
-                if (base + 32 * u >= nchunks) break;  // warp-uniform
-                int2 v = valid ? F::dot(args, smem, ld[u], q) : make_int2(0, 0);
-#pragma unroll
-                for (int m = 1; m < F::CPB; m <<= 1) {
-                    v.x += __shfl_xor_sync(0xffffffffu, v.x, m);
-                    if (F::MINS) v.y += __shfl_xor_sync(0xffffffffu, v.y, m);
-                }
-                if (valid && (q % F::CPB) == 0) {
-                    const int b = q / F::CPB;
-                    float val = F::finish(args, smem, ld[u], b, v);
-                    if (DIAG) {
-                        size_t o = (row - a.row_begin) * (size_t)a.nb + b;
-                        a.dbg_sumi[o] = v.x;
-                        if (a.dbg_mins) a.dbg_mins[o] = v.y;
-                        a.dbg_val[o] = val;
-                    } else {
-                        acc = __fadd_rn(acc, val);
-                    }
+        for (int b0 = 0; b0 < a.nb; b0 += lpr) {
+            const int b = b0 + li;
+            if (row_ok && b < a.nb) {
+                const typename F::Ld l = F::load(args, row, b);
+                int2 iv;
+                const float v = F::value(args, smem, l, b, iv);
+                if (DIAG) {
+                    const size_t o = (row - a.row_begin) * (size_t)a.nb + b;
+                    a.dbg_sumi[o] = iv.x;
+                    if (a.dbg_mins) a.dbg_mins[o] = iv.y;
+                    a.dbg_val[o] = v;
+                } else {
+                    acc = __fadd_rn(acc, v);
                 }
             }
         }
         if (!DIAG) {
-#pragma unroll
-            for (int m = 16; m > 0; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
-            if (lane == 0) out[row - a.row_begin] = acc;
+            for (int m = lpr >> 1; m > 0; m >>= 1)
+                acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+            if (li == 0 && row_ok) out[row - a.row_begin] = acc;
         }
     }
 }
 
 // ---------------------------------------------------------------- launch
 
-template <class F, int U, bool DIAG>
+template <class F, bool DIAG>
 static int launch_t(const KArgs &a, size_t m, cudaStream_t st, const char *name) {
     const size_t smem = F::Act::bytes(a.K);
-    auto kern = gemv_kernel<F, U, DIAG>;
-    static int occ = -1;  // per template instance; the device set is homogeneous (B200)
-    if (occ < 0) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        occ = 0;
+    auto kern = gemv_kernel<F, DIAG>;
+    static int per_sm_cached = -1;  // one value per template instance (B200 only)
+    static size_t smem_cached = 0;
+    if (per_sm_cached < 0 || smem_cached != smem) {
+        if (per_sm_cached < 0)
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        int per_sm = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WARPS * 32, smem);
+        per_sm_cached = per_sm < 1 ? 1 : per_sm;
+        smem_cached = smem;
     }
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WARPS * 32, smem);
-    if (per_sm < 1) per_sm = 1;
-    size_t rows = a.row_end - a.row_begin;
-    size_t want = (rows + WARPS - 1) / WARPS;
-    size_t cap = (size_t)num_sms() * per_sm;
+    const int rpw = 32 >> a.lpr_shift;
+    const size_t rows = a.row_end - a.row_begin;
+    const size_t want = (rows + (size_t)WARPS * rpw - 1) / ((size_t)WARPS * rpw);
+    const size_t cap = (size_t)num_sms() * per_sm_cached;
     size_t gx = want;
     if (m * gx > cap) gx = (cap + m - 1) / m;
     if (gx < 1) gx = 1;
@@ -551,11 +579,7 @@ static int launch_t(const KArgs &a, size_t m, cudaStream_t st, const char *name)
     return check_launch(name);
 }
 
-static size_t smem_limit_k(int act_kind) {
-    // shared bytes per element ~1.2; keep well inside the 160 KiB opt-in set above
-    (void)act_kind;
-    return 120 * 1024;
-}
+static const size_t MAX_K = 120 * 1024;
 
 int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
     const jkb_weight *w = L.w;
@@ -576,40 +600,43 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
     a.row_end = L.row_end;
     a.nb = (int)w->nb;
     a.K = (int)w->cols;
+    int sh = 0;
+    while ((1 << sh) < a.nb && sh < 5) sh++;
+    a.lpr_shift = sh;
     a.dbg_sumi = L.dbg_sumi;
     a.dbg_mins = L.dbg_mins;
     a.dbg_val = L.dbg_val;
-    if (w->cols > smem_limit_k(L.act_kind))
-        return fail(JKB_E_BOUNDS, w->name, w->offset, w->cols, smem_limit_k(L.act_kind),
+    if (w->cols > MAX_K)
+        return fail(JKB_E_BOUNDS, w->name, w->offset, w->cols, MAX_K,
                     "input length %zu exceeds the %zu-element activation limit of the GEMV "
                     "kernels",
-                    w->cols, smem_limit_k(L.act_kind));
+                    w->cols, MAX_K);
     if (L.row_end <= L.row_begin) return JKB_OK;
     const bool diag = L.dbg_sumi != nullptr;
     const size_t m = L.m ? L.m : 1;
-#define JKB_LAUNCH(F, U)                                                                  \
-    return diag ? launch_t<F, U, true>(a, m, st, "gemv_kernel<diag>")                     \
-                : launch_t<F, U, false>(a, m, st, "gemv_kernel")
+#define JKB_LAUNCH(F)                                                    \
+    return diag ? launch_t<F, true>(a, m, st, "gemv_kernel<diag>")       \
+                : launch_t<F, false>(a, m, st, "gemv_kernel")
     switch (w->gpu_format) {
     case GF_Q4_0:
-        if (L.act_kind == ACT_Q8_0) JKB_LAUNCH(FQ4_0, 4);
+        if (L.act_kind == ACT_Q8_0) JKB_LAUNCH(FQ4_0);
         break;
     case GF_Q8_0:
-        if (L.act_kind == ACT_Q8_0) JKB_LAUNCH(FQ8_0<ActQ80>, 4);
-        if (L.act_kind == ACT_I8) JKB_LAUNCH(FQ8_0<ActI8>, 4);
+        if (L.act_kind == ACT_Q8_0) JKB_LAUNCH(FQ8_0<ActQ80>);
+        if (L.act_kind == ACT_I8) JKB_LAUNCH(FQ8_0<ActI8<32>>);
         break;
     case GF_Q4_K:
-        if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FQ4_K, 4);
+        if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FQ4_K);
         break;
     case GF_Q6_K:
-        if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FQ6_K, 2);
+        if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FQ6_K);
         break;
     case GF_TQ2_0:
-        if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FTQ2<ActQ8K>, 4);
-        if (L.act_kind == ACT_I8) JKB_LAUNCH(FTQ2<ActI8>, 4);
+        if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FTQ2<ActQ8K>);
+        if (L.act_kind == ACT_I8) JKB_LAUNCH(FTQ2<ActI8<256>>);
         break;
     case GF_I2_S:
-        if (L.act_kind == ACT_I8) JKB_LAUNCH(FI2S, 4);
+        if (L.act_kind == ACT_I8) JKB_LAUNCH(FI2S);
         break;
     }
 #undef JKB_LAUNCH

@@ -2,15 +2,14 @@
 // GPU layouts used by the GEMV / BitLinear kernels (jkb_weight) and by the GEMM
 // (jkb_repacked_weight, the i8-expanded RepackedWeight of repack.rs:1092-1133).
 //
-// jkb_weight planes (every row contiguous, rows back to back, block order kept):
+// jkb_weight planes (every row contiguous, rows back to back, block order kept; the quant
+// plane's 16-byte chunks are lane-interleaved in groups of 32 blocks, see gpu_layout.cuh):
 //   Q4_0   qs: 16 B/block, the GGUF nibble bytes        d: f16 per block
 //   Q8_0   qs: 32 B/block, the GGUF i8 quants           d: f16 per block
 //   Q4_K_M qs: 128 B/block, GGUF qs bytes               sc: 16 B/block = d, dmin, scales[12]
-//   Q6_K   qs: 192 B/block, ql/qh regrouped per lane    sc: 16 B/block i8 scales, d: f16
-//          (item t = 2h+i owns A = ql[64h+16i..+16], B = ql[64h+32+16i..+16],
-//           H = qh[32h+16i..+16]; stored as A0..A3 | B0..B3 | H0..H3)
-//   TQ2_0  qs: 64 B/block, 2-bit codes re-ordered so that word W, bit pair j, byte b holds
-//          element 16W+4j+b of the 64-element chunk   d: f16 per block
+//   Q6_K   qs: 192 B/block, GGUF ql[128] then qh[64]    sc: 16 B/block i8 scales, d: f16
+//   TQ2_0  qs: 64 B/block, 2-bit codes re-ordered so that chunk p, word W, bit pair j, byte b
+//          holds element 64p+16W+4j+b                   d: f16 per block
 //   TQ1_0  decoded at load into the TQ2_0 GPU layout (same codes 0..2)
 //   I2_S   qs: 32 B/block, GGUF bytes unchanged; the trailer scale is kept on the host
 // Byte counts equal the GGUF payload (except TQ1_0, whose base-3 bytes grow from 54 to 66).
@@ -18,6 +17,7 @@
 #include <cstring>
 #include <vector>
 
+#include "gpu_layout.cuh"
 #include "jkb_internal.h"
 
 namespace jkb {
@@ -26,51 +26,45 @@ __device__ __forceinline__ uint16_t rd16(const uint8_t *p) {
     return (uint16_t)(p[0] | (p[1] << 8));
 }
 
-__global__ void relayout_kernel(int quant, const uint8_t *__restrict__ raw, size_t rows,
-                                size_t nb, size_t raw_row, int bb, uint8_t *__restrict__ qs,
-                                size_t qs_row, uint8_t *__restrict__ sc, size_t sc_row,
-                                uint16_t *__restrict__ d) {
+// One thread per (row, block): scale planes are written [row][block], quant bytes go to the
+// lane-interleaved chunk positions of gpu_layout.cuh. `payload` holds the block's quant bytes
+// in GPU chunk order (chunk j = payload[16j .. 16j+16]).
+__global__ void relayout_kernel(int quant, int gpu_format, const uint8_t *__restrict__ raw,
+                                size_t rows, size_t nb, size_t raw_row, int bb,
+                                uint8_t *__restrict__ qs, size_t qs_row, uint8_t *__restrict__ sc,
+                                size_t sc_row, uint16_t *__restrict__ d) {
     size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= rows * nb) return;
     size_t r = idx / nb, b = idx % nb;
     const uint8_t *blk = raw + r * raw_row + b * (size_t)bb;
+    uint8_t payload[192];
     switch (quant) {
-    case JKB_Q4_0: {
+    case JKB_Q4_0:  // 16 nibble bytes, GGUF order
         d[idx] = rd16(blk);
-        uint8_t *o = qs + r * qs_row + 16 * b;
-        for (int i = 0; i < 16; i++) o[i] = blk[2 + i];
+        for (int i = 0; i < 16; i++) payload[i] = blk[2 + i];
         break;
-    }
-    case JKB_Q8_0: {
+    case JKB_Q8_0:  // 32 i8 quants
         d[idx] = rd16(blk);
-        uint8_t *o = qs + r * qs_row + 32 * b;
-        for (int i = 0; i < 32; i++) o[i] = blk[2 + i];
+        for (int i = 0; i < 32; i++) payload[i] = blk[2 + i];
         break;
-    }
-    case JKB_Q4_K_M: {
+    case JKB_Q4_K_M: {  // d, dmin, scales[12] to the scale plane; qs[128] in GGUF order
         uint8_t *s = sc + r * sc_row + 16 * b;
         for (int i = 0; i < 16; i++) s[i] = blk[i];
-        uint8_t *o = qs + r * qs_row + 128 * b;
-        for (int i = 0; i < 128; i++) o[i] = blk[16 + i];
+        for (int i = 0; i < 128; i++) payload[i] = blk[16 + i];
         break;
     }
-    case JKB_Q6_K: {
+    case JKB_Q6_K: {  // ql[128] qh[64] in GGUF order; i8 scales and d to their planes
         uint8_t *s = sc + r * sc_row + 16 * b;
         for (int i = 0; i < 16; i++) s[i] = blk[192 + i];
         d[idx] = rd16(blk + 208);
-        uint8_t *o = qs + r * qs_row + 192 * b;
-        for (int t = 0; t < 4; t++) {
-            int h = t >> 1, i = t & 1;
-            for (int j = 0; j < 16; j++) {
-                o[16 * t + j] = blk[64 * h + 16 * i + j];
-                o[64 + 16 * t + j] = blk[64 * h + 32 + 16 * i + j];
-                o[128 + 16 * t + j] = blk[128 + 32 * h + 16 * i + j];
-            }
-        }
+        for (int i = 0; i < 192; i++) payload[i] = blk[i];
         break;
     }
     case JKB_TQ2_0:
     case JKB_TQ1_0: {
+        // 2-bit codes (value + 1) re-ordered so that chunk p, word W, bit pair j, byte q holds
+        // element 64p + 16W + 4j + q: (word >> 2j) & 0x03030303 then lines up with four
+        // consecutive activations.
         d[idx] = rd16(blk);
         uint8_t codes[256];
         if (quant == JKB_TQ2_0) {
@@ -85,20 +79,23 @@ __global__ void relayout_kernel(int quant, const uint8_t *__restrict__ raw, size
             }
             codes[255] = (uint8_t)(blk[53] % 3);
         }
-        uint8_t *o = qs + r * qs_row + 64 * b;
-        for (int i = 0; i < 64; i++) o[i] = 0;
+        for (int i = 0; i < 64; i++) payload[i] = 0;
         for (int e = 0; e < 256; e++) {
             int p = e >> 6, W = (e & 63) >> 4, j = (e & 15) >> 2, bq = e & 3;
-            o[16 * p + 4 * W + bq] |= (uint8_t)(codes[e] << (2 * j));
+            payload[16 * p + 4 * W + bq] |= (uint8_t)(codes[e] << (2 * j));
         }
         break;
     }
-    case JKB_I2_S: {
-        uint8_t *o = qs + r * qs_row + 32 * b;
-        for (int i = 0; i < 32; i++) o[i] = blk[i];
+    case JKB_I2_S:  // 32 bytes, GGUF order (byte g carries elements g, 32+g, 64+g, 96+g)
+        for (int i = 0; i < 32; i++) payload[i] = blk[i];
         break;
+    default: return;
     }
-    default: break;
+    const int qch = qs_chunks(gpu_format);
+    uint8_t *row = qs + r * qs_row;
+    for (int j = 0; j < qch; j++) {
+        uint8_t *o = row + qs_chunk_offset((int)nb, qch, (int)b, j);
+        for (int i = 0; i < 16; i++) o[i] = payload[16 * j + i];
     }
 }
 
@@ -367,8 +364,8 @@ static int weight_upload(const jkb_tensor_view *v, size_t rows, size_t cols, cud
     }
     size_t n = rows * w->nb;
     relayout_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
-        v->quant, raw, rows, w->nb, w->nb * (size_t)f->block_bytes, f->block_bytes, qs,
-        w->p.qs_row, sc, w->p.sc_row, d);
+        v->quant, w->gpu_format, raw, rows, w->nb, w->nb * (size_t)f->block_bytes,
+        f->block_bytes, qs, w->p.qs_row, sc, w->p.sc_row, d);
     rc = check_launch("relayout_kernel");
     if (owned) {
         cudaStreamSynchronize(st);
