@@ -72,10 +72,65 @@ __device__ __forceinline__ float f16_finite(uint32_t bits) {
     float v = __half2float(__ushort_as_half((unsigned short)bits));
     return ((bits >> 10) & 0x1F) == 0x1F ? 0.0f : v;
 }
+// Programmatic dependent launch: wait for the preceding grid's memory to be visible / allow
+// the next grid in the stream to start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+}
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
 __device__ __forceinline__ int4 lds4(const void *p) { return *reinterpret_cast<const int4 *>(p); }
 __device__ __forceinline__ int sbyte(uint32_t w, int k) { return (int)(int8_t)(w >> (8 * k)); }
 
 // ---------------------------------------------------------------- activation staging
+
+// Copies `nwords` 32-bit words of x into shared memory through scatter(word_index, value).
+// With a 16-byte aligned x it uses 16-byte loads, and each thread issues a round of up to 4
+// loads before any store, so staging costs about one memory round trip.
+template <class Scatter>
+__device__ __forceinline__ void stage_words(const uint8_t *x, int nwords, Scatter scatter) {
+    constexpr int R = 4;
+    const int nt = blockDim.x;
+    if ((((uintptr_t)x) & 15) == 0) {
+        const int nvec = nwords >> 2;
+        for (int base = 0; base < nvec; base += R * nt) {
+            uint4 v[R];
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int i = base + r * nt + threadIdx.x;
+                if (i < nvec) v[r] = __ldg(reinterpret_cast<const uint4 *>(x) + i);
+            }
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int i = base + r * nt + threadIdx.x;
+                if (i < nvec) {
+                    scatter(4 * i, v[r].x);
+                    scatter(4 * i + 1, v[r].y);
+                    scatter(4 * i + 2, v[r].z);
+                    scatter(4 * i + 3, v[r].w);
+                }
+            }
+        }
+        for (int wi = 4 * nvec + threadIdx.x; wi < nwords; wi += nt)
+            scatter(wi, __ldg(reinterpret_cast<const uint32_t *>(x) + wi));
+    } else {
+        for (int base = 0; base < nwords; base += R * nt) {
+            uint32_t v[R];
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int i = base + r * nt + threadIdx.x;
+                if (i < nwords) v[r] = __ldg(reinterpret_cast<const uint32_t *>(x) + i);
+            }
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int i = base + r * nt + threadIdx.x;
+                if (i < nwords) scatter(i, v[r]);
+            }
+        }
+    }
+}
 
 // BlockQ8K activations (quant_q8.rs:62-71). Superblock s: 256 i8 at s*256 with chunk j at
 // 16*(j ^ (s & 7)); its 16 bsums (two 16-byte halves, half h at 16*(h ^ ((s >> 2) & 1))).
@@ -96,11 +151,10 @@ struct ActQ8K {
         return reinterpret_cast<const int *>(s + K + (K / 256) * 36)[sb];
     }
     static __device__ void stage(const KArgs &a, const uint8_t *x, uint8_t *s) {
-        const int nb = a.K / 256, total = nb * 73;  // 292-byte BlockQ8K = 73 words
-        float *xd_ = (float *)(s + a.K + nb * 32);
-        for (int i = threadIdx.x; i < total; i += blockDim.x) {
-            const int blk = i / 73, w = i - blk * 73;
-            const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(x + (size_t)blk * 292) + w);
+        const int nb = a.K / 256, K = a.K;  // 292-byte BlockQ8K = 73 words
+        float *xd_ = (float *)(s + K + nb * 32);
+        stage_words(x, nb * 73, [&](int wi, uint32_t v) {
+            const int blk = wi / 73, w = wi - blk * 73;
             if (w == 0) {
                 xd_[blk] = __uint_as_float(v);
             } else if (w <= 64) {
@@ -108,9 +162,9 @@ struct ActQ8K {
                 *(uint32_t *)(s + blk * 256 + 16 * (j ^ (blk & 7)) + 4 * (ww & 3)) = v;
             } else {
                 const int ww = w - 65, h = ww >> 2;
-                *(uint32_t *)(s + a.K + blk * 32 + 16 * (h ^ ((blk >> 2) & 1)) + 4 * (ww & 3)) = v;
+                *(uint32_t *)(s + K + blk * 32 + 16 * (h ^ ((blk >> 2) & 1)) + 4 * (ww & 3)) = v;
             }
-        }
+        });
         __syncthreads();
         int *tot_ = (int *)(s + a.K + nb * 36);
         for (int blk = threadIdx.x; blk < nb; blk += blockDim.x) {
@@ -139,18 +193,17 @@ struct ActQ80 {
         return reinterpret_cast<const int *>(s + K + (K / 32) * 4)[b];
     }
     static __device__ void stage(const KArgs &a, const uint8_t *x, uint8_t *s) {
-        const int nb = a.K / 32, total = nb * 9;  // 36-byte BlockQ8_0 = 9 words
+        const int nb = a.K / 32;  // 36-byte BlockQ8_0 = 9 words
         float *xd_ = (float *)(s + a.K);
-        for (int i = threadIdx.x; i < total; i += blockDim.x) {
-            const int blk = i / 9, w = i - blk * 9;
-            const uint32_t v = __ldg(reinterpret_cast<const uint32_t *>(x + (size_t)blk * 36) + w);
+        stage_words(x, nb * 9, [&](int wi, uint32_t v) {
+            const int blk = wi / 9, w = wi - blk * 9;
             if (w == 0) {
                 xd_[blk] = __uint_as_float(v);
             } else {
                 const int ww = w - 1, j = ww >> 2;
                 *(uint32_t *)(s + blk * 32 + 16 * (j ^ ((blk >> 2) & 1)) + 4 * (ww & 3)) = v;
             }
-        }
+        });
         __syncthreads();
         int *tot_ = (int *)(s + a.K + nb * 4);
         for (int b = threadIdx.x; b < nb; b += blockDim.x) {
@@ -179,18 +232,16 @@ struct ActI8 {
         return reinterpret_cast<const int *>(s + K)[b];
     }
     static __device__ void stage(const KArgs &a, const uint8_t *x, uint8_t *s) {
-        const int nw = a.K / 4;
-        const bool aligned = (((uintptr_t)x) & 3) == 0;
-        for (int i = threadIdx.x; i < nw; i += blockDim.x) {
-            uint32_t v;
-            if (aligned) {
-                v = __ldg(reinterpret_cast<const uint32_t *>(x) + i);
-            } else {
-                v = (uint32_t)x[4 * i] | ((uint32_t)x[4 * i + 1] << 8) |
-                    ((uint32_t)x[4 * i + 2] << 16) | ((uint32_t)x[4 * i + 3] << 24);
-            }
-            const int e = 4 * i, b = e / BE, off = e - b * BE, j = off >> 4;
+        auto put = [&](int wi, uint32_t v) {
+            const int e = 4 * wi, b = e / BE, off = e - b * BE, j = off >> 4;
             *(uint32_t *)(s + b * BE + 16 * (j ^ swz(b)) + (off & 15)) = v;
+        };
+        if ((((uintptr_t)x) & 3) == 0) {
+            stage_words(x, a.K / 4, put);
+        } else {
+            for (int i = threadIdx.x; i < a.K / 4; i += blockDim.x)
+                put(i, (uint32_t)x[4 * i] | ((uint32_t)x[4 * i + 1] << 8) |
+                           ((uint32_t)x[4 * i + 2] << 16) | ((uint32_t)x[4 * i + 3] << 24));
         }
         __syncthreads();
         int *tot_ = (int *)(s + a.K);
@@ -212,6 +263,13 @@ __device__ __forceinline__ void load_chunks(const KArgs &a, size_t row, int b, u
     const uint8_t *rp = a.qs + row * a.qs_row;
 #pragma unroll
     for (int j = 0; j < QCH; j++) q[j] = ldg_stream(rp + qs_chunk_offset(a.nb, QCH, b, j));
+}
+
+template <int QCH>
+__device__ __forceinline__ void prefetch_chunks(const KArgs &a, size_t row, int b) {
+    const uint8_t *rp = a.qs + row * a.qs_row;
+#pragma unroll
+    for (int j = 0; j < QCH; j++) prefetch_l2(rp + qs_chunk_offset(a.nb, QCH, b, j));
 }
 
 // dot of the low (mask 0x0F) or in-place high (mask 0xF0, result x16) nibbles of 16 bytes
@@ -242,6 +300,9 @@ struct FQ4_0 {
         uint4 q[1];
         uint32_t d;
     };
+    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
+        prefetch_chunks<1>(a, row, b);
+    }
     static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
         Ld l;
         load_chunks<1>(a, row, b, l.q);
@@ -270,6 +331,9 @@ struct FQ8_0 {
         uint4 q[2];
         uint32_t d;
     };
+    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
+        prefetch_chunks<2>(a, row, b);
+    }
     static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
         Ld l;
         load_chunks<2>(a, row, b, l.q);
@@ -310,6 +374,9 @@ struct FQ4_K {
         uint4 q[8];
         uint4 s;
     };
+    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
+        prefetch_chunks<8>(a, row, b);
+    }
     static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
         Ld l;
         load_chunks<8>(a, row, b, l.q);
@@ -363,6 +430,9 @@ struct FQ6_K {
         uint4 s;
         uint32_t d;
     };
+    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
+        prefetch_chunks<12>(a, row, b);
+    }
     static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
         Ld l;
         load_chunks<12>(a, row, b, l.q);
@@ -428,6 +498,9 @@ struct FTQ2 {
         uint4 q[4];
         uint32_t d;
     };
+    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
+        prefetch_chunks<4>(a, row, b);
+    }
     static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
         Ld l;
         load_chunks<4>(a, row, b, l.q);
@@ -480,6 +553,9 @@ struct FI2S {
     struct Ld {
         uint4 q[2];
     };
+    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
+        prefetch_chunks<2>(a, row, b);
+    }
     static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
         Ld l;
         load_chunks<2>(a, row, b, l.q);
@@ -508,46 +584,65 @@ struct FI2S {
 
 // ---------------------------------------------------------------- the kernel
 
-constexpr int WARPS = 8;
+constexpr int MAX_WARPS = 8;
 
 template <class F, bool DIAG>
-__global__ void __launch_bounds__(WARPS * 32) gemv_kernel(KArgs a) {
+__global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int tok = blockIdx.y;
     KArgs args = a;
-    if (a.act_scales) args.act_scale = a.act_scales[tok];
-    F::Act::stage(args, a.x + (size_t)tok * a.x_row_stride, smem);
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
     const int lpr = 1 << a.lpr_shift, rpw = 32 >> a.lpr_shift;
     const int li = lane & (lpr - 1), rsub = lane >> a.lpr_shift;
-    const size_t wid = (size_t)blockIdx.x * WARPS + (threadIdx.x >> 5);
-    const size_t nwarps = (size_t)gridDim.x * WARPS;
+    const size_t wid = (size_t)blockIdx.x * warps + (threadIdx.x >> 5);
+    const size_t nwarps = (size_t)gridDim.x * warps;
     float *out = a.out + (size_t)tok * a.out_ld;
-    for (size_t r0 = a.row_begin + wid * rpw; r0 < a.row_end; r0 += nwarps * rpw) {
-        const size_t row = r0 + rsub;
-        const bool row_ok = row < a.row_end;
-        float acc = 0.0f;
-        for (int b0 = 0; b0 < a.nb; b0 += lpr) {
-            const int b = b0 + li;
-            if (row_ok && b < a.nb) {
-                const typename F::Ld l = F::load(args, row, b);
-                int2 iv;
-                const float v = F::value(args, smem, l, b, iv);
-                if (DIAG) {
-                    const size_t o = (row - a.row_begin) * (size_t)a.nb + b;
-                    a.dbg_sumi[o] = iv.x;
-                    if (a.dbg_mins) a.dbg_mins[o] = iv.y;
-                    a.dbg_val[o] = v;
-                } else {
-                    acc = __fadd_rn(acc, v);
-                }
+    const size_t stride = nwarps * rpw;
+    size_t r0 = a.row_begin + wid * rpw;  // warp-uniform position (r0, b0)
+    int b0 = 0;
+    float acc = 0.0f;
+    // one block of row r0 + rsub: the exact integer sums and the f32 block value
+    auto consume = [&](const typename F::Ld &l, int b) {
+        int2 iv;
+        const float v = F::value(args, smem, l, b, iv);
+        if (DIAG) {
+            const size_t o = (r0 + rsub - a.row_begin) * (size_t)a.nb + b;
+            a.dbg_sumi[o] = iv.x;
+            if (a.dbg_mins) a.dbg_mins[o] = iv.y;
+            a.dbg_val[o] = v;
+        } else {
+            acc = __fadd_rn(acc, v);
+        }
+    };
+    // advance to the next block column; at the end of a row, reduce its lanes and store
+    auto advance = [&]() {
+        b0 += lpr;
+        if (b0 >= a.nb) {
+            if (!DIAG) {
+                for (int m = lpr >> 1; m > 0; m >>= 1)
+                    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+                if (li == 0 && r0 + rsub < a.row_end) out[r0 + rsub - a.row_begin] = acc;
             }
+            acc = 0.0f;
+            b0 = 0;
+            r0 += stride;
         }
-        if (!DIAG) {
-            for (int m = lpr >> 1; m > 0; m >>= 1)
-                acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
-            if (li == 0 && row_ok) out[row - a.row_begin] = acc;
+    };
+    // Weights never depend on the previous kernel in the stream; the activation may. Start
+    // pulling this warp's first blocks into L2, then wait for the previous grid (programmatic
+    // dependent launch) before staging the activation.
+    if (r0 + rsub < a.row_end && li < a.nb) F::prefetch(args, r0 + rsub, li);
+    pdl_wait();
+    pdl_launch_dependents();
+    if (a.act_scales) args.act_scale = a.act_scales[tok];
+    F::Act::stage(args, a.x + (size_t)tok * a.x_row_stride, smem);
+    while (r0 < a.row_end) {
+        const int b = b0 + li;
+        if (r0 + rsub < a.row_end && b < a.nb) {
+            const typename F::Ld l = F::load(args, r0 + rsub, b);
+            consume(l, b);
         }
+        advance();
     }
 }
 
@@ -557,26 +652,38 @@ template <class F, bool DIAG>
 static int launch_t(const KArgs &a, size_t m, cudaStream_t st, const char *name) {
     const size_t smem = F::Act::bytes(a.K);
     auto kern = gemv_kernel<F, DIAG>;
-    static int per_sm_cached = -1;  // one value per template instance (B200 only)
+    // occupancy per CTA size (8, 4 or 2 warps), cached per template instance (B200 only)
+    static int per_sm_cached[4] = {-1, -1, -1, -1};
     static size_t smem_cached = 0;
-    if (per_sm_cached < 0 || smem_cached != smem) {
-        if (per_sm_cached < 0)
-            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-        int per_sm = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, WARPS * 32, smem);
-        per_sm_cached = per_sm < 1 ? 1 : per_sm;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        attr_set = true;
+    }
+    if (smem_cached != smem) {
+        for (int i = 0; i < 4; i++) per_sm_cached[i] = -1;
         smem_cached = smem;
     }
     const int rpw = 32 >> a.lpr_shift;
     const size_t rows = a.row_end - a.row_begin;
-    const size_t want = (rows + (size_t)WARPS * rpw - 1) / ((size_t)WARPS * rpw);
-    const size_t cap = (size_t)num_sms() * per_sm_cached;
+    const size_t sms = (size_t)num_sms();
+    // Fewer warps per CTA when the matrix is small, so that every SM gets work.
+    int warps = MAX_WARPS;
+    while (warps > 2 && m * ((rows + (size_t)warps * rpw - 1) / ((size_t)warps * rpw)) < sms)
+        warps >>= 1;
+    const int slot = warps == 8 ? 0 : warps == 4 ? 1 : 2;
+    if (per_sm_cached[slot] < 0) {
+        int per_sm = 0;
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, warps * 32, smem);
+        per_sm_cached[slot] = per_sm < 1 ? 1 : per_sm;
+    }
+    const size_t want = (rows + (size_t)warps * rpw - 1) / ((size_t)warps * rpw);
+    const size_t cap = sms * per_sm_cached[slot];
     size_t gx = want;
     if (m * gx > cap) gx = (cap + m - 1) / m;
     if (gx < 1) gx = 1;
-    dim3 grid((unsigned)gx, (unsigned)m);
-    kern<<<grid, WARPS * 32, smem, st>>>(a);
-    return check_launch(name);
+    cudaError_t e = launch_pdl(kern, dim3((unsigned)gx, (unsigned)m), dim3(warps * 32), smem, st, a);
+    return e == cudaSuccess ? JKB_OK : fail_cuda(e, name);
 }
 
 static const size_t MAX_K = 120 * 1024;

@@ -110,6 +110,25 @@ constexpr uint32_t ACT_MAGIC = 0x4A4B4131u;       // "JKA1"
 int num_sms();
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Launches with programmatic stream serialization: the kernel may start while the previous
+// kernel in the stream finishes; it must execute griddepcontrol.wait before touching memory
+// the previous kernel writes or reads.
+template <class... KArgsT, class... ArgsT>
+cudaError_t launch_pdl(void (*kern)(KArgsT...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, ArgsT... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Reference validators over a stored 2-D/1-D shape (quant.rs:1810-1894 and its per-format
 // twins quant.rs:762-892, :1315-1394, lib.rs:1195-1260): accepts [rows, cols] or GGUF
 // [cols, rows]; writes the (rows, cols) interpretation.

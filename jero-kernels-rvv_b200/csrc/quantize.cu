@@ -24,6 +24,8 @@ template <bool VEC>
 __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float *__restrict__ x,
                                                             size_t nblocks,
                                                             uint8_t *__restrict__ out) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
     size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     size_t blk = gid >> 3;
     int sub = (int)(gid & 7);
@@ -69,6 +71,8 @@ template <bool VEC>
 __global__ void __launch_bounds__(256) quantize_q8_k_kernel(const float *__restrict__ x,
                                                             size_t nblocks,
                                                             uint8_t *__restrict__ out) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
     size_t blk = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     int lane = threadIdx.x & 31;
     bool valid = blk < nblocks;
@@ -275,11 +279,11 @@ static int launch_q8_0(const float *x, size_t nblocks, void *out, cudaStream_t s
     size_t threads = nblocks * 8;
     unsigned grid = (unsigned)((threads + 255) / 256);
     bool vec = ((uintptr_t)x & 15) == 0;
-    if (vec)
-        quantize_q8_0_kernel<true><<<grid, 256, 0, st>>>(x, nblocks, (uint8_t *)out);
-    else
-        quantize_q8_0_kernel<false><<<grid, 256, 0, st>>>(x, nblocks, (uint8_t *)out);
-    return check_launch("quantize_q8_0_kernel");
+    cudaError_t e = vec ? launch_pdl(quantize_q8_0_kernel<true>, dim3(grid), dim3(256), 0, st, x,
+                                     nblocks, (uint8_t *)out)
+                        : launch_pdl(quantize_q8_0_kernel<false>, dim3(grid), dim3(256), 0, st, x,
+                                     nblocks, (uint8_t *)out);
+    return e == cudaSuccess ? JKB_OK : fail_cuda(e, "quantize_q8_0_kernel");
 }
 
 static int launch_q8_k(const float *x, size_t nblocks, void *out, cudaStream_t st) {
@@ -290,11 +294,11 @@ static int launch_q8_k(const float *x, size_t nblocks, void *out, cudaStream_t s
     size_t threads = nblocks * 32;
     unsigned grid = (unsigned)((threads + 255) / 256);
     bool vec = ((uintptr_t)x & 15) == 0;
-    if (vec)
-        quantize_q8_k_kernel<true><<<grid, 256, 0, st>>>(x, nblocks, (uint8_t *)out);
-    else
-        quantize_q8_k_kernel<false><<<grid, 256, 0, st>>>(x, nblocks, (uint8_t *)out);
-    return check_launch("quantize_q8_k_kernel");
+    cudaError_t e = vec ? launch_pdl(quantize_q8_k_kernel<true>, dim3(grid), dim3(256), 0, st, x,
+                                     nblocks, (uint8_t *)out)
+                        : launch_pdl(quantize_q8_k_kernel<false>, dim3(grid), dim3(256), 0, st, x,
+                                     nblocks, (uint8_t *)out);
+    return e == cudaSuccess ? JKB_OK : fail_cuda(e, "quantize_q8_k_kernel");
 }
 
 static bool check_act(const jkb_act_q8 *a) { return a && a->magic == ACT_MAGIC; }
