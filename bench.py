@@ -4,9 +4,13 @@
 Default workload: the Llama-3-8B decode GEMV set at batch 1 --
 Q4_K_M q/o 4096->4096, k/v 4096->1024, gate/up 4096->14336, down 14336->4096 and the Q6_K
 lm_head 4096->128256, each fed by its own Q8_K-quantized activation. One step quantizes the
-five activation vectors and runs the eight GEMVs through the C ABI (jkb200). Weights are
-synthetic N(0, 0.02) rows quantized by this file's numpy quantizers (a seeded pool of rows
-tiled to full size; GEMV time does not depend on the values), activations N(0, 1).
+five f32 activation vectors to Q8_K and runs the eight GEMVs through the C ABI (jkb200): by
+default with the f32-input entries (vec_dot_q4_k_m_rvv / vec_dot_q6_k_rvv, the quantization
+inside the GEMV launch), the matrices that share an input in one grouped launch -- q/k/v,
+o, gate/up, down, lm_head: 5 launches -- as a decoder layer allows; with --unfused as five
+quantize launches plus eight GEMV launches. Weights are synthetic N(0, 0.02) rows quantized
+by this file's numpy quantizers (a seeded pool of rows tiled to full size; GEMV time does not
+depend on the values), activations N(0, 1).
 
 Metric: algorithmic bytes per step (GGUF weight blocks + Q8_K activation blocks + f32 outputs,
 the BASELINE.md table) / step time, in GB/s. The seven layer matrices exist in two copies used
@@ -331,8 +335,24 @@ def run_gpu(args):
         offs[name] = (o, o + per)
         o += per
     fns = {Q4_K: jkb.gemv_q4_k_q8_k, Q6_K: jkb.gemv_q6_k_q8_k}
+    rvv = {Q4_K: jkb.vec_dot_q4_k_m_rvv, Q6_K: jkb.vec_dot_q6_k_rvv}
+    groups = {}  # activation stream -> matrices fed by it, in DECODE_8B order
+    for name, quant, per, cols, s, copies in shards:
+        groups.setdefault(s, []).append((name, quant, copies))
+
+    def run_group(s, copy):
+        """The matrices sharing activation s: one f32-input launch (grouped when several)."""
+        items = [(out[offs[n][0]:offs[n][1]], weights[(n, copy % c)]) for n, _, c in groups[s]]
+        if len(items) == 1:
+            rvv[groups[s][0][1]](items[0][0], items[0][1], xs[s])
+        else:
+            jkb.vec_dot_grouped_rvv(items, xs[s])
 
     def layer_part(copy):
+        if not args.unfused:
+            for s in ("x", "attn", "h", "a"):
+                run_group(s, copy)
+            return
         for s in ACTS:
             jkb.quantize_row_q8_k(xs[s], xq[s])
         for name, quant, per, cols, s, copies in shards:
@@ -342,6 +362,9 @@ def run_gpu(args):
             fns[quant](out[a:b], weights[(name, copy)], xq[s])
 
     def lm_head():
+        if not args.unfused:
+            run_group("f", 0)
+            return
         a, b = offs["lm_head"]
         fns[Q6_K](out[a:b], weights[("lm_head", 0)], xq["f"])
 
@@ -404,11 +427,15 @@ def run_gpu(args):
     def e2e_step(i):
         for s in ACTS:
             xs[s].copy_(host_in[s], non_blocking=True)
-        for s in ACTS:
-            jkb.quantize_row_q8_k(xs[s], xq[s])
-        for name, quant, per, cols, s, copies in shards:
-            a, b = offs[name]
-            fns[quant](out[a:b], weights[(name, i % copies)], xq[s])
+        if not args.unfused:
+            for s in ("x", "attn", "h", "a", "f"):
+                run_group(s, i)
+        else:
+            for s in ACTS:
+                jkb.quantize_row_q8_k(xs[s], xq[s])
+            for name, quant, per, cols, s, copies in shards:
+                a, b = offs[name]
+                fns[quant](out[a:b], weights[(name, i % copies)], xq[s])
         if world > 1:
             dist.all_gather_into_tensor(gathered, out)
         host_out.copy_(out, non_blocking=True)
@@ -448,12 +475,15 @@ def run_gpu(args):
                        "l2": "inputs larger than L2 (554 MB per step, layer weights in 2 "
                              "alternating copies)",
                        "parallelism": f"row-shard x{world}" + (" + NCCL all-gather" if world > 1 else "")},
-            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<FQ6_K> lm_head 4096->128256",
+            "roofline": {"bound": "hbm",
+                         "kernel": ("gemv_kernel<FQ6_K, ActQ8K>" if args.unfused else
+                                    "gemv_kernel<FQ6_K, ActQ8KF32>") + " lm_head 4096->128256",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": traffic, "algorithmic_bytes": lm_bytes,
                          "avg_ms": round(lm_ms, 5)},
-            "gpu_launches": args.steps * (len(ACTS) + len(DECODE_8B)),
+            "gpu_launches": args.steps * (len(ACTS) + len(DECODE_8B) if args.unfused
+                                          else len(groups)),
             "clocks": clocks,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
@@ -483,7 +513,11 @@ def run_kernel_case(args):
     ws = [jkb.Weight(jkb.TensorView(args.kernel, quant, [rows, cols], raw), rows, cols)
           for _ in range(copies)]
     x = torch.randn(cols, generator=torch.Generator().manual_seed(1)).cuda()
-    if quant == Q8_0:
+    if not args.unfused:
+        xq = x  # f32 input, quantized inside the GEMV launch
+        fn = {Q8_0: jkb.vec_dot_q8_0_rvv, Q4_K: jkb.vec_dot_q4_k_m_rvv,
+              Q6_K: jkb.vec_dot_q6_k_rvv}[quant]
+    elif quant == Q8_0:
         xq = jkb.empty_q8_0_blocks(cols // 32)
         jkb.quantize_row_q8_0(x, xq)
         fn = jkb.gemv_q8_0_q8_0
@@ -509,7 +543,8 @@ def run_kernel_case(args):
         e1.record(s)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.launches
-    print(json.dumps({"kernel": args.kernel, "rows": rows, "cols": cols, "copies": copies,
+    print(json.dumps({"kernel": args.kernel, "fused": not args.unfused, "rows": rows,
+                      "cols": cols, "copies": copies,
                       "us_per_launch": round(ms * 1e3, 3),
                       "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1)}))
 
@@ -526,6 +561,10 @@ def main():
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--cols", type=int, default=4096)
     ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--unfused", action="store_true",
+                    help="quantize each activation in its own launch and run one GEMV launch "
+                         "per matrix (jkb_quantize_row_q8_k + jkb_gemv_*) instead of the "
+                         "f32-input vec_dot_*_rvv / grouped launches")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -229,6 +229,39 @@ int jkb_vec_dot_q4_0(float *out, size_t out_len, const jkb_weight *w, const floa
 int jkb_vec_dot_i2_s(float *out, size_t out_len, const jkb_weight *w, const float *input,
                      size_t in_len, void *stream);
 
+/* ---- f32-activation integer paths (quantize the input to Q8, then the Q8 GEMV) ---- */
+/* The riscv64 entries below validate like the scalar vec_dot_* above, quantize the f32 input
+ * to BlockQ8K (Q4_K_M, Q6_K) or BlockQ8_0 (Q8_0, Q4_0) with the bit-exact quantizer and run the
+ * integer GEMV (vec_dot_q8_k_chunked_rvv quant_q8.rs:3280, vec_dot_q8_0_chunked_rvv
+ * quant_q8.rs:1712). Results equal jkb_quantize_row_q8_k / _q8_0 followed by jkb_gemv_*; the
+ * quantization runs inside the GEMV launch (each CTA quantizes the input while staging it). */
+/* lib.rs:1313 vec_dot_q4_k_m_rvv */
+int jkb_vec_dot_q4_k_m_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                           size_t in_len, void *stream);
+/* quant.rs:1056 vec_dot_q6_k_rvv */
+int jkb_vec_dot_q6_k_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                         size_t in_len, void *stream);
+/* quant.rs:999 vec_dot_q8_0_rvv */
+int jkb_vec_dot_q8_0_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                         size_t in_len, void *stream);
+/* quant.rs:1445 vec_dot_q4_0_rvv */
+int jkb_vec_dot_q4_0_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                         size_t in_len, void *stream);
+
+/* One product of jkb_vec_dot_grouped_rvv: out[0 .. out_len) = w x input. */
+typedef struct {
+    float *out;
+    size_t out_len;
+    const jkb_weight *w;
+} jkb_vec_dot_item;
+/* No reference counterpart: n_items (1..8) vec_dot_*_rvv calls that share one f32 input (the
+ * q/k/v or gate/up projections of a decoder layer) in one launch. Every weight must have the
+ * quant type of items[0] (Q4_0, Q8_0, Q4_K_M or Q6_K) and in_len columns; each item is
+ * validated exactly as its single call and its output equals that call's. Outputs must not
+ * overlap. */
+int jkb_vec_dot_grouped_rvv(const jkb_vec_dot_item *items, size_t n_items, const float *input,
+                            size_t in_len, void *stream);
+
 /* ---- ternary BitLinear (ime.rs) ---- */
 /* ime.rs:882 bitlinear_i8_rvv / :1005 bitlinear_i8_ime (bit-identical pair): TQ1_0, TQ2_0,
  * Q8_0 or I2_S weights, i8 activation (device) and its per-tensor scale. */

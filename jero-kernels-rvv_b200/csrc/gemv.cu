@@ -18,25 +18,38 @@
 //   BlockQ8K rows : xq[K] | bsums i16[16] per superblock | xd f32 | block totals i32
 //   BlockQ8_0 rows: xq[K] | xd f32 per block | block sums i32
 //   i8 rows       : xq[K] | block totals i32 (block = the weight format's block)
+#include <cooperative_groups.h>
 #include <cstdio>
 
 #include "gpu_layout.cuh"
 #include "jkb_internal.h"
+#include "quant_math.cuh"
 
 namespace jkb {
 
-struct KArgs {
+namespace cg = cooperative_groups;
+
+// One weight matrix of a launch. The launch walks a virtual row range [row_begin, row_end);
+// matrix i owns virtual rows [vbeg, next matrix's vbeg) and maps virtual row r to its own row
+// r - vbeg + row0, writing out[r - vbeg].
+struct MatArgs {
     const uint8_t *qs;
-    size_t qs_row;
     const uint8_t *sc;
-    size_t sc_row;
     const uint16_t *d;
+    float *out;
+    size_t vbeg, row0;
+};
+
+struct KArgs {
+    MatArgs mat[GEMV_MAX_MATS];
+    int nmat;
+    size_t qs_row;  // identical for every matrix of a launch (same format and cols)
+    size_t sc_row;
     const uint8_t *x;
     size_t x_row_stride;
     const float *act_scales;
     float act_scale;
     float i2s_scale;
-    float *out;
     size_t out_ld;
     size_t row_begin, row_end;
     int nb;  // blocks per row
@@ -44,6 +57,13 @@ struct KArgs {
     int lpr_shift;  // log2(lanes per row)
     int32_t *dbg_sumi, *dbg_mins;
     float *dbg_val;
+};
+
+// Row pointers of one weight row: quant plane, scale plane, f16 block scales.
+struct Row {
+    const uint8_t *q;
+    const uint8_t *s;
+    const uint16_t *d;
 };
 
 // ---------------------------------------------------------------- device helpers
@@ -135,6 +155,8 @@ __device__ __forceinline__ void stage_words(const uint8_t *x, int nwords, Scatte
 // BlockQ8K activations (quant_q8.rs:62-71). Superblock s: 256 i8 at s*256 with chunk j at
 // 16*(j ^ (s & 7)); its 16 bsums (two 16-byte halves, half h at 16*(h ^ ((s >> 2) & 1))).
 struct ActQ8K {
+    static constexpr bool kCluster = false;  // staged by each CTA alone
+    static int units(int) { return 0; }
     static __host__ __device__ size_t bytes(int K) {
         return (size_t)K + (size_t)(K / 256) * 40 + 16;
     }
@@ -180,6 +202,8 @@ struct ActQ8K {
 // BlockQ8_0 activations (quant_q8.rs:37-44). Block b: 32 i8 at b*32 with chunk j at
 // 16*(j ^ ((b >> 2) & 1)); f32 scale; integer sum of the 32 values.
 struct ActQ80 {
+    static constexpr bool kCluster = false;
+    static int units(int) { return 0; }
     static __host__ __device__ size_t bytes(int K) {
         return (size_t)K + (size_t)(K / 32) * 8 + 16;
     }
@@ -221,6 +245,8 @@ struct ActQ80 {
 // chunk j at 16*(j ^ swz(b)); integer total per block.
 template <int BE>
 struct ActI8 {
+    static constexpr bool kCluster = false;
+    static int units(int) { return 0; }
     static __host__ __device__ size_t bytes(int K) {
         return (size_t)K + (size_t)(K / BE) * 4 + 16;
     }
@@ -255,21 +281,190 @@ struct ActI8 {
     }
 };
 
+// Loads G consecutive f32 values at element e (a multiple of G) of x, as 16-byte vectors when x
+// is 16-byte aligned.
+template <int G>
+__device__ __forceinline__ void load_group(const float *x, bool vec, int e, float (&v)[G]) {
+    if (vec) {
+#pragma unroll
+        for (int i = 0; i < G; i += 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4 *>(x + e + i));
+            v[i] = t.x;
+            v[i + 1] = t.y;
+            v[i + 2] = t.z;
+            v[i + 3] = t.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < G; i++) v[i] = __ldg(x + e + i);
+    }
+}
+
+// f32 input quantized while staging, once per thread-block cluster. The CTAs of a cluster
+// split the quantization units (BlockQ8K superblocks / groups of four BlockQ8_0 blocks) among
+// their warps; each warp quantizes a unit and writes the result into the staging buffer of every
+// CTA of the cluster through distributed shared memory. Two cluster barriers bracket the writes:
+// the first makes sure every CTA of the cluster is running, the second makes every CTA's buffer
+// complete and visible. Every thread of every CTA reaches both.
+//
+// BlockQ8K (quantize_row_q8_k, quant_q8.rs:447-475), into the ActQ8K layout: lane l of the warp
+// takes elements 8l..8l+8 of the superblock; absmax by shuffles; lane l writes its 8 bytes, even
+// lanes the 16-element bsums, lane 0 the scale and the block total.
+struct ActQ8KF32 : ActQ8K {
+    static constexpr bool kCluster = true;  // launched as thread-block clusters
+    static int units(int K) { return K / 256; }
+    static __device__ void stage(const KArgs &a, const uint8_t *xb, uint8_t *s) {
+        cg::cluster_group cl = cg::this_cluster();
+        const unsigned C = cl.num_blocks(), rank = cl.block_rank();
+        const float *x = reinterpret_cast<const float *>(xb);
+        const bool vec = (((uintptr_t)x) & 15) == 0;
+        const int K = a.K, nsb = K / 256;
+        const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+        const int gw = (int)rank * nw + (threadIdx.x >> 5), gstride = (int)C * nw;
+        cl.sync();
+        // two superblocks per warp and round: both loads are issued before the arithmetic
+        for (int sb0 = gw; sb0 < nsb; sb0 += 2 * gstride) {  // warp-uniform
+            float vv[2][8];
+#pragma unroll
+            for (int r = 0; r < 2; r++)
+                if (sb0 + r * gstride < nsb)
+                    load_group<8>(x, vec, (sb0 + r * gstride) * 256 + 8 * lane, vv[r]);
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const int sb = sb0 + r * gstride;
+                if (sb >= nsb) break;  // warp-uniform
+                const float *v = vv[r];
+                float am = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 8; i++)
+                    if (finite_f(v[i])) am = fmaxf(am, fabsf(v[i]));
+#pragma unroll
+                for (int m = 1; m < 32; m <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, m));
+                float d, inv;
+                q8_scale(am, d, inv);
+                uint32_t p0 = 0, p1 = 0;
+                int si = 0;
+                if (am != 0.0f) {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const int q = round_scaled(v[i], inv);
+                        si += q;
+                        if (i < 4)
+                            p0 |= ((uint32_t)(q & 0xFF)) << (8 * i);
+                        else
+                            p1 |= ((uint32_t)(q & 0xFF)) << (8 * (i - 4));
+                    }
+                }
+                const int pair = si + __shfl_xor_sync(0xffffffffu, si, 1);
+                // lanes of equal parity hold the 16 distinct pair sums: reduce over them
+                int tot = pair;
+#pragma unroll
+                for (int m = 2; m < 32; m <<= 1) tot += __shfl_xor_sync(0xffffffffu, tot, m);
+                const int j = lane >> 1;  // 16-element group = chunk index
+                const uint32_t oq = sb * 256 + 16 * (j ^ (sb & 7)) + 8 * (lane & 1);
+                const uint32_t ob = K + sb * 32 + 16 * ((j >> 3) ^ ((sb >> 2) & 1)) + 2 * (j & 7);
+                const uint32_t od = K + nsb * 32 + 4 * sb, ot = K + nsb * 36 + 4 * sb;
+                for (unsigned dst = 0; dst < C; dst++) {
+                    uint8_t *rs = cl.map_shared_rank(s, dst);
+                    *reinterpret_cast<uint2 *>(rs + oq) = make_uint2(p0, p1);
+                    if ((lane & 1) == 0) *reinterpret_cast<int16_t *>(rs + ob) = (int16_t)pair;
+                    if (lane == 0) {
+                        *reinterpret_cast<float *>(rs + od) = d;
+                        *reinterpret_cast<int *>(rs + ot) = tot;
+                    }
+                }
+            }
+        }
+        cl.sync();
+    }
+};
+
+// BlockQ8_0 (quantize_row_q8_0_f32, quant_q8.rs:203-219), into the ActQ80 layout: a unit is
+// four consecutive 32-element blocks; lane l takes elements 4l..4l+4, so 8 lanes hold a block.
+struct ActQ80F32 : ActQ80 {
+    static constexpr bool kCluster = true;
+    static int units(int K) { return (K / 32 + 3) / 4; }
+    static __device__ void stage(const KArgs &a, const uint8_t *xb, uint8_t *s) {
+        cg::cluster_group cl = cg::this_cluster();
+        const unsigned C = cl.num_blocks(), rank = cl.block_rank();
+        const float *x = reinterpret_cast<const float *>(xb);
+        const bool vec = (((uintptr_t)x) & 15) == 0;
+        const int K = a.K, nbk = K / 32, nunit = (nbk + 3) / 4;
+        const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+        const int gw = (int)rank * nw + (threadIdx.x >> 5), gstride = (int)C * nw;
+        cl.sync();
+        const int sub = lane & 7;
+        // two units per warp and round: both loads are issued before the arithmetic
+        for (int u0 = gw; u0 < nunit; u0 += 2 * gstride) {  // warp-uniform
+            float vv[2][4];
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const int b = 4 * (u0 + r * gstride) + (lane >> 3);
+#pragma unroll
+                for (int i = 0; i < 4; i++) vv[r][i] = 0.0f;
+                if (u0 + r * gstride < nunit && b < nbk)
+                    load_group<4>(x, vec, b * 32 + 4 * sub, vv[r]);
+            }
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const int u = u0 + r * gstride;
+                if (u >= nunit) break;  // warp-uniform
+                const int b = 4 * u + (lane >> 3);
+                const bool valid = b < nbk;  // the last unit may hold fewer than four blocks
+                const float *v = vv[r];
+                float am = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    if (finite_f(v[i])) am = fmaxf(am, fabsf(v[i]));
+                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+                float d, inv;
+                q8_scale(am, d, inv);
+                uint32_t pk = 0;
+                int si = 0;
+                if (am != 0.0f) {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const int q = round_scaled(v[i], inv);
+                        si += q;
+                        pk |= ((uint32_t)(q & 0xFF)) << (8 * i);
+                    }
+                }
+                si += __shfl_xor_sync(0xffffffffu, si, 1);
+                si += __shfl_xor_sync(0xffffffffu, si, 2);
+                si += __shfl_xor_sync(0xffffffffu, si, 4);
+                if (valid) {
+                    const uint32_t oq = b * 32 + 16 * ((sub >> 2) ^ ((b >> 2) & 1)) + 4 * (sub & 3);
+                    const uint32_t od = K + 4 * b, ot = K + nbk * 4 + 4 * b;
+                    for (unsigned dst = 0; dst < C; dst++) {
+                        uint8_t *rs = cl.map_shared_rank(s, dst);
+                        *reinterpret_cast<uint32_t *>(rs + oq) = pk;
+                        if (sub == 0) {
+                            *reinterpret_cast<float *>(rs + od) = d;
+                            *reinterpret_cast<int *>(rs + ot) = si;
+                        }
+                    }
+                }
+            }
+        }
+        cl.sync();
+    }
+};
+
 // ---------------------------------------------------------------- formats
 // load(): the block's registers; value(): exact integer sums (iv) and the f32 block value.
 
 template <int QCH>
-__device__ __forceinline__ void load_chunks(const KArgs &a, size_t row, int b, uint4 (&q)[QCH]) {
-    const uint8_t *rp = a.qs + row * a.qs_row;
+__device__ __forceinline__ void load_chunks(const KArgs &a, const Row &rp, int b, uint4 (&q)[QCH]) {
 #pragma unroll
-    for (int j = 0; j < QCH; j++) q[j] = ldg_stream(rp + qs_chunk_offset(a.nb, QCH, b, j));
+    for (int j = 0; j < QCH; j++) q[j] = ldg_stream(rp.q + qs_chunk_offset(a.nb, QCH, b, j));
 }
 
 template <int QCH>
-__device__ __forceinline__ void prefetch_chunks(const KArgs &a, size_t row, int b) {
-    const uint8_t *rp = a.qs + row * a.qs_row;
+__device__ __forceinline__ void prefetch_chunks(const KArgs &a, const Row &rp, int b) {
 #pragma unroll
-    for (int j = 0; j < QCH; j++) prefetch_l2(rp + qs_chunk_offset(a.nb, QCH, b, j));
+    for (int j = 0; j < QCH; j++) prefetch_l2(rp.q + qs_chunk_offset(a.nb, QCH, b, j));
 }
 
 // dot of the low (mask 0x0F) or in-place high (mask 0xF0, result x16) nibbles of 16 bytes
@@ -300,13 +495,13 @@ struct FQ4_0 {
         uint4 q[1];
         uint32_t d;
     };
-    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
-        prefetch_chunks<1>(a, row, b);
+    static __device__ __forceinline__ void prefetch(const KArgs &a, const Row &rp, int b) {
+        prefetch_chunks<1>(a, rp, b);
     }
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
+    static __device__ __forceinline__ Ld load(const KArgs &a, const Row &rp, int b) {
         Ld l;
-        load_chunks<1>(a, row, b, l.q);
-        l.d = ldg_u16(a.d + row * a.nb + b);
+        load_chunks<1>(a, rp, b, l.q);
+        l.d = ldg_u16(rp.d + b);
         return l;
     }
     static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
@@ -331,13 +526,13 @@ struct FQ8_0 {
         uint4 q[2];
         uint32_t d;
     };
-    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
-        prefetch_chunks<2>(a, row, b);
+    static __device__ __forceinline__ void prefetch(const KArgs &a, const Row &rp, int b) {
+        prefetch_chunks<2>(a, rp, b);
     }
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
+    static __device__ __forceinline__ Ld load(const KArgs &a, const Row &rp, int b) {
         Ld l;
-        load_chunks<2>(a, row, b, l.q);
-        l.d = ldg_u16(a.d + row * a.nb + b);
+        load_chunks<2>(a, rp, b, l.q);
+        l.d = ldg_u16(rp.d + b);
         return l;
     }
     static __device__ __forceinline__ int sum(const uint8_t *s, const Ld &l, int b) {
@@ -374,13 +569,13 @@ struct FQ4_K {
         uint4 q[8];
         uint4 s;
     };
-    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
-        prefetch_chunks<8>(a, row, b);
+    static __device__ __forceinline__ void prefetch(const KArgs &a, const Row &rp, int b) {
+        prefetch_chunks<8>(a, rp, b);
     }
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
+    static __device__ __forceinline__ Ld load(const KArgs &a, const Row &rp, int b) {
         Ld l;
-        load_chunks<8>(a, row, b, l.q);
-        l.s = __ldg(reinterpret_cast<const uint4 *>(a.sc + row * a.sc_row + 16 * (size_t)b));
+        load_chunks<8>(a, rp, b, l.q);
+        l.s = __ldg(reinterpret_cast<const uint4 *>(rp.s + 16 * (size_t)b));
         return l;
     }
     static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
@@ -430,14 +625,14 @@ struct FQ6_K {
         uint4 s;
         uint32_t d;
     };
-    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
-        prefetch_chunks<12>(a, row, b);
+    static __device__ __forceinline__ void prefetch(const KArgs &a, const Row &rp, int b) {
+        prefetch_chunks<12>(a, rp, b);
     }
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
+    static __device__ __forceinline__ Ld load(const KArgs &a, const Row &rp, int b) {
         Ld l;
-        load_chunks<12>(a, row, b, l.q);
-        l.s = __ldg(reinterpret_cast<const uint4 *>(a.sc + row * a.sc_row + 16 * (size_t)b));
-        l.d = ldg_u16(a.d + row * a.nb + b);
+        load_chunks<12>(a, rp, b, l.q);
+        l.s = __ldg(reinterpret_cast<const uint4 *>(rp.s + 16 * (size_t)b));
+        l.d = ldg_u16(rp.d + b);
         return l;
     }
     static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
@@ -498,13 +693,13 @@ struct FTQ2 {
         uint4 q[4];
         uint32_t d;
     };
-    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
-        prefetch_chunks<4>(a, row, b);
+    static __device__ __forceinline__ void prefetch(const KArgs &a, const Row &rp, int b) {
+        prefetch_chunks<4>(a, rp, b);
     }
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
+    static __device__ __forceinline__ Ld load(const KArgs &a, const Row &rp, int b) {
         Ld l;
-        load_chunks<4>(a, row, b, l.q);
-        l.d = ldg_u16(a.d + row * a.nb + b);
+        load_chunks<4>(a, rp, b, l.q);
+        l.d = ldg_u16(rp.d + b);
         return l;
     }
     static __device__ __forceinline__ int codes(const uint8_t *s, const Ld &l, int b) {
@@ -553,12 +748,12 @@ struct FI2S {
     struct Ld {
         uint4 q[2];
     };
-    static __device__ __forceinline__ void prefetch(const KArgs &a, size_t row, int b) {
-        prefetch_chunks<2>(a, row, b);
+    static __device__ __forceinline__ void prefetch(const KArgs &a, const Row &rp, int b) {
+        prefetch_chunks<2>(a, rp, b);
     }
-    static __device__ __forceinline__ Ld load(const KArgs &a, size_t row, int b) {
+    static __device__ __forceinline__ Ld load(const KArgs &a, const Row &rp, int b) {
         Ld l;
-        load_chunks<2>(a, row, b, l.q);
+        load_chunks<2>(a, rp, b, l.q);
         return l;
     }
     static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
@@ -586,7 +781,39 @@ struct FI2S {
 
 constexpr int MAX_WARPS = 8;
 
-template <class F, bool DIAG>
+// M_SINGLE: one matrix, row sums to out. M_DIAG: one matrix, per-block integer sums and values
+// to the diagnostic arrays. M_MULTI: several matrices over one activation (virtual rows).
+enum { M_SINGLE = 0, M_DIAG = 1, M_MULTI = 2 };
+
+// Row pointers of virtual row r and its output slot (token 0).
+template <int MODE>
+__device__ __forceinline__ Row row_of(const KArgs &a, size_t r, float *&outp) {
+    const uint8_t *qs = a.mat[0].qs, *sc = a.mat[0].sc;
+    const uint16_t *d = a.mat[0].d;
+    float *o = a.mat[0].out;
+    size_t vbeg = a.mat[0].vbeg, row0 = a.mat[0].row0;
+    if (MODE == M_MULTI) {
+        // matrices are ordered by vbeg: the last one starting at or before r owns it
+#pragma unroll
+        for (int i = 1; i < GEMV_MAX_MATS; i++) {
+            if (i < a.nmat && r >= a.mat[i].vbeg) {
+                qs = a.mat[i].qs;
+                sc = a.mat[i].sc;
+                d = a.mat[i].d;
+                o = a.mat[i].out;
+                vbeg = a.mat[i].vbeg;
+                row0 = a.mat[i].row0;
+            }
+        }
+    }
+    const size_t lr = r - vbeg + row0;
+    outp = o + (r - vbeg);
+    return Row{qs + lr * a.qs_row, sc + lr * a.sc_row, d + lr * (size_t)a.nb};
+}
+
+// F: weight format. S: activation stager (F::Act, or a stager that quantizes f32 input into
+// the same shared-memory layout).
+template <class F, class S, int MODE>
 __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int tok = blockIdx.y;
@@ -596,16 +823,28 @@ __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
     const int li = lane & (lpr - 1), rsub = lane >> a.lpr_shift;
     const size_t wid = (size_t)blockIdx.x * warps + (threadIdx.x >> 5);
     const size_t nwarps = (size_t)gridDim.x * warps;
-    float *out = a.out + (size_t)tok * a.out_ld;
+    const size_t tok_off = (size_t)tok * a.out_ld;
     const size_t stride = nwarps * rpw;
     size_t r0 = a.row_begin + wid * rpw;  // warp-uniform position (r0, b0)
     int b0 = 0;
     float acc = 0.0f;
+    // Grouped launches keep the current row's pointers in registers (the owning matrix is
+    // looked up once per row); single-matrix launches form them from the parameters at each
+    // load, which keeps the register count of the long-running kernels down.
+    float *outp = nullptr;
+    Row rpm{};
+    if (MODE == M_MULTI) rpm = row_of<MODE>(a, r0 + rsub, outp);
+    auto row_ptrs = [&]() -> Row {
+        if (MODE == M_MULTI) return rpm;
+        const size_t r = r0 + rsub;
+        return Row{a.mat[0].qs + r * a.qs_row, a.mat[0].sc + r * a.sc_row,
+                   a.mat[0].d + r * (size_t)a.nb};
+    };
     // one block of row r0 + rsub: the exact integer sums and the f32 block value
     auto consume = [&](const typename F::Ld &l, int b) {
         int2 iv;
         const float v = F::value(args, smem, l, b, iv);
-        if (DIAG) {
+        if (MODE == M_DIAG) {
             const size_t o = (r0 + rsub - a.row_begin) * (size_t)a.nb + b;
             a.dbg_sumi[o] = iv.x;
             if (a.dbg_mins) a.dbg_mins[o] = iv.y;
@@ -618,28 +857,32 @@ __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
     auto advance = [&]() {
         b0 += lpr;
         if (b0 >= a.nb) {
-            if (!DIAG) {
+            if (MODE != M_DIAG) {
                 for (int m = lpr >> 1; m > 0; m >>= 1)
                     acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
-                if (li == 0 && r0 + rsub < a.row_end) out[r0 + rsub - a.row_begin] = acc;
+                if (li == 0 && r0 + rsub < a.row_end) {
+                    float *o = MODE == M_MULTI ? outp : a.mat[0].out + (r0 + rsub - a.row_begin);
+                    o[tok_off] = acc;
+                }
             }
             acc = 0.0f;
             b0 = 0;
             r0 += stride;
+            if (MODE == M_MULTI) rpm = row_of<MODE>(a, r0 + rsub, outp);
         }
     };
     // Weights never depend on the previous kernel in the stream; the activation may. Start
     // pulling this warp's first blocks into L2, then wait for the previous grid (programmatic
     // dependent launch) before staging the activation.
-    if (r0 + rsub < a.row_end && li < a.nb) F::prefetch(args, r0 + rsub, li);
+    if (r0 + rsub < a.row_end && li < a.nb) F::prefetch(args, row_ptrs(), li);
     pdl_wait();
     pdl_launch_dependents();
     if (a.act_scales) args.act_scale = a.act_scales[tok];
-    F::Act::stage(args, a.x + (size_t)tok * a.x_row_stride, smem);
+    S::stage(args, a.x + (size_t)tok * a.x_row_stride, smem);
     while (r0 < a.row_end) {
         const int b = b0 + li;
         if (r0 + rsub < a.row_end && b < a.nb) {
-            const typename F::Ld l = F::load(args, r0 + rsub, b);
+            const typename F::Ld l = F::load(args, row_ptrs(), b);
             consume(l, b);
         }
         advance();
@@ -648,12 +891,20 @@ __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
 
 // ---------------------------------------------------------------- launch
 
-template <class F, bool DIAG>
+// Largest cluster for stagers that quantize f32 input once per cluster. A launch uses the
+// smallest power of two (at most this) that leaves each warp of the cluster at most two
+// quantization units: larger clusters cut the repeated quantization of wide inputs and of
+// small CTAs, smaller ones pack the device better.
+constexpr unsigned GEMV_MAX_CLUSTER = 8;
+
+template <class F, class S, int MODE>
 static int launch_t(const KArgs &a, size_t m, cudaStream_t st, const char *name) {
-    const size_t smem = F::Act::bytes(a.K);
-    auto kern = gemv_kernel<F, DIAG>;
-    // occupancy per CTA size (8, 4 or 2 warps), cached per template instance (B200 only)
-    static int per_sm_cached[4] = {-1, -1, -1, -1};
+    const size_t smem = S::bytes(a.K);
+    auto kern = gemv_kernel<F, S, MODE>;
+    // resident CTAs on the device per CTA size (8, 4 or 2 warps) and cluster size (1, 2, 4,
+    // 8; for cluster launches the resident clusters times the cluster size), cached per
+    // template instance (B200 only)
+    static int resident_cached[3][4] = {{-1, -1, -1, -1}, {-1, -1, -1, -1}, {-1, -1, -1, -1}};
     static size_t smem_cached = 0;
     static bool attr_set = false;
     if (!attr_set) {
@@ -661,7 +912,8 @@ static int launch_t(const KArgs &a, size_t m, cudaStream_t st, const char *name)
         attr_set = true;
     }
     if (smem_cached != smem) {
-        for (int i = 0; i < 4; i++) per_sm_cached[i] = -1;
+        for (int i = 0; i < 3; i++)
+            for (int j = 0; j < 4; j++) resident_cached[i][j] = -1;
         smem_cached = smem;
     }
     const int rpw = 32 >> a.lpr_shift;
@@ -672,17 +924,44 @@ static int launch_t(const KArgs &a, size_t m, cudaStream_t st, const char *name)
     while (warps > 2 && m * ((rows + (size_t)warps * rpw - 1) / ((size_t)warps * rpw)) < sms)
         warps >>= 1;
     const int slot = warps == 8 ? 0 : warps == 4 ? 1 : 2;
-    if (per_sm_cached[slot] < 0) {
-        int per_sm = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, warps * 32, smem);
-        per_sm_cached[slot] = per_sm < 1 ? 1 : per_sm;
+    unsigned C = 1;
+    int cs = 0;
+    if (S::kCluster)
+        while (C < GEMV_MAX_CLUSTER && S::units(a.K) > 2 * warps * (int)C) {
+            C <<= 1;
+            cs++;
+        }
+    int &resident = resident_cached[slot][cs];
+    if (resident < 0) {
+        int n = 0;
+        if (C > 1) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(C);
+            cfg.blockDim = dim3(warps * 32);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = C;
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+            n *= (int)C;
+        } else {
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, warps * 32, smem);
+            n *= (int)sms;
+        }
+        resident = n < (int)C ? (int)C : n;
     }
     const size_t want = (rows + (size_t)warps * rpw - 1) / ((size_t)warps * rpw);
-    const size_t cap = sms * per_sm_cached[slot];
+    const size_t cap = (size_t)resident;
     size_t gx = want;
     if (m * gx > cap) gx = (cap + m - 1) / m;
+    gx = (gx + C - 1) / C * C;  // whole clusters
     if (gx < 1) gx = 1;
-    cudaError_t e = launch_pdl(kern, dim3((unsigned)gx, (unsigned)m), dim3(warps * 32), smem, st, a);
+    cudaError_t e = launch_pdl_cluster(kern, dim3((unsigned)gx, (unsigned)m), dim3(warps * 32),
+                                       smem, st, C, a);
     return e == cudaSuccess ? JKB_OK : fail_cuda(e, name);
 }
 
@@ -690,21 +969,41 @@ static const size_t MAX_K = 120 * 1024;
 
 int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
     const jkb_weight *w = L.w;
-    KArgs a;
-    a.qs = w->p.qs;
+    const bool multi = L.nmat > 1;
+    KArgs a = {};
+    if (multi) {
+        if (L.nmat > GEMV_MAX_MATS)
+            return fail(JKB_E_BOUNDS, "gemv", 0, (size_t)L.nmat, GEMV_MAX_MATS,
+                        "%d matrices in one launch (limit %d)", L.nmat, GEMV_MAX_MATS);
+        size_t v = 0;
+        for (int i = 0; i < L.nmat; i++) {
+            const jkb_weight *wi = L.ws[i];
+            if (wi->gpu_format != w->gpu_format || wi->cols != w->cols ||
+                wi->p.qs_row != w->p.qs_row || wi->p.sc_row != w->p.sc_row)
+                return fail(JKB_E_INVALID, wi->name, wi->offset, wi->byte_len, wi->gguf_bytes,
+                            "grouped GEMV: %s [%zu, %zu] does not share the format and width "
+                            "of %s [%zu, %zu]",
+                            wi->name, wi->rows, wi->cols, w->name, w->rows, w->cols);
+            a.mat[i] = MatArgs{wi->p.qs, wi->p.sc, wi->p.d, L.outs[i], v, 0};
+            v += wi->rows;
+        }
+        a.nmat = L.nmat;
+        a.row_begin = 0;
+        a.row_end = v;
+    } else {
+        a.mat[0] = MatArgs{w->p.qs, w->p.sc, w->p.d, L.out, L.row_begin, L.row_begin};
+        a.nmat = 1;
+        a.row_begin = L.row_begin;
+        a.row_end = L.row_end;
+    }
     a.qs_row = w->p.qs_row;
-    a.sc = w->p.sc;
     a.sc_row = w->p.sc_row;
-    a.d = w->p.d;
     a.x = (const uint8_t *)L.x;
     a.x_row_stride = L.x_row_stride;
     a.act_scales = L.act_scales;
     a.act_scale = L.act_scale;
     a.i2s_scale = w->p.i2s_scale;
-    a.out = L.out;
     a.out_ld = L.out_ld;
-    a.row_begin = L.row_begin;
-    a.row_end = L.row_end;
     a.nb = (int)w->nb;
     a.K = (int)w->cols;
     int sh = 0;
@@ -718,25 +1017,40 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
                     "input length %zu exceeds the %zu-element activation limit of the GEMV "
                     "kernels",
                     w->cols, MAX_K);
-    if (L.row_end <= L.row_begin) return JKB_OK;
+    if (a.row_end <= a.row_begin) return JKB_OK;
     const bool diag = L.dbg_sumi != nullptr;
-    const size_t m = L.m ? L.m : 1;
-#define JKB_LAUNCH(F)                                                    \
-    return diag ? launch_t<F, true>(a, m, st, "gemv_kernel<diag>")       \
-                : launch_t<F, false>(a, m, st, "gemv_kernel")
+    const size_t m = multi ? 1 : (L.m ? L.m : 1);
+    const bool f32_in = L.act_kind == ACT_F32_Q8_0 || L.act_kind == ACT_F32_Q8_K;
+    if ((multi && (!f32_in || diag)) || (diag && f32_in))
+        return fail(JKB_E_CAPABILITY, w->name, w->offset, w->byte_len, w->gguf_bytes,
+                    "no GEMV kernel for this combination of grouped/diagnostic launch and "
+                    "activation kind %d",
+                    L.act_kind);
+    // pre-quantized or i8 activations: single or diagnostic launches
+#define JKB_LAUNCH(F)                                                                   \
+    return diag ? launch_t<F, F::Act, M_DIAG>(a, m, st, "gemv_kernel<diag>")            \
+                : launch_t<F, F::Act, M_SINGLE>(a, m, st, "gemv_kernel")
+    // f32 activations quantized by the stager S: single or grouped launches
+#define JKB_LAUNCH_F32(F, S)                                                            \
+    return multi ? launch_t<F, S, M_MULTI>(a, m, st, "gemv_kernel<grouped>")            \
+                 : launch_t<F, S, M_SINGLE>(a, m, st, "gemv_kernel<f32>")
     switch (w->gpu_format) {
     case GF_Q4_0:
         if (L.act_kind == ACT_Q8_0) JKB_LAUNCH(FQ4_0);
+        if (L.act_kind == ACT_F32_Q8_0) JKB_LAUNCH_F32(FQ4_0, ActQ80F32);
         break;
     case GF_Q8_0:
         if (L.act_kind == ACT_Q8_0) JKB_LAUNCH(FQ8_0<ActQ80>);
         if (L.act_kind == ACT_I8) JKB_LAUNCH(FQ8_0<ActI8<32>>);
+        if (L.act_kind == ACT_F32_Q8_0) JKB_LAUNCH_F32(FQ8_0<ActQ80>, ActQ80F32);
         break;
     case GF_Q4_K:
         if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FQ4_K);
+        if (L.act_kind == ACT_F32_Q8_K) JKB_LAUNCH_F32(FQ4_K, ActQ8KF32);
         break;
     case GF_Q6_K:
         if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FQ6_K);
+        if (L.act_kind == ACT_F32_Q8_K) JKB_LAUNCH_F32(FQ6_K, ActQ8KF32);
         break;
     case GF_TQ2_0:
         if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FTQ2<ActQ8K>);
@@ -747,6 +1061,7 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
         break;
     }
 #undef JKB_LAUNCH
+#undef JKB_LAUNCH_F32
     return fail(JKB_E_CAPABILITY, w->name, w->offset, w->byte_len, w->gguf_bytes,
                 "no GEMV kernel for %s weights with activation kind %d", quant_name(w->quant),
                 L.act_kind);
@@ -778,6 +1093,34 @@ static int gemv_call(const char *fn, int quant, float *out, size_t out_len, cons
     L.w = w;
     L.x = x;
     L.act_kind = act_kind_for(quant);
+    L.out = out;
+    L.row_begin = 0;
+    L.row_end = w->rows;
+    L.m = 1;
+    return launch_gemv(L, as_stream(stream));
+}
+
+// vec_dot_*_rvv (lib.rs:1312-1319, quant.rs:999-1005, :1056-1062, :1445-1451): the scalar
+// vec_dot_* validation (validate_*_dimensions), then the input quantized to BlockQ8_0 / BlockQ8K
+// and the integer Q8 GEMV (vec_dot_q8_0_chunked_rvv / vec_dot_q8_k_chunked_rvv,
+// quant_q8.rs:1712-1750, :3280-3317). The reference quantizes into a stack chunk per 32 / 128
+// blocks; here every CTA quantizes the whole input into shared memory.
+static int rvv_act_kind(int quant) {
+    return (quant == JKB_Q4_0 || quant == JKB_Q8_0) ? ACT_F32_Q8_0 : ACT_F32_Q8_K;
+}
+
+static int vec_dot_rvv_call(const char *fn, int quant, float *out, size_t out_len,
+                            const jkb_weight *w, const float *input, size_t in_len,
+                            void *stream) {
+    int rc = validate_weight_call(fn, w, quant, out_len, in_len);
+    if (rc) return rc;
+    if (!out || !input) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
+    if ((rc = check_align(out, 4, fn, "output")) || (rc = check_align(input, 4, fn, "input")))
+        return rc;
+    GemvLaunch L{};
+    L.w = w;
+    L.x = input;
+    L.act_kind = rvv_act_kind(quant);
     L.out = out;
     L.row_begin = 0;
     L.row_end = w->rows;
@@ -822,6 +1165,62 @@ int jkb_gemv_tq1_0_q8_k(float *out, size_t out_len, const jkb_weight *w,
 int jkb_gemv_tq2_0_q8_k(float *out, size_t out_len, const jkb_weight *w,
                         const jkb_block_q8_k *x, size_t x_len, void *stream) {
     return gemv_call("gemv_tq2_0_q8_k", JKB_TQ2_0, out, out_len, w, x, x_len, stream);
+}
+
+int jkb_vec_dot_q4_k_m_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                           size_t in_len, void *stream) {
+    return vec_dot_rvv_call("vec_dot_q4_k_m", JKB_Q4_K_M, out, out_len, w, input, in_len, stream);
+}
+int jkb_vec_dot_q6_k_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                         size_t in_len, void *stream) {
+    return vec_dot_rvv_call("vec_dot_q6_k", JKB_Q6_K, out, out_len, w, input, in_len, stream);
+}
+int jkb_vec_dot_q8_0_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                         size_t in_len, void *stream) {
+    return vec_dot_rvv_call("vec_dot_q8_0", JKB_Q8_0, out, out_len, w, input, in_len, stream);
+}
+int jkb_vec_dot_q4_0_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                         size_t in_len, void *stream) {
+    return vec_dot_rvv_call("vec_dot_q4_0", JKB_Q4_0, out, out_len, w, input, in_len, stream);
+}
+
+int jkb_vec_dot_grouped_rvv(const jkb_vec_dot_item *items, size_t n_items, const float *input,
+                            size_t in_len, void *stream) {
+    static const char *fn = "vec_dot_grouped_rvv";
+    if (!items || !input) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
+    if (n_items == 0 || n_items > (size_t)GEMV_MAX_MATS)
+        return fail(JKB_E_BOUNDS, fn, 0, n_items, GEMV_MAX_MATS,
+                    "%zu items (expected 1..%d)", n_items, GEMV_MAX_MATS);
+    int rc = check_weight(items[0].w);
+    if (rc) return rc;
+    const int quant = items[0].w->quant;
+    if (quant != JKB_Q4_0 && quant != JKB_Q8_0 && quant != JKB_Q4_K_M && quant != JKB_Q6_K)
+        return fail(JKB_E_CAPABILITY, items[0].w->name, items[0].w->offset, items[0].w->byte_len,
+                    items[0].w->gguf_bytes,
+                    "%s: no vec_dot_*_rvv path for %s weights (Q4_0, Q8_0, Q4_K_M, Q6_K)", fn,
+                    quant_name(quant));
+    if ((rc = check_align(input, 4, fn, "input"))) return rc;
+    GemvLaunch L{};
+    for (size_t i = 0; i < n_items; i++) {
+        const jkb_vec_dot_item &it = items[i];
+        if ((rc = validate_weight_call(fn, it.w, quant, it.out_len, in_len))) return rc;
+        if (!it.out) return fail(JKB_E_INVALID, fn, i, 0, 0, "null output of item %zu", i);
+        if ((rc = check_align(it.out, 4, fn, "output"))) return rc;
+        L.ws[i] = it.w;
+        L.outs[i] = it.out;
+    }
+    L.w = items[0].w;
+    L.nmat = (int)n_items;
+    L.x = input;
+    L.act_kind = rvv_act_kind(quant);
+    L.m = 1;
+    if (n_items == 1) {  // one matrix: the single-matrix kernel
+        L.nmat = 0;
+        L.out = items[0].out;
+        L.row_begin = 0;
+        L.row_end = items[0].w->rows;
+    }
+    return launch_gemv(L, as_stream(stream));
 }
 
 int jkb_gemv_rows(float *out, size_t out_len, const jkb_weight *w, const void *x, size_t x_len,

@@ -112,21 +112,31 @@ inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s
 
 // Launches with programmatic stream serialization: the kernel may start while the previous
 // kernel in the stream finishes; it must execute griddepcontrol.wait before touching memory
-// the previous kernel writes or reads.
+// the previous kernel writes or reads. cluster_x > 1 launches thread-block clusters of
+// cluster_x CTAs along x (grid.x must be a multiple of it).
 template <class... KArgsT, class... ArgsT>
-cudaError_t launch_pdl(void (*kern)(KArgsT...), dim3 grid, dim3 block, size_t smem,
-                       cudaStream_t st, ArgsT... args) {
+cudaError_t launch_pdl_cluster(void (*kern)(KArgsT...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t st, unsigned cluster_x, ArgsT... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = cluster_x > 1 ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+template <class... KArgsT, class... ArgsT>
+cudaError_t launch_pdl(void (*kern)(KArgsT...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, ArgsT... args) {
+    return launch_pdl_cluster(kern, grid, block, smem, st, 1u, args...);
 }
 
 // Reference validators over a stored 2-D/1-D shape (quant.rs:1810-1894 and its per-format
@@ -143,10 +153,18 @@ int check_weight(const jkb_weight *w);
 
 // gemv.cu entry used by bitlinear.cu and the sharded paths.
 enum GpuFormat { GF_Q4_0, GF_Q8_0, GF_Q4_K, GF_Q6_K, GF_TQ2_0, GF_I2_S };
-enum ActKind { ACT_Q8_0 = 0, ACT_Q8_K = 1, ACT_I8 = 2 };
+// ACT_F32_*: f32 input rows that every CTA quantizes into its shared-memory staging buffer with
+// the bit-exact BlockQ8_0 / BlockQ8K quantizer (the reference's vec_dot_*_rvv paths).
+enum ActKind { ACT_Q8_0 = 0, ACT_Q8_K = 1, ACT_I8 = 2, ACT_F32_Q8_0 = 3, ACT_F32_Q8_K = 4 };
+constexpr int GEMV_MAX_MATS = 8;
 struct GemvLaunch {
-    const jkb_weight *w;
-    const void *x;           // activation rows (AoS blocks or i8)
+    const jkb_weight *w;     // the weight (the first one when nmat > 1)
+    // nmat > 1: one launch over weights ws[0..nmat) that share format, cols and activation;
+    // weight i writes outs[i][0..rows_i). row_begin/row_end/out/m are ignored (m = 1).
+    int nmat;
+    const jkb_weight *ws[GEMV_MAX_MATS];
+    float *outs[GEMV_MAX_MATS];
+    const void *x;           // activation rows (AoS blocks, i8 or f32)
     size_t x_row_stride;     // bytes between tokens (batch)
     int act_kind;
     const float *act_scales; // per-token scale (i8 activations, device) or nullptr

@@ -5,18 +5,9 @@
 #include <cstring>
 
 #include "jkb_internal.h"
+#include "quant_math.cuh"
 
 namespace jkb {
-
-__device__ __forceinline__ bool finite_f(float v) { return isfinite(v); }
-
-// round_scaled_to_i8 (quant_q8.rs:102-108)
-__device__ __forceinline__ int round_scaled(float v, float inv) {
-    if (!finite_f(v)) return 0;
-    float r = roundf(__fmul_rn(v, inv));
-    r = fminf(fmaxf(r, -127.0f), 127.0f);
-    return (int)r;
-}
 
 // quantize_block_q8_0_scalar (quant_q8.rs:203-219): 8 lanes per 32-element block, 4 values per
 // lane. absmax over finite values (a max is order independent), amax == 0 -> ZERO block.

@@ -26,6 +26,14 @@ class jkb_tensor_view(C.Structure):
     ]
 
 
+class jkb_vec_dot_item(C.Structure):
+    _fields_ = [
+        ("out", C.c_void_p),
+        ("out_len", C.c_size_t),
+        ("w", C.c_void_p),
+    ]
+
+
 class jkb_error_info(C.Structure):
     _fields_ = [
         ("status", C.c_int32),
@@ -84,6 +92,11 @@ SIGNATURES = {
     "jkb_vec_dot_q6_k": [P, S, P, P, S, P],
     "jkb_vec_dot_q4_0": [P, S, P, P, S, P],
     "jkb_vec_dot_i2_s": [P, S, P, P, S, P],
+    "jkb_vec_dot_q4_k_m_rvv": [P, S, P, P, S, P],
+    "jkb_vec_dot_q6_k_rvv": [P, S, P, P, S, P],
+    "jkb_vec_dot_q8_0_rvv": [P, S, P, P, S, P],
+    "jkb_vec_dot_q4_0_rvv": [P, S, P, P, S, P],
+    "jkb_vec_dot_grouped_rvv": [C.POINTER(jkb_vec_dot_item), S, P, S, P],
     "jkb_bitlinear_i8": [P, S, P, P, S, F, P],
     "jkb_bitlinear_i8_rvv": [P, S, P, P, S, F, P],
     "jkb_bitlinear_i8_ime": [P, S, P, P, S, F, P],

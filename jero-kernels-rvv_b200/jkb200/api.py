@@ -25,7 +25,8 @@ __all__ = [
     "gemv_q4_0_q8_0", "gemv_q4_0_q8_0_4x", "gemv_q8_0_q8_0", "gemv_q8_0_q8_0_4x",
     "gemv_q4_k_q8_k", "gemv_q6_k_q8_k", "gemv_tq1_0_q8_k", "gemv_tq2_0_q8_k", "gemv_rows",
     "gemv_block_dots", "vec_dot_q4_k_m", "vec_dot_q8_0", "vec_dot_q6_k", "vec_dot_q4_0",
-    "vec_dot_i2_s", "bitlinear_i8", "bitlinear_i8_rvv", "bitlinear_i8_ime",
+    "vec_dot_i2_s", "vec_dot_q4_k_m_rvv", "vec_dot_q6_k_rvv", "vec_dot_q8_0_rvv",
+    "vec_dot_q4_0_rvv", "vec_dot_grouped_rvv", "bitlinear_i8", "bitlinear_i8_rvv", "bitlinear_i8_ime",
     "bitlinear_i8_batch", "gemm_repacked", "gemm_repacked_rows", "gemv_repacked",
     "gemv_repacked_rows", "gemm_repacked_f32", "gemm_repacked_f32_noalloc",
     "empty_q8_0_blocks", "empty_q8_k_blocks",
@@ -526,6 +527,38 @@ def vec_dot_q4_0(out, weights, x, stream=None):
 def vec_dot_i2_s(out, weights, x, stream=None):
     """quant.rs:2199."""
     _vk("jkb_vec_dot_i2_s", out, weights, x, stream)
+
+
+def vec_dot_q4_k_m_rvv(out, weights, x, stream=None):
+    """lib.rs:1313: f32 input quantized to Q8_K, then the integer Q4_K_M x Q8_K GEMV."""
+    _vk("jkb_vec_dot_q4_k_m_rvv", out, weights, x, stream)
+
+
+def vec_dot_q6_k_rvv(out, weights, x, stream=None):
+    """quant.rs:1056: f32 input quantized to Q8_K, then the integer Q6_K x Q8_K GEMV."""
+    _vk("jkb_vec_dot_q6_k_rvv", out, weights, x, stream)
+
+
+def vec_dot_q8_0_rvv(out, weights, x, stream=None):
+    """quant.rs:999: f32 input quantized to Q8_0, then the integer Q8_0 x Q8_0 GEMV."""
+    _vk("jkb_vec_dot_q8_0_rvv", out, weights, x, stream)
+
+
+def vec_dot_q4_0_rvv(out, weights, x, stream=None):
+    """quant.rs:1445: f32 input quantized to Q8_0, then the integer Q4_0 x Q8_0 GEMV."""
+    _vk("jkb_vec_dot_q4_0_rvv", out, weights, x, stream)
+
+
+def vec_dot_grouped_rvv(items, x, stream=None):
+    """Several vec_dot_*_rvv products sharing the f32 input `x` in one launch (no reference
+    counterpart). `items` is a sequence of (out, weights) pairs; every weight has the quant
+    type of the first and x.numel() columns; each output equals its single call's."""
+    arr = (_lib.jkb_vec_dot_item * max(1, len(items)))()
+    for i, (out, w) in enumerate(items):
+        arr[i].out = _dptr(out)
+        arr[i].out_len = out.numel()
+        arr[i].w = w.handle
+    _check(_L().jkb_vec_dot_grouped_rvv(arr, len(items), _dptr(x), x.numel(), _stream(stream)))
 
 
 # ------------------------------------------------------------------------------- BitLinear
