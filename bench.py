@@ -567,6 +567,60 @@ def run_kernel_case(args):
                       "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1)}))
 
 
+def _graph_time(fn, launches, warm=3):
+    """us per call of fn() over a CUDA graph of `launches` back-to-back calls."""
+    import torch
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(launches):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+        torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / launches * 1e3
+
+
+def run_gemm_case(args):
+    """The repacked Q8_0 x Q8_0 GEMM (BASELINE configs[2] kind): M tokens x --rows x --cols,
+    activations quantized once (QuantizedActQ8), `--launches` GEMMs timed in a CUDA graph."""
+    import torch
+    import jkb200 as jkb
+
+    M, N, K = args.m, args.rows, args.cols
+    raw = synth_matrix(Q8_0, N, K, 4243)
+    rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", Q8_0, [N, K], raw), N, K)
+    x = torch.randn(M * K, generator=torch.Generator().manual_seed(2)).cuda()
+    act = jkb.QuantizedActQ8.quantize(x, M, K)
+    out = torch.empty(M * N, dtype=torch.float32, device="cuda")
+    us = _graph_time(lambda: rw.gemm(out, act), args.launches)
+    print(json.dumps({"kernel": "gemm_q8_0", "m": M, "rows": N, "cols": K,
+                      "us_per_launch": round(us, 2),
+                      "tops": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 2)}))
+
+
+def run_int8_peak(args):
+    """cuBLAS int8 GEMM throughput through torch._int_mm (the int8 roofline denominator)."""
+    import torch
+    res = {"kernel": "int8_peak"}
+    for name, (M, N, K) in (("8192^3", (8192, 8192, 8192)),
+                            ("gemm_shape", (args.m, args.rows, args.cols))):
+        a = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda")
+        b = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda").t()
+        us = _graph_time(lambda: torch._int_mm(a, b), args.launches)
+        res[name] = {"m": M, "n": N, "k": K, "us": round(us, 2),
+                     "tops": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 1)}
+    print(json.dumps(res))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -574,7 +628,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="jkb", choices=["jkb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0"],
+    ap.add_argument("--m", type=int, default=2048, help="tokens of --kernel gemm_q8_0 / int8_peak")
+    ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0", "gemm_q8_0", "int8_peak"],
                     help="run one GEMV shape (profiling case) instead of the benchmark")
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--cols", type=int, default=4096)
@@ -586,7 +641,11 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.kernel:
+    if args.kernel == "gemm_q8_0":
+        run_gemm_case(args)
+    elif args.kernel == "int8_peak":
+        run_int8_peak(args)
+    elif args.kernel:
         run_kernel_case(args)
     elif args.impl == "reference":
         run_reference(args)

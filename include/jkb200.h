@@ -107,6 +107,10 @@ int jkb_abi_version(void);
 const char *jkb_last_error(void);
 int jkb_last_error_info(jkb_error_info *out);
 void jkb_clear_error(void);
+/* No reference counterpart: the device error word of the tensor-core GEMM (bit 0: one of its
+ * bounded waits expired, so the call's output is not valid). Synchronizes `stream`, copies the
+ * word to *flags, clears it, and returns JKB_E_TIMEOUT when it was non-zero, JKB_OK otherwise. */
+int jkb_device_status(int32_t *flags, void *stream);
 
 /* ---- activation quantizers ---- */
 /* quant_q8.rs:395 quantize_row_q8_0 (alias of quantize_row_q8_0_f32, :370). */

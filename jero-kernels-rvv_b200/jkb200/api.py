@@ -29,7 +29,7 @@ __all__ = [
     "vec_dot_q4_0_rvv", "vec_dot_grouped_rvv", "bitlinear_i8", "bitlinear_i8_rvv", "bitlinear_i8_ime",
     "bitlinear_i8_batch", "gemm_repacked", "gemm_repacked_rows", "gemv_repacked",
     "gemv_repacked_rows", "gemm_repacked_f32", "gemm_repacked_f32_noalloc",
-    "empty_q8_0_blocks", "empty_q8_k_blocks",
+    "empty_q8_0_blocks", "empty_q8_k_blocks", "device_status",
     "device_view",
 ]
 
@@ -109,6 +109,14 @@ def _L():
 
 def abi_version() -> int:
     return int(_L().jkb_abi_version())
+
+
+def device_status(stream=None) -> int:
+    """Synchronizes the stream and returns (and clears) the device error word of the
+    tensor-core GEMM; raises K3Error (JKB_E_TIMEOUT) when a bounded wait in it expired."""
+    v = C.c_int32(0)
+    _check(_L().jkb_device_status(C.byref(v), _stream(stream)))
+    return int(v.value)
 
 
 def _dptr(t):
