@@ -476,6 +476,8 @@ def run_gpu(args):
         e2e_ms = float(t.item())
     e2e_val = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
 
+    prefill = None if args.no_gemm else run_prefill_gemm(world, rank)
+
     if rank == 0:
         peak, peak_kind = measured_peaks()
         lm_q, lm_rows, lm_cols = Q6_K, DECODE_8B[-1][2], DECODE_8B[-1][3]
@@ -506,6 +508,8 @@ def run_gpu(args):
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
         }
+        if prefill is not None:
+            res["prefill_gemm"] = prefill
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline_single()
         print(json.dumps(res), flush=True)
@@ -513,6 +517,82 @@ def run_gpu(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+PREFILL = [(512, 14336, 4096), (512, 4096, 14336), (2048, 14336, 4096), (2048, 4096, 14336)]
+
+
+def int8_peak_tops(launches=10):
+    """cuBLAS int8 GEMM throughput (torch._int_mm, 8192^3) on this GPU: the int8 tensor-core
+    roofline denominator (MEASURED_PEAKS.json has none)."""
+    import torch
+    a = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (8192, 8192), dtype=torch.int8, device="cuda").t()
+    us = _graph_time(lambda: torch._int_mm(a, b), launches)
+    del a, b
+    return 2.0 * 8192 ** 3 / (us * 1e-6) / 1e12
+
+
+def run_prefill_gemm(world, rank, launches=10):
+    """the repacked Q8_0 x Q8_0 prefill GEMM at M in {512, 2048} tokens for
+    4096 -> 14336 and 14336 -> 4096, output rows sharded over the ranks. Per shape, `launches`
+    back-to-back GEMMs (weight copies rotating so every launch reads more than the L2 holds) in
+    a CUDA graph, timed with CUDA events, max over ranks; reported for the default (fused
+    multiply-add) and the bit-exact epilogue. Activations are quantized once per shape
+    (QuantizedActQ8), outside the timed region."""
+    import torch
+    import torch.distributed as dist
+    import jkb200 as jkb
+
+    res = {"shapes": [], "note": "tcgen05 int8 MMA + per-32-group f32 scale epilogue"}
+    tot_ops = {False: 0.0, True: 0.0}
+    tot_us = {False: 0.0, True: 0.0}
+    for m, n, k in PREFILL:
+        per = n // world
+        raw = synth_matrix(Q8_0, n, k, 4243 + n, rank * per, (rank + 1) * per)
+        nbytes = per * (k // 32) * 34
+        copies = max(2, -(-300_000_000 // nbytes))
+        ws = [jkb.RepackedWeight.from_tensor(jkb.TensorView("w", Q8_0, [per, k], raw), per, k)
+              for _ in range(copies)]
+        x = torch.randn(m * k, generator=torch.Generator().manual_seed(2)).cuda()
+        act = jkb.QuantizedActQ8.quantize(x, m, k)
+        out = torch.empty(m * per, dtype=torch.float32, device="cuda")
+        row = {"m": m, "n": n, "k": k}
+        for exact in (False, True):
+            it = [0]
+
+            def one():
+                ws[it[0] % copies].gemm(out, act)
+                it[0] += 1
+
+            with jkb.gemm_exact(exact):
+                us = _graph_time(one, launches)
+            if world > 1:
+                t = torch.tensor([us], device="cuda")
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                us = float(t.item())
+            ops = 2.0 * m * n * k
+            row["exact_tops" if exact else "tops"] = round(ops / (us * 1e-6) / 1e12, 1)
+            row["exact_us" if exact else "us"] = round(us, 2)
+            tot_ops[exact] += ops
+            tot_us[exact] += us
+        res["shapes"].append(row)
+        for w in ws:
+            w.destroy()
+        del act, out, x
+        torch.cuda.empty_cache()
+    res["tops"] = round(tot_ops[False] / (tot_us[False] * 1e-6) / 1e12, 1)
+    res["exact_tops"] = round(tot_ops[True] / (tot_us[True] * 1e-6) / 1e12, 1)
+    peak = int8_peak_tops()
+    if world > 1:
+        t = torch.tensor([peak], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        peak = float(t.item()) * world
+    res["roofline"] = {"bound": "tensor", "achieved": res["tops"], "peak": round(peak, 1),
+                       "unit": "TOPS", "frac": round(res["tops"] / peak, 4),
+                       "peak_source": "measured in this run: cuBLAS int8 (torch._int_mm 8192^3)"
+                                      + (f" x {world} GPUs" if world > 1 else "")}
+    return res
 
 
 def run_kernel_case(args):
@@ -628,6 +708,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="jkb", choices=["jkb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true",
+                    help="leave out the prefill GEMM section (BASELINE configs[2])")
     ap.add_argument("--m", type=int, default=2048, help="tokens of --kernel gemm_q8_0 / int8_peak")
     ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0", "gemm_q8_0", "int8_peak"],
                     help="run one GEMV shape (profiling case) instead of the benchmark")

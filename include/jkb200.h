@@ -111,6 +111,14 @@ void jkb_clear_error(void);
  * bounded waits expired, so the call's output is not valid). Synchronizes `stream`, copies the
  * word to *flags, clears it, and returns JKB_E_TIMEOUT when it was non-zero, JKB_OK otherwise. */
 int jkb_device_status(int32_t *flags, void *stream);
+/* No reference counterpart: the f32 epilogue of the tensor-core repacked GEMM (32-element
+ * scale groups, batches of at least 32 tokens). 0 (the default): acc = fma((f32)c, xs * ws, acc)
+ * per group, within one rounding per group of the reference and far inside its 1e-5 relative
+ * tolerance; the integer group sums c are exact either way. 1: the reference's separately
+ * rounded product and sum (accumulate_scaled_tile_scalar, repack.rs:3045-3093), bit-identical
+ * outputs at about two thirds of the speed. Process-wide; takes effect at the next launch. */
+int jkb_gemm_set_exact(int exact);
+int jkb_gemm_get_exact(void);
 
 /* ---- activation quantizers ---- */
 /* quant_q8.rs:395 quantize_row_q8_0 (alias of quantize_row_q8_0_f32, :370). */
@@ -316,7 +324,7 @@ int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight 
  * that cannot allocate device memory, and so cannot create the jkb_act_q8 scratch handle. Two
  * examples: an engine that reserved all remaining HBM for its KV cache at start-up, and a host
  * whose per-token loop forbids cudaMalloc because it may synchronize the device and stall the
- * pipeline. The quantized activations go to a scratch array built into the library (3.25 MiB
+ * pipeline. The quantized activations go to a scratch array built into the library (3.75 MiB
  * of device memory on every GPU that loads it, held until exit). The batch must satisfy
  * m * round_up(cols, 32) <= 2097152 elements (e.g. 512 tokens x 4096); larger batches fail
  * with JKB_E_BOUNDS. The call allocates nothing. The first call on each device looks up the

@@ -1,28 +1,48 @@
 // tcgen05 tensor-core path of the repacked block-scaled GEMM for 32-element scale groups without
-// mins (Q8_0 / Q4_0 / TQ2_0 weights), bit-exact with accumulate_scaled_tile_scalar
-// (repack.rs:3045-3093):
+// mins (Q8_0 / Q4_0 / TQ2_0 / I2_S weights). Per output (m, n), as in
+// accumulate_scaled_tile_scalar (repack.rs:3045-3093):
 //     acc = 0; for g in K order: acc += (f32)c_g * (xs[m][g] * ws[n][g]),  c_g = sum_{k in g} xq*wq
+// The integer group sums c_g are exact (int8 MMA into int32). Two epilogues:
+//   EXACT = true   the reference's roundings: p = (f32)c * (xs*ws) rounded, then acc + p rounded,
+//                  so every output is bit-identical to the scalar reference;
+//   EXACT = false  acc = fma((f32)c, xs*ws, acc): one rounding fewer per group, each output within
+//                  one rounding of |c*xs*ws| per group of the reference (far inside 1e-5 relative).
 //
-// One persistent CTA per SM walks 128 x 128 output tiles (m fastest, so the CTAs working at the
-// same time share weight tiles in L2). Warp roles:
-//   warp 0      TMA producer: 128-byte K slices (4 groups) of the activation tile (128 rows) and
-//               the weight tile (128 rows) into a 4-stage shared-memory ring, 128-byte swizzle.
-//   warp 1      TMEM owner and MMA issuer: per 32-element group one tcgen05.mma.kind::i8
-//               (M=128, N=128, K=32) into one of four int32 TMEM accumulators (4 x 128 columns);
-//               tcgen05.commit signals the epilogue per group and frees the smem stage after its
-//               four groups.
-//   warps 2-9   epilogue: warp w reads TMEM lanes 32*(w%4).. (its 32 output rows), warps 2-5
-//               columns 0-63 and warps 6-9 columns 64-127. Each thread converts its 64 int32 sums
-//               to f32 exactly, forms xs*ws, the product and the running f32 sum in the
-//               reference's order and rounding, group after group.
-// The per-group scale epilogue is CUDA-core work (5 instructions per output per group) and
-// bounds the kernel: the 32 int8 MACs of tensor work per output per group cost far less.
+// The per-group f32 epilogue, not the tensor core, bounds this GEMM: per output and group the
+// MMA does 32 int8 MACs (about 1/256 of an SM-clock at the int8 rate), while the epilogue needs
+// an int32 -> f32 conversion, the scale product and the accumulation on CUDA cores. Per SM and
+// clock a B200 issues 4 warp instructions and has 128 FMA-pipe lanes (a packed f32x2 operation
+// takes two) and 64 ALU lanes. The epilogue is shaped for that budget:
+//   * the conversion is cvt.rn.f32.s32, which runs on the ALU pipe (exact: |c| < 2^24);
+//   * the scale product and the accumulation are packed f32x2 operations (one issue slot per
+//     two outputs) on the FMA pipe;
+//   * TMEM is read with the 16x256b shape, which gives each thread 4 weight rows and, per
+//     8-column repeat, one adjacent token pair: a thread needs 4 weight-row scales and COLS/4
+//     token scales per group, the latter as f32x2 pairs, two pairs per 16-byte shared load
+//     (the quantizer stores the transposed token scales permuted within 32-token blocks).
+//
+// Layout. The MMA's M side is 128 weight rows (TMEM lane = weight row), its N side BN tokens
+// (TMEM column = token); one persistent CTA per SM walks (weight tile, token tile) pairs, token
+// tiles fastest. Warp roles:
+//   warp 0     TMA producer: per stage 128 bytes of K (4 groups) of the weight tile and of the
+//              token tile (128-byte swizzle), the weight scales [128 rows][4 groups] and the
+//              token scales [4 groups][BN tokens] (from the transposed activation-scale plane).
+//   warp 1     TMEM owner and MMA issuer: one tcgen05.mma.kind::i8 (M=128, N=BN, K=32) per group
+//              into its own TMEM accumulator. Groups go in rounds of GPR (two round buffers of
+//              GPR accumulators alternate); one tcgen05.commit per round signals the epilogue,
+//              one per stage releases the stage's operands.
+//   warps 2..  epilogue, WPQ warps per TMEM lane quarter: warp w reads lanes 32*(w%4).. (its 32
+//              weight rows) and COLS = BN / WPQ token columns, per round one barrier wait and,
+//              per 16-lane x 32-column chunk, the GPR groups' loads in flight together before
+//              one wait; it converts, scales and accumulates in registers, releases the round
+//              buffer, and at the end of a tile stores out[m][n].
 //
 // Every mbarrier wait is bounded (about 2 s of globaltimer). On expiry the thread raises the
 // device error word and the abort flag; the roles leave their loops, the producer waits (bounded)
 // for its copies in flight, the MMA thread for its MMAs, and the CTA frees its TMEM and returns.
 #include <cuda.h>
 
+#include <atomic>
 #include <cstdio>
 
 #include "jkb_internal.h"
@@ -31,22 +51,35 @@ namespace jkb {
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 128;  // tile rows (tokens), tile columns, K bytes/stage
-constexpr int STAGES = 4;
-constexpr int NBUF = 4;                       // TMEM group accumulators
-constexpr int TMEM_COLS = NBUF * BN;          // 512
-constexpr int EPI_WARPS = 8;
-constexpr int THREADS = (2 + EPI_WARPS) * 32;
-constexpr int STAGE_A = BM * BK, STAGE_B = BN * BK;  // bytes
-constexpr uint32_t STAGE_TX = STAGE_A + STAGE_B;
+constexpr int BMW = 128;  // weight rows per tile (MMA M, TMEM lanes)
+constexpr int BK = 128;   // K bytes per stage
+constexpr int GPS = 4;    // scale groups per stage
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
-struct Smem {
-    uint8_t a[STAGES][STAGE_A];  // 1024-byte aligned (swizzle atoms)
-    uint8_t b[STAGES][STAGE_B];
-    float ws[EPI_WARPS][2][4][64];  // per epilogue warp: its 64 columns' scales of 4 groups,
-                                    // transposed, double-buffered
-    uint64_t full[STAGES], empty[STAGES], tfull[NBUF], tempty[NBUF], done;
+template <int BN_, int WPQ_, int GPR_, bool EXACT_>
+struct TcCfg {
+    static constexpr int BN = BN_, WPQ = WPQ_, GPR = GPR_;
+    static constexpr bool EXACT = EXACT_;
+    static constexpr int COLS = BN / WPQ;  // token columns per epilogue thread
+    static constexpr int EPI = 4 * WPQ;    // epilogue warps
+    static constexpr int THREADS = (2 + EPI) * 32;
+    // TMEM: two round buffers of GPR group accumulators (BN int32 columns each)
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int SA = BMW * BK, SB = BN * BK;  // operand bytes per stage
+    static constexpr int STAGE_TX = SA + SB + BMW * GPS * 4 + GPS * BN * 4;
+    static constexpr int STAGES_FIT = (200 * 1024) / STAGE_TX;
+    static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+    static_assert((COLS == 32 || COLS == 64) && BN % 32 == 0 && BN <= 256, "tile shape");
+    static_assert(GPS % GPR == 0 && 2 * GPR * BN <= TMEM_COLS, "two rounds of GPR buffers");
+};
+
+template <class C>
+struct TcSmem {
+    uint8_t a[C::STAGES][C::SA];  // weight tiles; 1024-byte aligned (swizzle atoms)
+    uint8_t b[C::STAGES][C::SB];  // token tiles
+    float ws[C::STAGES][BMW][GPS];
+    float xs[C::STAGES][GPS][C::BN];
+    uint64_t full[C::STAGES], empty[C::STAGES], tfull[2], tempty[2], done;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -76,9 +109,9 @@ __device__ __forceinline__ bool mbar_try(uint64_t *b, uint32_t parity) {
     return ok != 0;
 }
 // Waits for the phase of parity `parity` to complete; false after WAIT_NS or when another role
-// has aborted. The first try is inline; the polling loop is a call.
-__device__ __forceinline__ bool mbar_wait_slow(uint64_t *b, uint32_t parity,
-                                            volatile int *abort_flag, int *err) {
+// has aborted.
+__device__ __forceinline__ bool mbar_wait_slow(uint64_t *b, uint32_t parity, volatile int *abort_flag,
+                                               int *err) {
     const unsigned long long t0 = globaltimer();
     for (uint32_t i = 1;; i++) {
         if (mbar_try(b, parity)) return true;
@@ -124,28 +157,26 @@ __device__ __forceinline__ void tc_commit(uint64_t *b) {
                      smem_u32(b))
                  : "memory");
 }
-// D[tmem] (=|+=) A[smem desc] x B[smem desc]^T, int8 x int8 -> int32
+// D[tmem] = A[smem desc] x B[smem desc]^T, int8 x int8 -> int32 (D is overwritten)
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                       uint32_t idesc, uint32_t accumulate) {
+                                       uint32_t idesc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
+        "setp.ne.b32 p, 0, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        "l"(adesc), "l"(bdesc), "r"(idesc)
         : "memory");
 }
-// 32 consecutive TMEM columns of this thread's lane
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 16x256b.x4: 16 TMEM lanes x 32 columns; lane t gets rows t/4 and t/4 + 8 of the 16 and, per
+// 8-column repeat r, registers 4r..4r+3 = (row t/4, columns 8r + 2(t%4) + {0,1}), then the same
+// columns of row t/4 + 8.
+__device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, "
-        "%28, %29, %30, %31}, [%32];"
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+        "%11, %12, %13, %14, %15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
           "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
-          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
-          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
-          "=r"(r[31])
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() {
@@ -160,39 +191,64 @@ __device__ __forceinline__ uint64_t smem_desc(const void *p) {
            | (1ull << 46)                      // descriptor version (sm_100)
            | (2ull << 61);                     // SWIZZLE_128B
 }
-// kind::i8 instruction descriptor: D s32, A s8, B s8, both K-major, N = BN, M = BM.
-constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
+// kind::i8 instruction descriptor: D s32, A s8, B s8, both K-major, M = 128, N = bn.
+__host__ __device__ constexpr uint32_t idesc_i8(int bn) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) |
+           ((uint32_t)(BMW >> 4) << 24);
+}
 
-__global__ void __launch_bounds__(THREADS)
-    gemm_q8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const float *__restrict__ xs, const float *__restrict__ ws, int M, int G,
-                      size_t row_begin, size_t sub_n, int tiles_m, int tiles_n,
-                      float *__restrict__ out, int *err) {
+// Packed f32 pairs (two outputs per instruction).
+__device__ __forceinline__ uint64_t pk2(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+template <class C>
+__global__ void __launch_bounds__(C::THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                   const __grid_constant__ CUtensorMap tmWS, const __grid_constant__ CUtensorMap tmXS,
+                   int M, int G, int row_begin, int sub_n, int tiles_w, int tiles_t,
+                   float *__restrict__ out, int *err) {
+    constexpr int BN = C::BN, STAGES = C::STAGES, GPR = C::GPR, EPI = C::EPI, COLS = C::COLS;
     extern __shared__ uint8_t smem_raw[];
-    Smem &sm = *reinterpret_cast<Smem *>((((uintptr_t)smem_raw) + 1023) & ~(uintptr_t)1023);
+    TcSmem<C> &sm =
+        *reinterpret_cast<TcSmem<C> *>((((uintptr_t)smem_raw) + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kstages = G / 4;
-    const int ntiles = tiles_m * tiles_n;
+    const int kstages = G / GPS;
+    const int ntiles = tiles_w * tiles_t;
     volatile int *abort_flag = &sm.abort_flag;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; i++) {
             mbar_init(&sm.full[i], 1);
-            mbar_init(&sm.empty[i], 1);
+            mbar_init(&sm.empty[i], 1 + EPI);  // the MMA commit and every epilogue warp
         }
-        for (int i = 0; i < NBUF; i++) {
+        for (int i = 0; i < 2; i++) {
             mbar_init(&sm.tfull[i], 1);
-            mbar_init(&sm.tempty[i], EPI_WARPS);
+            mbar_init(&sm.tempty[i], EPI);
         }
         mbar_init(&sm.done, 1);
         sm.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 1) {  // TMEM: 512 columns for the four group accumulators
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(&sm.tmem_base)),
-                     "r"(TMEM_COLS));
+                     "r"(C::TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -200,22 +256,28 @@ __global__ void __launch_bounds__(THREADS)
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
 
+    // epilogue geometry: TMEM lane quarter, token-column slice
+    const int quarter = warp & 3, slice = (warp - 2) >> 2;
+    const uint32_t tlane = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(slice * COLS);
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-                const int tm = t % tiles_m, tn = t / tiles_m;
+                const int tt = t % tiles_t, tw = t / tiles_t;
+                const int wrow = row_begin + tw * BMW, tok = tt * BN;
                 for (int ks = 0; ks < kstages; ks++, it++) {
                     const int s = it % STAGES;
                     if (!mbar_wait(&sm.empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, err)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_tx(&sm.full[s], STAGE_TX);
-                    tma_load_2d(sm.a[s], &tmA, &sm.full[s], ks * BK, tm * BM);
-                    tma_load_2d(sm.b[s], &tmB, &sm.full[s], ks * BK, (int)(row_begin + tn * BN));
+                    mbar_arrive_tx(&sm.full[s], C::STAGE_TX);
+                    tma_load_2d(sm.a[s], &tmW, &sm.full[s], ks * BK, wrow);
+                    tma_load_2d(sm.b[s], &tmX, &sm.full[s], ks * BK, tok);
+                    tma_load_2d(&sm.ws[s][0][0], &tmWS, &sm.full[s], ks * GPS, wrow);
+                    tma_load_2d(&sm.xs[s][0][0], &tmXS, &sm.full[s], tok, ks * GPS);
                 }
             }
             if (!ok) {
@@ -231,7 +293,8 @@ __global__ void __launch_bounds__(THREADS)
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            uint32_t it = 0, gc = 0;
+            constexpr uint32_t IDESC = idesc_i8(BN);
+            uint32_t it = 0, rc = 0;  // stage and round counters
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 for (int ks = 0; ks < kstages && ok; ks++, it++) {
@@ -242,17 +305,19 @@ __global__ void __launch_bounds__(THREADS)
                     }
                     tc_fence_after();
                     const uint64_t ad = smem_desc(sm.a[s]), bd = smem_desc(sm.b[s]);
-                    for (int j = 0; j < 4; j++, gc++) {
-                        const int buf = gc % NBUF;
-                        if (!mbar_wait(&sm.tempty[buf], ((gc / NBUF) & 1) ^ 1, abort_flag, err)) {
+                    for (int r = 0; r < GPS / GPR; r++, rc++) {
+                        const int rb = rc & 1;
+                        if (!mbar_wait(&sm.tempty[rb], ((rc >> 1) & 1) ^ 1, abort_flag, err)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        // K step j: 32 bytes further along the 128-byte rows
-                        mma_i8(tmem + buf * BN, ad + (uint64_t)(2 * j), bd + (uint64_t)(2 * j),
-                               IDESC, 0u);
-                        tc_commit(&sm.tfull[buf]);
+                        for (int j = 0; j < GPR; j++) {
+                            const int g = r * GPR + j;  // K step g: 32 bytes along the rows
+                            mma_i8(tmem + (rb * GPR + j) * BN, ad + (uint64_t)(2 * g),
+                                   bd + (uint64_t)(2 * g), IDESC);
+                        }
+                        tc_commit(&sm.tfull[rb]);
                     }
                     tc_commit(&sm.empty[s]);
                 }
@@ -265,88 +330,122 @@ __global__ void __launch_bounds__(THREADS)
         }
     } else {
         // ------------------------------------------------ epilogue
-        const int ew = warp - 2;                 // 0..7
-        const int quarter = warp & 3;            // TMEM lane quarter this warp may access
-        const int half = ew >> 2;                // column half: 0 -> 0..63, 1 -> 64..127
-        const int row_in_tile = quarter * 32 + lane;
-        const uint32_t taddr_lane = tmem + ((uint32_t)(quarter * 32) << 16) + half * 64;
-        uint32_t gc = 0;
-        int blk = 0;  // scale block counter (4 groups) for the ws double buffer
+        // TMEM is read with the 16x256b shape: per load, lane t holds weight rows t/4 and
+        // t/4 + 8 of a 16-lane half and, per 8-column repeat r, the token pair 8r + 2(t%4) + {0,1}.
+        // A thread thus owns 4 weight rows (R_i = 32*quarter + t/4 + 8i) and COLS/4 tokens, and
+        // each token pair is one f32x2 operand.
+        const int r0 = quarter * 32 + (lane >> 2), kq = lane & 3;
+        uint32_t it = 0, rc = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-            const int tm = t % tiles_m, tn = t / tiles_m;
-            const int m = tm * BM + row_in_tile;
-            const size_t n0 = (size_t)tn * BN, c0n = n0 + half * 64;  // first column of the warp
-            float acc[64];
+            const int tt = t % tiles_t, tw = t / tiles_t;
+            // acc[cb][h][r][i]: column block cb (32 tokens), half h, repeat r, row R_{2h+i}
+            uint64_t acc[COLS / 32][2][4][2];
 #pragma unroll
-            for (int i = 0; i < 64; i++) acc[i] = 0.0f;
-            for (int gb = 0; gb < G && ok; gb += 4, blk++) {
-                // this warp's copy of the weight scales of groups gb..gb+3 for its 64 columns:
-                // lane l loads columns l and l + 32 (four groups each) and stores them transposed
-                float (*wsb)[64] = sm.ws[ew][blk & 1];
-                __syncwarp();  // the buffer's previous use (two blocks ago) is finished
+            for (int cb = 0; cb < COLS / 32; cb++)
 #pragma unroll
-                for (int h2 = 0; h2 < 2; h2++) {
-                    const int col = lane + 32 * h2;
-                    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (c0n + col < sub_n)
-                        v = __ldg(reinterpret_cast<const float4 *>(
-                            ws + (row_begin + c0n + col) * (size_t)G + gb));
-                    wsb[0][col] = v.x;
-                    wsb[1][col] = v.y;
-                    wsb[2][col] = v.z;
-                    wsb[3][col] = v.w;
+                for (int h = 0; h < 2; h++)
+#pragma unroll
+                    for (int r = 0; r < 4; r++) acc[cb][h][r][0] = acc[cb][h][r][1] = 0ull;
+            for (int ks = 0; ks < kstages && ok; ks++, it++) {
+                const int s = it % STAGES;
+                if (!mbar_wait(&sm.full[s], (it / STAGES) & 1, abort_flag, err)) {
+                    ok = false;
+                    break;
                 }
-                float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (m < M) xv = __ldg(reinterpret_cast<const float4 *>(xs + (size_t)m * G + gb));
-                __syncwarp();
-                for (int j = 0; j < 4; j++, gc++) {
-                    const int buf = gc % NBUF;
-                    if (!mbar_wait(&sm.tfull[buf], (gc / NBUF) & 1, abort_flag, err)) {
+                float4 w4[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+                    w4[i] = *reinterpret_cast<const float4 *>(&sm.ws[s][r0 + 8 * i][0]);
+                const float *xbase = &sm.xs[s][0][slice * COLS + 4 * kq];
+#pragma unroll
+                for (int rr = 0; rr < GPS / GPR; rr++, rc++) {
+                    const int rb = rc & 1;
+                    if (!mbar_wait(&sm.tfull[rb], (rc >> 1) & 1, abort_flag, err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const float xj = j == 0 ? xv.x : j == 1 ? xv.y : j == 2 ? xv.z : xv.w;
+                    // the round's GPR group accumulators, chunk by chunk (cb, h): all GPR loads
+                    // of a chunk in flight together, one wait, then their arithmetic
 #pragma unroll
-                    for (int hc = 0; hc < 2; hc++) {  // 32 columns at a time
-                        uint32_t c[32];
-                        tmem_ld32(taddr_lane + buf * BN + 32 * hc, c);
+                    for (int ch = 0; ch < 2 * (COLS / 32); ch++) {
+                        const int cb = ch >> 1, h = ch & 1;
+                        uint32_t c[GPR][16];
+#pragma unroll
+                        for (int j = 0; j < GPR; j++)
+                            tmem_ld16x256(tlane + (rb * GPR + j) * BN + ((uint32_t)(16 * h) << 16) +
+                                              32 * cb,
+                                          c[j]);
                         tmem_ld_wait();
-                        if (hc == 1) {  // the whole accumulator is in registers: release it
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&sm.tempty[buf]);
-                        }
-                        // exact i32 -> f32 (|c| < 2^22): bits(c + 0x4B400000) - 12582912.0f,
-                        // then the reference's separately rounded products and sum (the
-                        // intrinsics keep the compiler from contracting them into an FMA)
-                        const float *wsj = wsb[j] + 32 * hc;
 #pragma unroll
-                        for (int i = 0; i < 32; i++) {
-                            const float cf =
-                                __fadd_rn(__int_as_float((int)c[i] + 0x4B400000), -12582912.0f);
-                            const float sc = __fmul_rn(xj, wsj[i]);
-                            acc[32 * hc + i] = __fadd_rn(acc[32 * hc + i], __fmul_rn(cf, sc));
+                        for (int j = 0; j < GPR; j++) {
+                            const int g = rr * GPR + j;  // group within the stage
+                            // token scales of group g, permuted within 32-token blocks so that
+                            // one 16-byte load holds the pairs of repeats 2p and 2p + 1
+                            const float *xg = xbase + g * BN + 32 * cb;
+                            const ulonglong2 xv0 = *reinterpret_cast<const ulonglong2 *>(xg);
+                            const ulonglong2 xv1 = *reinterpret_cast<const ulonglong2 *>(xg + 16);
+                            uint64_t ws2[2];
+#pragma unroll
+                            for (int i = 0; i < 2; i++) {
+                                const float4 &wv4 = w4[2 * h + i];
+                                const float wv = g == 0 ? wv4.x : g == 1 ? wv4.y : g == 2 ? wv4.z : wv4.w;
+                                ws2[i] = pk2(__float_as_uint(wv), __float_as_uint(wv));
+                            }
+#pragma unroll
+                            for (int r = 0; r < 4; r++) {
+                                const uint64_t xp = r == 0 ? xv0.x : r == 1 ? xv0.y : r == 2 ? xv1.x : xv1.y;
+#pragma unroll
+                                for (int i = 0; i < 2; i++) {
+                                    // exact: |c| <= 32 * 127 * 127 < 2^24
+                                    const uint64_t cf = pk2(
+                                        __float_as_uint(__int2float_rn((int)c[j][4 * r + 2 * i])),
+                                        __float_as_uint(__int2float_rn((int)c[j][4 * r + 2 * i + 1])));
+                                    const uint64_t sc = mul2(ws2[i], xp);
+                                    uint64_t &a = acc[cb][h][r][i];
+                                    if (C::EXACT) {
+                                        // separately rounded product and sum, as the reference
+                                        float c0, c1, s0, s1, a0, a1;
+                                        upk2(cf, c0, c1);
+                                        upk2(sc, s0, s1);
+                                        upk2(a, a0, a1);
+                                        a0 = __fadd_rn(a0, __fmul_rn(c0, s0));
+                                        a1 = __fadd_rn(a1, __fmul_rn(c1, s1));
+                                        a = pk2(__float_as_uint(a0), __float_as_uint(a1));
+                                    } else {
+                                        a = fma2(cf, sc, a);
+                                    }
+                                }
+                            }
                         }
                     }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sm.tempty[rb]);
                 }
+                __syncwarp();  // every lane's reads of this stage's scales are done
+                if (lane == 0) mbar_arrive(&sm.empty[s]);
             }
             if (!ok) break;
-            if (m < M && sub_n > c0n) {
-                float *orow = out + (size_t)m * sub_n + c0n;
-                const size_t nrem = sub_n - c0n;  // columns left from the warp's first one
-                if (nrem >= 64 && (((uintptr_t)orow) & 15) == 0) {
+            const int m0 = tt * BN + slice * COLS + 2 * kq;
 #pragma unroll
-                    for (int i = 0; i < 64; i += 4)
-                        *reinterpret_cast<float4 *>(orow + i) =
-                            make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
-                } else {
+            for (int h = 0; h < 2; h++)
 #pragma unroll
-                    for (int i = 0; i < 64; i++)
-                        if ((size_t)i < nrem) orow[i] = acc[i];
+                for (int i = 0; i < 2; i++) {
+                    const int n = tw * BMW + r0 + 8 * (2 * h + i);
+                    if (n >= sub_n) continue;
+#pragma unroll
+                    for (int cb = 0; cb < COLS / 32; cb++)
+#pragma unroll
+                        for (int r = 0; r < 4; r++) {
+                            const int m = m0 + 32 * cb + 8 * r;
+                            float lo, hi;
+                            upk2(acc[cb][h][r][i], lo, hi);
+                            if (m < M) out[(size_t)m * sub_n + n] = lo;
+                            if (m + 1 < M) out[(size_t)(m + 1) * sub_n + n] = hi;
+                        }
                 }
-            }
         }
     }
     tc_fence_before();
@@ -354,7 +453,7 @@ __global__ void __launch_bounds__(THREADS)
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(TMEM_COLS));
+                     "r"(C::TMEM_COLS));
     }
 }
 
@@ -393,57 +492,125 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-bool encode_2d(CUtensorMap *tm, const void *base, uint64_t inner, uint64_t outer, uint32_t box_in,
-               uint32_t box_out) {
+// Row-major 2-D tensor map: `inner` elements per row (row pitch `pitch` bytes), `outer` rows.
+bool encode_2d(CUtensorMap *tm, CUtensorMapDataType dt, const void *base, uint64_t inner,
+               uint64_t outer, uint64_t pitch, uint32_t box_in, uint32_t box_out,
+               CUtensorMapSwizzle swz) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     const cuuint64_t dims[2] = {inner, outer};
-    const cuuint64_t strides[1] = {inner};  // bytes between rows (uint8 elements)
+    const cuuint64_t strides[1] = {pitch};
     const cuuint32_t box[2] = {box_in, box_out};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides,
-                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = enc(tm, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
+}
+
+template <class C>
+int launch_tc(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out, size_t row_begin,
+              size_t row_end, cudaStream_t st, int *err) {
+    const size_t kp = w->k_pad, G = kp / 32;
+    CUtensorMap tmW, tmX, tmWS, tmXS;
+    if (!encode_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->q, kp, w->rows, kp, BK, BMW,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, act->q, kp, act->m, kp, BK, C::BN,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&tmWS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->scales, G, w->rows, G * 4, GPS, BMW,
+                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_2d(&tmXS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act->x_scales_t,
+                   (act->m + 31) / 32 * 32, G, act->xt_pitch * 4, C::BN, GPS,
+                   CU_TENSOR_MAP_SWIZZLE_NONE))
+        return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
+    const size_t sub_n = row_end - row_begin;
+    const int tiles_w = (int)((sub_n + BMW - 1) / BMW), tiles_t = (int)((act->m + C::BN - 1) / C::BN);
+    const size_t ntiles = (size_t)tiles_w * tiles_t;
+    const size_t smem = sizeof(TcSmem<C>) + 1024;
+    static bool attr_set[128] = {};  // per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail_cuda(e, "gemm_repacked (cudaGetDevice)");
+    if (dev < 0 || dev >= 128)
+        return fail(JKB_E_INVALID, "gemm_repacked", 0, 0, 0, "device ordinal %d out of range", dev);
+    if (!attr_set[dev]) {
+        e = cudaFuncSetAttribute(gemm_tc_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+        if (e != cudaSuccess) return fail_cuda(e, "gemm_repacked (tensor-core kernel attribute)");
+        attr_set[dev] = true;
+    }
+    const size_t grid = ntiles < (size_t)num_sms() ? ntiles : (size_t)num_sms();
+    gemm_tc_kernel<C><<<(unsigned)grid, C::THREADS, smem, st>>>(
+        tmW, tmX, tmWS, tmXS, (int)act->m, (int)G, (int)row_begin, (int)sub_n, tiles_w, tiles_t,
+        out, err);
+    return check_launch("gemm_tc_kernel");
 }
 
 }  // namespace
 
+// Tile widths (tokens per tile). Measured on B200 with barrier rounds (2048 x 4096 x 14336,
+// FMA epilogue, normalized to full waves) the three configurations reach the same throughput
+// per SM within 1 %, so the choice is the number of waves times the tile width: the padding of
+// a partial last token tile and the idle SMs of a partial last wave are what differ. Ties go to
+// the wider tile (less operand traffic per output).
+constexpr int TILE_BN[3] = {128, 96, 64};
+
+// The tile width with the smallest estimated time: waves of (weight tile, token tile) pairs over
+// the SMs, each wave as long as one tile's token columns.
+int choose_tile(size_t m, size_t sub_n) {
+    const size_t tiles_w = (sub_n + BMW - 1) / BMW, sms = (size_t)num_sms();
+    int best = TILE_BN[0];
+    size_t best_t = 0;
+    for (int i = 0; i < 3; i++) {
+        const size_t tiles = tiles_w * ((m + TILE_BN[i] - 1) / TILE_BN[i]);
+        const size_t t = (tiles + sms - 1) / sms * (size_t)TILE_BN[i];
+        if (i == 0 || t < best_t) {
+            best = TILE_BN[i];
+            best_t = t;
+        }
+    }
+    return best;
+}
+
+// The three configurations: (tokens per tile, epilogue warps per lane quarter, groups per
+// barrier round).
+template <bool E> using TC64 = TcCfg<64, 2, 4, E>;
+template <bool E> using TC96 = TcCfg<96, 3, 2, E>;
+template <bool E> using TC128 = TcCfg<128, 2, 2, E>;
+
+std::atomic<int> g_gemm_exact{0};
+
 // Smallest batch the tensor-core path takes (one 128-row MMA tile is mostly padding below it).
 constexpr size_t TC_MIN_M = 32;
+
+template <bool EXACT>
+int launch_tc_bn(int bn, const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out,
+                 size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
+    switch (bn) {
+        case 64: return launch_tc<TC64<EXACT>>(w, act, out, row_begin, row_end, st, err);
+        case 128: return launch_tc<TC128<EXACT>>(w, act, out, row_begin, row_end, st, err);
+        default: return launch_tc<TC96<EXACT>>(w, act, out, row_begin, row_end, st, err);
+    }
+}
 
 int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out,
                    size_t row_begin, size_t row_end, cudaStream_t st, bool *used) {
     *used = false;
     const size_t kp = w->k_pad;
     if (w->group_elems != 32 || w->mins != nullptr || kp % BK != 0 || act->m < TC_MIN_M ||
-        act->k_pad != kp || (kp / 32) % 4 != 0 || act->m > (size_t)INT32_MAX)
+        act->k_pad != kp || act->m > (size_t)INT32_MAX || w->rows > (size_t)INT32_MAX ||
+        act->x_scales_t == nullptr)
         return JKB_OK;
     if ((((uintptr_t)w->q) & 15) || (((uintptr_t)act->q) & 15) || (((uintptr_t)w->scales) & 15) ||
-        (((uintptr_t)act->x_scales) & 15))
+        (((uintptr_t)act->x_scales_t) & 15) || (act->xt_pitch & 31))
         return JKB_OK;
     int *err = tc_error_word();
     if (!err) return JKB_OK;
-    CUtensorMap tmA, tmB;
-    if (!encode_2d(&tmA, act->q, kp, act->m, BK, BM) || !encode_2d(&tmB, w->q, kp, w->rows, BK, BN))
-        return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
-    const size_t sub_n = row_end - row_begin;
-    const int tiles_m = (int)((act->m + BM - 1) / BM), tiles_n = (int)((sub_n + BN - 1) / BN);
-    const size_t ntiles = (size_t)tiles_m * tiles_n;
-    const size_t smem = sizeof(Smem) + 1024;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q8_tc_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return fail_cuda(e, "gemm_repacked (tensor-core kernel attribute)");
-        attr_set = true;
-    }
-    const size_t grid = ntiles < (size_t)num_sms() ? ntiles : (size_t)num_sms();
-    gemm_q8_tc_kernel<<<(unsigned)grid, THREADS, smem, st>>>(
-        tmA, tmB, act->x_scales, w->scales, (int)act->m, (int)(kp / 32), row_begin, sub_n, tiles_m,
-        tiles_n, out, err);
     *used = true;
-    return check_launch("gemm_q8_tc_kernel");
+    const int bn = choose_tile(act->m, row_end - row_begin);
+    return g_gemm_exact.load(std::memory_order_relaxed)
+               ? launch_tc_bn<true>(bn, w, act, out, row_begin, row_end, st, err)
+               : launch_tc_bn<false>(bn, w, act, out, row_begin, row_end, st, err);
 }
 
 }  // namespace jkb
@@ -465,3 +632,10 @@ extern "C" int jkb_device_status(int32_t *flags, void *stream) {
                     "a bounded wait in a tensor-core GEMM expired (flags %d)", v)
              : JKB_OK;
 }
+
+extern "C" int jkb_gemm_set_exact(int exact) {
+    jkb::g_gemm_exact.store(exact ? 1 : 0, std::memory_order_relaxed);
+    return JKB_OK;
+}
+
+extern "C" int jkb_gemm_get_exact(void) { return jkb::g_gemm_exact.load(std::memory_order_relaxed); }

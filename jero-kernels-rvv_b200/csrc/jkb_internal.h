@@ -100,6 +100,12 @@ struct jkb_act_q8 {
     float *x_sums;        // [m_cap][k_pad/32]
     float *x_sums_16;     // [m_cap][k_pad/16]
     float *super_scales;  // [m_cap][ceil(k/256)]
+    // x_scales transposed, [k_pad/32][xt_pitch] (xt_pitch = capacity rounded up to 32), tokens
+    // permuted within 32-token blocks as the tensor-core GEMM epilogue reads them (see
+    // act_q8_kernel). nullptr when the buffer has no room for it (the GEMM then takes the dp4a
+    // path).
+    float *x_scales_t;
+    size_t xt_pitch;
 };
 
 namespace jkb {

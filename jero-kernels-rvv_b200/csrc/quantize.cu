@@ -123,11 +123,24 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ a
                                                      int8_t *__restrict__ q,
                                                      float *__restrict__ xs,
                                                      float *__restrict__ xsum,
-                                                     float *__restrict__ xs16) {
+                                                     float *__restrict__ xs16,
+                                                     float *__restrict__ xs_t,
+                                                     size_t xt_pitch) {
     size_t kb = kp / 32;
     size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= m * kb) return;
+    const size_t m_t = xs_t ? (m + 31) / 32 * 32 : m;  // tokens covered by the transposed plane
+    if (gid >= m_t * kb) return;
     size_t r = gid / kb, b = gid % kb;
+    // Transposed scales are stored permuted within each 32-token block: token 8u + 2v + e
+    // (u, v < 4, e < 2) goes to position 16(u >> 1) + 4v + 2(u & 1) + e, so that the token
+    // pairs 2v + {0, 8, 16, 24} of a block (one tensor-core epilogue lane's) are two 16-byte
+    // words. Positions of tokens >= m in the last block hold 0.
+    const size_t xt_at = b * xt_pitch + (r & ~(size_t)31) + 16 * ((r >> 4) & 1) +
+                         4 * ((r >> 1) & 3) + 2 * ((r >> 3) & 1) + (r & 1);
+    if (r >= m) {
+        xs_t[xt_at] = 0.0f;
+        return;
+    }
     const float *src = act + r * k;
     float c[32];
     float absmax = 0.0f, s = 0.0f;
@@ -170,6 +183,7 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ a
     qo[0] = make_uint4(words[0], words[1], words[2], words[3]);
     qo[1] = make_uint4(words[4], words[5], words[6], words[7]);
     xs[r * kb + b] = d;
+    if (xs_t) xs_t[xt_at] = d;
     xsum[r * kb + b] = s;
     xs16[r * (kp / 16) + 2 * b] = h0;
     xs16[r * (kp / 16) + 2 * b + 1] = h1;
@@ -399,9 +413,11 @@ int jkb_act_q8_create(size_t m_capacity, size_t k, jkb_act_q8 **out) {
     a->k_pad = (k + 31) / 32 * 32;
     size_t kb = a->k_pad / 32, kc = a->k_pad / 16, nsb = (k + 255) / 256;
     Arena ar;
+    a->xt_pitch = (m_capacity + 31) / 32 * 32;
     size_t qb = m_capacity * a->k_pad, fb = m_capacity * kb * 4, f16b = m_capacity * kc * 4,
-           sb = m_capacity * nsb * 4;
-    ar.cap = Arena::round(qb) + 2 * Arena::round(fb) + Arena::round(f16b) + Arena::round(sb);
+           sb = m_capacity * nsb * 4, tb = a->xt_pitch * kb * 4;
+    ar.cap = Arena::round(qb) + 2 * Arena::round(fb) + Arena::round(f16b) + Arena::round(sb) +
+             Arena::round(tb);
     cudaError_t e = cudaMalloc(&ar.base, ar.cap);
     if (e != cudaSuccess) {
         delete a;
@@ -413,6 +429,7 @@ int jkb_act_q8_create(size_t m_capacity, size_t k, jkb_act_q8 **out) {
     a->x_sums = (float *)ar.take(fb);
     a->x_sums_16 = (float *)ar.take(f16b);
     a->super_scales = (float *)ar.take(sb);
+    a->x_scales_t = (float *)ar.take(tb);
     *out = a;
     return JKB_OK;
 }
@@ -441,10 +458,11 @@ int jkb_act_q8_quantize(jkb_act_q8 *a, const float *input, size_t in_len, size_t
     if (arc) return arc;
     cudaStream_t st = as_stream(stream);
     size_t kb = a->k_pad / 32, nsb = (k + 255) / 256;
-    size_t n = m * kb;
+    size_t n = (a->x_scales_t ? (m + 31) / 32 * 32 : m) * kb;
     act_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(input, m, k, a->k_pad, a->q,
                                                                a->x_scales, a->x_sums,
-                                                               a->x_sums_16);
+                                                               a->x_sums_16, a->x_scales_t,
+                                                               a->xt_pitch);
     int rc = check_launch("act_q8_kernel");
     if (rc) return rc;
     size_t ns = m * nsb;

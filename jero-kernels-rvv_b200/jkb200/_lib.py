@@ -57,6 +57,8 @@ SIGNATURES = {
     "jkb_last_error_info": [C.POINTER(jkb_error_info)],
     "jkb_clear_error": [],
     "jkb_device_status": [PI32, P],
+    "jkb_gemm_set_exact": [I],
+    "jkb_gemm_get_exact": [],
     "jkb_quantize_row_q8_0": [P, S, P, S, P],
     "jkb_quantize_row_q8_0_f32": [P, S, P, S, P],
     "jkb_quantize_row_q8_k": [P, S, P, S, P],

@@ -29,7 +29,8 @@ __all__ = [
     "vec_dot_q4_0_rvv", "vec_dot_grouped_rvv", "bitlinear_i8", "bitlinear_i8_rvv", "bitlinear_i8_ime",
     "bitlinear_i8_batch", "gemm_repacked", "gemm_repacked_rows", "gemv_repacked",
     "gemv_repacked_rows", "gemm_repacked_f32", "gemm_repacked_f32_noalloc",
-    "empty_q8_0_blocks", "empty_q8_k_blocks", "device_status",
+    "empty_q8_0_blocks", "empty_q8_k_blocks", "device_status", "gemm_set_exact", "gemm_get_exact",
+    "gemm_exact",
     "device_view",
 ]
 
@@ -117,6 +118,33 @@ def device_status(stream=None) -> int:
     v = C.c_int32(0)
     _check(_L().jkb_device_status(C.byref(v), _stream(stream)))
     return int(v.value)
+
+
+def gemm_set_exact(exact: bool) -> None:
+    """Selects the tensor-core GEMM epilogue: False (default) fused multiply-add per scale group,
+    within the reference's 1e-5 relative tolerance; True the reference's separately rounded
+    product and sum, bit-identical outputs (accumulate_scaled_tile_scalar, repack.rs:3045)."""
+    _check(_L().jkb_gemm_set_exact(1 if exact else 0))
+
+
+def gemm_get_exact() -> bool:
+    return bool(_L().jkb_gemm_get_exact())
+
+
+class gemm_exact:
+    """Context manager: the bit-exact GEMM epilogue inside the block, the previous one after."""
+
+    def __init__(self, exact: bool = True):
+        self.exact = exact
+
+    def __enter__(self):
+        self.prev = gemm_get_exact()
+        gemm_set_exact(self.exact)
+        return self
+
+    def __exit__(self, *exc):
+        gemm_set_exact(self.prev)
+        return False
 
 
 def _dptr(t):

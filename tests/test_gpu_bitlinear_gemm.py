@@ -8,7 +8,7 @@ import pytest
 import torch
 
 import refgen as R
-from gpuutil import bits, dev, host, upload
+from gpuutil import assert_gemm_close, gemm_abs_bound, bits, dev, host, upload
 
 pytestmark = pytest.mark.gpu
 
@@ -121,19 +121,23 @@ def test_gemm_repacked_bit_exact(jkb, oracle, quant, m):
     act = oracle.normal(m * cols, 100 + m, 1.0)
     a = jkb.QuantizedActQ8.quantize(dev(act), m, cols)
     out = torch.empty(m * rows, dtype=torch.float32, device="cuda")
-    rw.gemm(out, a)
     ref = _oracle_gemm(oracle, quant, wb, rows, cols, act, m)
-    assert np.array_equal(bits(host(out).reshape(m, rows)), bits(ref))
-    if m == 1:
-        o1 = torch.empty(rows, dtype=torch.float32, device="cuda")
-        rw.gemv(o1, a)
-        assert np.array_equal(bits(host(o1)), bits(ref[0]))
-    parts = []
-    for r0, r1 in ((0, 9), (9, 64), (64, 72)):
-        o = torch.empty(m * (r1 - r0), dtype=torch.float32, device="cuda")
-        rw.gemm_rows(o, a, range(r0, r1))
-        parts.append(host(o).reshape(m, r1 - r0))
-    assert np.array_equal(bits(np.concatenate(parts, axis=1)), bits(ref))
+    with jkb.gemm_exact():  # the tensor-core path (m = 64) with the reference's roundings
+        rw.gemm(out, a)
+        assert np.array_equal(bits(host(out).reshape(m, rows)), bits(ref))
+        if m == 1:
+            o1 = torch.empty(rows, dtype=torch.float32, device="cuda")
+            rw.gemv(o1, a)
+            assert np.array_equal(bits(host(o1)), bits(ref[0]))
+        parts = []
+        for r0, r1 in ((0, 9), (9, 64), (64, 72)):
+            o = torch.empty(m * (r1 - r0), dtype=torch.float32, device="cuda")
+            rw.gemm_rows(o, a, range(r0, r1))
+            parts.append(host(o).reshape(m, r1 - r0))
+        assert np.array_equal(bits(np.concatenate(parts, axis=1)), bits(ref))
+    rw.gemm(out, a)  # default epilogue: bit-exact on the dp4a path, within tolerance on tcgen05
+    assert_gemm_close(host(out).reshape(m, rows), ref,
+                      gemm_abs_bound(oracle, quant, wb, rows, cols, act, m))
 
 
 @pytest.mark.parametrize("m,rows,cols", [(128, 512, 4096), (256, 384, 2048)])
@@ -144,9 +148,13 @@ def test_gemm_repacked_q8_0_prefill_shapes(jkb, oracle, m, rows, cols):
     act = oracle.normal(m * cols, 10, 1.0)
     scratch = jkb.QuantizedActQ8(m, cols)
     out = torch.empty(m * rows, dtype=torch.float32, device="cuda")
-    jkb.gemm_repacked_f32(out, rw, dev(act), m, scratch)
     ref = _oracle_gemm(oracle, 8, wb, rows, cols, act, m)
+    with jkb.gemm_exact():
+        jkb.gemm_repacked_f32(out, rw, dev(act), m, scratch)
     assert np.array_equal(bits(host(out).reshape(m, rows)), bits(ref))
+    jkb.gemm_repacked_f32(out, rw, dev(act), m, scratch)
+    assert_gemm_close(host(out).reshape(m, rows), ref,
+                      gemm_abs_bound(oracle, 8, wb, rows, cols, act, m))
 
 
 def test_gemm_validation(jkb, oracle):

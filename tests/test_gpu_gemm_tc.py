@@ -1,16 +1,22 @@
 """The tcgen05 tensor-core path of the repacked GEMM (32-element scale groups without mins:
 Q8_0, Q4_0, TQ2_0, I2_S weights; batches of at least 32 tokens; K a multiple of 128) vs the CPU
-oracle, bit for bit: every output accumulates its groups in K order as
-accumulate_scaled_tile_scalar does (repack.rs:3045-3093), acc += (f32)c * (xs * ws).
+oracle. Every output accumulates its groups in K order as accumulate_scaled_tile_scalar does
+(repack.rs:3045-3093), acc += (f32)c * (xs * ws):
+* with the exact epilogue (jkb.gemm_exact()) bit for bit;
+* with the default fused multiply-add epilogue within the f32 tolerance contract
+  (|err| <= 1e-5 * sum_k |x~||w~| per output, l2 relative error < 1e-5);
+* the integer group sums c themselves are exact in both: with unit scales the default epilogue
+  returns the integer dot products bit for bit.
 
-Shapes cover one tile (32 x 128 x 128: one K stage, a partial M tile), ragged M and N tiles,
-K = 14336 (448 groups), a row range that starts inside a tile, and every format the path
-takes. The device error word (bounded waits inside the kernel) must stay clear."""
+Shapes cover one tile (32 x 128 x 128: one K stage, a partial token tile), ragged token and
+weight-row tiles, K = 14336 (448 groups), a row range that starts inside a tile, batches that
+select each of the three tile widths (64, 96, 128 tokens), and every format the path takes.
+The device error word (bounded waits inside the kernel) must stay clear."""
 import numpy as np
 import pytest
 import torch
 
-from gpuutil import bits, dev, host
+from gpuutil import assert_gemm_close, bits, dev, gemm_abs_bound, host
 
 pytestmark = pytest.mark.gpu
 
@@ -28,16 +34,22 @@ def _oracle_gemm(oracle, quant, wb, rows, cols, act, m, r0=0, r1=None):
                                 nthreads=8)
 
 
-@pytest.mark.parametrize("quant,m,rows,cols", [
+SHAPES = [
     (8, 32, 128, 128),      # one tile, one K stage
-    (8, 200, 300, 4096),    # ragged M (72 of 128) and N (44 of 128) tiles
-    (8, 129, 257, 14336),   # K = 14336, one row past an M tile, one past an N tile
+    (8, 200, 300, 4096),    # ragged token and weight-row tiles
+    (8, 129, 257, 14336),   # K = 14336, one row past a tile on both sides
     (8, 512, 1024, 4096),   # several tiles per CTA on small grids
+    (8, 2048, 4096, 256),   # 2048 tokens x 32 weight tiles: the 64-token tile, 7 waves
+    (8, 96, 12800, 256),    # 100 weight tiles, one 96-token tile each: the 96-token tile
+    (8, 512, 18944, 256),   # 512 tokens x 148 weight tiles: the 128-token tile
+    (8, 200, 12032, 256),   # 94 weight tiles, a partial last 64-token tile
     (2, 64, 640, 1024),     # Q4_0
     (35, 96, 256, 512),     # TQ2_0
     (36, 40, 384, 2560),    # I2_S (per-tensor scale)
-])
-def test_tc_gemm_bit_exact(jkb, oracle, quant, m, rows, cols):
+]
+
+
+def _run(jkb, oracle, quant, m, rows, cols):
     wb = _weights(oracle, quant, rows, cols, 40 + rows)
     rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", quant, [rows, cols], wb), rows, cols)
     act = oracle.normal(m * cols, 50 + m, 1.0)
@@ -45,8 +57,48 @@ def test_tc_gemm_bit_exact(jkb, oracle, quant, m, rows, cols):
     out = torch.full((m * rows,), float("nan"), dtype=torch.float32, device="cuda")
     rw.gemm(out, a)
     assert jkb.device_status() == 0
+    rw.destroy()
+    return wb, act, host(out).reshape(m, rows)
+
+
+@pytest.mark.parametrize("quant,m,rows,cols", SHAPES)
+def test_tc_gemm_bit_exact(jkb, oracle, quant, m, rows, cols):
+    with jkb.gemm_exact():
+        wb, act, got = _run(jkb, oracle, quant, m, rows, cols)
     ref = _oracle_gemm(oracle, quant, wb, rows, cols, act, m)
-    assert np.array_equal(bits(host(out).reshape(m, rows)), bits(ref))
+    assert np.array_equal(bits(got), bits(ref))
+
+
+@pytest.mark.parametrize("quant,m,rows,cols", SHAPES)
+def test_tc_gemm_fma_within_tolerance(jkb, oracle, quant, m, rows, cols):
+    assert not jkb.gemm_get_exact()
+    wb, act, got = _run(jkb, oracle, quant, m, rows, cols)
+    ref = _oracle_gemm(oracle, quant, wb, rows, cols, act, m)
+    assert np.all(np.isfinite(got))
+    assert_gemm_close(got, ref, gemm_abs_bound(oracle, quant, wb, rows, cols, act, m))
+
+
+def test_tc_gemm_integer_group_sums_exact(jkb, oracle):
+    """Unit scales (Q8_0 d = 1.0; every activation block has absmax 127, so x_scale = 1.0 and
+    the quantized values are the inputs): each output is the exact integer dot product, which
+    the default epilogue must return bit for bit -- the int8 MMA sums are exact."""
+    m, rows, cols = 96, 256, 2048
+    rng = np.random.default_rng(3)
+    wq = rng.integers(-127, 128, (rows, cols)).astype(np.int8)
+    blk = np.zeros((rows, cols // 32, 34), np.uint8)
+    blk[..., 0:2] = np.frombuffer(np.float16(1.0).tobytes(), np.uint8)
+    blk[..., 2:] = wq.reshape(rows, cols // 32, 32).view(np.uint8)
+    wb = blk.reshape(-1)
+    x = rng.integers(-127, 128, (m, cols)).astype(np.float32)
+    x[:, ::32] = 127.0
+    rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", 8, [rows, cols], wb), rows, cols)
+    a = jkb.QuantizedActQ8.quantize(dev(x.reshape(-1)), m, cols)
+    out = torch.empty(m * rows, dtype=torch.float32, device="cuda")
+    rw.gemm(out, a)
+    assert jkb.device_status() == 0
+    want = x.astype(np.int64) @ wq.astype(np.int64).T
+    assert np.abs(want).max() < 2 ** 24
+    assert np.array_equal(host(out).reshape(m, rows), want.astype(np.float32))
     rw.destroy()
 
 
@@ -59,10 +111,14 @@ def test_tc_gemm_row_range(jkb, oracle):
     act = oracle.normal(m * cols, 8, 1.0)
     a = jkb.QuantizedActQ8.quantize(dev(act), m, cols)
     out = torch.empty(m * 233, dtype=torch.float32, device="cuda")
-    rw.gemm_rows(out, a, range(100, 333))
+    with jkb.gemm_exact():
+        rw.gemm_rows(out, a, range(100, 333))
     assert jkb.device_status() == 0
     ref = _oracle_gemm(oracle, 8, wb, rows, cols, act, m)
     assert np.array_equal(bits(host(out).reshape(m, 233)), bits(ref[:, 100:333]))
+    rw.gemm_rows(out, a, range(100, 333))
+    bound = gemm_abs_bound(oracle, 8, wb, rows, cols, act, m)
+    assert_gemm_close(host(out).reshape(m, 233), ref[:, 100:333], bound[:, 100:333])
     rw.destroy()
 
 
@@ -80,8 +136,12 @@ def test_tc_gemm_special_activations(jkb, oracle):
     act = act.reshape(-1)
     a = jkb.QuantizedActQ8.quantize(dev(act), m, cols)
     out = torch.empty(m * rows, dtype=torch.float32, device="cuda")
-    rw.gemm(out, a)
+    with jkb.gemm_exact():
+        rw.gemm(out, a)
     assert jkb.device_status() == 0
     ref = _oracle_gemm(oracle, 8, wb, rows, cols, act, m)
     assert np.array_equal(bits(host(out).reshape(m, rows)), bits(ref))
+    rw.gemm(out, a)
+    assert_gemm_close(host(out).reshape(m, rows), ref,
+                      gemm_abs_bound(oracle, 8, wb, rows, cols, act, m))
     rw.destroy()
