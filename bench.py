@@ -310,30 +310,28 @@ def run_gpu(args):
                                 device_id=torch.device("cuda", local))
     import jkb200 as jkb
 
+    from jkb200.shard import ShardedOutputs
+
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
-    # --- weights: this rank's row shard of every matrix (layer matrices in two copies)
+    # --- weights: this rank's row shard of every matrix (layer matrices in two copies); the
+    # output slices share one flat buffer that one all-gather per step collects
+    outs = ShardedOutputs([(name, rows) for name, _, rows, _, _ in DECODE_8B], world, rank)
     shards, weights, total_bytes = [], {}, 0
     for i, (name, quant, rows, cols, s) in enumerate(DECODE_8B):
-        per = rows // world
-        r0, r1 = rank * per, (rank + 1) * per
+        rr = outs.rows_of(name)
+        per = len(rr)
         total_bytes += algorithmic_bytes(quant, rows, cols)
         copies = 1 if name == "lm_head" else LAYER_COPIES
         for c in range(copies):
-            raw = synth_matrix(quant, rows, cols, 1000 + i + 97 * c, r0, r1)
+            raw = synth_matrix(quant, rows, cols, 1000 + i + 97 * c, rr.start, rr.stop)
             weights[(name, c)] = jkb.Weight(jkb.TensorView(f"{name}.{c}", quant, [per, cols], raw),
                                             per, cols)
         shards.append((name, quant, per, cols, s, copies))
     g = torch.Generator(device="cpu").manual_seed(7)
     xs = {s: torch.randn(n, generator=g).cuda() for s, n in ACTS.items()}
     xq = {s: jkb.empty_q8_k_blocks(n // 256) for s, n in ACTS.items()}
-    out_len = sum(per for _, _, per, _, _, _ in shards)
-    out = torch.empty(out_len, dtype=torch.float32, device="cuda")
-    gathered = torch.empty(out_len * world, dtype=torch.float32, device="cuda") if world > 1 else None
-    offs, o = {}, 0
-    for name, _, per, _, _, _ in shards:
-        offs[name] = (o, o + per)
-        o += per
+    out_len = outs.local_len
     fns = {Q4_K: jkb.gemv_q4_k_q8_k, Q6_K: jkb.gemv_q6_k_q8_k}
     rvv = {Q4_K: jkb.vec_dot_q4_k_m_rvv, Q6_K: jkb.vec_dot_q6_k_rvv}
     groups = {}  # activation stream -> matrices fed by it, in DECODE_8B order
@@ -342,7 +340,7 @@ def run_gpu(args):
 
     def run_group(s, copy):
         """The matrices sharing activation s: one f32-input launch (grouped when several)."""
-        items = [(out[offs[n][0]:offs[n][1]], weights[(n, copy % c)]) for n, _, c in groups[s]]
+        items = [(outs.local_slice(n), weights[(n, copy % c)]) for n, _, c in groups[s]]
         if len(items) == 1:
             rvv[groups[s][0][1]](items[0][0], items[0][1], xs[s])
         else:
@@ -358,15 +356,13 @@ def run_gpu(args):
         for name, quant, per, cols, s, copies in shards:
             if name == "lm_head":
                 continue
-            a, b = offs[name]
-            fns[quant](out[a:b], weights[(name, copy)], xq[s])
+            fns[quant](outs.local_slice(name), weights[(name, copy)], xq[s])
 
     def lm_head():
         if not args.unfused:
             run_group("f", 0)
             return
-        a, b = offs["lm_head"]
-        fns[Q6_K](out[a:b], weights[("lm_head", 0)], xq["f"])
+        fns[Q6_K](outs.local_slice("lm_head"), weights[("lm_head", 0)], xq["f"])
 
     def step(i, evs=None):
         layer_part(i % LAYER_COPIES)
@@ -375,8 +371,7 @@ def run_gpu(args):
         lm_head()
         if evs is not None:
             evs[1].record(stream)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
+        outs.gather()
 
     for i in range(args.warmup):  # eager warm-up (also sets kernel attributes)
         step(i)
@@ -438,9 +433,9 @@ def run_gpu(args):
 
     # --- e2e: the public API with host buffers (pinned f32 inputs in, f32 outputs out)
     host_in = {s: xs[s].cpu().pin_memory() for s in ACTS}
-    host_out = torch.empty(out_len, dtype=torch.float32).pin_memory()
+    host_out = torch.empty(outs.gathered.numel(), dtype=torch.float32).pin_memory()
     h2d = sum(v.numel() * 4 for v in host_in.values())
-    d2h = out_len * 4
+    d2h = outs.gathered.numel() * 4
 
     def e2e_step(i):
         for s in ACTS:
@@ -452,11 +447,9 @@ def run_gpu(args):
             for s in ACTS:
                 jkb.quantize_row_q8_k(xs[s], xq[s])
             for name, quant, per, cols, s, copies in shards:
-                a, b = offs[name]
-                fns[quant](out[a:b], weights[(name, i % copies)], xq[s])
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
-        host_out.copy_(out, non_blocking=True)
+                fns[quant](outs.local_slice(name), weights[(name, i % copies)], xq[s])
+        outs.gather()
+        host_out.copy_(outs.gathered, non_blocking=True)
 
     for i in range(args.warmup):
         e2e_step(i)

@@ -1,0 +1,101 @@
+"""One rank of the multi-GPU parity check (launched by tests/test_gpu_multigpu.py under torchrun).
+
+Llama-3-70B decode shapes: Q4_K_M 8192 -> 28672 and 28672 -> 8192, Q6_K
+lm_head 8192 -> 128256, plus a Q8_0 prefill GEMM (512 tokens, 8192 -> 28672). Every rank
+uploads only its output-row shard (jkb200.shard.shard_rows), computes it with the same kernels
+as a single-GPU call, and one NCCL all-gather collects the slices. Rank 0 also holds the full
+matrices and checks that the reassembled outputs equal the single-GPU results bit for bit: rows
+are independent, so sharding by rows changes no arithmetic (gemv_repacked_rows, repack.rs:4014).
+Prints one JSON line per rank and exits non-zero on a mismatch.
+"""
+import json
+import os
+import sys
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.join(ROOT, "jero-kernels-rvv_b200"))
+sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402  (seeded synthetic GGUF matrices)
+import jkb200 as jkb  # noqa: E402
+from jkb200.shard import ShardedOutputs, shard_rows  # noqa: E402
+
+Q4_K, Q6_K, Q8_0 = 12, 14, 8
+MATS = [("ffn_gate", Q4_K, 28672, 8192, "h"), ("ffn_down", Q4_K, 8192, 28672, "a"),
+        ("lm_head", Q6_K, 128256, 8192, "f")]
+ACTS = {"h": 8192, "a": 28672, "f": 8192}
+
+
+def main():
+    world = int(os.environ["WORLD_SIZE"])
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", local))
+    g = torch.Generator().manual_seed(11)
+    xs = {s: torch.randn(n, generator=g).cuda() for s, n in ACTS.items()}
+    xq = {s: jkb.empty_q8_k_blocks(n // 256) for s, n in ACTS.items()}
+    for s in ACTS:
+        jkb.quantize_row_q8_k(xs[s], xq[s])
+    outs = ShardedOutputs([(n, r) for n, _, r, _, _ in MATS], world, rank)
+    full_raw = {}
+    for i, (name, quant, rows, cols, s) in enumerate(MATS):
+        rr = outs.rows_of(name)
+        raw = bench.synth_matrix(quant, rows, cols, 500 + i, rr.start, rr.stop)
+        w = jkb.Weight(jkb.TensorView(name, quant, [len(rr), cols], raw), len(rr), cols)
+        fn = jkb.gemv_q4_k_q8_k if quant == Q4_K else jkb.gemv_q6_k_q8_k
+        fn(outs.local_slice(name), w, xq[s])
+        if rank == 0:
+            full_raw[name] = bench.synth_matrix(quant, rows, cols, 500 + i)
+    outs.gather()
+
+    # prefill GEMM, weight rows sharded the same way; its output is [m][rows], so each rank
+    # sends its slice transposed ([rows][m]) and rank 0 transposes the concatenation back
+    m, n, k = 512, 28672, 8192
+    rr = shard_rows(n, world, rank)
+    raw = bench.synth_matrix(Q8_0, n, k, 600, rr.start, rr.stop)
+    rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", Q8_0, [len(rr), k], raw), len(rr), k)
+    x = torch.randn(m * k, generator=torch.Generator().manual_seed(12)).cuda()
+    act = jkb.QuantizedActQ8.quantize(x, m, k)
+    part = torch.empty(m * len(rr), dtype=torch.float32, device="cuda")
+    rw.gemm(part, act)
+    slab = part.view(m, len(rr)).t().contiguous().view(-1)
+    gathered = [torch.empty(m * len(shard_rows(n, world, r)), dtype=torch.float32, device="cuda")
+                for r in range(world)]
+    dist.all_gather(gathered, slab)
+    torch.cuda.synchronize()
+
+    res = {"rank": rank, "world": world}
+    ok = True
+    if rank == 0:
+        for i, (name, quant, rows, cols, s) in enumerate(MATS):
+            w = jkb.Weight(jkb.TensorView(name, quant, [rows, cols], full_raw[name]), rows, cols)
+            ref = torch.empty(rows, dtype=torch.float32, device="cuda")
+            fn = jkb.gemv_q4_k_q8_k if quant == Q4_K else jkb.gemv_q6_k_q8_k
+            fn(ref, w, xq[s])
+            same = torch.equal(outs.output(name).view(torch.int32), ref.view(torch.int32))
+            res[name] = "bit-exact" if same else "MISMATCH"
+            ok &= same
+        rwf = jkb.RepackedWeight.from_tensor(
+            jkb.TensorView("w", Q8_0, [n, k], bench.synth_matrix(Q8_0, n, k, 600)), n, k)
+        ref = torch.empty(m * n, dtype=torch.float32, device="cuda")
+        rwf.gemm(ref, act)
+        got = torch.cat(gathered).view(n, m).t().contiguous().view(-1)
+        same = torch.equal(got.view(torch.int32), ref.view(torch.int32))
+        res["prefill_gemm"] = "bit-exact" if same else "MISMATCH"
+        ok &= same
+        res["device_status"] = jkb.device_status()
+    res["ok"] = bool(ok)
+    print(json.dumps(res), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    sys.exit(0 if ok else 1)
+
+
+if __name__ == "__main__":
+    main()
