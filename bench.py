@@ -310,13 +310,20 @@ def run_gpu(args):
                                 device_id=torch.device("cuda", local))
     import jkb200 as jkb
 
-    from jkb200.shard import ShardedOutputs
+    from jkb200.shard import PeerOutputs, ShardedOutputs
 
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
-    # --- weights: this rank's row shard of every matrix (layer matrices in two copies); the
-    # output slices share one flat buffer that one all-gather per step collects
-    outs = ShardedOutputs([(name, rows) for name, _, rows, _, _ in DECODE_8B], world, rank)
+    # --- weights: this rank's row shard of every matrix (layer matrices in two copies). With
+    # N > 1 the slices are collected either by one all-gather kernel of this library per step
+    # (peer: the rows pushed to every peer over NVLink, then a bounded wait for the peers' rows)
+    # or by one NCCL all-gather per step (nccl)
+    mats = [(name, rows) for name, _, rows, _, _ in DECODE_8B]
+    peer = world > 1 and args.collective == "peer"
+    outs = PeerOutputs(mats, world, rank) if peer else ShardedOutputs(mats, world, rank)
+
+    def lslice(name, i):
+        return outs.local_slice(name, i % 2) if peer else outs.local_slice(name)
     shards, weights, total_bytes = [], {}, 0
     for i, (name, quant, rows, cols, s) in enumerate(DECODE_8B):
         rr = outs.rows_of(name)
@@ -331,47 +338,48 @@ def run_gpu(args):
     g = torch.Generator(device="cpu").manual_seed(7)
     xs = {s: torch.randn(n, generator=g).cuda() for s, n in ACTS.items()}
     xq = {s: jkb.empty_q8_k_blocks(n // 256) for s, n in ACTS.items()}
-    out_len = outs.local_len
-    fns = {Q4_K: jkb.gemv_q4_k_q8_k, Q6_K: jkb.gemv_q6_k_q8_k}
-    rvv = {Q4_K: jkb.vec_dot_q4_k_m_rvv, Q6_K: jkb.vec_dot_q6_k_rvv}
     groups = {}  # activation stream -> matrices fed by it, in DECODE_8B order
     for name, quant, per, cols, s, copies in shards:
         groups.setdefault(s, []).append((name, quant, copies))
 
-    def run_group(s, copy):
+    def run_group(s, i):
         """The matrices sharing activation s: one f32-input launch (grouped when several)."""
-        items = [(outs.local_slice(n), weights[(n, copy % c)]) for n, _, c in groups[s]]
-        if len(items) == 1:
-            rvv[groups[s][0][1]](items[0][0], items[0][1], xs[s])
-        else:
-            jkb.vec_dot_grouped_rvv(items, xs[s])
+        items = [(lslice(n, i), weights[(n, i % c)]) for n, _, c in groups[s]]
+        jkb.vec_dot_grouped_rvv(items, xs[s])
 
-    def layer_part(copy):
+    def layer_part(i):
         if not args.unfused:
             for s in ("x", "attn", "h", "a"):
-                run_group(s, copy)
+                run_group(s, i)
             return
         for s in ACTS:
             jkb.quantize_row_q8_k(xs[s], xq[s])
         for name, quant, per, cols, s, copies in shards:
             if name == "lm_head":
                 continue
-            fns[quant](outs.local_slice(name), weights[(name, copy)], xq[s])
+            jkb.gemv_rows(lslice(name, i), weights[(name, i % copies)], xq[s], range(0, per))
 
-    def lm_head():
+    def lm_head(i):
         if not args.unfused:
-            run_group("f", 0)
+            run_group("f", i)
             return
-        fns[Q6_K](outs.local_slice("lm_head"), weights[("lm_head", 0)], xq["f"])
+        jkb.gemv_rows(lslice("lm_head", i), weights[("lm_head", 0)], xq["f"],
+                      range(0, shards[-1][2]))
+
+    def collect(i):
+        if peer:
+            outs.gather(i % 2)
+        else:
+            outs.gather()
 
     def step(i, evs=None):
-        layer_part(i % LAYER_COPIES)
+        layer_part(i)
         if evs is not None:
             evs[0].record(stream)
-        lm_head()
+        lm_head(i)
         if evs is not None:
             evs[1].record(stream)
-        outs.gather()
+        collect(i)
 
     for i in range(args.warmup):  # eager warm-up (also sets kernel attributes)
         step(i)
@@ -433,23 +441,18 @@ def run_gpu(args):
 
     # --- e2e: the public API with host buffers (pinned f32 inputs in, f32 outputs out)
     host_in = {s: xs[s].cpu().pin_memory() for s in ACTS}
-    host_out = torch.empty(outs.gathered.numel(), dtype=torch.float32).pin_memory()
+    full = (lambda i: outs.full(i % 2)) if peer else (lambda i: outs.gathered)
+    host_out = torch.empty(full(0).numel(), dtype=torch.float32).pin_memory()
     h2d = sum(v.numel() * 4 for v in host_in.values())
-    d2h = outs.gathered.numel() * 4
+    d2h = full(0).numel() * 4
 
     def e2e_step(i):
         for s in ACTS:
             xs[s].copy_(host_in[s], non_blocking=True)
-        if not args.unfused:
-            for s in ("x", "attn", "h", "a", "f"):
-                run_group(s, i)
-        else:
-            for s in ACTS:
-                jkb.quantize_row_q8_k(xs[s], xq[s])
-            for name, quant, per, cols, s, copies in shards:
-                fns[quant](outs.local_slice(name), weights[(name, i % copies)], xq[s])
-        outs.gather()
-        host_out.copy_(outs.gathered, non_blocking=True)
+        layer_part(i)
+        lm_head(i)
+        collect(i)
+        host_out.copy_(full(i), non_blocking=True)
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -487,7 +490,10 @@ def run_gpu(args):
                        "bytes_per_step": total_bytes,
                        "l2": "inputs larger than L2 (554 MB per step, layer weights in 2 "
                              "alternating copies)",
-                       "parallelism": f"row-shard x{world}" + (" + NCCL all-gather" if world > 1 else "")},
+                       "parallelism": f"row-shard x{world}" + (
+                           "" if world == 1 else
+                           " + one-kernel all-gather over NVLink peer memory" if peer
+                           else " + NCCL all-gather")},
             "roofline": {"bound": "hbm",
                          "kernel": ("gemv_kernel<FQ6_K, ActQ8K>" if args.unfused else
                                     "gemv_kernel<FQ6_K, ActQ8KF32>") + " lm_head 4096->128256",
@@ -495,8 +501,8 @@ def run_gpu(args):
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": traffic, "algorithmic_bytes": lm_bytes,
                          "avg_ms": round(lm_ms, 5)},
-            "gpu_launches": args.steps * (len(ACTS) + len(DECODE_8B) if args.unfused
-                                          else len(groups)),
+            "gpu_launches": args.steps * ((len(ACTS) + len(DECODE_8B) if args.unfused
+                                           else len(groups)) + (1 if peer else 0)),
             "clocks": clocks,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
@@ -507,6 +513,11 @@ def run_gpu(args):
             res["cpu_baseline"] = cpu_baseline_single()
         print(json.dumps(res), flush=True)
     del graph, graph_ev
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()  # no rank still writes into a peer's buffer past this point
+    if peer:
+        outs.destroy()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -701,6 +712,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="jkb", choices=["jkb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--collective", choices=["peer", "nccl"], default="peer",
+                    help="N > 1: collect the output-row shards with this library's one-kernel "
+                         "all-gather over NVLink peer memory (peer) or one NCCL all-gather per "
+                         "step (nccl)")
     ap.add_argument("--no-gemm", action="store_true",
                     help="leave out the prefill GEMM section (BASELINE configs[2])")
     ap.add_argument("--m", type=int, default=2048, help="tokens of --kernel gemm_q8_0 / int8_peak")

@@ -107,9 +107,10 @@ int jkb_abi_version(void);
 const char *jkb_last_error(void);
 int jkb_last_error_info(jkb_error_info *out);
 void jkb_clear_error(void);
-/* No reference counterpart: the device error word of the tensor-core GEMM (bit 0: one of its
- * bounded waits expired, so the call's output is not valid). Synchronizes `stream`, copies the
- * word to *flags, clears it, and returns JKB_E_TIMEOUT when it was non-zero, JKB_OK otherwise. */
+/* No reference counterpart: the device error word of the kernels with bounded waits (bit 0: a
+ * wait in the tensor-core GEMM expired, so that call's output is not valid; bit 1: a peer-group
+ * wait expired). Synchronizes `stream`, copies the word to *flags, clears it, and returns
+ * JKB_E_TIMEOUT when it was non-zero, JKB_OK otherwise. */
 int jkb_device_status(int32_t *flags, void *stream);
 /* No reference counterpart: the f32 epilogue of the tensor-core repacked GEMM (32-element
  * scale groups, batches of at least 32 tokens). 0 (the default): acc = fma((f32)c, xs * ws, acc)
@@ -334,6 +335,39 @@ int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight 
  * writes every scratch value it reads, so results never depend on an earlier call. */
 int jkb_gemm_repacked_f32_noalloc(float *out, size_t out_len, const jkb_repacked_weight *w,
                                   const float *input, size_t in_len, size_t m, void *stream);
+
+/* ---- multi-GPU output-row sharding: a one-kernel all-gather over NVLink (no reference
+ * counterpart; the reference splits work by row ranges, gemv_repacked_rows repack.rs:4014) ----
+ * One process per GPU. Every rank creates a peer group holding a device buffer of `bytes`, the
+ * ranks exchange the group handles (JKB_PEER_HANDLE_BYTES each, over any host channel) and
+ * open them (CUDA IPC: each rank maps every peer's buffer). Each rank computes its output-row
+ * shards into its own buffer at their global offsets (the buffer holds the full output
+ * vectors); jkb_peer_group_allgather then pushes this rank's chunks to the same offsets in every
+ * peer's buffer with coalesced stores over NVLink, signals each peer, and makes `stream` wait
+ * until every peer's push of the same call has arrived -- one kernel launch. Afterwards every
+ * rank holds the full vectors. All ranks call it with their own chunks in the same order. The
+ * arrival count lives on the device, so a captured CUDA graph replays correctly. Waits are
+ * bounded (about 2 s): on expiry bit 1 of the device error word (jkb_device_status) is set and
+ * the kernel returns; the group is then out of step and must be recreated. A chunk must not be
+ * rewritten before every rank has finished reading it: callers alternate two output slots by
+ * step parity (a rank cannot start step s + 2 before every rank has pushed step s + 1, which
+ * comes after its reads of step s). */
+#define JKB_PEER_HANDLE_BYTES 64
+#define JKB_PEER_MAX_RANKS 8
+#define JKB_PEER_MAX_CHUNKS 16
+typedef struct jkb_peer_group jkb_peer_group;
+int jkb_peer_group_create(int world, int rank, size_t bytes, jkb_peer_group **out);
+int jkb_peer_group_handle(const jkb_peer_group *pg, void *handle);
+/* handles: world * JKB_PEER_HANDLE_BYTES bytes, rank-ordered (this rank's own entry ignored) */
+int jkb_peer_group_open(jkb_peer_group *pg, const void *handles);
+int jkb_peer_group_buffer(const jkb_peer_group *pg, void **local, size_t *bytes);
+/* chunks: n byte ranges [offset[i], offset[i] + len[i]) of the buffer (16-byte multiples) */
+int jkb_peer_group_allgather(jkb_peer_group *pg, const size_t *offset, const size_t *len,
+                             size_t n, void *stream);
+/* Low-level: make `stream` wait until `arrivals` more peer signals have reached this rank than
+ * at its previous wait (each allgather delivers one per pushing CTA of every peer). */
+int jkb_peer_group_wait(jkb_peer_group *pg, uint64_t arrivals, void *stream);
+int jkb_peer_group_destroy(jkb_peer_group *pg);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

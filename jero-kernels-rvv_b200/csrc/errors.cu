@@ -156,11 +156,48 @@ int validate_weight_call(const char *fn, const jkb_weight *w, int expected_quant
     return JKB_OK;
 }
 
+// Device error word shared by the kernels with bounded waits: bit 0, a wait in the tensor-core
+// GEMM expired; bit 1, a peer-group wait (peer.cu) expired. Kernels get its address as an
+// argument; host code reads and clears it in jkb_device_status.
+__device__ int g_device_error;
+
+int *device_error_word() {
+    static int *ptr_by_device[128] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
+    if (!ptr_by_device[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+        ptr_by_device[dev] = (int *)p;
+    }
+    return ptr_by_device[dev];
+}
+
 }  // namespace jkb
 
 extern "C" {
 
 int jkb_abi_version(void) { return JKB_ABI_VERSION; }
+
+int jkb_device_status(int32_t *flags, void *stream) {
+    using namespace jkb;
+    if (!flags) return fail(JKB_E_INVALID, "device_status", 0, 0, 0, "null pointer");
+    int *err = device_error_word();
+    if (!err) return fail(JKB_E_CUDA, "device_status", 0, 0, 0, "no device error word");
+    int v = 0;
+    cudaStream_t st = as_stream(stream);
+    cudaError_t e = cudaMemcpyAsync(&v, err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess && v) e = cudaMemsetAsync(err, 0, sizeof(int), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail_cuda(e, "device_status");
+    *flags = v;
+    return v ? fail(JKB_E_TIMEOUT, "device_status", 0, 0, 0,
+                    "a bounded wait expired on the device (flags %d: bit 0 tensor-core GEMM, "
+                    "bit 1 peer-group wait)",
+                    v)
+             : JKB_OK;
+}
 
 const char *jkb_last_error(void) {
     using namespace jkb;

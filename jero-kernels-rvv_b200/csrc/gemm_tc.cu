@@ -459,20 +459,6 @@ __global__ void __launch_bounds__(C::THREADS, 1)
 
 // ---------------------------------------------------------------- host side
 
-__device__ int g_tc_error;  // device error word of this kernel (bit 0: a bounded wait expired)
-
-int *tc_error_word() {
-    static int *ptr_by_device[128] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
-    if (!ptr_by_device[dev]) {
-        void *p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_tc_error) != cudaSuccess) return nullptr;
-        ptr_by_device[dev] = (int *)p;
-    }
-    return ptr_by_device[dev];
-}
-
 // cuTensorMapEncodeTiled, resolved through the runtime's driver entry point so that the library
 // does not link the driver library (it still loads on machines without a GPU driver).
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -604,7 +590,7 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
     if ((((uintptr_t)w->q) & 15) || (((uintptr_t)act->q) & 15) || (((uintptr_t)w->scales) & 15) ||
         (((uintptr_t)act->x_scales_t) & 15) || (act->xt_pitch & 31))
         return JKB_OK;
-    int *err = tc_error_word();
+    int *err = device_error_word();
     if (!err) return JKB_OK;
     *used = true;
     const int bn = choose_tile(act->m, row_end - row_begin);
@@ -614,24 +600,6 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
 }
 
 }  // namespace jkb
-
-extern "C" int jkb_device_status(int32_t *flags, void *stream) {
-    using namespace jkb;
-    if (!flags) return fail(JKB_E_INVALID, "device_status", 0, 0, 0, "null pointer");
-    int *err = tc_error_word();
-    if (!err) return fail(JKB_E_CUDA, "device_status", 0, 0, 0, "no device error word");
-    int v = 0;
-    cudaStream_t st = as_stream(stream);
-    cudaError_t e = cudaMemcpyAsync(&v, err, sizeof(int), cudaMemcpyDeviceToHost, st);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-    if (e == cudaSuccess && v) e = cudaMemsetAsync(err, 0, sizeof(int), st);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-    if (e != cudaSuccess) return fail_cuda(e, "device_status");
-    *flags = v;
-    return v ? fail(JKB_E_TIMEOUT, "device_status", 0, 0, 0,
-                    "a bounded wait in a tensor-core GEMM expired (flags %d)", v)
-             : JKB_OK;
-}
 
 extern "C" int jkb_gemm_set_exact(int exact) {
     jkb::g_gemm_exact.store(exact ? 1 : 0, std::memory_order_relaxed);

@@ -20,6 +20,8 @@ int fail_cuda(cudaError_t e, const char *where);
 // Rejects a device pointer that is not `align`-byte aligned (JKB_E_BOUNDS). Block activations
 // carry an f32 field (align 4, like the reference #[repr(C)] structs); outputs are f32.
 int check_align(const void *p, size_t align, const char *fn, const char *what);
+// The device error word of kernels with bounded waits (per-device address; nullptr on failure).
+int *device_error_word();
 // Checks cudaGetLastError after a launch.
 int check_launch(const char *where);
 void clear_error();
@@ -183,5 +185,6 @@ struct GemvLaunch {
     float *dbg_val;
 };
 int launch_gemv(const GemvLaunch &L, cudaStream_t st);
+
 
 }  // namespace jkb

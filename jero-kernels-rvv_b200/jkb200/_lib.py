@@ -100,6 +100,13 @@ SIGNATURES = {
     "jkb_vec_dot_q8_0_rvv": [P, S, P, P, S, P],
     "jkb_vec_dot_q4_0_rvv": [P, S, P, P, S, P],
     "jkb_vec_dot_grouped_rvv": [C.POINTER(jkb_vec_dot_item), S, P, S, P],
+    "jkb_peer_group_create": [I, I, S, PP],
+    "jkb_peer_group_handle": [P, P],
+    "jkb_peer_group_open": [P, P],
+    "jkb_peer_group_buffer": [P, PP, PS],
+    "jkb_peer_group_allgather": [P, PS, PS, S, P],
+    "jkb_peer_group_wait": [P, C.c_uint64, P],
+    "jkb_peer_group_destroy": [P],
     "jkb_bitlinear_i8": [P, S, P, P, S, F, P],
     "jkb_bitlinear_i8_rvv": [P, S, P, P, S, F, P],
     "jkb_bitlinear_i8_ime": [P, S, P, P, S, F, P],

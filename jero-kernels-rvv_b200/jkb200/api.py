@@ -30,7 +30,7 @@ __all__ = [
     "bitlinear_i8_batch", "gemm_repacked", "gemm_repacked_rows", "gemv_repacked",
     "gemv_repacked_rows", "gemm_repacked_f32", "gemm_repacked_f32_noalloc",
     "empty_q8_0_blocks", "empty_q8_k_blocks", "device_status", "gemm_set_exact", "gemm_get_exact",
-    "gemm_exact",
+    "gemm_exact", "PeerGroup",
     "device_view",
 ]
 
@@ -595,6 +595,62 @@ def vec_dot_grouped_rvv(items, x, stream=None):
         arr[i].out_len = out.numel()
         arr[i].w = w.handle
     _check(_L().jkb_vec_dot_grouped_rvv(arr, len(items), _dptr(x), x.numel(), _stream(stream)))
+
+
+class PeerGroup:
+    """A rank's peer group (one process per GPU): a device buffer of `nbytes` with the same
+    layout on every rank, whose chunks allgather() copies from each rank to all the others over
+    NVLink in one kernel. Created collectively: every rank of the default process group (or
+    `group`) calls PeerGroup(nbytes); the CUDA IPC handles travel over torch.distributed."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, nbytes: int, world: int = None, rank: int = None, group=None):
+        import torch.distributed as dist
+
+        if world is None:
+            world = dist.get_world_size(group) if dist.is_initialized() else 1
+            rank = dist.get_rank(group) if dist.is_initialized() else 0
+        h = C.c_void_p()
+        _check(_L().jkb_peer_group_create(world, rank, nbytes, C.byref(h)))
+        self.handle, self.world, self.rank = h, world, rank
+        if world > 1:
+            mine = (C.c_uint8 * self.HANDLE_BYTES)()
+            _check(_L().jkb_peer_group_handle(h, mine))
+            allh = [None] * world
+            dist.all_gather_object(allh, bytes(mine), group=group)
+            buf = (C.c_uint8 * (self.HANDLE_BYTES * world)).from_buffer_copy(b"".join(allh))
+            _check(_L().jkb_peer_group_open(h, buf))
+        ptr, n = C.c_void_p(), C.c_size_t()
+        _check(_L().jkb_peer_group_buffer(h, C.byref(ptr), C.byref(n)))
+        self.buffer = device_view(ptr.value, (n.value // 4,), "<f4")
+
+    def allgather(self, chunks, stream=None):
+        """Copy this rank's `chunks` ((byte offset, byte length) pairs of the buffer) to the same
+        offsets on every peer and make the stream wait until every peer's chunks of the same call
+        have arrived (bounded: on expiry bit 1 of device_status())."""
+        self.allgather_arrays(self.chunk_arrays(chunks), stream)
+
+    @staticmethod
+    def chunk_arrays(chunks):
+        """The ctypes arrays allgather_arrays() takes (built once for a fixed chunk list)."""
+        n = len(chunks)
+        offs = (C.c_size_t * max(1, n))(*[c[0] for c in chunks])
+        lens = (C.c_size_t * max(1, n))(*[c[1] for c in chunks])
+        return offs, lens, n
+
+    def allgather_arrays(self, arrays, stream=None):
+        offs, lens, n = arrays
+        _check(_L().jkb_peer_group_allgather(self.handle, offs, lens, n, _stream(stream)))
+
+    def wait(self, arrivals: int, stream=None):
+        """Low level: make the stream wait for `arrivals` more peer signals (bounded)."""
+        _check(_L().jkb_peer_group_wait(self.handle, arrivals, _stream(stream)))
+
+    def destroy(self):
+        if getattr(self, "handle", None):
+            _L().jkb_peer_group_destroy(self.handle)
+            self.handle = None
 
 
 # ------------------------------------------------------------------------------- BitLinear

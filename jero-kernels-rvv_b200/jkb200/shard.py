@@ -10,8 +10,18 @@ need an all-reduce and change the f32 summation order.
 Layout of one rank's flat output buffer: the matrices in order, each contributing its slice,
 padded to the largest rank's total so that ``all_gather_into_tensor`` sees equal sizes.
 
-Failures of the collective (a peer that died or never joins, a process-group timeout) surface
-as ``CollectiveError`` on the host; every rank takes the same collective steps in the same order.
+Two ways to collect the slices:
+* ``ShardedOutputs``: each rank computes into a flat local buffer, one NCCL all-gather per step
+  collects them, and ``output()`` reassembles a full vector. Failures of the collective (a peer
+  that died or never joins, a process-group timeout) surface as ``CollectiveError``.
+* ``PeerOutputs``: every rank holds the full output vectors in a peer-group buffer (the same
+  layout on every rank) and computes its rows straight into their global positions; one kernel
+  per step (jkb_peer_group_allgather) copies them to every peer over NVLink and waits for the
+  peers' rows. The full vectors are then in place on every rank, in one of two slots alternated
+  by step parity (a fast rank never overwrites rows a slow rank is still reading: it cannot start
+  step s + 2 before every rank has finished step s). A wait that expires sets bit 1 of
+  jkb200.device_status().
+Every rank takes the same collective steps in the same order.
 """
 from __future__ import annotations
 
@@ -20,7 +30,7 @@ from dataclasses import dataclass
 import torch
 import torch.distributed as dist
 
-__all__ = ["shard_rows", "ShardedOutputs", "CollectiveError"]
+__all__ = ["shard_rows", "ShardedOutputs", "PeerOutputs", "CollectiveError"]
 
 
 class CollectiveError(RuntimeError):
@@ -94,3 +104,60 @@ class ShardedOutputs:
                                r * self.local_len + m.offs[r] + len(m.slices[r])]
                  for r in range(self.world)]
         return torch.cat(parts)
+
+
+class PeerOutputs:
+    """Full output vectors of a list of (name, rows) matrices in a peer-group buffer on every
+    rank: rank p computes rows shard_rows(rows, world, p) of each into ``local_slice(name,
+    slot)``; after ``gather(slot)`` every rank holds all rows of every matrix in
+    ``output(name, slot)``."""
+
+    SLOTS = 2
+
+    def __init__(self, mats, world: int, rank: int, group=None):
+        from .api import PeerGroup
+
+        self.world, self.rank = world, rank
+        self.offs, self.rows = {}, {}
+        total = 0
+        for name, rows in mats:
+            self.offs[name], self.rows[name] = total, rows
+            total += rows
+        self.total = total
+        self.pitch = (total + 3) // 4 * 4  # floats per slot (16-byte multiple)
+        self.group = PeerGroup(self.SLOTS * self.pitch * 4, world, rank, group)
+        self.slots = self.group.buffer[:self.SLOTS * self.pitch].view(self.SLOTS, self.pitch)
+
+    def rows_of(self, name: str) -> range:
+        return shard_rows(self.rows[name], self.world, self.rank)
+
+    def local_slice(self, name: str, slot: int) -> torch.Tensor:
+        rr = self.rows_of(name)
+        o = self.offs[name]
+        return self.slots[slot, o + rr.start:o + rr.stop]
+
+    def output(self, name: str, slot: int) -> torch.Tensor:
+        o = self.offs[name]
+        return self.slots[slot, o:o + self.rows[name]]
+
+    def full(self, slot: int) -> torch.Tensor:
+        """All matrices' outputs of a slot, in list order."""
+        return self.slots[slot, :self.total]
+
+    def chunks(self, slot: int):
+        """(byte offset, byte length) of this rank's rows of every matrix in a slot."""
+        out = []
+        for name in self.offs:
+            rr = self.rows_of(name)
+            if len(rr):
+                out.append((4 * (slot * self.pitch + self.offs[name] + rr.start), 4 * len(rr)))
+        return out
+
+    def gather(self, slot: int, stream=None):
+        """One kernel: this rank's rows of the slot to every peer, then wait for theirs."""
+        if not hasattr(self, "_chunks"):
+            self._chunks = [self.group.chunk_arrays(self.chunks(s)) for s in range(self.SLOTS)]
+        self.group.allgather_arrays(self._chunks[slot], stream)
+
+    def destroy(self):
+        self.group.destroy()

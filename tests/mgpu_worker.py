@@ -6,7 +6,10 @@ uploads only its output-row shard (jkb200.shard.shard_rows), computes it with th
 as a single-GPU call, and one NCCL all-gather collects the slices. Rank 0 also holds the full
 matrices and checks that the reassembled outputs equal the single-GPU results bit for bit: rows
 are independent, so sharding by rows changes no arithmetic (gemv_repacked_rows, repack.rs:4014).
-Prints one JSON line per rank and exits non-zero on a mismatch.
+The same shapes then go through the library's one-kernel all-gather (jkb200.shard.PeerOutputs:
+every rank pushes its rows into every peer's buffer over NVLink): over three steps alternating
+the two output slots, every rank's full outputs must equal its own single-GPU results bit for
+bit. Prints one JSON line per rank and exits non-zero on a mismatch.
 """
 import json
 import os
@@ -22,7 +25,7 @@ sys.path.insert(0, ROOT)
 
 import bench  # noqa: E402  (seeded synthetic GGUF matrices)
 import jkb200 as jkb  # noqa: E402
-from jkb200.shard import ShardedOutputs, shard_rows  # noqa: E402
+from jkb200.shard import PeerOutputs, ShardedOutputs, shard_rows  # noqa: E402
 
 Q4_K, Q6_K, Q8_0 = 12, 14, 8
 MATS = [("ffn_gate", Q4_K, 28672, 8192, "h"), ("ffn_down", Q4_K, 8192, 28672, "a"),
@@ -90,6 +93,47 @@ def main():
         res["prefill_gemm"] = "bit-exact" if same else "MISMATCH"
         ok &= same
         res["device_status"] = jkb.device_status()
+    # the library's one-kernel all-gather over NVLink: every rank computes its rows into their
+    # global positions and pushes them to every peer; three steps alternate the two slots with
+    # fresh inputs, and after each every rank checks all rows against its own single-GPU
+    # computation of the full matrices
+    torch.cuda.synchronize()
+    dist.barrier()
+    pouts = PeerOutputs([(nm, r) for nm, _, r, _, _ in MATS], world, rank)
+    shard_w, full_w = {}, {}
+    for i, (name, quant, rows, cols, s) in enumerate(MATS):
+        rr = pouts.rows_of(name)
+        raw = bench.synth_matrix(quant, rows, cols, 700 + i)
+        row_bytes = raw.size // rows
+        shard_w[name] = jkb.Weight(jkb.TensorView(name, quant, [len(rr), cols],
+                                                  raw[rr.start * row_bytes:rr.stop * row_bytes]),
+                                   len(rr), cols)
+        full_w[name] = jkb.Weight(jkb.TensorView(name, quant, [rows, cols], raw), rows, cols)
+    peer_ok = True
+    for step in range(3):
+        slot = step % 2
+        gs = torch.Generator().manual_seed(100 + step)
+        xq_s = {}
+        for s_, n_ in ACTS.items():
+            xq_s[s_] = jkb.empty_q8_k_blocks(n_ // 256)
+            jkb.quantize_row_q8_k(torch.randn(n_, generator=gs).cuda(), xq_s[s_])
+        for name, quant, rows, cols, s in MATS:
+            jkb.gemv_rows(pouts.local_slice(name, slot), shard_w[name], xq_s[s],
+                          range(0, len(pouts.rows_of(name))))
+        pouts.gather(slot)
+        for name, quant, rows, cols, s in MATS:
+            ref = torch.empty(rows, dtype=torch.float32, device="cuda")
+            jkb.gemv_rows(ref, full_w[name], xq_s[s], range(0, rows))
+            peer_ok &= torch.equal(pouts.output(name, slot).view(torch.int32),
+                                   ref.view(torch.int32))
+        torch.cuda.synchronize()
+    res["peer_allgather"] = "bit-exact" if peer_ok else "MISMATCH"
+    res["peer_status"] = jkb.device_status()
+    ok &= peer_ok and res["peer_status"] == 0
+    torch.cuda.synchronize()
+    dist.barrier()  # no rank still writes into a peer's buffer
+    pouts.destroy()
+
     res["ok"] = bool(ok)
     print(json.dumps(res), flush=True)
     dist.barrier()

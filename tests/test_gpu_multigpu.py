@@ -1,7 +1,9 @@
 """Multi-GPU parity of the row-sharded path (Llama-3-70B shapes): launches
 tests/mgpu_worker.py under torchrun on every visible GPU (at most 8) and checks that each rank
 reports bit-exact reassembled outputs (Q4_K_M 8192 -> 28672 and 28672 -> 8192, Q6_K
-8192 -> 128256 GEMVs and a Q8_0 prefill GEMM, each against the single-GPU call on rank 0).
+8192 -> 128256 GEMVs and a Q8_0 prefill GEMM, each against the single-GPU call on rank 0),
+both with the NCCL all-gather and with the library's one-kernel all-gather over NVLink peer
+memory (checked on every rank).
 Needs at least 2 GPUs; with one GPU the sharded host logic is covered by test_shard_gloo.py."""
 import json
 import os
@@ -32,3 +34,5 @@ def test_row_sharded_outputs_match_single_gpu():
     for key in ("ffn_gate", "ffn_down", "lm_head", "prefill_gemm"):
         assert r0[key] == "bit-exact", r0
     assert r0["device_status"] == 0
+    for r in lines:  # the NVLink all-gather kernel: every rank holds every row
+        assert r["peer_allgather"] == "bit-exact" and r["peer_status"] == 0, r
