@@ -4,11 +4,12 @@
 Default workload: the Llama-3-8B decode GEMV set at batch 1 --
 Q4_K_M q/o 4096->4096, k/v 4096->1024, gate/up 4096->14336, down 14336->4096 and the Q6_K
 lm_head 4096->128256, each fed by its own Q8_K-quantized activation. One step quantizes the
-five f32 activation vectors to Q8_K and runs the eight GEMVs through the C ABI (jkb200): by
-default with the f32-input entries (vec_dot_q4_k_m_rvv / vec_dot_q6_k_rvv, the quantization
-inside the GEMV launch), the matrices that share an input in one grouped launch -- q/k/v,
-o, gate/up, down, lm_head: 5 launches -- as a decoder layer allows; with --unfused as five
-quantize launches plus eight GEMV launches. Weights are synthetic N(0, 0.02) rows quantized
+five f32 activation vectors to Q8_K and runs the eight GEMVs through the C ABI (jkb200): the
+layer matrices with the f32-input entries (vec_dot_q4_k_m_rvv, the quantization inside the
+GEMV launch), the matrices that share an input in one grouped launch -- q/k/v, o, gate/up,
+down -- as a decoder layer allows, and the lm_head as quantize_row_q8_k + gemv_q6_k_q8_k
+(--prequant picks which inputs get their own quantize launch; measured best: the lm_head's);
+with --unfused as five quantize launches plus eight GEMV launches. Weights are synthetic N(0, 0.02) rows quantized
 by this file's numpy quantizers (a seeded pool of rows tiled to full size; GEMV time does not
 depend on the values), activations N(0, 1).
 
@@ -342,8 +343,17 @@ def run_gpu(args):
     for name, quant, per, cols, s, copies in shards:
         groups.setdefault(s, []).append((name, quant, copies))
 
+    prequant = set(args.prequant.split(",")) - {""}
+
     def run_group(s, i):
-        """The matrices sharing activation s: one f32-input launch (grouped when several)."""
+        """The matrices sharing activation s: one f32-input launch (grouped when several), or,
+        for the streams in --prequant, quantize_row_q8_k followed by gemv_*_q8_k per matrix."""
+        if s in prequant:
+            jkb.quantize_row_q8_k(xs[s], xq[s])
+            for n, _, c in groups[s]:
+                w = weights[(n, i % c)]
+                jkb.gemv_rows(lslice(n, i), w, xq[s], range(0, w.rows))
+            return
         items = [(lslice(n, i), weights[(n, i % c)]) for n, _, c in groups[s]]
         jkb.vec_dot_grouped_rvv(items, xs[s])
 
@@ -495,14 +505,15 @@ def run_gpu(args):
                            " + one-kernel all-gather over NVLink peer memory" if peer
                            else " + NCCL all-gather")},
             "roofline": {"bound": "hbm",
-                         "kernel": ("gemv_kernel<FQ6_K, ActQ8K>" if args.unfused else
-                                    "gemv_kernel<FQ6_K, ActQ8KF32>") + " lm_head 4096->128256",
+                         "kernel": ("gemv_kernel<FQ6_K, ActQ8K>" if args.unfused or "f" in prequant
+                                    else "gemv_kernel<FQ6_K, ActQ8KF32>") + " lm_head 4096->128256",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": traffic, "algorithmic_bytes": lm_bytes,
                          "avg_ms": round(lm_ms, 5)},
             "gpu_launches": args.steps * ((len(ACTS) + len(DECODE_8B) if args.unfused
-                                           else len(groups)) + (1 if peer else 0)),
+                                           else len(groups) + sum(len(groups[s]) for s in prequant))
+                                          + (1 if peer else 0)),
             "clocks": clocks,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
@@ -716,6 +727,10 @@ def main():
                     help="N > 1: collect the output-row shards with this library's one-kernel "
                          "all-gather over NVLink peer memory (peer) or one NCCL all-gather per "
                          "step (nccl)")
+    ap.add_argument("--prequant", default="f",
+                    help="comma list of activation streams (x, attn, h, a, f) quantized by their "
+                         "own quantize_row_q8_k launch ahead of pre-quantized GEMVs instead of "
+                         "inside the f32-input GEMV launch (default: f, the lm_head input)")
     ap.add_argument("--no-gemm", action="store_true",
                     help="leave out the prefill GEMM section (BASELINE configs[2])")
     ap.add_argument("--m", type=int, default=2048, help="tokens of --kernel gemm_q8_0 / int8_peak")
