@@ -325,7 +325,7 @@ int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight 
  * that cannot allocate device memory, and so cannot create the jkb_act_q8 scratch handle. Two
  * examples: an engine that reserved all remaining HBM for its KV cache at start-up, and a host
  * whose per-token loop forbids cudaMalloc because it may synchronize the device and stall the
- * pipeline. The quantized activations go to a scratch array built into the library (3.75 MiB
+ * pipeline. The quantized activations go to a scratch array built into the library (4.25 MiB
  * of device memory on every GPU that loads it, held until exit). The batch must satisfy
  * m * round_up(cols, 32) <= 2097152 elements (e.g. 512 tokens x 4096); larger batches fail
  * with JKB_E_BOUNDS. The call allocates nothing. The first call on each device looks up the

@@ -149,18 +149,18 @@ static int gemm_rows(const char *fn, float *out, size_t out_len, const jkb_repac
 // Scratch of jkb_gemm_repacked_f32_noalloc: the quantized activation batch lives in this
 // file-scope device array instead of a caller-created jkb_act_q8. It holds batches with
 // m * k_padded <= NOALLOC_MAX_ELEMS (2^21, e.g. 512 tokens x 4096). Every GPU that loads the
-// library keeps these 3.75 MiB until process exit, and all calls share them.
+// library keeps these 4.25 MiB until process exit, and all calls share them.
 constexpr size_t NOALLOC_MAX_ELEMS = size_t(1) << 21;
 constexpr size_t NOALLOC_Q_BYTES = NOALLOC_MAX_ELEMS;             // i8 values [m][k_pad]
 constexpr size_t NOALLOC_G32_BYTES = NOALLOC_MAX_ELEMS / 32 * 4;  // f32 per 32 elements
 constexpr size_t NOALLOC_G16_BYTES = NOALLOC_MAX_ELEMS / 16 * 4;  // f32 per 16 elements
 // regions, each 256-byte aligned: q | x_scales | x_sums | x_sums_16 | super_scales |
-// x_scales_t (super_scales needs m * ceil(k/256) <= m * k_pad / 32 floats; x_scales_t needs
-// k_pad / 32 * round_up(m, 32) floats, under 2x x_scales when m >= 32, the smallest batch the
-// tensor-core GEMM that reads it takes)
+// x_scales_t | x_nsums_t (super_scales needs m * ceil(k/256) <= m * k_pad / 32 floats; the two
+// transposed planes need k_pad / 32 * round_up(m, 32) floats each, under 2x x_scales when
+// m >= 32, the smallest batch the tensor-core GEMM that reads them takes)
 constexpr size_t NOALLOC_XT_BYTES = 2 * NOALLOC_G32_BYTES;
 constexpr size_t NOALLOC_BYTES =
-    NOALLOC_Q_BYTES + 3 * NOALLOC_G32_BYTES + NOALLOC_G16_BYTES + NOALLOC_XT_BYTES;
+    NOALLOC_Q_BYTES + 3 * NOALLOC_G32_BYTES + NOALLOC_G16_BYTES + 2 * NOALLOC_XT_BYTES;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_BYTES];
 
 // Host code cannot use g_noalloc_scratch's name as a device address; the address comes from
@@ -233,10 +233,10 @@ int jkb_gemm_repacked_f32_noalloc(float *out, size_t out_len, const jkb_repacked
     view.super_scales = reinterpret_cast<float *>(s + NOALLOC_Q_BYTES + 2 * NOALLOC_G32_BYTES +
                                                   NOALLOC_G16_BYTES);
     view.xt_pitch = (m + 31) / 32 * 32;
-    view.x_scales_t = kp / 32 * view.xt_pitch * 4 <= NOALLOC_XT_BYTES
-                          ? reinterpret_cast<float *>(s + NOALLOC_Q_BYTES + 3 * NOALLOC_G32_BYTES +
-                                                      NOALLOC_G16_BYTES)
-                          : nullptr;
+    const bool fits = kp / 32 * view.xt_pitch * 4 <= NOALLOC_XT_BYTES;
+    uint8_t *xt = s + NOALLOC_Q_BYTES + 3 * NOALLOC_G32_BYTES + NOALLOC_G16_BYTES;
+    view.x_scales_t = fits ? reinterpret_cast<float *>(xt) : nullptr;
+    view.x_nsums_t = fits ? reinterpret_cast<float *>(xt + NOALLOC_XT_BYTES) : nullptr;
     rc = jkb_act_q8_quantize(&view, input, in_len, m, w->cols, stream);
     if (rc) return rc;
     return gemm_rows("gemm_repacked_f32_noalloc", out, out_len, w, &view, 0, w->rows, false,

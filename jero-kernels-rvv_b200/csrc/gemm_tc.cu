@@ -1,12 +1,14 @@
-// tcgen05 tensor-core path of the repacked block-scaled GEMM for 32-element scale groups without
-// mins (Q8_0 / Q4_0 / TQ2_0 / I2_S weights). Per output (m, n), as in
+// tcgen05 tensor-core path of the repacked block-scaled GEMM for 32-element scale groups (Q8_0 /
+// Q4_0 / TQ2_0 / I2_S weights, and Q4_K_M with its min terms). Per output (m, n), as in
 // accumulate_scaled_tile_scalar (repack.rs:3045-3093):
-//     acc = 0; for g in K order: acc += (f32)c_g * (xs[m][g] * ws[n][g]),  c_g = sum_{k in g} xq*wq
-// The integer group sums c_g are exact (int8 MMA into int32). Two epilogues:
-//   EXACT = true   the reference's roundings: p = (f32)c * (xs*ws) rounded, then acc + p rounded,
-//                  so every output is bit-identical to the scalar reference;
-//   EXACT = false  acc = fma((f32)c, xs*ws, acc): one rounding fewer per group, each output within
-//                  one rounding of |c*xs*ws| per group of the reference (far inside 1e-5 relative).
+//     acc = 0; for g in K order: acc += (f32)c_g * (xs[m][g] * ws[n][g]) [- xsum[m][g] * wm[n][g]]
+// with c_g = sum_{k in g} xq*wq. The integer group sums c_g are exact (int8 MMA into int32). Two
+// epilogues:
+//   EXACT = true   the reference's roundings: p = (f32)c * (xs*ws) rounded, [p - xsum*wm rounded,]
+//                  then acc + p rounded, so every output is bit-identical to the scalar reference;
+//   EXACT = false  acc = fma((f32)c, xs*ws, acc) [then fma(-xsum, wm, acc)]: one rounding fewer
+//                  per product, each output within one rounding per group of the reference (far
+//                  inside 1e-5 relative).
 //
 // The per-group f32 epilogue, not the tensor core, bounds this GEMM: per output and group the
 // MMA does 32 int8 MACs (about 1/256 of an SM-clock at the int8 rate), while the epilogue needs
@@ -26,7 +28,8 @@
 // tiles fastest. Warp roles:
 //   warp 0     TMA producer: per stage 128 bytes of K (4 groups) of the weight tile and of the
 //              token tile (128-byte swizzle), the weight scales [128 rows][4 groups] and the
-//              token scales [4 groups][BN tokens] (from the transposed activation-scale plane).
+//              token scales [4 groups][BN tokens] (from the transposed activation-scale plane);
+//              with mins also the weight mins and the negated token group sums, laid out alike.
 //   warp 1     TMEM owner and MMA issuer: one tcgen05.mma.kind::i8 (M=128, N=BN, K=32) per group
 //              into its own TMEM accumulator. Groups go in rounds of GPR (two round buffers of
 //              GPR accumulators alternate); one tcgen05.commit per round signals the epilogue,
@@ -56,17 +59,19 @@ constexpr int BK = 128;   // K bytes per stage
 constexpr int GPS = 4;    // scale groups per stage
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
-template <int BN_, int WPQ_, int GPR_, bool EXACT_>
+template <int BN_, int WPQ_, int GPR_, bool EXACT_, bool MINS_ = false>
 struct TcCfg {
     static constexpr int BN = BN_, WPQ = WPQ_, GPR = GPR_;
     static constexpr bool EXACT = EXACT_;
+    // MINS: groups carry a min term (Q4_K_M): acc += c * (xs * ws) - x_sum * wm
+    static constexpr bool MINS = MINS_;
     static constexpr int COLS = BN / WPQ;  // token columns per epilogue thread
     static constexpr int EPI = 4 * WPQ;    // epilogue warps
     static constexpr int THREADS = (2 + EPI) * 32;
     // TMEM: two round buffers of GPR group accumulators (BN int32 columns each)
     static constexpr int TMEM_COLS = 512;
     static constexpr int SA = BMW * BK, SB = BN * BK;  // operand bytes per stage
-    static constexpr int STAGE_TX = SA + SB + BMW * GPS * 4 + GPS * BN * 4;
+    static constexpr int STAGE_TX = SA + SB + (BMW * GPS * 4 + GPS * BN * 4) * (MINS ? 2 : 1);
     static constexpr int STAGES_FIT = (200 * 1024) / STAGE_TX;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static_assert((COLS == 32 || COLS == 64) && BN % 32 == 0 && BN <= 256, "tile shape");
@@ -79,6 +84,8 @@ struct TcSmem {
     uint8_t b[C::STAGES][C::SB];  // token tiles
     float ws[C::STAGES][BMW][GPS];
     float xs[C::STAGES][GPS][C::BN];
+    float wm[C::MINS ? C::STAGES : 1][BMW][GPS];     // weight mins (MINS)
+    float xn[C::MINS ? C::STAGES : 1][GPS][C::BN];   // -x_sums, permuted like xs (MINS)
     uint64_t full[C::STAGES], empty[C::STAGES], tfull[2], tempty[2], done;
     uint32_t tmem_base;
     int abort_flag;
@@ -221,6 +228,7 @@ template <class C>
 __global__ void __launch_bounds__(C::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    const __grid_constant__ CUtensorMap tmWS, const __grid_constant__ CUtensorMap tmXS,
+                   const __grid_constant__ CUtensorMap tmWM, const __grid_constant__ CUtensorMap tmXN,
                    int M, int G, int row_begin, int sub_n, int tiles_w, int tiles_t,
                    float *__restrict__ out, int *err) {
     constexpr int BN = C::BN, STAGES = C::STAGES, GPR = C::GPR, EPI = C::EPI, COLS = C::COLS;
@@ -278,6 +286,10 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     tma_load_2d(sm.b[s], &tmX, &sm.full[s], ks * BK, tok);
                     tma_load_2d(&sm.ws[s][0][0], &tmWS, &sm.full[s], ks * GPS, wrow);
                     tma_load_2d(&sm.xs[s][0][0], &tmXS, &sm.full[s], tok, ks * GPS);
+                    if (C::MINS) {
+                        tma_load_2d(&sm.wm[s][0][0], &tmWM, &sm.full[s], ks * GPS, wrow);
+                        tma_load_2d(&sm.xn[s][0][0], &tmXN, &sm.full[s], tok, ks * GPS);
+                    }
                 }
             }
             if (!ok) {
@@ -353,11 +365,14 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     ok = false;
                     break;
                 }
-                float4 w4[4];
+                float4 w4[4], m4[4];
 #pragma unroll
-                for (int i = 0; i < 4; i++)
+                for (int i = 0; i < 4; i++) {
                     w4[i] = *reinterpret_cast<const float4 *>(&sm.ws[s][r0 + 8 * i][0]);
+                    if (C::MINS) m4[i] = *reinterpret_cast<const float4 *>(&sm.wm[s][r0 + 8 * i][0]);
+                }
                 const float *xbase = &sm.xs[s][0][slice * COLS + 4 * kq];
+                const float *nbase = &sm.xn[C::MINS ? s : 0][0][slice * COLS + 4 * kq];
 #pragma unroll
                 for (int rr = 0; rr < GPS / GPR; rr++, rc++) {
                     const int rb = rc & 1;
@@ -386,16 +401,28 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                             const float *xg = xbase + g * BN + 32 * cb;
                             const ulonglong2 xv0 = *reinterpret_cast<const ulonglong2 *>(xg);
                             const ulonglong2 xv1 = *reinterpret_cast<const ulonglong2 *>(xg + 16);
-                            uint64_t ws2[2];
+                            uint64_t ws2[2], wm2[2];
 #pragma unroll
                             for (int i = 0; i < 2; i++) {
                                 const float4 &wv4 = w4[2 * h + i];
                                 const float wv = g == 0 ? wv4.x : g == 1 ? wv4.y : g == 2 ? wv4.z : wv4.w;
                                 ws2[i] = pk2(__float_as_uint(wv), __float_as_uint(wv));
+                                if (C::MINS) {
+                                    const float4 &mv4 = m4[2 * h + i];
+                                    const float mv = g == 0 ? mv4.x : g == 1 ? mv4.y : g == 2 ? mv4.z : mv4.w;
+                                    wm2[i] = pk2(__float_as_uint(mv), __float_as_uint(mv));
+                                }
+                            }
+                            ulonglong2 nv0 = make_ulonglong2(0ull, 0ull), nv1 = nv0;
+                            if (C::MINS) {
+                                const float *ng = nbase + g * BN + 32 * cb;
+                                nv0 = *reinterpret_cast<const ulonglong2 *>(ng);
+                                nv1 = *reinterpret_cast<const ulonglong2 *>(ng + 16);
                             }
 #pragma unroll
                             for (int r = 0; r < 4; r++) {
                                 const uint64_t xp = r == 0 ? xv0.x : r == 1 ? xv0.y : r == 2 ? xv1.x : xv1.y;
+                                const uint64_t np = r == 0 ? nv0.x : r == 1 ? nv0.y : r == 2 ? nv1.x : nv1.y;
 #pragma unroll
                                 for (int i = 0; i < 2; i++) {
                                     // exact: |c| <= 32 * 127 * 127 < 2^24
@@ -405,16 +432,26 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                                     const uint64_t sc = mul2(ws2[i], xp);
                                     uint64_t &a = acc[cb][h][r][i];
                                     if (C::EXACT) {
-                                        // separately rounded product and sum, as the reference
+                                        // separately rounded products and sums, as the reference:
+                                        // acc += c * s [- x_sum * wm]
                                         float c0, c1, s0, s1, a0, a1;
                                         upk2(cf, c0, c1);
                                         upk2(sc, s0, s1);
                                         upk2(a, a0, a1);
-                                        a0 = __fadd_rn(a0, __fmul_rn(c0, s0));
-                                        a1 = __fadd_rn(a1, __fmul_rn(c1, s1));
+                                        float t0 = __fmul_rn(c0, s0), t1 = __fmul_rn(c1, s1);
+                                        if (C::MINS) {
+                                            float n0, n1, m0, m1;
+                                            upk2(np, n0, n1);
+                                            upk2(wm2[i], m0, m1);
+                                            t0 = __fadd_rn(t0, __fmul_rn(n0, m0));
+                                            t1 = __fadd_rn(t1, __fmul_rn(n1, m1));
+                                        }
+                                        a0 = __fadd_rn(a0, t0);
+                                        a1 = __fadd_rn(a1, t1);
                                         a = pk2(__float_as_uint(a0), __float_as_uint(a1));
                                     } else {
                                         a = fma2(cf, sc, a);
+                                        if (C::MINS) a = fma2(np, wm2[i], a);
                                     }
                                 }
                             }
@@ -498,7 +535,7 @@ template <class C>
 int launch_tc(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out, size_t row_begin,
               size_t row_end, cudaStream_t st, int *err) {
     const size_t kp = w->k_pad, G = kp / 32;
-    CUtensorMap tmW, tmX, tmWS, tmXS;
+    CUtensorMap tmW, tmX, tmWS, tmXS, tmWM, tmXN;
     if (!encode_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->q, kp, w->rows, kp, BK, BMW,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, act->q, kp, act->m, kp, BK, C::BN,
@@ -508,6 +545,15 @@ int launch_tc(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out, s
         !encode_2d(&tmXS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act->x_scales_t,
                    (act->m + 31) / 32 * 32, G, act->xt_pitch * 4, C::BN, GPS,
                    CU_TENSOR_MAP_SWIZZLE_NONE))
+        return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
+    tmWM = tmWS;
+    tmXN = tmXS;
+    if (C::MINS &&
+        (!encode_2d(&tmWM, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->mins, G, w->rows, G * 4, GPS, BMW,
+                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
+         !encode_2d(&tmXN, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act->x_nsums_t,
+                    (act->m + 31) / 32 * 32, G, act->xt_pitch * 4, C::BN, GPS,
+                    CU_TENSOR_MAP_SWIZZLE_NONE)))
         return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
     const size_t sub_n = row_end - row_begin;
     const int tiles_w = (int)((sub_n + BMW - 1) / BMW), tiles_t = (int)((act->m + C::BN - 1) / C::BN);
@@ -527,7 +573,8 @@ int launch_tc(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out, s
     }
     const size_t grid = ntiles < (size_t)num_sms() ? ntiles : (size_t)num_sms();
     gemm_tc_kernel<C><<<(unsigned)grid, C::THREADS, smem, st>>>(
-        tmW, tmX, tmWS, tmXS, (int)act->m, (int)G, (int)row_begin, (int)sub_n, tiles_w, tiles_t,
+        tmW, tmX, tmWS, tmXS, tmWM, tmXN, (int)act->m, (int)G, (int)row_begin, (int)sub_n, tiles_w,
+        tiles_t,
         out, err);
     return check_launch("gemm_tc_kernel");
 }
@@ -543,14 +590,16 @@ constexpr int TILE_BN[3] = {128, 96, 64};
 
 // The tile width with the smallest estimated time: waves of (weight tile, token tile) pairs over
 // the SMs, each wave as long as one tile's token columns.
-int choose_tile(size_t m, size_t sub_n) {
+// With min terms the 128-token configuration runs out of registers (it spills), so it is not
+// a candidate then.
+int choose_tile(size_t m, size_t sub_n, bool mins) {
     const size_t tiles_w = (sub_n + BMW - 1) / BMW, sms = (size_t)num_sms();
-    int best = TILE_BN[0];
+    int best = TILE_BN[mins ? 1 : 0];
     size_t best_t = 0;
-    for (int i = 0; i < 3; i++) {
+    for (int i = mins ? 1 : 0; i < 3; i++) {
         const size_t tiles = tiles_w * ((m + TILE_BN[i] - 1) / TILE_BN[i]);
         const size_t t = (tiles + sms - 1) / sms * (size_t)TILE_BN[i];
-        if (i == 0 || t < best_t) {
+        if (i == (mins ? 1 : 0) || t < best_t) {
             best = TILE_BN[i];
             best_t = t;
         }
@@ -560,22 +609,22 @@ int choose_tile(size_t m, size_t sub_n) {
 
 // The three configurations: (tokens per tile, epilogue warps per lane quarter, groups per
 // barrier round).
-template <bool E> using TC64 = TcCfg<64, 2, 4, E>;
-template <bool E> using TC96 = TcCfg<96, 3, 2, E>;
-template <bool E> using TC128 = TcCfg<128, 2, 2, E>;
+template <bool E, bool MN> using TC64 = TcCfg<64, 2, 4, E, MN>;
+template <bool E, bool MN> using TC96 = TcCfg<96, 3, 2, E, MN>;
+template <bool E, bool MN> using TC128 = TcCfg<128, 2, 2, E, MN>;
 
 std::atomic<int> g_gemm_exact{0};
 
 // Smallest batch the tensor-core path takes (one 128-row MMA tile is mostly padding below it).
 constexpr size_t TC_MIN_M = 32;
 
-template <bool EXACT>
+template <bool EXACT, bool MINS>
 int launch_tc_bn(int bn, const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out,
                  size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
     switch (bn) {
-        case 64: return launch_tc<TC64<EXACT>>(w, act, out, row_begin, row_end, st, err);
-        case 128: return launch_tc<TC128<EXACT>>(w, act, out, row_begin, row_end, st, err);
-        default: return launch_tc<TC96<EXACT>>(w, act, out, row_begin, row_end, st, err);
+        case 64: return launch_tc<TC64<EXACT, MINS>>(w, act, out, row_begin, row_end, st, err);
+        case 128: return launch_tc<TC128<EXACT, MINS>>(w, act, out, row_begin, row_end, st, err);
+        default: return launch_tc<TC96<EXACT, MINS>>(w, act, out, row_begin, row_end, st, err);
     }
 }
 
@@ -583,20 +632,25 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
                    size_t row_begin, size_t row_end, cudaStream_t st, bool *used) {
     *used = false;
     const size_t kp = w->k_pad;
-    if (w->group_elems != 32 || w->mins != nullptr || kp % BK != 0 || act->m < TC_MIN_M ||
-        act->k_pad != kp || act->m > (size_t)INT32_MAX || w->rows > (size_t)INT32_MAX ||
-        act->x_scales_t == nullptr)
+    const bool mins = w->mins != nullptr;
+    if (w->group_elems != 32 || kp % BK != 0 || act->m < TC_MIN_M || act->k_pad != kp ||
+        act->m > (size_t)INT32_MAX || w->rows > (size_t)INT32_MAX || act->x_scales_t == nullptr ||
+        (mins && act->x_nsums_t == nullptr))
         return JKB_OK;
     if ((((uintptr_t)w->q) & 15) || (((uintptr_t)act->q) & 15) || (((uintptr_t)w->scales) & 15) ||
-        (((uintptr_t)act->x_scales_t) & 15) || (act->xt_pitch & 31))
+        (((uintptr_t)act->x_scales_t) & 15) || (act->xt_pitch & 31) ||
+        (mins && ((((uintptr_t)w->mins) & 15) || (((uintptr_t)act->x_nsums_t) & 15))))
         return JKB_OK;
     int *err = device_error_word();
     if (!err) return JKB_OK;
     *used = true;
-    const int bn = choose_tile(act->m, row_end - row_begin);
-    return g_gemm_exact.load(std::memory_order_relaxed)
-               ? launch_tc_bn<true>(bn, w, act, out, row_begin, row_end, st, err)
-               : launch_tc_bn<false>(bn, w, act, out, row_begin, row_end, st, err);
+    const int bn = choose_tile(act->m, row_end - row_begin, mins);
+    const bool exact = g_gemm_exact.load(std::memory_order_relaxed);
+    if (mins)
+        return exact ? launch_tc_bn<true, true>(bn, w, act, out, row_begin, row_end, st, err)
+                     : launch_tc_bn<false, true>(bn, w, act, out, row_begin, row_end, st, err);
+    return exact ? launch_tc_bn<true, false>(bn, w, act, out, row_begin, row_end, st, err)
+                 : launch_tc_bn<false, false>(bn, w, act, out, row_begin, row_end, st, err);
 }
 
 }  // namespace jkb

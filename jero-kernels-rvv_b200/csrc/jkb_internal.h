@@ -107,6 +107,9 @@ struct jkb_act_q8 {
     // act_q8_kernel). nullptr when the buffer has no room for it (the GEMM then takes the dp4a
     // path).
     float *x_scales_t;
+    // -x_sums in the same transposed, permuted layout (the tensor-core GEMM's min term for
+    // Q4_K_M weights); nullptr when x_scales_t is
+    float *x_nsums_t;
     size_t xt_pitch;
 };
 

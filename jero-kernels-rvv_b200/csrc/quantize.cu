@@ -125,6 +125,7 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ a
                                                      float *__restrict__ xsum,
                                                      float *__restrict__ xs16,
                                                      float *__restrict__ xs_t,
+                                                     float *__restrict__ xsn_t,
                                                      size_t xt_pitch) {
     size_t kb = kp / 32;
     size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ a
                          4 * ((r >> 1) & 3) + 2 * ((r >> 3) & 1) + (r & 1);
     if (r >= m) {
         xs_t[xt_at] = 0.0f;
+        xsn_t[xt_at] = 0.0f;
         return;
     }
     const float *src = act + r * k;
@@ -183,7 +185,10 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ a
     qo[0] = make_uint4(words[0], words[1], words[2], words[3]);
     qo[1] = make_uint4(words[4], words[5], words[6], words[7]);
     xs[r * kb + b] = d;
-    if (xs_t) xs_t[xt_at] = d;
+    if (xs_t) {
+        xs_t[xt_at] = d;
+        xsn_t[xt_at] = -s;
+    }
     xsum[r * kb + b] = s;
     xs16[r * (kp / 16) + 2 * b] = h0;
     xs16[r * (kp / 16) + 2 * b + 1] = h1;
@@ -417,7 +422,7 @@ int jkb_act_q8_create(size_t m_capacity, size_t k, jkb_act_q8 **out) {
     size_t qb = m_capacity * a->k_pad, fb = m_capacity * kb * 4, f16b = m_capacity * kc * 4,
            sb = m_capacity * nsb * 4, tb = a->xt_pitch * kb * 4;
     ar.cap = Arena::round(qb) + 2 * Arena::round(fb) + Arena::round(f16b) + Arena::round(sb) +
-             Arena::round(tb);
+             2 * Arena::round(tb);
     cudaError_t e = cudaMalloc(&ar.base, ar.cap);
     if (e != cudaSuccess) {
         delete a;
@@ -430,6 +435,7 @@ int jkb_act_q8_create(size_t m_capacity, size_t k, jkb_act_q8 **out) {
     a->x_sums_16 = (float *)ar.take(f16b);
     a->super_scales = (float *)ar.take(sb);
     a->x_scales_t = (float *)ar.take(tb);
+    a->x_nsums_t = (float *)ar.take(tb);
     *out = a;
     return JKB_OK;
 }
@@ -462,7 +468,7 @@ int jkb_act_q8_quantize(jkb_act_q8 *a, const float *input, size_t in_len, size_t
     act_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(input, m, k, a->k_pad, a->q,
                                                                a->x_scales, a->x_sums,
                                                                a->x_sums_16, a->x_scales_t,
-                                                               a->xt_pitch);
+                                                               a->x_nsums_t, a->xt_pitch);
     int rc = check_launch("act_q8_kernel");
     if (rc) return rc;
     size_t ns = m * nsb;

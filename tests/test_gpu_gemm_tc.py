@@ -1,7 +1,8 @@
-"""The tcgen05 tensor-core path of the repacked GEMM (32-element scale groups without mins:
-Q8_0, Q4_0, TQ2_0, I2_S weights; batches of at least 32 tokens; K a multiple of 128) vs the CPU
-oracle. Every output accumulates its groups in K order as accumulate_scaled_tile_scalar does
-(repack.rs:3045-3093), acc += (f32)c * (xs * ws):
+"""The tcgen05 tensor-core path of the repacked GEMM (32-element scale groups: Q8_0, Q4_0,
+TQ2_0, I2_S and Q4_K_M weights, the last with their min terms; batches of at least 32 tokens;
+K a multiple of 128) vs the CPU oracle. Every output accumulates its groups in K order as
+accumulate_scaled_tile_scalar does (repack.rs:3045-3093), acc += (f32)c * (xs * ws)
+[- x_sum * wm]:
 * with the exact epilogue (jkb.gemm_exact()) bit for bit;
 * with the default fused multiply-add epilogue within the f32 tolerance contract
   (|err| <= 1e-5 * sum_k |x~||w~| per output, l2 relative error < 1e-5);
@@ -43,6 +44,9 @@ SHAPES = [
     (8, 96, 12800, 256),    # 100 weight tiles, one 96-token tile each: the 96-token tile
     (8, 512, 18944, 256),   # 512 tokens x 148 weight tiles: the 128-token tile
     (8, 200, 12032, 256),   # 94 weight tiles, a partial last 64-token tile
+    (12, 200, 300, 4096),   # Q4_K_M (min terms), ragged tiles
+    (12, 2048, 4096, 256),  # Q4_K_M, the 64-token tile over 7 waves
+    (12, 96, 12800, 256),   # Q4_K_M, the 96-token tile
     (2, 64, 640, 1024),     # Q4_0
     (35, 96, 256, 512),     # TQ2_0
     (36, 40, 384, 2560),    # I2_S (per-tensor scale)
