@@ -219,6 +219,12 @@ int jkb_gemv_tq2_0_q8_k(float *out, size_t out_len, const jkb_weight *w,
  * x points at BlockQ8_0 (Q4_0, Q8_0 weights) or BlockQ8K (Q4_K_M, Q6_K, TQ1_0, TQ2_0). */
 int jkb_gemv_rows(float *out, size_t out_len, const jkb_weight *w, const void *x, size_t x_len,
                   size_t row_begin, size_t row_end, void *stream);
+/* M tokens of the gemv_* calls above in one launch (no reference counterpart; the reference
+ * calls gemv once per token): x is m rows of BlockQ8_0 (Q4_0, Q8_0 weights) or BlockQ8K (Q4_K_M,
+ * Q6_K, TQ1_0, TQ2_0) blocks, m * blocks_per_row in all; out is [m][rows]. Each token's output
+ * is exactly its single call's. */
+int jkb_gemv_batch(float *out, size_t out_len, const jkb_weight *w, const void *x, size_t x_len,
+                   size_t m, void *stream);
 /* Diagnostic with no reference counterpart: the per-(row, block) integer sums (sumi and, for
  * Q4_K_M, summins) and the f32 block values the GEMV kernels form before summing a row.
  * Arrays are [rows][blocks_per_row]; summins may be NULL. */

@@ -1255,6 +1255,37 @@ int jkb_gemv_rows(float *out, size_t out_len, const jkb_weight *w, const void *x
     return launch_gemv(L, as_stream(stream));
 }
 
+int jkb_gemv_batch(float *out, size_t out_len, const jkb_weight *w, const void *x, size_t x_len,
+                   size_t m, void *stream) {
+    static const char *fn = "gemv_batch";
+    int rc = check_weight(w);
+    if (rc) return rc;
+    if (w->quant == JKB_I2_S)
+        return fail(JKB_E_CAPABILITY, w->name, w->offset, w->byte_len, w->gguf_bytes,
+                    "I2_S weights have no Q8 GEMV in the reference; use jkb_bitlinear_i8_batch");
+    if (m == 0 || x_len != m * w->nb)
+        return fail(JKB_E_BOUNDS, w->name, w->offset, x_len, m * w->nb,
+                    "%s: x_blocks len %zu != m (%zu) * %zu blocks", fn, x_len, m, w->nb);
+    if (out_len != m * w->rows)
+        return fail(JKB_E_BOUNDS, fn, 0, out_len * 4, m * w->rows * 4,
+                    "output length %zu != m (%zu) * rows (%zu)", out_len, m, w->rows);
+    if (!out || !x) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
+    if ((rc = check_align(out, 4, fn, "output")) || (rc = check_align(x, 4, fn, "x_blocks")))
+        return rc;
+    const int kind = act_kind_for(w->quant);
+    GemvLaunch L{};
+    L.w = w;
+    L.x = x;
+    L.x_row_stride = w->nb * (kind == ACT_Q8_0 ? sizeof(jkb_block_q8_0) : sizeof(jkb_block_q8_k));
+    L.act_kind = kind;
+    L.out = out;
+    L.out_ld = w->rows;
+    L.row_begin = 0;
+    L.row_end = w->rows;
+    L.m = m;
+    return launch_gemv(L, as_stream(stream));
+}
+
 int jkb_gemv_block_dots(const jkb_weight *w, const void *x, size_t x_len, int32_t *sumi,
                         int32_t *summins, float *block_values, void *stream) {
     int rc = check_weight(w);

@@ -89,6 +89,7 @@ SIGNATURES = {
     "jkb_gemv_tq1_0_q8_k": [P, S, P, P, S, P],
     "jkb_gemv_tq2_0_q8_k": [P, S, P, P, S, P],
     "jkb_gemv_rows": [P, S, P, P, S, S, S, P],
+    "jkb_gemv_batch": [P, S, P, P, S, S, P],
     "jkb_gemv_block_dots": [P, P, S, P, P, P, P],
     "jkb_vec_dot_q4_k_m": [P, S, P, P, S, P],
     "jkb_vec_dot_q8_0": [P, S, P, P, S, P],

@@ -30,7 +30,7 @@ __all__ = [
     "bitlinear_i8_batch", "gemm_repacked", "gemm_repacked_rows", "gemv_repacked",
     "gemv_repacked_rows", "gemm_repacked_f32", "gemm_repacked_f32_noalloc",
     "empty_q8_0_blocks", "empty_q8_k_blocks", "device_status", "gemm_set_exact", "gemm_get_exact",
-    "gemm_exact", "PeerGroup",
+    "gemm_exact", "PeerGroup", "gemv_batch",
     "device_view",
 ]
 
@@ -521,6 +521,14 @@ def gemv_rows(out, weights: Weight, x_blocks, row_range, stream=None):
     _check(_L().jkb_gemv_rows(_dptr(out), out.numel(), weights.handle, _dptr(x_blocks),
                               _nblocks(x_blocks, _act_block_bytes(weights.quant)), r0, r1,
                               _stream(stream)))
+
+
+def gemv_batch(out, weights: Weight, x_blocks, m: int, stream=None):
+    """M tokens of gemv_* in one launch (no reference counterpart): x_blocks holds m rows of
+    Q8 blocks, out is [m][rows]; each token's output equals its single call's."""
+    _check(_L().jkb_gemv_batch(_dptr(out), out.numel(), weights.handle, _dptr(x_blocks),
+                               _nblocks(x_blocks, _act_block_bytes(weights.quant)), m,
+                               _stream(stream)))
 
 
 def gemv_block_dots(weights: Weight, x_blocks, stream=None):

@@ -217,3 +217,39 @@ def test_gemv_validation_errors(jkb, oracle):
     w.destroy()
     with pytest.raises(jkb.InvalidHandle):
         jkb.gemv_q4_k_q8_k(torch.empty(8, device="cuda"), w, xq)
+
+
+@pytest.mark.parametrize("quant,rows,cols", [(12, 28672, 8192), (12, 8192, 28672),
+                                             (14, 128256, 8192)])
+def test_gemv_batch16_70b_shapes(jkb, oracle, quant, rows, cols):
+    """BASELINE configs[4] at batch 16 (Llama-3-70B Q4_K_M gate/up, down and the Q6_K lm_head, full
+    size): one jkb_gemv_batch launch equals the 16 single-token calls bit for bit, and sampled
+    rows of the first and last token match the oracle within the row tolerance."""
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench  # seeded synthetic GGUF matrices at full size
+
+    m = 16
+    wb = bench.synth_matrix(quant, rows, cols, 77 + rows)
+    w = upload(jkb, quant, wb, rows, cols)
+    xs = [oracle.normal(cols, 900 + t, 1.0) for t in range(m)]
+    xq = [oracle.quantize_act(quant, x) for x in xs]
+    xall = dev(np.concatenate([q.view(np.uint8).reshape(-1) for q in xq]))
+    out = torch.empty(m * rows, dtype=torch.float32, device="cuda")
+    jkb.gemv_batch(out, w, xall, m)
+    got = host(out).reshape(m, rows)
+    for t in range(m):
+        single = run_gemv(jkb, quant, w, dev(xq[t]))
+        assert np.array_equal(bits(got[t]), bits(single)), f"token {t}"
+    row_bytes = wb.size // rows
+    sample = np.unique(np.concatenate([np.arange(8), np.arange(rows - 8, rows),
+                                       np.random.default_rng(5).integers(0, rows, 48)]))
+    for t in (0, m - 1):
+        for r in sample:
+            part = wb[r * row_bytes:(r + 1) * row_bytes]
+            y_ref = oracle.gemv(quant, part, 1, cols, xq[t])
+            _, _, v_ref = oracle.block_dots(quant, part, 1, cols, xq[t])
+            ok, worst = R.gemv_tolerance_ok(got[t, r:r + 1], y_ref, v_ref, REL)
+            assert ok, f"token {t} row {r}: worst {worst:.3g} of bound"
+    w.destroy()
