@@ -55,6 +55,8 @@ struct KArgs {
     int nb;  // blocks per row
     int K;
     int lpr_shift;  // log2(lanes per row)
+    int ntok;       // M_TOK: tokens of the launch
+    int tpc;        // M_TOK: tokens per CTA (1..TOK_MAX), each staged in its own smem slot
     int32_t *dbg_sumi, *dbg_mins;
     float *dbg_val;
 };
@@ -783,7 +785,10 @@ constexpr int MAX_WARPS = 8;
 
 // M_SINGLE: one matrix, row sums to out. M_DIAG: one matrix, per-block integer sums and values
 // to the diagnostic arrays. M_MULTI: several matrices over one activation (virtual rows).
-enum { M_SINGLE = 0, M_DIAG = 1, M_MULTI = 2 };
+// M_TOK: one matrix, several tokens per CTA -- every weight block is loaded once and dotted
+// with up to TOK_MAX staged activations (token batches of pre-quantized input).
+enum { M_SINGLE = 0, M_DIAG = 1, M_MULTI = 2, M_TOK = 3 };
+constexpr int TOK_MAX = 8;
 
 // Row pointers of virtual row r and its output slot (token 0).
 template <int MODE>
@@ -816,7 +821,10 @@ __device__ __forceinline__ Row row_of(const KArgs &a, size_t r, float *&outp) {
 template <class F, class S, int MODE>
 __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
-    const int tok = blockIdx.y;
+    constexpr int TB = MODE == M_TOK ? TOK_MAX : 1;  // token slots per CTA
+    const int tok = MODE == M_TOK ? (int)blockIdx.y * a.tpc : (int)blockIdx.y;
+    const int nt = MODE == M_TOK ? min(a.tpc, a.ntok - tok) : 1;
+    const size_t slot = MODE == M_TOK ? (S::bytes(a.K) + 15) / 16 * 16 : 0;
     KArgs args = a;
     const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
     const int lpr = 1 << a.lpr_shift, rpw = 32 >> a.lpr_shift;
@@ -827,7 +835,9 @@ __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
     const size_t stride = nwarps * rpw;
     size_t r0 = a.row_begin + wid * rpw;  // warp-uniform position (r0, b0)
     int b0 = 0;
-    float acc = 0.0f;
+    float acc[TB];
+#pragma unroll
+    for (int t = 0; t < TB; t++) acc[t] = 0.0f;
     // Grouped launches keep the current row's pointers in registers (the owning matrix is
     // looked up once per row); single-matrix launches form them from the parameters at each
     // load, which keeps the register count of the long-running kernels down.
@@ -842,15 +852,19 @@ __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
     };
     // one block of row r0 + rsub: the exact integer sums and the f32 block value
     auto consume = [&](const typename F::Ld &l, int b) {
-        int2 iv;
-        const float v = F::value(args, smem, l, b, iv);
-        if (MODE == M_DIAG) {
-            const size_t o = (r0 + rsub - a.row_begin) * (size_t)a.nb + b;
-            a.dbg_sumi[o] = iv.x;
-            if (a.dbg_mins) a.dbg_mins[o] = iv.y;
-            a.dbg_val[o] = v;
-        } else {
-            acc = __fadd_rn(acc, v);
+#pragma unroll
+        for (int t = 0; t < TB; t++) {
+            if (t >= nt) break;
+            int2 iv;
+            const float v = F::value(args, smem + t * slot, l, b, iv);
+            if (MODE == M_DIAG) {
+                const size_t o = (r0 + rsub - a.row_begin) * (size_t)a.nb + b;
+                a.dbg_sumi[o] = iv.x;
+                if (a.dbg_mins) a.dbg_mins[o] = iv.y;
+                a.dbg_val[o] = v;
+            } else {
+                acc[t] = __fadd_rn(acc[t], v);
+            }
         }
     };
     // advance to the next block column; at the end of a row, reduce its lanes and store
@@ -858,14 +872,20 @@ __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
         b0 += lpr;
         if (b0 >= a.nb) {
             if (MODE != M_DIAG) {
-                for (int m = lpr >> 1; m > 0; m >>= 1)
-                    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
-                if (li == 0 && r0 + rsub < a.row_end) {
-                    float *o = MODE == M_MULTI ? outp : a.mat[0].out + (r0 + rsub - a.row_begin);
-                    o[tok_off] = acc;
+#pragma unroll
+                for (int t = 0; t < TB; t++) {
+                    if (t >= nt) break;
+                    for (int m = lpr >> 1; m > 0; m >>= 1)
+                        acc[t] = __fadd_rn(acc[t], __shfl_xor_sync(0xffffffffu, acc[t], m));
+                    if (li == 0 && r0 + rsub < a.row_end) {
+                        float *o =
+                            MODE == M_MULTI ? outp : a.mat[0].out + (r0 + rsub - a.row_begin);
+                        o[tok_off + (size_t)t * a.out_ld] = acc[t];
+                    }
                 }
             }
-            acc = 0.0f;
+#pragma unroll
+            for (int t = 0; t < TB; t++) acc[t] = 0.0f;
             b0 = 0;
             r0 += stride;
             if (MODE == M_MULTI) rpm = row_of<MODE>(a, r0 + rsub, outp);
@@ -877,8 +897,13 @@ __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
     if (r0 + rsub < a.row_end && li < a.nb) F::prefetch(args, row_ptrs(), li);
     pdl_wait();
     pdl_launch_dependents();
-    if (a.act_scales) args.act_scale = a.act_scales[tok];
-    S::stage(args, a.x + (size_t)tok * a.x_row_stride, smem);
+    if (MODE == M_TOK) {
+        for (int t = 0; t < nt; t++)
+            S::stage(args, a.x + (size_t)(tok + t) * a.x_row_stride, smem + t * slot);
+    } else {
+        if (a.act_scales) args.act_scale = a.act_scales[tok];
+        S::stage(args, a.x + (size_t)tok * a.x_row_stride, smem);
+    }
     while (r0 < a.row_end) {
         const int b = b0 + li;
         if (r0 + rsub < a.row_end && b < a.nb) {
@@ -898,8 +923,20 @@ __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
 constexpr unsigned GEMV_MAX_CLUSTER = 8;
 
 template <class F, class S, int MODE>
-static int launch_t(const KArgs &a, size_t m, cudaStream_t st, const char *name) {
-    const size_t smem = S::bytes(a.K);
+static int launch_t(const KArgs &a_in, size_t m, cudaStream_t st, const char *name) {
+    KArgs a = a_in;
+    size_t smem = S::bytes(a.K);
+    if (MODE == M_TOK) {  // as many token slots per CTA as fit in 150 KB, at most TOK_MAX
+        const size_t slot = (smem + 15) / 16 * 16;
+        size_t tpc = (150 * 1024) / slot;
+        tpc = tpc < (size_t)TOK_MAX ? tpc : (size_t)TOK_MAX;
+        tpc = tpc < m ? tpc : m;
+        if (tpc < 1) tpc = 1;
+        a.tpc = (int)tpc;
+        a.ntok = (int)m;
+        smem = slot * tpc;
+        m = (m + tpc - 1) / tpc;  // CTA rows of the grid
+    }
     auto kern = gemv_kernel<F, S, MODE>;
     // resident CTAs on the device per CTA size (8, 4 or 2 warps) and cluster size (1, 2, 4,
     // 8; for cluster launches the resident clusters times the cluster size), cached per
@@ -1019,6 +1056,9 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
                     w->cols, MAX_K);
     if (a.row_end <= a.row_begin) return JKB_OK;
     const bool diag = L.dbg_sumi != nullptr;
+    // token batches of pre-quantized input without per-token scales share weight loads
+    const bool tokb = !multi && !diag && (L.m ? L.m : 1) > 1 && L.act_scales == nullptr &&
+                      (L.act_kind == ACT_Q8_0 || L.act_kind == ACT_Q8_K);
     const size_t m = multi ? 1 : (L.m ? L.m : 1);
     const bool f32_in = L.act_kind == ACT_F32_Q8_0 || L.act_kind == ACT_F32_Q8_K;
     if ((multi && (!f32_in || diag)) || (diag && f32_in))
@@ -1028,8 +1068,9 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
                     L.act_kind);
     // pre-quantized or i8 activations: single or diagnostic launches
 #define JKB_LAUNCH(F)                                                                   \
-    return diag ? launch_t<F, F::Act, M_DIAG>(a, m, st, "gemv_kernel<diag>")            \
-                : launch_t<F, F::Act, M_SINGLE>(a, m, st, "gemv_kernel")
+    return diag  ? launch_t<F, F::Act, M_DIAG>(a, m, st, "gemv_kernel<diag>")           \
+           : tokb ? launch_t<F, F::Act, M_TOK>(a, m, st, "gemv_kernel<tokens>")          \
+                  : launch_t<F, F::Act, M_SINGLE>(a, m, st, "gemv_kernel")
     // f32 activations quantized by the stager S: single or grouped launches
 #define JKB_LAUNCH_F32(F, S)                                                            \
     return multi ? launch_t<F, S, M_MULTI>(a, m, st, "gemv_kernel<grouped>")            \
