@@ -596,22 +596,24 @@ def run_prefill_gemm(world, rank, launches=10):
             w.destroy()
         del act, out, x
         torch.cuda.empty_cache()
-    # Q4_K_M weights (min terms) on one shape, for reference (not part of configs[2])
+    # Q4_K_M (min terms) and Q6_K (16-element groups) weights on one shape each, for reference
+    # (not part of configs[2])
     m, n, k = 2048, 14336, 4096
     per = n // world
-    raw = synth_matrix(Q4_K, n, k, 4250, rank * per, (rank + 1) * per)
-    w = jkb.RepackedWeight.from_tensor(jkb.TensorView("w4k", Q4_K, [per, k], raw), per, k)
     x = torch.randn(m * k, generator=torch.Generator().manual_seed(3)).cuda()
     act = jkb.QuantizedActQ8.quantize(x, m, k)
     out = torch.empty(m * per, dtype=torch.float32, device="cuda")
-    us = _graph_time(lambda: w.gemm(out, act), launches)
-    if world > 1:
-        t = torch.tensor([us], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        us = float(t.item())
-    res["q4_k_m"] = {"m": m, "n": n, "k": k, "us": round(us, 2),
-                     "tops": round(2.0 * m * n * k / (us * 1e-6) / 1e12, 1)}
-    w.destroy()
+    for key, quant in (("q4_k_m", Q4_K), ("q6_k", Q6_K)):
+        raw = synth_matrix(quant, n, k, 4250, rank * per, (rank + 1) * per)
+        w = jkb.RepackedWeight.from_tensor(jkb.TensorView(key, quant, [per, k], raw), per, k)
+        us = _graph_time(lambda: w.gemm(out, act), launches)
+        if world > 1:
+            t = torch.tensor([us], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item())
+        res[key] = {"m": m, "n": n, "k": k, "us": round(us, 2),
+                    "tops": round(2.0 * m * n * k / (us * 1e-6) / 1e12, 1)}
+        w.destroy()
     del act, out, x
     res["tops"] = round(tot_ops[False] / (tot_us[False] * 1e-6) / 1e12, 1)
     res["exact_tops"] = round(tot_ops[True] / (tot_us[True] * 1e-6) / 1e12, 1)
@@ -702,14 +704,14 @@ def _graph_time(fn, launches, warm=3):
 
 
 def run_gemm_case(args):
-    """The repacked GEMM (BASELINE configs[2] kind) with Q8_0 (--kernel gemm_q8_0) or Q4_K_M
-    (gemm_q4_k) weights: M tokens x --rows x --cols, activations quantized once
+    """The repacked GEMM (BASELINE configs[2] kind) with Q8_0 (--kernel gemm_q8_0), Q4_K_M
+    (gemm_q4_k) or Q6_K (gemm_q6_k) weights: M tokens x --rows x --cols, activations quantized once
     (QuantizedActQ8), `--launches` GEMMs timed in a CUDA graph."""
     import torch
     import jkb200 as jkb
 
     M, N, K = args.m, args.rows, args.cols
-    quant = Q4_K if args.kernel == "gemm_q4_k" else Q8_0
+    quant = {"gemm_q4_k": Q4_K, "gemm_q6_k": Q6_K}.get(args.kernel, Q8_0)
     raw = synth_matrix(quant, N, K, 4243)
     rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", quant, [N, K], raw), N, K)
     x = torch.randn(M * K, generator=torch.Generator().manual_seed(2)).cuda()
@@ -754,7 +756,7 @@ def main():
                     help="leave out the prefill GEMM section (BASELINE configs[2])")
     ap.add_argument("--m", type=int, default=2048, help="tokens of --kernel gemm_q8_0 / int8_peak")
     ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0", "gemm_q8_0", "gemm_q4_k",
-                                         "int8_peak"],
+                                         "gemm_q6_k", "int8_peak"],
                     help="run one GEMV shape (profiling case) instead of the benchmark")
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--cols", type=int, default=4096)
@@ -766,7 +768,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.kernel in ("gemm_q8_0", "gemm_q4_k"):
+    if args.kernel in ("gemm_q8_0", "gemm_q4_k", "gemm_q6_k"):
         run_gemm_case(args)
     elif args.kernel == "int8_peak":
         run_int8_peak(args)

@@ -1,8 +1,8 @@
-// tcgen05 tensor-core path of the repacked block-scaled GEMM for 32-element scale groups (Q8_0 /
-// Q4_0 / TQ2_0 / I2_S weights, and Q4_K_M with its min terms). Per output (m, n), as in
-// accumulate_scaled_tile_scalar (repack.rs:3045-3093):
-//     acc = 0; for g in K order: acc += (f32)c_g * (xs[m][g] * ws[n][g]) [- xsum[m][g] * wm[n][g]]
-// with c_g = sum_{k in g} xq*wq. The integer group sums c_g are exact (int8 MMA into int32). Two
+// tcgen05 tensor-core path of the repacked block-scaled GEMM: 32-element scale groups (Q8_0 /
+// Q4_0 / TQ2_0 / I2_S weights, and Q4_K_M with its min terms) and 16-element groups (Q6_K). Per
+// output (m, n), as in accumulate_scaled_tile_scalar (repack.rs:3045-3093):
+//     acc = 0; for g in K order: acc += (f32)c_g * (xs[m][b] * ws[n][g]) [- xsum[m][g] * wm[n][g]]
+// with c_g = sum_{k in g} xq*wq and b the 32-element activation block of g. The integer group sums c_g are exact (int8 MMA into int32). Two
 // epilogues:
 //   EXACT = true   the reference's roundings: p = (f32)c * (xs*ws) rounded, [p - xsum*wm rounded,]
 //                  then acc + p rounded, so every output is bit-identical to the scalar reference;
@@ -59,34 +59,45 @@ constexpr int BK = 128;   // K bytes per stage
 constexpr int GPS = 4;    // scale groups per stage
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
-template <int BN_, int WPQ_, int GPR_, bool EXACT_, bool MINS_ = false>
+template <int BN_, int WPQ_, int GPR_, bool EXACT_, bool MINS_ = false, bool H16_ = false>
 struct TcCfg {
     static constexpr int BN = BN_, WPQ = WPQ_, GPR = GPR_;
     static constexpr bool EXACT = EXACT_;
     // MINS: groups carry a min term (Q4_K_M): acc += c * (xs * ws) - x_sum * wm
     static constexpr bool MINS = MINS_;
+    // H16: 16-element weight scale groups (Q6_K). The int8 MMA sums 32 elements, so a masking
+    // warp writes two copies of each token tile with alternate 16-byte halves of K zeroed, and
+    // every 32-element slice takes two MMAs (even and odd half-groups) into two accumulators.
+    static constexpr bool H16 = H16_;
+    static constexpr int SPL = H16 ? 2 : 1;    // accumulators per 32-element slice
+    static constexpr int NA = GPR * SPL;       // accumulators per round
+    static constexpr int NG = GPS * SPL;       // weight-scale groups per stage
     static constexpr int COLS = BN / WPQ;  // token columns per epilogue thread
     static constexpr int EPI = 4 * WPQ;    // epilogue warps
-    static constexpr int THREADS = (2 + EPI) * 32;
+    static constexpr int THREADS = (2 + EPI + (H16 ? 1 : 0)) * 32;
     // TMEM: two round buffers of GPR group accumulators (BN int32 columns each)
     static constexpr int TMEM_COLS = 512;
     static constexpr int SA = BMW * BK, SB = BN * BK;  // operand bytes per stage
-    static constexpr int STAGE_TX = SA + SB + (BMW * GPS * 4 + GPS * BN * 4) * (MINS ? 2 : 1);
-    static constexpr int STAGES_FIT = (200 * 1024) / STAGE_TX;
+    static constexpr int STAGE_TX = SA + SB + BMW * NG * 4 + GPS * BN * 4 +
+                                    (MINS ? BMW * GPS * 4 + GPS * BN * 4 : 0);
+    static constexpr int STAGES_FIT = (200 * 1024) / (STAGE_TX + (H16 ? 2 * SB : 0));
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static_assert((COLS == 32 || COLS == 64) && BN % 32 == 0 && BN <= 256, "tile shape");
-    static_assert(GPS % GPR == 0 && 2 * GPR * BN <= TMEM_COLS, "two rounds of GPR buffers");
+    static_assert(GPS % GPR == 0 && 2 * NA * BN <= TMEM_COLS, "two rounds of NA buffers");
+    static_assert(!(H16 && MINS), "16-element groups carry no mins");
 };
 
 template <class C>
 struct TcSmem {
     uint8_t a[C::STAGES][C::SA];  // weight tiles; 1024-byte aligned (swizzle atoms)
     uint8_t b[C::STAGES][C::SB];  // token tiles
-    float ws[C::STAGES][BMW][GPS];
+    uint8_t blo[C::H16 ? C::STAGES : 1][C::H16 ? C::SB : 1024];  // H16: odd 16-byte halves zeroed
+    uint8_t bhi[C::H16 ? C::STAGES : 1][C::H16 ? C::SB : 1024];  // H16: even 16-byte halves zeroed
+    float ws[C::STAGES][BMW][C::NG];
     float xs[C::STAGES][GPS][C::BN];
     float wm[C::MINS ? C::STAGES : 1][BMW][GPS];     // weight mins (MINS)
     float xn[C::MINS ? C::STAGES : 1][GPS][C::BN];   // -x_sums, permuted like xs (MINS)
-    uint64_t full[C::STAGES], empty[C::STAGES], tfull[2], tempty[2], done;
+    uint64_t full[C::STAGES], empty[C::STAGES], masked[C::STAGES], tfull[2], tempty[2], done;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -232,6 +243,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                    int M, int G, int row_begin, int sub_n, int tiles_w, int tiles_t,
                    float *__restrict__ out, int *err) {
     constexpr int BN = C::BN, STAGES = C::STAGES, GPR = C::GPR, EPI = C::EPI, COLS = C::COLS;
+    constexpr int NA = C::NA, SPL = C::SPL;
     extern __shared__ uint8_t smem_raw[];
     TcSmem<C> &sm =
         *reinterpret_cast<TcSmem<C> *>((((uintptr_t)smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -244,6 +256,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         for (int i = 0; i < STAGES; i++) {
             mbar_init(&sm.full[i], 1);
             mbar_init(&sm.empty[i], 1 + EPI);  // the MMA commit and every epilogue warp
+            mbar_init(&sm.masked[i], 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&sm.tfull[i], 1);
@@ -284,7 +297,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     mbar_arrive_tx(&sm.full[s], C::STAGE_TX);
                     tma_load_2d(sm.a[s], &tmW, &sm.full[s], ks * BK, wrow);
                     tma_load_2d(sm.b[s], &tmX, &sm.full[s], ks * BK, tok);
-                    tma_load_2d(&sm.ws[s][0][0], &tmWS, &sm.full[s], ks * GPS, wrow);
+                    tma_load_2d(&sm.ws[s][0][0], &tmWS, &sm.full[s], ks * C::NG, wrow);
                     tma_load_2d(&sm.xs[s][0][0], &tmXS, &sm.full[s], tok, ks * GPS);
                     if (C::MINS) {
                         tma_load_2d(&sm.wm[s][0][0], &tmWM, &sm.full[s], ks * GPS, wrow);
@@ -311,12 +324,15 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 for (int ks = 0; ks < kstages && ok; ks++, it++) {
                     const int s = it % STAGES;
-                    if (!mbar_wait(&sm.full[s], (it / STAGES) & 1, abort_flag, err)) {
+                    if (!mbar_wait(C::H16 ? &sm.masked[s] : &sm.full[s], (it / STAGES) & 1,
+                                   abort_flag, err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint64_t ad = smem_desc(sm.a[s]), bd = smem_desc(sm.b[s]);
+                    const uint64_t bdl = smem_desc(sm.blo[C::H16 ? s : 0]),
+                                   bdh = smem_desc(sm.bhi[C::H16 ? s : 0]);
                     for (int r = 0; r < GPS / GPR; r++, rc++) {
                         const int rb = rc & 1;
                         if (!mbar_wait(&sm.tempty[rb], ((rc >> 1) & 1) ^ 1, abort_flag, err)) {
@@ -326,8 +342,14 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                         tc_fence_after();
                         for (int j = 0; j < GPR; j++) {
                             const int g = r * GPR + j;  // K step g: 32 bytes along the rows
-                            mma_i8(tmem + (rb * GPR + j) * BN, ad + (uint64_t)(2 * g),
-                                   bd + (uint64_t)(2 * g), IDESC);
+                            const uint32_t d = tmem + (rb * NA + SPL * j) * BN;
+                            if (C::H16) {
+                                mma_i8(d, ad + (uint64_t)(2 * g), bdl + (uint64_t)(2 * g), IDESC);
+                                mma_i8(d + BN, ad + (uint64_t)(2 * g), bdh + (uint64_t)(2 * g),
+                                       IDESC);
+                            } else {
+                                mma_i8(d, ad + (uint64_t)(2 * g), bd + (uint64_t)(2 * g), IDESC);
+                            }
                         }
                         tc_commit(&sm.tfull[rb]);
                     }
@@ -338,6 +360,33 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             tc_commit(&sm.done);
             const uint64_t t0 = globaltimer();
             while (!mbar_try(&sm.done, 0) && globaltimer() - t0 < WAIT_NS) {
+            }
+        }
+    } else if (C::H16 && warp == 2 + EPI) {
+        // ------------------------------------------------ masking warp (H16)
+        // Two copies of each token tile, one with the odd and one with the even 16-byte halves
+        // of every 32-byte K slice zeroed. In the 128-byte swizzle, the 16-byte unit at
+        // position p of row r holds logical unit p ^ (r & 7).
+        uint32_t it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            for (int ks = 0; ks < kstages; ks++, it++) {
+                const int s = it % STAGES;
+                if (!mbar_wait(&sm.full[s], (it / STAGES) & 1, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+                for (int idx = lane; idx < BN * 8; idx += 32) {
+                    const int row = idx >> 3, logical = (idx & 7) ^ (row & 7);
+                    const uint4 v = *reinterpret_cast<const uint4 *>(&sm.b[s][16 * idx]);
+                    *reinterpret_cast<uint4 *>(&sm.blo[C::H16 ? s : 0][16 * idx]) = (logical & 1) ? z : v;
+                    *reinterpret_cast<uint4 *>(&sm.bhi[C::H16 ? s : 0][16 * idx]) = (logical & 1) ? v : z;
+                }
+                // the copies are read by the tensor core (async proxy)
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.masked[s]);
             }
         }
     } else {
@@ -365,10 +414,12 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     ok = false;
                     break;
                 }
-                float4 w4[4], m4[4];
+                float4 w4[4][SPL], m4[4];
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
-                    w4[i] = *reinterpret_cast<const float4 *>(&sm.ws[s][r0 + 8 * i][0]);
+#pragma unroll
+                    for (int v = 0; v < SPL; v++)
+                        w4[i][v] = *reinterpret_cast<const float4 *>(&sm.ws[s][r0 + 8 * i][4 * v]);
                     if (C::MINS) m4[i] = *reinterpret_cast<const float4 *>(&sm.wm[s][r0 + 8 * i][0]);
                 }
                 const float *xbase = &sm.xs[s][0][slice * COLS + 4 * kq];
@@ -386,16 +437,19 @@ __global__ void __launch_bounds__(C::THREADS, 1)
 #pragma unroll
                     for (int ch = 0; ch < 2 * (COLS / 32); ch++) {
                         const int cb = ch >> 1, h = ch & 1;
-                        uint32_t c[GPR][16];
+                        uint32_t c[NA][16];
 #pragma unroll
-                        for (int j = 0; j < GPR; j++)
-                            tmem_ld16x256(tlane + (rb * GPR + j) * BN + ((uint32_t)(16 * h) << 16) +
+                        for (int j = 0; j < NA; j++)
+                            tmem_ld16x256(tlane + (rb * NA + j) * BN + ((uint32_t)(16 * h) << 16) +
                                               32 * cb,
                                           c[j]);
                         tmem_ld_wait();
 #pragma unroll
-                        for (int j = 0; j < GPR; j++) {
-                            const int g = rr * GPR + j;  // group within the stage
+                        for (int j = 0; j < NA; j++) {
+                            // accumulator j: 32-element slice g of the stage (token-scale group)
+                            // and, with H16, its even or odd 16-element half (weight-scale group gw)
+                            const int g = rr * GPR + j / SPL;
+                            const int gw = C::H16 ? 2 * g + (j % SPL) : g;
                             // token scales of group g, permuted within 32-token blocks so that
                             // one 16-byte load holds the pairs of repeats 2p and 2p + 1
                             const float *xg = xbase + g * BN + 32 * cb;
@@ -404,8 +458,9 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                             uint64_t ws2[2], wm2[2];
 #pragma unroll
                             for (int i = 0; i < 2; i++) {
-                                const float4 &wv4 = w4[2 * h + i];
-                                const float wv = g == 0 ? wv4.x : g == 1 ? wv4.y : g == 2 ? wv4.z : wv4.w;
+                                const float4 &wv4 = w4[2 * h + i][gw >> 2];
+                                const int gq = gw & 3;
+                                const float wv = gq == 0 ? wv4.x : gq == 1 ? wv4.y : gq == 2 ? wv4.z : wv4.w;
                                 ws2[i] = pk2(__float_as_uint(wv), __float_as_uint(wv));
                                 if (C::MINS) {
                                     const float4 &mv4 = m4[2 * h + i];
@@ -540,8 +595,8 @@ int launch_tc(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out, s
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, act->q, kp, act->m, kp, BK, C::BN,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_2d(&tmWS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->scales, G, w->rows, G * 4, GPS, BMW,
-                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_2d(&tmWS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->scales, G * C::SPL, w->rows,
+                   G * C::SPL * 4, C::NG, BMW, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !encode_2d(&tmXS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act->x_scales_t,
                    (act->m + 31) / 32 * 32, G, act->xt_pitch * 4, C::BN, GPS,
                    CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -590,8 +645,8 @@ constexpr int TILE_BN[3] = {128, 96, 64};
 
 // The tile width with the smallest estimated time: waves of (weight tile, token tile) pairs over
 // the SMs, each wave as long as one tile's token columns.
-// With min terms the 128-token configuration runs out of registers (it spills), so it is not
-// a candidate then.
+// With min terms or 16-element groups the 128-token configuration runs out of registers (it
+// spills), so it is not a candidate then.
 int choose_tile(size_t m, size_t sub_n, bool mins) {
     const size_t tiles_w = (sub_n + BMW - 1) / BMW, sms = (size_t)num_sms();
     int best = TILE_BN[mins ? 1 : 0];
@@ -609,22 +664,25 @@ int choose_tile(size_t m, size_t sub_n, bool mins) {
 
 // The three configurations: (tokens per tile, epilogue warps per lane quarter, groups per
 // barrier round).
-template <bool E, bool MN> using TC64 = TcCfg<64, 2, 4, E, MN>;
-template <bool E, bool MN> using TC96 = TcCfg<96, 3, 2, E, MN>;
-template <bool E, bool MN> using TC128 = TcCfg<128, 2, 2, E, MN>;
+template <bool E, bool MN, bool H> using TC64 = TcCfg<64, 2, H ? 2 : 4, E, MN, H>;
+template <bool E, bool MN, bool H> using TC96 = TcCfg<96, 3, H ? 1 : 2, E, MN, H>;
+template <bool E, bool MN, bool H> using TC128 = TcCfg<128, 2, H ? 1 : 2, E, MN, H>;
 
 std::atomic<int> g_gemm_exact{0};
 
 // Smallest batch the tensor-core path takes (one 128-row MMA tile is mostly padding below it).
 constexpr size_t TC_MIN_M = 32;
 
-template <bool EXACT, bool MINS>
+template <bool EXACT, bool MINS, bool H16>
 int launch_tc_bn(int bn, const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out,
                  size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
     switch (bn) {
-        case 64: return launch_tc<TC64<EXACT, MINS>>(w, act, out, row_begin, row_end, st, err);
-        case 128: return launch_tc<TC128<EXACT, MINS>>(w, act, out, row_begin, row_end, st, err);
-        default: return launch_tc<TC96<EXACT, MINS>>(w, act, out, row_begin, row_end, st, err);
+        case 64:
+            return launch_tc<TC64<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
+        case 128:
+            return launch_tc<TC128<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
+        default:
+            return launch_tc<TC96<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
     }
 }
 
@@ -632,8 +690,9 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
                    size_t row_begin, size_t row_end, cudaStream_t st, bool *used) {
     *used = false;
     const size_t kp = w->k_pad;
-    const bool mins = w->mins != nullptr;
-    if (w->group_elems != 32 || kp % BK != 0 || act->m < TC_MIN_M || act->k_pad != kp ||
+    const bool mins = w->mins != nullptr, h16 = w->group_elems == 16;
+    if ((w->group_elems != 32 && !(h16 && !mins)) || kp % BK != 0 || act->m < TC_MIN_M ||
+        act->k_pad != kp ||
         act->m > (size_t)INT32_MAX || w->rows > (size_t)INT32_MAX || act->x_scales_t == nullptr ||
         (mins && act->x_nsums_t == nullptr))
         return JKB_OK;
@@ -644,13 +703,16 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
     int *err = device_error_word();
     if (!err) return JKB_OK;
     *used = true;
-    const int bn = choose_tile(act->m, row_end - row_begin, mins);
+    const int bn = choose_tile(act->m, row_end - row_begin, mins || h16);
     const bool exact = g_gemm_exact.load(std::memory_order_relaxed);
+    if (h16)
+        return exact ? launch_tc_bn<true, false, true>(bn, w, act, out, row_begin, row_end, st, err)
+                     : launch_tc_bn<false, false, true>(bn, w, act, out, row_begin, row_end, st, err);
     if (mins)
-        return exact ? launch_tc_bn<true, true>(bn, w, act, out, row_begin, row_end, st, err)
-                     : launch_tc_bn<false, true>(bn, w, act, out, row_begin, row_end, st, err);
-    return exact ? launch_tc_bn<true, false>(bn, w, act, out, row_begin, row_end, st, err)
-                 : launch_tc_bn<false, false>(bn, w, act, out, row_begin, row_end, st, err);
+        return exact ? launch_tc_bn<true, true, false>(bn, w, act, out, row_begin, row_end, st, err)
+                     : launch_tc_bn<false, true, false>(bn, w, act, out, row_begin, row_end, st, err);
+    return exact ? launch_tc_bn<true, false, false>(bn, w, act, out, row_begin, row_end, st, err)
+                 : launch_tc_bn<false, false, false>(bn, w, act, out, row_begin, row_end, st, err);
 }
 
 }  // namespace jkb

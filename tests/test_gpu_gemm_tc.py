@@ -1,5 +1,6 @@
 """The tcgen05 tensor-core path of the repacked GEMM (32-element scale groups: Q8_0, Q4_0,
-TQ2_0, I2_S and Q4_K_M weights, the last with their min terms; batches of at least 32 tokens;
+TQ2_0, I2_S and Q4_K_M weights, the last with their min terms; 16-element groups: Q6_K;
+batches of at least 32 tokens;
 K a multiple of 128) vs the CPU oracle. Every output accumulates its groups in K order as
 accumulate_scaled_tile_scalar does (repack.rs:3045-3093), acc += (f32)c * (xs * ws)
 [- x_sum * wm]:
@@ -47,6 +48,9 @@ SHAPES = [
     (12, 200, 300, 4096),   # Q4_K_M (min terms), ragged tiles
     (12, 2048, 4096, 256),  # Q4_K_M, the 64-token tile over 7 waves
     (12, 96, 12800, 256),   # Q4_K_M, the 96-token tile
+    (14, 200, 300, 4096),   # Q6_K (16-element groups: masked token tiles, two MMAs a slice)
+    (14, 2048, 4096, 256),  # Q6_K, the 64-token tile
+    (14, 96, 12800, 256),   # Q6_K, the 96-token tile
     (2, 64, 640, 1024),     # Q4_0
     (35, 96, 256, 512),     # TQ2_0
     (36, 40, 384, 2560),    # I2_S (per-tensor scale)
