@@ -430,18 +430,29 @@ typedef struct {
     int quant;
     size_t be, bb; /* block elements, block bytes */
     int act_k;     /* 1: BlockQ8K activations, 0: BlockQ8_0 */
+    int dot;       /* 1: has an integer block dot / GEMV in the reference's quant_q8.rs */
 } fmt_t;
 
 static const fmt_t FMTS[] = {
-    {OR_Q4_0, 32, 18, 0},   {OR_Q8_0, 32, 34, 0},    {OR_Q4_K, 256, 144, 1},
-    {OR_Q6_K, 256, 210, 1}, {OR_TQ2_0, 256, 66, 1}, {OR_TQ1_0, 256, 54, 1},
-    {OR_I2_S, 128, 32, 0},
+    {OR_Q4_0, 32, 18, 0, 1},   {OR_Q8_0, 32, 34, 0, 1},    {OR_Q4_K, 256, 144, 1, 1},
+    {OR_Q6_K, 256, 210, 1, 1}, {OR_TQ2_0, 256, 66, 1, 1}, {OR_TQ1_0, 256, 54, 1, 1},
+    {OR_I2_S, 128, 32, 0, 1},  {OR_Q4_1, 32, 20, 0, 0},   {OR_IQ4_NL, 32, 18, 0, 0},
 };
 
 static const fmt_t *fmt_of(int quant) {
     for (size_t i = 0; i < sizeof(FMTS) / sizeof(FMTS[0]); i++)
         if (FMTS[i].quant == quant) return &FMTS[i];
     return NULL;
+}
+
+/* The IQ4_NL non-linear code book (quant.rs:80-82, the published ggml table). */
+static const int8_t OR_KVALUES_IQ4NL[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
+                                            1,    13,   25,  38,  53,  69,  89,  113};
+
+/* Formats with a block dot against Q8 activations (GEMV, vec_dot, BitLinear paths). */
+static const fmt_t *dot_fmt(int quant) {
+    const fmt_t *f = fmt_of(quant);
+    return f && f->dot ? f : NULL;
 }
 
 size_t or_weight_bytes(int quant, size_t rows, size_t cols) {
@@ -465,7 +476,7 @@ static float block_value(int quant, const uint8_t *w, const void *x, size_t b, i
 
 int or_block_dots(int quant, const uint8_t *w, size_t rows, size_t cols, const void *x,
                   int32_t *sumi, int32_t *summins, float *contrib) {
-    const fmt_t *f = fmt_of(quant);
+    const fmt_t *f = dot_fmt(quant);
     if (!f || quant == OR_I2_S || cols % f->be) return 1;
     size_t nb = cols / f->be;
     for (size_t r = 0; r < rows; r++)
@@ -481,7 +492,8 @@ int or_block_dots(int quant, const uint8_t *w, size_t rows, size_t cols, const v
 
 /* dot_*_row (quant_q8.rs:1217-1235, :2817-2830, :2972-3004): `.map(block).sum()` -> -0.0 start. */
 float or_vec_dot(int quant, const uint8_t *w_row, const void *x, size_t n_blocks) {
-    const fmt_t *f = fmt_of(quant);
+    const fmt_t *f = dot_fmt(quant);
+    if (!f) return NAN;
     float s = -0.0f;
     for (size_t b = 0; b < n_blocks; b++) s += block_value(quant, w_row + b * f->bb, x, b, 0, 0);
     return s;
@@ -491,7 +503,7 @@ float or_vec_dot(int quant, const uint8_t *w_row, const void *x, size_t n_blocks
  * accumulate from 0.0 block by block; tail rows use the 1-row `.sum()` path. */
 static void gemv_range(int quant, float *out, const uint8_t *w, size_t cols, const void *x,
                        size_t r0, size_t r1) {
-    const fmt_t *f = fmt_of(quant);
+    const fmt_t *f = dot_fmt(quant);
     size_t nb = cols / f->be, rs = nb * f->bb;
     size_t r = r0;
     for (; r + 4 <= r1; r += 4) {
@@ -507,7 +519,7 @@ static void gemv_range(int quant, float *out, const uint8_t *w, size_t cols, con
 /* gemv_q4_0_q8_0 :1586, gemv_q8_0_q8_0 :1670, gemv_q4_k_q8_k :3101, gemv_q6_k_q8_k :3189,
  * gemv_tq1_0_q8_k :3221, gemv_tq2_0_q8_k :3250 (validation done by the caller). */
 int or_gemv(int quant, float *out, const uint8_t *w, size_t rows, size_t cols, const void *x) {
-    const fmt_t *f = fmt_of(quant);
+    const fmt_t *f = dot_fmt(quant);
     if (!f || quant == OR_I2_S || cols == 0 || cols % f->be) return 1;
     gemv_range(quant, out, w, cols, x, 0, rows);
     return 0;
@@ -532,7 +544,7 @@ static void *gemv_job_run(void *p) {
  * would split work. Output covers [row_begin, row_end). */
 int or_gemv_rows_mt(int quant, float *out, const uint8_t *w, size_t rows, size_t cols,
                     const void *x, size_t row_begin, size_t row_end, int nthreads) {
-    const fmt_t *f = fmt_of(quant);
+    const fmt_t *f = dot_fmt(quant);
     if (!f || quant == OR_I2_S || cols % f->be || row_end > rows || row_begin > row_end) return 1;
     if (nthreads < 1) nthreads = 1;
     size_t n = row_end - row_begin;
@@ -618,6 +630,32 @@ void or_dequantize_block(int quant, const uint8_t *blk, float i2s_scale, float *
         }
         return;
     }
+    case OR_Q4_1: {
+        /* quant.rs:118-136: y = d * q + m over unsigned nibbles; zeros when d == m == 0 */
+        float d = or_f16_to_f32_finite(rd16(blk)), m = or_f16_to_f32_finite(rd16(blk + 2));
+        if (d == 0.0f && m == 0.0f) {
+            memset(out, 0, 32 * sizeof(float));
+            return;
+        }
+        for (int i = 0; i < 16; i++) {
+            out[i] = d * (float)(blk[4 + i] & 0x0F) + m;
+            out[i + 16] = d * (float)((blk[4 + i] >> 4) & 0x0F) + m;
+        }
+        return;
+    }
+    case OR_IQ4_NL: {
+        /* quant.rs:332-356: y = d * KVALUES_IQ4NL[nibble]; zeros when d == 0 */
+        float d = or_f16_to_f32_finite(rd16(blk));
+        if (d == 0.0f) {
+            memset(out, 0, 32 * sizeof(float));
+            return;
+        }
+        for (int i = 0; i < 16; i++) {
+            out[i] = d * (float)OR_KVALUES_IQ4NL[blk[2 + i] & 0x0F];
+            out[i + 16] = d * (float)OR_KVALUES_IQ4NL[blk[2 + i] >> 4];
+        }
+        return;
+    }
     case OR_I2_S: {
         int8_t q[128];
         unpack_i2_s(blk, q);
@@ -666,7 +704,7 @@ int or_dequantize_rows(int quant, const uint8_t *w, size_t rows, size_t cols, fl
  * row_sum from 0.0 of per-block dot_product_f32_scalar; I2_S rows are 0.0 when the scale is 0. */
 int or_vec_dot_f32(int quant, float *out, const uint8_t *w, size_t w_len, size_t rows,
                    size_t cols, const float *input) {
-    const fmt_t *f = fmt_of(quant);
+    const fmt_t *f = dot_fmt(quant);
     if (!f || cols % f->be || quant == OR_TQ1_0) return 1;
     size_t nb = cols / f->be;
     if (w_len < or_weight_bytes(quant, rows, cols)) return 1;
@@ -712,7 +750,7 @@ static int bitlinear_block(int quant, const uint8_t *blk, float i2s, int8_t *wv,
 
 static void bitlinear_rows(float *out, int quant, const uint8_t *w, size_t rows, size_t cols,
                            const int8_t *act, float act_scale, float i2s, size_t r0, size_t r1) {
-    const fmt_t *f = fmt_of(quant);
+    const fmt_t *f = dot_fmt(quant);
     size_t nb = cols / f->be;
     int8_t wv[256];
     for (size_t r = r0; r < r1; r++) {
@@ -739,7 +777,7 @@ static float i2s_trailer(int quant, const uint8_t *w, size_t rows, size_t cols) 
 /* bitlinear_i8_rvv ime.rs:882-938 (bitlinear_i8_ime :1005-1114 is bit-identical). */
 int or_bitlinear_i8(float *out, int quant, const uint8_t *w, size_t w_len, size_t rows,
                     size_t cols, const int8_t *act, float act_scale) {
-    const fmt_t *f = fmt_of(quant);
+    const fmt_t *f = dot_fmt(quant);
     if (!f || (quant != OR_TQ1_0 && quant != OR_TQ2_0 && quant != OR_Q8_0 && quant != OR_I2_S))
         return 2;
     if (rows == 0 || cols == 0 || cols % f->be || w_len < or_weight_bytes(quant, rows, cols))
@@ -773,7 +811,7 @@ static void *bl_job_run(void *p) {
 int or_bitlinear_i8_rows_mt(float *out, int quant, const uint8_t *w, size_t w_len, size_t rows,
                             size_t cols, const int8_t *act, float act_scale, size_t m,
                             const float *act_scales, int nthreads) {
-    const fmt_t *f = fmt_of(quant);
+    const fmt_t *f = dot_fmt(quant);
     if (!f || cols % f->be || w_len < or_weight_bytes(quant, rows, cols)) return 1;
     (void)act_scale;
     if (nthreads < 1) nthreads = 1;
@@ -803,7 +841,7 @@ size_t or_repack_scale_groups(int quant, size_t cols) {
     return quant == OR_Q6_K ? kp / 16 : kp / 32;
 }
 
-int or_repack_has_mins(int quant) { return quant == OR_Q4_K; }
+int or_repack_has_mins(int quant) { return quant == OR_Q4_K || quant == OR_Q4_1; }
 
 int or_repack_block_scaled(int quant, const uint8_t *raw, size_t raw_len, size_t rows,
                            size_t cols, int8_t *q, float *scales, float *mins) {
@@ -889,6 +927,28 @@ int or_repack_block_scaled(int quant, const uint8_t *raw, size_t raw_len, size_t
                 memcpy(qr + 256 * b, t, 256);
                 break;
             }
+            case OR_Q4_1: {
+                /* repack.rs:1814-1826: scale d, min -m (0.0 when m == 0), unsigned quants */
+                float d = or_f16_to_f32_finite(rd16(blk)), m = or_f16_to_f32_finite(rd16(blk + 2));
+                sr[b] = d;
+                mr[b] = m == 0.0f ? 0.0f : -m;
+                for (int i = 0; i < 16; i++) {
+                    qr[32 * b + i] = (int8_t)(blk[4 + i] & 0x0F);
+                    qr[32 * b + 16 + i] = (int8_t)((blk[4 + i] >> 4) & 0x0F);
+                }
+                break;
+            }
+            case OR_IQ4_NL: {
+                /* repack.rs:1861-1873: scale d; quants left 0 when d == 0 */
+                float d = or_f16_to_f32_finite(rd16(blk));
+                sr[b] = d;
+                if (d != 0.0f)
+                    for (int i = 0; i < 16; i++) {
+                        qr[32 * b + i] = OR_KVALUES_IQ4NL[blk[2 + i] & 0x0F];
+                        qr[32 * b + 16 + i] = OR_KVALUES_IQ4NL[blk[2 + i] >> 4];
+                    }
+                break;
+            }
             case OR_I2_S: {
                 int8_t t[128];
                 unpack_i2_s(blk, t);
@@ -905,7 +965,7 @@ int or_repack_block_scaled(int quant, const uint8_t *raw, size_t raw_len, size_t
 
 typedef struct {
     float *out;
-    int quant;
+    int cps; /* 16-element chunks per scale group: 2 (32-element groups) or 1 (Q6_K) */
     const int8_t *wq;
     const float *ws, *wm;
     size_t cols;
@@ -920,7 +980,7 @@ typedef struct {
 static void *gemm_job_run(void *p) {
     gemm_job *j = (gemm_job *)p;
     size_t kp = (j->cols + 31) / 32 * 32, kb = kp / 32, kc = kp / 16;
-    int cps = j->quant == OR_Q6_K ? 1 : 2;
+    int cps = j->cps;
     size_t gsz = 16 * (size_t)cps, sg = kp / gsz;
     size_t sub_n = j->row_end - j->row_begin;
     for (size_t n = j->n0; n < j->n1; n++) {
@@ -949,12 +1009,10 @@ static void *gemm_job_run(void *p) {
     return NULL;
 }
 
-int or_gemm_repacked(float *out, int quant, const int8_t *wq, const float *ws, const float *wm,
-                     size_t rows, size_t cols, const int8_t *xq, const float *xs,
-                     const float *xsum, const float *xsum16, size_t m, size_t row_begin,
-                     size_t row_end, int nthreads) {
-    if (row_begin > row_end || row_end > rows || m == 0) return 1;
-    if (or_repack_has_mins(quant) && (!wm || !xsum)) return 1;
+static int gemm_run(float *out, int cps, const int8_t *wq, const float *ws, const float *wm,
+                    size_t cols, const int8_t *xq, const float *xs, const float *xsum,
+                    const float *xsum16, size_t m, size_t row_begin, size_t row_end,
+                    int nthreads) {
     if (nthreads < 1) nthreads = 1;
     size_t n = row_end - row_begin;
     if (n == 0) return 0;
@@ -963,13 +1021,208 @@ int or_gemm_repacked(float *out, int quant, const int8_t *wq, const float *ws, c
     gemm_job jobs[256];
     int nt = 0;
     for (size_t r = row_begin; r < row_end && nt < 256; r += per, nt++) {
-        jobs[nt] = (gemm_job){out,  quant, wq,        ws,      or_repack_has_mins(quant) ? wm : NULL,
-                              cols, xq,    xs,        xsum,    xsum16,
-                              m,    row_begin, row_end, r,     r + per < row_end ? r + per : row_end};
+        jobs[nt] = (gemm_job){out,  cps,       wq,      ws,    wm, cols, xq,
+                              xs,   xsum,      xsum16,  m,     row_begin, row_end,
+                              r,    r + per < row_end ? r + per : row_end};
         pthread_create(&th[nt], NULL, gemm_job_run, &jobs[nt]);
     }
     for (int i = 0; i < nt; i++) pthread_join(th[i], NULL);
     return 0;
+}
+
+int or_gemm_repacked(float *out, int quant, const int8_t *wq, const float *ws, const float *wm,
+                     size_t rows, size_t cols, const int8_t *xq, const float *xs,
+                     const float *xsum, const float *xsum16, size_t m, size_t row_begin,
+                     size_t row_end, int nthreads) {
+    if (row_begin > row_end || row_end > rows || m == 0) return 1;
+    if (or_repack_has_mins(quant) && (!wm || !xsum)) return 1;
+    return gemm_run(out, quant == OR_Q6_K ? 1 : 2, wq, ws, or_repack_has_mins(quant) ? wm : NULL,
+                    cols, xq, xs, xsum, xsum16, m, row_begin, row_end, nthreads);
+}
+
+/* ------------------------------------------------------------------------------------------ */
+/* Compact 4-bit nibble matrices (PackedNibbleMatrix, repack.rs:4188-5545)                      */
+/* ------------------------------------------------------------------------------------------ */
+
+int or_nibble_supported(int quant) {
+    /* validate_nibble_quant, repack.rs:4231-4236 */
+    return quant == OR_Q4_0 || quant == OR_Q4_1 || quant == OR_IQ4_NL || quant == OR_Q4_K;
+}
+
+/* pack_pair_split_nibbles_into_tile (repack.rs:4281-4305, scalar branch): even row in the low
+ * nibbles, odd row in the high nibbles; bytes 0..64 hold columns 0..15 (low nibbles of the GGUF
+ * bytes), bytes 64..128 columns 16..31 (high nibbles). */
+static void pack_pair(const uint8_t *e, const uint8_t *o, uint8_t *tile, int pair) {
+    for (int k = 0; k < 16; k++) {
+        tile[pair * 16 + k] = (uint8_t)((e[k] & 0x0F) | ((o[k] & 0x0F) << 4));
+        tile[64 + pair * 16 + k] = (uint8_t)((e[k] >> 4) | (o[k] & 0xF0));
+    }
+}
+
+/* repack_nibble_into_tile_range over all tiles (repack.rs:4414-4645). Q4_0 / IQ4_NL blocks whose
+ * scale decodes to zero (including non-finite scales) keep zero scale bits and zero nibbles. */
+int or_nibble_pack_tiles(int quant, const uint8_t *raw, size_t raw_len, size_t rows, size_t cols,
+                         uint8_t *tiles, uint16_t *scales_f16, uint16_t *mins_f16,
+                         uint8_t *headers) {
+    const fmt_t *f = fmt_of(quant);
+    if (!or_nibble_supported(quant) || !f || rows == 0 || cols == 0 || cols % f->be) return 1;
+    if (raw_len < or_weight_bytes(quant, rows, cols)) return 1;
+    size_t nt_count = (rows + 7) / 8, kb = cols / 32, nsb = cols / 256;
+    size_t rb = cols / f->be * f->bb;
+    memset(tiles, 0, nt_count * kb * 128);
+    if (quant == OR_Q4_K) {
+        if (!headers) return 1;
+        memset(headers, 0, nt_count * nsb * 8 * 16);
+    } else {
+        if (!scales_f16 || (quant == OR_Q4_1 && !mins_f16)) return 1;
+        memset(scales_f16, 0, nt_count * kb * 8 * 2);
+        if (quant == OR_Q4_1) memset(mins_f16, 0, nt_count * kb * 8 * 2);
+    }
+    static const uint8_t zero[32] = {0};
+    for (size_t nt = 0; nt < nt_count; nt++) {
+        uint8_t *tl = tiles + nt * kb * 128;
+        for (int pair = 0; pair < 4; pair++) {
+            size_t re = nt * 8 + 2 * (size_t)pair;
+            if (re >= rows) break;
+            int has_odd = re + 1 < rows;
+            const uint8_t *er = raw + re * rb, *orw = has_odd ? raw + (re + 1) * rb : NULL;
+            if (quant == OR_Q4_0 || quant == OR_IQ4_NL) {
+                for (size_t b = 0; b < kb; b++) {
+                    const uint8_t *be = er + b * 18;
+                    uint16_t eb = rd16(be);
+                    int ez = or_f16_to_f32_finite(eb) == 0.0f;
+                    scales_f16[(nt * kb + b) * 8 + 2 * pair] = ez ? 0 : eb;
+                    int oz = 1;
+                    const uint8_t *no = zero;
+                    if (has_odd) {
+                        const uint8_t *bo = orw + b * 18;
+                        uint16_t ob = rd16(bo);
+                        oz = or_f16_to_f32_finite(ob) == 0.0f;
+                        scales_f16[(nt * kb + b) * 8 + 2 * pair + 1] = oz ? 0 : ob;
+                        if (!oz) no = bo + 2;
+                    }
+                    const uint8_t *ne = ez ? zero : be + 2;
+                    if (!ez || !oz) pack_pair(ne, no, tl + b * 128, pair);
+                }
+            } else if (quant == OR_Q4_1) {
+                for (size_t b = 0; b < kb; b++) {
+                    const uint8_t *be = er + b * 20;
+                    size_t ie = (nt * kb + b) * 8 + 2 * pair;
+                    scales_f16[ie] = rd16(be);
+                    mins_f16[ie] = rd16(be + 2);
+                    const uint8_t *no = zero;
+                    if (has_odd) {
+                        const uint8_t *bo = orw + b * 20;
+                        scales_f16[ie + 1] = rd16(bo);
+                        mins_f16[ie + 1] = rd16(bo + 2);
+                        no = bo + 4;
+                    }
+                    pack_pair(be + 4, no, tl + b * 128, pair);
+                }
+            } else { /* Q4_K_M: pack_q4k_pair_chunk32_into_tiles, repack.rs:4307-4392 */
+                for (size_t sb = 0; sb < nsb; sb++) {
+                    const uint8_t *be = er + sb * 144;
+                    memcpy(headers + ((nt * nsb + sb) * 8 + 2 * pair) * 16, be, 16);
+                    const uint8_t *bo = NULL;
+                    if (has_odd) {
+                        bo = orw + sb * 144;
+                        memcpy(headers + ((nt * nsb + sb) * 8 + 2 * pair + 1) * 16, bo, 16);
+                    }
+                    for (int c = 0; c < 4; c++) {
+                        const uint8_t *qe = be + 16 + 32 * c, *qo = bo ? bo + 16 + 32 * c : zero;
+                        uint8_t *lo = tl + (sb * 8 + 2 * c) * 128, *hi = lo + 128;
+                        for (int k = 0; k < 16; k++) {
+                            lo[pair * 16 + k] = (uint8_t)((qe[k] & 0x0F) | ((qo[k] & 0x0F) << 4));
+                            hi[pair * 16 + k] = (uint8_t)((qe[k] >> 4) | (qo[k] & 0xF0));
+                            lo[64 + pair * 16 + k] =
+                                (uint8_t)((qe[16 + k] & 0x0F) | ((qo[16 + k] & 0x0F) << 4));
+                            hi[64 + pair * 16 + k] = (uint8_t)((qe[16 + k] >> 4) | (qo[16 + k] & 0xF0));
+                        }
+                    }
+                }
+            }
+        }
+    }
+    return 0;
+}
+
+/* decode_tile_scales (repack.rs:5038-5092) and unpack_nibble_tile_to_chunks (:5095-5134), laid
+ * out row-major for the checker: q [rows][cols] (Q4_0 nibble - 8, IQ4_NL code book, else the
+ * unsigned nibble), ws [rows][cols / 32], wm [rows][cols / 32] (Q4_1: -m or 0.0; Q4_K_M:
+ * dmin * m; untouched for formats without mins). */
+int or_nibble_decode_tiles(int quant, size_t rows, size_t cols, const uint8_t *tiles,
+                           const uint16_t *scales_f16, const uint16_t *mins_f16,
+                           const uint8_t *headers, int8_t *q, float *ws, float *wm) {
+    if (!or_nibble_supported(quant) || rows == 0 || cols == 0 || cols % 32) return 1;
+    if (quant == OR_Q4_K && cols % 256) return 1;
+    int mins = quant == OR_Q4_1 || quant == OR_Q4_K;
+    if (mins && !wm) return 1;
+    size_t kb = cols / 32, nsb = cols / 256;
+    for (size_t r = 0; r < rows; r++) {
+        size_t nt = r / 8, j = r % 8, pair = j / 2;
+        int odd = (int)(j & 1);
+        for (size_t b = 0; b < kb; b++) {
+            const uint8_t *t = tiles + (nt * kb + b) * 128;
+            for (int k = 0; k < 32; k++) {
+                uint8_t byte = t[(k < 16 ? 0 : 64) + pair * 16 + (size_t)(k & 15)];
+                uint8_t nib = odd ? (uint8_t)(byte >> 4) : (uint8_t)(byte & 0x0F);
+                int8_t v = quant == OR_Q4_0      ? (int8_t)((int)nib - 8)
+                           : quant == OR_IQ4_NL ? OR_KVALUES_IQ4NL[nib]
+                                                : (int8_t)nib;
+                q[r * cols + b * 32 + (size_t)k] = v;
+            }
+            size_t mi = (nt * kb + b) * 8 + j;
+            if (quant == OR_Q4_0 || quant == OR_IQ4_NL) {
+                ws[r * kb + b] = or_f16_to_f32_finite(scales_f16[mi]);
+            } else if (quant == OR_Q4_1) {
+                ws[r * kb + b] = or_f16_to_f32_finite(scales_f16[mi]);
+                float m = or_f16_to_f32_finite(mins_f16[mi]);
+                wm[r * kb + b] = m == 0.0f ? 0.0f : -m;
+            }
+        }
+        if (quant == OR_Q4_K)
+            for (size_t sb = 0; sb < nsb; sb++) {
+                const uint8_t *h = headers + ((nt * nsb + sb) * 8 + j) * 16;
+                float d = or_f16_to_f32_finite(rd16(h)), dmin = or_f16_to_f32_finite(rd16(h + 2));
+                uint8_t sc[8], mm[8];
+                unpack_k4_scales(h + 4, sc, mm);
+                for (int is = 0; is < 8; is++) {
+                    ws[r * kb + sb * 8 + (size_t)is] = d * (float)sc[is];
+                    wm[r * kb + sb * 8 + (size_t)is] = dmin * (float)mm[is];
+                }
+            }
+    }
+    return 0;
+}
+
+/* PackedNibbleMatrix::dequantize_row (repack.rs:5001-5036): q * scale - min, min 0.0 for the
+ * formats without mins. */
+int or_nibble_dequantize_row(int quant, const int8_t *q, const float *ws, const float *wm,
+                             size_t cols, size_t row, float *out) {
+    if (!or_nibble_supported(quant) || cols % 32) return 1;
+    int mins = quant == OR_Q4_1 || quant == OR_Q4_K;
+    size_t kb = cols / 32;
+    for (size_t b = 0; b < kb; b++) {
+        float sc = ws[row * kb + b], mn = mins ? wm[row * kb + b] : 0.0f;
+        for (int k = 0; k < 32; k++)
+            out[b * 32 + (size_t)k] = (float)q[row * cols + b * 32 + (size_t)k] * sc - mn;
+    }
+    return 0;
+}
+
+/* execute_nibble_gemm_rows host branch (repack.rs:5181-5397): per output, acc from 0.0; per
+ * 32-element block in K order the i32 dot of the unpacked tile, then
+ * accumulate_scaled_tile_scalar (:3045-3093) with chunks_per_scale = 2 and the mins term for
+ * Q4_1 / Q4_K_M. Output [m][row_end - row_begin]. */
+int or_gemm_nibble(float *out, int quant, const int8_t *q, const float *ws, const float *wm,
+                   size_t rows, size_t cols, const int8_t *xq, const float *xs,
+                   const float *xsum, size_t m, size_t row_begin, size_t row_end, int nthreads) {
+    if (!or_nibble_supported(quant) || cols % 32) return 1;
+    if (row_begin > row_end || row_end > rows || m == 0) return 1;
+    int mins = quant == OR_Q4_1 || quant == OR_Q4_K;
+    if (mins && (!wm || !xsum)) return 1;
+    return gemm_run(out, 2, q, ws, mins ? wm : NULL, cols, xq, xs, xsum, NULL, m, row_begin,
+                    row_end, nthreads);
 }
 
 /* ------------------------------------------------------------------------------------------ */
@@ -1127,6 +1380,59 @@ static void quant_q6_k_block(const float *x, uint8_t *o) {
     wr16(o + 208, or_f32_to_f16(d));
 }
 
+/* Q4_1: the published ggml reference rule (min / (max - min) / 15, q = min(15, trunc(x/d + 0.5))). */
+static void quant_q4_1_block(const float *x, uint8_t *o) {
+    float lo = x[0], hi = x[0];
+    for (int i = 1; i < 32; i++) {
+        lo = fminf(lo, x[i]);
+        hi = fmaxf(hi, x[i]);
+    }
+    float d = (hi - lo) / 15.0f;
+    float id = d != 0.0f ? 1.0f / d : 0.0f;
+    wr16(o, or_f32_to_f16(d));
+    wr16(o + 2, or_f32_to_f16(lo));
+    for (int j = 0; j < 16; j++) {
+        int q0 = (int)((x[j] - lo) * id + 0.5f), q1 = (int)((x[16 + j] - lo) * id + 0.5f);
+        if (q0 > 15) q0 = 15;
+        if (q1 > 15) q1 = 15;
+        o[4 + j] = (uint8_t)(q0 | (q1 << 4));
+    }
+}
+
+/* IQ4_NL (this project's own rule): d = signed absmax / -127 so the extreme maps to code 0,
+ * each element to its nearest code-book value, then one least-squares refit of d. */
+static void quant_iq4_nl_block(const float *x, uint8_t *o) {
+    float amax = 0.0f, mx = 0.0f;
+    for (int i = 0; i < 32; i++)
+        if (fabsf(x[i]) > amax) {
+            amax = fabsf(x[i]);
+            mx = x[i];
+        }
+    float d = mx / -127.0f;
+    uint8_t idx[32];
+    for (int i = 0; i < 32; i++) {
+        int best = 0;
+        float be = INFINITY;
+        for (int c = 0; c < 16; c++) {
+            float e = fabsf(x[i] - d * (float)OR_KVALUES_IQ4NL[c]);
+            if (e < be) {
+                be = e;
+                best = c;
+            }
+        }
+        idx[i] = (uint8_t)best;
+    }
+    float sxv = 0.0f, svv = 0.0f;
+    for (int i = 0; i < 32; i++) {
+        float v = (float)OR_KVALUES_IQ4NL[idx[i]];
+        sxv += x[i] * v;
+        svv += v * v;
+    }
+    if (svv > 0.0f && d != 0.0f) d = sxv / svv;
+    wr16(o, or_f32_to_f16(d));
+    for (int j = 0; j < 16; j++) o[2 + j] = (uint8_t)(idx[j] | (idx[16 + j] << 4));
+}
+
 int or_quantize_weights(int quant, const float *w, size_t rows, size_t cols, uint8_t *out) {
     const fmt_t *f = fmt_of(quant);
     if (!f || cols % f->be) return 1;
@@ -1140,6 +1446,8 @@ int or_quantize_weights(int quant, const float *w, size_t rows, size_t cols, uin
             case OR_Q8_0: quant_q8_0_block(x, o); break;
             case OR_Q4_K: quant_q4_k_block(x, o); break;
             case OR_Q6_K: quant_q6_k_block(x, o); break;
+            case OR_Q4_1: quant_q4_1_block(x, o); break;
+            case OR_IQ4_NL: quant_iq4_nl_block(x, o); break;
             default: return 1;
             }
         }

@@ -39,9 +39,11 @@ typedef struct {
 
 enum {
     OR_Q4_0 = 2,
+    OR_Q4_1 = 3,
     OR_Q8_0 = 8,
     OR_Q4_K = 12,
     OR_Q6_K = 14,
+    OR_IQ4_NL = 20,
     OR_TQ1_0 = 34,
     OR_TQ2_0 = 35,
     OR_I2_S = 36
@@ -107,6 +109,23 @@ int or_gemm_repacked(float *out, int quant, const int8_t *wq, const float *ws, c
                      size_t rows, size_t cols, const int8_t *xq, const float *xs,
                      const float *xsum, const float *xsum16, size_t m, size_t row_begin,
                      size_t row_end, int nthreads);
+
+/* ---- Compact 4-bit nibble matrices (PackedNibbleMatrix, repack.rs:4188-5545) ----
+ * Q4_0, Q4_1, IQ4_NL, Q4_K_M. The tile layout is the reference's: tiles [n_tiles][k_blocks32]
+ * of 128 bytes (8 rows x 32 nibbles), scales_f16 / mins_f16 [n_tiles][k_blocks32][8] f16 bits,
+ * headers [n_tiles][cols / 256][8] x 16 bytes (Q4_K_M). */
+int or_nibble_supported(int quant);
+int or_nibble_pack_tiles(int quant, const uint8_t *raw, size_t raw_len, size_t rows, size_t cols,
+                         uint8_t *tiles, uint16_t *scales_f16, uint16_t *mins_f16,
+                         uint8_t *headers);
+int or_nibble_decode_tiles(int quant, size_t rows, size_t cols, const uint8_t *tiles,
+                           const uint16_t *scales_f16, const uint16_t *mins_f16,
+                           const uint8_t *headers, int8_t *q, float *ws, float *wm);
+int or_nibble_dequantize_row(int quant, const int8_t *q, const float *ws, const float *wm,
+                             size_t cols, size_t row, float *out);
+int or_gemm_nibble(float *out, int quant, const int8_t *q, const float *ws, const float *wm,
+                   size_t rows, size_t cols, const int8_t *xq, const float *xs,
+                   const float *xsum, size_t m, size_t row_begin, size_t row_end, int nthreads);
 
 /* ---- seeded synthetic inputs and this project's own weight quantizers ---- */
 uint64_t or_splitmix64(uint64_t *state);

@@ -20,8 +20,11 @@ LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 
 # QuantType codes shared with include/jkb200.h (GGML type ids where one exists).
 Q4_0, Q8_0, Q4_K, Q6_K, TQ1_0, TQ2_0, I2_S = 2, 8, 12, 14, 34, 35, 36
+Q4_1, IQ4_NL = 3, 20
 BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210),
-         TQ1_0: (256, 54), TQ2_0: (256, 66), I2_S: (128, 32)}
+         TQ1_0: (256, 54), TQ2_0: (256, 66), I2_S: (128, 32), Q4_1: (32, 20), IQ4_NL: (32, 18)}
+NIBBLE = (Q4_0, Q4_1, IQ4_NL, Q4_K)  # PackedNibbleMatrix formats (repack.rs:4231-4236)
+NIBBLE_MINS = (Q4_1, Q4_K)
 ACT_IS_Q8K = {Q4_0: False, Q8_0: False, Q4_K: True, Q6_K: True, TQ1_0: True, TQ2_0: True}
 
 # quant_q8.rs:37-44 and :62-71
@@ -77,6 +80,11 @@ def lib() -> C.CDLL:
             "or_quantize_weights": (I, [I, P, S, S, P]),
             "or_pack_ternary": (I, [I, P, S, S, F, P]),
             "or_weight_bytes": (S, [I, S, S]),
+            "or_nibble_supported": (I, [I]),
+            "or_nibble_pack_tiles": (I, [I, P, S, S, S, P, P, P, P]),
+            "or_nibble_decode_tiles": (I, [I, S, S, P, P, P, P, P, P, P]),
+            "or_nibble_dequantize_row": (I, [I, P, P, P, S, S, P]),
+            "or_gemm_nibble": (I, [P, I, P, P, P, S, S, P, P, P, S, S, S, I]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -247,4 +255,55 @@ def gemm_repacked(quant, wq, ws, wm, rows, cols, xq, xs, xsum, xs16, m, row_begi
     assert lib().or_gemm_repacked(_p(out), quant, _p(wq), _p(ws), _p(wm), rows, cols, _p(xq),
                                   _p(xs), _p(xsum), _p(xs16), m, row_begin, row_end,
                                   nthreads) == 0
+    return out
+
+
+# ---- compact nibble matrices (PackedNibbleMatrix) ----
+
+def nibble_pack_tiles(quant, raw, rows, cols):
+    """The reference's tile layout (repack_nibble_into_tile_range): (tiles u8 [n_tiles*kb*128],
+    scales_f16 or None, mins_f16 or None, headers u8 [n_tiles*(cols/256)*8*16] or None)."""
+    nt, kb = (rows + 7) // 8, cols // 32
+    tiles = np.zeros(nt * kb * 128, np.uint8)
+    sc = mn = hd = None
+    if quant == Q4_K:
+        hd = np.zeros(nt * (cols // 256) * 8 * 16, np.uint8)
+    else:
+        sc = np.zeros(nt * kb * 8, np.uint16)
+        if quant == Q4_1:
+            mn = np.zeros(nt * kb * 8, np.uint16)
+    raw = np.ascontiguousarray(raw, np.uint8)
+    assert lib().or_nibble_pack_tiles(quant, _p(raw), raw.size, rows, cols, _p(tiles), _p(sc),
+                                      _p(mn), _p(hd)) == 0
+    return tiles, sc, mn, hd
+
+
+def nibble_decode_tiles(quant, rows, cols, tiles, sc, mn, hd):
+    """decode_tile_scales + unpack_nibble_tile_to_chunks, row-major: (q [rows][cols] i8,
+    ws [rows][cols/32], wm [rows][cols/32] or None)."""
+    kb = cols // 32
+    q = np.zeros((rows, cols), np.int8)
+    ws = np.zeros((rows, kb), np.float32)
+    wm = np.zeros((rows, kb), np.float32) if quant in NIBBLE_MINS else None
+    assert lib().or_nibble_decode_tiles(quant, rows, cols, _p(tiles), _p(sc), _p(mn), _p(hd),
+                                        _p(q), _p(ws), _p(wm)) == 0
+    return q, ws, wm
+
+
+def nibble_decode(quant, raw, rows, cols):
+    return nibble_decode_tiles(quant, rows, cols, *nibble_pack_tiles(quant, raw, rows, cols))
+
+
+def nibble_dequantize_row(quant, q, ws, wm, cols, row):
+    out = np.zeros(cols, np.float32)
+    assert lib().or_nibble_dequantize_row(quant, _p(q), _p(ws), _p(wm), cols, row, _p(out)) == 0
+    return out
+
+
+def gemm_nibble(quant, q, ws, wm, rows, cols, xq, xs, xsum, m, row_begin=0, row_end=None,
+                nthreads=1):
+    row_end = rows if row_end is None else row_end
+    out = np.zeros((m, row_end - row_begin), np.float32)
+    assert lib().or_gemm_nibble(_p(out), quant, _p(q), _p(ws), _p(wm), rows, cols, _p(xq),
+                                _p(xs), _p(xsum), m, row_begin, row_end, nthreads) == 0
     return out

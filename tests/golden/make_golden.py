@@ -94,6 +94,19 @@ def kats():
              "q": 0},
             {"name": "tiny", "input": "const:1e-20", "weight": "ones", "q": 0},
         ]}
+    # quant.rs:2836-2853: Q4_1 d = 0.5, m = -0.25, bytes 0xF0 -> lo nibble 0 gives -0.25, hi
+    # nibble 15 gives 7.25; a zero d with m = -0.5 dequantizes to -0.5 everywhere.
+    out["q4_1_dequant"] = {"ref": "src/quant.rs:2836-2853",
+                           "cases": [{"block_hex": (h16(0x3800) + h16(0xB400) +
+                                                    bytes([0xF0] * 16)).hex(),
+                                      "lo": -0.25, "hi": 7.25},
+                                     {"block_hex": (h16(0x0000) + h16(0xB800) + bytes(16)).hex(),
+                                      "lo": -0.5, "hi": -0.5}]}
+    # quant.rs:2895-2905: IQ4_NL d = 1.0, qs[0] = 0xF0, qs[1] = 0x08 -> out[0] = -127,
+    # out[16] = 113, out[1] = 1, out[17] = -127.
+    out["iq4_nl_dequant"] = {"ref": "src/quant.rs:2895-2905",
+                             "block_hex": (h16(0x3C00) + bytes([0xF0, 0x08]) + bytes(14)).hex(),
+                             "expect": {"0": -127.0, "16": 113.0, "1": 1.0, "17": -127.0}}
     # quant_q8.rs:3414-3482: quantizer sanitization on test_f32_row inputs.
     out["q8_sanitize"] = {"ref": "src/quant_q8.rs:3388-3395,3414-3482"}
     return out
@@ -135,6 +148,19 @@ def fixtures():
         data[f"{name}__summins"] = summins
         data[f"{name}__contrib"] = contrib
         data[f"{name}__y"] = y
+    # compact nibble GEMM (PackedNibbleMatrix) of the formats without a GEMV here: weights,
+    # activation and the oracle's output
+    for name, q, rows, cols, m in (("nib_q4_1", O.Q4_1, 13, 256, 5),
+                                   ("nib_iq4_nl", O.IQ4_NL, 11, 512, 3)):
+        seed = sum(map(ord, name))
+        w = O.quantize_weights(q, O.normal(rows * cols, 0x5EED0000 + seed, 0.02), rows, cols)
+        x = O.normal(m * cols, 0xAC70000 + seed, 1.0)
+        xq, xs, xsum, _, _ = O.act_q8_quantize(x, m, cols)
+        nq, ws, wm = O.nibble_decode(q, w, rows, cols)
+        data[f"{name}__nmeta"] = np.array([q, rows, cols, m], np.int64)
+        data[f"{name}__w"] = w
+        data[f"{name}__x"] = x
+        data[f"{name}__out"] = O.gemm_nibble(q, nq, ws, wm, rows, cols, xq, xs, xsum, m)
     return data
 
 

@@ -165,3 +165,38 @@ def gemv_tolerance_ok(got, oracle_out, contrib, rel=1e-5):
     bound = rel * np.abs(np.asarray(contrib, np.float64)).sum(axis=-1) + 1.2e-38
     ok = np.abs(got - ref) <= bound
     return bool(ok.all()), float(np.max(np.abs(got - ref) / bound))
+
+
+def small_f32(i, modulo, offset, scale):
+    """tests/wave3_prefill_gqa_and_gemm.rs:17-20, vectorised over an index array."""
+    return ((np.asarray(i) % modulo).astype(np.float32) - np.float32(offset)) * np.float32(scale)
+
+
+def fill_pseudo_quant_tensor(quant, rows, cols):
+    """tests/wave3_prefill_gqa_and_gemm.rs:22-100 (the nibble formats and Q8_0): block b of the
+    flattened tensor gets fixed scale bits and index-derived payload bytes."""
+    be, bb = {2: (32, 18), 20: (32, 18), 3: (32, 20), 12: (256, 144), 8: (32, 34)}[quant]
+    nblk = rows * cols // be
+    b = np.arange(nblk)[:, None]
+    out = np.zeros((nblk, bb), np.uint8)
+    if quant == 8:
+        out[:, 0:2] = [0x00, 0x34]
+        k = np.arange(32)[None, :]
+        out[:, 2:] = (((b * 7 + k * 5) % 21) - 10).astype(np.int8).view(np.uint8)
+    elif quant in (2, 20):
+        out[:, 0:2] = [0x00, 0x38]
+        k = np.arange(16)[None, :]
+        out[:, 2:] = (((b + k * 3) & 0x0F) | (((b * 3 + k * 5 + 1) & 0x0F) << 4)).astype(np.uint8)
+    elif quant == 3:
+        out[:, 0:2] = [0x00, 0x38]
+        out[:, 2:4] = [0x00, 0x34]
+        k = np.arange(16)[None, :]
+        out[:, 4:] = (((b + k * 3) & 0x0F) | (((b * 5 + k + 2) & 0x0F) << 4)).astype(np.uint8)
+    else:
+        out[:, 0:2] = [0x00, 0x34]
+        out[:, 2:4] = [0x00, 0x30]
+        k = np.arange(12)[None, :]
+        out[:, 4:16] = ((b * 5 + k * 3 + 1) & 0x3F).astype(np.uint8)
+        k = np.arange(128)[None, :]
+        out[:, 16:] = ((b * 7 + k * 11 + 3) & 0xFF).astype(np.uint8)
+    return out.reshape(-1)

@@ -239,7 +239,7 @@ def test_wave4_k_quants_ternary_rel_err(oracle, k):
 def test_golden_fixtures_match_live_oracle(oracle):
     """The committed oracle fixtures are reproduced bit for bit by the current oracle."""
     f = np.load(os.path.join(GOLDEN, "oracle_fixtures.npz"))
-    names = sorted({k.split("__")[0] for k in f.files})
+    names = sorted({k.split("__")[0] for k in f.files if k.endswith("__meta")})
     assert len(names) >= 9
     for name in names:
         q, rows, cols = (int(v) for v in f[f"{name}__meta"])
@@ -296,3 +296,120 @@ def test_repack_lossless_and_gemm_rows_stitch(oracle, quant):
     ref = oracle.dequantize_rows(quant, w, rows, cols).astype(np.float64) @ \
         act.reshape(m, cols).astype(np.float64).T
     assert R.cosine(full.reshape(-1), ref.T.reshape(-1)) > 0.9995
+
+
+# ---------------------------------------------------------------- compact nibble matrices
+
+def test_q4_1_iq4_nl_dequant_kats(oracle, kats):
+    """quant.rs:2836-2853 (Q4_1, including a zero d with a non-zero min) and :2895-2905
+    (IQ4_NL code book)."""
+    for c in kats["q4_1_dequant"]["cases"]:
+        d = oracle.dequantize_block(oracle.Q4_1, _u8(c["block_hex"]))
+        assert np.allclose(d[:16], c["lo"], atol=1e-6) and np.allclose(d[16:], c["hi"], atol=1e-6)
+    k = kats["iq4_nl_dequant"]
+    d = oracle.dequantize_block(oracle.IQ4_NL, _u8(k["block_hex"]))
+    for idx, v in k["expect"].items():
+        assert abs(d[int(idx)] - v) < 1e-6, (idx, d[int(idx)])
+
+
+def _q4_0_kat_tensor(rows, cols):
+    """repack.rs:5902-5918: Q4_0 d = 0.5 and an index-derived nibble pattern."""
+    nb = cols // 32
+    raw = np.zeros((rows, nb, 18), np.uint8)
+    raw[..., 0:2] = [0x00, 0x38]
+    r = np.arange(rows)[:, None, None]
+    b = np.arange(nb)[None, :, None]
+    i = np.arange(16)[None, None, :]
+    raw[..., 2:] = (((r + i + b * 3) & 0x0F) | (((r * 3 + i + 5) & 0x0F) << 4)).astype(np.uint8)
+    return raw.reshape(-1)
+
+
+def test_nibble_q4_0_footprint_dequant_and_gemm_kat(oracle):
+    """repack.rs:5899-5988 (wave3_packed_nibble_footprint_and_gemm_parity): the tile layout is
+    exactly the GGUF size, dequantize_row reproduces the Q4_0 dequantizer, and the nibble GEMM
+    tracks the f32 dot product of the dequantized row and the activation."""
+    rows, cols, m = 16, 64, 4
+    raw = _q4_0_kat_tensor(rows, cols)
+    tiles, sc, mn, hd = oracle.nibble_pack_tiles(oracle.Q4_0, raw, rows, cols)
+    assert tiles.nbytes + sc.nbytes == raw.nbytes
+    q, ws, wm = oracle.nibble_decode_tiles(oracle.Q4_0, rows, cols, tiles, sc, mn, hd)
+    deq = oracle.dequantize_rows(oracle.Q4_0, raw, rows, cols).reshape(rows, cols)
+    for r in range(rows):
+        row = oracle.nibble_dequantize_row(oracle.Q4_0, q, ws, wm, cols, r)
+        assert np.array_equal(row, deq[r])
+    x = ((np.arange(m * cols) % 19).astype(np.float32) - 9.0) * 0.25
+    xq, xs, xsum, xs16, _ = oracle.act_q8_quantize(x, m, cols)
+    out = oracle.gemm_nibble(oracle.Q4_0, q, ws, wm, rows, cols, xq, xs, xsum, m)
+    ref = x.reshape(m, cols) @ deq.T
+    assert np.all(np.abs(out - ref) < 0.05 * np.maximum(np.abs(ref), 1.0) + 0.25)
+    rq, rs, rm = oracle.repack_block_scaled(oracle.Q4_0, raw, rows, cols)
+    rep = oracle.gemm_repacked(oracle.Q4_0, rq, rs, rm, rows, cols, xq, xs, xsum, xs16, m)
+    assert np.all(np.abs(out - rep) < 1e-4)
+
+
+@pytest.mark.parametrize("quant", [2, 3, 20, 12])
+def test_nibble_all_formats_match_repacked(oracle, quant):
+    """tests/wave3_prefill_gqa_and_gemm.rs:233-279: every nibble format (Q4_0, Q4_1, IQ4_NL,
+    Q4_K_M) at [256, 512] on the suite's pseudo-quant tensors: the tile layout is exactly the
+    GGUF size and the nibble GEMM equals the repacked GEMM (the suite allows 1e-4; the
+    arithmetic is identical, so the oracle's two paths agree bit for bit)."""
+    rows, cols, m = 256, 512, 17
+    raw = R.fill_pseudo_quant_tensor(quant, rows, cols)
+    tiles, sc, mn, hd = oracle.nibble_pack_tiles(quant, raw, rows, cols)
+    meta = sum(a.nbytes for a in (sc, mn, hd) if a is not None)
+    assert tiles.nbytes + meta == raw.nbytes
+    q, ws, wm = oracle.nibble_decode_tiles(quant, rows, cols, tiles, sc, mn, hd)
+    x = np.float32(0.5) + R.small_f32(np.arange(m * cols), 13, 5.0, 0.25)
+    xq, xs, xsum, xs16, _ = oracle.act_q8_quantize(x, m, cols)
+    out = oracle.gemm_nibble(quant, q, ws, wm, rows, cols, xq, xs, xsum, m, nthreads=4)
+    rq, rs, rm = oracle.repack_block_scaled(quant, raw, rows, cols)
+    rep = oracle.gemm_repacked(quant, rq, rs, rm, rows, cols, xq, xs, xsum, xs16, m, nthreads=4)
+    assert np.all(np.abs(out - rep) < 1e-4)
+    assert np.array_equal(out.view(np.uint32), rep.view(np.uint32))
+    # the decoded nibble matrix reproduces the block dequantizer row by row
+    deq = oracle.dequantize_rows(quant, raw, rows, cols).reshape(rows, cols)
+    for r in (0, 7, 8, 255):
+        assert np.array_equal(oracle.nibble_dequantize_row(quant, q, ws, wm, cols, r), deq[r])
+
+
+def test_nibble_unaligned_rows_footprint(oracle):
+    """tests/wave3_prefill_gqa_and_gemm.rs:270-278: 203 Q4_K_M rows (tiles of 8 rows pad to
+    208) stay within 1.05x of the GGUF bytes."""
+    rows, cols = 203, 512
+    raw = R.fill_pseudo_quant_tensor(12, rows, cols)
+    tiles, _, _, hd = oracle.nibble_pack_tiles(12, raw, rows, cols)
+    assert (tiles.nbytes + hd.nbytes) * 100 <= raw.nbytes * 105
+
+
+def test_nibble_zero_scale_blocks(oracle):
+    """repack.rs:4458-4500: Q4_0 / IQ4_NL blocks whose scale decodes to zero (0, NaN, Inf) keep
+    zero scale bits and zero nibbles in the tiles; they contribute nothing to the GEMM."""
+    rows, cols = 9, 64
+    for quant in (2, 20):
+        raw = R.fill_pseudo_quant_tensor(quant, rows, cols).reshape(rows, 2, 18).copy()
+        raw[1, 0, 0:2] = [0x00, 0x7C]  # +Inf
+        raw[4, 1, 0:2] = [0x01, 0x7E]  # NaN
+        raw[8, 0, 0:2] = [0x00, 0x00]  # 0
+        raw = raw.reshape(-1)
+        tiles, sc, _, _ = oracle.nibble_pack_tiles(quant, raw, rows, cols)
+        assert sc.reshape(2, 2, 8)[0, 0, 1] == 0 and sc.reshape(2, 2, 8)[0, 1, 4] == 0
+        assert sc.reshape(2, 2, 8)[1, 0, 0] == 0
+        q, ws, wm = oracle.nibble_decode_tiles(quant, rows, cols, tiles, sc, None, None)
+        zero = oracle.Q4_0 == quant and -8 or -127
+        assert np.all(q[1, 0:32] == zero) and np.all(q[4, 32:64] == zero)
+        assert ws[1, 0] == 0.0 and ws[4, 1] == 0.0 and ws[8, 0] == 0.0
+        deq = oracle.dequantize_rows(quant, raw, rows, cols).reshape(rows, cols)
+        assert np.all(deq[1, 0:32] == 0.0)
+
+
+def test_nibble_golden_fixtures_match_live_oracle(oracle):
+    """The committed nibble GEMM fixtures (Q4_1, IQ4_NL) are reproduced bit for bit."""
+    f = np.load(os.path.join(GOLDEN, "oracle_fixtures.npz"))
+    names = sorted({k.split("__")[0] for k in f.files if k.endswith("__nmeta")})
+    assert len(names) == 2
+    for name in names:
+        q, rows, cols, m = (int(v) for v in f[f"{name}__nmeta"])
+        xq, xs, xsum, _, _ = oracle.act_q8_quantize(f[f"{name}__x"], m, cols)
+        nq, ws, wm = oracle.nibble_decode(q, f[f"{name}__w"], rows, cols)
+        out = oracle.gemm_nibble(q, nq, ws, wm, rows, cols, xq, xs, xsum, m)
+        assert np.array_equal(out.view(np.uint32), f[f"{name}__out"].view(np.uint32))
