@@ -614,6 +614,20 @@ def run_prefill_gemm(world, rank, launches=10):
         res[key] = {"m": m, "n": n, "k": k, "us": round(us, 2),
                     "tops": round(2.0 * m * n * k / (us * 1e-6) / 1e12, 1)}
         w.destroy()
+    # the same Q4_K_M weights as a PackedNibbleMatrix: 4-bit codes on the device (the GGUF
+    # bytes), expanded to int8 in shared memory by the kernel's converter warps
+    raw = synth_matrix(Q4_K, n, k, 4250, rank * per, (rank + 1) * per)
+    nm = jkb.PackedNibbleMatrix.from_tensor(jkb.TensorView("nibble", Q4_K, [k, per], raw), per, k)
+    us = _graph_time(lambda: nm.gemm(out, act), launches)
+    if world > 1:
+        t = torch.tensor([us], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item())
+    res["nibble_q4_k_m"] = {"m": m, "n": n, "k": k, "us": round(us, 2),
+                            "tops": round(2.0 * m * n * k / (us * 1e-6) / 1e12, 1),
+                            "device_bytes": nm.packed_bytes(),
+                            "i8_repacked_device_bytes": per * k + 2 * per * (k // 32) * 4}
+    nm.destroy()
     del act, out, x
     res["tops"] = round(tot_ops[False] / (tot_us[False] * 1e-6) / 1e12, 1)
     res["exact_tops"] = round(tot_ops[True] / (tot_us[True] * 1e-6) / 1e12, 1)

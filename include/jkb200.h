@@ -52,9 +52,11 @@ typedef enum {
     JKB_F32 = 0,
     JKB_F16 = 1,
     JKB_Q4_0 = 2,
+    JKB_Q4_1 = 3, /* compact nibble matrices only */
     JKB_Q8_0 = 8,
     JKB_Q4_K_M = 12,
     JKB_Q6_K = 14,
+    JKB_IQ4_NL = 20, /* compact nibble matrices only */
     JKB_BF16 = 30,
     JKB_TQ1_0 = 34,
     JKB_TQ2_0 = 35,
@@ -341,6 +343,71 @@ int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight 
  * writes every scratch value it reads, so results never depend on an earlier call. */
 int jkb_gemm_repacked_f32_noalloc(float *out, size_t out_len, const jkb_repacked_weight *w,
                                   const float *input, size_t in_len, size_t m, void *stream);
+
+/* ---- PackedNibbleMatrix: compact 4-bit weights and their GEMM (repack.rs:4188-5545) ----
+ * Q4_0, Q4_1, IQ4_NL and Q4_K_M weights stay 4-bit on the device: the handle holds each row's
+ * GGUF quant bytes and block scales (exactly the GGUF payload size), and the GEMM expands the
+ * codes to int8 in shared memory. Results are those of execute_nibble_gemm_rows
+ * (repack.rs:5181-5397): per output, 32-element blocks in K order, acc += (f32)c * (xs * ws)
+ * [- x_sum * wm]. Batches of at least 32 tokens with cols a multiple of 128 run on the tensor
+ * cores (default: fused multiply-add per block, within 1e-5 relative; jkb_gemm_set_exact(1):
+ * bit-identical); smaller batches and other shapes run a bit-identical row kernel. */
+typedef struct jkb_nibble_matrix jkb_nibble_matrix;
+/* repack.rs:4788 PackedNibbleMatrix::from_tensor (explicit [rows, cols]) */
+int jkb_packed_nibble_matrix_from_tensor(const jkb_tensor_view *view, size_t rows, size_t cols,
+                                         void *stream, jkb_nibble_matrix **out);
+/* repack.rs:4654 PackedNibbleMatrix::repack (orientation inferred) */
+int jkb_packed_nibble_matrix_repack(const jkb_tensor_view *view, void *stream,
+                                    jkb_nibble_matrix **out);
+/* repack.rs:4686 PackedNibbleMatrix::from_scale_f16_buffers (Q4_0 / IQ4_NL) and :4743
+ * from_q4_k_buffers: host buffers in the reference's tile layout -- nibble_tiles
+ * [n_tiles][cols / 32] x 128 bytes (n_tiles = ceil(rows / 8)), scales_f16 [n_tiles][cols / 32][8],
+ * headers [n_tiles][cols / 256][8] x 16 bytes; counts are in tiles, scales and headers. */
+int jkb_packed_nibble_matrix_from_scale_f16_buffers(int32_t quant, size_t rows, size_t cols,
+                                                    const uint8_t *nibble_tiles, size_t n_tiles,
+                                                    const uint16_t *scales_f16, size_t n_scales,
+                                                    void *stream, jkb_nibble_matrix **out);
+int jkb_packed_nibble_matrix_from_q4_k_buffers(size_t rows, size_t cols,
+                                               const uint8_t *nibble_tiles, size_t n_tiles,
+                                               const uint8_t *headers, size_t n_headers,
+                                               void *stream, jkb_nibble_matrix **out);
+/* repack.rs:4414 repack_nibble_into_tile_range, on the host: tiles tile_begin..tile_end of the
+ * reference's layout (the input of the two constructors above). Output lengths are counts:
+ * n_out_tiles = tiles * (cols / 32), n_scales = n_mins = tiles * (cols / 32) * 8 (Q4_0 and
+ * IQ4_NL scales; Q4_1 scales and mins), n_headers = tiles * (cols / 256) * 8 (Q4_K_M). Unused
+ * outputs may be NULL with count 0. The view's bytes must be host memory. */
+int jkb_repack_nibble_into_tile_range(const jkb_tensor_view *view, size_t rows, size_t cols,
+                                      size_t tile_begin, size_t tile_end, uint8_t *out_tiles,
+                                      size_t n_out_tiles, uint16_t *out_scales_f16,
+                                      size_t n_scales, uint16_t *out_mins_f16, size_t n_mins,
+                                      uint8_t *out_headers, size_t n_headers);
+int jkb_packed_nibble_matrix_destroy(jkb_nibble_matrix *w);
+/* rows, cols, quant, n_tiles (rows.div_ceil(8)), k_blocks32, packed_bytes (device bytes of the
+ * codes and scales; equal to raw_tensor_bytes), raw_tensor_bytes (GGUF size) */
+int jkb_packed_nibble_matrix_info(const jkb_nibble_matrix *w, size_t *rows, size_t *cols,
+                                  int32_t *quant, size_t *n_tiles, size_t *k_blocks32,
+                                  size_t *packed_bytes, size_t *raw_tensor_bytes);
+/* Device views: qs [rows][cols / 2] code bytes, meta [rows][blocks] scale words. */
+int jkb_packed_nibble_matrix_buffers(const jkb_nibble_matrix *w, uint8_t **qs, uint8_t **meta);
+/* repack.rs:4945 gemm: out [act.m][rows] */
+int jkb_packed_nibble_matrix_gemm(float *out, size_t out_len, const jkb_nibble_matrix *w,
+                                  const jkb_act_q8 *act, void *stream);
+/* repack.rs:4954 gemm_rows: out [act.m][row_end - row_begin] */
+int jkb_packed_nibble_matrix_gemm_rows(float *out, size_t out_len, const jkb_nibble_matrix *w,
+                                       const jkb_act_q8 *act, size_t row_begin, size_t row_end,
+                                       void *stream);
+/* repack.rs:4968 gemv (act.m must be 1) */
+int jkb_packed_nibble_matrix_gemv(float *out, size_t out_len, const jkb_nibble_matrix *w,
+                                  const jkb_act_q8 *act, void *stream);
+/* repack.rs:5001 dequantize_row: out [cols] f32 (device) */
+int jkb_packed_nibble_matrix_dequantize_row(const jkb_nibble_matrix *w, size_t row, float *out,
+                                            size_t out_len, void *stream);
+/* repack.rs:5140 gemm_q4_0_ime / :5162 gemm_q4_k_ime: the GEMM, CapabilityMismatch unless the
+ * matrix is Q4_0 / Q4_K_M. */
+int jkb_gemm_q4_0_ime(float *out, size_t out_len, const jkb_nibble_matrix *w,
+                      const jkb_act_q8 *act, void *stream);
+int jkb_gemm_q4_k_ime(float *out, size_t out_len, const jkb_nibble_matrix *w,
+                      const jkb_act_q8 *act, void *stream);
 
 /* ---- multi-GPU output-row sharding: a one-kernel all-gather over NVLink (no reference
  * counterpart; the reference splits work by row ranges, gemv_repacked_rows repack.rs:4014) ----

@@ -66,6 +66,8 @@ const char *quant_name(int quant) {
     case JKB_F32: return "F32";
     case JKB_F16: return "F16";
     case JKB_BF16: return "BF16";
+    case JKB_Q4_1: return "Q4_1";
+    case JKB_IQ4_NL: return "IQ4_NL";
     default: {
         const Fmt *f = fmt_of(quant);
         return f ? f->name : "Unknown";

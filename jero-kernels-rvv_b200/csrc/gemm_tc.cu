@@ -49,6 +49,7 @@
 #include <cstdio>
 
 #include "jkb_internal.h"
+#include "nibble.cuh"
 
 namespace jkb {
 
@@ -59,32 +60,46 @@ constexpr int BK = 128;   // K bytes per stage
 constexpr int GPS = 4;    // scale groups per stage
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
-template <int BN_, int WPQ_, int GPR_, bool EXACT_, bool MINS_ = false, bool H16_ = false>
+template <int BN_, int WPQ_, int GPR_, bool EXACT_, bool MINS_ = false, bool H16_ = false,
+          int NIB_ = NIB_NONE>
 struct TcCfg {
     static constexpr int BN = BN_, WPQ = WPQ_, GPR = GPR_;
     static constexpr bool EXACT = EXACT_;
-    // MINS: groups carry a min term (Q4_K_M): acc += c * (xs * ws) - x_sum * wm
+    // MINS: groups carry a min term (Q4_K_M, Q4_1): acc += c * (xs * ws) - x_sum * wm
     static constexpr bool MINS = MINS_;
     // H16: 16-element weight scale groups (Q6_K). The int8 MMA sums 32 elements, so a masking
     // warp writes two copies of each token tile with alternate 16-byte halves of K zeroed, and
     // every 32-element slice takes two MMAs (even and odd half-groups) into two accumulators.
     static constexpr bool H16 = H16_;
+    // NIB: the weight tile arrives as 4-bit codes (a jkb_nibble_matrix, format NibFmt) and two
+    // converter warps write its int8 values into the MMA's operand tile and its scales (and
+    // mins) into the epilogue's scale tiles.
+    static constexpr int NIB = NIB_;
+    static constexpr int CONV = NIB ? 2 : 0;   // converter warps
     static constexpr int SPL = H16 ? 2 : 1;    // accumulators per 32-element slice
     static constexpr int NA = GPR * SPL;       // accumulators per round
     static constexpr int NG = GPS * SPL;       // weight-scale groups per stage
     static constexpr int COLS = BN / WPQ;  // token columns per epilogue thread
     static constexpr int EPI = 4 * WPQ;    // epilogue warps
-    static constexpr int THREADS = (2 + EPI + (H16 ? 1 : 0)) * 32;
+    static constexpr int THREADS = (2 + EPI + (H16 ? 1 : 0) + CONV) * 32;
     // TMEM: two round buffers of GPR group accumulators (BN int32 columns each)
     static constexpr int TMEM_COLS = 512;
     static constexpr int SA = BMW * BK, SB = BN * BK;  // operand bytes per stage
-    static constexpr int STAGE_TX = SA + SB + BMW * NG * 4 + GPS * BN * 4 +
-                                    (MINS ? BMW * GPS * 4 + GPS * BN * 4 : 0);
-    static constexpr int STAGES_FIT = (200 * 1024) / (STAGE_TX + (H16 ? 2 * SB : 0));
+    static constexpr int SAN = NIB ? BMW * BK / 2 : 0;  // 4-bit weight tile bytes per stage
+    // bytes the TMA brings per stage (weight tile or its 4-bit codes, token tile, scale tiles
+    // the TMA loads) and the stage's shared-memory footprint
+    static constexpr int STAGE_TX =
+        NIB ? SAN + SB + GPS * BN * 4 + (MINS ? GPS * BN * 4 : 0)
+            : SA + SB + BMW * NG * 4 + GPS * BN * 4 + (MINS ? BMW * GPS * 4 + GPS * BN * 4 : 0);
+    static constexpr int STAGE_SMEM =
+        STAGE_TX + (H16 ? 2 * SB : 0) + (NIB ? SA + BMW * NG * 4 + (MINS ? BMW * GPS * 4 : 0) : 0);
+    static constexpr int STAGES_FIT = (200 * 1024) / STAGE_SMEM;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static_assert((COLS == 32 || COLS == 64) && BN % 32 == 0 && BN <= 256, "tile shape");
     static_assert(GPS % GPR == 0 && 2 * NA * BN <= TMEM_COLS, "two rounds of NA buffers");
     static_assert(!(H16 && MINS), "16-element groups carry no mins");
+    static_assert(!(H16 && NIB), "nibble formats use 32-element groups");
+    static_assert(!NIB || MINS == (NIB == NIB_Q4_1 || NIB == NIB_Q4_K), "nibble min terms");
 };
 
 template <class C>
@@ -93,6 +108,7 @@ struct TcSmem {
     uint8_t b[C::STAGES][C::SB];  // token tiles
     uint8_t blo[C::H16 ? C::STAGES : 1][C::H16 ? C::SB : 1024];  // H16: odd 16-byte halves zeroed
     uint8_t bhi[C::H16 ? C::STAGES : 1][C::H16 ? C::SB : 1024];  // H16: even 16-byte halves zeroed
+    uint8_t an[C::NIB ? C::STAGES : 1][C::NIB ? C::SAN : 1024];  // NIB: 4-bit codes [128][64]
     float ws[C::STAGES][BMW][C::NG];
     float xs[C::STAGES][GPS][C::BN];
     float wm[C::MINS ? C::STAGES : 1][BMW][GPS];     // weight mins (MINS)
@@ -241,7 +257,8 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                    const __grid_constant__ CUtensorMap tmWS, const __grid_constant__ CUtensorMap tmXS,
                    const __grid_constant__ CUtensorMap tmWM, const __grid_constant__ CUtensorMap tmXN,
                    int M, int G, int row_begin, int sub_n, int tiles_w, int tiles_t,
-                   float *__restrict__ out, int *err) {
+                   float *__restrict__ out, int *err, const uint8_t *__restrict__ nmeta,
+                   int nmeta_nb, int w_rows) {
     constexpr int BN = C::BN, STAGES = C::STAGES, GPR = C::GPR, EPI = C::EPI, COLS = C::COLS;
     constexpr int NA = C::NA, SPL = C::SPL;
     extern __shared__ uint8_t smem_raw[];
@@ -256,7 +273,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         for (int i = 0; i < STAGES; i++) {
             mbar_init(&sm.full[i], 1);
             mbar_init(&sm.empty[i], 1 + EPI);  // the MMA commit and every epilogue warp
-            mbar_init(&sm.masked[i], 1);
+            mbar_init(&sm.masked[i], C::CONV ? C::CONV : 1);  // masking or converter warps
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&sm.tfull[i], 1);
@@ -295,12 +312,17 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                         break;
                     }
                     mbar_arrive_tx(&sm.full[s], C::STAGE_TX);
-                    tma_load_2d(sm.a[s], &tmW, &sm.full[s], ks * BK, wrow);
+                    if (C::NIB)
+                        tma_load_2d(sm.an[C::NIB ? s : 0], &tmW, &sm.full[s], ks * (BK / 2), wrow);
+                    else
+                        tma_load_2d(sm.a[s], &tmW, &sm.full[s], ks * BK, wrow);
                     tma_load_2d(sm.b[s], &tmX, &sm.full[s], ks * BK, tok);
-                    tma_load_2d(&sm.ws[s][0][0], &tmWS, &sm.full[s], ks * C::NG, wrow);
+                    if (!C::NIB)
+                        tma_load_2d(&sm.ws[s][0][0], &tmWS, &sm.full[s], ks * C::NG, wrow);
                     tma_load_2d(&sm.xs[s][0][0], &tmXS, &sm.full[s], tok, ks * GPS);
                     if (C::MINS) {
-                        tma_load_2d(&sm.wm[s][0][0], &tmWM, &sm.full[s], ks * GPS, wrow);
+                        if (!C::NIB)
+                            tma_load_2d(&sm.wm[s][0][0], &tmWM, &sm.full[s], ks * GPS, wrow);
                         tma_load_2d(&sm.xn[s][0][0], &tmXN, &sm.full[s], tok, ks * GPS);
                     }
                 }
@@ -324,8 +346,8 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
                 for (int ks = 0; ks < kstages && ok; ks++, it++) {
                     const int s = it % STAGES;
-                    if (!mbar_wait(C::H16 ? &sm.masked[s] : &sm.full[s], (it / STAGES) & 1,
-                                   abort_flag, err)) {
+                    if (!mbar_wait((C::H16 || C::NIB) ? &sm.masked[s] : &sm.full[s],
+                                   (it / STAGES) & 1, abort_flag, err)) {
                         ok = false;
                         break;
                     }
@@ -389,6 +411,115 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                 if (lane == 0) mbar_arrive(&sm.masked[s]);
             }
         }
+    } else if (C::NIB && warp >= 2 + EPI) {
+        // ------------------------------------------------ converter warps (NIB)
+        // Converter cw takes weight rows 64cw .. 64cw + 63 of the tile. Per stage it writes the
+        // int8 values of its rows' 4-bit codes into the operand tile (the layout the TMA's
+        // 128-byte swizzle would give: 16-byte unit u of row r at 16 * (u ^ (r & 7))) and the
+        // rows' scales (and mins) into ws / wm. The scale words of the next stage are loaded
+        // while this one converts.
+        const int cw = warp - (2 + EPI);
+        constexpr int F = C::NIB;
+        const uint32_t *m32 = reinterpret_cast<const uint32_t *>(nmeta);
+        const uint16_t *m16 = reinterpret_cast<const uint16_t *>(nmeta);
+        // meta words of rows 64cw + lane and 64cw + lane + 32 at stage (t, ks)
+        auto load_meta = [&](int t, int ks, uint4 (&mv)[2]) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                mv[h] = make_uint4(0u, 0u, 0u, 0u);
+                if (t >= ntiles) continue;
+                const int row = row_begin + (t / tiles_t) * BMW + 64 * cw + lane + 32 * h;
+                if (row >= w_rows) continue;
+                const size_t rb = (size_t)row * (size_t)nmeta_nb;
+                if (F == NIB_Q4_K) {
+                    mv[h] = __ldg(reinterpret_cast<const uint4 *>(nmeta) + rb + (ks >> 1));
+                } else if (F == NIB_Q4_1) {
+                    mv[h] = __ldg(reinterpret_cast<const uint4 *>(m32 + rb + 4 * ks));
+                } else {
+                    const uint2 v = __ldg(reinterpret_cast<const uint2 *>(m16 + rb + 4 * ks));
+                    mv[h] = make_uint4(v.x, v.y, 0u, 0u);
+                }
+            }
+        };
+        uint32_t it = 0;
+        bool ok = true;
+        uint4 cur[2], nxt[2];
+        load_meta(blockIdx.x, 0, cur);
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            for (int ks = 0; ks < kstages; ks++, it++) {
+                const int s = it % STAGES;
+                if (ks + 1 < kstages)
+                    load_meta(t, ks + 1, nxt);
+                else
+                    load_meta(t + gridDim.x, 0, nxt);
+                if (!mbar_wait(&sm.full[s], (it / STAGES) & 1, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                // scales and mins of the stage's 4 groups
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int r = 64 * cw + lane + 32 * h;
+                    const uint4 v = cur[h];
+                    float4 w4, n4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (F == NIB_Q4_K) {
+                        const float d = nib_f16_finite(v.x & 0xFFFF), dmin = nib_f16_finite(v.x >> 16);
+                        float sw[4], sm4[4];
+#pragma unroll
+                        for (int g = 0; g < 4; g++) {
+                            int sc, mn;
+                            nib_k4_scale_min(v.y, v.z, v.w, 4 * (ks & 1) + g, sc, mn);
+                            sw[g] = __fmul_rn(d, (float)sc);
+                            sm4[g] = __fmul_rn(dmin, (float)mn);
+                        }
+                        w4 = make_float4(sw[0], sw[1], sw[2], sw[3]);
+                        n4 = make_float4(sm4[0], sm4[1], sm4[2], sm4[3]);
+                    } else if (F == NIB_Q4_1) {
+                        w4 = make_float4(nib_f16_finite(v.x), nib_f16_finite(v.y),
+                                         nib_f16_finite(v.z), nib_f16_finite(v.w));
+                        n4 = make_float4(nib_q4_1_min(v.x >> 16), nib_q4_1_min(v.y >> 16),
+                                         nib_q4_1_min(v.z >> 16), nib_q4_1_min(v.w >> 16));
+                    } else {
+                        w4 = make_float4(nib_d_scale(v.x), nib_d_scale(v.x >> 16),
+                                         nib_d_scale(v.y), nib_d_scale(v.y >> 16));
+                    }
+                    *reinterpret_cast<float4 *>(&sm.ws[s][r][0]) = w4;
+                    if (C::MINS) *reinterpret_cast<float4 *>(&sm.wm[C::MINS ? s : 0][r][0]) = n4;
+                }
+                // codes -> int8 values: 64 rows x 4 chunks of 16 bytes, 8 chunks per lane. A
+                // chunk's low nibbles fill unit ulo, its high nibbles unit uhi of the row.
+#pragma unroll 4
+                for (int i = 0; i < 8; i++) {
+                    const int q = lane + 32 * i;
+                    const int r = 64 * cw + (q >> 2), j = q & 3;
+                    const uint4 c = *reinterpret_cast<const uint4 *>(&sm.an[C::NIB ? s : 0][r * 64 + 16 * j]);
+                    const uint4 lo = make_uint4(
+                        nib_values4<F>(c.x & 0x0F0F0F0Fu), nib_values4<F>(c.y & 0x0F0F0F0Fu),
+                        nib_values4<F>(c.z & 0x0F0F0F0Fu), nib_values4<F>(c.w & 0x0F0F0F0Fu));
+                    const uint4 hi = make_uint4(nib_values4<F>((c.x >> 4) & 0x0F0F0F0Fu),
+                                                nib_values4<F>((c.y >> 4) & 0x0F0F0F0Fu),
+                                                nib_values4<F>((c.z >> 4) & 0x0F0F0F0Fu),
+                                                nib_values4<F>((c.w >> 4) & 0x0F0F0F0Fu));
+                    // Q4_K_M chunk j holds elements 64(j/2) + 16(j&1) (low) and + 32 (high);
+                    // the other formats' chunk j is block j: elements 32j (low), 32j + 16 (high)
+                    const int ulo = F == NIB_Q4_K ? 4 * (j >> 1) + (j & 1) : 2 * j;
+                    const int uhi = F == NIB_Q4_K ? ulo + 2 : ulo + 1;
+                    // odd Q4_K_M rows store their high unit first: each 8-lane phase of a
+                    // 16-byte store then covers 8 distinct bank groups
+                    const bool sw = F == NIB_Q4_K && (r & 1);
+                    uint8_t *row = &sm.a[s][r * 128];
+                    const int x = r & 7;
+                    *reinterpret_cast<uint4 *>(row + 16 * ((sw ? uhi : ulo) ^ x)) = sw ? hi : lo;
+                    *reinterpret_cast<uint4 *>(row + 16 * ((sw ? ulo : uhi) ^ x)) = sw ? lo : hi;
+                }
+                // the operand tile is read by the tensor core (async proxy)
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sm.masked[s]);
+                cur[0] = nxt[0];
+                cur[1] = nxt[1];
+            }
+        }
     } else {
         // ------------------------------------------------ epilogue
         // TMEM is read with the 16x256b shape: per load, lane t holds weight rows t/4 and
@@ -410,7 +541,10 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     for (int r = 0; r < 4; r++) acc[cb][h][r][0] = acc[cb][h][r][1] = 0ull;
             for (int ks = 0; ks < kstages && ok; ks++, it++) {
                 const int s = it % STAGES;
-                if (!mbar_wait(&sm.full[s], (it / STAGES) & 1, abort_flag, err)) {
+                // NIB: the token scales come with the TMA (full), the weight scales from the
+                // converter warps (masked)
+                if (!mbar_wait(&sm.full[s], (it / STAGES) & 1, abort_flag, err) ||
+                    (C::NIB && !mbar_wait(&sm.masked[s], (it / STAGES) & 1, abort_flag, err))) {
                     ok = false;
                     break;
                 }
@@ -586,29 +720,30 @@ bool encode_2d(CUtensorMap *tm, CUtensorMapDataType dt, const void *base, uint64
     return r == CUDA_SUCCESS;
 }
 
+// The weight side of one launch: its tensor maps and, for nibble weights, the scale plane the
+// converter warps read.
+struct TcWeight {
+    CUtensorMap tmW, tmWS, tmWM;
+    const uint8_t *nmeta = nullptr;
+    int nmeta_nb = 0;
+    size_t rows = 0, k = 0;
+};
+
 template <class C>
-int launch_tc(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out, size_t row_begin,
-              size_t row_end, cudaStream_t st, int *err) {
-    const size_t kp = w->k_pad, G = kp / 32;
-    CUtensorMap tmW, tmX, tmWS, tmXS, tmWM, tmXN;
-    if (!encode_2d(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->q, kp, w->rows, kp, BK, BMW,
+int launch_tc_common(const TcWeight &wt, const jkb_act_q8 *act, float *out, size_t row_begin,
+                     size_t row_end, cudaStream_t st, int *err) {
+    const size_t kp = wt.k, G = kp / 32;
+    CUtensorMap tmX, tmXS, tmXN;
+    if (!encode_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, act->q, kp, act->m, kp, BK, C::BN,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_2d(&tmX, CU_TENSOR_MAP_DATA_TYPE_UINT8, act->q, kp, act->m, kp, BK, C::BN,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_2d(&tmWS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->scales, G * C::SPL, w->rows,
-                   G * C::SPL * 4, C::NG, BMW, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !encode_2d(&tmXS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act->x_scales_t,
                    (act->m + 31) / 32 * 32, G, act->xt_pitch * 4, C::BN, GPS,
                    CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
-    tmWM = tmWS;
     tmXN = tmXS;
-    if (C::MINS &&
-        (!encode_2d(&tmWM, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->mins, G, w->rows, G * 4, GPS, BMW,
-                    CU_TENSOR_MAP_SWIZZLE_NONE) ||
-         !encode_2d(&tmXN, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act->x_nsums_t,
-                    (act->m + 31) / 32 * 32, G, act->xt_pitch * 4, C::BN, GPS,
-                    CU_TENSOR_MAP_SWIZZLE_NONE)))
+    if (C::MINS && !encode_2d(&tmXN, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act->x_nsums_t,
+                              (act->m + 31) / 32 * 32, G, act->xt_pitch * 4, C::BN, GPS,
+                              CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
     const size_t sub_n = row_end - row_begin;
     const int tiles_w = (int)((sub_n + BMW - 1) / BMW), tiles_t = (int)((act->m + C::BN - 1) / C::BN);
@@ -628,10 +763,46 @@ int launch_tc(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out, s
     }
     const size_t grid = ntiles < (size_t)num_sms() ? ntiles : (size_t)num_sms();
     gemm_tc_kernel<C><<<(unsigned)grid, C::THREADS, smem, st>>>(
-        tmW, tmX, tmWS, tmXS, tmWM, tmXN, (int)act->m, (int)G, (int)row_begin, (int)sub_n, tiles_w,
-        tiles_t,
-        out, err);
+        wt.tmW, tmX, wt.tmWS, tmXS, wt.tmWM, tmXN, (int)act->m, (int)G, (int)row_begin,
+        (int)sub_n, tiles_w, tiles_t, out, err, wt.nmeta, wt.nmeta_nb, (int)wt.rows);
     return check_launch("gemm_tc_kernel");
+}
+
+// i8 repacked weight: int8 tile, f32 scales (and mins) by TMA.
+template <class C>
+int launch_tc(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out, size_t row_begin,
+              size_t row_end, cudaStream_t st, int *err) {
+    const size_t kp = w->k_pad, G = kp / 32;
+    TcWeight wt;
+    wt.rows = w->rows;
+    wt.k = kp;
+    if (!encode_2d(&wt.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->q, kp, w->rows, kp, BK, BMW,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&wt.tmWS, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->scales, G * C::SPL, w->rows,
+                   G * C::SPL * 4, C::NG, BMW, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
+    wt.tmWM = wt.tmWS;
+    if (C::MINS && !encode_2d(&wt.tmWM, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->mins, G, w->rows,
+                              G * 4, GPS, BMW, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
+    return launch_tc_common<C>(wt, act, out, row_begin, row_end, st, err);
+}
+
+// Nibble weight: the 4-bit code plane by TMA (64 bytes of each of 128 rows per stage, no
+// swizzle), the scale plane read by the converter warps.
+template <class C>
+int launch_tc_nib(const jkb_nibble_matrix *w, const jkb_act_q8 *act, float *out,
+                  size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
+    TcWeight wt;
+    wt.rows = w->rows;
+    wt.k = w->cols;
+    wt.nmeta = w->meta;
+    wt.nmeta_nb = (int)w->nb;
+    if (!encode_2d(&wt.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, w->cols / 2, w->rows,
+                   w->cols / 2, BK / 2, BMW, CU_TENSOR_MAP_SWIZZLE_NONE))
+        return fail(JKB_E_CUDA, "gemm_nibble", 0, 0, 0, "cuTensorMapEncodeTiled failed");
+    wt.tmWS = wt.tmWM = wt.tmW;  // unused
+    return launch_tc_common<C>(wt, act, out, row_begin, row_end, st, err);
 }
 
 }  // namespace
@@ -667,6 +838,10 @@ int choose_tile(size_t m, size_t sub_n, bool mins) {
 template <bool E, bool MN, bool H> using TC64 = TcCfg<64, 2, H ? 2 : 4, E, MN, H>;
 template <bool E, bool MN, bool H> using TC96 = TcCfg<96, 3, H ? 1 : 2, E, MN, H>;
 template <bool E, bool MN, bool H> using TC128 = TcCfg<128, 2, H ? 1 : 2, E, MN, H>;
+
+template <bool E, int NB> using TN64 = TcCfg<64, 2, 4, E, NB == NIB_Q4_1 || NB == NIB_Q4_K, false, NB>;
+template <bool E, int NB> using TN96 = TcCfg<96, 3, 2, E, NB == NIB_Q4_1 || NB == NIB_Q4_K, false, NB>;
+template <bool E, int NB> using TN128 = TcCfg<128, 2, 2, E, NB == NIB_Q4_1 || NB == NIB_Q4_K, false, NB>;
 
 std::atomic<int> g_gemm_exact{0};
 
@@ -713,6 +888,61 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
                      : launch_tc_bn<false, true, false>(bn, w, act, out, row_begin, row_end, st, err);
     return exact ? launch_tc_bn<true, false, false>(bn, w, act, out, row_begin, row_end, st, err)
                  : launch_tc_bn<false, false, false>(bn, w, act, out, row_begin, row_end, st, err);
+}
+
+template <bool EXACT, int NB>
+int launch_nib_bn(int bn, const jkb_nibble_matrix *w, const jkb_act_q8 *act, float *out,
+                  size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
+    switch (bn) {
+        case 64:
+            return launch_tc_nib<TN64<EXACT, NB>>(w, act, out, row_begin, row_end, st, err);
+        case 128:
+            if constexpr (NB == NIB_Q4_1 || NB == NIB_Q4_K)
+                return launch_tc_nib<TN96<EXACT, NB>>(w, act, out, row_begin, row_end, st, err);
+            else
+                return launch_tc_nib<TN128<EXACT, NB>>(w, act, out, row_begin, row_end, st, err);
+        default:
+            return launch_tc_nib<TN96<EXACT, NB>>(w, act, out, row_begin, row_end, st, err);
+    }
+}
+
+template <int NB>
+int launch_nib_fmt(int bn, bool exact, const jkb_nibble_matrix *w, const jkb_act_q8 *act,
+                   float *out, size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
+    return exact ? launch_nib_bn<true, NB>(bn, w, act, out, row_begin, row_end, st, err)
+                 : launch_nib_bn<false, NB>(bn, w, act, out, row_begin, row_end, st, err);
+}
+
+// Tensor-core path of the compact nibble GEMM: taken for batches of at least TC_MIN_M tokens
+// with K a multiple of 128 (the stage depth); *used reports whether it ran.
+int gemm_tc_nibble_launch(const jkb_nibble_matrix *w, const jkb_act_q8 *act, float *out,
+                          size_t row_begin, size_t row_end, cudaStream_t st, bool *used) {
+    *used = false;
+    const size_t k = w->cols;
+    const bool mins = w->quant == JKB_Q4_1 || w->quant == JKB_Q4_K_M;
+    if (k % BK != 0 || act->m < TC_MIN_M || act->k_pad != k || act->m > (size_t)INT32_MAX ||
+        w->rows > (size_t)INT32_MAX || act->x_scales_t == nullptr ||
+        (mins && act->x_nsums_t == nullptr))
+        return JKB_OK;
+    if ((((uintptr_t)w->qs) & 15) || (((uintptr_t)w->meta) & 15) || (((uintptr_t)act->q) & 15) ||
+        (((uintptr_t)act->x_scales_t) & 15) || (act->xt_pitch & 31) ||
+        (mins && (((uintptr_t)act->x_nsums_t) & 15)))
+        return JKB_OK;
+    int *err = device_error_word();
+    if (!err) return JKB_OK;
+    *used = true;
+    const int bn = choose_tile(act->m, row_end - row_begin, mins);
+    const bool exact = g_gemm_exact.load(std::memory_order_relaxed);
+    switch (w->quant) {
+        case JKB_Q4_0:
+            return launch_nib_fmt<NIB_Q4_0>(bn, exact, w, act, out, row_begin, row_end, st, err);
+        case JKB_Q4_1:
+            return launch_nib_fmt<NIB_Q4_1>(bn, exact, w, act, out, row_begin, row_end, st, err);
+        case JKB_IQ4_NL:
+            return launch_nib_fmt<NIB_IQ4_NL>(bn, exact, w, act, out, row_begin, row_end, st, err);
+        default:
+            return launch_nib_fmt<NIB_Q4_K>(bn, exact, w, act, out, row_begin, row_end, st, err);
+    }
 }
 
 }  // namespace jkb

@@ -55,6 +55,15 @@ struct Arena {
     }
 };
 
+// Load-time helpers shared by the weight handles (weights.cu): validate_matrix_view
+// (repack.rs:1151-1284), the RepackedWeight::repack orientation rule (repack.rs:2255-2282) and
+// the device staging of a view's raw bytes (*owned: a temporary the caller frees).
+int validate_matrix_view(const jkb_tensor_view *v, const Fmt *f, size_t rows, size_t cols);
+int infer_rows_cols(const jkb_tensor_view *v, const Fmt *f, size_t *rows, size_t *cols,
+                    const char *who);
+int stage_raw(const jkb_tensor_view *v, size_t need, cudaStream_t st, uint8_t **dev,
+              bool *owned);
+
 // GPU layout of one weight matrix (see weights.cu for the per-format plane contents).
 struct WeightPlanes {
     const uint8_t *qs = nullptr;  // quant plane, row pitch qs_row bytes
@@ -93,6 +102,20 @@ struct jkb_repacked_weight {
     float *mins;     // [rows][scale_groups] or nullptr
 };
 
+// Compact 4-bit weight (PackedNibbleMatrix); plane layout in nibble.cuh.
+struct jkb_nibble_matrix {
+    uint32_t magic;
+    int quant;            // JKB_Q4_0, JKB_Q4_1, JKB_IQ4_NL or JKB_Q4_K_M
+    size_t rows, cols;
+    size_t nb;            // format blocks per row (cols / 32, or cols / 256 for Q4_K_M)
+    size_t meta_bytes;    // scale bytes per block: 2, 4 or 16
+    char name[64];
+    uint8_t *base;
+    size_t device_bytes;  // allocation (planes rounded to 256 bytes)
+    uint8_t *qs;          // [rows][cols / 2]
+    uint8_t *meta;        // [rows][nb] x meta_bytes
+};
+
 struct jkb_act_q8 {
     uint32_t magic;
     size_t m_cap, k, k_pad, m;
@@ -117,6 +140,7 @@ namespace jkb {
 constexpr uint32_t WEIGHT_MAGIC = 0x4A4B5731u;    // "JKW1"
 constexpr uint32_t REPACKED_MAGIC = 0x4A4B5231u;  // "JKR1"
 constexpr uint32_t ACT_MAGIC = 0x4A4B4131u;       // "JKA1"
+constexpr uint32_t NIBBLE_MAGIC = 0x4A4B4E31u;    // "JKN1"
 
 int num_sms();
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }

@@ -212,7 +212,7 @@ __global__ void repack_i8_kernel(int quant, const uint8_t *__restrict__ raw, siz
 }
 
 // validate_matrix_shape + validate_matrix_view (repack.rs:1151-1284).
-static int validate_matrix_view(const jkb_tensor_view *v, const Fmt *f, size_t rows,
+int validate_matrix_view(const jkb_tensor_view *v, const Fmt *f, size_t rows,
                                 size_t cols) {
     const char *nm = v->name ? v->name : "";
     if (rows == 0 || cols == 0)
@@ -244,11 +244,13 @@ static int validate_matrix_view(const jkb_tensor_view *v, const Fmt *f, size_t r
     return JKB_OK;
 }
 
-// RepackedWeight::repack orientation rule (repack.rs:2255-2282).
-static int infer_rows_cols(const jkb_tensor_view *v, const Fmt *f, size_t *rows, size_t *cols) {
+// RepackedWeight::repack orientation rule (repack.rs:2255-2282; PackedNibbleMatrix::repack
+// :4654-4679 is the same rule). `who` names the caller in the error.
+int infer_rows_cols(const jkb_tensor_view *v, const Fmt *f, size_t *rows, size_t *cols,
+                    const char *who) {
     if (v->ndim != 2)
         return fail(JKB_E_BOUNDS, v->name ? v->name : "", v->offset, v->byte_len, v->byte_len,
-                    "RepackedWeight::repack requires a 2D tensor, got %uD", v->ndim);
+                    "%s requires a 2D tensor, got %uD", who, v->ndim);
     size_t d0 = v->shape[0], d1 = v->shape[1], be = (size_t)f->block_elems;
     if (d0 % be == 0 && d1 % be != 0) {
         *rows = d1;
@@ -264,8 +266,8 @@ static int infer_rows_cols(const jkb_tensor_view *v, const Fmt *f, size_t *rows,
 }
 
 // Stages the raw GGUF bytes on the device (a load-time temporary) and reads the I2_S trailer.
-static int stage_raw(const jkb_tensor_view *v, size_t need, cudaStream_t st, uint8_t **dev,
-                     bool *owned) {
+int stage_raw(const jkb_tensor_view *v, size_t need, cudaStream_t st, uint8_t **dev,
+              bool *owned) {
     if (v->data_on_device) {
         *dev = (uint8_t *)v->data;
         *owned = false;
@@ -468,7 +470,7 @@ int jkb_weight_upload_infer(const jkb_tensor_view *view, void *stream, jkb_weigh
                     view->byte_len, view->byte_len, "unsupported tensor quant %s",
                     quant_name(view->quant));
     size_t r = 0, c = 0;
-    int rc = infer_rows_cols(view, f, &r, &c);
+    int rc = infer_rows_cols(view, f, &r, &c, "RepackedWeight::repack");
     if (rc) return rc;
     return weight_upload(view, r, c, as_stream(stream), out);
 }
@@ -508,7 +510,7 @@ int jkb_repacked_weight_repack(const jkb_tensor_view *view, void *stream,
                     view->byte_len, view->byte_len, "unsupported tensor quant %s for repack",
                     quant_name(view->quant));
     size_t r = 0, c = 0;
-    int rc = infer_rows_cols(view, f, &r, &c);
+    int rc = infer_rows_cols(view, f, &r, &c, "RepackedWeight::repack");
     if (rc) return rc;
     return repacked_upload(view, r, c, as_stream(stream), out);
 }

@@ -122,6 +122,21 @@ SIGNATURES = {
     "jkb_gemv_repacked_rows": [P, S, P, P, S, S, P],
     "jkb_gemm_repacked_f32": [P, S, P, P, S, S, P, P],
     "jkb_gemm_repacked_f32_noalloc": [P, S, P, P, S, S, P],
+    "jkb_packed_nibble_matrix_from_tensor": [C.POINTER(jkb_tensor_view), S, S, P, PP],
+    "jkb_packed_nibble_matrix_repack": [C.POINTER(jkb_tensor_view), P, PP],
+    "jkb_packed_nibble_matrix_from_scale_f16_buffers": [I, S, S, P, S, P, S, P, PP],
+    "jkb_packed_nibble_matrix_from_q4_k_buffers": [S, S, P, S, P, S, P, PP],
+    "jkb_repack_nibble_into_tile_range": [C.POINTER(jkb_tensor_view), S, S, S, S, P, S, P, S, P,
+                                          S, P, S],
+    "jkb_packed_nibble_matrix_destroy": [P],
+    "jkb_packed_nibble_matrix_info": [P, PS, PS, PI32, PS, PS, PS, PS],
+    "jkb_packed_nibble_matrix_buffers": [P, PP, PP],
+    "jkb_packed_nibble_matrix_gemm": [P, S, P, P, P],
+    "jkb_packed_nibble_matrix_gemm_rows": [P, S, P, P, S, S, P],
+    "jkb_packed_nibble_matrix_gemv": [P, S, P, P, P],
+    "jkb_packed_nibble_matrix_dequantize_row": [P, S, P, S, P],
+    "jkb_gemm_q4_0_ime": [P, S, P, P, P],
+    "jkb_gemm_q4_k_ime": [P, S, P, P, P],
 }
 _RESTYPE = {"jkb_last_error": C.c_char_p, "jkb_clear_error": None}
 

@@ -31,7 +31,8 @@ __all__ = [
     "gemv_repacked_rows", "gemm_repacked_f32", "gemm_repacked_f32_noalloc",
     "empty_q8_0_blocks", "empty_q8_k_blocks", "device_status", "gemm_set_exact", "gemm_get_exact",
     "gemm_exact", "PeerGroup", "gemv_batch",
-    "device_view",
+    "device_view", "PackedNibbleMatrix", "gemm_q4_0_ime", "gemm_q4_k_ime",
+    "repack_nibble_into_tile_range",
 ]
 
 
@@ -40,9 +41,11 @@ class QuantType(enum.IntEnum):
     F32 = 0
     F16 = 1
     Q4_0 = 2
+    Q4_1 = 3
     Q8_0 = 8
     Q4_K_M = 12
     Q6_K = 14
+    IQ4_NL = 20
     BF16 = 30
     TQ1_0 = 34
     TQ2_0 = 35
@@ -53,7 +56,7 @@ class QuantType(enum.IntEnum):
 BLOCK = {
     QuantType.Q4_0: (32, 18), QuantType.Q8_0: (32, 34), QuantType.Q4_K_M: (256, 144),
     QuantType.Q6_K: (256, 210), QuantType.TQ1_0: (256, 54), QuantType.TQ2_0: (256, 66),
-    QuantType.I2_S: (128, 32),
+    QuantType.I2_S: (128, 32), QuantType.Q4_1: (32, 20), QuantType.IQ4_NL: (32, 18),
 }
 BLOCK_Q8_0_BYTES = 36
 BLOCK_Q8_K_BYTES = 292
@@ -380,6 +383,159 @@ class RepackedWeight:
             self.destroy()
         except Exception:
             pass
+
+
+class PackedNibbleMatrix:
+    """PackedNibbleMatrix (repack.rs:4188-5545): Q4_0 / Q4_1 / IQ4_NL / Q4_K_M weights kept
+    4-bit on the device (exactly the GGUF bytes) with a GEMM that expands the codes on the fly."""
+
+    def __init__(self, handle, name=""):
+        self._h = handle
+        self.name = name
+        r, c, q, nt, kb = (C.c_size_t(), C.c_size_t(), C.c_int32(), C.c_size_t(),
+                           C.c_size_t())
+        pb, rb = C.c_size_t(), C.c_size_t()
+        _check(_L().jkb_packed_nibble_matrix_info(self._h, C.byref(r), C.byref(c), C.byref(q),
+                                                  C.byref(nt), C.byref(kb), C.byref(pb),
+                                                  C.byref(rb)))
+        self.rows, self.cols, self.quant = r.value, c.value, QuantType(q.value)
+        self.n_tiles, self.k_blocks32 = nt.value, kb.value
+        self._packed, self._raw = pb.value, rb.value
+
+    @classmethod
+    def from_tensor(cls, view: TensorView, rows: int, cols: int, stream=None):
+        """repack.rs:4788 PackedNibbleMatrix::from_tensor."""
+        h = C.c_void_p()
+        v = view._c()
+        _check(_L().jkb_packed_nibble_matrix_from_tensor(C.byref(v), rows, cols,
+                                                         _stream(stream), C.byref(h)))
+        return cls(h.value, view.name)
+
+    @classmethod
+    def repack(cls, view: TensorView, stream=None):
+        """repack.rs:4654 PackedNibbleMatrix::repack."""
+        h = C.c_void_p()
+        v = view._c()
+        _check(_L().jkb_packed_nibble_matrix_repack(C.byref(v), _stream(stream), C.byref(h)))
+        return cls(h.value, view.name)
+
+    @classmethod
+    def from_scale_f16_buffers(cls, quant, rows: int, cols: int, nibble_tiles, scales_f16,
+                               stream=None):
+        """repack.rs:4686: host numpy buffers in the reference's tile layout."""
+        t = np.ascontiguousarray(nibble_tiles, np.uint8)
+        sc = np.ascontiguousarray(scales_f16, np.uint16)
+        h = C.c_void_p()
+        _check(_L().jkb_packed_nibble_matrix_from_scale_f16_buffers(
+            int(quant), rows, cols, t.ctypes.data, t.size // 128, sc.ctypes.data, sc.size,
+            _stream(stream), C.byref(h)))
+        return cls(h.value)
+
+    @classmethod
+    def from_q4_k_buffers(cls, rows: int, cols: int, nibble_tiles, headers, stream=None):
+        """repack.rs:4743: host numpy buffers in the reference's tile layout."""
+        t = np.ascontiguousarray(nibble_tiles, np.uint8)
+        hd = np.ascontiguousarray(headers, np.uint8)
+        h = C.c_void_p()
+        _check(_L().jkb_packed_nibble_matrix_from_q4_k_buffers(
+            rows, cols, t.ctypes.data, t.size // 128, hd.ctypes.data, hd.size // 16,
+            _stream(stream), C.byref(h)))
+        return cls(h.value)
+
+    def packed_bytes(self) -> int:
+        """repack.rs:4914: device bytes of the codes and scales."""
+        return self._packed
+
+    def resident_bytes(self) -> int:
+        return self._packed
+
+    def raw_tensor_bytes(self) -> int:
+        return self._raw
+
+    def buffers(self):
+        """Zero-copy device views: codes [rows][cols / 2] and scale words [rows][blocks * bytes]."""
+        pq, pm = C.c_void_p(), C.c_void_p()
+        _check(_L().jkb_packed_nibble_matrix_buffers(self.handle, C.byref(pq), C.byref(pm)))
+        mb = (self._packed - self.rows * (self.cols // 2)) // max(self.rows, 1)
+        return (device_view(pq.value, (self.rows, self.cols // 2), "u1"),
+                device_view(pm.value, (self.rows, mb), "u1"))
+
+    @property
+    def handle(self):
+        if self._h is None:
+            raise InvalidHandle(6, self.name, 0, 0, 0, "PackedNibbleMatrix destroyed")
+        return self._h
+
+    def gemm(self, out, act: QuantizedActQ8, stream=None):
+        """repack.rs:4945 gemm: out [act.m][rows]."""
+        _check(_L().jkb_packed_nibble_matrix_gemm(_dptr(out), out.numel(), self.handle, act._h,
+                                                  _stream(stream)))
+
+    def gemm_rows(self, out, act: QuantizedActQ8, row_range, stream=None):
+        """repack.rs:4954 gemm_rows: out [act.m][len(row_range)]."""
+        _check(_L().jkb_packed_nibble_matrix_gemm_rows(_dptr(out), out.numel(), self.handle,
+                                                       act._h, row_range.start, row_range.stop,
+                                                       _stream(stream)))
+
+    def gemv(self, out, act: QuantizedActQ8, stream=None):
+        """repack.rs:4968 gemv (act.m == 1)."""
+        _check(_L().jkb_packed_nibble_matrix_gemv(_dptr(out), out.numel(), self.handle, act._h,
+                                                  _stream(stream)))
+
+    def dequantize_row(self, row: int, out, stream=None):
+        """repack.rs:5001 dequantize_row: out f32 [cols] (device)."""
+        _check(_L().jkb_packed_nibble_matrix_dequantize_row(self.handle, row, _dptr(out),
+                                                            out.numel(), _stream(stream)))
+
+    def destroy(self):
+        if getattr(self, "_h", None):
+            _L().jkb_packed_nibble_matrix_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+def gemm_q4_0_ime(out, weights: PackedNibbleMatrix, act: QuantizedActQ8, stream=None):
+    """repack.rs:5140 gemm_q4_0_ime (CapabilityMismatch unless Q4_0)."""
+    _check(_L().jkb_gemm_q4_0_ime(_dptr(out), out.numel(), weights.handle, act._h,
+                                  _stream(stream)))
+
+
+def gemm_q4_k_ime(out, weights: PackedNibbleMatrix, act: QuantizedActQ8, stream=None):
+    """repack.rs:5162 gemm_q4_k_ime (CapabilityMismatch unless Q4_K_M)."""
+    _check(_L().jkb_gemm_q4_k_ime(_dptr(out), out.numel(), weights.handle, act._h,
+                                  _stream(stream)))
+
+
+def repack_nibble_into_tile_range(view: TensorView, rows: int, cols: int, tile_range):
+    """repack.rs:4414 repack_nibble_into_tile_range on host bytes: returns (tiles u8 [n*kb*128],
+    scales_f16 or None, mins_f16 or None, headers u8 [n*(cols/256)*8*16] or None) for the tiles
+    of tile_range, in the reference's layout."""
+    n = tile_range.stop - tile_range.start
+    kb = cols // 32
+    tiles = np.zeros(max(n, 0) * kb * 128, np.uint8)
+    sc = mn = hd = None
+    q = view.quant
+    if q == QuantType.Q4_K_M:
+        hd = np.zeros(max(n, 0) * (cols // 256) * 8 * 16, np.uint8)
+    elif q in (QuantType.Q4_0, QuantType.IQ4_NL, QuantType.Q4_1):
+        sc = np.zeros(max(n, 0) * kb * 8, np.uint16)
+        if q == QuantType.Q4_1:
+            mn = np.zeros(max(n, 0) * kb * 8, np.uint16)
+    v = view._c()
+
+    def ptr(a):
+        return None if a is None else a.ctypes.data
+
+    _check(_L().jkb_repack_nibble_into_tile_range(
+        C.byref(v), rows, cols, tile_range.start, tile_range.stop, ptr(tiles), tiles.size // 128,
+        ptr(sc), 0 if sc is None else sc.size, ptr(mn), 0 if mn is None else mn.size, ptr(hd),
+        0 if hd is None else hd.size // 16))
+    return tiles, sc, mn, hd
 
 
 # ------------------------------------------------------------------------------- quantizers

@@ -177,3 +177,91 @@ def test_python_api_surface_imports():
         assert hasattr(jkb200, name), name
     assert jkb200.QuantType.Q4_K_M == 12 and jkb200.QuantType.I2_S == 36
     assert jkb200.BLOCK[jkb200.QuantType.Q6_K] == (256, 210)
+
+
+# ---------------------------------------------------------------- PackedNibbleMatrix (host side)
+
+@pytest.mark.parametrize("quant", [2, 3, 20, 12])
+def test_repack_nibble_into_tile_range_matches_oracle(oracle, quant):
+    """The library's host tile packer (repack_nibble_into_tile_range, repack.rs:4414-4645)
+    writes the reference's tile layout byte for byte, for the whole matrix and for a sub-range
+    of tiles (ragged last tile: 203 rows)."""
+    import jkb200 as jkb
+    import refgen as R
+
+    rows, cols = 203, 512
+    raw = R.fill_pseudo_quant_tensor(quant, rows, cols)
+    view = jkb.TensorView("nib", quant, [cols, rows], raw)
+    ref = oracle.nibble_pack_tiles(quant, raw, rows, cols)
+    got = jkb.repack_nibble_into_tile_range(view, rows, cols, range(0, 26))
+    for a, b in zip(got, ref):
+        assert (a is None) == (b is None)
+        if a is not None:
+            assert np.array_equal(a, b)
+    kb = cols // 32
+    part = jkb.repack_nibble_into_tile_range(view, rows, cols, range(5, 26))
+    assert np.array_equal(part[0], ref[0][5 * kb * 128:])
+    if quant == 12:
+        assert np.array_equal(part[3], ref[3][5 * (cols // 256) * 8 * 16:])
+    else:
+        assert np.array_equal(part[1], ref[1][5 * kb * 8:])
+
+
+def test_repack_nibble_into_tile_range_validation():
+    import jkb200 as jkb
+    import refgen as R
+
+    rows, cols = 16, 64
+    raw = R.fill_pseudo_quant_tensor(2, rows, cols)
+    view = jkb.TensorView("nib", 2, [cols, rows], raw)
+    with pytest.raises(jkb.TensorBoundsError) as e:
+        jkb.repack_nibble_into_tile_range(view, rows, cols, range(0, 3))
+    assert "exceeds n_tiles (2)" in e.value.reason
+    L = jkb._lib.load()
+    v = view._c()
+    tiles = np.zeros(4 * 128, np.uint8)
+    sc = np.zeros(3, np.uint16)
+    rc = L.jkb_repack_nibble_into_tile_range(C.byref(v), rows, cols, 0, 2, tiles.ctypes.data, 4,
+                                             sc.ctypes.data, 3, None, 0, None, 0)
+    assert rc == 1 and b"out_scales_f16 slice length mismatch" in L.jkb_last_error()
+    rc = L.jkb_repack_nibble_into_tile_range(C.byref(v), rows, cols, 0, 2, tiles.ctypes.data, 3,
+                                             None, 0, None, 0, None, 0)
+    assert rc == 1 and b"nibble out_tiles length 3 != 4" in L.jkb_last_error()
+    q8 = jkb.TensorView("q8", 8, [cols, rows], np.zeros(rows * 2 * 34, np.uint8))
+    with pytest.raises(jkb.CapabilityMismatch):
+        jkb.repack_nibble_into_tile_range(q8, rows, cols, range(0, 2))
+    raw1 = R.fill_pseudo_quant_tensor(3, rows, cols)
+    v1 = jkb.TensorView("q41", 3, [cols, rows], raw1)._c()
+    sc = np.zeros(32, np.uint16)
+    rc = L.jkb_repack_nibble_into_tile_range(C.byref(v1), rows, cols, 0, 2, tiles.ctypes.data, 4,
+                                             sc.ctypes.data, 32, None, 0, None, 0)
+    assert rc == 1 and b"Q4_1 requires out_mins_f16 slice" in L.jkb_last_error()
+
+
+def test_nibble_constructor_validation_fails_closed():
+    """Validation order of PackedNibbleMatrix::{from_tensor, from_scale_f16_buffers,
+    from_q4_k_buffers} (repack.rs:4686-4788): every error is reported before any device work."""
+    import jkb200 as jkb
+
+    with pytest.raises(jkb.CapabilityMismatch):
+        jkb.PackedNibbleMatrix.from_tensor(
+            jkb.TensorView("q8", 8, [64, 4], np.zeros(4 * 2 * 34, np.uint8)), 4, 64, stream=0)
+    with pytest.raises(jkb.TensorBoundsError) as e:
+        jkb.PackedNibbleMatrix.from_tensor(
+            jkb.TensorView("q4", 2, [64, 4], np.zeros(4 * 2 * 18, np.uint8)), 4, 48, stream=0)
+    assert "multiple of Q4_0 block size" in e.value.reason
+    with pytest.raises(jkb.TensorBoundsError):
+        jkb.PackedNibbleMatrix.repack(jkb.TensorView("q4", 2, [256], np.zeros(144, np.uint8)), stream=0)
+    with pytest.raises(jkb.CapabilityMismatch):
+        jkb.PackedNibbleMatrix.from_scale_f16_buffers(jkb.QuantType.Q4_K_M, 8, 256,
+                                                      np.zeros(8 * 128, np.uint8),
+                                                      np.zeros(64, np.uint16), stream=0)
+    with pytest.raises(jkb.TensorBoundsError) as e:
+        jkb.PackedNibbleMatrix.from_scale_f16_buffers(jkb.QuantType.Q4_0, 8, 64,
+                                                      np.zeros(2 * 128, np.uint8),
+                                                      np.zeros(15, np.uint16), stream=0)
+    assert e.value.reason == "nibble buffer lengths do not match geometry"
+    with pytest.raises(jkb.TensorBoundsError) as e:
+        jkb.PackedNibbleMatrix.from_q4_k_buffers(8, 96, np.zeros(3 * 128, np.uint8),
+                                                 np.zeros(8 * 16, np.uint8), stream=0)
+    assert e.value.reason == "invalid rows/cols for Q4_K_M"
