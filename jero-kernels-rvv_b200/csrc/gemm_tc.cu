@@ -71,11 +71,12 @@ struct TcCfg {
     // warp writes two copies of each token tile with alternate 16-byte halves of K zeroed, and
     // every 32-element slice takes two MMAs (even and odd half-groups) into two accumulators.
     static constexpr bool H16 = H16_;
-    // NIB: the weight tile arrives as 4-bit codes (a jkb_nibble_matrix, format NibFmt) and two
+    // NIB: the weight tile arrives as 4-bit codes (a jkb_nibble_matrix, format NibFmt);
     // converter warps write its int8 values into the MMA's operand tile and its scales (and
-    // mins) into the epilogue's scale tiles.
+    // mins) into the scale tiles. Two warps for the formats whose codes expand in a few integer
+    // operations; IQ4_NL's code-book lookups take four, one on each SM sub-partition.
     static constexpr int NIB = NIB_;
-    static constexpr int CONV = NIB ? 2 : 0;   // converter warps
+    static constexpr int CONV = NIB == NIB_IQ4_NL ? 4 : NIB ? 2 : 0;  // converter warps
     static constexpr int SPL = H16 ? 2 : 1;    // accumulators per 32-element slice
     static constexpr int NA = GPR * SPL;       // accumulators per round
     static constexpr int NG = GPS * SPL;       // weight-scale groups per stage
@@ -86,10 +87,11 @@ struct TcCfg {
     static constexpr int TMEM_COLS = 512;
     static constexpr int SA = BMW * BK, SB = BN * BK;  // operand bytes per stage
     static constexpr int SAN = NIB ? BMW * BK / 2 : 0;  // 4-bit weight tile bytes per stage
+    static constexpr int SMT = NIB ? BMW * 16 : 0;       // scale words: 16 bytes per row
     // bytes the TMA brings per stage (weight tile or its 4-bit codes, token tile, scale tiles
     // the TMA loads) and the stage's shared-memory footprint
     static constexpr int STAGE_TX =
-        NIB ? SAN + SB + GPS * BN * 4 + (MINS ? GPS * BN * 4 : 0)
+        NIB ? SAN + SMT + SB + GPS * BN * 4 + (MINS ? GPS * BN * 4 : 0)
             : SA + SB + BMW * NG * 4 + GPS * BN * 4 + (MINS ? BMW * GPS * 4 + GPS * BN * 4 : 0);
     static constexpr int STAGE_SMEM =
         STAGE_TX + (H16 ? 2 * SB : 0) + (NIB ? SA + BMW * NG * 4 + (MINS ? BMW * GPS * 4 : 0) : 0);
@@ -99,20 +101,27 @@ struct TcCfg {
     static_assert(GPS % GPR == 0 && 2 * NA * BN <= TMEM_COLS, "two rounds of NA buffers");
     static_assert(!(H16 && MINS), "16-element groups carry no mins");
     static_assert(!(H16 && NIB), "nibble formats use 32-element groups");
+    static_assert((BMW * NG * 4) % 128 == 0 && (GPS * BN * 4) % 128 == 0 &&
+                      (BMW * GPS * 4) % 128 == 0 && SAN % 128 == 0 && SMT % 128 == 0,
+                  "per-stage TMA destinations stay 128-byte aligned");
     static_assert(!NIB || MINS == (NIB == NIB_Q4_1 || NIB == NIB_Q4_K), "nibble min terms");
+    static_assert(EPI % 4 == 0, "four converter warps 2 + EPI .. + 3 cover the 4 sub-partitions");
 };
 
+// Every TMA destination starts on a 128-byte boundary, the 128-byte-swizzled operand tiles on
+// 1024-byte boundaries (the struct itself is placed 1024-byte aligned).
 template <class C>
 struct TcSmem {
-    uint8_t a[C::STAGES][C::SA];  // weight tiles; 1024-byte aligned (swizzle atoms)
-    uint8_t b[C::STAGES][C::SB];  // token tiles
-    uint8_t blo[C::H16 ? C::STAGES : 1][C::H16 ? C::SB : 1024];  // H16: odd 16-byte halves zeroed
-    uint8_t bhi[C::H16 ? C::STAGES : 1][C::H16 ? C::SB : 1024];  // H16: even 16-byte halves zeroed
-    uint8_t an[C::NIB ? C::STAGES : 1][C::NIB ? C::SAN : 1024];  // NIB: 4-bit codes [128][64]
-    float ws[C::STAGES][BMW][C::NG];
-    float xs[C::STAGES][GPS][C::BN];
-    float wm[C::MINS ? C::STAGES : 1][BMW][GPS];     // weight mins (MINS)
-    float xn[C::MINS ? C::STAGES : 1][GPS][C::BN];   // -x_sums, permuted like xs (MINS)
+    alignas(1024) uint8_t a[C::STAGES][C::SA];  // weight tiles (swizzle atoms)
+    alignas(1024) uint8_t b[C::STAGES][C::SB];  // token tiles
+    alignas(1024) uint8_t blo[C::H16 ? C::STAGES : 1][C::H16 ? C::SB : 1024];  // H16: odd halves zeroed
+    alignas(1024) uint8_t bhi[C::H16 ? C::STAGES : 1][C::H16 ? C::SB : 1024];  // H16: even halves zeroed
+    alignas(128) uint8_t an[C::NIB ? C::STAGES : 1][C::NIB ? C::SAN : 128];  // NIB: codes [128][64]
+    alignas(128) uint8_t mt[C::NIB ? C::STAGES : 1][C::NIB ? C::SMT : 128];  // NIB: scale words
+    alignas(128) float ws[C::STAGES][BMW][C::NG];
+    alignas(128) float xs[C::STAGES][GPS][C::BN];
+    alignas(128) float wm[C::MINS ? C::STAGES : 1][BMW][GPS];     // weight mins (MINS)
+    alignas(128) float xn[C::MINS ? C::STAGES : 1][GPS][C::BN];   // -x_sums, permuted like xs
     uint64_t full[C::STAGES], empty[C::STAGES], masked[C::STAGES], tfull[2], tempty[2], done;
     uint32_t tmem_base;
     int abort_flag;
@@ -162,6 +171,23 @@ __device__ __forceinline__ bool mbar_wait_slow(uint64_t *b, uint32_t parity, vol
 __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t parity, volatile int *abort_flag,
                                           int *err) {
     return mbar_try(b, parity) || mbar_wait_slow(b, parity, abort_flag, err);
+}
+// Bounded like mbar_wait_slow, with a short sleep between polls: for warps that run ahead of
+// the MMA and would otherwise take issue slots from the epilogue warps.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t *b, uint32_t parity,
+                                                 volatile int *abort_flag, int *err) {
+    if (mbar_try(b, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (;;) {
+        __nanosleep(256);
+        if (mbar_try(b, parity)) return true;
+        if (*abort_flag) return false;
+        if (globaltimer() - t0 > WAIT_NS) {
+            *abort_flag = 1;
+            atomicOr(err, 1);
+            return false;
+        }
+    }
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t *b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
@@ -251,14 +277,79 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
     return r;
 }
 
+// NIB: converts stage s (K stage ks of its tile): the 4-bit codes in an[s] to int8 values in
+// a[s], in the layout the TMA's 128-byte swizzle gives (16-byte unit u of row r at
+// 16 * (u ^ (r & 7))), and the scale words in mt[s] to the f32 scales (and mins) in ws[s] /
+// wm[s]. Thread e of the 32 * CONV converter threads takes rows e, e + 32 * CONV, ... of the
+// scales and 16-byte code chunks e, e + 32 * CONV, ... (4 per row; a chunk's low nibbles fill
+// one 16-byte unit of the row, its high nibbles another).
+template <class C>
+__device__ __forceinline__ void nib_convert(TcSmem<C> &sm, int s, int ks, int e) {
+    constexpr int F = C::NIB, N = 32 * (C::CONV ? C::CONV : 1);
+#pragma unroll
+    for (int i = 0; i < (BMW + N - 1) / N; i++) {
+        const int r = e + i * N;
+        if (r >= BMW) break;
+        const uint4 v = *reinterpret_cast<const uint4 *>(&sm.mt[C::NIB ? s : 0][16 * r]);
+        float4 w4, n4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (F == NIB_Q4_K) {
+            // the header of the 256-element block; this stage holds its groups 4(ks&1)..+3
+            const float d = nib_f16_finite(v.x & 0xFFFF), dmin = nib_f16_finite(v.x >> 16);
+            float sw[4], sm4[4];
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                int sc, mn;
+                nib_k4_scale_min(v.y, v.z, v.w, 4 * (ks & 1) + g, sc, mn);
+                sw[g] = __fmul_rn(d, (float)sc);
+                sm4[g] = __fmul_rn(dmin, (float)mn);
+            }
+            w4 = make_float4(sw[0], sw[1], sw[2], sw[3]);
+            n4 = make_float4(sm4[0], sm4[1], sm4[2], sm4[3]);
+        } else if (F == NIB_Q4_1) {
+            // (d, m) of the stage's 4 blocks
+            w4 = make_float4(nib_f16_finite(v.x), nib_f16_finite(v.y), nib_f16_finite(v.z),
+                             nib_f16_finite(v.w));
+            n4 = make_float4(nib_q4_1_min(v.x >> 16), nib_q4_1_min(v.y >> 16),
+                             nib_q4_1_min(v.z >> 16), nib_q4_1_min(v.w >> 16));
+        } else {
+            // f16 d of 8 blocks; this stage's 4 are half ks & 1
+            const uint32_t d01 = (ks & 1) ? v.z : v.x, d23 = (ks & 1) ? v.w : v.y;
+            w4 = make_float4(nib_d_scale(d01), nib_d_scale(d01 >> 16), nib_d_scale(d23),
+                             nib_d_scale(d23 >> 16));
+        }
+        *reinterpret_cast<float4 *>(&sm.ws[s][r][0]) = w4;
+        if (C::MINS) *reinterpret_cast<float4 *>(&sm.wm[C::MINS ? s : 0][r][0]) = n4;
+    }
+    static_assert((BMW * 4) % N == 0, "code chunks split evenly");
+#pragma unroll
+    for (int i = 0; i < BMW * 4 / N; i++) {
+        const int q = e + i * N;
+        const int r = q >> 2, j = q & 3;
+        const uint4 c = *reinterpret_cast<const uint4 *>(&sm.an[C::NIB ? s : 0][r * 64 + 16 * j]);
+        const uint4 lo = make_uint4(
+            nib_values4<F>(c.x & 0x0F0F0F0Fu), nib_values4<F>(c.y & 0x0F0F0F0Fu),
+            nib_values4<F>(c.z & 0x0F0F0F0Fu), nib_values4<F>(c.w & 0x0F0F0F0Fu));
+        const uint4 hi = make_uint4(
+            nib_values4<F>((c.x >> 4) & 0x0F0F0F0Fu), nib_values4<F>((c.y >> 4) & 0x0F0F0F0Fu),
+            nib_values4<F>((c.z >> 4) & 0x0F0F0F0Fu), nib_values4<F>((c.w >> 4) & 0x0F0F0F0Fu));
+        // Q4_K_M chunk j holds elements 64(j/2) + 16(j&1) (low nibbles) and + 32 (high); the
+        // other formats' chunk j is block j: elements 32j (low) and 32j + 16 (high)
+        const int ulo = F == NIB_Q4_K ? 4 * (j >> 1) + (j & 1) : 2 * j;
+        const int uhi = F == NIB_Q4_K ? ulo + 2 : ulo + 1;
+        uint8_t *row = &sm.a[s][r * 128];
+        const int x = r & 7;
+        *reinterpret_cast<uint4 *>(row + 16 * (ulo ^ x)) = lo;
+        *reinterpret_cast<uint4 *>(row + 16 * (uhi ^ x)) = hi;
+    }
+}
+
 template <class C>
 __global__ void __launch_bounds__(C::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    const __grid_constant__ CUtensorMap tmWS, const __grid_constant__ CUtensorMap tmXS,
                    const __grid_constant__ CUtensorMap tmWM, const __grid_constant__ CUtensorMap tmXN,
                    int M, int G, int row_begin, int sub_n, int tiles_w, int tiles_t,
-                   float *__restrict__ out, int *err, const uint8_t *__restrict__ nmeta,
-                   int nmeta_nb, int w_rows) {
+                   float *__restrict__ out, int *err) {
     constexpr int BN = C::BN, STAGES = C::STAGES, GPR = C::GPR, EPI = C::EPI, COLS = C::COLS;
     constexpr int NA = C::NA, SPL = C::SPL;
     extern __shared__ uint8_t smem_raw[];
@@ -273,7 +364,8 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         for (int i = 0; i < STAGES; i++) {
             mbar_init(&sm.full[i], 1);
             mbar_init(&sm.empty[i], 1 + EPI);  // the MMA commit and every epilogue warp
-            mbar_init(&sm.masked[i], C::CONV ? C::CONV : 1);  // masking or converter warps
+            // the masking warp (H16) or the converter warps (NIB)
+            mbar_init(&sm.masked[i], C::CONV ? C::CONV : 1);
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&sm.tfull[i], 1);
@@ -312,9 +404,15 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                         break;
                     }
                     mbar_arrive_tx(&sm.full[s], C::STAGE_TX);
-                    if (C::NIB)
+                    if (C::NIB) {
                         tma_load_2d(sm.an[C::NIB ? s : 0], &tmW, &sm.full[s], ks * (BK / 2), wrow);
-                    else
+                        // 16 bytes of scale words per row: Q4_0 / IQ4_NL the f16 d of 8 blocks
+                        // (this stage's 4 are half ks & 1), Q4_1 the 4 (d, m) words, Q4_K_M the
+                        // header of the 256-element block (half ks & 1 of its groups)
+                        const int mx = C::NIB == NIB_Q4_1 ? 4 * ks
+                                     : C::NIB == NIB_Q4_K ? 4 * (ks >> 1) : 8 * (ks >> 1);
+                        tma_load_2d(sm.mt[C::NIB ? s : 0], &tmWS, &sm.full[s], mx, wrow);
+                    } else
                         tma_load_2d(sm.a[s], &tmW, &sm.full[s], ks * BK, wrow);
                     tma_load_2d(sm.b[s], &tmX, &sm.full[s], ks * BK, tok);
                     if (!C::NIB)
@@ -413,111 +511,25 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         }
     } else if (C::NIB && warp >= 2 + EPI) {
         // ------------------------------------------------ converter warps (NIB)
-        // Converter cw takes weight rows 64cw .. 64cw + 63 of the tile. Per stage it writes the
-        // int8 values of its rows' 4-bit codes into the operand tile (the layout the TMA's
-        // 128-byte swizzle would give: 16-byte unit u of row r at 16 * (u ^ (r & 7))) and the
-        // rows' scales (and mins) into ws / wm. The scale words of the next stage are loaded
-        // while this one converts.
-        const int cw = warp - (2 + EPI);
-        constexpr int F = C::NIB;
-        const uint32_t *m32 = reinterpret_cast<const uint32_t *>(nmeta);
-        const uint16_t *m16 = reinterpret_cast<const uint16_t *>(nmeta);
-        // meta words of rows 64cw + lane and 64cw + lane + 32 at stage (t, ks)
-        auto load_meta = [&](int t, int ks, uint4 (&mv)[2]) {
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                mv[h] = make_uint4(0u, 0u, 0u, 0u);
-                if (t >= ntiles) continue;
-                const int row = row_begin + (t / tiles_t) * BMW + 64 * cw + lane + 32 * h;
-                if (row >= w_rows) continue;
-                const size_t rb = (size_t)row * (size_t)nmeta_nb;
-                if (F == NIB_Q4_K) {
-                    mv[h] = __ldg(reinterpret_cast<const uint4 *>(nmeta) + rb + (ks >> 1));
-                } else if (F == NIB_Q4_1) {
-                    mv[h] = __ldg(reinterpret_cast<const uint4 *>(m32 + rb + 4 * ks));
-                } else {
-                    const uint2 v = __ldg(reinterpret_cast<const uint2 *>(m16 + rb + 4 * ks));
-                    mv[h] = make_uint4(v.x, v.y, 0u, 0u);
-                }
-            }
-        };
+        // Each stage, once its TMA has landed: the codes and scale words to the operand and
+        // scale tiles (nib_convert, an equal share per warp), then a signal on masked for the
+        // MMA and the epilogue. Running ahead of the MMA, the warps sleep between polls instead
+        // of taking issue slots from the epilogue warps.
+        const int e = (warp - 2 - EPI) * 32 + lane;
         uint32_t it = 0;
         bool ok = true;
-        uint4 cur[2], nxt[2];
-        load_meta(blockIdx.x, 0, cur);
         for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
             for (int ks = 0; ks < kstages; ks++, it++) {
                 const int s = it % STAGES;
-                if (ks + 1 < kstages)
-                    load_meta(t, ks + 1, nxt);
-                else
-                    load_meta(t + gridDim.x, 0, nxt);
-                if (!mbar_wait(&sm.full[s], (it / STAGES) & 1, abort_flag, err)) {
+                if (!mbar_wait_sleepy(&sm.full[s], (it / STAGES) & 1, abort_flag, err)) {
                     ok = false;
                     break;
                 }
-                // scales and mins of the stage's 4 groups
-#pragma unroll
-                for (int h = 0; h < 2; h++) {
-                    const int r = 64 * cw + lane + 32 * h;
-                    const uint4 v = cur[h];
-                    float4 w4, n4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (F == NIB_Q4_K) {
-                        const float d = nib_f16_finite(v.x & 0xFFFF), dmin = nib_f16_finite(v.x >> 16);
-                        float sw[4], sm4[4];
-#pragma unroll
-                        for (int g = 0; g < 4; g++) {
-                            int sc, mn;
-                            nib_k4_scale_min(v.y, v.z, v.w, 4 * (ks & 1) + g, sc, mn);
-                            sw[g] = __fmul_rn(d, (float)sc);
-                            sm4[g] = __fmul_rn(dmin, (float)mn);
-                        }
-                        w4 = make_float4(sw[0], sw[1], sw[2], sw[3]);
-                        n4 = make_float4(sm4[0], sm4[1], sm4[2], sm4[3]);
-                    } else if (F == NIB_Q4_1) {
-                        w4 = make_float4(nib_f16_finite(v.x), nib_f16_finite(v.y),
-                                         nib_f16_finite(v.z), nib_f16_finite(v.w));
-                        n4 = make_float4(nib_q4_1_min(v.x >> 16), nib_q4_1_min(v.y >> 16),
-                                         nib_q4_1_min(v.z >> 16), nib_q4_1_min(v.w >> 16));
-                    } else {
-                        w4 = make_float4(nib_d_scale(v.x), nib_d_scale(v.x >> 16),
-                                         nib_d_scale(v.y), nib_d_scale(v.y >> 16));
-                    }
-                    *reinterpret_cast<float4 *>(&sm.ws[s][r][0]) = w4;
-                    if (C::MINS) *reinterpret_cast<float4 *>(&sm.wm[C::MINS ? s : 0][r][0]) = n4;
-                }
-                // codes -> int8 values: 64 rows x 4 chunks of 16 bytes, 8 chunks per lane. A
-                // chunk's low nibbles fill unit ulo, its high nibbles unit uhi of the row.
-#pragma unroll 4
-                for (int i = 0; i < 8; i++) {
-                    const int q = lane + 32 * i;
-                    const int r = 64 * cw + (q >> 2), j = q & 3;
-                    const uint4 c = *reinterpret_cast<const uint4 *>(&sm.an[C::NIB ? s : 0][r * 64 + 16 * j]);
-                    const uint4 lo = make_uint4(
-                        nib_values4<F>(c.x & 0x0F0F0F0Fu), nib_values4<F>(c.y & 0x0F0F0F0Fu),
-                        nib_values4<F>(c.z & 0x0F0F0F0Fu), nib_values4<F>(c.w & 0x0F0F0F0Fu));
-                    const uint4 hi = make_uint4(nib_values4<F>((c.x >> 4) & 0x0F0F0F0Fu),
-                                                nib_values4<F>((c.y >> 4) & 0x0F0F0F0Fu),
-                                                nib_values4<F>((c.z >> 4) & 0x0F0F0F0Fu),
-                                                nib_values4<F>((c.w >> 4) & 0x0F0F0F0Fu));
-                    // Q4_K_M chunk j holds elements 64(j/2) + 16(j&1) (low) and + 32 (high);
-                    // the other formats' chunk j is block j: elements 32j (low), 32j + 16 (high)
-                    const int ulo = F == NIB_Q4_K ? 4 * (j >> 1) + (j & 1) : 2 * j;
-                    const int uhi = F == NIB_Q4_K ? ulo + 2 : ulo + 1;
-                    // odd Q4_K_M rows store their high unit first: each 8-lane phase of a
-                    // 16-byte store then covers 8 distinct bank groups
-                    const bool sw = F == NIB_Q4_K && (r & 1);
-                    uint8_t *row = &sm.a[s][r * 128];
-                    const int x = r & 7;
-                    *reinterpret_cast<uint4 *>(row + 16 * ((sw ? uhi : ulo) ^ x)) = sw ? hi : lo;
-                    *reinterpret_cast<uint4 *>(row + 16 * ((sw ? ulo : uhi) ^ x)) = sw ? lo : hi;
-                }
+                if constexpr (C::NIB != NIB_NONE) nib_convert<C>(sm, s, ks, e);
                 // the operand tile is read by the tensor core (async proxy)
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sm.masked[s]);
-                cur[0] = nxt[0];
-                cur[1] = nxt[1];
             }
         }
     } else {
@@ -720,12 +732,9 @@ bool encode_2d(CUtensorMap *tm, CUtensorMapDataType dt, const void *base, uint64
     return r == CUDA_SUCCESS;
 }
 
-// The weight side of one launch: its tensor maps and, for nibble weights, the scale plane the
-// converter warps read.
+// The weight side of one launch: its tensor maps (nibble weights: codes, scale words).
 struct TcWeight {
     CUtensorMap tmW, tmWS, tmWM;
-    const uint8_t *nmeta = nullptr;
-    int nmeta_nb = 0;
     size_t rows = 0, k = 0;
 };
 
@@ -764,7 +773,7 @@ int launch_tc_common(const TcWeight &wt, const jkb_act_q8 *act, float *out, size
     const size_t grid = ntiles < (size_t)num_sms() ? ntiles : (size_t)num_sms();
     gemm_tc_kernel<C><<<(unsigned)grid, C::THREADS, smem, st>>>(
         wt.tmW, tmX, wt.tmWS, tmXS, wt.tmWM, tmXN, (int)act->m, (int)G, (int)row_begin,
-        (int)sub_n, tiles_w, tiles_t, out, err, wt.nmeta, wt.nmeta_nb, (int)wt.rows);
+        (int)sub_n, tiles_w, tiles_t, out, err);
     return check_launch("gemm_tc_kernel");
 }
 
@@ -788,20 +797,23 @@ int launch_tc(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out, s
     return launch_tc_common<C>(wt, act, out, row_begin, row_end, st, err);
 }
 
-// Nibble weight: the 4-bit code plane by TMA (64 bytes of each of 128 rows per stage, no
-// swizzle), the scale plane read by the converter warps.
+// Nibble weight: by TMA, without swizzle, per stage 64 bytes of codes and 16 bytes of scale
+// words of each of the tile's 128 rows.
 template <class C>
 int launch_tc_nib(const jkb_nibble_matrix *w, const jkb_act_q8 *act, float *out,
                   size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
     TcWeight wt;
     wt.rows = w->rows;
     wt.k = w->cols;
-    wt.nmeta = w->meta;
-    wt.nmeta_nb = (int)w->nb;
+    const bool f16 = C::NIB == NIB_Q4_0 || C::NIB == NIB_IQ4_NL;
+    const size_t mpitch = w->nb * w->meta_bytes;  // scale bytes per row
     if (!encode_2d(&wt.tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs, w->cols / 2, w->rows,
-                   w->cols / 2, BK / 2, BMW, CU_TENSOR_MAP_SWIZZLE_NONE))
+                   w->cols / 2, BK / 2, BMW, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_2d(&wt.tmWS, f16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32,
+                   w->meta, mpitch / (f16 ? 2 : 4), w->rows, mpitch, f16 ? 8 : 4, BMW,
+                   CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(JKB_E_CUDA, "gemm_nibble", 0, 0, 0, "cuTensorMapEncodeTiled failed");
-    wt.tmWS = wt.tmWM = wt.tmW;  // unused
+    wt.tmWM = wt.tmW;  // unused
     return launch_tc_common<C>(wt, act, out, row_begin, row_end, st, err);
 }
 
@@ -839,9 +851,14 @@ template <bool E, bool MN, bool H> using TC64 = TcCfg<64, 2, H ? 2 : 4, E, MN, H
 template <bool E, bool MN, bool H> using TC96 = TcCfg<96, 3, H ? 1 : 2, E, MN, H>;
 template <bool E, bool MN, bool H> using TC128 = TcCfg<128, 2, H ? 1 : 2, E, MN, H>;
 
-template <bool E, int NB> using TN64 = TcCfg<64, 2, 4, E, NB == NIB_Q4_1 || NB == NIB_Q4_K, false, NB>;
-template <bool E, int NB> using TN96 = TcCfg<96, 3, 2, E, NB == NIB_Q4_1 || NB == NIB_Q4_K, false, NB>;
-template <bool E, int NB> using TN128 = TcCfg<128, 2, 2, E, NB == NIB_Q4_1 || NB == NIB_Q4_K, false, NB>;
+// The nibble GEMM's configurations: the repacked GEMM's three with two converter warps; with
+// IQ4_NL's four (14 warps and more leave 144 registers a thread or fewer) only the 64-token
+// tile, at two groups per round, stays clear of spills.
+template <int NB> constexpr bool NMINS = NB == NIB_Q4_1 || NB == NIB_Q4_K;
+template <bool E, int NB>
+using TN64 = TcCfg<64, 2, NB == NIB_IQ4_NL ? 2 : 4, E, NMINS<NB>, false, NB>;
+template <bool E, int NB> using TN96 = TcCfg<96, 3, 2, E, NMINS<NB>, false, NB>;
+template <bool E, int NB> using TN128 = TcCfg<128, 2, 2, E, NMINS<NB>, false, NB>;
 
 std::atomic<int> g_gemm_exact{0};
 
@@ -890,37 +907,56 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
                  : launch_tc_bn<false, false, false>(bn, w, act, out, row_begin, row_end, st, err);
 }
 
+
 template <bool EXACT, int NB>
 int launch_nib_bn(int bn, const jkb_nibble_matrix *w, const jkb_act_q8 *act, float *out,
                   size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
-    switch (bn) {
-        case 64:
-            return launch_tc_nib<TN64<EXACT, NB>>(w, act, out, row_begin, row_end, st, err);
-        case 128:
-            if constexpr (NB == NIB_Q4_1 || NB == NIB_Q4_K)
-                return launch_tc_nib<TN96<EXACT, NB>>(w, act, out, row_begin, row_end, st, err);
-            else
-                return launch_tc_nib<TN128<EXACT, NB>>(w, act, out, row_begin, row_end, st, err);
-        default:
+    if constexpr (NB != NIB_IQ4_NL) {
+        if (bn == 96)
             return launch_tc_nib<TN96<EXACT, NB>>(w, act, out, row_begin, row_end, st, err);
+        if constexpr (!NMINS<NB>)
+            if (bn == 128)
+                return launch_tc_nib<TN128<EXACT, NB>>(w, act, out, row_begin, row_end, st, err);
     }
+    return launch_tc_nib<TN64<EXACT, NB>>(w, act, out, row_begin, row_end, st, err);
 }
 
 template <int NB>
-int launch_nib_fmt(int bn, bool exact, const jkb_nibble_matrix *w, const jkb_act_q8 *act,
-                   float *out, size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
+int launch_nib_fmt(bool exact, const jkb_nibble_matrix *w, const jkb_act_q8 *act, float *out,
+                   size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
+    // IQ4_NL: the 64-token tile only; the others choose like the repacked GEMM
+    const int bn = NB == NIB_IQ4_NL ? 64 : choose_tile(act->m, row_end - row_begin, NMINS<NB>);
     return exact ? launch_nib_bn<true, NB>(bn, w, act, out, row_begin, row_end, st, err)
                  : launch_nib_bn<false, NB>(bn, w, act, out, row_begin, row_end, st, err);
 }
 
-// Tensor-core path of the compact nibble GEMM: taken for batches of at least TC_MIN_M tokens
-// with K a multiple of 128 (the stage depth); *used reports whether it ran.
+// Smallest batch for which the tensor-core path beats the nibble row kernel. Measured on B200:
+// a row-kernel call costs about 2.85 ps per (weight row, 32-element block, token), a
+// tensor-core call about 1.4 us per 128-element K stage per wave of 128-row weight tiles over
+// the SMs, independent of the batch up to its 64-token tile. Equal at
+// m = 1.4 us * waves / (4 * 2.85 ps * rows), about 122880 * waves / rows; never below 8 tokens,
+// always from 32.
+size_t nibble_tc_min_m(size_t rows) {
+    const size_t tiles = (rows + BMW - 1) / BMW, sms = (size_t)num_sms();
+    const size_t waves = (tiles + sms - 1) / sms;
+    size_t m = (122880 * waves + rows - 1) / (rows ? rows : 1);
+    return m < 8 ? 8 : m > TC_MIN_M ? TC_MIN_M : m;
+}
+
+// Tensor-core path of the compact nibble GEMM: taken for batches of at least nibble_tc_min_m
+// tokens with K a multiple of 128 (the stage depth) and 16-byte scale rows; *used reports
+// whether it ran.
 int gemm_tc_nibble_launch(const jkb_nibble_matrix *w, const jkb_act_q8 *act, float *out,
                           size_t row_begin, size_t row_end, cudaStream_t st, bool *used) {
     *used = false;
     const size_t k = w->cols;
     const bool mins = w->quant == JKB_Q4_1 || w->quant == JKB_Q4_K_M;
-    if (k % BK != 0 || act->m < TC_MIN_M || act->k_pad != k || act->m > (size_t)INT32_MAX ||
+    // the scale-word rows must be 16-byte multiples (the TMA's row pitch): Q4_0 / IQ4_NL need
+    // cols % 256 == 0, the other formats hold already at cols % 128 == 0
+    const size_t mpitch = w->nb * w->meta_bytes;
+    if (k % BK != 0 || mpitch % 16 != 0 || act->m < nibble_tc_min_m(w->rows) ||
+        act->k_pad != k ||
+        act->m > (size_t)INT32_MAX ||
         w->rows > (size_t)INT32_MAX || act->x_scales_t == nullptr ||
         (mins && act->x_nsums_t == nullptr))
         return JKB_OK;
@@ -931,19 +967,19 @@ int gemm_tc_nibble_launch(const jkb_nibble_matrix *w, const jkb_act_q8 *act, flo
     int *err = device_error_word();
     if (!err) return JKB_OK;
     *used = true;
-    const int bn = choose_tile(act->m, row_end - row_begin, mins);
     const bool exact = g_gemm_exact.load(std::memory_order_relaxed);
     switch (w->quant) {
         case JKB_Q4_0:
-            return launch_nib_fmt<NIB_Q4_0>(bn, exact, w, act, out, row_begin, row_end, st, err);
+            return launch_nib_fmt<NIB_Q4_0>(exact, w, act, out, row_begin, row_end, st, err);
         case JKB_Q4_1:
-            return launch_nib_fmt<NIB_Q4_1>(bn, exact, w, act, out, row_begin, row_end, st, err);
+            return launch_nib_fmt<NIB_Q4_1>(exact, w, act, out, row_begin, row_end, st, err);
         case JKB_IQ4_NL:
-            return launch_nib_fmt<NIB_IQ4_NL>(bn, exact, w, act, out, row_begin, row_end, st, err);
+            return launch_nib_fmt<NIB_IQ4_NL>(exact, w, act, out, row_begin, row_end, st, err);
         default:
-            return launch_nib_fmt<NIB_Q4_K>(bn, exact, w, act, out, row_begin, row_end, st, err);
+            return launch_nib_fmt<NIB_Q4_K>(exact, w, act, out, row_begin, row_end, st, err);
     }
 }
+
 
 }  // namespace jkb
 

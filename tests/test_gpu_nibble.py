@@ -63,11 +63,15 @@ def _gemm(jkb, nm, act, m, cols, rows, r=None):
     return host(out).reshape(m, n)
 
 
-# (m, rows, cols): row kernel shapes (m < 32 or cols % 128 != 0) and tensor-core shapes
+# (m, rows, cols): row kernel shapes (m below the tensor-core threshold -- at most 32, from 8 on
+# large matrices -- or cols % 128 != 0) and tensor-core shapes
 ROWS_SHAPES = [(1, 203, 512), (5, 64, 256), (17, 256, 512), (31, 130, 1024), (40, 77, 160),
                (64, 33, 800)]
 TC_SHAPES = [(32, 128, 256), (64, 300, 1024), (100, 203, 4096), (200, 256, 512),
-             (512, 1024, 2048), (96, 12800, 256)]
+             (512, 1024, 2048), (96, 12800, 256), (512, 18944, 256), (9, 14336, 256)]
+# (96, 12800, 256) and (512, 18944, 256) select the 96- and 128-token tiles (formats without min
+# terms; the min formats take 96 or 64, IQ4_NL always 64); (9, 14336, 256) is a 9-token batch
+# that takes the tensor cores on a large matrix
 
 
 def _cols_ok(quant, cols):
@@ -85,6 +89,17 @@ def test_nibble_row_kernel_bit_exact(jkb, oracle, quant, m, rows, cols):
     got = _gemm(jkb, nm, act, m, cols, rows)
     ref = _oracle(oracle, quant, wb, rows, cols, act, m)
     assert np.array_equal(bits(got), bits(ref))
+
+
+@pytest.mark.parametrize("quant", [Q4_0, IQ4_NL])
+def test_nibble_unaligned_scale_rows_take_row_kernel(jkb, oracle, quant):
+    """Q4_0 / IQ4_NL with cols % 256 != 0: the f16 scale rows are not 16-byte multiples, so even
+    large batches run the row kernel -- bit for bit in the default epilogue."""
+    m, rows, cols = 48, 96, 384
+    wb = _weights(oracle, quant, rows, cols, 61)
+    act = oracle.normal(m * cols, 62, 1.0)
+    got = _gemm(jkb, _matrix(jkb, quant, wb, rows, cols), act, m, cols, rows)
+    assert np.array_equal(bits(got), bits(_oracle(oracle, quant, wb, rows, cols, act, m)))
 
 
 @pytest.mark.parametrize("quant", FORMATS)
