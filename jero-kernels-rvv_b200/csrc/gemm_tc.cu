@@ -77,6 +77,16 @@ struct TcCfg {
     // operations; IQ4_NL's code-book lookups take four, one on each SM sub-partition.
     static constexpr int NIB = NIB_;
     static constexpr int CONV = NIB == NIB_IQ4_NL ? 4 : NIB ? 2 : 0;  // converter warps
+    // Q4_K_M in the fused multiply-add epilogue: the odd groups of a 256-element block (the
+    // high nibbles of its bytes) enter the MMA in place as 16 * code (unsigned A) and their
+    // scales carry the 1/16. Powers of two scale exactly, so the products equal the plain
+    // expansion's unless a scale product falls below the normal range; the exact epilogue keeps
+    // the plain expansion.
+    static constexpr bool HI16 = NIB == NIB_Q4_K && !EXACT;
+    // Q4_0: the codes enter the MMA as they are (unsigned A, 0..15) and a second MMA per group
+    // adds a constant -8 tile times the same activations into the same accumulator: the exact
+    // integer sum of (code - 8) * x without per-element offsets in the conversion.
+    static constexpr bool NEG8 = NIB == NIB_Q4_0;
     static constexpr int SPL = H16 ? 2 : 1;    // accumulators per 32-element slice
     static constexpr int NA = GPR * SPL;       // accumulators per round
     static constexpr int NG = GPS * SPL;       // weight-scale groups per stage
@@ -95,7 +105,7 @@ struct TcCfg {
             : SA + SB + BMW * NG * 4 + GPS * BN * 4 + (MINS ? BMW * GPS * 4 + GPS * BN * 4 : 0);
     static constexpr int STAGE_SMEM =
         STAGE_TX + (H16 ? 2 * SB : 0) + (NIB ? SA + BMW * NG * 4 + (MINS ? BMW * GPS * 4 : 0) : 0);
-    static constexpr int STAGES_FIT = (200 * 1024) / STAGE_SMEM;
+    static constexpr int STAGES_FIT = ((NEG8 ? 184 : 200) * 1024) / STAGE_SMEM;
     static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
     static_assert((COLS == 32 || COLS == 64) && BN % 32 == 0 && BN <= 256, "tile shape");
     static_assert(GPS % GPR == 0 && 2 * NA * BN <= TMEM_COLS, "two rounds of NA buffers");
@@ -122,6 +132,7 @@ struct TcSmem {
     alignas(128) float xs[C::STAGES][GPS][C::BN];
     alignas(128) float wm[C::MINS ? C::STAGES : 1][BMW][GPS];     // weight mins (MINS)
     alignas(128) float xn[C::MINS ? C::STAGES : 1][GPS][C::BN];   // -x_sums, permuted like xs
+    alignas(1024) uint8_t neg8[C::NEG8 ? C::SA : 1024];  // NEG8: a weight tile of -8
     uint64_t full[C::STAGES], empty[C::STAGES], masked[C::STAGES], tfull[2], tempty[2], done;
     uint32_t tmem_base;
     int abort_flag;
@@ -227,6 +238,16 @@ __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t
         "l"(adesc), "l"(bdesc), "r"(idesc)
         : "memory");
 }
+// D[tmem] += A x B^T
+__device__ __forceinline__ void mma_i8_acc(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                           uint32_t idesc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, 1, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc)
+        : "memory");
+}
 // 16x256b.x4: 16 TMEM lanes x 32 columns; lane t gets rows t/4 and t/4 + 8 of the 16 and, per
 // 8-column repeat r, registers 4r..4r+3 = (row t/4, columns 8r + 2(t%4) + {0,1}), then the same
 // columns of row t/4 + 8.
@@ -293,18 +314,27 @@ __device__ __forceinline__ void nib_convert(TcSmem<C> &sm, int s, int ks, int e)
         const uint4 v = *reinterpret_cast<const uint4 *>(&sm.mt[C::NIB ? s : 0][16 * r]);
         float4 w4, n4 = make_float4(0.f, 0.f, 0.f, 0.f);
         if (F == NIB_Q4_K) {
-            // the header of the 256-element block; this stage holds its groups 4(ks&1)..+3
+            // the header of the 256-element block; this stage holds its groups 4h..4h+3,
+            // h = ks & 1. Their 6-bit scales and mins, one per byte (unpack_q4_q5_k_scales_mins,
+            // quant_q8.rs:1818-1830; v.y, v.z, v.w = scales[0..4], [4..8], [8..12]):
+            //   h = 0: sc = scales[g] & 63, m = scales[g + 4] & 63
+            //   h = 1: sc = scales[g + 8] & 15 | (scales[g] >> 6) << 4,
+            //          m = scales[g + 8] >> 4 | (scales[g + 4] >> 6) << 4
             const float d = nib_f16_finite(v.x & 0xFFFF), dmin = nib_f16_finite(v.x >> 16);
-            float sw[4], sm4[4];
-#pragma unroll
-            for (int g = 0; g < 4; g++) {
-                int sc, mn;
-                nib_k4_scale_min(v.y, v.z, v.w, 4 * (ks & 1) + g, sc, mn);
-                sw[g] = __fmul_rn(d, (float)sc);
-                sm4[g] = __fmul_rn(dmin, (float)mn);
+            uint32_t scb, mnb;
+            if (ks & 1) {
+                scb = (v.w & 0x0F0F0F0Fu) | ((v.y >> 2) & 0x30303030u);
+                mnb = ((v.w >> 4) & 0x0F0F0F0Fu) | ((v.z >> 2) & 0x30303030u);
+            } else {
+                scb = v.y & 0x3F3F3F3Fu;
+                mnb = v.z & 0x3F3F3F3Fu;
             }
-            w4 = make_float4(sw[0], sw[1], sw[2], sw[3]);
-            n4 = make_float4(sm4[0], sm4[1], sm4[2], sm4[3]);
+            // groups 1 and 3 are the high nibbles: with HI16 their scale carries 1/16
+            const float dh = C::HI16 ? __fmul_rn(d, 0.0625f) : d;
+            w4 = make_float4(__fmul_rn(d, nib_byte_f32<0>(scb)), __fmul_rn(dh, nib_byte_f32<1>(scb)),
+                             __fmul_rn(d, nib_byte_f32<2>(scb)), __fmul_rn(dh, nib_byte_f32<3>(scb)));
+            n4 = make_float4(__fmul_rn(dmin, nib_byte_f32<0>(mnb)), __fmul_rn(dmin, nib_byte_f32<1>(mnb)),
+                             __fmul_rn(dmin, nib_byte_f32<2>(mnb)), __fmul_rn(dmin, nib_byte_f32<3>(mnb)));
         } else if (F == NIB_Q4_1) {
             // (d, m) of the stage's 4 blocks
             w4 = make_float4(nib_f16_finite(v.x), nib_f16_finite(v.y), nib_f16_finite(v.z),
@@ -326,12 +356,15 @@ __device__ __forceinline__ void nib_convert(TcSmem<C> &sm, int s, int ks, int e)
         const int q = e + i * N;
         const int r = q >> 2, j = q & 3;
         const uint4 c = *reinterpret_cast<const uint4 *>(&sm.an[C::NIB ? s : 0][r * 64 + 16 * j]);
+        // NEG8: Q4_0 codes as they are (the -8 comes from the second MMA)
+        constexpr int FV = C::NEG8 ? NIB_Q4_1 : F;
         const uint4 lo = make_uint4(
-            nib_values4<F>(c.x & 0x0F0F0F0Fu), nib_values4<F>(c.y & 0x0F0F0F0Fu),
-            nib_values4<F>(c.z & 0x0F0F0F0Fu), nib_values4<F>(c.w & 0x0F0F0F0Fu));
-        const uint4 hi = make_uint4(
-            nib_values4<F>((c.x >> 4) & 0x0F0F0F0Fu), nib_values4<F>((c.y >> 4) & 0x0F0F0F0Fu),
-            nib_values4<F>((c.z >> 4) & 0x0F0F0F0Fu), nib_values4<F>((c.w >> 4) & 0x0F0F0F0Fu));
+            nib_values4<FV>(c.x & 0x0F0F0F0Fu), nib_values4<FV>(c.y & 0x0F0F0F0Fu),
+            nib_values4<FV>(c.z & 0x0F0F0F0Fu), nib_values4<FV>(c.w & 0x0F0F0F0Fu));
+        const uint4 hi = C::HI16
+            ? make_uint4(c.x & 0xF0F0F0F0u, c.y & 0xF0F0F0F0u, c.z & 0xF0F0F0F0u, c.w & 0xF0F0F0F0u)
+            : make_uint4(nib_values4<FV>((c.x >> 4) & 0x0F0F0F0Fu), nib_values4<FV>((c.y >> 4) & 0x0F0F0F0Fu),
+                         nib_values4<FV>((c.z >> 4) & 0x0F0F0F0Fu), nib_values4<FV>((c.w >> 4) & 0x0F0F0F0Fu));
         // Q4_K_M chunk j holds elements 64(j/2) + 16(j&1) (low nibbles) and + 32 (high); the
         // other formats' chunk j is block j: elements 32j (low) and 32j + 16 (high)
         const int ulo = F == NIB_Q4_K ? 4 * (j >> 1) + (j & 1) : 2 * j;
@@ -380,6 +413,13 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                          smem_u32(&sm.tmem_base)),
                      "r"(C::TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (C::NEG8) {
+        // the constant -8 tile (every byte 0xF8), read by the tensor core (async proxy)
+        for (int i = threadIdx.x; i < C::SA / 16; i += C::THREADS)
+            reinterpret_cast<uint4 *>(sm.neg8)[i] = make_uint4(0xF8F8F8F8u, 0xF8F8F8F8u,
+                                                                0xF8F8F8F8u, 0xF8F8F8F8u);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     tc_fence_before();
     __syncthreads();
@@ -438,7 +478,10 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t IDESC = idesc_i8(BN);
+            // A unsigned for the in-place high nibbles (HI16) and the raw codes (NEG8)
+            constexpr uint32_t IDESC = idesc_i8(BN) & ~((C::HI16 || C::NEG8) ? (1u << 7) : 0u);
+            constexpr uint32_t IDESC_S = idesc_i8(BN);
+            const uint64_t nd = smem_desc(sm.neg8);
             uint32_t it = 0, rc = 0;  // stage and round counters
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
@@ -469,6 +512,9 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                                        IDESC);
                             } else {
                                 mma_i8(d, ad + (uint64_t)(2 * g), bd + (uint64_t)(2 * g), IDESC);
+                                if (C::NEG8)
+                                    mma_i8_acc(d, nd + (uint64_t)(2 * g), bd + (uint64_t)(2 * g),
+                                               IDESC_S);
                             }
                         }
                         tc_commit(&sm.tfull[rb]);

@@ -55,6 +55,12 @@ __device__ __forceinline__ void nib_k4_scale_min(uint32_t w1, uint32_t w2, uint3
     }
 }
 
+// Byte K (0..3) of w as an exact f32: 0x4B0000XX is 2^23 + XX.
+template <int K>
+__device__ __forceinline__ float nib_byte_f32(uint32_t w) {
+    return __int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7540u + K)) - 8388608.0f;
+}
+
 // Four nibble codes (one per byte, 0..15) to the int8 weight values of format F:
 // Q4_0 code - 8; IQ4_NL the code book KVALUES_IQ4NL (quant.rs:80-82); Q4_1 / Q4_K_M the code.
 template <int F>
