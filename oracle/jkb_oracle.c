@@ -327,6 +327,54 @@ float or_dot_q4_k_q8_k_block(const uint8_t *w, const or_block_q8_k *x, int32_t *
     return (d * x->d) * i2f(sumi) - (dmin * x->d) * i2f(summins);
 }
 
+/* quant_q8.rs:688-703 (dot_q5_0_q8_0_block_scalar): f16 d, u32 qh, 16 nibble bytes; element j
+ * = (low nibble of byte j | bit j of qh << 4) - 16, element j + 16 = (high nibble | bit j + 16
+ * << 4) - 16. Zero when d == 0 or xd == 0; else (f32)sumi * (d * xd). */
+float or_dot_q5_0_q8_0_block(const uint8_t *w, const or_block_q8_0 *x, int32_t *sumi_out) {
+    float dw = or_f16_to_f32_finite(rd16(w));
+    uint32_t qh = (uint32_t)w[2] | ((uint32_t)w[3] << 8) | ((uint32_t)w[4] << 16) |
+                  ((uint32_t)w[5] << 24);
+    int32_t sumi = 0;
+    for (int j = 0; j < 16; j++) {
+        int32_t q0 = (int32_t)((w[6 + j] & 0x0F) | (((qh >> j) & 1) << 4)) - 16;
+        int32_t q1 = (int32_t)(((w[6 + j] >> 4) & 0x0F) | (((qh >> (j + 16)) & 1) << 4)) - 16;
+        sumi += q0 * x->qs[j] + q1 * x->qs[j + 16];
+    }
+    if (sumi_out) *sumi_out = sumi;
+    if (dw == 0.0f || x->d == 0.0f) return 0.0f;
+    return i2f(sumi) * (dw * x->d);
+}
+
+/* quant_q8.rs:1866-1899 (dot_q5_k_q8_k_block_scalar): the Q4_K block with a fifth bit per
+ * element from qh[32] @16 (bit 2c for the low half of chunk c, 2c + 1 for the high half); qs
+ * @48. Block value (d * xd) * sumi - (dmin * xd) * summins. */
+float or_dot_q5_k_q8_k_block(const uint8_t *w, const or_block_q8_k *x, int32_t *sumi_out,
+                             int32_t *summins_out) {
+    float d = or_f16_to_f32_finite(rd16(w));
+    float dmin = or_f16_to_f32_finite(rd16(w + 2));
+    uint8_t sc[8], mn[8];
+    unpack_k4_scales(w + 4, sc, mn);
+    const uint8_t *qh = w + 16, *qs = w + 48;
+    int32_t sumi = 0, summins = 0;
+    for (int c = 0; c < 4; c++) {
+        int32_t slo = 0, shi = 0;
+        for (int l = 0; l < 32; l++) {
+            uint8_t b = qs[c * 32 + l];
+            int32_t h1 = (qh[l] >> (2 * c)) & 1 ? 16 : 0, h2 = (qh[l] >> (2 * c + 1)) & 1 ? 16 : 0;
+            slo += ((int32_t)(b & 0x0F) | h1) * x->qs[c * 64 + l];
+            shi += ((int32_t)(b >> 4) | h2) * x->qs[c * 64 + 32 + l];
+        }
+        sumi += (int32_t)sc[2 * c] * slo + (int32_t)sc[2 * c + 1] * shi;
+        int32_t blo = (int32_t)x->bsums[4 * c] + x->bsums[4 * c + 1];
+        int32_t bhi = (int32_t)x->bsums[4 * c + 2] + x->bsums[4 * c + 3];
+        summins += (int32_t)mn[2 * c] * blo + (int32_t)mn[2 * c + 1] * bhi;
+    }
+    if (sumi_out) *sumi_out = sumi;
+    if (summins_out) *summins_out = summins;
+    if ((d == 0.0f && dmin == 0.0f) || x->d == 0.0f) return 0.0f;
+    return (d * x->d) * i2f(sumi) - (dmin * x->d) * i2f(summins);
+}
+
 /* quant_q8.rs:1903-1942: ql[128] qh[64] i8 scales[16] f16 d @208; quads of 16 with i8 scales. */
 float or_dot_q6_k_q8_k_block(const uint8_t *w, const or_block_q8_k *x, int32_t *sumi_out) {
     float d = or_f16_to_f32_finite(rd16(w + 208));
@@ -437,6 +485,7 @@ static const fmt_t FMTS[] = {
     {OR_Q4_0, 32, 18, 0, 1},   {OR_Q8_0, 32, 34, 0, 1},    {OR_Q4_K, 256, 144, 1, 1},
     {OR_Q6_K, 256, 210, 1, 1}, {OR_TQ2_0, 256, 66, 1, 1}, {OR_TQ1_0, 256, 54, 1, 1},
     {OR_I2_S, 128, 32, 0, 1},  {OR_Q4_1, 32, 20, 0, 0},   {OR_IQ4_NL, 32, 18, 0, 0},
+    {OR_Q5_0, 32, 22, 0, 1},   {OR_Q5_K, 256, 176, 1, 1},
 };
 
 static const fmt_t *fmt_of(int quant) {
@@ -467,6 +516,8 @@ static float block_value(int quant, const uint8_t *w, const void *x, size_t b, i
     case OR_Q4_0: return or_dot_q4_0_q8_0_block(w, (const or_block_q8_0 *)x + b, si);
     case OR_Q8_0: return or_dot_q8_0_q8_0_block(w, (const or_block_q8_0 *)x + b, si);
     case OR_Q4_K: return or_dot_q4_k_q8_k_block(w, (const or_block_q8_k *)x + b, si, sm);
+    case OR_Q5_0: return or_dot_q5_0_q8_0_block(w, (const or_block_q8_0 *)x + b, si);
+    case OR_Q5_K: return or_dot_q5_k_q8_k_block(w, (const or_block_q8_k *)x + b, si, sm);
     case OR_Q6_K: return or_dot_q6_k_q8_k_block(w, (const or_block_q8_k *)x + b, si);
     case OR_TQ2_0: return or_dot_tq2_0_q8_k_block(w, (const or_block_q8_k *)x + b, si);
     case OR_TQ1_0: return or_dot_tq1_0_q8_k_block(w, (const or_block_q8_k *)x + b, si);
@@ -627,6 +678,48 @@ void or_dequantize_block(int quant, const uint8_t *blk, float i2s_scale, float *
             for (int l = 0; l < 32; l++) out[64 * c + l] = d1 * (float)(qs[32 * c + l] & 0x0F) - m1;
             for (int l = 0; l < 32; l++)
                 out[64 * c + 32 + l] = d2 * (float)((qs[32 * c + l] >> 4) & 0x0F) - m2;
+        }
+        return;
+    }
+    case OR_Q5_0: {
+        /* quant.rs:140-163: y = d * ((nibble | high bit << 4) - 16); zeros when d == 0 */
+        float d = or_f16_to_f32_finite(rd16(blk));
+        if (d == 0.0f) {
+            memset(out, 0, 32 * sizeof(float));
+            return;
+        }
+        uint32_t qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) | ((uint32_t)blk[4] << 16) |
+                      ((uint32_t)blk[5] << 24);
+        for (int j = 0; j < 16; j++) {
+            int q0 = (int)((blk[6 + j] & 0x0F) | (((qh >> j) & 1) << 4)) - 16;
+            int q1 = (int)(((blk[6 + j] >> 4) & 0x0F) | (((qh >> (j + 16)) & 1) << 4)) - 16;
+            out[j] = d * (float)q0;
+            out[j + 16] = d * (float)q1;
+        }
+        return;
+    }
+    case OR_Q5_K: {
+        /* quant.rs:651-705: y = (d * sc) * q - dmin * m, q = nibble + 16 * high bit; zeros when
+         * d == dmin == 0 */
+        float d = or_f16_to_f32_finite(rd16(blk)), dmin = or_f16_to_f32_finite(rd16(blk + 2));
+        if (d == 0.0f && dmin == 0.0f) {
+            memset(out, 0, 256 * sizeof(float));
+            return;
+        }
+        uint8_t sc[8], m[8];
+        unpack_k4_scales(blk + 4, sc, m);
+        const uint8_t *qh = blk + 16, *qs = blk + 48;
+        for (int c = 0; c < 4; c++) {
+            float d1 = d * (float)sc[2 * c], m1 = dmin * (float)m[2 * c];
+            float d2 = d * (float)sc[2 * c + 1], m2 = dmin * (float)m[2 * c + 1];
+            for (int l = 0; l < 32; l++) {
+                int q1 = (qs[32 * c + l] & 0x0F) + (((qh[l] >> (2 * c)) & 1) ? 16 : 0);
+                out[64 * c + l] = d1 * (float)q1 - m1;
+            }
+            for (int l = 0; l < 32; l++) {
+                int q2 = (qs[32 * c + l] >> 4) + (((qh[l] >> (2 * c + 1)) & 1) ? 16 : 0);
+                out[64 * c + 32 + l] = d2 * (float)q2 - m2;
+            }
         }
         return;
     }
@@ -841,7 +934,9 @@ size_t or_repack_scale_groups(int quant, size_t cols) {
     return quant == OR_Q6_K ? kp / 16 : kp / 32;
 }
 
-int or_repack_has_mins(int quant) { return quant == OR_Q4_K || quant == OR_Q4_1; }
+int or_repack_has_mins(int quant) {
+    return quant == OR_Q4_K || quant == OR_Q4_1 || quant == OR_Q5_K;
+}
 
 int or_repack_block_scaled(int quant, const uint8_t *raw, size_t raw_len, size_t rows,
                            size_t cols, int8_t *q, float *scales, float *mins) {
@@ -925,6 +1020,43 @@ int or_repack_block_scaled(int quant, const uint8_t *raw, size_t raw_len, size_t
                 float d = quant == OR_TQ2_0 ? unpack_tq2_0(blk, t) : unpack_tq1_0(blk, t);
                 for (int s = 0; s < 8; s++) sr[b * 8 + s] = d;
                 memcpy(qr + 256 * b, t, 256);
+                break;
+            }
+            case OR_Q5_0: {
+                /* repack.rs:1827-1840: scale d; quants (5-bit code - 16) left 0 when d == 0 */
+                float d = or_f16_to_f32_finite(rd16(blk));
+                sr[b] = d;
+                uint32_t qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) |
+                              ((uint32_t)blk[4] << 16) | ((uint32_t)blk[5] << 24);
+                if (d != 0.0f)
+                    for (int j = 0; j < 16; j++) {
+                        qr[32 * b + j] =
+                            (int8_t)((int)((blk[6 + j] & 0x0F) | (((qh >> j) & 1) << 4)) - 16);
+                        qr[32 * b + 16 + j] = (int8_t)(
+                            (int)(((blk[6 + j] >> 4) & 0x0F) | (((qh >> (j + 16)) & 1) << 4)) - 16);
+                    }
+                break;
+            }
+            case OR_Q5_K: {
+                /* repack.rs:1959-1995: scales d * sc, mins dmin * m, unsigned 5-bit quants */
+                float d = or_f16_to_f32_finite(rd16(blk));
+                float dmin = or_f16_to_f32_finite(rd16(blk + 2));
+                uint8_t sc[8], m[8];
+                unpack_k4_scales(blk + 4, sc, m);
+                const uint8_t *qh = blk + 16, *qs = blk + 48;
+                for (int c = 0; c < 4; c++) {
+                    size_t g0 = b * 8 + 2 * c;
+                    sr[g0] = d * (float)sc[2 * c];
+                    mr[g0] = dmin * (float)m[2 * c];
+                    sr[g0 + 1] = d * (float)sc[2 * c + 1];
+                    mr[g0 + 1] = dmin * (float)m[2 * c + 1];
+                    for (int l = 0; l < 32; l++) {
+                        qr[256 * b + 64 * c + l] =
+                            (int8_t)((qs[32 * c + l] & 0x0F) + (((qh[l] >> (2 * c)) & 1) ? 16 : 0));
+                        qr[256 * b + 64 * c + 32 + l] =
+                            (int8_t)((qs[32 * c + l] >> 4) + (((qh[l] >> (2 * c + 1)) & 1) ? 16 : 0));
+                    }
+                }
                 break;
             }
             case OR_Q4_1: {
@@ -1433,6 +1565,83 @@ static void quant_iq4_nl_block(const float *x, uint8_t *o) {
     for (int j = 0; j < 16; j++) o[2 + j] = (uint8_t)(idx[j] | (idx[16 + j] << 4));
 }
 
+/* Q5_0: the published ggml reference rule (signed max / -16, q = min(31, trunc(x/d + 16.5)),
+ * the fifth bits in qh). */
+static void quant_q5_0_block(const float *x, uint8_t *o) {
+    float amax = 0.0f, mx = 0.0f;
+    for (int i = 0; i < 32; i++)
+        if (fabsf(x[i]) > amax) {
+            amax = fabsf(x[i]);
+            mx = x[i];
+        }
+    float d = mx / -16.0f;
+    float id = d != 0.0f ? 1.0f / d : 0.0f;
+    wr16(o, or_f32_to_f16(d));
+    uint32_t qh = 0;
+    for (int j = 0; j < 16; j++) {
+        int q0 = (int)(x[j] * id + 16.5f), q1 = (int)(x[16 + j] * id + 16.5f);
+        if (q0 > 31) q0 = 31;
+        if (q1 > 31) q1 = 31;
+        if (q0 < 0) q0 = 0;
+        if (q1 < 0) q1 = 0;
+        o[6 + j] = (uint8_t)((q0 & 0x0F) | ((q1 & 0x0F) << 4));
+        qh |= (uint32_t)((q0 >> 4) & 1) << j;
+        qh |= (uint32_t)((q1 >> 4) & 1) << (j + 16);
+    }
+    o[2] = (uint8_t)qh;
+    o[3] = (uint8_t)(qh >> 8);
+    o[4] = (uint8_t)(qh >> 16);
+    o[5] = (uint8_t)(qh >> 24);
+}
+
+/* Q5_K: the Q4_K rule with 5-bit codes (0..31), the fifth bits in qh[32]. */
+static void quant_q5_k_block(const float *x, uint8_t *o) {
+    float scale[8], minv[8], max_scale = 0.0f, max_min = 0.0f;
+    for (int j = 0; j < 8; j++) {
+        float lo = x[32 * j], hi = x[32 * j];
+        for (int i = 1; i < 32; i++) {
+            lo = fminf(lo, x[32 * j + i]);
+            hi = fmaxf(hi, x[32 * j + i]);
+        }
+        if (lo > 0.0f) lo = 0.0f;
+        scale[j] = (hi - lo) / 31.0f;
+        minv[j] = -lo;
+        if (scale[j] > max_scale) max_scale = scale[j];
+        if (minv[j] > max_min) max_min = minv[j];
+    }
+    float d = max_scale / 63.0f, dmin = max_min / 63.0f;
+    uint8_t ls[8], lm[8];
+    for (int j = 0; j < 8; j++) {
+        int a = d > 0.0f ? (int)lrintf(scale[j] / d) : 0, b = dmin > 0.0f ? (int)lrintf(minv[j] / dmin) : 0;
+        ls[j] = (uint8_t)(a < 0 ? 0 : a > 63 ? 63 : a);
+        lm[j] = (uint8_t)(b < 0 ? 0 : b > 63 ? 63 : b);
+    }
+    uint16_t dh = or_f32_to_f16(d), mh = or_f32_to_f16(dmin);
+    wr16(o, dh);
+    wr16(o + 2, mh);
+    uint8_t *s = o + 4;
+    for (int j = 0; j < 4; j++) {
+        s[j] = (uint8_t)((ls[j] & 63) | ((ls[j + 4] >> 4) << 6));
+        s[j + 4] = (uint8_t)((lm[j] & 63) | ((lm[j + 4] >> 4) << 6));
+        s[j + 8] = (uint8_t)((ls[j + 4] & 15) | ((lm[j + 4] & 15) << 4));
+    }
+    float df = or_f16_to_f32_ieee(dh), mf = or_f16_to_f32_ieee(mh);
+    uint8_t *qh = o + 16, *qs = o + 48;
+    memset(qh, 0, 32);
+    for (int c = 0; c < 4; c++)
+        for (int l = 0; l < 32; l++) {
+            int q[2];
+            for (int h = 0; h < 2; h++) {
+                int j = 2 * c + h;
+                float dl = df * (float)ls[j], ml = mf * (float)lm[j];
+                int v = dl > 0.0f ? (int)lrintf((x[64 * c + 32 * h + l] + ml) / dl) : 0;
+                q[h] = v < 0 ? 0 : v > 31 ? 31 : v;
+            }
+            qs[32 * c + l] = (uint8_t)((q[0] & 15) | ((q[1] & 15) << 4));
+            qh[l] |= (uint8_t)(((q[0] >> 4) << (2 * c)) | ((q[1] >> 4) << (2 * c + 1)));
+        }
+}
+
 int or_quantize_weights(int quant, const float *w, size_t rows, size_t cols, uint8_t *out) {
     const fmt_t *f = fmt_of(quant);
     if (!f || cols % f->be) return 1;
@@ -1447,6 +1656,8 @@ int or_quantize_weights(int quant, const float *w, size_t rows, size_t cols, uin
             case OR_Q4_K: quant_q4_k_block(x, o); break;
             case OR_Q6_K: quant_q6_k_block(x, o); break;
             case OR_Q4_1: quant_q4_1_block(x, o); break;
+            case OR_Q5_0: quant_q5_0_block(x, o); break;
+            case OR_Q5_K: quant_q5_k_block(x, o); break;
             case OR_IQ4_NL: quant_iq4_nl_block(x, o); break;
             default: return 1;
             }

@@ -40,8 +40,10 @@ typedef struct {
 enum {
     OR_Q4_0 = 2,
     OR_Q4_1 = 3,
+    OR_Q5_0 = 6,
     OR_Q8_0 = 8,
     OR_Q4_K = 12,
+    OR_Q5_K = 13,
     OR_Q6_K = 14,
     OR_IQ4_NL = 20,
     OR_TQ1_0 = 34,
@@ -71,6 +73,9 @@ float or_dot_q8_0_q8_0_block(const uint8_t *w, const or_block_q8_0 *x, int32_t *
 float or_dot_q4_k_q8_k_block(const uint8_t *w, const or_block_q8_k *x, int32_t *sumi,
                              int32_t *summins);
 float or_dot_q6_k_q8_k_block(const uint8_t *w, const or_block_q8_k *x, int32_t *sumi);
+float or_dot_q5_0_q8_0_block(const uint8_t *w, const or_block_q8_0 *x, int32_t *sumi);
+float or_dot_q5_k_q8_k_block(const uint8_t *w, const or_block_q8_k *x, int32_t *sumi,
+                             int32_t *summins);
 float or_dot_tq2_0_q8_k_block(const uint8_t *w, const or_block_q8_k *x, int32_t *sumi);
 float or_dot_tq1_0_q8_k_block(const uint8_t *w, const or_block_q8_k *x, int32_t *sumi);
 

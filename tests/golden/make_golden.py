@@ -107,6 +107,38 @@ def kats():
     out["iq4_nl_dequant"] = {"ref": "src/quant.rs:2895-2905",
                              "block_hex": (h16(0x3C00) + bytes([0xF0, 0x08]) + bytes(14)).hex(),
                              "expect": {"0": -127.0, "16": 113.0, "1": 1.0, "17": -127.0}}
+    # quant.rs:2665-2697: Q5_K d = 1.0, dmin = 0.5, scales[0..8] = 2,3,4,5,1,2,3,4, qh = 0x09,
+    # qs[0..32] = 0x53, qs[32..64] = 0x24: the 256 dequantized values sum to 4928, and the f32
+    # matvec against ones gives 4928.
+    raw = bytearray(176)
+    raw[0:2] = h16(0x3C00)
+    raw[2:4] = h16(0x3800)
+    for i, v in ((4, 2), (8, 1), (5, 3), (9, 2), (6, 4), (10, 3), (7, 5), (11, 4)):
+        raw[i] = v
+    raw[16:48] = bytes([0x09] * 32)
+    raw[48:80] = bytes([0x53] * 32)
+    raw[80:112] = bytes([0x24] * 32)
+    out["q5_k_dequant_sum"] = {"ref": "src/quant.rs:2665-2697", "quant": 13, "rows": 1,
+                               "cols": 256, "block_hex": bytes(raw).hex(), "input": [1.0] * 256,
+                               "expected": [4928.0], "abs_tol": 1e-3, "sum": 4928.0}
+    # quant.rs:2855-2862: Q5_0 d = 0.5, qh bit 0 set, qs[0] = 0x21: element 0 is
+    # (1 | 16) - 16 = 1 -> 0.5, element 16 is (2 | 0) - 16 = -14 -> -7.
+    blk = h16(0x3800) + bytes([1, 0, 0, 0]) + bytes([0x21]) + bytes(15)
+    out["q5_0_dequant"] = {"ref": "src/quant.rs:2855-2862", "block_hex": blk.hex(),
+                           "expect": {"0": 0.5, "16": -7.0}}
+    # quant.rs:2910-2966: a two-block Q5_0 row (d = 0.5 / 1.0, qh 0xAAAA5555 / 0x0F0FF0F0, the
+    # nibble patterns below) against x = (i - 31) / 16 (f32 path) and against the Q8_0 blocks of
+    # d = 1.0, q = i - 31 (Q8 path): both within 1e-4 of the f32 dot with the dequantized row.
+    row = bytearray(44)
+    row[0:2] = h16(0x3800)
+    row[2:6] = struct.pack("<I", 0xAAAA5555)
+    for i in range(16):
+        row[6 + i] = (i & 0x0F) | (((15 - i) & 0x0F) << 4)
+    row[22:24] = h16(0x3C00)
+    row[24:28] = struct.pack("<I", 0x0F0FF0F0)
+    row[28:44] = bytes([0x5A] * 16)
+    out["q5_0_two_block_row"] = {"ref": "src/quant.rs:2910-2966", "row_hex": bytes(row).hex(),
+                                 "abs_tol": 1e-4}
     # quant_q8.rs:3414-3482: quantizer sanitization on test_f32_row inputs.
     out["q8_sanitize"] = {"ref": "src/quant_q8.rs:3388-3395,3414-3482"}
     return out
@@ -127,6 +159,7 @@ def fixtures():
         ("q4_k", O.Q4_K, 5, 512), ("q4_k_b", O.Q4_K, 19, 1024),
         ("q6_k", O.Q6_K, 5, 512), ("q6_k_b", O.Q6_K, 21, 768),
         ("tq2_0", O.TQ2_0, 7, 512),
+        ("q5_0", O.Q5_0, 9, 512), ("q5_k", O.Q5_K, 7, 768),
     ]
     for name, q, rows, cols in cases:
         seed = sum(map(ord, name))

@@ -413,3 +413,57 @@ def test_nibble_golden_fixtures_match_live_oracle(oracle):
         nq, ws, wm = oracle.nibble_decode(q, f[f"{name}__w"], rows, cols)
         out = oracle.gemm_nibble(q, nq, ws, wm, rows, cols, xq, xs, xsum, m)
         assert np.array_equal(out.view(np.uint32), f[f"{name}__out"].view(np.uint32))
+
+
+# ---------------------------------------------------------------- Q5_0 / Q5_K
+
+def test_q5_k_kat_4928(oracle, kats):
+    """quant.rs:2665-2697: the Q5_K block dequantizes to values summing to 4928, and the f32
+    matvec with ones returns 4928."""
+    k = kats["q5_k_dequant_sum"]
+    w = _u8(k["block_hex"])
+    assert abs(float(oracle.dequantize_block(oracle.Q5_K, w).astype(np.float64).sum()) - 4928.0) < 1e-3
+    out = oracle.vec_dot_f32(oracle.Q5_K, w, 1, 256, np.ones(256, np.float32))
+    assert abs(out[0] - 4928.0) < 1e-3
+
+
+def test_q5_0_kats(oracle, kats):
+    """quant.rs:2855-2862 (block dequantization) and :2910-2966 (a two-block row through the f32
+    path and through Q8_0 activations, both within 1e-4 of the dequantized f32 dot)."""
+    k = kats["q5_0_dequant"]
+    d = oracle.dequantize_block(oracle.Q5_0, _u8(k["block_hex"]))
+    for idx, v in k["expect"].items():
+        assert abs(d[int(idx)] - v) < 1e-6
+    k = kats["q5_0_two_block_row"]
+    row = _u8(k["row_hex"])
+    deq = oracle.dequantize_rows(oracle.Q5_0, row, 1, 64).reshape(-1)
+    x = (np.arange(64, dtype=np.float32) - 31.0) * np.float32(0.0625)
+    ref = float(np.float32(sum(np.float32(a) * np.float32(b) for a, b in zip(deq, x))))
+    got = oracle.vec_dot_f32(oracle.Q5_0, row, 1, 64, x)[0]
+    assert abs(got - ref) < k["abs_tol"]
+    q8 = np.zeros(2, oracle.BLOCK_Q8_0)
+    q8["d"] = 1.0
+    q8["qs"] = (np.arange(64) - 31).reshape(2, 32)
+    exact = float(np.dot(deq.astype(np.float64), (np.arange(64) - 31).astype(np.float64)))
+    assert abs(oracle.vec_dot(oracle.Q5_0, row, q8) - exact) < k["abs_tol"]
+
+
+@pytest.mark.parametrize("quant", [6, 13])
+def test_q5_gemv_tolerance_and_repack(oracle, quant):
+    """The Q5 GEMVs meet the suite's l2 contract against the f64 product over the dequantized
+    blocks, and their repacked form reproduces the dequantizer (tests/test_repack_gemv_gemm.rs:
+    619-700)."""
+    rows, cols = 33, 1024
+    w = oracle.quantize_weights(quant, oracle.normal(rows * cols, 8, 0.02), rows, cols)
+    x = oracle.normal(cols, 9, 1.0)
+    xq = oracle.quantize_act(quant, x)
+    o = oracle.gemv(quant, w, rows, cols, xq)
+    rq = R.ref_matvec(oracle, quant, w, rows, cols, R.dequant_q8(xq))
+    assert R.l2_rel_err(o, rq) < 1e-5
+    assert R.cosine(o, R.ref_matvec(oracle, quant, w, rows, cols, x)) > 0.999
+    q, s, mn = oracle.repack_block_scaled(quant, w, rows, cols)
+    deq = q.astype(np.float32).reshape(rows, -1, 32) * s[:, :, None]
+    if mn is not None:
+        deq = deq - mn[:, :, None]
+    assert np.allclose(deq.reshape(rows, -1), oracle.dequantize_rows(quant, w, rows, cols),
+                       rtol=1e-6, atol=1e-7)
