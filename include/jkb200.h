@@ -53,8 +53,10 @@ typedef enum {
     JKB_F16 = 1,
     JKB_Q4_0 = 2,
     JKB_Q4_1 = 3, /* compact nibble matrices only */
+    JKB_Q5_0 = 6,
     JKB_Q8_0 = 8,
     JKB_Q4_K_M = 12,
+    JKB_Q5_K = 13,
     JKB_Q6_K = 14,
     JKB_IQ4_NL = 20, /* compact nibble matrices only */
     JKB_BF16 = 30,
@@ -186,6 +188,11 @@ int jkb_vec_dot_q4_k_q8_k(const uint8_t *w_blocks, size_t w_len, const jkb_block
 /* quant_q8.rs:3056 vec_dot_q6_k_q8_k */
 int jkb_vec_dot_q6_k_q8_k(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_k *x,
                           size_t x_len, float *result, void *stream);
+/* quant_q8.rs:1478 vec_dot_q5_0_q8_0_blocks / :3041 vec_dot_q5_k_q8_k */
+int jkb_vec_dot_q5_0_q8_0_blocks(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_0 *x,
+                                 size_t x_len, float *result, void *stream);
+int jkb_vec_dot_q5_k_q8_k(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_k *x,
+                          size_t x_len, float *result, void *stream);
 /* quant_q8.rs:3071 vec_dot_tq1_0_q8_k */
 int jkb_vec_dot_tq1_0_q8_k(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_k *x,
                            size_t x_len, float *result, void *stream);
@@ -210,6 +217,13 @@ int jkb_gemv_q4_k_q8_k(float *out, size_t out_len, const jkb_weight *w, const jk
 /* quant_q8.rs:3189 gemv_q6_k_q8_k */
 int jkb_gemv_q6_k_q8_k(float *out, size_t out_len, const jkb_weight *w, const jkb_block_q8_k *x,
                        size_t x_len, void *stream);
+/* quant_q8.rs:1628 gemv_q5_0_q8_0 (and :1657 the _4x alias), :3160 gemv_q5_k_q8_k */
+int jkb_gemv_q5_0_q8_0(float *out, size_t out_len, const jkb_weight *w, const jkb_block_q8_0 *x,
+                       size_t x_len, void *stream);
+int jkb_gemv_q5_0_q8_0_4x(float *out, size_t out_len, const jkb_weight *w,
+                          const jkb_block_q8_0 *x, size_t x_len, void *stream);
+int jkb_gemv_q5_k_q8_k(float *out, size_t out_len, const jkb_weight *w, const jkb_block_q8_k *x,
+                       size_t x_len, void *stream);
 /* quant_q8.rs:3221 gemv_tq1_0_q8_k */
 int jkb_gemv_tq1_0_q8_k(float *out, size_t out_len, const jkb_weight *w,
                         const jkb_block_q8_k *x, size_t x_len, void *stream);
@@ -218,7 +232,8 @@ int jkb_gemv_tq2_0_q8_k(float *out, size_t out_len, const jkb_weight *w,
                         const jkb_block_q8_k *x, size_t x_len, void *stream);
 /* Row-sliced form of the gemv_* calls above (the analogue of gemv_repacked_rows,
  * repack.rs:4014): writes out[0 .. row_end - row_begin] for weight rows [row_begin, row_end).
- * x points at BlockQ8_0 (Q4_0, Q8_0 weights) or BlockQ8K (Q4_K_M, Q6_K, TQ1_0, TQ2_0). */
+ * x points at BlockQ8_0 (Q4_0, Q5_0, Q8_0 weights) or BlockQ8K (Q4_K_M, Q5_K, Q6_K, TQ1_0,
+ * TQ2_0). */
 int jkb_gemv_rows(float *out, size_t out_len, const jkb_weight *w, const void *x, size_t x_len,
                   size_t row_begin, size_t row_end, void *stream);
 /* M tokens of the gemv_* calls above in one launch (no reference counterpart; the reference
@@ -246,6 +261,14 @@ int jkb_vec_dot_q6_k(float *out, size_t out_len, const jkb_weight *w, const floa
 /* quant.rs:1458 vec_dot_q4_0 (scalar :1401) */
 int jkb_vec_dot_q4_0(float *out, size_t out_len, const jkb_weight *w, const float *input,
                      size_t in_len, void *stream);
+/* quant.rs:2036 vec_dot_q5_0 (host branch: vec_dot_generic_block, :1995-2029) and :1238
+ * vec_dot_q5_k / lib.rs:188 VectorKernel::vec_dot_q5_k (host branch: vec_dot_q5_k_scalar,
+ * quant.rs:1181-1222): per block the dequantized values' sequential f32 dot, rows summed in
+ * block order -- bit-exact. */
+int jkb_vec_dot_q5_0(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                     size_t in_len, void *stream);
+int jkb_vec_dot_q5_k(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                     size_t in_len, void *stream);
 /* quant.rs:2199 vec_dot_i2_s */
 int jkb_vec_dot_i2_s(float *out, size_t out_len, const jkb_weight *w, const float *input,
                      size_t in_len, void *stream);
@@ -267,6 +290,12 @@ int jkb_vec_dot_q8_0_rvv(float *out, size_t out_len, const jkb_weight *w, const 
                          size_t in_len, void *stream);
 /* quant.rs:1445 vec_dot_q4_0_rvv */
 int jkb_vec_dot_q4_0_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                         size_t in_len, void *stream);
+/* the riscv64 branches of vec_dot_q5_0 (vec_dot_q5_0_4row_rvv) and vec_dot_q5_k
+ * (quant.rs:1225 vec_dot_q5_k_rvv): input quantized, then the integer GEMV */
+int jkb_vec_dot_q5_0_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                         size_t in_len, void *stream);
+int jkb_vec_dot_q5_k_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
                          size_t in_len, void *stream);
 
 /* One product of jkb_vec_dot_grouped_rvv: out[0 .. out_len) = w x input. */

@@ -18,6 +18,21 @@ __device__ __forceinline__ float f16_fin(uint32_t bits) {
 // (quant_q8.rs:672-717, :1834-1862, :1903-1942, :1960-2003).
 
 __device__ float raw_block(int quant, const uint8_t *w, const uint8_t *xb) {
+    if (quant == JKB_Q5_0) {  // quant_q8.rs:688-703
+        float xd = *reinterpret_cast<const float *>(xb);
+        const int8_t *xq = reinterpret_cast<const int8_t *>(xb + 4);
+        float dw = f16_fin(rd16d(w));
+        const uint32_t qh = (uint32_t)w[2] | ((uint32_t)w[3] << 8) | ((uint32_t)w[4] << 16) |
+                            ((uint32_t)w[5] << 24);
+        int sumi = 0;
+        for (int j = 0; j < 16; j++) {
+            const int q0 = (int)((w[6 + j] & 0x0F) | (((qh >> j) & 1) << 4)) - 16;
+            const int q1 = (int)((w[6 + j] >> 4) | (((qh >> (j + 16)) & 1) << 4)) - 16;
+            sumi += q0 * xq[j] + q1 * xq[j + 16];
+        }
+        if (dw == 0.0f || xd == 0.0f) return 0.0f;
+        return __fmul_rn((float)sumi, __fmul_rn(dw, xd));
+    }
     if (quant == JKB_Q4_0 || quant == JKB_Q8_0) {
         float xd = *reinterpret_cast<const float *>(xb);
         const int8_t *xq = reinterpret_cast<const int8_t *>(xb + 4);
@@ -51,6 +66,29 @@ __device__ float raw_block(int quant, const uint8_t *w, const uint8_t *xb) {
                 uint8_t b = w[16 + 32 * c + l];
                 lo += (int)(b & 0x0F) * xq[64 * c + l];
                 hi += (int)(b >> 4) * xq[64 * c + 32 + l];
+            }
+            sumi += sc0 * lo + sc1 * hi;
+            mins += m0 * ((int)bs[4 * c] + bs[4 * c + 1]) + m1 * ((int)bs[4 * c + 2] + bs[4 * c + 3]);
+        }
+        if ((d == 0.0f && dmin == 0.0f) || xd == 0.0f) return 0.0f;
+        return __fsub_rn(__fmul_rn(__fmul_rn(d, xd), (float)sumi),
+                         __fmul_rn(__fmul_rn(dmin, xd), (float)mins));
+    }
+    case JKB_Q5_K: {  // quant_q8.rs:1866-1899
+        float d = f16_fin(rd16d(w)), dmin = f16_fin(rd16d(w + 2));
+        const uint8_t *s = w + 4, *qh = w + 16, *qs = w + 48;
+        int sumi = 0, mins = 0;
+        for (int c = 0; c < 4; c++) {
+            int j0 = 2 * c, j1 = 2 * c + 1;
+            int sc0 = j0 < 4 ? (s[j0] & 63) : ((s[j0 + 4] & 0x0F) | ((s[j0 - 4] >> 6) << 4));
+            int sc1 = j1 < 4 ? (s[j1] & 63) : ((s[j1 + 4] & 0x0F) | ((s[j1 - 4] >> 6) << 4));
+            int m0 = j0 < 4 ? (s[j0 + 4] & 63) : ((s[j0 + 4] >> 4) | ((s[j0] >> 6) << 4));
+            int m1 = j1 < 4 ? (s[j1 + 4] & 63) : ((s[j1 + 4] >> 4) | ((s[j1] >> 6) << 4));
+            int lo = 0, hi = 0;
+            for (int l = 0; l < 32; l++) {
+                uint8_t b = qs[32 * c + l];
+                lo += ((int)(b & 0x0F) | (((qh[l] >> j0) & 1) << 4)) * xq[64 * c + l];
+                hi += ((int)(b >> 4) | (((qh[l] >> j1) & 1) << 4)) * xq[64 * c + 32 + l];
             }
             sumi += sc0 * lo + sc1 * hi;
             mins += m0 * ((int)bs[4 * c] + bs[4 * c + 1]) + m1 * ((int)bs[4 * c + 2] + bs[4 * c + 3]);
@@ -136,7 +174,7 @@ static int vec_dot_raw(const char *fn, int quant, const uint8_t *w, size_t w_len
     if (x_len > 16384)
         return fail(JKB_E_BOUNDS, fn, 0, x_len, 16384, "%s: %zu blocks exceed the 16384-block row "
                     "limit of the GPU kernel", fn, x_len);
-    int xbb = (quant == JKB_Q4_0 || quant == JKB_Q8_0) ? 36 : 292;
+    int xbb = (quant == JKB_Q4_0 || quant == JKB_Q8_0 || quant == JKB_Q5_0) ? 36 : 292;
     vec_dot_raw_kernel<<<1, 256, x_len * sizeof(float), as_stream(stream)>>>(
         quant, w, f->block_bytes, (const uint8_t *)x, xbb, (int)x_len, result);
     return check_launch(fn);
@@ -208,6 +246,48 @@ __device__ float block_dot_f32(const DqArgs &a, size_t r, int b) {
             }
             for (int l = 0; l < 32; l++) {
                 float v = __fsub_rn(__fmul_rn(d2, (float)(q[32 * c + l] >> 4)), mm2);
+                s = __fadd_rn(s, __fmul_rn(v, x[64 * c + 32 + l]));
+            }
+        }
+        return s;
+    }
+    case JKB_Q5_0: {  // dequantize_q5_0_block (quant.rs:140-163); qh in the scale plane
+        float d = f16_fin(a.d[r * a.nb + b]);
+        const uint8_t *hp = a.sc + r * a.sc_row + 4 * (size_t)b;
+        const uint32_t qh = (uint32_t)hp[0] | ((uint32_t)hp[1] << 8) | ((uint32_t)hp[2] << 16) |
+                            ((uint32_t)hp[3] << 24);
+        for (int i = 0; i < 32; i++) {
+            int n = i < 16 ? (q[i] & 0x0F) : (q[i - 16] >> 4);
+            n |= (int)((qh >> i) & 1) << 4;
+            float v = d == 0.0f ? 0.0f : __fmul_rn(d, (float)(n - 16));
+            s = __fadd_rn(s, __fmul_rn(v, x[i]));
+        }
+        return s;
+    }
+    case JKB_Q5_K: {  // dequantize_q5_k_block (quant.rs:651-705); q = qs[128] | qh[32]
+        const uint8_t *sv = a.sc + r * a.sc_row + 16 * (size_t)b;
+        float d = f16_fin(rd16d(sv)), dmin = f16_fin(rd16d(sv + 2));
+        if (d == 0.0f && dmin == 0.0f) {
+            for (int e = 0; e < 256; e++) s = __fadd_rn(s, __fmul_rn(0.0f, x[e]));
+            return s;
+        }
+        const uint8_t *s6 = sv + 4, *qh = q + 128;
+        for (int c = 0; c < 4; c++) {
+            int j0 = 2 * c, j1 = 2 * c + 1;
+            int sc0 = j0 < 4 ? (s6[j0] & 63) : ((s6[j0 + 4] & 0x0F) | ((s6[j0 - 4] >> 6) << 4));
+            int sc1 = j1 < 4 ? (s6[j1] & 63) : ((s6[j1 + 4] & 0x0F) | ((s6[j1 - 4] >> 6) << 4));
+            int m0 = j0 < 4 ? (s6[j0 + 4] & 63) : ((s6[j0 + 4] >> 4) | ((s6[j0] >> 6) << 4));
+            int m1 = j1 < 4 ? (s6[j1 + 4] & 63) : ((s6[j1 + 4] >> 4) | ((s6[j1] >> 6) << 4));
+            float d1 = __fmul_rn(d, (float)sc0), mm1 = __fmul_rn(dmin, (float)m0);
+            float d2 = __fmul_rn(d, (float)sc1), mm2 = __fmul_rn(dmin, (float)m1);
+            for (int l = 0; l < 32; l++) {
+                int n = (q[32 * c + l] & 0x0F) + (((qh[l] >> j0) & 1) ? 16 : 0);
+                float v = __fsub_rn(__fmul_rn(d1, (float)n), mm1);
+                s = __fadd_rn(s, __fmul_rn(v, x[64 * c + l]));
+            }
+            for (int l = 0; l < 32; l++) {
+                int n = (q[32 * c + l] >> 4) + (((qh[l] >> j1) & 1) ? 16 : 0);
+                float v = __fsub_rn(__fmul_rn(d2, (float)n), mm2);
                 s = __fadd_rn(s, __fmul_rn(v, x[64 * c + 32 + l]));
             }
         }
@@ -344,6 +424,14 @@ int jkb_vec_dot_q6_k_q8_k(const uint8_t *w, size_t w_len, const jkb_block_q8_k *
                           float *result, void *stream) {
     return vec_dot_raw("vec_dot_q6_k_q8_k", JKB_Q6_K, w, w_len, x, x_len, result, stream);
 }
+int jkb_vec_dot_q5_0_q8_0_blocks(const uint8_t *w, size_t w_len, const jkb_block_q8_0 *x,
+                                 size_t x_len, float *result, void *stream) {
+    return vec_dot_raw("vec_dot_q5_0_q8_0_blocks", JKB_Q5_0, w, w_len, x, x_len, result, stream);
+}
+int jkb_vec_dot_q5_k_q8_k(const uint8_t *w, size_t w_len, const jkb_block_q8_k *x, size_t x_len,
+                          float *result, void *stream) {
+    return vec_dot_raw("vec_dot_q5_k_q8_k", JKB_Q5_K, w, w_len, x, x_len, result, stream);
+}
 int jkb_vec_dot_tq1_0_q8_k(const uint8_t *w, size_t w_len, const jkb_block_q8_k *x,
                            size_t x_len, float *result, void *stream) {
     return vec_dot_raw("vec_dot_tq1_0_q8_k", JKB_TQ1_0, w, w_len, x, x_len, result, stream);
@@ -368,6 +456,14 @@ int jkb_vec_dot_q6_k(float *out, size_t out_len, const jkb_weight *w, const floa
 int jkb_vec_dot_q4_0(float *out, size_t out_len, const jkb_weight *w, const float *input,
                      size_t in_len, void *stream) {
     return vec_dot_f32_call("vec_dot_q4_0", JKB_Q4_0, out, out_len, w, input, in_len, stream);
+}
+int jkb_vec_dot_q5_0(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                     size_t in_len, void *stream) {
+    return vec_dot_f32_call("vec_dot_q5_0", JKB_Q5_0, out, out_len, w, input, in_len, stream);
+}
+int jkb_vec_dot_q5_k(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                     size_t in_len, void *stream) {
+    return vec_dot_f32_call("vec_dot_q5_k", JKB_Q5_K, out, out_len, w, input, in_len, stream);
 }
 int jkb_vec_dot_i2_s(float *out, size_t out_len, const jkb_weight *w, const float *input,
                      size_t in_len, void *stream) {

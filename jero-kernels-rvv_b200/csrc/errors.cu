@@ -52,7 +52,8 @@ static const Fmt FMTS[] = {
     {JKB_Q4_0, "Q4_0", 32, 18, 0},     {JKB_Q8_0, "Q8_0", 32, 34, 0},
     {JKB_Q4_K_M, "Q4_K_M", 256, 144, 0}, {JKB_Q6_K, "Q6_K", 256, 210, 0},
     {JKB_TQ1_0, "TQ1_0", 256, 54, 0},  {JKB_TQ2_0, "TQ2_0", 256, 66, 0},
-    {JKB_I2_S, "I2_S", 128, 32, 32},
+    {JKB_I2_S, "I2_S", 128, 32, 32},  {JKB_Q5_0, "Q5_0", 32, 22, 0},
+    {JKB_Q5_K, "Q5_K", 256, 176, 0},
 };
 
 const Fmt *fmt_of(int quant) {

@@ -615,6 +615,122 @@ struct FQ4_K {
     }
 };
 
+// Bits 0..3 of v to the low bit of bytes 0..3 (v * 0x00204081 places bit i at 8i; the four
+// shifted copies do not overlap, so nothing carries).
+__device__ __forceinline__ uint32_t spread4(uint32_t v) {
+    return ((v & 0xF) * 0x00204081u) & 0x01010101u;
+}
+
+// Q5_0 x Q8_0 (quant_q8.rs:688-703): element j = (low nibble of byte j | bit j of qh << 4) - 16,
+// element j + 16 = (high nibble | bit j + 16 of qh << 4) - 16. The fifth bits enter as 0/1
+// bytes dotted with the activations (times 16), the -16 through the block sum.
+struct FQ5_0 {
+    static constexpr int BE = 32;
+    using Act = ActQ80;
+    struct Ld {
+        uint4 q[1];
+        uint32_t h;
+        uint32_t d;
+    };
+    static __device__ __forceinline__ void prefetch(const KArgs &a, const Row &rp, int b) {
+        prefetch_chunks<1>(a, rp, b);
+    }
+    static __device__ __forceinline__ Ld load(const KArgs &a, const Row &rp, int b) {
+        Ld l;
+        load_chunks<1>(a, rp, b, l.q);
+        l.h = __ldg(reinterpret_cast<const uint32_t *>(rp.s) + b);
+        l.d = ldg_u16(rp.d + b);
+        return l;
+    }
+    static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
+                                                  int b, int2 &iv) {
+        const int4 x0 = lds4(Act::chunk(s, b, 0)), x1 = lds4(Act::chunk(s, b, 1));
+        const int lo = dot_lo(l.q[0], x0, 0);
+        const int hi = dot_hi16(l.q[0], x1, 0) >> 4;
+        int hb = dp4a_ss((int)spread4(l.h), x0.x, 0);
+        hb = dp4a_ss((int)spread4(l.h >> 4), x0.y, hb);
+        hb = dp4a_ss((int)spread4(l.h >> 8), x0.z, hb);
+        hb = dp4a_ss((int)spread4(l.h >> 12), x0.w, hb);
+        hb = dp4a_ss((int)spread4(l.h >> 16), x1.x, hb);
+        hb = dp4a_ss((int)spread4(l.h >> 20), x1.y, hb);
+        hb = dp4a_ss((int)spread4(l.h >> 24), x1.z, hb);
+        hb = dp4a_ss((int)spread4(l.h >> 28), x1.w, hb);
+        const int sumi = lo + hi + 16 * hb - 16 * Act::tot(s, a.K, b);
+        iv = make_int2(sumi, 0);
+        const float dw = f16_finite(l.d), xd = Act::xd(s, a.K, b);
+        if (dw == 0.0f || xd == 0.0f) return 0.0f;
+        return __fmul_rn((float)sumi, __fmul_rn(dw, xd));
+    }
+};
+
+// Q5_K x Q8_K (quant_q8.rs:1866-1899): the Q4_K block plus a fifth bit per element from qh[32]
+// (bit 2c of qh[l] for element 64c + l, bit 2c + 1 for element 64c + 32 + l). Chunks 0-7 are qs
+// as for Q4_K, chunks 8 and 9 hold qh[0..16] and qh[16..32]; the 5-bit values (0..31) are
+// formed per byte and dotted directly.
+struct FQ5_K {
+    static constexpr int BE = 256;
+    using Act = ActQ8K;
+    struct Ld {
+        uint4 q[10];
+        uint4 s;
+    };
+    static __device__ __forceinline__ void prefetch(const KArgs &a, const Row &rp, int b) {
+        prefetch_chunks<10>(a, rp, b);
+    }
+    static __device__ __forceinline__ Ld load(const KArgs &a, const Row &rp, int b) {
+        Ld l;
+        load_chunks<10>(a, rp, b, l.q);
+        l.s = __ldg(reinterpret_cast<const uint4 *>(rp.s + 16 * (size_t)b));
+        return l;
+    }
+    // bit `bit` of every byte of h moved to bit 4 of the byte
+    static __device__ __forceinline__ uint32_t bit4(uint32_t h, int bit) {
+        return (bit <= 4 ? (h << (4 - bit)) : (h >> (bit - 4))) & 0x10101010u;
+    }
+    static __device__ __forceinline__ int dot5(uint4 q, uint4 h, int4 x, bool high, int bit) {
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w}, hw[4] = {h.x, h.y, h.z, h.w};
+        const int xw[4] = {x.x, x.y, x.z, x.w};
+        int acc = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const uint32_t nib = (high ? (qw[k] >> 4) : qw[k]) & 0x0F0F0F0Fu;
+            acc = dp4a_ss((int)(nib | bit4(hw[k], bit)), xw[k], acc);
+        }
+        return acc;
+    }
+    static __device__ __forceinline__ float value(const KArgs &a, const uint8_t *s, const Ld &l,
+                                                  int b, int2 &iv) {
+        const uint32_t sc_lo = l.s.y & 0x3F3F3F3F, m_lo = l.s.z & 0x3F3F3F3F;
+        const uint32_t sc_hi = (l.s.w & 0x0F0F0F0F) | ((l.s.y >> 2) & 0x30303030);
+        const uint32_t m_hi = ((l.s.w >> 4) & 0x0F0F0F0F) | ((l.s.z >> 2) & 0x30303030);
+        const int4 b0 = ActQ8K::bsums_half(s, a.K, b, 0), b1 = ActQ8K::bsums_half(s, a.K, b, 1);
+        const int bs[16] = {(int)(int16_t)b0.x, b0.x >> 16, (int)(int16_t)b0.y, b0.y >> 16,
+                            (int)(int16_t)b0.z, b0.z >> 16, (int)(int16_t)b0.w, b0.w >> 16,
+                            (int)(int16_t)b1.x, b1.x >> 16, (int)(int16_t)b1.y, b1.y >> 16,
+                            (int)(int16_t)b1.z, b1.z >> 16, (int)(int16_t)b1.w, b1.w >> 16};
+        int sumi = 0, mins = 0;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint4 qa = l.q[2 * c], qb = l.q[2 * c + 1];
+            const int slo = dot5(qa, l.q[8], lds4(ActQ8K::chunk(s, b, 4 * c)), false, 2 * c) +
+                            dot5(qb, l.q[9], lds4(ActQ8K::chunk(s, b, 4 * c + 1)), false, 2 * c);
+            const int shi = dot5(qa, l.q[8], lds4(ActQ8K::chunk(s, b, 4 * c + 2)), true, 2 * c + 1) +
+                            dot5(qb, l.q[9], lds4(ActQ8K::chunk(s, b, 4 * c + 3)), true, 2 * c + 1);
+            const uint32_t scw = c < 2 ? sc_lo : sc_hi, mw = c < 2 ? m_lo : m_hi;
+            const int k = 2 * (c & 1);
+            sumi += (int)((scw >> (8 * k)) & 0xFF) * slo + (int)((scw >> (8 * k + 8)) & 0xFF) * shi;
+            mins += (int)((mw >> (8 * k)) & 0xFF) * (bs[4 * c] + bs[4 * c + 1]) +
+                    (int)((mw >> (8 * k + 8)) & 0xFF) * (bs[4 * c + 2] + bs[4 * c + 3]);
+        }
+        iv = make_int2(sumi, mins);
+        const float d = f16_finite(l.s.x & 0xFFFF), dmin = f16_finite(l.s.x >> 16);
+        const float xd = ActQ8K::xd(s, a.K, b);
+        if ((d == 0.0f && dmin == 0.0f) || xd == 0.0f) return 0.0f;
+        return __fsub_rn(__fmul_rn(__fmul_rn(d, xd), (float)sumi),
+                         __fmul_rn(__fmul_rn(dmin, xd), (float)mins));
+    }
+};
+
 // Q6_K x Q8_K (quant_q8.rs:1903-1942). Chunks 0-7 are ql, 8-11 qh (GGUF order). For half h
 // and is = i: A = ql[64h+16i..] (chunk 4h+i), B = ql[64h+32+16i..] (4h+2+i),
 // H = qh[32h+16i..] (8+2h+i); the four 6-bit values pair with activation chunks 8h+i+{0,2,4,6}
@@ -1093,6 +1209,14 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
         if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FQ6_K);
         if (L.act_kind == ACT_F32_Q8_K) JKB_LAUNCH_F32(FQ6_K, ActQ8KF32);
         break;
+    case GF_Q5_0:
+        if (L.act_kind == ACT_Q8_0) JKB_LAUNCH(FQ5_0);
+        if (L.act_kind == ACT_F32_Q8_0) JKB_LAUNCH_F32(FQ5_0, ActQ80F32);
+        break;
+    case GF_Q5_K:
+        if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FQ5_K);
+        if (L.act_kind == ACT_F32_Q8_K) JKB_LAUNCH_F32(FQ5_K, ActQ8KF32);
+        break;
     case GF_TQ2_0:
         if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FTQ2<ActQ8K>);
         if (L.act_kind == ACT_I8) JKB_LAUNCH(FTQ2<ActI8<256>>);
@@ -1111,7 +1235,7 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
 // ---------------------------------------------------------------- ABI glue
 
 static int act_kind_for(int quant) {
-    return (quant == JKB_Q4_0 || quant == JKB_Q8_0) ? ACT_Q8_0 : ACT_Q8_K;
+    return (quant == JKB_Q4_0 || quant == JKB_Q8_0 || quant == JKB_Q5_0) ? ACT_Q8_0 : ACT_Q8_K;
 }
 
 // gemv_* validation order (quant_q8.rs:1586-1603 and twins): quant + shape validator, then
@@ -1147,7 +1271,8 @@ static int gemv_call(const char *fn, int quant, float *out, size_t out_len, cons
 // quant_q8.rs:1712-1750, :3280-3317). The reference quantizes into a stack chunk per 32 / 128
 // blocks; here every CTA quantizes the whole input into shared memory.
 static int rvv_act_kind(int quant) {
-    return (quant == JKB_Q4_0 || quant == JKB_Q8_0) ? ACT_F32_Q8_0 : ACT_F32_Q8_K;
+    return (quant == JKB_Q4_0 || quant == JKB_Q8_0 || quant == JKB_Q5_0) ? ACT_F32_Q8_0
+                                                                        : ACT_F32_Q8_K;
 }
 
 static int vec_dot_rvv_call(const char *fn, int quant, float *out, size_t out_len,
@@ -1199,6 +1324,18 @@ int jkb_gemv_q6_k_q8_k(float *out, size_t out_len, const jkb_weight *w, const jk
                        size_t x_len, void *stream) {
     return gemv_call("gemv_q6_k_q8_k", JKB_Q6_K, out, out_len, w, x, x_len, stream);
 }
+int jkb_gemv_q5_0_q8_0(float *out, size_t out_len, const jkb_weight *w, const jkb_block_q8_0 *x,
+                       size_t x_len, void *stream) {
+    return gemv_call("gemv_q5_0_q8_0", JKB_Q5_0, out, out_len, w, x, x_len, stream);
+}
+int jkb_gemv_q5_0_q8_0_4x(float *out, size_t out_len, const jkb_weight *w,
+                          const jkb_block_q8_0 *x, size_t x_len, void *stream) {
+    return gemv_call("gemv_q5_0_q8_0", JKB_Q5_0, out, out_len, w, x, x_len, stream);
+}
+int jkb_gemv_q5_k_q8_k(float *out, size_t out_len, const jkb_weight *w, const jkb_block_q8_k *x,
+                       size_t x_len, void *stream) {
+    return gemv_call("gemv_q5_k_q8_k", JKB_Q5_K, out, out_len, w, x, x_len, stream);
+}
 int jkb_gemv_tq1_0_q8_k(float *out, size_t out_len, const jkb_weight *w,
                         const jkb_block_q8_k *x, size_t x_len, void *stream) {
     return gemv_call("gemv_tq1_0_q8_k", JKB_TQ1_0, out, out_len, w, x, x_len, stream);
@@ -1224,6 +1361,14 @@ int jkb_vec_dot_q4_0_rvv(float *out, size_t out_len, const jkb_weight *w, const 
                          size_t in_len, void *stream) {
     return vec_dot_rvv_call("vec_dot_q4_0", JKB_Q4_0, out, out_len, w, input, in_len, stream);
 }
+int jkb_vec_dot_q5_0_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                         size_t in_len, void *stream) {
+    return vec_dot_rvv_call("vec_dot_q5_0", JKB_Q5_0, out, out_len, w, input, in_len, stream);
+}
+int jkb_vec_dot_q5_k_rvv(float *out, size_t out_len, const jkb_weight *w, const float *input,
+                         size_t in_len, void *stream) {
+    return vec_dot_rvv_call("vec_dot_q5_k", JKB_Q5_K, out, out_len, w, input, in_len, stream);
+}
 
 int jkb_vec_dot_grouped_rvv(const jkb_vec_dot_item *items, size_t n_items, const float *input,
                             size_t in_len, void *stream) {
@@ -1235,11 +1380,13 @@ int jkb_vec_dot_grouped_rvv(const jkb_vec_dot_item *items, size_t n_items, const
     int rc = check_weight(items[0].w);
     if (rc) return rc;
     const int quant = items[0].w->quant;
-    if (quant != JKB_Q4_0 && quant != JKB_Q8_0 && quant != JKB_Q4_K_M && quant != JKB_Q6_K)
+    if (quant != JKB_Q4_0 && quant != JKB_Q8_0 && quant != JKB_Q4_K_M && quant != JKB_Q6_K &&
+        quant != JKB_Q5_0 && quant != JKB_Q5_K)
         return fail(JKB_E_CAPABILITY, items[0].w->name, items[0].w->offset, items[0].w->byte_len,
                     items[0].w->gguf_bytes,
-                    "%s: no vec_dot_*_rvv path for %s weights (Q4_0, Q8_0, Q4_K_M, Q6_K)", fn,
-                    quant_name(quant));
+                    "%s: no vec_dot_*_rvv path for %s weights (Q4_0, Q8_0, Q4_K_M, Q6_K, Q5_0, "
+                    "Q5_K)",
+                    fn, quant_name(quant));
     if ((rc = check_align(input, 4, fn, "input"))) return rc;
     GemvLaunch L{};
     for (size_t i = 0; i < n_items; i++) {

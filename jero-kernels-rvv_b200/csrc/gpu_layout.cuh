@@ -15,9 +15,10 @@ namespace jkb {
 
 // 16-byte quant chunks per block in the GPU layout
 __host__ __device__ constexpr int qs_chunks(int gpu_format) {
-    // GF_Q4_0, GF_Q8_0, GF_Q4_K, GF_Q6_K, GF_TQ2_0, GF_I2_S
+    // GF_Q4_0, GF_Q8_0, GF_Q4_K, GF_Q6_K, GF_TQ2_0, GF_I2_S, GF_Q5_0, GF_Q5_K
     return gpu_format == 0 ? 1 : gpu_format == 1 ? 2 : gpu_format == 2 ? 8
-         : gpu_format == 3 ? 12 : gpu_format == 4 ? 4 : 2;
+         : gpu_format == 3 ? 12 : gpu_format == 4 ? 4 : gpu_format == 5 ? 2
+         : gpu_format == 6 ? 1 : 10;
 }
 
 // Byte offset of chunk j of block b inside one row's quant payload.

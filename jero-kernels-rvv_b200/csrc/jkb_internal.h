@@ -68,7 +68,7 @@ int stage_raw(const jkb_tensor_view *v, size_t need, cudaStream_t st, uint8_t **
 struct WeightPlanes {
     const uint8_t *qs = nullptr;  // quant plane, row pitch qs_row bytes
     size_t qs_row = 0;
-    const uint8_t *sc = nullptr;  // 16-byte-per-block scale plane (Q4_K_M, Q6_K)
+    const uint8_t *sc = nullptr;  // per-block scale plane: 16 B (Q4_K_M, Q5_K, Q6_K), 4 B (Q5_0 qh)
     size_t sc_row = 0;
     const uint16_t *d = nullptr;  // f16 block scales [rows][nb] (Q4_0, Q8_0, Q6_K, TQ*)
     float i2s_scale = 0.0f;       // I2_S per-tensor trailer scale (non-finite -> 0)
@@ -187,7 +187,7 @@ int validate_weight_call(const char *fn, const jkb_weight *w, int expected_quant
 int check_weight(const jkb_weight *w);
 
 // gemv.cu entry used by bitlinear.cu and the sharded paths.
-enum GpuFormat { GF_Q4_0, GF_Q8_0, GF_Q4_K, GF_Q6_K, GF_TQ2_0, GF_I2_S };
+enum GpuFormat { GF_Q4_0, GF_Q8_0, GF_Q4_K, GF_Q6_K, GF_TQ2_0, GF_I2_S, GF_Q5_0, GF_Q5_K };
 // ACT_F32_*: f32 input rows that every CTA quantizes into its shared-memory staging buffer with
 // the bit-exact BlockQ8_0 / BlockQ8K quantizer (the reference's vec_dot_*_rvv paths).
 enum ActKind { ACT_Q8_0 = 0, ACT_Q8_K = 1, ACT_I8 = 2, ACT_F32_Q8_0 = 3, ACT_F32_Q8_K = 4 };

@@ -7,6 +7,8 @@
 //   Q4_0   qs: 16 B/block, the GGUF nibble bytes        d: f16 per block
 //   Q8_0   qs: 32 B/block, the GGUF i8 quants           d: f16 per block
 //   Q4_K_M qs: 128 B/block, GGUF qs bytes               sc: 16 B/block = d, dmin, scales[12]
+//   Q5_0   qs: 16 B/block, the GGUF nibble bytes        sc: 4 B/block = qh   d: f16 per block
+//   Q5_K   qs: 160 B/block, GGUF qs[128] then qh[32]    sc: 16 B/block = d, dmin, scales[12]
 //   Q6_K   qs: 192 B/block, GGUF ql[128] then qh[64]    sc: 16 B/block i8 scales, d: f16
 //   TQ2_0  qs: 64 B/block, 2-bit codes re-ordered so that chunk p, word W, bit pair j, byte b
 //          holds element 64p+16W+4j+b                   d: f16 per block
@@ -51,6 +53,20 @@ __global__ void relayout_kernel(int quant, int gpu_format, const uint8_t *__rest
         uint8_t *s = sc + r * sc_row + 16 * b;
         for (int i = 0; i < 16; i++) s[i] = blk[i];
         for (int i = 0; i < 128; i++) payload[i] = blk[16 + i];
+        break;
+    }
+    case JKB_Q5_0: {  // 16 nibble bytes, GGUF order; qh to the scale plane, d to its plane
+        uint8_t *s = sc + r * sc_row + 4 * b;
+        for (int i = 0; i < 4; i++) s[i] = blk[2 + i];
+        d[idx] = rd16(blk);
+        for (int i = 0; i < 16; i++) payload[i] = blk[6 + i];
+        break;
+    }
+    case JKB_Q5_K: {  // d, dmin, scales[12] to the scale plane; qs[128] then qh[32]
+        uint8_t *s = sc + r * sc_row + 16 * b;
+        for (int i = 0; i < 16; i++) s[i] = blk[i];
+        for (int i = 0; i < 128; i++) payload[i] = blk[48 + i];
+        for (int i = 0; i < 32; i++) payload[128 + i] = blk[16 + i];
         break;
     }
     case JKB_Q6_K: {  // ql[128] qh[64] in GGUF order; i8 scales and d to their planes
@@ -153,6 +169,46 @@ __global__ void repack_i8_kernel(int quant, const uint8_t *__restrict__ raw, siz
             for (int l = 0; l < 32; l++) {
                 qr[256 * b + 64 * c + l] = (int8_t)(blk[16 + 32 * c + l] & 0x0F);
                 qr[256 * b + 64 * c + 32 + l] = (int8_t)((blk[16 + 32 * c + l] >> 4) & 0x0F);
+            }
+        }
+        break;
+    }
+    case JKB_Q5_0: {  // repack.rs:1827-1840: (5-bit code - 16), left 0 when d == 0
+        float dd = f16_finite_dev(rd16(blk));
+        sr[b] = dd;
+        const uint32_t qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) |
+                            ((uint32_t)blk[4] << 16) | ((uint32_t)blk[5] << 24);
+        for (int i = 0; i < 16; i++) {
+            const int q0 = (int)((blk[6 + i] & 0x0F) | (((qh >> i) & 1) << 4)) - 16;
+            const int q1 = (int)(((blk[6 + i] >> 4) & 0x0F) | (((qh >> (i + 16)) & 1) << 4)) - 16;
+            qr[32 * b + i] = dd != 0.0f ? (int8_t)q0 : 0;
+            qr[32 * b + 16 + i] = dd != 0.0f ? (int8_t)q1 : 0;
+        }
+        break;
+    }
+    case JKB_Q5_K: {  // repack.rs:1959-1995: scales d * sc, mins dmin * m, unsigned 5-bit codes
+        float dd = f16_finite_dev(rd16(blk)), dmin = f16_finite_dev(rd16(blk + 2));
+        const uint8_t *s = blk + 4, *qh = blk + 16, *qs = blk + 48;
+        uint8_t scv[8], mv[8];
+        for (int j = 0; j < 4; j++) {
+            scv[j] = s[j] & 0x3F;
+            mv[j] = s[j + 4] & 0x3F;
+        }
+        for (int j = 4; j < 8; j++) {
+            scv[j] = (uint8_t)((s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4));
+            mv[j] = (uint8_t)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+        }
+        for (int c = 0; c < 4; c++) {
+            size_t g0 = b * 8 + 2 * c;
+            sr[g0] = __fmul_rn(dd, (float)scv[2 * c]);
+            mr[g0] = __fmul_rn(dmin, (float)mv[2 * c]);
+            sr[g0 + 1] = __fmul_rn(dd, (float)scv[2 * c + 1]);
+            mr[g0 + 1] = __fmul_rn(dmin, (float)mv[2 * c + 1]);
+            for (int l = 0; l < 32; l++) {
+                qr[256 * b + 64 * c + l] =
+                    (int8_t)((qs[32 * c + l] & 0x0F) + (((qh[l] >> (2 * c)) & 1) ? 16 : 0));
+                qr[256 * b + 64 * c + 32 + l] =
+                    (int8_t)((qs[32 * c + l] >> 4) + (((qh[l] >> (2 * c + 1)) & 1) ? 16 : 0));
             }
         }
         break;
@@ -330,6 +386,8 @@ static int weight_upload(const jkb_tensor_view *v, size_t rows, size_t cols, cud
     case JKB_Q8_0: qp = 32; has_d = true; w->gpu_format = GF_Q8_0; break;
     case JKB_Q4_K_M: qp = 128; scp = 16; w->gpu_format = GF_Q4_K; break;
     case JKB_Q6_K: qp = 192; scp = 16; has_d = true; w->gpu_format = GF_Q6_K; break;
+    case JKB_Q5_0: qp = 16; scp = 4; has_d = true; w->gpu_format = GF_Q5_0; break;
+    case JKB_Q5_K: qp = 160; scp = 16; w->gpu_format = GF_Q5_K; break;
     case JKB_TQ1_0:
     case JKB_TQ2_0: qp = 64; has_d = true; w->gpu_format = GF_TQ2_0; break;
     case JKB_I2_S: qp = 32; w->gpu_format = GF_I2_S; break;
@@ -407,7 +465,7 @@ static int repacked_upload(const jkb_tensor_view *v, size_t rows, size_t cols, c
     w->group_elems = v->quant == JKB_Q6_K ? 16 : 32;
     w->scale_groups = w->k_pad / w->group_elems;
     snprintf(w->name, sizeof(w->name), "%s", nm);
-    bool mins = v->quant == JKB_Q4_K_M;
+    bool mins = v->quant == JKB_Q4_K_M || v->quant == JKB_Q5_K;
     Arena a;
     size_t qb = rows * w->k_pad, sb = rows * w->scale_groups * 4;
     a.cap = Arena::round(qb) + Arena::round(sb) * (mins ? 2 : 1);

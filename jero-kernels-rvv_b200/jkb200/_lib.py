@@ -78,6 +78,8 @@ SIGNATURES = {
     "jkb_vec_dot_q8_0_q8_0": [P, S, P, S, P, P],
     "jkb_vec_dot_q4_k_q8_k": [P, S, P, S, P, P],
     "jkb_vec_dot_q6_k_q8_k": [P, S, P, S, P, P],
+    "jkb_vec_dot_q5_0_q8_0_blocks": [P, S, P, S, P, P],
+    "jkb_vec_dot_q5_k_q8_k": [P, S, P, S, P, P],
     "jkb_vec_dot_tq1_0_q8_k": [P, S, P, S, P, P],
     "jkb_vec_dot_tq2_0_q8_k": [P, S, P, S, P, P],
     "jkb_gemv_q4_0_q8_0": [P, S, P, P, S, P],
@@ -86,6 +88,9 @@ SIGNATURES = {
     "jkb_gemv_q8_0_q8_0_4x": [P, S, P, P, S, P],
     "jkb_gemv_q4_k_q8_k": [P, S, P, P, S, P],
     "jkb_gemv_q6_k_q8_k": [P, S, P, P, S, P],
+    "jkb_gemv_q5_0_q8_0": [P, S, P, P, S, P],
+    "jkb_gemv_q5_0_q8_0_4x": [P, S, P, P, S, P],
+    "jkb_gemv_q5_k_q8_k": [P, S, P, P, S, P],
     "jkb_gemv_tq1_0_q8_k": [P, S, P, P, S, P],
     "jkb_gemv_tq2_0_q8_k": [P, S, P, P, S, P],
     "jkb_gemv_rows": [P, S, P, P, S, S, S, P],
@@ -95,7 +100,11 @@ SIGNATURES = {
     "jkb_vec_dot_q8_0": [P, S, P, P, S, P],
     "jkb_vec_dot_q6_k": [P, S, P, P, S, P],
     "jkb_vec_dot_q4_0": [P, S, P, P, S, P],
+    "jkb_vec_dot_q5_0": [P, S, P, P, S, P],
+    "jkb_vec_dot_q5_k": [P, S, P, P, S, P],
     "jkb_vec_dot_i2_s": [P, S, P, P, S, P],
+    "jkb_vec_dot_q5_0_rvv": [P, S, P, P, S, P],
+    "jkb_vec_dot_q5_k_rvv": [P, S, P, P, S, P],
     "jkb_vec_dot_q4_k_m_rvv": [P, S, P, P, S, P],
     "jkb_vec_dot_q6_k_rvv": [P, S, P, P, S, P],
     "jkb_vec_dot_q8_0_rvv": [P, S, P, P, S, P],

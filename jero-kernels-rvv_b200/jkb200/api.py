@@ -32,7 +32,9 @@ __all__ = [
     "empty_q8_0_blocks", "empty_q8_k_blocks", "device_status", "gemm_set_exact", "gemm_get_exact",
     "gemm_exact", "PeerGroup", "gemv_batch",
     "device_view", "PackedNibbleMatrix", "gemm_q4_0_ime", "gemm_q4_k_ime",
-    "repack_nibble_into_tile_range",
+    "repack_nibble_into_tile_range", "vec_dot_q5_0_q8_0_blocks", "vec_dot_q5_k_q8_k",
+    "gemv_q5_0_q8_0", "gemv_q5_0_q8_0_4x", "gemv_q5_k_q8_k", "vec_dot_q5_0", "vec_dot_q5_k",
+    "vec_dot_q5_0_rvv", "vec_dot_q5_k_rvv",
 ]
 
 
@@ -42,8 +44,10 @@ class QuantType(enum.IntEnum):
     F16 = 1
     Q4_0 = 2
     Q4_1 = 3
+    Q5_0 = 6
     Q8_0 = 8
     Q4_K_M = 12
+    Q5_K = 13
     Q6_K = 14
     IQ4_NL = 20
     BF16 = 30
@@ -57,6 +61,7 @@ BLOCK = {
     QuantType.Q4_0: (32, 18), QuantType.Q8_0: (32, 34), QuantType.Q4_K_M: (256, 144),
     QuantType.Q6_K: (256, 210), QuantType.TQ1_0: (256, 54), QuantType.TQ2_0: (256, 66),
     QuantType.I2_S: (128, 32), QuantType.Q4_1: (32, 20), QuantType.IQ4_NL: (32, 18),
+    QuantType.Q5_0: (32, 22), QuantType.Q5_K: (256, 176),
 }
 BLOCK_Q8_0_BYTES = 36
 BLOCK_Q8_K_BYTES = 292
@@ -610,6 +615,16 @@ def vec_dot_q6_k_q8_k(w_blocks, x_blocks, result, stream=None):
     _vec_dot("jkb_vec_dot_q6_k_q8_k", w_blocks, x_blocks, BLOCK_Q8_K_BYTES, result, stream)
 
 
+def vec_dot_q5_0_q8_0_blocks(w_blocks, x_blocks, result, stream=None):
+    """quant_q8.rs:1478."""
+    _vec_dot("jkb_vec_dot_q5_0_q8_0_blocks", w_blocks, x_blocks, BLOCK_Q8_0_BYTES, result, stream)
+
+
+def vec_dot_q5_k_q8_k(w_blocks, x_blocks, result, stream=None):
+    """quant_q8.rs:3041."""
+    _vec_dot("jkb_vec_dot_q5_k_q8_k", w_blocks, x_blocks, BLOCK_Q8_K_BYTES, result, stream)
+
+
 def vec_dot_tq1_0_q8_k(w_blocks, x_blocks, result, stream=None):
     """quant_q8.rs:3071."""
     _vec_dot("jkb_vec_dot_tq1_0_q8_k", w_blocks, x_blocks, BLOCK_Q8_K_BYTES, result, stream)
@@ -657,6 +672,21 @@ def gemv_q6_k_q8_k(out, weights, x_blocks, stream=None):
     _gemv("jkb_gemv_q6_k_q8_k", out, weights, x_blocks, BLOCK_Q8_K_BYTES, stream)
 
 
+def gemv_q5_0_q8_0(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:1628."""
+    _gemv("jkb_gemv_q5_0_q8_0", out, weights, x_blocks, BLOCK_Q8_0_BYTES, stream)
+
+
+def gemv_q5_0_q8_0_4x(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:1657."""
+    _gemv("jkb_gemv_q5_0_q8_0_4x", out, weights, x_blocks, BLOCK_Q8_0_BYTES, stream)
+
+
+def gemv_q5_k_q8_k(out, weights, x_blocks, stream=None):
+    """quant_q8.rs:3160."""
+    _gemv("jkb_gemv_q5_k_q8_k", out, weights, x_blocks, BLOCK_Q8_K_BYTES, stream)
+
+
 def gemv_tq1_0_q8_k(out, weights, x_blocks, stream=None):
     """quant_q8.rs:3221."""
     _gemv("jkb_gemv_tq1_0_q8_k", out, weights, x_blocks, BLOCK_Q8_K_BYTES, stream)
@@ -668,7 +698,8 @@ def gemv_tq2_0_q8_k(out, weights, x_blocks, stream=None):
 
 
 def _act_block_bytes(quant):
-    return BLOCK_Q8_0_BYTES if quant in (QuantType.Q4_0, QuantType.Q8_0) else BLOCK_Q8_K_BYTES
+    return (BLOCK_Q8_0_BYTES if quant in (QuantType.Q4_0, QuantType.Q8_0, QuantType.Q5_0)
+            else BLOCK_Q8_K_BYTES)
 
 
 def gemv_rows(out, weights: Weight, x_blocks, row_range, stream=None):
@@ -722,6 +753,26 @@ def vec_dot_q6_k(out, weights, x, stream=None):
 def vec_dot_q4_0(out, weights, x, stream=None):
     """quant.rs:1458."""
     _vk("jkb_vec_dot_q4_0", out, weights, x, stream)
+
+
+def vec_dot_q5_0(out, weights, x, stream=None):
+    """quant.rs:2036 vec_dot_q5_0 (host branch)."""
+    _vk("jkb_vec_dot_q5_0", out, weights, x, stream)
+
+
+def vec_dot_q5_k(out, weights, x, stream=None):
+    """quant.rs:1238 vec_dot_q5_k / lib.rs:188 VectorKernel::vec_dot_q5_k (host branch)."""
+    _vk("jkb_vec_dot_q5_k", out, weights, x, stream)
+
+
+def vec_dot_q5_0_rvv(out, weights, x, stream=None):
+    """vec_dot_q5_0's riscv64 branch (vec_dot_q5_0_4row_rvv): quantize + integer GEMV."""
+    _vk("jkb_vec_dot_q5_0_rvv", out, weights, x, stream)
+
+
+def vec_dot_q5_k_rvv(out, weights, x, stream=None):
+    """quant.rs:1225 vec_dot_q5_k_rvv: quantize + integer GEMV."""
+    _vk("jkb_vec_dot_q5_k_rvv", out, weights, x, stream)
 
 
 def vec_dot_i2_s(out, weights, x, stream=None):

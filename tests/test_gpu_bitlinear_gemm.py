@@ -90,7 +90,7 @@ def _weights(oracle, quant, rows, cols, seed):
     return oracle.quantize_weights(quant, oracle.normal(rows * cols, seed, 0.02), rows, cols)
 
 
-@pytest.mark.parametrize("quant", [8, 2, 12, 14, 35, 36])
+@pytest.mark.parametrize("quant", [8, 2, 12, 14, 35, 36, 6, 13])
 def test_repacked_weight_buffers_bit_exact(jkb, oracle, quant):
     rows, cols = 29, 1024
     wb = _weights(oracle, quant, rows, cols, 4)
@@ -110,7 +110,7 @@ def _oracle_gemm(oracle, quant, wb, rows, cols, act, m, r0=0, r1=None):
                                 nthreads=8)
 
 
-@pytest.mark.parametrize("quant", [8, 2, 12, 14, 35, 36])
+@pytest.mark.parametrize("quant", [8, 2, 12, 14, 35, 36, 6, 13])
 @pytest.mark.parametrize("m", [1, 5, 17, 64])
 def test_gemm_repacked_bit_exact(jkb, oracle, quant, m):
     """tests/test_repack_gemv_gemm.rs:751-829 shapes (M in {1,5,8,17,64}) on the GPU,

@@ -20,8 +20,9 @@ pytestmark = pytest.mark.gpu
 REL = 1e-5
 
 RVV_FN = {2: "vec_dot_q4_0_rvv", 8: "vec_dot_q8_0_rvv", 12: "vec_dot_q4_k_m_rvv",
-          14: "vec_dot_q6_k_rvv"}
-GEMV_FN = {2: "gemv_q4_0_q8_0", 8: "gemv_q8_0_q8_0", 12: "gemv_q4_k_q8_k", 14: "gemv_q6_k_q8_k"}
+          14: "vec_dot_q6_k_rvv", 6: "vec_dot_q5_0_rvv", 13: "vec_dot_q5_k_rvv"}
+GEMV_FN = {2: "gemv_q4_0_q8_0", 8: "gemv_q8_0_q8_0", 12: "gemv_q4_k_q8_k", 14: "gemv_q6_k_q8_k",
+           6: "gemv_q5_0_q8_0", 13: "gemv_q5_k_q8_k"}
 
 
 def weights(oracle, quant, rows, cols, seed):
@@ -30,7 +31,7 @@ def weights(oracle, quant, rows, cols, seed):
 
 def quantize_then_gemv(jkb, quant, w, x_dev):
     cols = x_dev.numel()
-    if quant in (2, 8):
+    if quant in (2, 8, 6):
         xq = jkb.empty_q8_0_blocks(cols // 32)
         jkb.quantize_row_q8_0(x_dev, xq)
     else:
@@ -60,7 +61,8 @@ def check_against_oracle(oracle, quant, wb, rows, cols, x, y):
 # Shapes cover every cluster size the launcher picks (1, 2, 4 and 8 CTAs), CTAs of 2, 4 and 8
 # warps, a partial last Q8_0 unit (96 columns) and a single block (32 columns).
 CASES = [(12, 37, 1024), (12, 64, 768), (12, 300, 14336), (12, 2048, 8192), (14, 33, 512),
-         (14, 129, 4096), (8, 17, 96), (8, 70, 4096), (8, 40, 14336), (2, 5, 32), (2, 200, 2048)]
+         (14, 129, 4096), (8, 17, 96), (8, 70, 4096), (8, 40, 14336), (2, 5, 32), (2, 200, 2048),
+         (6, 33, 1024), (6, 300, 14336), (13, 37, 1024), (13, 129, 4096)]
 
 
 @pytest.mark.parametrize("quant,rows,cols", CASES)
@@ -75,7 +77,7 @@ def test_rvv_equals_quantize_then_gemv(jkb, oracle, quant, rows, cols):
     w.destroy()
 
 
-@pytest.mark.parametrize("quant", [2, 8, 12, 14])
+@pytest.mark.parametrize("quant", [2, 8, 12, 14, 6, 13])
 def test_rvv_special_inputs(jkb, oracle, quant):
     """Non-finite inputs quantize to 0 (round_scaled_to_i8, quant_q8.rs:102-108) and do not
     enter the block absmax; all-zero and -0.0 blocks give a zero scale; extreme magnitudes."""

@@ -54,6 +54,8 @@ SHAPES = [
     (2, 64, 640, 1024),     # Q4_0
     (35, 96, 256, 512),     # TQ2_0
     (36, 40, 384, 2560),    # I2_S (per-tensor scale)
+    (6, 200, 300, 4096),    # Q5_0
+    (13, 200, 300, 4096),   # Q5_K (min terms)
 ]
 
 

@@ -19,9 +19,11 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 REL = 1e-5
 
 GEMV_FN = {2: "gemv_q4_0_q8_0", 8: "gemv_q8_0_q8_0", 12: "gemv_q4_k_q8_k",
-           14: "gemv_q6_k_q8_k", 34: "gemv_tq1_0_q8_k", 35: "gemv_tq2_0_q8_k"}
+           14: "gemv_q6_k_q8_k", 34: "gemv_tq1_0_q8_k", 35: "gemv_tq2_0_q8_k",
+           6: "gemv_q5_0_q8_0", 13: "gemv_q5_k_q8_k"}
 VEC_DOT_FN = {2: "vec_dot_q4_0_q8_0", 8: "vec_dot_q8_0_q8_0", 12: "vec_dot_q4_k_q8_k",
-              14: "vec_dot_q6_k_q8_k", 34: "vec_dot_tq1_0_q8_k", 35: "vec_dot_tq2_0_q8_k"}
+              14: "vec_dot_q6_k_q8_k", 34: "vec_dot_tq1_0_q8_k", 35: "vec_dot_tq2_0_q8_k",
+              6: "vec_dot_q5_0_q8_0_blocks", 13: "vec_dot_q5_k_q8_k"}
 
 
 def run_gemv(jkb, quant, w, xq_bytes):
@@ -38,7 +40,7 @@ def check_case(jkb, oracle, quant, wbytes, rows, cols, x, orient="rc"):
     sumi, summins, vals = (host(t) for t in jkb.gemv_block_dots(w, xd))
     s_ref, m_ref, v_ref = oracle.block_dots(quant, wbytes, rows, cols, xq)
     assert np.array_equal(sumi, s_ref), "per-block integer sums differ"
-    if quant == 12:
+    if quant in (12, 13):
         assert np.array_equal(summins, m_ref), "per-block min sums differ"
     assert np.array_equal(bits(vals), bits(v_ref)), "per-block f32 values differ"
     y = run_gemv(jkb, quant, w, xd)
@@ -53,7 +55,7 @@ def check_case(jkb, oracle, quant, wbytes, rows, cols, x, orient="rc"):
 
 def test_golden_fixtures(jkb, oracle):
     f = np.load(os.path.join(GOLDEN, "oracle_fixtures.npz"))
-    names = sorted({k.split("__")[0] for k in f.files})
+    names = sorted({k.split("__")[0] for k in f.files if k.endswith("__meta")})
     for name in names:
         q, rows, cols = (int(v) for v in f[f"{name}__meta"])
         wb = f[f"{name}__w"]
@@ -61,7 +63,7 @@ def test_golden_fixtures(jkb, oracle):
         xd = dev(f[f"{name}__xq"])
         sumi, summins, vals = (host(t) for t in jkb.gemv_block_dots(w, xd))
         assert np.array_equal(sumi, f[f"{name}__sumi"]), name
-        if q == 12:
+        if q in (12, 13):
             assert np.array_equal(summins, f[f"{name}__summins"]), name
         assert np.array_equal(bits(vals), bits(f[f"{name}__contrib"])), name
         y = run_gemv(jkb, q, w, xd)
@@ -70,7 +72,7 @@ def test_golden_fixtures(jkb, oracle):
         w.destroy()
 
 
-@pytest.mark.parametrize("quant", [2, 8, 12, 14, 35])
+@pytest.mark.parametrize("quant", [2, 8, 12, 14, 35, 6, 13])
 @pytest.mark.parametrize("rows,cols", [(1, 256), (5, 4096), (67, 1024), (300, 14336)])
 def test_gemv_random_normal(jkb, oracle, quant, rows, cols):
     if quant == 35:
@@ -116,7 +118,7 @@ def test_zero_and_nonfinite_scales(jkb, oracle):
     """f16_to_f32_finite (lib.rs:714-717): NaN/Inf block scales act as 0; zero-scale and
     zero-activation blocks contribute exactly 0 (quant_q8.rs:675-677, :1837-1839)."""
     rows, cols = 9, 512
-    for quant in (2, 8, 12, 14, 35):
+    for quant in (2, 8, 12, 14, 35, 6, 13):
         wb = oracle.quantize_weights(quant, oracle.normal(rows * cols, 3, 0.02), rows, cols) \
             if quant != 35 else oracle.pack_ternary(35, oracle.ternary(rows * cols, 3), rows,
                                                    cols, 0.02)
@@ -126,14 +128,14 @@ def test_zero_and_nonfinite_scales(jkb, oracle):
         blk[0, 0, doff:doff + 2] = [0x00, 0x7C]  # +Inf
         blk[1, 0, doff:doff + 2] = [0x01, 0x7E]  # NaN
         blk[2, 1, doff:doff + 2] = [0x00, 0x00]  # zero
-        if quant == 12:
+        if quant in (12, 13):
             blk[3, 1, 0:4] = 0  # d = dmin = 0
         x = oracle.normal(cols, 4, 1.0)
         x[:be] = 0.0  # first activation block all zero -> xd = 0
         check_case(jkb, oracle, quant, blk.reshape(-1), rows, cols, x)
 
 
-@pytest.mark.parametrize("quant", [2, 8, 12, 14, 34, 35])
+@pytest.mark.parametrize("quant", [2, 8, 12, 14, 34, 35, 6, 13])
 def test_vec_dot_single_row_bit_exact(jkb, oracle, quant):
     """vec_dot_*_q8_* on raw GGUF bytes: block values in parallel, then the reference's
     sequential `.sum()` -- bit-exact with the oracle."""
@@ -153,7 +155,8 @@ def test_vec_dot_single_row_bit_exact(jkb, oracle, quant):
 
 @pytest.mark.parametrize("quant,fn", [(12, "vec_dot_q4_k_m"), (8, "vec_dot_q8_0"),
                                       (14, "vec_dot_q6_k"), (2, "vec_dot_q4_0"),
-                                      (36, "vec_dot_i2_s")])
+                                      (36, "vec_dot_i2_s"), (6, "vec_dot_q5_0"),
+                                      (13, "vec_dot_q5_k")])
 def test_vec_dot_f32_activation_bit_exact(jkb, oracle, quant, fn):
     """VectorKernel f32-activation entries: dequantize -> sequential f32 dot (lib.rs:1268,
     quant.rs:899/1012/1401/2199), reproduced bit for bit."""
@@ -175,8 +178,10 @@ def test_kats_through_gpu(jkb, oracle):
 
     with open(os.path.join(GOLDEN, "kats.json")) as f:
         kats = json.load(f)
-    fns = {8: "vec_dot_q8_0", 14: "vec_dot_q6_k", 2: "vec_dot_q4_0", 12: "vec_dot_q4_k_m"}
-    for name in ("q8_0_vec_dot_f32", "q6_k_vec_dot_f32", "q4_0_vec_dot_f32", "q4_k_m_two_block"):
+    fns = {8: "vec_dot_q8_0", 14: "vec_dot_q6_k", 2: "vec_dot_q4_0", 12: "vec_dot_q4_k_m",
+           13: "vec_dot_q5_k"}
+    for name in ("q8_0_vec_dot_f32", "q6_k_vec_dot_f32", "q4_0_vec_dot_f32", "q4_k_m_two_block",
+                 "q5_k_dequant_sum"):
         k = kats[name]
         wb = np.frombuffer(bytes.fromhex(k["block_hex"]), np.uint8).copy()
         shape = k.get("shape", [k["rows"], k["cols"]])
