@@ -719,15 +719,19 @@ def _graph_time(fn, launches, warm=3):
 
 def run_gemm_case(args):
     """The repacked GEMM (BASELINE configs[2] kind) with Q8_0 (--kernel gemm_q8_0), Q4_K_M
-    (gemm_q4_k) or Q6_K (gemm_q6_k) weights: M tokens x --rows x --cols, activations quantized once
+    (gemm_q4_k) or Q6_K (gemm_q6_k) weights, or the compact nibble GEMM on Q4_K_M weights
+    (gemm_nib_q4_k, PackedNibbleMatrix): M tokens x --rows x --cols, activations quantized once
     (QuantizedActQ8), `--launches` GEMMs timed in a CUDA graph."""
     import torch
     import jkb200 as jkb
 
     M, N, K = args.m, args.rows, args.cols
-    quant = {"gemm_q4_k": Q4_K, "gemm_q6_k": Q6_K}.get(args.kernel, Q8_0)
+    quant = {"gemm_q4_k": Q4_K, "gemm_q6_k": Q6_K, "gemm_nib_q4_k": Q4_K}.get(args.kernel, Q8_0)
     raw = synth_matrix(quant, N, K, 4243)
-    rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", quant, [N, K], raw), N, K)
+    if args.kernel == "gemm_nib_q4_k":
+        rw = jkb.PackedNibbleMatrix.from_tensor(jkb.TensorView("w", quant, [N, K], raw), N, K)
+    else:
+        rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", quant, [N, K], raw), N, K)
     x = torch.randn(M * K, generator=torch.Generator().manual_seed(2)).cuda()
     act = jkb.QuantizedActQ8.quantize(x, M, K)
     out = torch.empty(M * N, dtype=torch.float32, device="cuda")
@@ -770,7 +774,7 @@ def main():
                     help="leave out the prefill GEMM section (BASELINE configs[2])")
     ap.add_argument("--m", type=int, default=2048, help="tokens of --kernel gemm_q8_0 / int8_peak")
     ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0", "gemm_q8_0", "gemm_q4_k",
-                                         "gemm_q6_k", "int8_peak"],
+                                         "gemm_q6_k", "gemm_nib_q4_k", "int8_peak"],
                     help="run one GEMV shape (profiling case) instead of the benchmark")
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--cols", type=int, default=4096)
@@ -782,7 +786,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.kernel in ("gemm_q8_0", "gemm_q4_k", "gemm_q6_k"):
+    if args.kernel in ("gemm_q8_0", "gemm_q4_k", "gemm_q6_k", "gemm_nib_q4_k"):
         run_gemm_case(args)
     elif args.kernel == "int8_peak":
         run_int8_peak(args)
