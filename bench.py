@@ -39,8 +39,10 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "jero-kernels-rvv_b200"))
 
-Q4_K, Q6_K, Q8_0 = 12, 14, 8
-BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), Q8_0: (32, 34)}
+Q4_K, Q6_K, Q8_0, TQ2_0, I2_S = 12, 14, 8, 35, 36
+BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), Q8_0: (32, 34), TQ2_0: (256, 66), I2_S: (128, 32)}
+# BitNet-b1.58-2B FFN: hidden 2560, intermediate 6912
+BITNET_HIDDEN, BITNET_FFN = 2560, 6912
 
 # (name, quant, rows, cols, activation stream)
 DECODE_8B = [
@@ -483,6 +485,7 @@ def run_gpu(args):
     e2e_val = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
 
     prefill = None if args.no_gemm else run_prefill_gemm(world, rank)
+    bitnet = None if args.no_bitnet else run_bitnet(world, rank)
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
@@ -520,6 +523,8 @@ def run_gpu(args):
         }
         if prefill is not None:
             res["prefill_gemm"] = prefill
+        if bitnet is not None:
+            res["bitnet"] = bitnet
         if world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline_single()
         print(json.dumps(res), flush=True)
@@ -535,6 +540,119 @@ def run_gpu(args):
 
 
 PREFILL = [(512, 14336, 4096), (512, 4096, 14336), (2048, 14336, 4096), (2048, 4096, 14336)]
+
+
+def synth_ternary(quant, rows, cols, seed, scale=0.02):
+    """iid ternary weights (-1, 0, +1 with p = 1/3 each) packed as TQ2_0 (every block's f16
+    scale = the tensor scale; byte i of a block holds elements 4i..4i+3, two bits each, value+1)
+    or I2_S (byte g of a 128-element block holds elements g, 32+g, 64+g, 96+g in bits 7:6, 5:4,
+    3:2, 1:0; the f32 tensor scale in a 32-byte trailer)."""
+    t = np.random.default_rng(seed).integers(0, 3, size=(rows, cols), dtype=np.uint8)
+    if quant == TQ2_0:
+        c = t.reshape(rows, cols // 256, 64, 4)
+        blk = np.empty((rows, cols // 256, 66), np.uint8)
+        blk[..., 0:2] = np.frombuffer(np.float16(scale).tobytes(), np.uint8)
+        blk[..., 2:] = c[..., 0] | (c[..., 1] << 2) | (c[..., 2] << 4) | (c[..., 3] << 6)
+        return blk.reshape(-1)
+    c = t.reshape(rows, cols // 128, 4, 32)
+    out = np.zeros(rows * cols // 4 + 32, np.uint8)
+    out[:-32] = ((c[:, :, 0] << 6) | (c[:, :, 1] << 4) | (c[:, :, 2] << 2) | c[:, :, 3]).reshape(-1)
+    out[-32:-28] = np.frombuffer(np.float32(scale).tobytes(), np.uint8)
+    return out
+
+
+def run_bitnet(world, rank, launches=20):
+    """BitNet-b1.58-2B ternary BitLinear, TQ2_0 and I2_S weights, hidden
+    2560 -> ffn 6912 and back, activations i8 per-token absmax-quantized (the SubLN quantizer
+    with unit norm weights) from N(0, 1). Output rows are sharded over the ranks; every number is
+    the max over ranks of a CUDA-event-timed CUDA graph of `launches` back-to-back calls.
+      batch 1:   bitlinear_i8 per shape, weight copies rotating so that each launch reads from
+                 HBM (GB/s of weight blocks + i8 activation + f32 output);
+      batch 128: bitlinear_i8_batch (each token one bitlinear_i8 call; up to eight tokens share
+                 every weight load) and the repacked tensor-core GEMM on the same weights with
+                 Q8_0-quantized activations (RepackedWeight.gemm), in TOPS (2*M*N*K);
+      FFN:       the whole chain SubLN -> gate/up -> ReLU^2 + SubLN -> down (jkb_bitnet_ffn) at
+                 1 and 128 tokens, in microseconds per call (unsharded, on every rank)."""
+    import torch
+    import torch.distributed as dist
+    import jkb200 as jkb
+
+    def maxr(us):
+        if world > 1:
+            t = torch.tensor([us], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item())
+        return us
+
+    H, F, M = BITNET_HIDDEN, BITNET_FFN, 128
+    res = {"shapes": [], "note": "hidden 2560, ffn 6912; ternary iid p=1/3, scale 0.02"}
+    norm = {n: torch.ones(n, device="cuda") for n in (H, F)}
+
+    def act_i8(n, m, seed):
+        x = torch.randn(m * n, generator=torch.Generator().manual_seed(seed)).cuda()
+        q = torch.empty(m * n, dtype=torch.int8, device="cuda")
+        sc = torch.empty(m, dtype=torch.float32, device="cuda")
+        jkb.subln_quantize_absmax_i8_rows(q, x, norm[n], m, n, 1e-5, sc)
+        return x, q, sc
+
+    for quant, qname in ((TQ2_0, "tq2_0"), (I2_S, "i2_s")):
+        for rows, cols in ((F, H), (H, F)):
+            per = rows // world
+            be, bb = BLOCK[quant]
+            wbytes = per * (cols // be) * bb
+            copies = max(2, -(-300_000_000 // wbytes))
+            raws = [synth_ternary(quant, per, cols, 77 + c) for c in range(min(copies, 4))]
+            ws = [jkb.Weight(jkb.TensorView("w", quant, [per, cols], raws[c % len(raws)]), per,
+                             cols) for c in range(copies)]
+            x1, q1, s1 = act_i8(cols, 1, 5)
+            out = torch.empty(per, dtype=torch.float32, device="cuda")
+            scale1 = float(s1.item())
+            it = [0]
+
+            def one():
+                jkb.bitlinear_i8(out, ws[it[0] % copies], q1, scale1)
+                it[0] += 1
+
+            us1 = maxr(_graph_time(one, max(launches, copies)))
+            nbytes = (rows // world) * (cols // be) * bb + cols + per * 4
+            row = {"quant": qname, "rows": rows, "cols": cols,
+                   "batch1_us": round(us1, 2),
+                   "batch1_gbs": round(nbytes * world / (us1 * 1e-6) / 1e9, 1)}
+            for w in ws[1:]:
+                w.destroy()
+            w = ws[0]
+            xm, qm, sm = act_i8(cols, M, 6)
+            ob = torch.empty(M * per, dtype=torch.float32, device="cuda")
+            usb = maxr(_graph_time(lambda: jkb.bitlinear_i8_batch(ob, w, qm, sm), launches))
+            row["batch128_bitlinear_us"] = round(usb, 2)
+            row["batch128_bitlinear_tops"] = round(2.0 * M * rows * cols / (usb * 1e-6) / 1e12,
+                                                   1)
+            rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", quant, [per, cols], raws[0]),
+                                                per, cols)
+            act = jkb.QuantizedActQ8.quantize(xm, M, cols)
+            usg = maxr(_graph_time(lambda: rw.gemm(ob, act), launches))
+            row["batch128_gemm_us"] = round(usg, 2)
+            row["batch128_gemm_tops"] = round(2.0 * M * rows * cols / (usg * 1e-6) / 1e12, 1)
+            res["shapes"].append(row)
+            rw.destroy()
+            act.destroy()
+            w.destroy()
+            del ob, xm, qm, sm
+        # the FFN chain (each rank runs the whole chain)
+        wg = jkb.Weight(jkb.TensorView("gate", quant, [F, H], synth_ternary(quant, F, H, 91)), F, H)
+        wu = jkb.Weight(jkb.TensorView("up", quant, [F, H], synth_ternary(quant, F, H, 92)), F, H)
+        wd = jkb.Weight(jkb.TensorView("down", quant, [H, F], synth_ternary(quant, H, F, 93)), H, F)
+        for m in (1, M):
+            ffn = jkb.BitNetFFN(wg, wu, wd, norm[H], norm[F], 1e-5, m)
+            x = torch.randn(m * H, generator=torch.Generator().manual_seed(8)).cuda()
+            out = torch.empty(m * H, dtype=torch.float32, device="cuda")
+            us = maxr(_graph_time(lambda: ffn.forward(out, x, m), launches))
+            res[f"ffn_{qname}_m{m}_us"] = round(us, 2)
+            ffn.destroy()
+        for w in (wg, wu, wd):
+            w.destroy()
+    torch.cuda.empty_cache()
+    return res
 
 
 def int8_peak_tops(launches=10):
@@ -772,6 +890,8 @@ def main():
                          "inside the f32-input GEMV launch (default: f, the lm_head input)")
     ap.add_argument("--no-gemm", action="store_true",
                     help="leave out the prefill GEMM section (BASELINE configs[2])")
+    ap.add_argument("--no-bitnet", action="store_true",
+                    help="leave out the BitNet BitLinear section (BASELINE configs[3])")
     ap.add_argument("--m", type=int, default=2048, help="tokens of --kernel gemm_q8_0 / int8_peak")
     ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0", "gemm_q8_0", "gemm_q4_k",
                                          "gemm_q6_k", "gemm_nib_q4_k", "int8_peak"],

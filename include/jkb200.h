@@ -149,6 +149,16 @@ int jkb_subln_quantize_absmax_i8(int8_t *out_i8, size_t out_len, const float *in
 int jkb_subln_quantize_absmax_i8_rows(int8_t *out_i8, const float *input,
                                       const float *norm_weight, size_t m, size_t len, float eps,
                                       float *scales_out, void *stream);
+/* lib.rs:1111 relu_squared_gate_f32: out[i] = max(0, gate[i])^2 * up[i] (device buffers). */
+int jkb_relu_squared_gate_f32(float *out, size_t out_len, const float *gate, size_t gate_len,
+                              const float *up, size_t up_len, void *stream);
+/* relu_squared_gate_f32 followed by subln_quantize_absmax_i8 on the result, m rows of len in
+ * one kernel (gate, up [m][len]; out_i8 [m][len]; scales_out [m]). relu_out ([m][len], may be
+ * NULL) receives the gated activation. Each row equals the two reference calls in sequence. */
+int jkb_relu_squared_subln_quantize_i8_rows(int8_t *out_i8, float *relu_out, const float *gate,
+                                            const float *up, const float *norm_weight, size_t m,
+                                            size_t len, float eps, float *scales_out,
+                                            void *stream);
 
 /* ---- QuantizedActQ8 (repack.rs:461-724) ---- */
 /* Allocates device buffers for up to m_capacity rows of k elements (load time). */
@@ -325,6 +335,34 @@ int jkb_bitlinear_i8_ime(float *out, size_t out_len, const jkb_weight *w, const 
  * out [m][rows]; each token is exactly one reference call. */
 int jkb_bitlinear_i8_batch(float *out, size_t out_len, const jkb_weight *w, const int8_t *act_i8,
                            size_t act_len, const float *act_scales, size_t m, void *stream);
+
+/* ---- BitNet b1.58 feed-forward chain ---- */
+/* No single reference function: the chain the reference composes in
+ * tests/empirical_challenge_m3_bitnet.rs:582-686 for m tokens --
+ *   act1, s1 = subln_quantize_absmax_i8(x, norm1, eps)           (lib.rs:1042)
+ *   gate = bitlinear_i8(w_gate, act1, s1), up = bitlinear_i8(w_up, act1, s1)   (ime.rs:882)
+ *   h = relu_squared_gate_f32(gate, up)                            (lib.rs:1111)
+ *   act2, s2 = subln_quantize_absmax_i8(h, norm2, eps)
+ *   out = bitlinear_i8(w_down, act2, s2)
+ * w_gate / w_up are [intermediate, hidden], w_down [hidden, intermediate] (TQ1_0, TQ2_0, Q8_0 or
+ * I2_S, each validated as its bitlinear_i8 call). The handle borrows the weights and the device
+ * norm weights (norm1 [hidden], norm2 [intermediate]) and owns the intermediates for up to
+ * m_capacity tokens, allocated here; forward allocates nothing. x and out are [m][hidden] on the
+ * device; the four kernels run on `stream`. */
+typedef struct jkb_bitnet_ffn jkb_bitnet_ffn;
+int jkb_bitnet_ffn_create(const jkb_weight *w_gate, const jkb_weight *w_up,
+                          const jkb_weight *w_down, const float *norm1, size_t norm1_len,
+                          const float *norm2, size_t norm2_len, float eps, size_t m_capacity,
+                          jkb_bitnet_ffn **out);
+int jkb_bitnet_ffn_forward(jkb_bitnet_ffn *ffn, float *out, size_t out_len, const float *x,
+                           size_t x_len, size_t m, void *stream);
+/* Device views of the last forward's intermediates ([m_capacity] rows each; NULL to skip):
+ * act1 i8 [hidden], scale1, gate / up / relu f32 [intermediate], act2 i8 [intermediate],
+ * scale2. */
+int jkb_bitnet_ffn_buffers(const jkb_bitnet_ffn *ffn, int8_t **act1, float **scale1,
+                           float **gate, float **up, float **relu, int8_t **act2,
+                           float **scale2);
+int jkb_bitnet_ffn_destroy(jkb_bitnet_ffn *ffn);
 
 /* ---- RepackedWeight + GEMM (repack.rs) ---- */
 /* repack.rs:2288 RepackedWeight::from_tensor (explicit [rows, cols]) */

@@ -381,7 +381,7 @@ static int vec_dot_f32_call(const char *fn, int quant, float *out, size_t out_le
 // ---------------------------------------------------------------- BitLinear glue
 
 // validate_bitlinear_dimensions (ime.rs:660-763)
-static int validate_bitlinear(const jkb_weight *w, size_t output_len, size_t input_len) {
+int validate_bitlinear(const jkb_weight *w, size_t output_len, size_t input_len) {
     int rc = check_weight(w);
     if (rc) return rc;
     if (w->quant != JKB_TQ1_0 && w->quant != JKB_TQ2_0 && w->quant != JKB_Q8_0 &&

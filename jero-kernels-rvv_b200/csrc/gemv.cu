@@ -259,7 +259,12 @@ struct ActI8 {
     static __device__ __forceinline__ int tot(const uint8_t *s, int K, int b) {
         return reinterpret_cast<const int *>(s + K)[b];
     }
+    // the token's activation scale, stored after the block totals by stage()
+    static __device__ __forceinline__ float scale(const KArgs &a, const uint8_t *s) {
+        return *reinterpret_cast<const float *>(s + a.K + (a.K / BE) * 4);
+    }
     static __device__ void stage(const KArgs &a, const uint8_t *x, uint8_t *s) {
+        if (threadIdx.x == 0) *reinterpret_cast<float *>(s + a.K + (a.K / BE) * 4) = a.act_scale;
         auto put = [&](int wi, uint32_t v) {
             const int e = 4 * wi, b = e / BE, off = e - b * BE, j = off >> 4;
             *(uint32_t *)(s + b * BE + 16 * (j ^ swz(b)) + (off & 15)) = v;
@@ -557,7 +562,7 @@ __device__ __forceinline__ float FQ8_0<ActI8<32>>::value(const KArgs &a, const u
                                                           const Ld &l, int b, int2 &iv) {
     const int sumi = sum(s, l, b);
     iv = make_int2(sumi, 0);
-    return __fmul_rn((float)sumi, __fmul_rn(f16_finite(l.d), a.act_scale));
+    return __fmul_rn((float)sumi, __fmul_rn(f16_finite(l.d), ActI8<32>::scale(a, s)));
 }
 
 // Q4_K x Q8_K (quant_q8.rs:1817-1862). Chunk pair (2c, 2c+1) holds qs[32c..32c+32]: low
@@ -854,7 +859,7 @@ __device__ __forceinline__ float FTQ2<ActI8<256>>::value(const KArgs &a, const u
                                                          const Ld &l, int b, int2 &iv) {
     const int sumi = codes(s, l, b) - ActI8<256>::tot(s, a.K, b);
     iv = make_int2(sumi, 0);
-    return __fmul_rn((float)sumi, __fmul_rn(f16_finite(l.d), a.act_scale));
+    return __fmul_rn((float)sumi, __fmul_rn(f16_finite(l.d), ActI8<256>::scale(a, s)));
 }
 
 // I2_S BitLinear (quant.rs:370-377, ime.rs:918-929). Chunk h holds bytes 16h..16h+16; byte g
@@ -891,7 +896,7 @@ struct FI2S {
         }
         const int sumi = t - Act::tot(s, a.K, b);
         iv = make_int2(sumi, 0);
-        return __fmul_rn((float)sumi, __fmul_rn(a.i2s_scale, a.act_scale));
+        return __fmul_rn((float)sumi, __fmul_rn(a.i2s_scale, Act::scale(a, s)));
     }
 };
 
@@ -1014,8 +1019,10 @@ __global__ void __launch_bounds__(MAX_WARPS * 32) gemv_kernel(KArgs a) {
     pdl_wait();
     pdl_launch_dependents();
     if (MODE == M_TOK) {
-        for (int t = 0; t < nt; t++)
+        for (int t = 0; t < nt; t++) {
+            if (a.act_scales) args.act_scale = a.act_scales[tok + t];
             S::stage(args, a.x + (size_t)(tok + t) * a.x_row_stride, smem + t * slot);
+        }
     } else {
         if (a.act_scales) args.act_scale = a.act_scales[tok];
         S::stage(args, a.x + (size_t)tok * a.x_row_stride, smem);
@@ -1132,7 +1139,8 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
         for (int i = 0; i < L.nmat; i++) {
             const jkb_weight *wi = L.ws[i];
             if (wi->gpu_format != w->gpu_format || wi->cols != w->cols ||
-                wi->p.qs_row != w->p.qs_row || wi->p.sc_row != w->p.sc_row)
+                wi->p.qs_row != w->p.qs_row || wi->p.sc_row != w->p.sc_row ||
+                wi->p.i2s_scale != w->p.i2s_scale)
                 return fail(JKB_E_INVALID, wi->name, wi->offset, wi->byte_len, wi->gguf_bytes,
                             "grouped GEMV: %s [%zu, %zu] does not share the format and width "
                             "of %s [%zu, %zu]",
@@ -1172,12 +1180,18 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
                     w->cols, MAX_K);
     if (a.row_end <= a.row_begin) return JKB_OK;
     const bool diag = L.dbg_sumi != nullptr;
-    // token batches of pre-quantized input without per-token scales share weight loads
-    const bool tokb = !multi && !diag && (L.m ? L.m : 1) > 1 && L.act_scales == nullptr &&
-                      (L.act_kind == ACT_Q8_0 || L.act_kind == ACT_Q8_K);
-    const size_t m = multi ? 1 : (L.m ? L.m : 1);
+    // token batches of pre-quantized input (Q8 blocks, or i8 with per-token scales) share
+    // weight loads
+    const bool tokb = !multi && !diag && (L.m ? L.m : 1) > 1 &&
+                      (L.act_kind == ACT_I8 ||
+                       (L.act_scales == nullptr &&
+                        (L.act_kind == ACT_Q8_0 || L.act_kind == ACT_Q8_K)));
+    // grouped launches: f32 input (one token), or i8 BitLinear activations (m tokens, every
+    // matrix writing [m][out_ld])
+    const bool multi_i8 = multi && L.act_kind == ACT_I8;
+    const size_t m = multi && !multi_i8 ? 1 : (L.m ? L.m : 1);
     const bool f32_in = L.act_kind == ACT_F32_Q8_0 || L.act_kind == ACT_F32_Q8_K;
-    if ((multi && (!f32_in || diag)) || (diag && f32_in))
+    if ((multi && ((!f32_in && !multi_i8) || diag)) || (diag && f32_in))
         return fail(JKB_E_CAPABILITY, w->name, w->offset, w->byte_len, w->gguf_bytes,
                     "no GEMV kernel for this combination of grouped/diagnostic launch and "
                     "activation kind %d",
@@ -1187,6 +1201,10 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
     return diag  ? launch_t<F, F::Act, M_DIAG>(a, m, st, "gemv_kernel<diag>")           \
            : tokb ? launch_t<F, F::Act, M_TOK>(a, m, st, "gemv_kernel<tokens>")          \
                   : launch_t<F, F::Act, M_SINGLE>(a, m, st, "gemv_kernel")
+    // i8 activations over several matrices (the BitNet gate and up projections)
+#define JKB_LAUNCH_I8(F)                                                                \
+    if (multi) return launch_t<F, F::Act, M_MULTI>(a, m, st, "gemv_kernel<grouped i8>"); \
+    JKB_LAUNCH(F)
     // f32 activations quantized by the stager S: single or grouped launches
 #define JKB_LAUNCH_F32(F, S)                                                            \
     return multi ? launch_t<F, S, M_MULTI>(a, m, st, "gemv_kernel<grouped>")            \
@@ -1198,7 +1216,7 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
         break;
     case GF_Q8_0:
         if (L.act_kind == ACT_Q8_0) JKB_LAUNCH(FQ8_0<ActQ80>);
-        if (L.act_kind == ACT_I8) JKB_LAUNCH(FQ8_0<ActI8<32>>);
+        if (L.act_kind == ACT_I8) { JKB_LAUNCH_I8(FQ8_0<ActI8<32>>); }
         if (L.act_kind == ACT_F32_Q8_0) JKB_LAUNCH_F32(FQ8_0<ActQ80>, ActQ80F32);
         break;
     case GF_Q4_K:
@@ -1219,13 +1237,14 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
         break;
     case GF_TQ2_0:
         if (L.act_kind == ACT_Q8_K) JKB_LAUNCH(FTQ2<ActQ8K>);
-        if (L.act_kind == ACT_I8) JKB_LAUNCH(FTQ2<ActI8<256>>);
+        if (L.act_kind == ACT_I8) { JKB_LAUNCH_I8(FTQ2<ActI8<256>>); }
         break;
     case GF_I2_S:
-        if (L.act_kind == ACT_I8) JKB_LAUNCH(FI2S);
+        if (L.act_kind == ACT_I8) { JKB_LAUNCH_I8(FI2S); }
         break;
     }
 #undef JKB_LAUNCH
+#undef JKB_LAUNCH_I8
 #undef JKB_LAUNCH_F32
     return fail(JKB_E_CAPABILITY, w->name, w->offset, w->byte_len, w->gguf_bytes,
                 "no GEMV kernel for %s weights with activation kind %d", quant_name(w->quant),

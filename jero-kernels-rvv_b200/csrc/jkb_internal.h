@@ -213,5 +213,16 @@ struct GemvLaunch {
 };
 int launch_gemv(const GemvLaunch &L, cudaStream_t st);
 
+// validate_bitlinear_dimensions (ime.rs:660-763) on a handle (dots.cu).
+int validate_bitlinear(const jkb_weight *w, size_t output_len, size_t input_len);
+
+// subln_quantize_absmax_i8 over m rows of len (quantize.cu); gate: the rows are
+// relu_squared_gate_f32(input, up), stored to relu_out when non-null. Arguments are validated
+// by the caller; len <= SUBLN_MAX_LEN.
+constexpr size_t SUBLN_MAX_LEN = 200 * 1024 / 4;
+int launch_subln(bool gate, int8_t *out_i8, float *relu_out, const float *input,
+                 const float *up, const float *norm_weight, size_t m, size_t len, float eps,
+                 float *scales_out, cudaStream_t st);
+
 
 }  // namespace jkb

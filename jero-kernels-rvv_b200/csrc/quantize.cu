@@ -209,34 +209,111 @@ __global__ void act_super_kernel(const float *__restrict__ xs, size_t m, size_t 
     sup[gid] = v;
 }
 
+// relu_squared_gate_scalar (lib.rs:1130-1137): max(0, g)^2 * u, the two products rounded in the
+// reference's order ((relu * relu) * up). NaN and -0 gates give +0 (g > 0 is false), as in the
+// reference and its vfmax form.
+__device__ __forceinline__ float relu_squared_gate(float g, float u) {
+    const float r = g > 0.0f ? g : 0.0f;
+    return __fmul_rn(__fmul_rn(r, r), u);
+}
+
+// relu_squared_gate_f32 (lib.rs:1111-1148): elementwise over n values.
+__global__ void __launch_bounds__(256) relu_squared_kernel(const float *__restrict__ gate,
+                                                           const float *__restrict__ up,
+                                                           size_t n, float *__restrict__ out) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x)
+        out[i] = relu_squared_gate(__ldg(gate + i), __ldg(up + i));
+}
+
 // subln_quantize_absmax_i8 (lib.rs:1042-1101), one CTA per row. The sum of squares is the
-// reference's sequential f32 dot (lib.rs:770-777), so one thread walks it in element order;
-// the absmax and the quantization are elementwise and run on all threads.
-__global__ void __launch_bounds__(256) subln_kernel(const float *__restrict__ in,
-                                                    const float *__restrict__ w, size_t len,
-                                                    float eps, int8_t *__restrict__ out,
-                                                    float *__restrict__ scales) {
-    extern __shared__ float sx[];
-    __shared__ float s_inv_rms, s_red[8];
-    const float *x = in + (size_t)blockIdx.x * len;
-    int8_t *o = out + (size_t)blockIdx.x * len;
-    for (size_t i = threadIdx.x; i < len; i += blockDim.x) {
-        float v = __ldg(x + i);
-        sx[i] = __fmul_rn(v, v);
+// reference's sequential f32 dot (dot_product_f32_scalar, lib.rs:770-777), so one thread walks
+// it in element order; everything else is elementwise (the absmax a max-reduction) and runs on
+// all threads. The row is read from global memory once (16-byte loads where the row allows)
+// and kept in shared memory for the three passes.
+// GATE: the row is relu_squared_gate_f32 of (in, up) (lib.rs:1111-1148), formed here and stored
+// to relu_out when that is non-null, so that the BitNet FFN's activation of the down projection
+// is one kernel; otherwise the row is in itself.
+constexpr int SUBLN_THREADS = 512;
+
+template <bool GATE>
+__global__ void __launch_bounds__(SUBLN_THREADS) subln_kernel(
+    const float *__restrict__ in, const float *__restrict__ up, const float *__restrict__ w,
+    size_t len, float eps, int8_t *__restrict__ out, float *__restrict__ scales,
+    float *__restrict__ relu_out) {
+    extern __shared__ __align__(16) float sx[];
+    __shared__ float s_inv_rms, s_red[SUBLN_THREADS / 32];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+    const size_t row = (size_t)blockIdx.x * len;
+    int8_t *o = out + row;
+    auto aligned16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+    const bool vec = (len & 3) == 0 && aligned16(in + row) &&
+                     (!GATE || (aligned16(up + row) && (!relu_out || aligned16(relu_out + row))));
+    // pass 0: the row (or its ReLU^2 gating) into shared memory
+    if (vec) {
+        const size_t n4 = len / 4;
+        const float4 *i4 = reinterpret_cast<const float4 *>(in + row);
+        for (size_t i = threadIdx.x; i < n4; i += blockDim.x) {
+            float4 v = __ldg(i4 + i);
+            if (GATE) {
+                const float4 u = __ldg(reinterpret_cast<const float4 *>(up + row) + i);
+                v = make_float4(relu_squared_gate(v.x, u.x), relu_squared_gate(v.y, u.y),
+                                relu_squared_gate(v.z, u.z), relu_squared_gate(v.w, u.w));
+                if (relu_out) reinterpret_cast<float4 *>(relu_out + row)[i] = v;
+            }
+            reinterpret_cast<float4 *>(sx)[i] = v;
+        }
+    } else {
+        for (size_t i = threadIdx.x; i < len; i += blockDim.x) {
+            float v = __ldg(in + row + i);
+            if (GATE) {
+                v = relu_squared_gate(v, __ldg(up + row + i));
+                if (relu_out) relu_out[row + i] = v;
+            }
+            sx[i] = v;
+        }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
+        // sum += x * x in element order: a dependent chain of f32 adds (the products are
+        // independent of it); 16-byte loads two groups ahead keep it at the add latency
         float s0 = 0.0f;
-        for (size_t i = 0; i < len; i++) s0 = __fadd_rn(s0, sx[i]);
+        const size_t n8 = len / 8;
+        if (n8) {
+            const float4 *s4 = reinterpret_cast<const float4 *>(sx);
+            float4 a = s4[0], b = s4[1];
+            for (size_t j = 0; j < n8; j++) {
+                float4 na = a, nb = b;
+                if (j + 1 < n8) {
+                    na = s4[2 * j + 2];
+                    nb = s4[2 * j + 3];
+                }
+                s0 = __fadd_rn(s0, __fmul_rn(a.x, a.x));
+                s0 = __fadd_rn(s0, __fmul_rn(a.y, a.y));
+                s0 = __fadd_rn(s0, __fmul_rn(a.z, a.z));
+                s0 = __fadd_rn(s0, __fmul_rn(a.w, a.w));
+                s0 = __fadd_rn(s0, __fmul_rn(b.x, b.x));
+                s0 = __fadd_rn(s0, __fmul_rn(b.y, b.y));
+                s0 = __fadd_rn(s0, __fmul_rn(b.z, b.z));
+                s0 = __fadd_rn(s0, __fmul_rn(b.w, b.w));
+                a = na;
+                b = nb;
+            }
+        }
+        for (size_t i = n8 * 8; i < len; i++) s0 = __fadd_rn(s0, __fmul_rn(sx[i], sx[i]));
         float mean_sq = __fdiv_rn(s0, (float)len);
         s_inv_rms = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean_sq, eps)));
     }
     __syncthreads();
-    float inv_rms = s_inv_rms;
+    // pass 1: x_norm = x * inv_rms * norm_weight (in place) and its absmax
+    const float inv_rms = s_inv_rms;
     float mx = 0.0f;
     for (size_t i = threadIdx.x; i < len; i += blockDim.x) {
-        float xn = __fmul_rn(__fmul_rn(__ldg(x + i), inv_rms), __ldg(w + i));
-        float av = fabsf(xn);
+        const float xn = __fmul_rn(__fmul_rn(sx[i], inv_rms), __ldg(w + i));
+        const float av = fabsf(xn);
         sx[i] = xn;
         if (av > mx) mx = av;
     }
@@ -254,13 +331,14 @@ __global__ void __launch_bounds__(256) subln_kernel(const float *__restrict__ in
         s_red[0] = v;
     }
     __syncthreads();
-    float max_val = s_red[0];
+    // pass 2: quantize (or the guarded all-zero row)
+    const float max_val = s_red[0];
     if (isnan(max_val) || max_val < 1e-12f) {
         for (size_t i = threadIdx.x; i < len; i += blockDim.x) o[i] = 0;
         if (threadIdx.x == 0) scales[blockIdx.x] = __fdiv_rn(1.0f, 127.0f);
         return;
     }
-    float scale = __fdiv_rn(max_val, 127.0f);
+    const float scale = __fdiv_rn(max_val, 127.0f);
     for (size_t i = threadIdx.x; i < len; i += blockDim.x) {
         float q = roundf(__fdiv_rn(sx[i], scale));
         int qi = 0;
@@ -268,6 +346,22 @@ __global__ void __launch_bounds__(256) subln_kernel(const float *__restrict__ in
         o[i] = (int8_t)qi;
     }
     if (threadIdx.x == 0) scales[blockIdx.x] = scale;
+}
+
+// Launches subln_kernel<GATE> over m rows of len (arguments validated by the callers).
+int launch_subln(bool gate, int8_t *out_i8, float *relu_out, const float *input,
+                 const float *up, const float *norm_weight, size_t m, size_t len, float eps,
+                 float *scales_out, cudaStream_t st) {
+    auto kern = gate ? subln_kernel<true> : subln_kernel<false>;
+    static bool attr[2] = {false, false};
+    if (!attr[gate]) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(SUBLN_MAX_LEN * 4));
+        attr[gate] = true;
+    }
+    cudaError_t e = launch_pdl(kern, dim3((unsigned)m), dim3(SUBLN_THREADS), len * sizeof(float), st,
+                               input, up, norm_weight, len, eps, out_i8, scales_out, relu_out);
+    return e == cudaSuccess ? JKB_OK : fail_cuda(e, "subln_kernel");
 }
 
 // validate_activation_input / validate_activation_quant_slice (quant_q8.rs:111-149)
@@ -377,20 +471,55 @@ int jkb_subln_quantize_absmax_i8_rows(int8_t *out_i8, const float *input,
         (rc = check_align(norm_weight, 4, "subln", "norm_weight")) ||
         (rc = check_align(scales_out, 4, "subln", "scale")))
         return rc;
-    size_t smem = len * sizeof(float);
-    if (smem > 200 * 1024)
-        return fail(JKB_E_BOUNDS, "subln", 0, len, 200 * 1024 / 4,
-                    "row length %zu exceeds the %d-element limit of the GPU kernel", len,
-                    200 * 1024 / 4);
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(subln_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             200 * 1024);
-        attr = true;
-    }
-    subln_kernel<<<(unsigned)m, 256, smem, as_stream(stream)>>>(input, norm_weight, len, eps,
-                                                                out_i8, scales_out);
-    return check_launch("subln_kernel");
+    if (len > SUBLN_MAX_LEN)
+        return fail(JKB_E_BOUNDS, "subln", 0, len, SUBLN_MAX_LEN,
+                    "row length %zu exceeds the %zu-element limit of the GPU kernel", len,
+                    SUBLN_MAX_LEN);
+    return launch_subln(false, out_i8, nullptr, input, nullptr, norm_weight, m, len, eps,
+                        scales_out, as_stream(stream));
+}
+
+int jkb_relu_squared_gate_f32(float *out, size_t out_len, const float *gate, size_t gate_len,
+                              const float *up, size_t up_len, void *stream) {
+    if (gate_len == 0 || out_len != gate_len || up_len != gate_len)
+        return fail(JKB_E_BOUNDS, "relu_squared", 0, out_len * 4, gate_len * 4,
+                    "dimension mismatch: gate=%zu, up=%zu, out=%zu", gate_len, up_len, out_len);
+    if (!out || !gate || !up) return fail(JKB_E_INVALID, "relu_squared", 0, 0, 0, "null pointer");
+    int rc;
+    if ((rc = check_align(out, 4, "relu_squared", "out")) ||
+        (rc = check_align(gate, 4, "relu_squared", "gate")) ||
+        (rc = check_align(up, 4, "relu_squared", "up")))
+        return rc;
+    size_t grid = (gate_len + 255) / 256;
+    const size_t cap = (size_t)num_sms() * 8;
+    if (grid > cap) grid = cap;
+    cudaError_t e = launch_pdl(relu_squared_kernel, dim3((unsigned)grid), dim3(256), 0,
+                               as_stream(stream), gate, up, gate_len, out);
+    return e == cudaSuccess ? JKB_OK : fail_cuda(e, "relu_squared_kernel");
+}
+
+int jkb_relu_squared_subln_quantize_i8_rows(int8_t *out_i8, float *relu_out, const float *gate,
+                                            const float *up, const float *norm_weight, size_t m,
+                                            size_t len, float eps, float *scales_out,
+                                            void *stream) {
+    if (len == 0 || m == 0)
+        return fail(JKB_E_BOUNDS, "subln", 0, 0, len * 4,
+                    "dimension mismatch: input=%zu, rows=%zu", len, m);
+    if (!out_i8 || !gate || !up || !norm_weight || !scales_out)
+        return fail(JKB_E_INVALID, "subln", 0, 0, 0, "null pointer");
+    int rc;
+    if ((rc = check_align(gate, 4, "relu_squared", "gate")) ||
+        (rc = check_align(up, 4, "relu_squared", "up")) ||
+        (relu_out && (rc = check_align(relu_out, 4, "relu_squared", "out"))) ||
+        (rc = check_align(norm_weight, 4, "subln", "norm_weight")) ||
+        (rc = check_align(scales_out, 4, "subln", "scale")))
+        return rc;
+    if (len > SUBLN_MAX_LEN)
+        return fail(JKB_E_BOUNDS, "subln", 0, len, SUBLN_MAX_LEN,
+                    "row length %zu exceeds the %zu-element limit of the GPU kernel", len,
+                    SUBLN_MAX_LEN);
+    return launch_subln(true, out_i8, relu_out, gate, up, norm_weight, m, len, eps, scales_out,
+                        as_stream(stream));
 }
 
 int jkb_subln_quantize_absmax_i8(int8_t *out_i8, size_t out_len, const float *input,

@@ -34,7 +34,8 @@ __all__ = [
     "device_view", "PackedNibbleMatrix", "gemm_q4_0_ime", "gemm_q4_k_ime",
     "repack_nibble_into_tile_range", "vec_dot_q5_0_q8_0_blocks", "vec_dot_q5_k_q8_k",
     "gemv_q5_0_q8_0", "gemv_q5_0_q8_0_4x", "gemv_q5_k_q8_k", "vec_dot_q5_0", "vec_dot_q5_k",
-    "vec_dot_q5_0_rvv", "vec_dot_q5_k_rvv",
+    "vec_dot_q5_0_rvv", "vec_dot_q5_k_rvv", "relu_squared_gate_f32",
+    "relu_squared_subln_quantize_i8_rows", "BitNetFFN",
 ]
 
 
@@ -585,6 +586,62 @@ def subln_quantize_absmax_i8_rows(out_i8, x, norm_weight, m, length, eps, scales
     _check(_L().jkb_subln_quantize_absmax_i8_rows(_dptr(out_i8), _dptr(x), _dptr(norm_weight), m,
                                                   length, eps, _dptr(scales_out),
                                                   _stream(stream)))
+
+
+def relu_squared_gate_f32(out, gate, up, stream=None):
+    """lib.rs:1111 relu_squared_gate_f32: out = max(0, gate)^2 * up."""
+    _check(_L().jkb_relu_squared_gate_f32(_dptr(out), out.numel(), _dptr(gate), gate.numel(),
+                                          _dptr(up), up.numel(), _stream(stream)))
+
+
+def relu_squared_subln_quantize_i8_rows(out_i8, relu_out, gate, up, norm_weight, m, length, eps,
+                                        scales_out, stream=None):
+    """relu_squared_gate_f32 then subln_quantize_absmax_i8 on each of m rows, one kernel."""
+    _check(_L().jkb_relu_squared_subln_quantize_i8_rows(
+        _dptr(out_i8), _dptr(relu_out), _dptr(gate), _dptr(up), _dptr(norm_weight), m, length,
+        eps, _dptr(scales_out), _stream(stream)))
+
+
+class BitNetFFN:
+    """The BitNet b1.58 FFN chain (tests/empirical_challenge_m3_bitnet.rs:582-686) over device
+    buffers: SubLN -> gate/up bitlinear_i8 -> relu_squared_gate_f32 -> SubLN -> down
+    bitlinear_i8. Borrows the weights and the norm weights; owns the intermediates."""
+
+    def __init__(self, w_gate: "Weight", w_up: "Weight", w_down: "Weight", norm1: torch.Tensor,
+                 norm2: torch.Tensor, eps: float, m_capacity: int = 1):
+        h = C.c_void_p()
+        _check(_L().jkb_bitnet_ffn_create(w_gate.handle, w_up.handle, w_down.handle,
+                                          _dptr(norm1), norm1.numel(), _dptr(norm2),
+                                          norm2.numel(), eps, m_capacity, C.byref(h)))
+        self._h = h.value
+        # keep the borrowed objects alive as long as the handle
+        self._refs = (w_gate, w_up, w_down, norm1, norm2)
+        self.hidden, self.inter = w_gate.cols, w_gate.rows
+        self.m_capacity = m_capacity
+
+    def forward(self, out: torch.Tensor, x: torch.Tensor, m: int = 1, stream=None):
+        _check(_L().jkb_bitnet_ffn_forward(self._h, _dptr(out), out.numel(), _dptr(x), x.numel(),
+                                           m, _stream(stream)))
+
+    def buffers(self):
+        """Device views of the intermediates: act1, scale1, gate, up, relu, act2, scale2."""
+        ptrs = [C.c_void_p() for _ in range(7)]
+        _check(_L().jkb_bitnet_ffn_buffers(self._h, *[C.byref(p) for p in ptrs]))
+        M, H, I = self.m_capacity, self.hidden, self.inter
+        shapes = [((M, H), "i1"), ((M,), "<f4"), ((M, I), "<f4"), ((M, I), "<f4"),
+                  ((M, I), "<f4"), ((M, I), "i1"), ((M,), "<f4")]
+        return tuple(device_view(p.value, sh, dt) for p, (sh, dt) in zip(ptrs, shapes))
+
+    def destroy(self):
+        if getattr(self, "_h", None):
+            _L().jkb_bitnet_ffn_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
 
 
 # ------------------------------------------------------------------------------- block dots

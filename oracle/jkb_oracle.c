@@ -258,6 +258,18 @@ int or_subln_quantize_absmax_i8(int8_t *out, const float *in, const float *norm_
     return 0;
 }
 
+/* relu_squared_gate_scalar (lib.rs:1130-1137): out[i] = (relu * relu) * up[i] with
+ * relu = g > 0 ? g : 0 (NaN and -0 gates give +0). */
+int or_relu_squared_gate_f32(float *out, const float *gate, const float *up, size_t len) {
+    if (len == 0) return 1;
+    for (size_t i = 0; i < len; i++) {
+        float g = gate[i];
+        float relu = g > 0.0f ? g : 0.0f;
+        out[i] = relu * relu * up[i];
+    }
+    return 0;
+}
+
 /* ------------------------------------------------------------------------------------------ */
 /* Block dots (quant_q8.rs)                                                                    */
 /* ------------------------------------------------------------------------------------------ */

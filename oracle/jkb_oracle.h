@@ -66,6 +66,7 @@ int or_act_q8_quantize(const float *act, size_t m, size_t k, int8_t *q, float *x
                        float *x_sums, float *x_sums_16, float *super_scales);
 int or_subln_quantize_absmax_i8(int8_t *out, const float *in, const float *norm_w, size_t len,
                                 float eps, float *scale_out);
+int or_relu_squared_gate_f32(float *out, const float *gate, const float *up, size_t len);
 
 /* ---- block dots (value as the reference returns it; integer sums through out-params) ---- */
 float or_dot_q4_0_q8_0_block(const uint8_t *w, const or_block_q8_0 *x, int32_t *sumi);

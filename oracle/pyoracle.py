@@ -63,6 +63,7 @@ def lib() -> C.CDLL:
             "or_quantize_block32": (None, [P, P, P, P]),
             "or_act_q8_quantize": (I, [P, S, S, P, P, P, P, P]),
             "or_subln_quantize_absmax_i8": (I, [P, P, P, S, F, P]),
+            "or_relu_squared_gate_f32": (I, [P, P, P, S]),
             "or_block_dots": (I, [I, P, S, S, P, P, P, P]),
             "or_gemv": (I, [I, P, P, S, S, P]),
             "or_gemv_rows_mt": (I, [I, P, P, S, S, P, S, S, I]),
@@ -205,6 +206,29 @@ def subln_quantize_absmax_i8(x, norm_w, eps):
     if lib().or_subln_quantize_absmax_i8(_p(out), _p(x), _p(norm_w), x.size, eps, _p(scale)):
         raise ValueError("subln: bad length")
     return out, float(scale[0])
+
+
+def relu_squared_gate_f32(gate, up) -> np.ndarray:
+    gate = np.ascontiguousarray(gate, np.float32)
+    up = np.ascontiguousarray(up, np.float32)
+    if gate.size == 0 or up.size != gate.size:
+        raise ValueError("relu_squared: dimension mismatch")
+    out = np.zeros(gate.size, np.float32)
+    assert lib().or_relu_squared_gate_f32(_p(out), _p(gate), _p(up), gate.size) == 0
+    return out
+
+
+def bitnet_ffn(x, norm1, norm2, eps, gate_q, w_gate, up_q, w_up, down_q, w_down, hidden, inter):
+    """The BitNet FFN chain of tests/empirical_challenge_m3_bitnet.rs:582-686 (PATH A) for one
+    token: SubLN -> gate/up BitLinear -> ReLU^2 gating -> SubLN -> down BitLinear. Returns every
+    intermediate: act1, scale1, gate, up, relu, act2, scale2, out."""
+    act1, s1 = subln_quantize_absmax_i8(x, norm1, eps)
+    g = bitlinear_i8(gate_q, w_gate, inter, hidden, act1, s1)
+    u = bitlinear_i8(up_q, w_up, inter, hidden, act1, s1)
+    h = relu_squared_gate_f32(g, u)
+    act2, s2 = subln_quantize_absmax_i8(h, norm2, eps)
+    out = bitlinear_i8(down_q, w_down, hidden, inter, act2, s2)
+    return dict(act1=act1, scale1=s1, gate=g, up=u, relu=h, act2=act2, scale2=s2, out=out)
 
 
 def bitlinear_i8(quant, w, rows, cols, act, act_scale) -> np.ndarray:

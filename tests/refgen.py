@@ -200,3 +200,23 @@ def fill_pseudo_quant_tensor(quant, rows, cols):
         k = np.arange(128)[None, :]
         out[:, 16:] = ((b * 7 + k * 11 + 3) & 0xFF).astype(np.uint8)
     return out.reshape(-1)
+
+
+def bitnet_chain_weights(hidden: int, inter: int):
+    """The synthetic FFN weights of tests/empirical_challenge_m3_bitnet.rs:602-622: gate and up
+    are TQ2_0 [inter, hidden] of bytes 0xAA with every block's f16 scale (bytes 0..2) 1.0, down
+    is TQ1_0 [hidden, inter] of bytes 0x55 with scale 1.0. Returns (gate_up_bytes, down_bytes)."""
+    gate = np.full(inter * hidden // 256 * 66, 0xAA, np.uint8).reshape(-1, 66)
+    gate[:, 0:2] = np.frombuffer(np.uint16(0x3C00).tobytes(), np.uint8)
+    down = np.full(hidden * inter // 256 * 54, 0x55, np.uint8).reshape(-1, 54)
+    down[:, 0:2] = np.frombuffer(np.uint16(0x3C00).tobytes(), np.uint8)
+    return gate.reshape(-1), down.reshape(-1)
+
+
+def bitnet_chain_scenarios(hidden: int):
+    """The three inputs of tests/empirical_challenge_m3_bitnet.rs:588-596: sin(0.05 i) * 2 (f32
+    arithmetic; numpy's float32 sin stands in for Rust's), all zeros, all 1e5."""
+    i = np.arange(hidden, dtype=np.float32)
+    return [("normal_random", (np.sin(i * np.float32(0.05)) * np.float32(2.0)).astype(np.float32)),
+            ("all_zeros", np.zeros(hidden, np.float32)),
+            ("extreme_large", np.full(hidden, 1e5, np.float32))]

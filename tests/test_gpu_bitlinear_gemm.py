@@ -49,10 +49,16 @@ def test_bitlinear_i8_vs_oracle(jkb, oracle, quant, rows, cols):
         assert np.array_equal(bits(host(o2)), bits(y))
 
 
-def test_bitlinear_batch_matches_single_calls(jkb, oracle):
-    rows, cols, m = 640, 2560, 16
-    wb = ternary_weights(oracle, 35, rows, cols, 3)
-    w = upload(jkb, 35, wb, rows, cols)
+@pytest.mark.parametrize("quant,m", [(35, 16), (34, 11), (36, 9), (8, 3)])
+def test_bitlinear_batch_matches_single_calls(jkb, oracle, quant, m):
+    """Token batches (up to eight tokens per CTA share each weight load, each with its own
+    scale) equal the single-token calls bit for bit."""
+    rows, cols = 640, 2560
+    if quant == 8:
+        wb = oracle.quantize_weights(8, oracle.normal(rows * cols, 3, 0.02), rows, cols)
+    else:
+        wb = ternary_weights(oracle, quant, rows, cols, 3)
+    w = upload(jkb, quant, wb, rows, cols)
     acts, scales = [], []
     for t in range(m):
         a, s = bitnet_act(oracle, cols, 100 + t)
@@ -63,7 +69,7 @@ def test_bitlinear_batch_matches_single_calls(jkb, oracle):
     out = torch.empty(m * rows, dtype=torch.float32, device="cuda")
     jkb.bitlinear_i8_batch(out, w, dev(A), dev(S))
     ob = host(out).reshape(m, rows)
-    ref = oracle.bitlinear_i8_batch(35, wb, rows, cols, A, S, nthreads=4)
+    ref = oracle.bitlinear_i8_batch(quant, wb, rows, cols, A, S, nthreads=4)
     for t in range(m):
         one = torch.empty(rows, dtype=torch.float32, device="cuda")
         jkb.bitlinear_i8(one, w, dev(acts[t]), scales[t])

@@ -270,6 +270,52 @@ def test_bitlinear_tq1_tq2_same_trits_bit_identical(oracle):
         oracle.bitlinear_i8(12, np.zeros(144, np.uint8), 1, 256, np.zeros(256, np.int8), 1.0)
 
 
+def test_relu_squared_gate_oracle(oracle):
+    """lib.rs:1130-1137: (relu * relu) * up with relu = g > 0 ? g : 0, each product rounded to
+    f32; NaN and -0 gates give +0, so the product's sign is the sign of up."""
+    rng = np.random.default_rng(3)
+    g = rng.normal(0, 3, 4099).astype(np.float32)
+    u = rng.normal(0, 3, 4099).astype(np.float32)
+    g[:6] = [np.nan, -0.0, 0.0, np.inf, -np.inf, 1e20]
+    u[:6] = [-1.0, -2.0, 3.0, 2.0, 5.0, 1.0]
+    got = oracle.relu_squared_gate_f32(g, u)
+    r = np.where(g > 0, g, np.float32(0)).astype(np.float32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        want = ((r * r).astype(np.float32) * u).astype(np.float32)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert got[0] == 0 and np.signbit(got[0]) and np.signbit(got[1])
+    assert got[3] == np.inf and got[4] == 0 and got[5] == np.inf
+    with pytest.raises(ValueError, match="dimension mismatch"):
+        oracle.relu_squared_gate_f32(g, u[:-1])
+
+
+def test_bitnet_chain_reference_scenarios(oracle):
+    """tests/empirical_challenge_m3_bitnet.rs:582-686 on the oracle: the reference's synthetic
+    weights (gate = up = all +1 at scale 1; down TQ1_0 bytes 0x55) and its three inputs. The
+    reference asserts finite outputs; the weights also fix the values in closed form: every
+    gate / up output is sum(act1) * scale1, every intermediate element equals the same h, act2
+    is +-127 (or 0), and each down row is two TQ1_0 blocks with 102 trits of -1 each."""
+    hidden, inter, eps = 256, 512, 1e-5
+    wg, wd = R.bitnet_chain_weights(hidden, inter)
+    n1, n2 = np.ones(hidden, np.float32), np.ones(inter, np.float32)
+    deq = oracle.dequantize_rows(34, wd, hidden, inter)
+    assert np.all(deq.reshape(hidden, 2, 256).astype(np.int32).sum(axis=2) == -102)
+    for name, x in R.bitnet_chain_scenarios(hidden):
+        r = oracle.bitnet_ffn(x, n1, n2, eps, 35, wg, 35, wg, 34, wd, hidden, inter)
+        assert np.all(np.isfinite(r["out"])), name
+        g0 = np.float32(np.float32(r["act1"].astype(np.int32).sum()) * np.float32(r["scale1"]))
+        assert np.all(r["gate"] == g0) and np.array_equal(r["gate"], r["up"]), name
+        assert np.all(r["relu"] == np.float32(np.float32(max(g0, 0) * max(g0, 0)) * g0)), name
+        if name == "all_zeros":
+            assert not r["act1"].any() and r["scale1"] == np.float32(1) / np.float32(127)
+        if r["relu"][0] > 0:
+            assert np.all(r["act2"] == 127)
+            v = np.float32(-102 * 127) * np.float32(r["scale2"])
+            assert np.all(r["out"] == np.float32(np.float32(0) + v) + v), name
+        else:
+            assert not r["act2"].any() and not r["out"].any(), name
+
+
 @pytest.mark.parametrize("quant", [2, 8, 12, 14, 35, 36])
 def test_repack_lossless_and_gemm_rows_stitch(oracle, quant):
     """tests/test_repack_gemv_gemm.rs:619-700 (repacked values reproduce the dequantizer) and
