@@ -568,11 +568,13 @@ def run_bitnet(world, rank, launches=20):
     the max over ranks of a CUDA-event-timed CUDA graph of `launches` back-to-back calls.
       batch 1:   bitlinear_i8 per shape, weight copies rotating so that each launch reads from
                  HBM (GB/s of weight blocks + i8 activation + f32 output);
-      batch 128: bitlinear_i8_batch (each token one bitlinear_i8 call; up to eight tokens share
-                 every weight load) and the repacked tensor-core GEMM on the same weights with
-                 Q8_0-quantized activations (RepackedWeight.gemm), in TOPS (2*M*N*K);
+      batch 128: bitlinear_i8_batch (the GEMV kernel: each token one bitlinear_i8 call, up to
+                 eight tokens sharing every weight load) and bitlinear_i8_gemm (tcgen05, one
+                 TMEM accumulator per BitLinear block; default and bit-exact epilogue), in TOPS
+                 (2*M*N*K);
       FFN:       the whole chain SubLN -> gate/up -> ReLU^2 + SubLN -> down (jkb_bitnet_ffn) at
-                 1 and 128 tokens, in microseconds per call (unsharded, on every rank)."""
+                 1 token (GEMV kernels) and 128 tokens (tensor-core projections), in
+                 microseconds per call (unsharded, on every rank)."""
     import torch
     import torch.distributed as dist
     import jkb200 as jkb
@@ -629,10 +631,13 @@ def run_bitnet(world, rank, launches=20):
                                                    1)
             rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", quant, [per, cols], raws[0]),
                                                 per, cols)
-            act = jkb.QuantizedActQ8.quantize(xm, M, cols)
-            usg = maxr(_graph_time(lambda: rw.gemm(ob, act), launches))
-            row["batch128_gemm_us"] = round(usg, 2)
-            row["batch128_gemm_tops"] = round(2.0 * M * rows * cols / (usg * 1e-6) / 1e12, 1)
+            act = jkb.QuantizedActQ8(M, cols)
+            for exact, key in ((False, "batch128_tc"), (True, "batch128_tc_exact")):
+                with jkb.gemm_exact(exact):
+                    usg = maxr(_graph_time(
+                        lambda: jkb.bitlinear_i8_gemm(ob, rw, qm, sm, M, act), launches))
+                row[key + "_us"] = round(usg, 2)
+                row[key + "_tops"] = round(2.0 * M * rows * cols / (usg * 1e-6) / 1e12, 1)
             res["shapes"].append(row)
             rw.destroy()
             act.destroy()
@@ -642,14 +647,19 @@ def run_bitnet(world, rank, launches=20):
         wg = jkb.Weight(jkb.TensorView("gate", quant, [F, H], synth_ternary(quant, F, H, 91)), F, H)
         wu = jkb.Weight(jkb.TensorView("up", quant, [F, H], synth_ternary(quant, F, H, 92)), F, H)
         wd = jkb.Weight(jkb.TensorView("down", quant, [H, F], synth_ternary(quant, H, F, 93)), H, F)
+        raws = {"gate": (F, H, 91), "up": (F, H, 92), "down": (H, F, 93)}
+        rep = tuple(jkb.RepackedWeight.from_tensor(
+            jkb.TensorView(n, quant, [r, c], synth_ternary(quant, r, c, sd)), r, c)
+            for n, (r, c, sd) in raws.items())
         for m in (1, M):
-            ffn = jkb.BitNetFFN(wg, wu, wd, norm[H], norm[F], 1e-5, m)
+            ffn = jkb.BitNetFFN(wg, wu, wd, norm[H], norm[F], 1e-5, m,
+                                repacked=rep if m >= 32 else None)
             x = torch.randn(m * H, generator=torch.Generator().manual_seed(8)).cuda()
             out = torch.empty(m * H, dtype=torch.float32, device="cuda")
             us = maxr(_graph_time(lambda: ffn.forward(out, x, m), launches))
             res[f"ffn_{qname}_m{m}_us"] = round(us, 2)
             ffn.destroy()
-        for w in (wg, wu, wd):
+        for w in (wg, wu, wd) + rep:
             w.destroy()
     torch.cuda.empty_cache()
     return res

@@ -345,15 +345,19 @@ int jkb_bitlinear_i8_batch(float *out, size_t out_len, const jkb_weight *w, cons
  *   act2, s2 = subln_quantize_absmax_i8(h, norm2, eps)
  *   out = bitlinear_i8(w_down, act2, s2)
  * w_gate / w_up are [intermediate, hidden], w_down [hidden, intermediate] (TQ1_0, TQ2_0, Q8_0 or
- * I2_S, each validated as its bitlinear_i8 call). The handle borrows the weights and the device
- * norm weights (norm1 [hidden], norm2 [intermediate]) and owns the intermediates for up to
- * m_capacity tokens, allocated here; forward allocates nothing. x and out are [m][hidden] on the
- * device; the four kernels run on `stream`. */
+ * I2_S, each validated as its bitlinear_i8 call). r_gate / r_up / r_down are NULL or
+ * RepackedWeights of the same three tensors: then batches of at least 32 tokens run the
+ * projections as jkb_bitlinear_i8_gemm (tensor cores), the others as jkb_bitlinear_i8 /
+ * _batch. The handle borrows the weights and the device norm weights (norm1 [hidden], norm2
+ * [intermediate]) and owns the intermediates for up to m_capacity tokens, allocated here;
+ * forward allocates nothing. x and out are [m][hidden] on the device; the kernels run on
+ * `stream`. */
 typedef struct jkb_bitnet_ffn jkb_bitnet_ffn;
 int jkb_bitnet_ffn_create(const jkb_weight *w_gate, const jkb_weight *w_up,
-                          const jkb_weight *w_down, const float *norm1, size_t norm1_len,
-                          const float *norm2, size_t norm2_len, float eps, size_t m_capacity,
-                          jkb_bitnet_ffn **out);
+                          const jkb_weight *w_down, const jkb_repacked_weight *r_gate,
+                          const jkb_repacked_weight *r_up, const jkb_repacked_weight *r_down,
+                          const float *norm1, size_t norm1_len, const float *norm2,
+                          size_t norm2_len, float eps, size_t m_capacity, jkb_bitnet_ffn **out);
 int jkb_bitnet_ffn_forward(jkb_bitnet_ffn *ffn, float *out, size_t out_len, const float *x,
                            size_t x_len, size_t m, void *stream);
 /* Device views of the last forward's intermediates ([m_capacity] rows each; NULL to skip):
@@ -396,6 +400,18 @@ int jkb_gemv_repacked_rows(float *out, size_t out_len, const jkb_repacked_weight
 int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight *w,
                           const float *input, size_t in_len, size_t m, jkb_act_q8 *scratch,
                           void *stream);
+/* bitlinear_i8 (ime.rs:882-938) for m tokens on the tensor cores: a RepackedWeight of TQ1_0,
+ * TQ2_0, I2_S or Q8_0 (repacked from the same bytes as the jkb_weight of jkb_bitlinear_i8),
+ * act [m][cols] i8 and act_scales [m] f32 (device), out [m][rows]. scratch (capacity >= m, k
+ * == cols) receives the activations in the GEMM's layout. From 32 tokens each BitLinear block
+ * (256 elements for TQ1_0 / TQ2_0, 128 for I2_S, 32 for Q8_0) is one tensor-core accumulator
+ * and its value (f32)c * (d * s) is added in K order: with jkb_gemm_set_exact(1) every output
+ * equals the reference's row sum bit for bit, by default within its 1e-5 relative tolerance
+ * (one rounding fewer per block). Smaller batches run the repacked GEMM's 32-element groups
+ * (within the tolerance). */
+int jkb_bitlinear_i8_gemm(float *out, size_t out_len, const jkb_repacked_weight *w,
+                          const int8_t *act_i8, size_t act_len, const float *act_scales,
+                          size_t m, jkb_act_q8 *scratch, void *stream);
 /* No counterpart in the reference. The same computation as jkb_gemm_repacked_f32 for callers
  * that cannot allocate device memory, and so cannot create the jkb_act_q8 scratch handle. Two
  * examples: an engine that reserved all remaining HBM for its KV cache at start-up, and a host

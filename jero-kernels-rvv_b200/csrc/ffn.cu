@@ -6,13 +6,15 @@
 //   out = bitlinear_i8(W_down, act2, s2)
 // as the reference composes it (tests/empirical_challenge_m3_bitnet.rs:582-686), for m tokens.
 //
-// Four or five kernels in one stream, each launched with programmatic stream serialization so
-// that the next one's weight prefetch overlaps the previous one's tail: the SubLN quantizer;
-// the gate and up projections (one grouped BitLinear launch for a single token, sharing one
-// activation staging per CTA; for token batches one launch per matrix, each CTA dotting every
-// weight block it loads with up to eight staged tokens); ReLU^2 gating fused with the second
-// SubLN quantizer (h leaves the CTA only as the copy kept for inspection); the down
-// projection. Every step is the single-call kernel
+// The kernels run in one stream, each launched with programmatic stream serialization so that
+// the next one's weight prefetch overlaps the previous one's tail: the SubLN quantizer; the
+// gate and up projections; ReLU^2 gating fused with the second SubLN quantizer (h leaves the
+// CTA only as the copy kept for inspection); the down projection. The projections take the
+// GEMV kernel (a single token: gate and up in one grouped launch sharing one activation
+// staging per CTA; small batches: one launch per matrix, each CTA dotting every weight block
+// it loads with up to eight staged tokens) or, for batches of at least 32 tokens when the
+// handle holds RepackedWeights of the three matrices, the tensor-core BitLinear GEMM (one
+// TMEM accumulator per BitLinear block). Every step is the single-call kernel
 // of the corresponding reference function, so each intermediate equals what those calls
 // produce.
 #include "jkb_internal.h"
@@ -23,6 +25,10 @@
 struct jkb_bitnet_ffn {
     uint32_t magic;
     const jkb_weight *gate, *up, *down;
+    // optional RepackedWeights of the same tensors: batches of at least TC_BATCH tokens run the
+    // three projections on the tensor cores (jkb_bitlinear_i8_gemm)
+    const jkb_repacked_weight *rgate, *rup, *rdown;
+    jkb_act_q8 *act_h, *act_i;  // their activation scratch (k = hidden, k = intermediate)
     const float *norm1, *norm2;
     float eps;
     size_t hidden, inter, m_cap;
@@ -45,6 +51,19 @@ constexpr uint32_t FFN_MAGIC = 0x4A4B4631u;  // "JKF1"
 static bool check_ffn(const jkb_bitnet_ffn *f) { return f && f->magic == FFN_MAGIC; }
 
 static size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Smallest batch that takes the tensor-core projections (the GEMM's smallest token tile).
+constexpr size_t TC_BATCH = 32;
+
+static int check_repacked_pair(const jkb_repacked_weight *r, const jkb_weight *w) {
+    if (!r || r->magic != REPACKED_MAGIC)
+        return fail(JKB_E_INVALID, "bitnet_ffn", 0, 0, 0, "null or destroyed repacked weight");
+    if (r->quant != w->quant || r->rows != w->rows || r->cols != w->cols)
+        return fail(JKB_E_BOUNDS, r->name, 0, r->rows, w->rows,
+                    "repacked weight %s [%zu, %zu] does not match %s [%zu, %zu]", r->name,
+                    r->rows, r->cols, w->name, w->rows, w->cols);
+    return JKB_OK;
+}
 
 // The three BitLinear steps of m tokens (the activations and their scales on the device).
 static int ffn_projections_up(const jkb_bitnet_ffn *f, size_t m, cudaStream_t st) {
@@ -82,9 +101,10 @@ using namespace jkb;
 extern "C" {
 
 int jkb_bitnet_ffn_create(const jkb_weight *w_gate, const jkb_weight *w_up,
-                          const jkb_weight *w_down, const float *norm1, size_t norm1_len,
-                          const float *norm2, size_t norm2_len, float eps, size_t m_capacity,
-                          jkb_bitnet_ffn **out) {
+                          const jkb_weight *w_down, const jkb_repacked_weight *r_gate,
+                          const jkb_repacked_weight *r_up, const jkb_repacked_weight *r_down,
+                          const float *norm1, size_t norm1_len, const float *norm2,
+                          size_t norm2_len, float eps, size_t m_capacity, jkb_bitnet_ffn **out) {
     static const char *fn = "bitnet_ffn";
     if (!out) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null out");
     *out = nullptr;
@@ -106,6 +126,11 @@ int jkb_bitnet_ffn_create(const jkb_weight *w_gate, const jkb_weight *w_up,
         (rc = check_align(norm2, 4, "subln", "norm_weight")))
         return rc;
     if (m_capacity == 0) return fail(JKB_E_BOUNDS, fn, 0, 0, 0, "m_capacity must be positive");
+    const bool tc = r_gate || r_up || r_down;
+    if (tc && ((rc = check_repacked_pair(r_gate, w_gate)) ||
+               (rc = check_repacked_pair(r_up, w_up)) ||
+               (rc = check_repacked_pair(r_down, w_down))))
+        return rc;
     if (inter > SUBLN_MAX_LEN || hidden > SUBLN_MAX_LEN)
         return fail(JKB_E_BOUNDS, "subln", 0, inter > hidden ? inter : hidden, SUBLN_MAX_LEN,
                     "row length exceeds the %zu-element limit of the GPU kernel", SUBLN_MAX_LEN);
@@ -143,6 +168,18 @@ int jkb_bitnet_ffn_create(const jkb_weight *w_gate, const jkb_weight *w_up,
     f->relu = (float *)(f->base + off[4]);
     f->act2 = (int8_t *)(f->base + off[5]);
     f->scale2 = (float *)(f->base + off[6]);
+    if (tc && m_capacity >= TC_BATCH) {
+        f->rgate = r_gate;
+        f->rup = r_up;
+        f->rdown = r_down;
+        if ((rc = jkb_act_q8_create(m_capacity, hidden, &f->act_h)) ||
+            (rc = jkb_act_q8_create(m_capacity, inter, &f->act_i))) {
+            if (f->act_h) jkb_act_q8_destroy(f->act_h);
+            cudaFree(f->base);
+            free(f);
+            return rc;
+        }
+    }
     f->magic = FFN_MAGIC;
     *out = f;
     return JKB_OK;
@@ -170,10 +207,22 @@ int jkb_bitnet_ffn_forward(jkb_bitnet_ffn *f, float *out, size_t out_len, const 
     if ((rc = launch_subln(false, f->act1, nullptr, x, nullptr, f->norm1, m, f->hidden, f->eps,
                            f->scale1, st)))
         return rc;
-    if ((rc = ffn_projections_up(f, m, st))) return rc;
+    const bool tc = f->rgate && m >= TC_BATCH;
+    if (tc) {
+        if ((rc = jkb_bitlinear_i8_gemm(f->gate_out, m * f->inter, f->rgate, f->act1,
+                                        m * f->hidden, f->scale1, m, f->act_h, stream)) ||
+            (rc = jkb_bitlinear_i8_gemm(f->up_out, m * f->inter, f->rup, f->act1, m * f->hidden,
+                                        f->scale1, m, f->act_h, stream)))
+            return rc;
+    } else if ((rc = ffn_projections_up(f, m, st))) {
+        return rc;
+    }
     if ((rc = launch_subln(true, f->act2, f->relu, f->gate_out, f->up_out, f->norm2, m, f->inter,
                            f->eps, f->scale2, st)))
         return rc;
+    if (tc)
+        return jkb_bitlinear_i8_gemm(out, out_len, f->rdown, f->act2, m * f->inter, f->scale2, m,
+                                     f->act_i, stream);
     GemvLaunch L{};
     L.w = f->down;
     L.x = f->act2;
@@ -208,6 +257,8 @@ int jkb_bitnet_ffn_destroy(jkb_bitnet_ffn *f) {
     if (!check_ffn(f))
         return fail(JKB_E_INVALID, "bitnet_ffn", 0, 0, 0, "invalid bitnet_ffn handle");
     f->magic = 0;
+    if (f->act_h) jkb_act_q8_destroy(f->act_h);
+    if (f->act_i) jkb_act_q8_destroy(f->act_i);
     cudaFree(f->base);
     free(f);
     return JKB_OK;

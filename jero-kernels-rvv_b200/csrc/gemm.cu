@@ -269,6 +269,42 @@ int jkb_gemv_repacked_rows(float *out, size_t out_len, const jkb_repacked_weight
                      as_stream(stream));
 }
 
+int jkb_bitlinear_i8_gemm(float *out, size_t out_len, const jkb_repacked_weight *w,
+                          const int8_t *act_i8, size_t act_len, const float *act_scales,
+                          size_t m, jkb_act_q8 *scratch, void *stream) {
+    static const char *fn = "bitlinear_i8_gemm";
+    if (!w || w->magic != REPACKED_MAGIC)
+        return fail(JKB_E_INVALID, fn, 0, 0, 0, "null or destroyed repacked weight");
+    if (w->quant != JKB_TQ1_0 && w->quant != JKB_TQ2_0 && w->quant != JKB_Q8_0 &&
+        w->quant != JKB_I2_S)
+        return fail(JKB_E_BOUNDS, w->name, 0, w->device_bytes, w->device_bytes,
+                    "unsupported quantization format for BitLinear: %s; expected TQ1_0, TQ2_0, "
+                    "Q8_0, or I2_S",
+                    quant_name(w->quant));
+    if (!scratch || scratch->magic != ACT_MAGIC)
+        return fail(JKB_E_INVALID, fn, 0, 0, 0, "null or destroyed activation handle");
+    if (scratch->k != w->cols || scratch->k_pad != w->cols)
+        return fail(JKB_E_BOUNDS, fn, 0, scratch->k, w->cols,
+                    "activation handle k %zu != weight cols %zu", scratch->k, w->cols);
+    if (m == 0 || m > scratch->m_cap || act_len != m * w->cols || out_len != m * w->rows)
+        return fail(JKB_E_BOUNDS, w->name, 0, act_len, m * w->cols,
+                    "bitlinear batch: act len %zu / out len %zu do not match m=%zu x [%zu, %zu] "
+                    "(activation capacity %zu)",
+                    act_len, out_len, m, w->rows, w->cols, scratch->m_cap);
+    if (!out || !act_i8 || !act_scales) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
+    int rc;
+    if ((rc = check_align(out, 4, fn, "output")) ||
+        (rc = check_align(act_scales, 4, fn, "act_scales")))
+        return rc;
+    cudaStream_t st = as_stream(stream);
+    if ((rc = act_q8_from_i8(scratch, act_i8, act_scales, m, st))) return rc;
+    bool used = false;
+    rc = gemm_tc_bitlinear_launch(w, scratch, out, st, &used);
+    if (rc || used) return rc;
+    // small batches: the repacked GEMM over 32-element groups (within the 1e-5 contract)
+    return gemm_rows(fn, out, out_len, w, scratch, 0, w->rows, false, st);
+}
+
 int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight *w,
                           const float *input, size_t in_len, size_t m, jkb_act_q8 *scratch,
                           void *stream) {

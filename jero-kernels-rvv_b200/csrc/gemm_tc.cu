@@ -61,7 +61,7 @@ constexpr int GPS = 4;    // scale groups per stage
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
 template <int BN_, int WPQ_, int GPR_, bool EXACT_, bool MINS_ = false, bool H16_ = false,
-          int NIB_ = NIB_NONE>
+          int NIB_ = NIB_NONE, int AB_ = 1>
 struct TcCfg {
     static constexpr int BN = BN_, WPQ = WPQ_, GPR = GPR_;
     static constexpr bool EXACT = EXACT_;
@@ -87,6 +87,15 @@ struct TcCfg {
     // adds a constant -8 tile times the same activations into the same accumulator: the exact
     // integer sum of (code - 8) * x without per-element offsets in the conversion.
     static constexpr bool NEG8 = NIB == NIB_Q4_0;
+    // AB: K steps (32 elements each) summed into one accumulator before the epilogue scales
+    // it. 1: the 32-element scale groups. 4 / 8: BitLinear over the blocks of I2_S (128
+    // elements) and TQ1_0 / TQ2_0 (256), whose value is (f32)c_block * (d * s) with the block's
+    // weight scale d and the token's activation scale s (ime.rs:918-929); the accumulator of a
+    // block spans AB / 4 stages and every 32-element group of the block carries the same d and
+    // s, so the epilogue reads group 0's.
+    static constexpr int AB = AB_;
+    static_assert(AB == 1 || ((AB == 4 || AB == 8) && GPR == 1 && !H16 && !MINS && !NIB),
+                  "BitLinear blocks: one accumulator per round, plain int8 weights");
     static constexpr int SPL = H16 ? 2 : 1;    // accumulators per 32-element slice
     static constexpr int NA = GPR * SPL;       // accumulators per round
     static constexpr int NG = GPS * SPL;       // weight-scale groups per stage
@@ -496,6 +505,31 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     const uint64_t ad = smem_desc(sm.a[s]), bd = smem_desc(sm.b[s]);
                     const uint64_t bdl = smem_desc(sm.blo[C::H16 ? s : 0]),
                                    bdh = smem_desc(sm.bhi[C::H16 ? s : 0]);
+                    if constexpr (C::AB > 1) {
+                        // BitLinear block: its AB K steps into one accumulator (the first one
+                        // overwrites), one commit to the epilogue after the block's last stage
+                        const int gs = ks * GPS;
+                        const bool bfirst = gs % C::AB == 0, blast = (gs + GPS) % C::AB == 0;
+                        const int rb = rc & 1;
+                        if (bfirst) {
+                            if (!mbar_wait(&sm.tempty[rb], ((rc >> 1) & 1) ^ 1, abort_flag, err)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                        }
+                        const uint32_t d = tmem + rb * BN;
+                        for (int g = 0; g < GPS; g++) {
+                            if (bfirst && g == 0)
+                                mma_i8(d, ad + (uint64_t)(2 * g), bd + (uint64_t)(2 * g), IDESC);
+                            else
+                                mma_i8_acc(d, ad + (uint64_t)(2 * g), bd + (uint64_t)(2 * g), IDESC);
+                        }
+                        if (blast) {
+                            tc_commit(&sm.tfull[rb]);
+                            rc++;
+                        }
+                    } else
                     for (int r = 0; r < GPS / GPR; r++, rc++) {
                         const int rb = rc & 1;
                         if (!mbar_wait(&sm.tempty[rb], ((rc >> 1) & 1) ^ 1, abort_flag, err)) {
@@ -616,8 +650,11 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                 }
                 const float *xbase = &sm.xs[s][0][slice * COLS + 4 * kq];
                 const float *nbase = &sm.xn[C::MINS ? s : 0][0][slice * COLS + 4 * kq];
+                // BitLinear blocks: one round after the block's last stage, none before
+                const bool blast = C::AB == 1 || (ks * GPS + GPS) % C::AB == 0;
 #pragma unroll
-                for (int rr = 0; rr < GPS / GPR; rr++, rc++) {
+                for (int rr = 0; rr < (C::AB > 1 ? 1 : GPS / GPR); rr++, rc++) {
+                    if (!blast) break;  // (break skips the round counter's increment)
                     const int rb = rc & 1;
                     if (!mbar_wait(&sm.tfull[rb], (rc >> 1) & 1, abort_flag, err)) {
                         ok = false;
@@ -672,7 +709,8 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                                 const uint64_t np = r == 0 ? nv0.x : r == 1 ? nv0.y : r == 2 ? nv1.x : nv1.y;
 #pragma unroll
                                 for (int i = 0; i < 2; i++) {
-                                    // exact: |c| <= 32 * 127 * 127 < 2^24
+                                    // exact: |c| <= 32 * 127 * 127 (BitLinear blocks:
+                                    // 256 * 2 * 128) < 2^24
                                     const uint64_t cf = pk2(
                                         __float_as_uint(__int2float_rn((int)c[j][4 * r + 2 * i])),
                                         __float_as_uint(__int2float_rn((int)c[j][4 * r + 2 * i + 1])));
@@ -953,6 +991,54 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
                  : launch_tc_bn<false, false, false>(bn, w, act, out, row_begin, row_end, st, err);
 }
 
+
+// BitLinear configurations: one accumulator per block (GPR = 1), AB K steps per block.
+template <bool E, int AB> using TB64 = TcCfg<64, 2, 1, E, false, false, NIB_NONE, AB>;
+template <bool E, int AB> using TB96 = TcCfg<96, 3, 1, E, false, false, NIB_NONE, AB>;
+template <bool E, int AB> using TB128 = TcCfg<128, 2, 1, E, false, false, NIB_NONE, AB>;
+
+template <bool EXACT, int AB>
+int launch_bl_bn(int bn, const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out,
+                 cudaStream_t st, int *err) {
+    switch (bn) {
+        case 64: return launch_tc<TB64<EXACT, AB>>(w, act, out, 0, w->rows, st, err);
+        case 128: return launch_tc<TB128<EXACT, AB>>(w, act, out, 0, w->rows, st, err);
+        default: return launch_tc<TB96<EXACT, AB>>(w, act, out, 0, w->rows, st, err);
+    }
+}
+
+// Tensor-core BitLinear over a token batch (bitlinear_i8 per token, ime.rs:882-938): a
+// repacked TQ1_0 / TQ2_0 / I2_S / Q8_0 weight and i8 activations whose every 32-element group
+// carries its token's scale (act_q8_from_i8). A TQ block's 8 K steps (I2_S: 4) sum into one
+// accumulator and the epilogue adds (f32)c_block * (d * s) per block in K order, so with the
+// exact epilogue each output is the reference's row sum bit for bit; Q8_0's 32-element blocks
+// are the plain GEMM's groups. Conditions as gemm_tc_launch; *used reports whether it ran.
+int gemm_tc_bitlinear_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out,
+                             cudaStream_t st, bool *used) {
+    const int ab = (w->quant == JKB_TQ1_0 || w->quant == JKB_TQ2_0) ? 8
+                   : w->quant == JKB_I2_S                          ? 4
+                                                                   : 1;
+    if (ab == 1) return gemm_tc_launch(w, act, out, 0, w->rows, st, used);
+    *used = false;
+    const size_t kp = w->k_pad;
+    if (w->group_elems != 32 || w->mins || kp % (32 * (size_t)ab) != 0 || kp % BK != 0 ||
+        act->m < TC_MIN_M || act->k_pad != kp || act->m > (size_t)INT32_MAX ||
+        w->rows > (size_t)INT32_MAX || act->x_scales_t == nullptr)
+        return JKB_OK;
+    if ((((uintptr_t)w->q) & 15) || (((uintptr_t)act->q) & 15) || (((uintptr_t)w->scales) & 15) ||
+        (((uintptr_t)act->x_scales_t) & 15) || (act->xt_pitch & 31))
+        return JKB_OK;
+    int *err = device_error_word();
+    if (!err) return JKB_OK;
+    *used = true;
+    const int bn = choose_tile(act->m, w->rows, false);
+    const bool exact = g_gemm_exact.load(std::memory_order_relaxed);
+    if (ab == 8)
+        return exact ? launch_bl_bn<true, 8>(bn, w, act, out, st, err)
+                     : launch_bl_bn<false, 8>(bn, w, act, out, st, err);
+    return exact ? launch_bl_bn<true, 4>(bn, w, act, out, st, err)
+                 : launch_bl_bn<false, 4>(bn, w, act, out, st, err);
+}
 
 template <bool EXACT, int NB>
 int launch_nib_bn(int bn, const jkb_nibble_matrix *w, const jkb_act_q8 *act, float *out,

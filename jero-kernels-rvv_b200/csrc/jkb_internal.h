@@ -213,6 +213,13 @@ struct GemvLaunch {
 };
 int launch_gemv(const GemvLaunch &L, cudaStream_t st);
 
+// Fills a jkb_act_q8 from i8 BitLinear activations with per-token scales (quantize.cu).
+int act_q8_from_i8(jkb_act_q8 *a, const int8_t *act_i8, const float *scales, size_t m,
+                   cudaStream_t st);
+// Tensor-core BitLinear GEMM (gemm_tc.cu); *used = false when its conditions do not hold.
+int gemm_tc_bitlinear_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out,
+                             cudaStream_t st, bool *used);
+
 // validate_bitlinear_dimensions (ime.rs:660-763) on a handle (dots.cu).
 int validate_bitlinear(const jkb_weight *w, size_t output_len, size_t input_len);
 

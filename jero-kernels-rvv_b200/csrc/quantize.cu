@@ -194,6 +194,51 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ a
     xs16[r * (kp / 16) + 2 * b + 1] = h1;
 }
 
+// i8 BitLinear activations (per-token scale) in the jkb_act_q8 layout the tensor-core GEMM
+// reads: q the i8 rows (k == k_pad: BitLinear widths are multiples of the block), every
+// 32-element group's scale the token's (x_scales and its transposed, permuted copy, as
+// act_q8_kernel places it), sums zero. One thread per (token, 32-element group).
+__global__ void __launch_bounds__(256) act_from_i8_kernel(const int8_t *__restrict__ act,
+                                                          const float *__restrict__ scales,
+                                                          size_t m, size_t kp,
+                                                          int8_t *__restrict__ q,
+                                                          float *__restrict__ xs,
+                                                          float *__restrict__ xsum,
+                                                          float *__restrict__ xs_t,
+                                                          size_t xt_pitch) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+    const size_t kb = kp / 32;
+    const size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t m_t = xs_t ? (m + 31) / 32 * 32 : m;
+    if (gid >= m_t * kb) return;
+    const size_t r = gid / kb, b = gid % kb;
+    const size_t xt_at = b * xt_pitch + (r & ~(size_t)31) + 16 * ((r >> 4) & 1) +
+                         4 * ((r >> 1) & 3) + 2 * ((r >> 3) & 1) + (r & 1);
+    if (r >= m) {
+        xs_t[xt_at] = 0.0f;
+        return;
+    }
+    const float s = __ldg(scales + r);
+    const int8_t *src = act + r * kp + b * 32;
+    uint4 *dst = reinterpret_cast<uint4 *>(q + r * kp + b * 32);
+    if ((((uintptr_t)src) & 15) == 0) {
+        dst[0] = __ldg(reinterpret_cast<const uint4 *>(src));
+        dst[1] = __ldg(reinterpret_cast<const uint4 *>(src) + 1);
+    } else {
+        uint32_t w[8];
+        for (int i = 0; i < 8; i++)
+            w[i] = (uint32_t)(uint8_t)src[4 * i] | ((uint32_t)(uint8_t)src[4 * i + 1] << 8) |
+                   ((uint32_t)(uint8_t)src[4 * i + 2] << 16) |
+                   ((uint32_t)(uint8_t)src[4 * i + 3] << 24);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+    xs[r * kb + b] = s;
+    xsum[r * kb + b] = 0.0f;
+    if (xs_t) xs_t[xt_at] = s;
+}
+
 // super_scales_256 (repack.rs:623-630): slot starts at 0.0, `if sc > slot { slot = sc }` over
 // the 32-blocks of each 256 span.
 __global__ void act_super_kernel(const float *__restrict__ xs, size_t m, size_t kb, size_t nsb,
@@ -406,6 +451,21 @@ static int launch_q8_k(const float *x, size_t nblocks, void *out, cudaStream_t s
 }
 
 static bool check_act(const jkb_act_q8 *a) { return a && a->magic == ACT_MAGIC; }
+
+// Fills act from m rows of i8 BitLinear activations and their per-token scales (device);
+// act->k must be a multiple of 32 and m at most its capacity (checked by the caller).
+int act_q8_from_i8(jkb_act_q8 *a, const int8_t *act_i8, const float *scales, size_t m,
+                   cudaStream_t st) {
+    const size_t kb = a->k_pad / 32;
+    const size_t m_t = a->x_scales_t ? (m + 31) / 32 * 32 : m;
+    const size_t threads = m_t * kb;
+    cudaError_t e = launch_pdl(act_from_i8_kernel, dim3((unsigned)((threads + 255) / 256)),
+                               dim3(256), 0, st, act_i8, scales, m, a->k_pad, a->q,
+                               a->x_scales, a->x_sums, a->x_scales_t, a->xt_pitch);
+    if (e != cudaSuccess) return fail_cuda(e, "act_from_i8_kernel");
+    a->m = m;
+    return JKB_OK;
+}
 
 }  // namespace jkb
 

@@ -68,10 +68,11 @@ SIGNATURES = {
     "jkb_subln_quantize_absmax_i8_rows": [P, P, P, S, S, F, P, P],
     "jkb_relu_squared_gate_f32": [P, S, P, S, P, S, P],
     "jkb_relu_squared_subln_quantize_i8_rows": [P, P, P, P, P, S, S, F, P, P],
-    "jkb_bitnet_ffn_create": [P, P, P, P, S, P, S, F, S, PP],
+    "jkb_bitnet_ffn_create": [P, P, P, P, P, P, P, S, P, S, F, S, PP],
     "jkb_bitnet_ffn_forward": [P, P, S, P, S, S, P],
     "jkb_bitnet_ffn_buffers": [P, PP, PP, PP, PP, PP, PP, PP],
     "jkb_bitnet_ffn_destroy": [P],
+    "jkb_bitlinear_i8_gemm": [P, S, P, P, S, P, S, P, P],
     "jkb_act_q8_create": [S, S, PP],
     "jkb_act_q8_destroy": [P],
     "jkb_act_q8_quantize": [P, P, S, S, S, P],

@@ -35,7 +35,7 @@ __all__ = [
     "repack_nibble_into_tile_range", "vec_dot_q5_0_q8_0_blocks", "vec_dot_q5_k_q8_k",
     "gemv_q5_0_q8_0", "gemv_q5_0_q8_0_4x", "gemv_q5_k_q8_k", "vec_dot_q5_0", "vec_dot_q5_k",
     "vec_dot_q5_0_rvv", "vec_dot_q5_k_rvv", "relu_squared_gate_f32",
-    "relu_squared_subln_quantize_i8_rows", "BitNetFFN",
+    "relu_squared_subln_quantize_i8_rows", "BitNetFFN", "bitlinear_i8_gemm",
 ]
 
 
@@ -608,14 +608,17 @@ class BitNetFFN:
     bitlinear_i8. Borrows the weights and the norm weights; owns the intermediates."""
 
     def __init__(self, w_gate: "Weight", w_up: "Weight", w_down: "Weight", norm1: torch.Tensor,
-                 norm2: torch.Tensor, eps: float, m_capacity: int = 1):
+                 norm2: torch.Tensor, eps: float, m_capacity: int = 1, repacked=None):
+        """repacked: None or RepackedWeights (gate, up, down) of the same tensors, for the
+        tensor-core projections of batches of at least 32 tokens."""
         h = C.c_void_p()
-        _check(_L().jkb_bitnet_ffn_create(w_gate.handle, w_up.handle, w_down.handle,
+        rg, ru, rd = (r._h for r in repacked) if repacked else (None, None, None)
+        _check(_L().jkb_bitnet_ffn_create(w_gate.handle, w_up.handle, w_down.handle, rg, ru, rd,
                                           _dptr(norm1), norm1.numel(), _dptr(norm2),
                                           norm2.numel(), eps, m_capacity, C.byref(h)))
         self._h = h.value
         # keep the borrowed objects alive as long as the handle
-        self._refs = (w_gate, w_up, w_down, norm1, norm2)
+        self._refs = (w_gate, w_up, w_down, norm1, norm2, repacked)
         self.hidden, self.inter = w_gate.cols, w_gate.rows
         self.m_capacity = m_capacity
 
@@ -935,6 +938,14 @@ def bitlinear_i8(out, weights, act_i8, act_scale: float, stream=None):
 
 bitlinear_i8_rvv = bitlinear_i8
 bitlinear_i8_ime = bitlinear_i8
+
+
+def bitlinear_i8_gemm(out, repacked, act_i8, act_scales, m, scratch, stream=None):
+    """bitlinear_i8 for m tokens on the tensor cores (RepackedWeight of TQ1_0 / TQ2_0 / I2_S /
+    Q8_0; scratch a QuantizedActQ8 of capacity >= m and k == cols)."""
+    _check(_L().jkb_bitlinear_i8_gemm(_dptr(out), out.numel(), repacked._h, _dptr(act_i8),
+                                      act_i8.numel(), _dptr(act_scales), m, scratch._h,
+                                      _stream(stream)))
 
 
 def bitlinear_i8_batch(out, weights, act_i8, act_scales, stream=None):

@@ -177,3 +177,55 @@ def test_gemm_validation(jkb, oracle):
     b = jkb.QuantizedActQ8.quantize(dev(oracle.normal(512, 2)), 1, 512)
     with pytest.raises(jkb.TensorBoundsError):
         rw.gemm(torch.empty(rows, device="cuda"), b)
+
+
+@pytest.mark.parametrize("exact", [False, True])
+@pytest.mark.parametrize("rows,cols,m", [(640, 2560, 128), (2560, 6912, 40), (6912, 2560, 64),
+                                         (256, 1024, 8), (384, 512, 33)])
+@pytest.mark.parametrize("quant", [35, 34, 36, 8])
+def test_bitlinear_gemm_tensor_cores(jkb, oracle, quant, rows, cols, m, exact):
+    """jkb_bitlinear_i8_gemm against the reference's per-token bitlinear_i8 (ime.rs:882-938).
+    From 32 tokens every BitLinear block is one tensor-core accumulator and its value
+    (f32)c * (d * s) is added in K order: the exact epilogue gives the reference's row sums bit
+    for bit, the default one stays within the 1e-5 contract. Below 32 tokens the repacked
+    GEMM's 32-element groups run (within the contract)."""
+    wb = _weights(oracle, quant, rows, cols, rows + cols + m)
+    acts, scales = zip(*[bitnet_act(oracle, cols, 500 + t) for t in range(m)])
+    A = np.concatenate(acts)
+    S = np.array(scales, np.float32)
+    rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", quant, [rows, cols], wb), rows, cols)
+    scratch = jkb.QuantizedActQ8(m + 3, cols)
+    out = torch.empty(m * rows, dtype=torch.float32, device="cuda")
+    with jkb.gemm_exact(exact):
+        jkb.bitlinear_i8_gemm(out, rw, dev(A), dev(S), m, scratch)
+    y = host(out).reshape(m, rows)
+    ref = oracle.bitlinear_i8_batch(quant, wb, rows, cols, A, S, nthreads=8)
+    if exact and m >= 32:
+        assert np.array_equal(bits(y), bits(ref))
+    else:
+        deq = np.abs(oracle.dequantize_rows(quant, wb, rows, cols).astype(np.float64))
+        xa = np.abs(A.reshape(m, cols).astype(np.float64)) * S.astype(np.float64)[:, None]
+        bound = xa @ deq.T
+        assert np.all(np.abs(y.astype(np.float64) - ref) <= 1e-5 * bound + 1e-30)
+    rw.destroy()
+    scratch.destroy()
+
+
+def test_bitlinear_gemm_validation(jkb, oracle):
+    rows, cols, m = 128, 512, 32
+    wq = oracle.quantize_weights(12, oracle.normal(rows * cols, 1, 0.02), rows, cols)
+    rq = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", 12, [rows, cols], wq), rows, cols)
+    scratch = jkb.QuantizedActQ8(m, cols)
+    A = torch.zeros(m * cols, dtype=torch.int8, device="cuda")
+    S = torch.ones(m, device="cuda")
+    out = torch.empty(m * rows, device="cuda")
+    with pytest.raises(jkb.TensorBoundsError, match="unsupported quantization format"):
+        jkb.bitlinear_i8_gemm(out, rq, A, S, m, scratch)
+    wt = ternary_weights(oracle, 35, rows, cols, 2)
+    rt = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", 35, [rows, cols], wt), rows, cols)
+    with pytest.raises(jkb.TensorBoundsError, match="capacity"):
+        jkb.bitlinear_i8_gemm(torch.empty((m + 1) * rows, device="cuda"), rt,
+                              torch.zeros((m + 1) * cols, dtype=torch.int8, device="cuda"),
+                              torch.ones(m + 1, device="cuda"), m + 1, scratch)
+    with pytest.raises(jkb.TensorBoundsError, match="k 256 != weight cols 512"):
+        jkb.bitlinear_i8_gemm(out, rt, A, S, m, jkb.QuantizedActQ8(m, 256))

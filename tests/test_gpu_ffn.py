@@ -200,3 +200,54 @@ def test_chain_validation(jkb, oracle):
     q4 = upload(jkb, 2, np.zeros(inter * hidden // 32 * 18, np.uint8), inter, hidden)
     with pytest.raises(jkb.TensorBoundsError, match="unsupported quantization format"):
         jkb.BitNetFFN(q4, Wu, Wd, n1, n2, EPS)
+
+
+@pytest.mark.parametrize("quant,dq", [(35, 35), (36, 36), (35, 34)])
+def test_chain_tensor_core_batch(jkb, oracle, quant, dq):
+    """Batches of at least 32 tokens with RepackedWeights: the three projections on the tensor
+    cores (one accumulator per BitLinear block). With the exact epilogue every projection output
+    is the reference's bitlinear_i8 of the GPU's own activations bit for bit; by default the
+    chain stays within tolerance of the GEMV chain."""
+    hidden, inter, m = 2560, 6912, 48
+    wg = _ternary(oracle, quant, inter, hidden, 41, 0.0173)
+    wu = _ternary(oracle, quant, inter, hidden, 42, 0.0173)
+    wd = _ternary(oracle, dq, hidden, inter, 43, 0.021)
+    rng = np.random.default_rng(9)
+    n1 = (0.5 + rng.random(hidden)).astype(np.float32)
+    n2 = (0.5 + rng.random(inter)).astype(np.float32)
+    Wg = upload(jkb, quant, wg, inter, hidden, name="gate")
+    Wu = upload(jkb, quant, wu, inter, hidden, name="up")
+    Wd = upload(jkb, dq, wd, hidden, inter, name="down")
+    rep = tuple(jkb.RepackedWeight.from_tensor(jkb.TensorView(n, q, [r, c], b), r, c)
+                for n, q, b, r, c in (("gate", quant, wg, inter, hidden),
+                                      ("up", quant, wu, inter, hidden),
+                                      ("down", dq, wd, hidden, inter)))
+    d1, d2 = dev(n1), dev(n2)
+    tc = jkb.BitNetFFN(Wg, Wu, Wd, d1, d2, EPS, m, repacked=rep)
+    gv = jkb.BitNetFFN(Wg, Wu, Wd, d1, d2, EPS, m)
+    X = np.stack([oracle.normal(hidden, 60 + t, 1.0) for t in range(m)])
+    x = dev(X.reshape(-1))
+    out = torch.empty(m * hidden, dtype=torch.float32, device="cuda")
+    with jkb.gemm_exact(True):
+        tc.forward(out, x, m)
+    y = host(out).reshape(m, hidden)
+    a1, s1, g, u, h, a2, s2 = [host(t) for t in tc.buffers()]
+    for t in (0, 17, m - 1):
+        ra1, rs1 = oracle.subln_quantize_absmax_i8(X[t], n1, EPS)
+        assert np.array_equal(a1[t], ra1) and bits(np.float32(s1[t])) == bits(np.float32(rs1))
+        for got, w in ((g[t], wg), (u[t], wu)):
+            ref = oracle.bitlinear_i8(quant, w, inter, hidden, a1[t], float(s1[t]))
+            assert np.array_equal(bits(got), bits(ref))
+        rh = oracle.relu_squared_gate_f32(g[t], u[t])
+        assert np.array_equal(bits(h[t]), bits(rh))
+        ra2, rs2 = oracle.subln_quantize_absmax_i8(rh, n2, EPS)
+        assert np.array_equal(a2[t], ra2) and bits(np.float32(s2[t])) == bits(np.float32(rs2))
+        ref = oracle.bitlinear_i8(dq, wd, hidden, inter, a2[t], float(s2[t]))
+        assert np.array_equal(bits(y[t]), bits(ref))
+    # default epilogue against the GEMV chain
+    out2 = torch.empty(m * hidden, dtype=torch.float32, device="cuda")
+    tc.forward(out, x, m)
+    gv.forward(out2, x, m)
+    assert R.l2_rel_err(host(out), host(out2)) < 1e-3
+    with pytest.raises(jkb.TensorBoundsError, match="does not match"):
+        jkb.BitNetFFN(Wg, Wu, Wd, d1, d2, EPS, m, repacked=(rep[0], rep[1], rep[0]))
