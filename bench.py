@@ -854,8 +854,17 @@ def run_gemm_case(args):
     import jkb200 as jkb
 
     M, N, K = args.m, args.rows, args.cols
-    quant = {"gemm_q4_k": Q4_K, "gemm_q6_k": Q6_K, "gemm_nib_q4_k": Q4_K}.get(args.kernel, Q8_0)
-    raw = synth_matrix(quant, N, K, 4243)
+    # the formats without a quantizer in this file: seeded random bytes (GEMM time does not
+    # depend on the values; non-finite f16 scales decode to 0 as in the reference)
+    raw_fmt = {"gemm_q4_1": (3, 32, 20), "gemm_q5_1": (7, 32, 24), "gemm_iq4_nl": (20, 32, 18),
+               "gemm_q2_k": (10, 256, 84), "gemm_q3_k": (11, 256, 110)}
+    if args.kernel in raw_fmt:
+        quant, be, bb = raw_fmt[args.kernel]
+        raw = np.random.default_rng(4243).integers(0, 256, N * (K // be) * bb, dtype=np.uint8)
+    else:
+        quant = {"gemm_q4_k": Q4_K, "gemm_q6_k": Q6_K, "gemm_nib_q4_k": Q4_K}.get(args.kernel,
+                                                                                   Q8_0)
+        raw = synth_matrix(quant, N, K, 4243)
     if args.kernel == "gemm_nib_q4_k":
         rw = jkb.PackedNibbleMatrix.from_tensor(jkb.TensorView("w", quant, [N, K], raw), N, K)
     else:
@@ -904,7 +913,8 @@ def main():
                     help="leave out the BitNet BitLinear section (BASELINE configs[3])")
     ap.add_argument("--m", type=int, default=2048, help="tokens of --kernel gemm_q8_0 / int8_peak")
     ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0", "gemm_q8_0", "gemm_q4_k",
-                                         "gemm_q6_k", "gemm_nib_q4_k", "int8_peak"],
+                                         "gemm_q6_k", "gemm_nib_q4_k", "gemm_q4_1", "gemm_q5_1",
+                                         "gemm_iq4_nl", "gemm_q2_k", "gemm_q3_k", "int8_peak"],
                     help="run one GEMV shape (profiling case) instead of the benchmark")
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--cols", type=int, default=4096)
@@ -916,7 +926,7 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.kernel in ("gemm_q8_0", "gemm_q4_k", "gemm_q6_k", "gemm_nib_q4_k"):
+    if args.kernel and args.kernel.startswith("gemm_"):
         run_gemm_case(args)
     elif args.kernel == "int8_peak":
         run_int8_peak(args)

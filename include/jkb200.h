@@ -52,13 +52,16 @@ typedef enum {
     JKB_F32 = 0,
     JKB_F16 = 1,
     JKB_Q4_0 = 2,
-    JKB_Q4_1 = 3, /* compact nibble matrices only */
+    JKB_Q4_1 = 3, /* RepackedWeight and compact nibble matrices */
     JKB_Q5_0 = 6,
+    JKB_Q5_1 = 7, /* RepackedWeight only */
     JKB_Q8_0 = 8,
+    JKB_Q2_K = 10, /* RepackedWeight only */
+    JKB_Q3_K = 11, /* RepackedWeight only */
     JKB_Q4_K_M = 12,
     JKB_Q5_K = 13,
     JKB_Q6_K = 14,
-    JKB_IQ4_NL = 20, /* compact nibble matrices only */
+    JKB_IQ4_NL = 20, /* RepackedWeight and compact nibble matrices */
     JKB_BF16 = 30,
     JKB_TQ1_0 = 34,
     JKB_TQ2_0 = 35,
@@ -376,6 +379,10 @@ int jkb_repacked_weight_from_tensor(const jkb_tensor_view *view, size_t rows, si
 int jkb_repacked_weight_repack(const jkb_tensor_view *view, void *stream,
                                jkb_repacked_weight **out);
 int jkb_repacked_weight_destroy(jkb_repacked_weight *w);
+/* repack.rs:2529 RepackedWeight::dequantize_row: out[0 .. cols) = scale * q - min per group
+ * (device output). */
+int jkb_repacked_weight_dequantize_row(const jkb_repacked_weight *w, size_t row, float *out,
+                                       size_t out_len, void *stream);
 /* Device views: q [rows][k_pad] i8, scales and mins [rows][scale_groups] f32 (mins NULL
  * unless Q4_K_M). */
 int jkb_repacked_weight_buffers(const jkb_repacked_weight *w, size_t *rows, size_t *cols,

@@ -53,7 +53,9 @@ static const Fmt FMTS[] = {
     {JKB_Q4_K_M, "Q4_K_M", 256, 144, 0}, {JKB_Q6_K, "Q6_K", 256, 210, 0},
     {JKB_TQ1_0, "TQ1_0", 256, 54, 0},  {JKB_TQ2_0, "TQ2_0", 256, 66, 0},
     {JKB_I2_S, "I2_S", 128, 32, 32},  {JKB_Q5_0, "Q5_0", 32, 22, 0},
-    {JKB_Q5_K, "Q5_K", 256, 176, 0},
+    {JKB_Q5_K, "Q5_K", 256, 176, 0},   {JKB_Q4_1, "Q4_1", 32, 20, 0},
+    {JKB_Q5_1, "Q5_1", 32, 24, 0},     {JKB_IQ4_NL, "IQ4_NL", 32, 18, 0},
+    {JKB_Q2_K, "Q2_K", 256, 84, 0},    {JKB_Q3_K, "Q3_K", 256, 110, 0},
 };
 
 const Fmt *fmt_of(int quant) {
@@ -67,8 +69,6 @@ const char *quant_name(int quant) {
     case JKB_F32: return "F32";
     case JKB_F16: return "F16";
     case JKB_BF16: return "BF16";
-    case JKB_Q4_1: return "Q4_1";
-    case JKB_IQ4_NL: return "IQ4_NL";
     default: {
         const Fmt *f = fmt_of(quant);
         return f ? f->name : "Unknown";

@@ -251,6 +251,73 @@ __global__ void repack_i8_kernel(int quant, const uint8_t *__restrict__ raw, siz
         }
         break;
     }
+    case JKB_Q4_1: {  // repack.rs:1814-1826: scale d, min -m (0.0 when m == 0), unsigned codes
+        const float dd = f16_finite_dev(rd16(blk)), m = f16_finite_dev(rd16(blk + 2));
+        sr[b] = dd;
+        mr[b] = m == 0.0f ? 0.0f : -m;
+        for (int i = 0; i < 16; i++) {
+            qr[32 * b + i] = (int8_t)(blk[4 + i] & 0x0F);
+            qr[32 * b + 16 + i] = (int8_t)(blk[4 + i] >> 4);
+        }
+        break;
+    }
+    case JKB_Q5_1: {  // repack.rs:1841-1855 with unpack_q5_1_block_i8 (quant.rs:169-190)
+        const float dd = f16_finite_dev(rd16(blk)), m = f16_finite_dev(rd16(blk + 2));
+        sr[b] = dd;
+        mr[b] = m == 0.0f ? 0.0f : -m;
+        const uint32_t qh = (uint32_t)blk[4] | ((uint32_t)blk[5] << 8) |
+                            ((uint32_t)blk[6] << 16) | ((uint32_t)blk[7] << 24);
+        for (int i = 0; i < 16; i++) {
+            qr[32 * b + i] = (int8_t)((blk[8 + i] & 0x0F) | (((qh >> i) & 1) << 4));
+            qr[32 * b + 16 + i] = (int8_t)((blk[8 + i] >> 4) | (((qh >> (i + 16)) & 1) << 4));
+        }
+        break;
+    }
+    case JKB_IQ4_NL: {  // repack.rs:1856-1873: the code book values, left 0 when d == 0
+        // KVALUES_IQ4NL (quant.rs:80-82)
+        constexpr int8_t kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
+                                   1,    13,   25,  38,  53,  69,  89,  113};
+        const float dd = f16_finite_dev(rd16(blk));
+        sr[b] = dd;
+        for (int i = 0; i < 16; i++) {
+            qr[32 * b + i] = dd != 0.0f ? kv[blk[2 + i] & 0x0F] : 0;
+            qr[32 * b + 16 + i] = dd != 0.0f ? kv[blk[2 + i] >> 4] : 0;
+        }
+        break;
+    }
+    case JKB_Q2_K: {  // repack.rs:1874-1892 with unpack_q2_k_block_i8 (quant.rs:198-246)
+        // sub-block s (16 elements) takes the 2-bit field 2 * ((s % 8) / 2) of
+        // qs[32 (s / 8) + 16 (s % 2) + l]; scale d * (sc & 15), min dmin * (sc >> 4)
+        const float dd = f16_finite_dev(rd16(blk + 80)), dmin = f16_finite_dev(rd16(blk + 82));
+        for (int s = 0; s < 16; s++) {
+            sr[16 * b + s] = __fmul_rn(dd, (float)(blk[s] & 0x0F));
+            mr[16 * b + s] = __fmul_rn(dmin, (float)(blk[s] >> 4));
+            const int sh = 2 * ((s % 8) / 2);
+            const uint8_t *qs = blk + 16 + 32 * (s / 8) + 16 * (s % 2);
+            for (int l = 0; l < 16; l++) qr[256 * b + 16 * s + l] = (int8_t)((qs[l] >> sh) & 3);
+        }
+        break;
+    }
+    case JKB_Q3_K: {  // repack.rs:1893-1908 with unpack_q3_k_block_i8 (quant.rs:255-330)
+        // 6-bit scale s: low 4 bits from byte s (s < 8, low nibble) or s - 8 (high nibble),
+        // top 2 bits from byte 8 + s % 4 at bit 2 (s / 4); codes minus 4 where the hmask bit
+        // s / 2 of hmask[16 (s % 2) + l] is clear
+        const uint8_t *hm = blk, *raw6 = blk + 96;
+        const float dd = f16_finite_dev(rd16(blk + 108));
+        for (int s = 0; s < 16; s++) {
+            const int lo = s < 8 ? raw6[s] & 0x0F : raw6[s - 8] >> 4;
+            const int hi = (raw6[8 + s % 4] >> (2 * (s / 4))) & 3;
+            sr[16 * b + s] = __fmul_rn(dd, (float)((lo | (hi << 4)) - 32));
+            const int sh = 2 * ((s % 8) / 2);
+            const uint8_t *qs = blk + 32 + 32 * (s / 8) + 16 * (s % 2);
+            for (int l = 0; l < 16; l++) {
+                const int code = (qs[l] >> sh) & 3;
+                const int high = (hm[16 * (s % 2) + l] >> (s / 2)) & 1;
+                qr[256 * b + 16 * s + l] = (int8_t)(code - (high ? 0 : 4));
+            }
+        }
+        break;
+    }
     case JKB_I2_S: {
         for (int s = 0; s < 4; s++) sr[b * 4 + s] = i2s;
         for (int g = 0; g < 32; g++) {
@@ -358,7 +425,11 @@ static int weight_upload(const jkb_tensor_view *v, size_t rows, size_t cols, cud
     *out = nullptr;
     const Fmt *f = fmt_of(v->quant);
     const char *nm = v->name ? v->name : "";
-    if (!f)
+    // Q4_1, Q5_1, IQ4_NL, Q2_K and Q3_K have no block dot against Q8 activations in the
+    // reference (quant_q8.rs): they exist only as RepackedWeights and nibble matrices
+    const bool gemv_fmt = f && v->quant != JKB_Q4_1 && v->quant != JKB_Q5_1 &&
+                          v->quant != JKB_IQ4_NL && v->quant != JKB_Q2_K && v->quant != JKB_Q3_K;
+    if (!gemv_fmt)
         return fail(JKB_E_CAPABILITY, nm, v->offset, v->byte_len, v->byte_len,
                     "unsupported tensor quant %s for the GEMV layout", quant_name(v->quant));
     if (!v->data) return fail(JKB_E_INVALID, nm, v->offset, 0, 0, "null tensor data");
@@ -440,6 +511,19 @@ static int weight_upload(const jkb_tensor_view *v, size_t rows, size_t cols, cud
     return JKB_OK;
 }
 
+// RepackedWeight::dequantize_row (repack.rs:2529-2598), BlockScaledI8 storage: per element
+// scale * q - min of its group, two roundings.
+__global__ void repacked_dequant_row_kernel(const int8_t *__restrict__ q,
+                                            const float *__restrict__ scales,
+                                            const float *__restrict__ mins, size_t cols,
+                                            int group_elems, float *__restrict__ out) {
+    const size_t c = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cols) return;
+    const size_t g = c / (size_t)group_elems;
+    const float wm = mins ? mins[g] : 0.0f;
+    out[c] = __fsub_rn(__fmul_rn(scales[g], (float)q[c]), wm);
+}
+
 static int repacked_upload(const jkb_tensor_view *v, size_t rows, size_t cols, cudaStream_t st,
                            jkb_repacked_weight **out) {
     if (!v || !out)
@@ -462,10 +546,13 @@ static int repacked_upload(const jkb_tensor_view *v, size_t rows, size_t cols, c
     w->rows = rows;
     w->cols = cols;
     w->k_pad = (cols + 31) / 32 * 32;
-    w->group_elems = v->quant == JKB_Q6_K ? 16 : 32;
+    // BlockScaledTileLayout::from_validated_dims (repack.rs:1338-1366)
+    w->group_elems =
+        (v->quant == JKB_Q6_K || v->quant == JKB_Q3_K || v->quant == JKB_Q2_K) ? 16 : 32;
     w->scale_groups = w->k_pad / w->group_elems;
     snprintf(w->name, sizeof(w->name), "%s", nm);
-    bool mins = v->quant == JKB_Q4_K_M || v->quant == JKB_Q5_K;
+    bool mins = v->quant == JKB_Q4_K_M || v->quant == JKB_Q5_K || v->quant == JKB_Q4_1 ||
+                v->quant == JKB_Q5_1 || v->quant == JKB_Q2_K;
     Arena a;
     size_t qb = rows * w->k_pad, sb = rows * w->scale_groups * 4;
     a.cap = Arena::round(qb) + Arena::round(sb) * (mins ? 2 : 1);
@@ -580,6 +667,23 @@ int jkb_repacked_weight_destroy(jkb_repacked_weight *w) {
     cudaFree(w->base);
     delete w;
     return JKB_OK;
+}
+
+int jkb_repacked_weight_dequantize_row(const jkb_repacked_weight *w, size_t row, float *out,
+                                       size_t out_len, void *stream) {
+    if (!w || w->magic != REPACKED_MAGIC)
+        return fail(JKB_E_INVALID, "jkb_repacked_weight", 0, 0, 0, "null or destroyed handle");
+    if (row >= w->rows || out_len != w->cols)
+        return fail(JKB_E_BOUNDS, "RepackedWeight::dequantize_row", row, out_len * 4,
+                    w->cols * 4, "invalid row (%zu/%zu) or output length (%zu/%zu)", row,
+                    w->rows, out_len, w->cols);
+    if (!out) return fail(JKB_E_INVALID, "RepackedWeight::dequantize_row", 0, 0, 0, "null output");
+    int rc = check_align(out, 4, "RepackedWeight::dequantize_row", "output");
+    if (rc) return rc;
+    repacked_dequant_row_kernel<<<(unsigned)((w->cols + 255) / 256), 256, 0, as_stream(stream)>>>(
+        w->q + row * w->k_pad, w->scales + row * w->scale_groups,
+        w->mins ? w->mins + row * w->scale_groups : nullptr, w->cols, (int)w->group_elems, out);
+    return check_launch("repacked_dequant_row_kernel");
 }
 
 int jkb_repacked_weight_buffers(const jkb_repacked_weight *w, size_t *rows, size_t *cols,

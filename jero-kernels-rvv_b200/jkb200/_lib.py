@@ -73,6 +73,7 @@ SIGNATURES = {
     "jkb_bitnet_ffn_buffers": [P, PP, PP, PP, PP, PP, PP, PP],
     "jkb_bitnet_ffn_destroy": [P],
     "jkb_bitlinear_i8_gemm": [P, S, P, P, S, P, S, P, P],
+    "jkb_repacked_weight_dequantize_row": [P, S, P, S, P],
     "jkb_act_q8_create": [S, S, PP],
     "jkb_act_q8_destroy": [P],
     "jkb_act_q8_quantize": [P, P, S, S, S, P],

@@ -46,7 +46,10 @@ class QuantType(enum.IntEnum):
     Q4_0 = 2
     Q4_1 = 3
     Q5_0 = 6
+    Q5_1 = 7
     Q8_0 = 8
+    Q2_K = 10
+    Q3_K = 11
     Q4_K_M = 12
     Q5_K = 13
     Q6_K = 14
@@ -62,7 +65,8 @@ BLOCK = {
     QuantType.Q4_0: (32, 18), QuantType.Q8_0: (32, 34), QuantType.Q4_K_M: (256, 144),
     QuantType.Q6_K: (256, 210), QuantType.TQ1_0: (256, 54), QuantType.TQ2_0: (256, 66),
     QuantType.I2_S: (128, 32), QuantType.Q4_1: (32, 20), QuantType.IQ4_NL: (32, 18),
-    QuantType.Q5_0: (32, 22), QuantType.Q5_K: (256, 176),
+    QuantType.Q5_0: (32, 22), QuantType.Q5_K: (256, 176), QuantType.Q5_1: (32, 24),
+    QuantType.Q2_K: (256, 84), QuantType.Q3_K: (256, 110),
 }
 BLOCK_Q8_0_BYTES = 36
 BLOCK_Q8_K_BYTES = 292
@@ -338,6 +342,14 @@ class RepackedWeight:
                                                 C.byref(g), None, None, None))
         self.rows, self.cols, self.quant, self.scale_groups = r.value, c.value, QuantType(
             q.value), g.value
+
+    def dequantize_row(self, row: int, out: torch.Tensor = None, stream=None) -> torch.Tensor:
+        """repack.rs:2529 RepackedWeight::dequantize_row (scale * q - min per group)."""
+        if out is None:
+            out = torch.empty(self.cols, dtype=torch.float32, device="cuda")
+        _check(_L().jkb_repacked_weight_dequantize_row(self._h, row, _dptr(out), out.numel(),
+                                                       _stream(stream)))
+        return out
 
     @classmethod
     def from_tensor(cls, view: TensorView, rows: int, cols: int, stream=None):

@@ -497,7 +497,8 @@ static const fmt_t FMTS[] = {
     {OR_Q4_0, 32, 18, 0, 1},   {OR_Q8_0, 32, 34, 0, 1},    {OR_Q4_K, 256, 144, 1, 1},
     {OR_Q6_K, 256, 210, 1, 1}, {OR_TQ2_0, 256, 66, 1, 1}, {OR_TQ1_0, 256, 54, 1, 1},
     {OR_I2_S, 128, 32, 0, 1},  {OR_Q4_1, 32, 20, 0, 0},   {OR_IQ4_NL, 32, 18, 0, 0},
-    {OR_Q5_0, 32, 22, 0, 1},   {OR_Q5_K, 256, 176, 1, 1},
+    {OR_Q5_0, 32, 22, 0, 1},   {OR_Q5_K, 256, 176, 1, 1},  {OR_Q5_1, 32, 24, 0, 0},
+    {OR_Q2_K, 256, 84, 1, 0},  {OR_Q3_K, 256, 110, 1, 0},
 };
 
 static const fmt_t *fmt_of(int quant) {
@@ -627,6 +628,57 @@ int or_gemv_rows_mt(int quant, float *out, const uint8_t *w, size_t rows, size_t
 /* ------------------------------------------------------------------------------------------ */
 /* f32-activation host fallback: dequantize block -> f32 dot (quant.rs, lib.rs)                */
 /* ------------------------------------------------------------------------------------------ */
+
+/* unpack_q5_1_block_i8 (quant.rs:169-190): unsigned 5-bit codes (nibble | high bit << 4, the
+ * high bits of elements j and j + 16 in bits j and j + 16 of qh); returns d and *m. */
+static float unpack_q5_1(const uint8_t *blk, int8_t *q, float *m) {
+    float d = or_f16_to_f32_finite(rd16(blk));
+    *m = or_f16_to_f32_finite(rd16(blk + 2));
+    uint32_t qh = (uint32_t)blk[4] | ((uint32_t)blk[5] << 8) | ((uint32_t)blk[6] << 16) |
+                  ((uint32_t)blk[7] << 24);
+    for (int j = 0; j < 16; j++) {
+        q[j] = (int8_t)((blk[8 + j] & 0x0F) | (((qh >> j) & 1) << 4));
+        q[j + 16] = (int8_t)(((blk[8 + j] >> 4) & 0x0F) | (((qh >> (j + 16)) & 1) << 4));
+    }
+    return d;
+}
+
+/* unpack_q2_k_block_i8 (quant.rs:198-246): 84-byte super-block = scales[16] (low nibble scale,
+ * high nibble min), qs[64], f16 d, f16 dmin. Sub-block is (0..15) covers elements 16 is ..;
+ * half h = is / 8, shift 2 * ((is % 8) / 2), bytes qs[32 h + 16 (is % 2) + l]. Codes 0..3,
+ * scale d * (sc & 15), min dmin * (sc >> 4). */
+static void unpack_q2_k(const uint8_t *blk, int8_t *q, float *sc, float *mn) {
+    float d = or_f16_to_f32_finite(rd16(blk + 80)), dmin = or_f16_to_f32_finite(rd16(blk + 82));
+    const uint8_t *qs = blk + 16;
+    for (int is = 0; is < 16; is++) {
+        int h = is / 8, shift = 2 * ((is % 8) / 2), half16 = is % 2;
+        sc[is] = d * (float)(blk[is] & 0x0F);
+        mn[is] = dmin * (float)(blk[is] >> 4);
+        for (int l = 0; l < 16; l++)
+            q[16 * is + l] = (int8_t)((qs[32 * h + 16 * half16 + l] >> shift) & 3);
+    }
+}
+
+/* unpack_q3_k_block_i8 (quant.rs:255-330): 110-byte super-block = hmask[32], qs[64],
+ * scales[12] (sixteen 6-bit values: low 4 bits from bytes 0..7, top 2 bits from bytes 8..11),
+ * f16 d. Sub-block is: the 2-bit code of qs[32 h + 16 (is % 2) + l] at shift 2 ((is % 8) / 2),
+ * minus 4 when bit (is / 2) of hmask[16 (is % 2) + l] is clear; scale d * (s6 - 32). */
+static void unpack_q3_k(const uint8_t *blk, int8_t *q, float *sc) {
+    const uint8_t *hm = blk, *qs = blk + 32, *raw = blk + 96;
+    float d = or_f16_to_f32_finite(rd16(blk + 108));
+    for (int is = 0; is < 16; is++) {
+        int lo = is < 8 ? raw[is] & 0x0F : raw[is - 8] >> 4;
+        int hi = (raw[8 + (is % 4)] >> (2 * (is / 4))) & 3;
+        int s6 = lo | (hi << 4);
+        sc[is] = d * (float)(s6 - 32);
+        int h = is / 8, shift = 2 * ((is % 8) / 2), half16 = is % 2;
+        for (int l = 0; l < 16; l++) {
+            int code = (qs[32 * h + 16 * half16 + l] >> shift) & 3;
+            int high = (hm[16 * half16 + l] >> (is / 2)) & 1;
+            q[16 * is + l] = (int8_t)(code - (high ? 0 : 4));
+        }
+    }
+}
 
 /* quant.rs:551-568 (Q4_0), :570-588 (Q8_0), :594-648 (Q6_K), lib.rs:720-766 (Q4_K_M),
  * quant.rs:380-388 (I2_S with the tensor scale), ime.rs:636-658 / :595-624 (TQ2_0 / TQ1_0 times d). */
@@ -759,6 +811,33 @@ void or_dequantize_block(int quant, const uint8_t *blk, float i2s_scale, float *
             out[i] = d * (float)OR_KVALUES_IQ4NL[blk[2 + i] & 0x0F];
             out[i + 16] = d * (float)OR_KVALUES_IQ4NL[blk[2 + i] >> 4];
         }
+        return;
+    }
+    case OR_Q5_1: {
+        /* quant.rs:192-196: y = d * q + m over unsigned 5-bit codes; zeros when d == m == 0 */
+        int8_t q[32];
+        float m, d = unpack_q5_1(blk, q, &m);
+        if (d == 0.0f && m == 0.0f) {
+            memset(out, 0, 32 * sizeof(float));
+            return;
+        }
+        for (int i = 0; i < 32; i++) out[i] = d * (float)q[i] + m;
+        return;
+    }
+    case OR_Q2_K: {
+        /* quant.rs:249-252: y = dl * q - ml per 16-element sub-block */
+        int8_t q[256];
+        float sc[16], mn[16];
+        unpack_q2_k(blk, q, sc, mn);
+        for (int i = 0; i < 256; i++) out[i] = sc[i / 16] * (float)q[i] - mn[i / 16];
+        return;
+    }
+    case OR_Q3_K: {
+        /* quant.rs:333-342: y = dl * q per 16-element sub-block */
+        int8_t q[256];
+        float sc[16];
+        unpack_q3_k(blk, q, sc);
+        for (int i = 0; i < 256; i++) out[i] = sc[i / 16] * (float)q[i];
         return;
     }
     case OR_I2_S: {
@@ -939,15 +1018,19 @@ int or_bitlinear_i8_rows_mt(float *out, int quant, const uint8_t *w, size_t w_le
 /* Repacked block-scaled weights (repack.rs:1724-2103) and the scalar GEMM (:2995-3093)        */
 /* ------------------------------------------------------------------------------------------ */
 
-/* BlockScaledTileLayout::from_validated_dims repack.rs:1330-1366: Q6_K uses 16-element scale
- * groups (chunks_per_scale = 1), every other format 32-element groups; Q4_K carries mins. */
+/* BlockScaledTileLayout::from_validated_dims repack.rs:1330-1366: Q6_K, Q3_K and Q2_K use
+ * 16-element scale groups (chunks_per_scale = 1), every other format 32-element groups;
+ * Q4_K_M, Q5_K, Q4_1, Q5_1 and Q2_K carry mins. */
+static int g16(int quant) { return quant == OR_Q6_K || quant == OR_Q2_K || quant == OR_Q3_K; }
+
 size_t or_repack_scale_groups(int quant, size_t cols) {
     size_t kp = (cols + 31) / 32 * 32;
-    return quant == OR_Q6_K ? kp / 16 : kp / 32;
+    return g16(quant) ? kp / 16 : kp / 32;
 }
 
 int or_repack_has_mins(int quant) {
-    return quant == OR_Q4_K || quant == OR_Q4_1 || quant == OR_Q5_K;
+    return quant == OR_Q4_K || quant == OR_Q4_1 || quant == OR_Q5_K || quant == OR_Q5_1 ||
+           quant == OR_Q2_K;
 }
 
 int or_repack_block_scaled(int quant, const uint8_t *raw, size_t raw_len, size_t rows,
@@ -1093,6 +1176,23 @@ int or_repack_block_scaled(int quant, const uint8_t *raw, size_t raw_len, size_t
                     }
                 break;
             }
+            case OR_Q5_1: {
+                /* repack.rs:1841-1855: scale d, min -m (0.0 when m == 0), unsigned 5-bit codes */
+                float m, d = unpack_q5_1(blk, qr + 32 * b, &m);
+                sr[b] = d;
+                mr[b] = m == 0.0f ? 0.0f : -m;
+                break;
+            }
+            case OR_Q2_K: {
+                /* repack.rs:1874-1892: 16 (scale, min) pairs per super-block, codes 0..3 */
+                unpack_q2_k(blk, qr + 256 * b, sr + 16 * b, mr + 16 * b);
+                break;
+            }
+            case OR_Q3_K: {
+                /* repack.rs:1893-1908: 16 signed scales per super-block, codes -4..3 */
+                unpack_q3_k(blk, qr + 256 * b, sr + 16 * b);
+                break;
+            }
             case OR_I2_S: {
                 int8_t t[128];
                 unpack_i2_s(blk, t);
@@ -1109,7 +1209,7 @@ int or_repack_block_scaled(int quant, const uint8_t *raw, size_t raw_len, size_t
 
 typedef struct {
     float *out;
-    int cps; /* 16-element chunks per scale group: 2 (32-element groups) or 1 (Q6_K) */
+    int cps; /* 16-element chunks per scale group: 2 (32-element groups) or 1 (Q6_K/Q3_K/Q2_K) */
     const int8_t *wq;
     const float *ws, *wm;
     size_t cols;
@@ -1180,7 +1280,7 @@ int or_gemm_repacked(float *out, int quant, const int8_t *wq, const float *ws, c
                      size_t row_end, int nthreads) {
     if (row_begin > row_end || row_end > rows || m == 0) return 1;
     if (or_repack_has_mins(quant) && (!wm || !xsum)) return 1;
-    return gemm_run(out, quant == OR_Q6_K ? 1 : 2, wq, ws, or_repack_has_mins(quant) ? wm : NULL,
+    return gemm_run(out, g16(quant) ? 1 : 2, wq, ws, or_repack_has_mins(quant) ? wm : NULL,
                     cols, xq, xs, xsum, xsum16, m, row_begin, row_end, nthreads);
 }
 

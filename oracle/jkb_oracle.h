@@ -41,6 +41,9 @@ enum {
     OR_Q4_0 = 2,
     OR_Q4_1 = 3,
     OR_Q5_0 = 6,
+    OR_Q5_1 = 7,
+    OR_Q2_K = 10,
+    OR_Q3_K = 11,
     OR_Q8_0 = 8,
     OR_Q4_K = 12,
     OR_Q5_K = 13,

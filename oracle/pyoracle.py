@@ -21,9 +21,13 @@ LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 # QuantType codes shared with include/jkb200.h (GGML type ids where one exists).
 Q4_0, Q8_0, Q4_K, Q6_K, TQ1_0, TQ2_0, I2_S = 2, 8, 12, 14, 34, 35, 36
 Q4_1, IQ4_NL, Q5_0, Q5_K = 3, 20, 6, 13
+Q5_1, Q2_K, Q3_K = 7, 10, 11
 BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210),
          TQ1_0: (256, 54), TQ2_0: (256, 66), I2_S: (128, 32), Q4_1: (32, 20), IQ4_NL: (32, 18),
-         Q5_0: (32, 22), Q5_K: (256, 176)}
+         Q5_0: (32, 22), Q5_K: (256, 176), Q5_1: (32, 24), Q2_K: (256, 84), Q3_K: (256, 110)}
+# formats a RepackedWeight holds (BlockScaledTileLayout::for_tensor, repack.rs:1308-1336)
+REPACKABLE = (Q8_0, Q4_0, Q4_1, Q5_0, Q5_1, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, IQ4_NL, TQ1_0,
+              TQ2_0, I2_S)
 NIBBLE = (Q4_0, Q4_1, IQ4_NL, Q4_K)  # PackedNibbleMatrix formats (repack.rs:4231-4236)
 NIBBLE_MINS = (Q4_1, Q4_K)
 ACT_IS_Q8K = {Q4_0: False, Q8_0: False, Q4_K: True, Q6_K: True, TQ1_0: True, TQ2_0: True,

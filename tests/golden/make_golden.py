@@ -139,6 +139,29 @@ def kats():
     row[28:44] = bytes([0x5A] * 16)
     out["q5_0_two_block_row"] = {"ref": "src/quant.rs:2910-2966", "row_hex": bytes(row).hex(),
                                  "abs_tol": 1e-4}
+    # quant.rs:2864-2873: Q5_1 d = 0.5, m = 1.0, qh bits 0 and 16 set, qs[0] = 0x32: element 0
+    # is 0.5 * (2 + 16) + 1 = 10, element 16 is 0.5 * (3 + 16) + 1 = 10.5.
+    blk = h16(0x3800) + h16(0x3C00) + struct.pack("<I", 0x00010001) + bytes([0x32]) + bytes(15)
+    out["q5_1_dequant"] = {"ref": "src/quant.rs:2864-2873", "block_hex": blk.hex(),
+                           "expect": {"0": 10.0, "16": 10.5}}
+    # quant.rs:2875-2884: Q2_K sub-block 0 scale 2, min 1, code 3, d = 1.0, dmin = 0.5:
+    # element 0 is 1 * 2 * 3 - 0.5 * 1 = 5.5.
+    raw = bytearray(84)
+    raw[0] = (1 << 4) | 2
+    raw[16] = 0x03
+    raw[80:82] = h16(0x3C00)
+    raw[82:84] = h16(0x3800)
+    out["q2_k_dequant"] = {"ref": "src/quant.rs:2875-2884", "block_hex": bytes(raw).hex(),
+                           "expect": {"0": 5.5}}
+    # quant.rs:2886-2893: Q3_K hmask 0, every 6-bit scale 33 (scales[0..8] = 0x11,
+    # scales[8..12] = 0xAA), qs[0] = 3, d = 0.5: element 0 is 0.5 * (33 - 32) * (3 - 4) = -0.5.
+    raw = bytearray(110)
+    raw[96:104] = bytes([0x11] * 8)
+    raw[104:108] = bytes([0xAA] * 4)
+    raw[32] = 0x03
+    raw[108:110] = h16(0x3800)
+    out["q3_k_dequant"] = {"ref": "src/quant.rs:2886-2893", "block_hex": bytes(raw).hex(),
+                           "expect": {"0": -0.5}}
     # quant_q8.rs:3414-3482: quantizer sanitization on test_f32_row inputs.
     out["q8_sanitize"] = {"ref": "src/quant_q8.rs:3388-3395,3414-3482"}
     return out

@@ -220,3 +220,104 @@ def bitnet_chain_scenarios(hidden: int):
     return [("normal_random", (np.sin(i * np.float32(0.05)) * np.float32(2.0)).astype(np.float32)),
             ("all_zeros", np.zeros(hidden, np.float32)),
             ("extreme_large", np.full(hidden, 1e5, np.float32))]
+
+
+# ---- tests/test_repack_gemv_gemm.rs generators ----
+
+def f16_bits_trunc(v) -> int:
+    """f32_to_f16_bits of tests/test_repack_gemv_gemm.rs:31-45: the mantissa truncated (no
+    rounding), exponents below the f16 range flushed to a signed zero, above it clamped to
+    0x7BFF."""
+    bits = int(np.float32(v).view(np.uint32))
+    sign = (bits >> 16) & 0x8000
+    exp = (bits >> 23) & 0xFF
+    mant = bits & 0x7FFFFF
+    if exp <= 127 - 15:
+        return sign
+    if exp >= 127 + 16:
+        return sign | 0x7BFF
+    return sign | ((exp - 112) << 10) | (mant >> 13)
+
+
+def make_activations(m: int, k: int, seed: int) -> np.ndarray:
+    """make_activations (tests/test_repack_gemv_gemm.rs:51-63): xorshift64 states, each
+    multiplied by 0x2545F4914F6CDD1D, top 24 bits as a unit float, mapped to [-1, 1)."""
+    out = np.empty(m * k, np.float32)
+    s = ((seed * 0x9E3779B97F4A7C15) & MASK64) | 1
+    for i in range(m * k):
+        s ^= s >> 12
+        s ^= (s << 25) & MASK64
+        s ^= s >> 27
+        u = (s * 0x2545F4914F6CDD1D) & MASK64
+        out[i] = np.float32(u >> 40) / np.float32(1 << 24)
+    return (out * np.float32(2.0) - np.float32(1.0)).astype(np.float32)
+
+
+def build_synthetic_quant_tensor(quant: int, rows: int, cols: int, seed: int) -> np.ndarray:
+    """build_synthetic_quant_tensor (tests/test_repack_gemv_gemm.rs:86-390) for the formats of
+    its wave-2 test: Q4_1 (3), Q5_0 (6), Q5_1 (7), Q2_K (10), Q3_K (11), IQ4_NL (20), I2_S (36).
+    Scales are f32 expressions rounded through f16_bits_trunc, as there."""
+    f = np.float32
+    h = lambda v: int(f16_bits_trunc(v)).to_bytes(2, "little")
+    u32 = lambda v: (v & 0xFFFFFFFF).to_bytes(4, "little")
+    out = bytearray()
+    if quant == 36:
+        nb = cols // 128
+        for r in range(rows):
+            for b in range(nb):
+                for gp in range(32):
+                    t0 = (r + gp + seed) % 3
+                    t1 = (b + gp + 1 + seed) % 3
+                    t2 = (r + b + gp + 2) % 3
+                    t3 = (r * 3 + gp + 1) % 3
+                    out.append((t0 << 6) | (t1 << 4) | (t2 << 2) | t3)
+        trailer = bytearray(32)
+        trailer[0:4] = np.float32(0.125).tobytes()
+        return np.frombuffer(bytes(out + trailer), np.uint8).copy()
+    for r in range(rows):
+        for b in range(cols // (256 if quant in (10, 11) else 32)):
+            if quant == 3:
+                d = f(0.0625) * (f(1.0) + f((r + b) % 4) * f(0.5))
+                m = f(-0.25) + f((r * 3 + b) % 5) * f(0.125)
+                out += h(d) + h(m)
+                out += bytes(((r * 7 + b * 3 + i + seed) & 15) |
+                             (((r * 11 + b * 5 + i * 3 + seed) & 15) << 4) for i in range(16))
+            elif quant == 6:
+                d = f(0.0625) * (f(1.0) + f((r + b) % 4) * f(0.25))
+                qh = (r * 0x9E3779B1) ^ (b * 0x85EBCA77) ^ (seed * 0x01010101)
+                out += h(d) + u32(qh)
+                out += bytes(((r * 5 + b * 9 + i + seed) & 15) |
+                             (((r * 13 + b * 3 + i * 5 + seed) & 15) << 4) for i in range(16))
+            elif quant == 7:
+                d = f(0.0625) * (f(1.0) + f((r + b) % 3) * f(0.25))
+                m = f(-0.25) + f((r * 2 + b * 3) % 7) * f(0.0625)
+                qh = (r * 0x517CC1B7) ^ (b * 0x27220A95) ^ seed
+                out += h(d) + h(m) + u32(qh)
+                out += bytes(((r * 9 + b * 7 + i + seed) & 15) |
+                             (((r * 3 + b * 11 + i * 7 + seed) & 15) << 4) for i in range(16))
+            elif quant == 10:
+                sc = [((r * 5 + b * 3 + s + 1) % 15) + 1 for s in range(16)]
+                mn = [(r * 3 + b * 7 + s + 2) % 13 for s in range(16)]
+                out += bytes((sc[s] & 15) | ((mn[s] & 15) << 4) for s in range(16))
+                out += bytes((r * 17 + b * 11 + i * 5 + seed) & 0xFF for i in range(64))
+                out += h(0.0625) + h(0.03125)
+            elif quant == 11:
+                out += bytes((r * 13 + b * 7 + i * 9 + seed) & 0xFF for i in range(96))
+                out += bytes((r * 19 + b * 23 + s * 11 + seed + 7) & 0xFF for s in range(12))
+                out += h(0.0625)
+            elif quant == 20:
+                d = f(0.03125) * (f(1.0) + f((r + b) % 4) * f(0.25))
+                out += h(d)
+                out += bytes(((r * 5 + b * 3 + i + seed) & 15) |
+                             (((r * 7 + b * 9 + i * 3 + seed) & 15) << 4) for i in range(16))
+            else:
+                raise ValueError(f"no generator for quant {quant}")
+    return np.frombuffer(bytes(out), np.uint8).copy()
+
+
+def cosine_and_rel_l2(actual, reference):
+    """cosine_similarity_and_rel_l2 (tests/test_repack_gemv_gemm.rs:65-84), in f64."""
+    a = np.asarray(actual, np.float64).ravel()
+    r = np.asarray(reference, np.float64).ravel()
+    denom = max(np.linalg.norm(a) * np.linalg.norm(r), 1e-12)
+    return float(a @ r / denom), float(np.linalg.norm(a - r) / max(np.linalg.norm(r), 1e-12))

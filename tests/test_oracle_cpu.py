@@ -513,3 +513,43 @@ def test_q5_gemv_tolerance_and_repack(oracle, quant):
         deq = deq - mn[:, :, None]
     assert np.allclose(deq.reshape(rows, -1), oracle.dequantize_rows(quant, w, rows, cols),
                        rtol=1e-6, atol=1e-7)
+
+
+def test_q5_1_q2_k_q3_k_dequant_kats(oracle, kats):
+    """quant.rs:2864-2893: Q5_1 (high bits from qh), Q2_K (sub-block scale and min), Q3_K
+    (6-bit scale 33 split over the scale bytes, cleared hmask bit subtracts 4)."""
+    for key, quant in (("q5_1_dequant", oracle.Q5_1), ("q2_k_dequant", oracle.Q2_K),
+                       ("q3_k_dequant", oracle.Q3_K)):
+        k = kats[key]
+        d = oracle.dequantize_block(quant, _u8(k["block_hex"]))
+        for idx, v in k["expect"].items():
+            assert abs(d[int(idx)] - v) < 1e-6, (key, idx, d[int(idx)])
+
+
+WAVE2 = [(3, 256, 19, 1.5e-2), (6, 256, 21, 1.2e-2), (7, 256, 17, 1.5e-2), (10, 512, 15, 2.0e-2),
+         (11, 512, 19, 1.5e-2), (20, 256, 23, 1.5e-2), (36, 256, 17, 1.5e-2)]
+
+
+@pytest.mark.parametrize("q_idx", range(len(WAVE2)))
+def test_wave2_repack_gemm_contract(oracle, q_idx):
+    """tests/test_repack_gemv_gemm.rs:919-997 on the oracle, with the test's own synthetic
+    tensors and activations: the repacked weight's rows (scale * q - min, repack.rs:2529-2598)
+    within 1e-4 of the block dequantizers, and the repacked GEMM over Q8 activations against the
+    f32 product: cosine > 0.999 and relative l2 error below the test's per-format bound, for
+    M in {1, 5, 8, 17, 64}."""
+    quant, cols, rows, max_rel = WAVE2[q_idx]
+    raw = R.build_synthetic_quant_tensor(quant, rows, cols, q_idx + 17)
+    q, s, mn = oracle.repack_block_scaled(quant, raw, rows, cols)
+    gsz = q.shape[1] // s.shape[1]
+    deq = oracle.dequantize_rows(quant, raw, rows, cols)
+    rep = np.repeat(s, gsz, axis=1) * q.astype(np.float32)
+    if mn is not None:
+        rep = rep - np.repeat(mn, gsz, axis=1)
+    assert np.all(np.abs(rep[:, :cols] - deq) < 1e-4)
+    for m in (1, 5, 8, 17, 64):
+        x = R.make_activations(m, cols, 300 + q_idx * 10 + m)
+        xq, xs, xsum, xs16, _ = oracle.act_q8_quantize(x, m, cols)
+        got = oracle.gemm_repacked(quant, q, s, mn, rows, cols, xq, xs, xsum, xs16, m)
+        want = x.reshape(m, cols).astype(np.float64) @ deq.astype(np.float64).T
+        cos, rel = R.cosine_and_rel_l2(got, want)
+        assert cos > 0.999 and rel < max_rel, (quant, m, cos, rel)
