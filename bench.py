@@ -878,6 +878,28 @@ def run_gemm_case(args):
                       "tops": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 2)}))
 
 
+def run_bitlinear_case(args):
+    """The tensor-core BitLinear (bitlinear_i8_gemm) on TQ2_0 weights: M tokens x --rows x
+    --cols, i8 activations from the SubLN quantizer, `--launches` calls timed in a CUDA graph
+    (the profiling case of the BitNet section)."""
+    import torch
+    import jkb200 as jkb
+
+    M, N, K = args.m, args.rows, args.cols
+    raw = synth_ternary(TQ2_0, N, K, 77)
+    rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", TQ2_0, [N, K], raw), N, K)
+    x = torch.randn(M * K, generator=torch.Generator().manual_seed(6)).cuda()
+    q = torch.empty(M * K, dtype=torch.int8, device="cuda")
+    sc = torch.empty(M, dtype=torch.float32, device="cuda")
+    jkb.subln_quantize_absmax_i8_rows(q, x, torch.ones(K, device="cuda"), M, K, 1e-5, sc)
+    act = jkb.QuantizedActQ8(M, K)
+    out = torch.empty(M * N, dtype=torch.float32, device="cuda")
+    us = _graph_time(lambda: jkb.bitlinear_i8_gemm(out, rw, q, sc, M, act), args.launches)
+    print(json.dumps({"kernel": "bitlinear_tc", "m": M, "rows": N, "cols": K,
+                      "us_per_call": round(us, 2),
+                      "tops": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 2)}))
+
+
 def run_int8_peak(args):
     """cuBLAS int8 GEMM throughput through torch._int_mm (the int8 roofline denominator)."""
     import torch
@@ -914,7 +936,8 @@ def main():
     ap.add_argument("--m", type=int, default=2048, help="tokens of --kernel gemm_q8_0 / int8_peak")
     ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0", "gemm_q8_0", "gemm_q4_k",
                                          "gemm_q6_k", "gemm_nib_q4_k", "gemm_q4_1", "gemm_q5_1",
-                                         "gemm_iq4_nl", "gemm_q2_k", "gemm_q3_k", "int8_peak"],
+                                         "gemm_iq4_nl", "gemm_q2_k", "gemm_q3_k", "int8_peak",
+                                         "bitlinear_tc"],
                     help="run one GEMV shape (profiling case) instead of the benchmark")
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--cols", type=int, default=4096)
@@ -926,7 +949,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.kernel and args.kernel.startswith("gemm_"):
+    if args.kernel == "bitlinear_tc":
+        run_bitlinear_case(args)
+    elif args.kernel and args.kernel.startswith("gemm_"):
         run_gemm_case(args)
     elif args.kernel == "int8_peak":
         run_int8_peak(args)

@@ -115,7 +115,10 @@ struct TcCfg {
     static constexpr int STAGE_SMEM =
         STAGE_TX + (H16 ? 2 * SB : 0) + (NIB ? SA + BMW * NG * 4 + (MINS ? BMW * GPS * 4 : 0) : 0);
     static constexpr int STAGES_FIT = ((NEG8 ? 184 : 200) * 1024) / STAGE_SMEM;
-    static constexpr int STAGES = STAGES_FIT > 6 ? 6 : STAGES_FIT;
+    // BitLinear blocks run on small batches, where a CTA's time is its stages' load latency:
+    // they keep up to eight stages in flight, the block-scaled GEMM six
+    static constexpr int STAGES_MAX = AB_ > 1 ? 8 : 6;
+    static constexpr int STAGES = STAGES_FIT > STAGES_MAX ? STAGES_MAX : STAGES_FIT;
     static_assert((COLS == 32 || COLS == 64) && BN % 32 == 0 && BN <= 256, "tile shape");
     static_assert(GPS % GPR == 0 && 2 * NA * BN <= TMEM_COLS, "two rounds of NA buffers");
     static_assert(!(H16 && MINS), "16-element groups carry no mins");
@@ -992,7 +995,10 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
 }
 
 
-// BitLinear configurations: one accumulator per block (GPR = 1), AB K steps per block.
+// BitLinear configurations: one accumulator per block (GPR = 1), AB K steps per block. The
+// 32-token tile (one epilogue warp per lane quarter) serves matrices with few 128-row weight
+// tiles, where the token tiles are what spreads the work over the SMs.
+template <bool E, int AB> using TB32 = TcCfg<32, 1, 1, E, false, false, NIB_NONE, AB>;
 template <bool E, int AB> using TB64 = TcCfg<64, 2, 1, E, false, false, NIB_NONE, AB>;
 template <bool E, int AB> using TB96 = TcCfg<96, 3, 1, E, false, false, NIB_NONE, AB>;
 template <bool E, int AB> using TB128 = TcCfg<128, 2, 1, E, false, false, NIB_NONE, AB>;
@@ -1001,6 +1007,7 @@ template <bool EXACT, int AB>
 int launch_bl_bn(int bn, const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out,
                  cudaStream_t st, int *err) {
     switch (bn) {
+        case 32: return launch_tc<TB32<EXACT, AB>>(w, act, out, 0, w->rows, st, err);
         case 64: return launch_tc<TB64<EXACT, AB>>(w, act, out, 0, w->rows, st, err);
         case 128: return launch_tc<TB128<EXACT, AB>>(w, act, out, 0, w->rows, st, err);
         default: return launch_tc<TB96<EXACT, AB>>(w, act, out, 0, w->rows, st, err);
@@ -1031,7 +1038,17 @@ int gemm_tc_bitlinear_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act
     int *err = device_error_word();
     if (!err) return JKB_OK;
     *used = true;
-    const int bn = choose_tile(act->m, w->rows, false);
+    // the repacked GEMM's choice, or the 32-token tile when it takes fewer tile-widths of
+    // waves (small weight matrices: BitNet's 2560-row down projection has 20 weight tiles)
+    int bn = choose_tile(act->m, w->rows, false);
+    {
+        const size_t tiles_w = (w->rows + BMW - 1) / BMW, sms = (size_t)num_sms();
+        auto cost = [&](size_t b) {
+            const size_t tiles = tiles_w * ((act->m + b - 1) / b);
+            return (tiles + sms - 1) / sms * b;
+        };
+        if (cost(32) < cost((size_t)bn)) bn = 32;
+    }
     const bool exact = g_gemm_exact.load(std::memory_order_relaxed);
     if (ab == 8)
         return exact ? launch_bl_bn<true, 8>(bn, w, act, out, st, err)

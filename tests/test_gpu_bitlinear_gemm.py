@@ -181,7 +181,7 @@ def test_gemm_validation(jkb, oracle):
 
 @pytest.mark.parametrize("exact", [False, True])
 @pytest.mark.parametrize("rows,cols,m", [(640, 2560, 128), (2560, 6912, 40), (6912, 2560, 64),
-                                         (256, 1024, 8), (384, 512, 33)])
+                                         (256, 1024, 8), (384, 512, 33), (6912, 2560, 128)])
 @pytest.mark.parametrize("quant", [35, 34, 36, 8])
 def test_bitlinear_gemm_tensor_cores(jkb, oracle, quant, rows, cols, m, exact):
     """jkb_bitlinear_i8_gemm against the reference's per-token bitlinear_i8 (ime.rs:882-938).
