@@ -237,6 +237,7 @@ int jkb_gemm_repacked_f32_noalloc(float *out, size_t out_len, const jkb_repacked
     uint8_t *xt = s + NOALLOC_Q_BYTES + 3 * NOALLOC_G32_BYTES + NOALLOC_G16_BYTES;
     view.x_scales_t = fits ? reinterpret_cast<float *>(xt) : nullptr;
     view.x_nsums_t = fits ? reinterpret_cast<float *>(xt + NOALLOC_XT_BYTES) : nullptr;
+    view.x_nsums16_t = nullptr;  // 16-element min groups (Q2_K) take the dp4a kernel here
     rc = jkb_act_q8_quantize(&view, input, in_len, m, w->cols, stream);
     if (rc) return rc;
     return gemm_rows("gemm_repacked_f32_noalloc", out, out_len, w, &view, 0, w->rows, false,

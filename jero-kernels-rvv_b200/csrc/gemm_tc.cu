@@ -111,7 +111,7 @@ struct TcCfg {
     // the TMA loads) and the stage's shared-memory footprint
     static constexpr int STAGE_TX =
         NIB ? SAN + SMT + SB + GPS * BN * 4 + (MINS ? GPS * BN * 4 : 0)
-            : SA + SB + BMW * NG * 4 + GPS * BN * 4 + (MINS ? BMW * GPS * 4 + GPS * BN * 4 : 0);
+            : SA + SB + BMW * NG * 4 + GPS * BN * 4 + (MINS ? BMW * NG * 4 + NG * BN * 4 : 0);
     static constexpr int STAGE_SMEM =
         STAGE_TX + (H16 ? 2 * SB : 0) + (NIB ? SA + BMW * NG * 4 + (MINS ? BMW * GPS * 4 : 0) : 0);
     static constexpr int STAGES_FIT = ((NEG8 ? 184 : 200) * 1024) / STAGE_SMEM;
@@ -121,7 +121,6 @@ struct TcCfg {
     static constexpr int STAGES = STAGES_FIT > STAGES_MAX ? STAGES_MAX : STAGES_FIT;
     static_assert((COLS == 32 || COLS == 64) && BN % 32 == 0 && BN <= 256, "tile shape");
     static_assert(GPS % GPR == 0 && 2 * NA * BN <= TMEM_COLS, "two rounds of NA buffers");
-    static_assert(!(H16 && MINS), "16-element groups carry no mins");
     static_assert(!(H16 && NIB), "nibble formats use 32-element groups");
     static_assert((BMW * NG * 4) % 128 == 0 && (GPS * BN * 4) % 128 == 0 &&
                       (BMW * GPS * 4) % 128 == 0 && SAN % 128 == 0 && SMT % 128 == 0,
@@ -142,8 +141,9 @@ struct TcSmem {
     alignas(128) uint8_t mt[C::NIB ? C::STAGES : 1][C::NIB ? C::SMT : 128];  // NIB: scale words
     alignas(128) float ws[C::STAGES][BMW][C::NG];
     alignas(128) float xs[C::STAGES][GPS][C::BN];
-    alignas(128) float wm[C::MINS ? C::STAGES : 1][BMW][GPS];     // weight mins (MINS)
-    alignas(128) float xn[C::MINS ? C::STAGES : 1][GPS][C::BN];   // -x_sums, permuted like xs
+    alignas(128) float wm[C::MINS ? C::STAGES : 1][BMW][C::NG];    // weight mins (MINS)
+    // -x_sums (-x_sums_16 for 16-element groups), permuted like xs
+    alignas(128) float xn[C::MINS ? C::STAGES : 1][C::NG][C::BN];
     alignas(1024) uint8_t neg8[C::NEG8 ? C::SA : 1024];  // NEG8: a weight tile of -8
     uint64_t full[C::STAGES], empty[C::STAGES], masked[C::STAGES], tfull[2], tempty[2], done;
     uint32_t tmem_base;
@@ -472,8 +472,8 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     tma_load_2d(&sm.xs[s][0][0], &tmXS, &sm.full[s], tok, ks * GPS);
                     if (C::MINS) {
                         if (!C::NIB)
-                            tma_load_2d(&sm.wm[s][0][0], &tmWM, &sm.full[s], ks * GPS, wrow);
-                        tma_load_2d(&sm.xn[s][0][0], &tmXN, &sm.full[s], tok, ks * GPS);
+                            tma_load_2d(&sm.wm[s][0][0], &tmWM, &sm.full[s], ks * C::NG, wrow);
+                        tma_load_2d(&sm.xn[s][0][0], &tmXN, &sm.full[s], tok, ks * C::NG);
                     }
                 }
             }
@@ -643,13 +643,16 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                     ok = false;
                     break;
                 }
-                float4 w4[4][SPL], m4[4];
+                float4 w4[4][SPL], m4[4][SPL];
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
 #pragma unroll
-                    for (int v = 0; v < SPL; v++)
+                    for (int v = 0; v < SPL; v++) {
                         w4[i][v] = *reinterpret_cast<const float4 *>(&sm.ws[s][r0 + 8 * i][4 * v]);
-                    if (C::MINS) m4[i] = *reinterpret_cast<const float4 *>(&sm.wm[s][r0 + 8 * i][0]);
+                        if (C::MINS)
+                            m4[i][v] = *reinterpret_cast<const float4 *>(
+                                &sm.wm[C::MINS ? s : 0][r0 + 8 * i][4 * v]);
+                    }
                 }
                 const float *xbase = &sm.xs[s][0][slice * COLS + 4 * kq];
                 const float *nbase = &sm.xn[C::MINS ? s : 0][0][slice * COLS + 4 * kq];
@@ -695,14 +698,15 @@ __global__ void __launch_bounds__(C::THREADS, 1)
                                 const float wv = gq == 0 ? wv4.x : gq == 1 ? wv4.y : gq == 2 ? wv4.z : wv4.w;
                                 ws2[i] = pk2(__float_as_uint(wv), __float_as_uint(wv));
                                 if (C::MINS) {
-                                    const float4 &mv4 = m4[2 * h + i];
-                                    const float mv = g == 0 ? mv4.x : g == 1 ? mv4.y : g == 2 ? mv4.z : mv4.w;
+                                    // min group = weight-scale group gw (32 or 16 elements)
+                                    const float4 &mv4 = m4[2 * h + i][gw >> 2];
+                                    const float mv = gq == 0 ? mv4.x : gq == 1 ? mv4.y : gq == 2 ? mv4.z : mv4.w;
                                     wm2[i] = pk2(__float_as_uint(mv), __float_as_uint(mv));
                                 }
                             }
                             ulonglong2 nv0 = make_ulonglong2(0ull, 0ull), nv1 = nv0;
                             if (C::MINS) {
-                                const float *ng = nbase + g * BN + 32 * cb;
+                                const float *ng = nbase + gw * BN + 32 * cb;
                                 nv0 = *reinterpret_cast<const ulonglong2 *>(ng);
                                 nv1 = *reinterpret_cast<const ulonglong2 *>(ng + 16);
                             }
@@ -837,9 +841,11 @@ int launch_tc_common(const TcWeight &wt, const jkb_act_q8 *act, float *out, size
                    CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
     tmXN = tmXS;
-    if (C::MINS && !encode_2d(&tmXN, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, act->x_nsums_t,
-                              (act->m + 31) / 32 * 32, G, act->xt_pitch * 4, C::BN, GPS,
-                              CU_TENSOR_MAP_SWIZZLE_NONE))
+    // min terms: -x_sums per 32-element group, or -x_sums_16 per 16-element group (H16)
+    if (C::MINS && !encode_2d(&tmXN, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                              C::H16 ? act->x_nsums16_t : act->x_nsums_t,
+                              (act->m + 31) / 32 * 32, G * C::SPL, act->xt_pitch * 4, C::BN,
+                              C::NG, CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
     const size_t sub_n = row_end - row_begin;
     const int tiles_w = (int)((sub_n + BMW - 1) / BMW), tiles_t = (int)((act->m + C::BN - 1) / C::BN);
@@ -878,8 +884,8 @@ int launch_tc(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out, s
                    G * C::SPL * 4, C::NG, BMW, CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
     wt.tmWM = wt.tmWS;
-    if (C::MINS && !encode_2d(&wt.tmWM, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->mins, G, w->rows,
-                              G * 4, GPS, BMW, CU_TENSOR_MAP_SWIZZLE_NONE))
+    if (C::MINS && !encode_2d(&wt.tmWM, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->mins, G * C::SPL,
+                              w->rows, G * C::SPL * 4, C::NG, BMW, CU_TENSOR_MAP_SWIZZLE_NONE))
         return fail(JKB_E_CUDA, "gemm_repacked", 0, 0, 0, "cuTensorMapEncodeTiled failed");
     return launch_tc_common<C>(wt, act, out, row_begin, row_end, st, err);
 }
@@ -952,16 +958,25 @@ std::atomic<int> g_gemm_exact{0};
 // Smallest batch the tensor-core path takes (one 128-row MMA tile is mostly padding below it).
 constexpr size_t TC_MIN_M = 32;
 
+// 16-element groups with min terms (Q2_K): the 64-token tile at one group a round, the only
+// configuration that keeps its scales, mins and token sums in registers without spilling.
+template <bool E> using TC64_H16_MINS = TcCfg<64, 2, 1, E, true, true>;
+
 template <bool EXACT, bool MINS, bool H16>
 int launch_tc_bn(int bn, const jkb_repacked_weight *w, const jkb_act_q8 *act, float *out,
                  size_t row_begin, size_t row_end, cudaStream_t st, int *err) {
-    switch (bn) {
-        case 64:
-            return launch_tc<TC64<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
-        case 128:
-            return launch_tc<TC128<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
-        default:
-            return launch_tc<TC96<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
+    if constexpr (MINS && H16) {
+        return launch_tc<TC64_H16_MINS<EXACT>>(w, act, out, row_begin, row_end, st, err);
+    } else {
+        switch (bn) {
+            case 64:
+                return launch_tc<TC64<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
+            case 128:
+                return launch_tc<TC128<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st,
+                                                          err);
+            default:
+                return launch_tc<TC96<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
+        }
     }
 }
 
@@ -970,20 +985,24 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
     *used = false;
     const size_t kp = w->k_pad;
     const bool mins = w->mins != nullptr, h16 = w->group_elems == 16;
-    if ((w->group_elems != 32 && !(h16 && !mins)) || kp % BK != 0 || act->m < TC_MIN_M ||
+    const float *xn = h16 ? act->x_nsums16_t : act->x_nsums_t;  // min terms' token sums
+    if ((w->group_elems != 32 && !h16) || kp % BK != 0 || act->m < TC_MIN_M ||
         act->k_pad != kp ||
         act->m > (size_t)INT32_MAX || w->rows > (size_t)INT32_MAX || act->x_scales_t == nullptr ||
-        (mins && act->x_nsums_t == nullptr))
+        (mins && xn == nullptr))
         return JKB_OK;
     if ((((uintptr_t)w->q) & 15) || (((uintptr_t)act->q) & 15) || (((uintptr_t)w->scales) & 15) ||
         (((uintptr_t)act->x_scales_t) & 15) || (act->xt_pitch & 31) ||
-        (mins && ((((uintptr_t)w->mins) & 15) || (((uintptr_t)act->x_nsums_t) & 15))))
+        (mins && ((((uintptr_t)w->mins) & 15) || (((uintptr_t)xn) & 15))))
         return JKB_OK;
     int *err = device_error_word();
     if (!err) return JKB_OK;
     *used = true;
     const int bn = choose_tile(act->m, row_end - row_begin, mins || h16);
     const bool exact = g_gemm_exact.load(std::memory_order_relaxed);
+    if (h16 && mins)  // Q2_K: 16-element groups with min terms
+        return exact ? launch_tc_bn<true, true, true>(bn, w, act, out, row_begin, row_end, st, err)
+                     : launch_tc_bn<false, true, true>(bn, w, act, out, row_begin, row_end, st, err);
     if (h16)
         return exact ? launch_tc_bn<true, false, true>(bn, w, act, out, row_begin, row_end, st, err)
                      : launch_tc_bn<false, false, true>(bn, w, act, out, row_begin, row_end, st, err);

@@ -133,6 +133,9 @@ struct jkb_act_q8 {
     // -x_sums in the same transposed, permuted layout (the tensor-core GEMM's min term for
     // Q4_K_M weights); nullptr when x_scales_t is
     float *x_nsums_t;
+    // -x_sums_16 in the same transposed, permuted layout, [k_pad/16][xt_pitch] (the min term of
+    // 16-element groups, Q2_K); nullptr when x_scales_t is
+    float *x_nsums16_t;
     size_t xt_pitch;
 };
 

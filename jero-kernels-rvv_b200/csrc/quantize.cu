@@ -126,6 +126,7 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ a
                                                      float *__restrict__ xs16,
                                                      float *__restrict__ xs_t,
                                                      float *__restrict__ xsn_t,
+                                                     float *__restrict__ xsn16_t,
                                                      size_t xt_pitch) {
     size_t kb = kp / 32;
     size_t gid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -138,9 +139,11 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ a
     // words. Positions of tokens >= m in the last block hold 0.
     const size_t xt_at = b * xt_pitch + (r & ~(size_t)31) + 16 * ((r >> 4) & 1) +
                          4 * ((r >> 1) & 3) + 2 * ((r >> 3) & 1) + (r & 1);
+    const size_t xt16_at = xt_at + b * xt_pitch;  // 16-element group 2b (2b + 1 one row on)
     if (r >= m) {
         xs_t[xt_at] = 0.0f;
         xsn_t[xt_at] = 0.0f;
+        if (xsn16_t) xsn16_t[xt16_at] = xsn16_t[xt16_at + xt_pitch] = 0.0f;
         return;
     }
     const float *src = act + r * k;
@@ -188,6 +191,10 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ a
     if (xs_t) {
         xs_t[xt_at] = d;
         xsn_t[xt_at] = -s;
+        if (xsn16_t) {
+            xsn16_t[xt16_at] = -h0;
+            xsn16_t[xt16_at + xt_pitch] = -h1;
+        }
     }
     xsum[r * kb + b] = s;
     xs16[r * (kp / 16) + 2 * b] = h0;
@@ -611,7 +618,7 @@ int jkb_act_q8_create(size_t m_capacity, size_t k, jkb_act_q8 **out) {
     size_t qb = m_capacity * a->k_pad, fb = m_capacity * kb * 4, f16b = m_capacity * kc * 4,
            sb = m_capacity * nsb * 4, tb = a->xt_pitch * kb * 4;
     ar.cap = Arena::round(qb) + 2 * Arena::round(fb) + Arena::round(f16b) + Arena::round(sb) +
-             2 * Arena::round(tb);
+             2 * Arena::round(tb) + Arena::round(2 * tb);
     cudaError_t e = cudaMalloc(&ar.base, ar.cap);
     if (e != cudaSuccess) {
         delete a;
@@ -625,6 +632,7 @@ int jkb_act_q8_create(size_t m_capacity, size_t k, jkb_act_q8 **out) {
     a->super_scales = (float *)ar.take(sb);
     a->x_scales_t = (float *)ar.take(tb);
     a->x_nsums_t = (float *)ar.take(tb);
+    a->x_nsums16_t = (float *)ar.take(2 * tb);
     *out = a;
     return JKB_OK;
 }
@@ -657,7 +665,8 @@ int jkb_act_q8_quantize(jkb_act_q8 *a, const float *input, size_t in_len, size_t
     act_q8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(input, m, k, a->k_pad, a->q,
                                                                a->x_scales, a->x_sums,
                                                                a->x_sums_16, a->x_scales_t,
-                                                               a->x_nsums_t, a->xt_pitch);
+                                                               a->x_nsums_t, a->x_nsums16_t,
+                                                               a->xt_pitch);
     int rc = check_launch("act_q8_kernel");
     if (rc) return rc;
     size_t ns = m * nsb;
