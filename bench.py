@@ -1,25 +1,28 @@
 #!/usr/bin/env python
 """Benchmark of the jero-kernels-rvv quantized-matmul hot path on B200 (sm_100a).
 
-Default workload: the Llama-3-8B decode GEMV set at batch 1 --
-Q4_K_M q/o 4096->4096, k/v 4096->1024, gate/up 4096->14336, down 14336->4096 and the Q6_K
-lm_head 4096->128256, each fed by its own Q8_K-quantized activation. One step quantizes the
-five f32 activation vectors to Q8_K and runs the eight GEMVs through the C ABI (jkb200): the
-layer matrices with the f32-input entries (vec_dot_q4_k_m_rvv, the quantization inside the
-GEMV launch), the matrices that share an input in one grouped launch -- q/k/v, o, gate/up,
-down -- as a decoder layer allows, and the lm_head as quantize_row_q8_k + gemv_q6_k_q8_k
-(--prequant picks which inputs get their own quantize launch; measured best: the lm_head's);
-with --unfused as five quantize launches plus eight GEMV launches. Weights are synthetic N(0, 0.02) rows quantized
-by this file's numpy quantizers (a seeded pool of rows tiled to full size; GEMV time does not
-depend on the values), activations N(0, 1).
+Headline workload (`--workload 8b`): the Llama-3-8B decode GEMV set at
+batch 1 -- Q4_K_M q/o 4096->4096, k/v 4096->1024, gate/up 4096->14336, down 14336->4096 and the
+Q6_K lm_head 4096->128256, each fed by its own Q8_K-quantized activation. One step runs the
+matrices through the C ABI (jkb200), grouped by the activation stream that feeds them, as a
+decoder layer allows (q/k/v, o, gate/up, down, lm_head): the layer groups with the f32-input
+entries (vec_dot_grouped_rvv, the quantization inside the GEMV launch) and the lm_head as
+quantize_row_q8_k + gemv_q6_k_q8_k (--prequant picks which streams get their own quantize
+launch); with --unfused as five quantize launches plus eight GEMV launches. Weights are
+synthetic N(0, 0.02) rows quantized by this file's numpy quantizers (a seeded pool of rows tiled
+to full size; GEMV time does not depend on the values), activations N(0, 1).
 
-Metric: algorithmic bytes per step (GGUF weight blocks + Q8_K activation blocks + f32 outputs,
-the BASELINE.md table) / step time, in GB/s. The seven layer matrices exist in two copies used
-on alternate steps and the lm_head is 431 MB, so every step streams 554 MB (> 4x the 126 MB L2).
+Metric: algorithmic bytes per step (GGUF weight blocks + Q8_K activation blocks + f32 outputs)
+/ step time, in GB/s. The seven layer matrices exist in two copies used on alternate steps and
+the lm_head is 431 MB, so every step streams 554 MB (> 4x the 126 MB L2).
 
 With --gpus N (torchrun, one rank per GPU) every matrix is sharded by output rows; each rank
-runs its slices and one NCCL all-gather per step collects the output slices on every rank
-(strong scaling: the same total work at every N).
+runs its slices, and one launch of this library's all-gather kernel per step pushes the output
+slices to every peer over NVLink (--collective nccl: one NCCL all-gather instead). Strong
+scaling: the same total work at every N.
+
+Sections of the same JSON line: the Llama-3-70B decode set at batch 1 and 16, the
+Q4_0 GEMV, the Q8_0 prefill GEMM and BitNet BitLinear.
 
 `--impl reference` times the CPU restatement of the reference's scalar path (oracle/) on all
 host cores over the same workload (rank 0 only).
@@ -39,8 +42,9 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "jero-kernels-rvv_b200"))
 
-Q4_K, Q6_K, Q8_0, TQ2_0, I2_S = 12, 14, 8, 35, 36
-BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), Q8_0: (32, 34), TQ2_0: (256, 66), I2_S: (128, 32)}
+Q4_0, Q4_K, Q6_K, Q8_0, TQ2_0, I2_S = 2, 12, 14, 8, 35, 36
+BLOCK = {Q4_0: (32, 18), Q4_K: (256, 144), Q6_K: (256, 210), Q8_0: (32, 34), TQ2_0: (256, 66),
+         I2_S: (128, 32)}
 # BitNet-b1.58-2B FFN: hidden 2560, intermediate 6912
 BITNET_HIDDEN, BITNET_FFN = 2560, 6912
 
@@ -52,7 +56,25 @@ DECODE_8B = [
     ("ffn_down", Q4_K, 4096, 14336, "a"), ("lm_head", Q6_K, 128256, 4096, "f"),
 ]
 ACTS = {"x": 4096, "attn": 4096, "h": 4096, "a": 14336, "f": 4096}
-LAYER_COPIES = 2
+# Llama-3-70B decode: Q4_K_M gate/up 8192->28672, down 28672->8192, Q6_K
+# lm_head 8192->128256, weights N(0, 0.015), batch 1 and 16, sharded over 1/2/4/8 GPUs
+DECODE_70B = [
+    ("ffn_gate", Q4_K, 28672, 8192, "h"), ("ffn_up", Q4_K, 28672, 8192, "h"),
+    ("ffn_down", Q4_K, 8192, 28672, "a"), ("lm_head", Q6_K, 128256, 8192, "f"),
+]
+ACTS_70B = {"h": 8192, "a": 28672, "f": 8192}
+DECODE_SETS = {
+    "8b": {"key": "llama3_8b_decode", "config": "configs[1]", "mats": DECODE_8B, "acts": ACTS,
+           "copies": 2, "sigma": 0.02, "workload": "llama3-8b-decode-gemv-set",
+           "lm_profile": "gemv_q6_k_lm_head_4096x128256",
+           "l2": "inputs larger than L2 (554 MB per step, layer weights in 2 alternating "
+                 "copies)"},
+    "70b": {"key": "llama3_70b_decode", "config": "configs[4]", "mats": DECODE_70B,
+            "acts": ACTS_70B, "copies": 1, "sigma": 0.015, "batch16": True,
+            "workload": "llama3-70b-decode-gemv-set",
+            "lm_profile": "gemv_q6_k_lm_head_4096x128256",
+            "l2": "inputs larger than L2 (1.26 GB per step)"},
+}
 POOL_ROWS = 512
 
 
@@ -136,24 +158,43 @@ def quantize_q8_0(w: np.ndarray) -> np.ndarray:
     return out.reshape(-1)
 
 
-QUANTIZERS = {Q4_K: quantize_q4_k, Q6_K: quantize_q6_k, Q8_0: quantize_q8_0}
+def quantize_q4_0(w: np.ndarray) -> np.ndarray:
+    """Q4_0 blocks from f32 rows: the signed value of largest magnitude over -8 as the f16 block
+    scale, q = min(15, trunc(x / d + 8.5)) in f32 (the oracle's rule, written with numpy)."""
+    R, K = w.shape
+    x = np.ascontiguousarray(w, np.float32).reshape(R, K // 32, 32)
+    mx = np.take_along_axis(x, np.abs(x).argmax(-1)[..., None], -1)[..., 0]
+    d = (mx / np.float32(-8.0)).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        idv = np.where(d != 0, np.float32(1.0) / d, np.float32(0.0)).astype(np.float32)
+    q = np.trunc((x * idv[..., None]).astype(np.float32) + np.float32(8.5)).clip(0, 15)
+    q = q.astype(np.uint8)
+    out = np.zeros((R, K // 32, 18), np.uint8)
+    out[..., 0:2] = _f16(d).view(np.uint8).reshape(R, K // 32, 2)
+    out[..., 2:] = q[..., :16] | (q[..., 16:] << 4)
+    return out.reshape(-1)
 
 
-def synth_matrix(quant, rows, cols, seed, row_begin=0, row_end=None):
-    """GGUF bytes of rows [row_begin, row_end) of a seeded N(0, 0.02) matrix: a pool of
+QUANTIZERS = {Q4_0: quantize_q4_0, Q4_K: quantize_q4_k, Q6_K: quantize_q6_k, Q8_0: quantize_q8_0}
+
+
+def synth_matrix(quant, rows, cols, seed, row_begin=0, row_end=None, sigma=0.02):
+    """GGUF bytes of rows [row_begin, row_end) of a seeded N(0, sigma) matrix: a pool of
     POOL_ROWS quantized rows tiled over the matrix."""
     row_end = rows if row_end is None else row_end
     rng = np.random.default_rng(seed)
-    pool = rng.standard_normal((min(POOL_ROWS, rows), cols), dtype=np.float32) * np.float32(0.02)
+    pool = rng.standard_normal((min(POOL_ROWS, rows), cols), dtype=np.float32) * np.float32(sigma)
     qp = QUANTIZERS[quant](pool).reshape(pool.shape[0], -1)
     idx = np.arange(row_begin, row_end) % pool.shape[0]
     return np.ascontiguousarray(qp[idx]).reshape(-1)
 
 
-def algorithmic_bytes(quant, rows, cols):
+def algorithmic_bytes(quant, rows, cols, batch=1):
+    """GGUF weight block bytes + per token the Q8 activation blocks (Q8_K for the K-quants,
+    Q8_0 otherwise) and the f32 outputs."""
     be, bb = BLOCK[quant]
     act = cols // 256 * 292 if quant in (Q4_K, Q6_K) else cols // 32 * 36
-    return rows * (cols // be) * bb + act + 4 * rows
+    return rows * (cols // be) * bb + batch * (act + 4 * rows)
 
 
 # ----------------------------------------------------------------------------- helpers
@@ -233,28 +274,47 @@ def cpu_oracle_step(O, mats, xq, nthreads):
         O.gemv_mt(quant, w, rows, cols, xq[stream], nthreads)
 
 
-def cpu_workload(O, frac_rows=1.0):
-    """The decode workload restricted to the first frac of each matrix's rows (CPU arms)."""
+def cpu_workload(O, spec):
+    """The whole decode set on the host (CPU arms): every matrix once (the host has no L2 to
+    defeat at this size), the Q8_K activations of the same seeded streams."""
     mats = []
-    for i, (name, quant, rows, cols, stream) in enumerate(DECODE_8B):
-        r = max(4, int(rows * frac_rows) // 4 * 4)
-        mats.append((name, quant, r, cols, stream, synth_matrix(quant, rows, cols, 1000 + i, 0, r)))
+    for i, (name, quant, rows, cols, stream) in enumerate(spec["mats"]):
+        mats.append((name, quant, rows, cols, stream,
+                     synth_matrix(quant, rows, cols, 1000 + i, sigma=spec["sigma"])))
     rng = np.random.default_rng(7)
-    xq = {s: O.quantize_row_q8_k(rng.standard_normal(n, dtype=np.float32)) for s, n in ACTS.items()}
+    xq = {s: O.quantize_row_q8_k(rng.standard_normal(n, dtype=np.float32))
+          for s, n in spec["acts"].items()}
     nbytes = sum(algorithmic_bytes(q, r, c) for _, q, r, c, _, _ in mats)
     return mats, xq, nbytes
 
 
+def cpu_model():
+    """The host CPU's model name (/proc/cpuinfo), or the platform's processor string."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.lower().startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def run_reference(args):
+    """The reference's scalar path (the oracle's C restatement; the Rust crate cannot be built
+    here) on the host cores, on the same workload, metric and config as the GPU arm: each step
+    is one whole decode step, every matrix's rows split over all host threads (the reference's
+    own row-range parallelism, gemv_repacked_rows repack.rs:4014). Rank 0 only."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import pyoracle as O
 
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    spec = DECODE_SETS[args.workload]
     cores = os.cpu_count() or 1
-    frac = 0.125
-    mats, xq, nbytes = cpu_workload(O, frac)
+    mats, xq, nbytes = cpu_workload(O, spec)
     for _ in range(args.warmup):
         cpu_oracle_step(O, mats, xq, cores)
     t0 = time.perf_counter()
@@ -262,29 +322,28 @@ def run_reference(args):
         cpu_oracle_step(O, mats, xq, cores)
     dt = (time.perf_counter() - t0) / args.steps
     gbs = nbytes / dt / 1e9
-    sample = (f"each step: rows [0, {frac:g} * N) of every GEMV of the decode set "
-              f"({nbytes / 1e6:.1f} MB), oracle scalar port, row-range split over {cores} threads")
+    sample = (f"{args.steps} whole decode steps ({nbytes / 1e6:.1f} MB each), oracle scalar "
+              f"port, every matrix's rows split over {cores} threads")
     print(json.dumps({
         "impl": "reference", "metric": "quant GEMV weight GB/s", "value": round(gbs, 3),
         "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8 dot / f32 scale", "data": "synthetic",
-        "config": {"workload": "llama3-8b-decode-gemv-set (sampled rows)", "batch": 1},
+        "config": decode_config(spec, args.gpus, args.collective == "peer"),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores,
-                         "kind": "port", "sample": sample},
+                         "kind": "port", "sample": sample, "cpu_model": cpu_model()},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
-def cpu_baseline_single():
-    """Oracle port on one host core over a bounded sample of the decode workload, repeated for
+def cpu_baseline_single(spec):
+    """Oracle port on one host core over whole decode steps of the same workload, repeated for
     about 10 s."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import pyoracle as O
 
-    frac = 1 / 16
-    mats, xq, nbytes = cpu_workload(O, frac)
+    mats, xq, nbytes = cpu_workload(O, spec)
     n, t0 = 0, time.perf_counter()
     while True:
         cpu_oracle_step(O, mats, xq, 1)
@@ -293,11 +352,269 @@ def cpu_baseline_single():
             break
     dt = (time.perf_counter() - t0) / n
     return {"value": round(nbytes / dt / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"{n} passes over rows [0, N/16) of each decode GEMV "
-                      f"({nbytes / 1e6:.1f} MB per pass), single thread"}
+            "cpu_model": cpu_model(),
+            "sample": f"{n} whole decode steps ({nbytes / 1e6:.1f} MB each), single thread"}
 
 
 # ----------------------------------------------------------------------------- GPU arm
+
+class DecodeSet:
+    """This rank's part of one decode GEMV set (BASELINE configs[1] or configs[4]): the output-row
+    shard of every matrix as a jkb200 Weight, the f32 activation streams in one device buffer,
+    and the calls of one step through the public API.
+
+    A step runs, per activation stream in order, the matrices that stream feeds (a decoder layer
+    computes q/k/v from one input, gate/up from another, ...):
+      * batch 1, streams not in `prequant`: one f32-input launch, grouped when several matrices
+        share the stream (vec_dot_grouped_rvv; the input is quantized to Q8_K inside the launch);
+      * batch 1, streams in `prequant` (default: the lm_head's): quantize_row_q8_k, then one
+        pre-quantized gemv_rows launch per matrix;
+      * batch m > 1: quantize_rows_q8_k of the m tokens, then one gemv_batch launch per matrix;
+      * `unfused`: every stream quantized by its own launch, one GEMV launch per matrix.
+    With world > 1 the output shards are collected once per step, by the library's all-gather
+    kernel over NVLink peer memory (`peer`) or by one NCCL all-gather.
+    Layer matrices can exist in `layer_copies` copies used on alternate steps, so that a step
+    never finds its weights in the L2."""
+
+    def __init__(self, jkb, mats, acts, world, rank, *, peer=True, batch=1, layer_copies=1,
+                 prequant=("f",), unfused=False, seed=1000, sigma=0.02):
+        import torch
+        from jkb200.shard import PeerOutputs, ShardedOutputs
+
+        self.jkb, self.mats, self.acts = jkb, mats, acts
+        self.world, self.rank, self.batch = world, rank, batch
+        self.peer = peer and world > 1
+        self.unfused, self.prequant = unfused, set(prequant) - {""}
+        names = [(name, rows) for name, _, rows, _, _ in mats]
+        self.outs = (PeerOutputs(names, world, rank, batch=batch) if self.peer
+                     else ShardedOutputs(names, world, rank, batch=batch))
+        self.weights, self.shards, self.bytes_per_step = {}, [], 0
+        for i, (name, quant, rows, cols, s) in enumerate(mats):
+            rr = self.outs.rows_of(name)
+            self.bytes_per_step += algorithmic_bytes(quant, rows, cols, batch)
+            copies = 1 if name == "lm_head" else layer_copies
+            for c in range(copies):
+                raw = synth_matrix(quant, rows, cols, seed + i + 97 * c, rr.start, rr.stop, sigma)
+                self.weights[(name, c)] = jkb.Weight(
+                    jkb.TensorView(f"{name}.{c}", quant, [len(rr), cols], raw), len(rr), cols)
+            self.shards.append((name, quant, len(rr), cols, s, copies))
+        g = torch.Generator(device="cpu").manual_seed(7)
+        # all activation streams in one device buffer: the e2e loop moves a step's inputs with
+        # one host-to-device copy
+        self.x_all = torch.cat([torch.randn(batch * n, generator=g) for n in acts.values()]).cuda()
+        self.xs, self.xq, off = {}, {}, 0
+        for s, n in acts.items():
+            self.xs[s] = self.x_all[off:off + batch * n]
+            self.xq[s] = jkb.empty_q8_k_blocks(batch * n // 256)
+            off += batch * n
+        self.groups = {}  # activation stream -> matrices fed by it, in mats order
+        for name, quant, per, cols, s, copies in self.shards:
+            self.groups.setdefault(s, []).append((name, copies))
+        self.lm_stream = mats[-1][4]
+        self.launches_per_step = self._count_launches()
+
+    def _count_launches(self):
+        n = 1 if self.peer else 0
+        for s, items in self.groups.items():
+            if self.batch > 1 or self.unfused or s in self.prequant:
+                n += 1 + len(items)
+            else:
+                n += 1
+        return n
+
+    def lslice(self, name, i):
+        return self.outs.local_slice(name, i % 2) if self.peer else self.outs.local_slice(name)
+
+    def run_group(self, s, i):
+        jkb = self.jkb
+        items = [(self.lslice(n, i), self.weights[(n, i % c)]) for n, c in self.groups[s]]
+        if self.batch > 1:
+            jkb.quantize_rows_q8_k(self.xs[s], self.batch, self.acts[s], self.xq[s])
+            for out, w in items:
+                jkb.gemv_batch(out, w, self.xq[s], self.batch)
+        elif self.unfused or s in self.prequant:
+            jkb.quantize_row_q8_k(self.xs[s], self.xq[s])
+            for out, w in items:
+                jkb.gemv_rows(out, w, self.xq[s], range(0, w.rows))
+        else:
+            jkb.vec_dot_grouped_rvv(items, self.xs[s])
+
+    def layer_part(self, i):
+        for s in self.groups:
+            if s != self.lm_stream:
+                self.run_group(s, i)
+
+    def collect(self, i):
+        if self.peer:
+            self.outs.gather(i % 2)
+        else:
+            self.outs.gather()
+
+    def step(self, i, marks=None, stream=None):
+        """One step. `marks`: 4 events recorded before the layer GEMVs, before the lm_head group,
+        after it and after the collection of the shards."""
+        if marks is not None:
+            marks[0].record(stream)
+        self.layer_part(i)
+        if marks is not None:
+            marks[1].record(stream)
+        self.run_group(self.lm_stream, i)
+        if marks is not None:
+            marks[2].record(stream)
+        self.collect(i)
+        if marks is not None:
+            marks[3].record(stream)
+
+    def output(self, name, i):
+        """Full output of matrix `name` after step i: [rows], or [batch][rows]."""
+        if self.peer:
+            return self.outs.output(name, i % 2)
+        if self.world == 1:
+            t = self.outs.local_slice(name)
+            return t if self.batch == 1 else t.view(self.batch, -1)
+        return self.outs.output(name)
+
+    def full(self, i):
+        """The buffer holding every matrix's full output after step i (the e2e read-back)."""
+        if self.peer:
+            return self.outs.full(i % 2)
+        return self.outs.gathered
+
+    def destroy(self):
+        for w in self.weights.values():
+            w.destroy()
+        if self.peer:
+            self.outs.destroy()
+
+
+def _max_over_ranks(v, world, op="max"):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.MIN)
+    return float(t.item())
+
+
+def time_decode(ds, steps, warmup, stream, world, local=0, sample_clocks=False):
+    """Times `steps` decode steps of DecodeSet `ds` captured as one CUDA graph (a launch-bound
+    loop), with CUDA events on the launching stream, max over ranks. A second graph of the same
+    steps carries events at the group boundaries of every step (layer GEMVs | lm_head group |
+    collection of the shards): an event between two kernels ends the programmatic overlap of
+    their launches, so it is timed separately and gives the split, not the headline."""
+    import torch
+    import torch.distributed as dist
+
+    for i in range(warmup):  # eager warm-up (also sets kernel attributes)
+        ds.step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    marks = [[torch.cuda.Event(enable_timing=True, external=True) for _ in range(4)]
+             for _ in range(steps)]
+    graph, graph_ev = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(steps):
+            ds.step(i)
+    with torch.cuda.graph(graph_ev, stream=stream):
+        for i in range(steps):
+            ds.step(i, marks[i], stream)
+    graph.replay()  # untimed first replays (graph upload)
+    graph_ev.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks, sampler = None, None
+    if sample_clocks:
+        t_start.record(stream)
+        graph.replay()
+        t_end.record(stream)
+        torch.cuda.synchronize()
+        # nvidia-smi samples every 100 ms and the timed replay lasts milliseconds: about 0.5 s of
+        # untimed replays of the same graph run right before it, so the clock samples are taken
+        # under this workload.
+        n_load = max(1, int(500.0 / max(t_start.elapsed_time(t_end), 1e-3)))
+        sampler = ClockSampler(local)
+        sampler.start()
+        time.sleep(0.2)
+        for _ in range(n_load):
+            graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_start.record(stream)
+    graph.replay()  # the K timed steps
+    t_end.record(stream)
+    graph_ev.replay()  # K more steps with the split events, under the same clocks
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    if sampler is not None:
+        clocks = sampler.stop()
+        clocks["window"] = (f"nvidia-smi every 100 ms over {n_load} untimed replays of the timed "
+                            "graph and the timed replays")
+    ms = _max_over_ranks(t_start.elapsed_time(t_end), world)
+    split = [sum(m[j].elapsed_time(m[j + 1]) for m in marks) / steps for j in range(3)]
+    split = [_max_over_ranks(v, world) for v in split]
+    del graph, graph_ev
+    return {"ms_step": ms / steps, "layer_ms": split[0], "lm_head_ms": split[1],
+            "gather_ms": split[2], "clocks": clocks}
+
+
+def e2e_decode(ds, steps, warmup, world):
+    """The same steps through the public API with host buffers: every step copies its f32 inputs
+    in from pinned host memory and its full outputs out to pinned host memory, eager launches,
+    timed with CUDA events on the launching stream (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    host_in = ds.x_all.cpu().pin_memory()
+    host_out = torch.empty(ds.full(0).numel(), dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        ds.x_all.copy_(host_in, non_blocking=True)
+        ds.step(i)
+        host_out.copy_(ds.full(i), non_blocking=True)
+
+    for i in range(warmup):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(warmup, warmup + steps):  # step numbers continue, so output slots alternate
+        e2e_step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1), world)
+    return {"ms_step": ms / steps, "h2d_bytes_per_step": host_in.numel() * 4,
+            "d2h_bytes_per_step": host_out.numel() * 4}
+
+
+def decode_section(jkb, spec, world, rank, stream, steps, warmup, batch, peer):
+    """configs[4]-style numbers for one decode set and batch: GB/s of the whole job, the
+    fraction of measured HBM per GPU, and the per-step split (max over ranks)."""
+    mats, acts, copies, sigma = spec["mats"], spec["acts"], spec["copies"], spec["sigma"]
+    ds = DecodeSet(jkb, mats, acts, world, rank, peer=peer, batch=batch, layer_copies=copies,
+                   sigma=sigma)
+    t = time_decode(ds, steps, warmup, stream, world)
+    peak, _ = measured_peaks()
+    gbs = ds.bytes_per_step / (t["ms_step"] * 1e-3) / 1e9
+    res = {"batch": batch, "bytes_per_step": ds.bytes_per_step,
+           "us_per_step": round(t["ms_step"] * 1e3, 2), "gbs": round(gbs, 1),
+           "hbm_frac_per_gpu": round(gbs / world / peak, 4),
+           "split_us": {"layer_gemvs": round(t["layer_ms"] * 1e3, 2),
+                        "lm_head": round(t["lm_head_ms"] * 1e3, 2),
+                        "gather": round(t["gather_ms"] * 1e3, 2)},
+           "launches_per_step": ds.launches_per_step}
+    ds.destroy()
+    return res
+
 
 def run_gpu(args):
     import torch
@@ -313,235 +630,138 @@ def run_gpu(args):
                                 device_id=torch.device("cuda", local))
     import jkb200 as jkb
 
-    from jkb200.shard import PeerOutputs, ShardedOutputs
-
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
-    # --- weights: this rank's row shard of every matrix (layer matrices in two copies). With
-    # N > 1 the slices are collected either by one all-gather kernel of this library per step
-    # (peer: the rows pushed to every peer over NVLink, then a bounded wait for the peers' rows)
-    # or by one NCCL all-gather per step (nccl)
-    mats = [(name, rows) for name, _, rows, _, _ in DECODE_8B]
-    peer = world > 1 and args.collective == "peer"
-    outs = PeerOutputs(mats, world, rank) if peer else ShardedOutputs(mats, world, rank)
-
-    def lslice(name, i):
-        return outs.local_slice(name, i % 2) if peer else outs.local_slice(name)
-    shards, weights, total_bytes = [], {}, 0
-    for i, (name, quant, rows, cols, s) in enumerate(DECODE_8B):
-        rr = outs.rows_of(name)
-        per = len(rr)
-        total_bytes += algorithmic_bytes(quant, rows, cols)
-        copies = 1 if name == "lm_head" else LAYER_COPIES
-        for c in range(copies):
-            raw = synth_matrix(quant, rows, cols, 1000 + i + 97 * c, rr.start, rr.stop)
-            weights[(name, c)] = jkb.Weight(jkb.TensorView(f"{name}.{c}", quant, [per, cols], raw),
-                                            per, cols)
-        shards.append((name, quant, per, cols, s, copies))
-    g = torch.Generator(device="cpu").manual_seed(7)
-    # the five f32 activation streams live in one device buffer, so that the e2e loop moves a
-    # step's inputs with one host-to-device copy
-    x_all = torch.cat([torch.randn(n, generator=g) for n in ACTS.values()]).cuda()
-    xs, off = {}, 0
-    for s, n in ACTS.items():
-        xs[s] = x_all[off:off + n]
-        off += n
-    xq = {s: jkb.empty_q8_k_blocks(n // 256) for s, n in ACTS.items()}
-    groups = {}  # activation stream -> matrices fed by it, in DECODE_8B order
-    for name, quant, per, cols, s, copies in shards:
-        groups.setdefault(s, []).append((name, quant, copies))
-
-    prequant = set(args.prequant.split(",")) - {""}
-
-    def run_group(s, i):
-        """The matrices sharing activation s: one f32-input launch (grouped when several), or,
-        for the streams in --prequant, quantize_row_q8_k followed by gemv_*_q8_k per matrix."""
-        if s in prequant:
-            jkb.quantize_row_q8_k(xs[s], xq[s])
-            for n, _, c in groups[s]:
-                w = weights[(n, i % c)]
-                jkb.gemv_rows(lslice(n, i), w, xq[s], range(0, w.rows))
-            return
-        items = [(lslice(n, i), weights[(n, i % c)]) for n, _, c in groups[s]]
-        jkb.vec_dot_grouped_rvv(items, xs[s])
-
-    def layer_part(i):
-        if not args.unfused:
-            for s in ("x", "attn", "h", "a"):
-                run_group(s, i)
-            return
-        for s in ACTS:
-            jkb.quantize_row_q8_k(xs[s], xq[s])
-        for name, quant, per, cols, s, copies in shards:
-            if name == "lm_head":
-                continue
-            jkb.gemv_rows(lslice(name, i), weights[(name, i % copies)], xq[s], range(0, per))
-
-    def lm_head(i):
-        if not args.unfused:
-            run_group("f", i)
-            return
-        jkb.gemv_rows(lslice("lm_head", i), weights[("lm_head", 0)], xq["f"],
-                      range(0, shards[-1][2]))
-
-    def collect(i):
-        if peer:
-            outs.gather(i % 2)
-        else:
-            outs.gather()
-
-    def step(i, evs=None):
-        layer_part(i)
-        if evs is not None:
-            evs[0].record(stream)
-        lm_head(i)
-        if evs is not None:
-            evs[1].record(stream)
-        collect(i)
-
-    for i in range(args.warmup):  # eager warm-up (also sets kernel attributes)
-        step(i)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    # The K timed steps are captured as one CUDA graph (launch-bound loop). A second graph of the
-    # same K steps carries external timing events around every lm_head GEMV, so the dominant
-    # kernel is timed on its own stream; it is kept out of the first graph because an event
-    # between two kernels ends the programmatic overlap of their launches.
-    evs = [(torch.cuda.Event(enable_timing=True, external=True),
-            torch.cuda.Event(enable_timing=True, external=True)) for _ in range(args.steps)]
-    graph, graph_ev = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for i in range(args.steps):
-            step(i)
-    with torch.cuda.graph(graph_ev, stream=stream):
-        for i in range(args.steps):
-            step(i, evs[i])
-    graph.replay()  # untimed first replays (graph upload)
-    graph_ev.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t_start.record(stream)
-    graph.replay()
-    t_end.record(stream)
-    torch.cuda.synchronize()
-    # nvidia-smi samples every 100 ms and the timed replay lasts milliseconds: about 0.5 s of
-    # untimed replays of the same graph run right before it, so the clock samples are taken
-    # under this workload.
-    n_load = max(1, int(500.0 / max(t_start.elapsed_time(t_end), 1e-3)))
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.2)
-    for _ in range(n_load):
-        graph.replay()
-    t_start.record(stream)
-    graph.replay()  # the K timed steps
-    t_end.record(stream)
-    graph_ev.replay()  # K more steps with the lm_head timing events, under the same clocks
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clocks = sampler.stop()
-    clocks["window"] = (f"nvidia-smi every 100 ms over {n_load} untimed replays of the timed "
-                        "graph and the timed replays")
-    ms = t_start.elapsed_time(t_end)
-    lm_ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / args.steps
+    peer = args.collective == "peer"
+    spec = DECODE_SETS[args.workload]
+    # --- the headline: this rank's row shard of every matrix of the decode set
+    ds = DecodeSet(jkb, spec["mats"], spec["acts"], world, rank, peer=peer,
+                   layer_copies=spec["copies"], prequant=args.prequant.split(","),
+                   unfused=args.unfused, sigma=spec["sigma"])
+    t = time_decode(ds, args.steps, args.warmup, stream, world, local, sample_clocks=True)
+    total_bytes = ds.bytes_per_step
+    ms_step = t["ms_step"]
     value = total_bytes / (ms_step * 1e-3) / 1e9
-
-    # --- e2e: the public API with host buffers (pinned f32 inputs in, f32 outputs out)
-    host_in = x_all.cpu().pin_memory()
-    full = (lambda i: outs.full(i % 2)) if peer else (lambda i: outs.gathered)
-    host_out = torch.empty(full(0).numel(), dtype=torch.float32).pin_memory()
-    h2d = host_in.numel() * 4
-    d2h = full(0).numel() * 4
-
-    def e2e_step(i):
-        x_all.copy_(host_in, non_blocking=True)
-        layer_part(i)
-        lm_head(i)
-        collect(i)
-        host_out.copy_(full(i), non_blocking=True)
-
-    for i in range(args.warmup):
-        e2e_step(i)
+    e2e = e2e_decode(ds, args.steps, args.warmup, world)
+    e2e_val = total_bytes / (e2e["ms_step"] * 1e-3) / 1e9
+    launches = ds.launches_per_step
+    ds.destroy()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        e2e_step(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    e2e_val = total_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
 
+    sections = {}
+    if not args.no_sections:
+        other = "70b" if args.workload == "8b" else "8b"
+        sections[DECODE_SETS[other]["key"]] = {
+            "config": DECODE_SETS[other]["config"],
+            "batch1": decode_section(jkb, DECODE_SETS[other], world, rank, stream, args.steps,
+                                     args.warmup, 1, peer)}
+        for key, sp in DECODE_SETS.items():
+            if sp.get("batch16"):
+                sec = sections.setdefault(sp["key"], {"config": sp["config"]})
+                sec["batch16"] = decode_section(jkb, sp, world, rank, stream,
+                                                max(4, args.steps // 4), args.warmup, 16, peer)
+        sections["q4_0_gemv_4096"] = run_q4_0_gemv(jkb, world)
     prefill = None if args.no_gemm else run_prefill_gemm(world, rank)
     bitnet = None if args.no_bitnet else run_bitnet(world, rank)
 
     if rank == 0:
         peak, peak_kind = measured_peaks()
-        lm_q, lm_rows, lm_cols = Q6_K, DECODE_8B[-1][2], DECODE_8B[-1][3]
+        lm_q, lm_rows, lm_cols = spec["mats"][-1][1:4]
         lm_bytes = algorithmic_bytes(lm_q, lm_rows, lm_cols) / world
+        lm_ms = t["lm_head_ms"]
         achieved = lm_bytes / (lm_ms * 1e-3) / 1e9
-        traffic = profile_traffic("gemv_q6_k_lm_head_4096x128256")
+        # DRAM bytes per launch of the ncu capture, scaled from the 8B lm_head (431,457,856
+        # algorithmic bytes) to this launch's algorithmic bytes
+        traffic = profile_traffic(spec["lm_profile"])
+        if traffic is not None:
+            traffic = round(traffic * lm_bytes / algorithmic_bytes(Q6_K, 128256, 4096))
+        lm_kernel = ("gemv_kernel<FQ6_K, ActQ8K>" if args.unfused or "f" in args.prequant
+                     else "gemv_kernel<FQ6_K, ActQ8KF32>")
         res = {
             "metric": "quant GEMV weight GB/s", "value": round(value, 2), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8 dot / f32 scale", "data": "synthetic",
-            "config": {"workload": "llama3-8b-decode-gemv-set (BASELINE configs[1])",
-                       "batch": 1, "weights": "Q4_K_M layers + Q6_K lm_head",
-                       "bytes_per_step": total_bytes,
-                       "l2": "inputs larger than L2 (554 MB per step, layer weights in 2 "
-                             "alternating copies)",
-                       "parallelism": f"row-shard x{world}" + (
-                           "" if world == 1 else
-                           " + one-kernel all-gather over NVLink peer memory" if peer
-                           else " + NCCL all-gather")},
+            "config": decode_config(spec, world, peer),
+            "split_us": {"layer_gemvs": round(t["layer_ms"] * 1e3, 2),
+                         "lm_head": round(t["lm_head_ms"] * 1e3, 2),
+                         "gather": round(t["gather_ms"] * 1e3, 2),
+                         "note": "a second graph of the same steps with events at the group "
+                                 "boundaries (events end the launch overlap there)"},
             "roofline": {"bound": "hbm",
-                         "kernel": ("gemv_kernel<FQ6_K, ActQ8K>" if args.unfused or "f" in prequant
-                                    else "gemv_kernel<FQ6_K, ActQ8KF32>") + " lm_head 4096->128256",
+                         "kernel": f"{lm_kernel} lm_head {lm_cols}->{lm_rows}"
+                                   + (f" (row shard 1/{world})" if world > 1 else ""),
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": traffic, "algorithmic_bytes": lm_bytes,
-                         "avg_ms": round(lm_ms, 5)},
-            "gpu_launches": args.steps * ((len(ACTS) + len(DECODE_8B) if args.unfused
-                                           else len(groups) + sum(len(groups[s]) for s in prequant))
-                                          + (1 if peer else 0)),
-            "clocks": clocks,
-            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                         "avg_ms": round(lm_ms, 5),
+                         "timed": "lm_head group (its quantize_row_q8_k launch + the GEMV) "
+                                  "between events, averaged over the K steps"},
+            "gpu_launches": args.steps * launches,
+            "clocks": t["clocks"],
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
+                    "d2h_bytes_per_step": e2e["d2h_bytes_per_step"]},
         }
+        res.update(sections)
         if prefill is not None:
             res["prefill_gemm"] = prefill
         if bitnet is not None:
             res["bitnet"] = bitnet
         if world == 1 and not args.no_cpu_baseline:
-            res["cpu_baseline"] = cpu_baseline_single()
+            res["cpu_baseline"] = cpu_baseline_single(spec)
         print(json.dumps(res), flush=True)
-    del graph, graph_ev
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()  # no rank still writes into a peer's buffer past this point
-    if peer:
-        outs.destroy()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def decode_config(spec, world, peer):
+    return {"workload": f"{spec['workload']} (BASELINE {spec['config']})", "batch": 1,
+            "weights": "Q4_K_M layers + Q6_K lm_head",
+            "l2": spec["l2"],
+            "parallelism": f"row-shard x{world}" + (
+                "" if world == 1 else
+                " + one-kernel all-gather over NVLink peer memory" if peer
+                else " + NCCL all-gather")}
+
+
+def run_q4_0_gemv(jkb, world, launches=60):
+    """Q4_0 x Q8_0 GEMV, N = K = 4096, batch 1, weights N(0, 0.02). Each
+    rank runs the whole matrix (replicas: 9.4 MB is below what sharding pays for); weight copies
+    rotate so the graph of `launches` back-to-back calls streams more than 2x the L2. Two entry
+    points: gemv_q4_0_q8_0 over a pre-quantized Q8_0 input, and vec_dot_q4_0_rvv with the f32
+    input quantized inside the launch. Max over ranks."""
+    import torch
+
+    rows = cols = 4096
+    nbytes = algorithmic_bytes(Q4_0, rows, cols)
+    copies = -(-260_000_000 // nbytes)
+    raw = synth_matrix(Q4_0, rows, cols, 4240)
+    ws = [jkb.Weight(jkb.TensorView("q4_0", Q4_0, [rows, cols], raw), rows, cols)
+          for _ in range(copies)]
+    x = torch.randn(cols, generator=torch.Generator().manual_seed(3)).cuda()
+    xq = jkb.empty_q8_0_blocks(cols // 32)
+    jkb.quantize_row_q8_0(x, xq)
+    out = torch.empty(rows, dtype=torch.float32, device="cuda")
+    peak, _ = measured_peaks()
+    res = {"config": "configs[0]", "rows": rows, "cols": cols, "algorithmic_bytes": nbytes,
+           "l2": f"{copies} weight copies rotating ({copies * nbytes / 1e6:.0f} MB)"}
+    for key, fn, inp in (("prequantized", jkb.gemv_q4_0_q8_0, xq),
+                         ("f32_input", jkb.vec_dot_q4_0_rvv, x)):
+        it = [0]
+
+        def one():
+            fn(out, ws[it[0] % copies], inp)
+            it[0] += 1
+
+        us = _max_over_ranks(_graph_time(one, max(launches, copies)), world)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[key] = {"us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    for w in ws:
+        w.destroy()
+    return res
 
 
 PREFILL = [(512, 14336, 4096), (512, 4096, 14336), (2048, 14336, 4096), (2048, 4096, 14336)]
@@ -934,6 +1154,12 @@ def main():
                     help="comma list of activation streams (x, attn, h, a, f) quantized by their "
                          "own quantize_row_q8_k launch ahead of pre-quantized GEMVs instead of "
                          "inside the f32-input GEMV launch (default: f, the lm_head input)")
+    ap.add_argument("--workload", choices=sorted(DECODE_SETS), default="8b",
+                    help="the decode GEMV set of the headline: 8b (BASELINE configs[1]) or 70b "
+                         "(configs[4]); the other set is reported as a section")
+    ap.add_argument("--no-sections", action="store_true",
+                    help="leave out the other decode set, the batch-16 70B step and the Q4_0 "
+                         "GEMV (configs[0]) sections")
     ap.add_argument("--no-gemm", action="store_true",
                     help="leave out the prefill GEMM section (BASELINE configs[2])")
     ap.add_argument("--no-bitnet", action="store_true",

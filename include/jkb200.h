@@ -424,13 +424,21 @@ int jkb_bitlinear_i8_gemm(float *out, size_t out_len, const jkb_repacked_weight 
  * examples: an engine that reserved all remaining HBM for its KV cache at start-up, and a host
  * whose per-token loop forbids cudaMalloc because it may synchronize the device and stall the
  * pipeline. The quantized activations go to a scratch array built into the library (4.25 MiB
- * of device memory on every GPU that loads it, held until exit). The batch must satisfy
+ * of device memory on every GPU that uses it, held until exit). The batch must satisfy
  * m * round_up(cols, 32) <= 2097152 elements (e.g. 512 tokens x 4096); larger batches fail
- * with JKB_E_BOUNDS. The call allocates nothing. The first call on each device looks up the
- * scratch address (cudaGetSymbolAddress) with that device current; make that first call
- * before any stream capture. All calls share the one array, so calls whose executions overlap
- * on the GPU (different streams, or threads sharing a device) race; serialize them. Each call
- * writes every scratch value it reads, so results never depend on an earlier call. */
+ * with JKB_E_BOUNDS. Once set up on a device, a call allocates nothing.
+ * Set-up: the first call on each device looks up the scratch address (cudaGetSymbolAddress)
+ * with that device current. Under CUDA's default lazy module loading that first call is also
+ * when the driver loads this part of the library on the device and reserves the 4.25 MiB, so
+ * it can fail with out-of-memory if the caller has already claimed all free HBM. Make one call
+ * per device at start-up, before reserving HBM and before any stream capture.
+ * All calls share the one array, so calls whose executions overlap on the GPU (different
+ * streams, or threads sharing a device) race; serialize them. Each call writes every scratch
+ * value it reads, so results never depend on an earlier call. Weights with 16-element min
+ * groups (Q2_K) run this entry point on the CUDA-core dp4a GEMM (about 7 TOPS against 134 on
+ * the tensor cores through jkb_gemm_repacked_f32), because the scratch has no plane for their
+ * 16-element activation sums. The address is cached per device ordinal: after cudaDeviceReset
+ * every device pointer this library holds for that device, this one included, is invalid. */
 int jkb_gemm_repacked_f32_noalloc(float *out, size_t out_len, const jkb_repacked_weight *w,
                                   const float *input, size_t in_len, size_t m, void *stream);
 
@@ -524,7 +532,9 @@ int jkb_peer_group_handle(const jkb_peer_group *pg, void *handle);
 /* handles: world * JKB_PEER_HANDLE_BYTES bytes, rank-ordered (this rank's own entry ignored) */
 int jkb_peer_group_open(jkb_peer_group *pg, const void *handles);
 int jkb_peer_group_buffer(const jkb_peer_group *pg, void **local, size_t *bytes);
-/* chunks: n byte ranges [offset[i], offset[i] + len[i]) of the buffer (16-byte multiples) */
+/* chunks: n byte ranges [offset[i], offset[i] + len[i]) of the buffer; offsets and lengths
+ * must be 4-byte aligned (the 16-byte aligned body of a chunk is copied as 16-byte words, its
+ * head and tail as 4-byte words) */
 int jkb_peer_group_allgather(jkb_peer_group *pg, const size_t *offset, const size_t *len,
                              size_t n, void *stream);
 /* Low-level: make `stream` wait until `arrivals` more peer signals have reached this rank than

@@ -8,7 +8,10 @@ single-GPU call, and one all-gather per step collects the slices. No K split is 
 need an all-reduce and change the f32 summation order.
 
 Layout of one rank's flat output buffer: the matrices in order, each contributing its slice,
-padded to the largest rank's total so that ``all_gather_into_tensor`` sees equal sizes.
+padded to the largest rank's total so that ``all_gather_into_tensor`` sees equal sizes. With a
+batch of m tokens a rank's slice of a matrix is its [m][rows of the shard] block (the layout
+jkb_gemv_batch writes), so every rank's part stays one contiguous range; ``output()``
+reassembles the [m][rows] matrix.
 
 Two ways to collect the slices:
 * ``ShardedOutputs``: each rank computes into a flat local buffer, one NCCL all-gather per step
@@ -59,8 +62,9 @@ class ShardedOutputs:
     """Flat per-rank output buffer for a list of (name, rows) matrices, its all-gather, and the
     reassembly of full output vectors from the gathered slices."""
 
-    def __init__(self, mats, world: int, rank: int, device="cuda", dtype=torch.float32):
-        self.world, self.rank = world, rank
+    def __init__(self, mats, world: int, rank: int, device="cuda", dtype=torch.float32,
+                 batch: int = 1):
+        self.world, self.rank, self.batch = world, rank, batch
         self.mats: dict[str, _Mat] = {}
         totals = [0] * world
         for name, rows in mats:
@@ -69,7 +73,7 @@ class ShardedOutputs:
                 sl = shard_rows(rows, world, r)
                 slices.append(sl)
                 offs.append(totals[r])
-                totals[r] += len(sl)
+                totals[r] += batch * len(sl)
             self.mats[name] = _Mat(name, rows, slices, offs)
         self.local_len = max(totals)
         self.local = torch.zeros(self.local_len, dtype=dtype, device=device)
@@ -81,10 +85,11 @@ class ShardedOutputs:
         return self.mats[name].slices[self.rank]
 
     def local_slice(self, name: str) -> torch.Tensor:
-        """View of this rank's output slice of matrix `name` in the flat buffer."""
+        """View of this rank's output slice of matrix `name` in the flat buffer ([batch][rows
+        of the shard], flattened)."""
         m = self.mats[name]
         o = m.offs[self.rank]
-        return self.local[o:o + len(m.slices[self.rank])]
+        return self.local[o:o + self.batch * len(m.slices[self.rank])]
 
     def gather(self, group=None):
         """All-gather the flat buffers (one collective, every rank must call it)."""
@@ -97,32 +102,36 @@ class ShardedOutputs:
                                   f"{type(e).__name__}: {e}") from e
 
     def output(self, name: str) -> torch.Tensor:
-        """The full output vector of matrix `name` assembled from the gathered slices (valid
-        after gather(); a new tensor)."""
-        m = self.mats[name]
+        """The full output of matrix `name` assembled from the gathered slices (valid after
+        gather(); a new tensor): [rows] for a batch of 1, else [batch][rows]."""
+        m, b = self.mats[name], self.batch
         parts = [self.gathered[r * self.local_len + m.offs[r]:
-                               r * self.local_len + m.offs[r] + len(m.slices[r])]
+                               r * self.local_len + m.offs[r] + b * len(m.slices[r])]
                  for r in range(self.world)]
-        return torch.cat(parts)
+        if b == 1:
+            return torch.cat(parts)
+        return torch.cat([p.view(b, -1) for p in parts], dim=1)
 
 
 class PeerOutputs:
     """Full output vectors of a list of (name, rows) matrices in a peer-group buffer on every
     rank: rank p computes rows shard_rows(rows, world, p) of each into ``local_slice(name,
     slot)``; after ``gather(slot)`` every rank holds all rows of every matrix in
-    ``output(name, slot)``."""
+    ``output(name, slot)``. With a batch of m tokens a matrix takes m * rows floats of a slot,
+    rank p's part being its [m][rows of the shard] block at offset m * (first row of the shard),
+    so each rank still pushes one contiguous chunk per matrix."""
 
     SLOTS = 2
 
-    def __init__(self, mats, world: int, rank: int, group=None):
+    def __init__(self, mats, world: int, rank: int, group=None, batch: int = 1):
         from .api import PeerGroup
 
-        self.world, self.rank = world, rank
+        self.world, self.rank, self.batch = world, rank, batch
         self.offs, self.rows = {}, {}
         total = 0
         for name, rows in mats:
             self.offs[name], self.rows[name] = total, rows
-            total += rows
+            total += batch * rows
         self.total = total
         self.pitch = (total + 3) // 4 * 4  # floats per slot (16-byte multiple)
         self.group = PeerGroup(self.SLOTS * self.pitch * 4, world, rank, group)
@@ -132,13 +141,20 @@ class PeerOutputs:
         return shard_rows(self.rows[name], self.world, self.rank)
 
     def local_slice(self, name: str, slot: int) -> torch.Tensor:
-        rr = self.rows_of(name)
+        rr, b = self.rows_of(name), self.batch
         o = self.offs[name]
-        return self.slots[slot, o + rr.start:o + rr.stop]
+        return self.slots[slot, o + b * rr.start:o + b * rr.stop]
 
     def output(self, name: str, slot: int) -> torch.Tensor:
-        o = self.offs[name]
-        return self.slots[slot, o:o + self.rows[name]]
+        """[rows] (a view) for a batch of 1, else the [batch][rows] matrix (a new tensor)."""
+        o, b, rows = self.offs[name], self.batch, self.rows[name]
+        if b == 1:
+            return self.slots[slot, o:o + rows]
+        parts = []
+        for r in range(self.world):
+            rr = shard_rows(rows, self.world, r)
+            parts.append(self.slots[slot, o + b * rr.start:o + b * rr.stop].view(b, -1))
+        return torch.cat(parts, dim=1)
 
     def full(self, slot: int) -> torch.Tensor:
         """All matrices' outputs of a slot, in list order."""
@@ -146,11 +162,12 @@ class PeerOutputs:
 
     def chunks(self, slot: int):
         """(byte offset, byte length) of this rank's rows of every matrix in a slot."""
-        out = []
+        out, b = [], self.batch
         for name in self.offs:
             rr = self.rows_of(name)
             if len(rr):
-                out.append((4 * (slot * self.pitch + self.offs[name] + rr.start), 4 * len(rr)))
+                out.append((4 * (slot * self.pitch + self.offs[name] + b * rr.start),
+                            4 * b * len(rr)))
         return out
 
     def gather(self, slot: int, stream=None):
