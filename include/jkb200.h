@@ -177,6 +177,73 @@ int jkb_act_q8_buffers(const jkb_act_q8 *act, size_t *m, size_t *k, size_t *k_pa
                        int8_t **q, float **x_scales, float **x_sums, float **x_sums_16,
                        float **super_scales);
 
+/* repack.rs:441 quantize_row_f32_to_q8_32 (scalar :376-400): per 32 elements of the device
+ * f32 input (the tail zero-padded, non-finite values read as 0) the i8 quants, the absmax / 127
+ * scale and the sequential f32 sum (quantize_block32_scalar, repack.rs:175-204). Device outputs
+ * of at least round_up(in_len, 32) quants and in_len / 32 rounded up scales and sums. */
+int jkb_quantize_row_f32_to_q8_32(const float *input, size_t in_len, int8_t *out_quants,
+                                  size_t q_len, float *out_scales, size_t scales_len,
+                                  float *out_sums, size_t sums_len, void *stream);
+
+/* ---- scratch arenas (jero_core ScratchWorkspace / ScratchScope) and QuantizedActQ8View ----
+ * A jkb_scratch is a bump arena over one device region: created with its own device memory
+ * (jkb_scratch_create, at set-up) or over caller-owned device memory (jkb_scratch_wrap, which
+ * allocates nothing on the device). Every carve starts at a JKB_SCRATCH_ALIGNMENT boundary;
+ * reset rewinds to 0; a scope is a saved cursor (jkb_scratch_scope_begin) that
+ * jkb_scratch_scope_end rewinds to, as dropping a ScratchScope does. The _in_scratch and
+ * _in_scope calls below carve from the arena's cursor (the two names exist for drop-in parity;
+ * they behave the same) and leave it untouched when they fail. Carved memory is overwritten by
+ * later carves after a reset or scope end, so results must be consumed (in stream order) before
+ * then. Not thread-safe: one arena per caller thread. */
+#define JKB_SCRATCH_ALIGNMENT 128
+typedef struct jkb_scratch jkb_scratch;
+int jkb_scratch_create(size_t bytes, jkb_scratch **out);
+int jkb_scratch_wrap(void *device_base, size_t bytes, jkb_scratch **out);
+int jkb_scratch_destroy(jkb_scratch *ws);
+int jkb_scratch_reset(jkb_scratch *ws);
+int jkb_scratch_used_bytes(const jkb_scratch *ws, size_t *used);
+int jkb_scratch_remaining_bytes(const jkb_scratch *ws, size_t *remaining);
+int jkb_scratch_alloc(jkb_scratch *ws, size_t bytes, void **out);
+int jkb_scratch_scope_begin(const jkb_scratch *ws, size_t *mark);
+int jkb_scratch_scope_end(jkb_scratch *ws, size_t mark);
+/* quant_q8.rs:405 quantize_row_q8_0_in_scratch / :429 _in_scope: x_len / 32 BlockQ8_0 carved
+ * from the arena and filled from device x; *out is their device address. */
+int jkb_quantize_row_q8_0_in_scratch(const float *x, size_t x_len, jkb_scratch *ws,
+                                     jkb_block_q8_0 **out, void *stream);
+int jkb_quantize_row_q8_0_in_scope(const float *x, size_t x_len, jkb_scratch *ws,
+                                   jkb_block_q8_0 **out, void *stream);
+/* quant_q8.rs:602 quantize_row_q8_k_in_scratch / :626 _in_scope (x_len / 256 BlockQ8K) */
+int jkb_quantize_row_q8_k_in_scratch(const float *x, size_t x_len, jkb_scratch *ws,
+                                     jkb_block_q8_k **out, void *stream);
+int jkb_quantize_row_q8_k_in_scope(const float *x, size_t x_len, jkb_scratch *ws,
+                                   jkb_block_q8_k **out, void *stream);
+
+/* QuantizedActQ8View (repack.rs:806-1090): a borrowed view of quantized activations in device
+ * memory the library does not own (an arena's planes, or a jkb_act_q8's). Rows are row-major:
+ * q [m][k_padded] i8, x_scales and x_sums [m][k_padded / 32], x_sums_16 [m][k_padded / 16],
+ * super_scales [m][ceil(k / 256)]. (The reference's view also carries sanitized f32 rows for
+ * dense F32 / F16 / BF16 weights, which the GPU path does not build.) */
+typedef struct {
+    size_t m, k, k_padded;
+    int8_t *q;
+    float *x_scales;
+    float *x_sums;
+    float *x_sums_16;
+    float *super_scales;
+} jkb_act_q8_view;
+/* repack.rs:824 QuantizedActQ8View::scratch_bytes_for_row: arena bytes one row of k needs,
+ * alignment padding included (0 for k == 0). */
+size_t jkb_act_q8_view_scratch_bytes_for_row(size_t k);
+/* repack.rs:870 quantize_row_in_scratch / :969 quantize_row_in_scope: quantizes one device f32
+ * row of k elements into planes carved from the arena (the QuantizedActQ8 quantizer, bit-exact)
+ * and fills *out (m = 1). */
+int jkb_act_q8_view_quantize_row_in_scratch(const float *act, size_t k, jkb_scratch *ws,
+                                            jkb_act_q8_view *out, void *stream);
+int jkb_act_q8_view_quantize_row_in_scope(const float *act, size_t k, jkb_scratch *ws,
+                                          jkb_act_q8_view *out, void *stream);
+/* repack.rs:708 QuantizedActQ8::as_view: the handle's current batch as a view. */
+int jkb_act_q8_as_view(const jkb_act_q8 *act, jkb_act_q8_view *out);
+
 /* ---- weights (GEMV / BitLinear layout) ---- */
 /* Validates the view like the reference validators, uploads and relayouts into the GPU layout
  * for an explicit [rows, cols] interpretation (RepackedWeight::from_tensor, repack.rs:2288). */
@@ -383,6 +450,56 @@ int jkb_repacked_weight_destroy(jkb_repacked_weight *w);
  * (device output). */
 int jkb_repacked_weight_dequantize_row(const jkb_repacked_weight *w, size_t row, float *out,
                                        size_t out_len, void *stream);
+/* ---- parallel load path (repack.rs:1286-1449, :1579-1722, :2366-2440) ----
+ * A loader splits a weight's 8-row tiles over worker threads: each fills its tile range of host
+ * buffers in the reference's tile layout with jkb_repack_into_tile_range (or
+ * jkb_repack_q4_k_m_parallel_slices), then one jkb_repacked_weight_from_tile_buffers call
+ * uploads the assembled buffers. The tile layout is the reference's: tiles [n_tiles][k_chunks]
+ * of 128 bytes (8 weight rows x 16 K values, row j of a tile at bytes 16j .. 16j + 16), scales
+ * and mins [n_tiles][scale_groups][8] f32; rows past `rows` in the last tile are zero. */
+typedef struct {
+    int32_t quant;
+    int32_t has_mins;          /* Q4_K_M, Q5_K, Q4_1, Q5_1, Q2_K */
+    size_t rows, cols;
+    size_t row_bytes;          /* GGUF bytes per weight row */
+    size_t k_padded;           /* cols rounded up to 32 */
+    size_t n_tiles;            /* ceil(rows / 8) */
+    size_t k_chunks;           /* k_padded / 16 */
+    size_t chunks_per_scale;   /* 1 for 16-element scale groups (Q6_K, Q3_K, Q2_K), else 2 */
+    size_t scale_groups;       /* k_chunks / chunks_per_scale */
+    size_t total_tiles;        /* n_tiles * k_chunks (128-byte tiles) */
+    size_t total_scales;       /* n_tiles * scale_groups * 8 */
+    size_t total_mins;         /* total_scales when has_mins, else 0 */
+} jkb_block_scaled_tile_layout;
+/* repack.rs:2372 RepackedWeight::block_scaled_layout (BlockScaledTileLayout::for_tensor,
+ * :1308): validates the view like from_tensor and fills *out. Host-only; needs no GPU. */
+int jkb_block_scaled_layout(const jkb_tensor_view *view, size_t rows, size_t cols,
+                            jkb_block_scaled_tile_layout *out);
+/* repack.rs:1579 repack_into_tile_range: tiles [tile_begin, tile_end) into caller buffers of
+ * exactly n_out_tiles = tiles * k_chunks 128-byte tiles and n_scales = tiles * scale_groups * 8
+ * floats (n_mins the same, for formats with mins; ignored otherwise). The view's bytes must be
+ * host memory. Host-only, allocates nothing; disjoint tile ranges may run on parallel threads. */
+int jkb_repack_into_tile_range(const jkb_tensor_view *view, size_t rows, size_t cols,
+                               size_t tile_begin, size_t tile_end, uint8_t *out_tiles,
+                               size_t n_out_tiles, float *out_scales, size_t n_scales,
+                               float *out_mins, size_t n_mins);
+/* repack.rs:1659 repack_q4_k_m_parallel_slices: the same for Q4_K_M weights (CapabilityMismatch
+ * otherwise) with the tiles as raw bytes (tiles_len = tiles * k_chunks * 128) and mandatory
+ * mins. */
+int jkb_repack_q4_k_m_parallel_slices(const jkb_tensor_view *view, size_t rows, size_t cols,
+                                      size_t tile_begin, size_t tile_end, int8_t *out_tiles_i8,
+                                      size_t tiles_len, float *out_scales, size_t n_scales,
+                                      float *out_mins, size_t n_mins);
+/* repack.rs:2386 RepackedWeight::from_tile_buffers: host buffers of the whole layout (n_tiles
+ * == total_tiles 128-byte tiles, n_scales == total_scales, mins of total_mins for formats with
+ * mins and NULL otherwise) -> a jkb_repacked_weight (device buffers allocated here, the tiles
+ * converted to the device layout on `stream`; returns after the upload finished). The layout
+ * must be one jkb_block_scaled_layout filled. */
+int jkb_repacked_weight_from_tile_buffers(const jkb_block_scaled_tile_layout *layout,
+                                          const uint8_t *tiles, size_t n_tiles,
+                                          const float *scales, size_t n_scales,
+                                          const float *mins, size_t n_mins, void *stream,
+                                          jkb_repacked_weight **out);
 /* Device views: q [rows][k_pad] i8, scales and mins [rows][scale_groups] f32 (mins NULL
  * unless Q4_K_M). */
 int jkb_repacked_weight_buffers(const jkb_repacked_weight *w, size_t *rows, size_t *cols,
@@ -402,6 +519,27 @@ int jkb_gemv_repacked(float *out, size_t out_len, const jkb_repacked_weight *w,
 int jkb_gemv_repacked_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
                            const jkb_act_q8 *act, size_t row_begin, size_t row_end,
                            void *stream);
+/* repack.rs:4030 gemv_repacked_view / :4045 gemv_repacked_view_rows (and RepackedWeight::
+ * gemv_view / gemv_view_rows, :2628 / :2638): the single-token GEMV over a view (act->m must be
+ * 1); out [row_end - row_begin]. */
+int jkb_gemv_repacked_view(float *out, size_t out_len, const jkb_repacked_weight *w,
+                           const jkb_act_q8_view *act, void *stream);
+int jkb_gemv_repacked_view_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
+                                const jkb_act_q8_view *act, size_t row_begin, size_t row_end,
+                                void *stream);
+/* repack.rs:4101 gemv_repacked_f32 / :4114 gemv_repacked_f32_rows: device f32 input [cols]
+ * quantized into the caller's act handle (capacity >= 1 row, k == cols; the reference allocates
+ * a QuantizedActQ8 here), then the GEMV of rows [row_begin, row_end). */
+int jkb_gemv_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight *w,
+                          const float *input, size_t in_len, jkb_act_q8 *scratch, void *stream);
+int jkb_gemv_repacked_f32_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
+                               const float *input, size_t in_len, size_t row_begin,
+                               size_t row_end, jkb_act_q8 *scratch, void *stream);
+/* repack.rs:4143 gemm_repacked_f32_rows: as jkb_gemm_repacked_f32 for weight rows
+ * [row_begin, row_end); out [m][row_end - row_begin]. */
+int jkb_gemm_repacked_f32_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
+                               const float *input, size_t in_len, size_t m, size_t row_begin,
+                               size_t row_end, jkb_act_q8 *scratch, void *stream);
 /* repack.rs:4129 gemm_repacked_f32: quantizes input [m][cols] into the caller's act handle
  * (the reference allocates a QuantizedActQ8 here; this ABI never allocates), then GEMMs. */
 int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight *w,

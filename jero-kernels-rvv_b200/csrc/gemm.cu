@@ -192,6 +192,35 @@ static uint8_t *noalloc_scratch(int *rc) {
     return ptr_by_device[dev];
 }
 
+// A QuantizedActQ8View (caller-owned planes) as the activation record the GEMM reads. One
+// token never takes the tensor-core path, so the transposed planes stay absent.
+static int act_of_view(const char *fn, const jkb_act_q8_view *v, jkb_act_q8 *a) {
+    if (!v) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null activation view");
+    if (v->k == 0 || v->k_padded != (v->k + 31) / 32 * 32)
+        return fail(JKB_E_BOUNDS, fn, 0, v->k, v->k_padded,
+                    "activation view k %zu / k_padded %zu are inconsistent", v->k, v->k_padded);
+    if (v->m && (!v->q || !v->x_scales || !v->x_sums || !v->x_sums_16))
+        return fail(JKB_E_INVALID, fn, 0, 0, 0, "activation view with a null plane");
+    int rc;
+    if ((rc = check_align(v->q, 16, fn, "view q")) ||
+        (rc = check_align(v->x_scales, 4, fn, "view x_scales")) ||
+        (rc = check_align(v->x_sums, 4, fn, "view x_sums")) ||
+        (rc = check_align(v->x_sums_16, 4, fn, "view x_sums_16")))
+        return rc;
+    memset(a, 0, sizeof(*a));
+    a->magic = ACT_MAGIC;
+    a->m_cap = a->m = v->m;
+    a->k = v->k;
+    a->k_pad = v->k_padded;
+    a->q = v->q;
+    a->x_scales = v->x_scales;
+    a->x_sums = v->x_sums;
+    a->x_sums_16 = v->x_sums_16;
+    a->super_scales = v->super_scales;
+    a->xt_pitch = (v->m + 31) / 32 * 32;
+    return JKB_OK;
+}
+
 }  // namespace jkb
 
 using namespace jkb;
@@ -304,6 +333,61 @@ int jkb_bitlinear_i8_gemm(float *out, size_t out_len, const jkb_repacked_weight 
     if (rc || used) return rc;
     // small batches: the repacked GEMM over 32-element groups (within the 1e-5 contract)
     return gemm_rows(fn, out, out_len, w, scratch, 0, w->rows, false, st);
+}
+
+int jkb_gemv_repacked_view(float *out, size_t out_len, const jkb_repacked_weight *w,
+                           const jkb_act_q8_view *act, void *stream) {
+    size_t rows = (w && w->magic == REPACKED_MAGIC) ? w->rows : 0;
+    return jkb_gemv_repacked_view_rows(out, out_len, w, act, 0, rows, stream);
+}
+
+int jkb_gemv_repacked_view_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
+                                const jkb_act_q8_view *act, size_t row_begin, size_t row_end,
+                                void *stream) {
+    jkb_act_q8 a;
+    int rc = act_of_view("gemv_repacked_view_rows", act, &a);
+    if (rc) return rc;
+    return gemm_rows("gemv_repacked_view_rows", out, out_len, w, &a, row_begin, row_end, true,
+                     as_stream(stream));
+}
+
+int jkb_gemv_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight *w,
+                          const float *input, size_t in_len, jkb_act_q8 *scratch, void *stream) {
+    size_t rows = (w && w->magic == REPACKED_MAGIC) ? w->rows : 0;
+    return jkb_gemv_repacked_f32_rows(out, out_len, w, input, in_len, 0, rows, scratch, stream);
+}
+
+int jkb_gemv_repacked_f32_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
+                               const float *input, size_t in_len, size_t row_begin,
+                               size_t row_end, jkb_act_q8 *scratch, void *stream) {
+    static const char *fn = "gemv_repacked_f32_rows";
+    if (!w || w->magic != REPACKED_MAGIC)
+        return fail(JKB_E_INVALID, fn, 0, 0, 0, "null or destroyed weight");
+    // QuantizedActQ8::quantize_row (repack.rs:531) then gemv_repacked_rows (:4014)
+    if (in_len == 0)
+        return fail(JKB_E_BOUNDS, "QuantizedActQ8", 0, 0, 0,
+                    "activation length 0 does not match m (1) * k (0)");
+    if (in_len != w->cols)
+        return fail(JKB_E_BOUNDS, "gemm_repacked", 0, out_len * 4, w->device_bytes,
+                    "activation k %zu != weight cols %zu", in_len, w->cols);
+    int rc = jkb_act_q8_quantize(scratch, input, in_len, 1, in_len, stream);
+    if (rc) return rc;
+    return gemm_rows(fn, out, out_len, w, scratch, row_begin, row_end, true, as_stream(stream));
+}
+
+int jkb_gemm_repacked_f32_rows(float *out, size_t out_len, const jkb_repacked_weight *w,
+                               const float *input, size_t in_len, size_t m, size_t row_begin,
+                               size_t row_end, jkb_act_q8 *scratch, void *stream) {
+    if (!w || w->magic != REPACKED_MAGIC)
+        return fail(JKB_E_INVALID, "gemm_repacked_f32", 0, 0, 0, "null or destroyed weight");
+    // gemm_repacked_f32_rows validation (repack.rs:4150-4162)
+    if (m == 0 || w->cols == 0 || in_len != m * w->cols)
+        return fail(JKB_E_BOUNDS, "gemm_repacked_f32", 0, in_len * 4, m * w->cols * 4,
+                    "input length %zu != m (%zu) * cols (%zu)", in_len, m, w->cols);
+    int rc = jkb_act_q8_quantize(scratch, input, in_len, m, w->cols, stream);
+    if (rc) return rc;
+    return gemm_rows("gemm_repacked_f32_rows", out, out_len, w, scratch, row_begin, row_end,
+                     false, as_stream(stream));
 }
 
 int jkb_gemm_repacked_f32(float *out, size_t out_len, const jkb_repacked_weight *w,

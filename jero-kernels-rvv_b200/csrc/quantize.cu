@@ -115,6 +115,79 @@ __global__ void __launch_bounds__(256) quantize_q8_k_kernel(const float *__restr
     if ((lane & 1) == 0) *reinterpret_cast<int16_t *>(ob + 260 + lane) = (int16_t)s;
 }
 
+// quantize_block32_scalar (repack.rs:175-204) on the `valid` leading elements of src (the
+// rest of the 32 read as 0, non-finite values as 0): the i8 quants packed in words[8], the scale
+// absmax / 127 (0 when absmax < 1e-30), the sequential f32 sum from 0.0 and the two 16-element
+// half sums from -0.0 (QuantizedActQ8's x_sums_16), all in element order as in the reference.
+struct QBlock32 {
+    uint32_t words[8];
+    float d, s, h0, h1;
+};
+__device__ __forceinline__ void quant_block32(const float *__restrict__ src, size_t valid,
+                                              QBlock32 &o) {
+    float c[32];
+    float absmax = 0.0f, s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) {
+        float v = (size_t)i < valid ? __ldg(src + i) : 0.0f;
+        v = finite_f(v) ? v : 0.0f;
+        c[i] = v;
+        s = __fadd_rn(s, v);
+        float av = fabsf(v);
+        if (av > absmax) absmax = av;
+    }
+    float h0 = -0.0f, h1 = -0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; i++) h0 = __fadd_rn(h0, c[i]);
+#pragma unroll
+    for (int i = 16; i < 32; i++) h1 = __fadd_rn(h1, c[i]);
+    float d = 0.0f;
+    if (absmax < 1e-30f) {
+#pragma unroll
+        for (int i = 0; i < 8; i++) o.words[i] = 0;
+    } else {
+        d = __fdiv_rn(absmax, 127.0f);
+        float inv = __fdiv_rn(127.0f, absmax);
+#pragma unroll
+        for (int w = 0; w < 8; w++) {
+            uint32_t pk = 0;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float t = roundf(__fmul_rn(c[4 * w + j], inv));
+                t = fminf(fmaxf(t, -127.0f), 127.0f);
+                pk |= ((uint32_t)((int)t & 0xFF)) << (8 * j);
+            }
+            o.words[w] = pk;
+        }
+    }
+    o.d = d;
+    o.s = s;
+    o.h0 = h0;
+    o.h1 = h1;
+}
+
+// quantize_row_f32_to_q8_32 (repack.rs:376-455): one thread per 32-element block of one row.
+__global__ void __launch_bounds__(256) q8_32_row_kernel(const float *__restrict__ x, size_t len,
+                                                        int8_t *__restrict__ q,
+                                                        float *__restrict__ scales,
+                                                        float *__restrict__ sums) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+    const size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b * 32 >= len) return;
+    QBlock32 o;
+    quant_block32(x + 32 * b, len - 32 * b < 32 ? len - 32 * b : 32, o);
+    int8_t *qb = q + 32 * b;
+    if ((((uintptr_t)qb) & 15) == 0) {
+        reinterpret_cast<uint4 *>(qb)[0] = make_uint4(o.words[0], o.words[1], o.words[2], o.words[3]);
+        reinterpret_cast<uint4 *>(qb)[1] = make_uint4(o.words[4], o.words[5], o.words[6], o.words[7]);
+    } else {
+        for (int i = 0; i < 32; i++) qb[i] = (int8_t)((o.words[i / 4] >> (8 * (i % 4))) & 0xFF);
+    }
+    scales[b] = o.d;
+    sums[b] = o.s;
+}
+
 // QuantizedActQ8::quantize_into (repack.rs:542-650) with quantize_block32_scalar
 // (repack.rs:175-204): one thread per 32-element block, so the f32 sums run sequentially in
 // element order exactly as in the reference (x_sums from 0.0, x_sums_16 from -0.0).
@@ -146,44 +219,10 @@ __global__ void __launch_bounds__(256) act_q8_kernel(const float *__restrict__ a
         if (xsn16_t) xsn16_t[xt16_at] = xsn16_t[xt16_at + xt_pitch] = 0.0f;
         return;
     }
-    const float *src = act + r * k;
-    float c[32];
-    float absmax = 0.0f, s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; i++) {
-        size_t idx = b * 32 + i;
-        float v = idx < k ? __ldg(src + idx) : 0.0f;
-        v = finite_f(v) ? v : 0.0f;
-        c[i] = v;
-        s = __fadd_rn(s, v);
-        float av = fabsf(v);
-        if (av > absmax) absmax = av;
-    }
-    float h0 = -0.0f, h1 = -0.0f;
-#pragma unroll
-    for (int i = 0; i < 16; i++) h0 = __fadd_rn(h0, c[i]);
-#pragma unroll
-    for (int i = 16; i < 32; i++) h1 = __fadd_rn(h1, c[i]);
-    uint32_t words[8];
-    float d = 0.0f;
-    if (absmax < 1e-30f) {
-#pragma unroll
-        for (int i = 0; i < 8; i++) words[i] = 0;
-    } else {
-        d = __fdiv_rn(absmax, 127.0f);
-        float inv = __fdiv_rn(127.0f, absmax);
-#pragma unroll
-        for (int w = 0; w < 8; w++) {
-            uint32_t pk = 0;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                float t = roundf(__fmul_rn(c[4 * w + j], inv));
-                t = fminf(fmaxf(t, -127.0f), 127.0f);
-                pk |= ((uint32_t)((int)t & 0xFF)) << (8 * j);
-            }
-            words[w] = pk;
-        }
-    }
+    QBlock32 o;
+    quant_block32(act + r * k + b * 32, k > b * 32 ? (k - b * 32 < 32 ? k - b * 32 : 32) : 0, o);
+    const uint32_t *words = o.words;
+    const float d = o.d, s = o.s, h0 = o.h0, h1 = o.h1;
     uint4 *qo = reinterpret_cast<uint4 *>(q + r * kp + b * 32);
     qo[0] = make_uint4(words[0], words[1], words[2], words[3]);
     qo[1] = make_uint4(words[4], words[5], words[6], words[7]);
@@ -486,6 +525,31 @@ int jkb_quantize_row_q8_0_f32(const float *x, size_t x_len, jkb_block_q8_0 *out,
     if (rc) return rc;
     if (!x || !out) return fail(JKB_E_INVALID, "quantize_row_q8_0_f32", 0, 0, 0, "null pointer");
     return launch_q8_0(x, out_len, out, as_stream(stream));
+}
+
+int jkb_quantize_row_f32_to_q8_32(const float *input, size_t in_len, int8_t *out_quants,
+                                  size_t q_len, float *out_scales, size_t scales_len,
+                                  float *out_sums, size_t sums_len, void *stream) {
+    static const char *fn = "quantize_row_f32_to_q8_32";
+    // validate_q8_row_buffers (repack.rs:336-365)
+    if (in_len == 0)
+        return fail(JKB_E_BOUNDS, fn, 0, 0, 0, "activation slice must be non-empty");
+    const size_t blocks = (in_len + 31) / 32, req = blocks * 32;
+    if (q_len < req || scales_len < blocks || sums_len < blocks)
+        return fail(JKB_E_BOUNDS, fn, 0, req, q_len,
+                    "insufficient Q8 output buffers: quants=%zu/%zu, scales=%zu/%zu, sums=%zu/%zu",
+                    q_len, req, scales_len, blocks, sums_len, blocks);
+    if (!input || !out_quants || !out_scales || !out_sums)
+        return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
+    int rc;
+    if ((rc = check_align(input, 4, fn, "input")) ||
+        (rc = check_align(out_scales, 4, fn, "out_scales")) ||
+        (rc = check_align(out_sums, 4, fn, "out_sums")))
+        return rc;
+    cudaError_t e = launch_pdl(q8_32_row_kernel, dim3((unsigned)((blocks + 255) / 256)),
+                               dim3(256), 0, as_stream(stream), input, in_len, out_quants,
+                               out_scales, out_sums);
+    return e == cudaSuccess ? JKB_OK : fail_cuda(e, "q8_32_row_kernel");
 }
 
 int jkb_quantize_row_q8_0(const float *x, size_t x_len, jkb_block_q8_0 *out, size_t out_len,

@@ -21,6 +21,7 @@
 
 #include "gpu_layout.cuh"
 #include "jkb_internal.h"
+#include "repack_block.cuh"
 
 namespace jkb {
 
@@ -115,223 +116,19 @@ __global__ void relayout_kernel(int quant, int gpu_format, const uint8_t *__rest
     }
 }
 
-__device__ __forceinline__ float f16_finite_dev(uint16_t bits) {
-    float v = __half2float(__ushort_as_half(bits));
-    return ((bits >> 10) & 0x1F) == 0x1F ? 0.0f : v;
-}
-
-// repack_block_scaled_range_into_i8 (repack.rs:1724-2103) for the covered formats, one thread
-// per (row, block): i8 values row-major [rows][k_pad], f32 scales [rows][groups].
+// repack_block_scaled_range_into_i8 (repack.rs:1724-2103), one thread per (row, block): i8
+// values row-major [rows][k_pad], f32 scales (and mins) [rows][groups]. The per-block decoder
+// (repack_block.cuh) is shared with the host tile packer of jkb_repack_into_tile_range.
 __global__ void repack_i8_kernel(int quant, const uint8_t *__restrict__ raw, size_t rows,
                                  size_t nb, size_t raw_row, int bb, float i2s, int8_t *q,
                                  size_t k_pad, float *scales, float *mins, size_t groups) {
     size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= rows * nb) return;
     size_t r = idx / nb, b = idx % nb;
-    const uint8_t *blk = raw + r * raw_row + b * (size_t)bb;
-    int8_t *qr = q + r * k_pad;
-    float *sr = scales + r * groups;
-    float *mr = mins ? mins + r * groups : nullptr;
-    switch (quant) {
-    case JKB_Q8_0: {
-        float dd = f16_finite_dev(rd16(blk));
-        sr[b] = dd;
-        for (int i = 0; i < 32; i++) qr[32 * b + i] = dd != 0.0f ? (int8_t)blk[2 + i] : 0;
-        break;
-    }
-    case JKB_Q4_0: {
-        float dd = f16_finite_dev(rd16(blk));
-        sr[b] = dd;
-        for (int i = 0; i < 16; i++) {
-            qr[32 * b + i] = dd != 0.0f ? (int8_t)((blk[2 + i] & 0x0F) - 8) : 0;
-            qr[32 * b + 16 + i] = dd != 0.0f ? (int8_t)(((blk[2 + i] >> 4) & 0x0F) - 8) : 0;
-        }
-        break;
-    }
-    case JKB_Q4_K_M: {
-        float dd = f16_finite_dev(rd16(blk)), dmin = f16_finite_dev(rd16(blk + 2));
-        const uint8_t *s = blk + 4;
-        uint8_t scv[8], mv[8];
-        for (int j = 0; j < 4; j++) {
-            scv[j] = s[j] & 0x3F;
-            mv[j] = s[j + 4] & 0x3F;
-        }
-        for (int j = 4; j < 8; j++) {
-            scv[j] = (uint8_t)((s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4));
-            mv[j] = (uint8_t)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
-        }
-        for (int c = 0; c < 4; c++) {
-            size_t g0 = b * 8 + 2 * c;
-            sr[g0] = __fmul_rn(dd, (float)scv[2 * c]);
-            mr[g0] = __fmul_rn(dmin, (float)mv[2 * c]);
-            sr[g0 + 1] = __fmul_rn(dd, (float)scv[2 * c + 1]);
-            mr[g0 + 1] = __fmul_rn(dmin, (float)mv[2 * c + 1]);
-            for (int l = 0; l < 32; l++) {
-                qr[256 * b + 64 * c + l] = (int8_t)(blk[16 + 32 * c + l] & 0x0F);
-                qr[256 * b + 64 * c + 32 + l] = (int8_t)((blk[16 + 32 * c + l] >> 4) & 0x0F);
-            }
-        }
-        break;
-    }
-    case JKB_Q5_0: {  // repack.rs:1827-1840: (5-bit code - 16), left 0 when d == 0
-        float dd = f16_finite_dev(rd16(blk));
-        sr[b] = dd;
-        const uint32_t qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) |
-                            ((uint32_t)blk[4] << 16) | ((uint32_t)blk[5] << 24);
-        for (int i = 0; i < 16; i++) {
-            const int q0 = (int)((blk[6 + i] & 0x0F) | (((qh >> i) & 1) << 4)) - 16;
-            const int q1 = (int)(((blk[6 + i] >> 4) & 0x0F) | (((qh >> (i + 16)) & 1) << 4)) - 16;
-            qr[32 * b + i] = dd != 0.0f ? (int8_t)q0 : 0;
-            qr[32 * b + 16 + i] = dd != 0.0f ? (int8_t)q1 : 0;
-        }
-        break;
-    }
-    case JKB_Q5_K: {  // repack.rs:1959-1995: scales d * sc, mins dmin * m, unsigned 5-bit codes
-        float dd = f16_finite_dev(rd16(blk)), dmin = f16_finite_dev(rd16(blk + 2));
-        const uint8_t *s = blk + 4, *qh = blk + 16, *qs = blk + 48;
-        uint8_t scv[8], mv[8];
-        for (int j = 0; j < 4; j++) {
-            scv[j] = s[j] & 0x3F;
-            mv[j] = s[j + 4] & 0x3F;
-        }
-        for (int j = 4; j < 8; j++) {
-            scv[j] = (uint8_t)((s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4));
-            mv[j] = (uint8_t)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
-        }
-        for (int c = 0; c < 4; c++) {
-            size_t g0 = b * 8 + 2 * c;
-            sr[g0] = __fmul_rn(dd, (float)scv[2 * c]);
-            mr[g0] = __fmul_rn(dmin, (float)mv[2 * c]);
-            sr[g0 + 1] = __fmul_rn(dd, (float)scv[2 * c + 1]);
-            mr[g0 + 1] = __fmul_rn(dmin, (float)mv[2 * c + 1]);
-            for (int l = 0; l < 32; l++) {
-                qr[256 * b + 64 * c + l] =
-                    (int8_t)((qs[32 * c + l] & 0x0F) + (((qh[l] >> (2 * c)) & 1) ? 16 : 0));
-                qr[256 * b + 64 * c + 32 + l] =
-                    (int8_t)((qs[32 * c + l] >> 4) + (((qh[l] >> (2 * c + 1)) & 1) ? 16 : 0));
-            }
-        }
-        break;
-    }
-    case JKB_Q6_K: {
-        float dd = f16_finite_dev(rd16(blk + 208));
-        for (int s = 0; s < 16; s++) sr[b * 16 + s] = __fmul_rn(dd, (float)(int8_t)blk[192 + s]);
-        const uint8_t *ql = blk, *qh = blk + 128;
-        for (int h = 0; h < 2; h++)
-            for (int l = 0; l < 32; l++) {
-                int lb = 64 * h, hb = 32 * h, n = 256 * (int)b + 128 * h;
-                int q1 = (int)((ql[lb + l] & 0x0F) | ((qh[hb + l] & 3) << 4)) - 32;
-                int q2 = (int)((ql[lb + l + 32] & 0x0F) | (((qh[hb + l] >> 2) & 3) << 4)) - 32;
-                int q3 = (int)(((ql[lb + l] >> 4) & 0x0F) | (((qh[hb + l] >> 4) & 3) << 4)) - 32;
-                int q4 = (int)(((ql[lb + l + 32] >> 4) & 0x0F) | (((qh[hb + l] >> 6) & 3) << 4)) - 32;
-                bool z = dd == 0.0f;
-                qr[n + l] = z ? 0 : (int8_t)q1;
-                qr[n + l + 32] = z ? 0 : (int8_t)q2;
-                qr[n + l + 64] = z ? 0 : (int8_t)q3;
-                qr[n + l + 96] = z ? 0 : (int8_t)q4;
-            }
-        break;
-    }
-    case JKB_TQ2_0:
-    case JKB_TQ1_0: {
-        float dd = f16_finite_dev(rd16(blk));
-        for (int s = 0; s < 8; s++) sr[b * 8 + s] = dd;
-        if (quant == JKB_TQ2_0) {
-            for (int e = 0; e < 256; e++)
-                qr[256 * b + e] = (int8_t)(((blk[2 + e / 4] >> (2 * (e % 4))) & 3) - 1);
-        } else {
-            for (int i = 0; i < 51; i++) {
-                unsigned v = blk[2 + i];
-                for (int j = 0; j < 5; j++) {
-                    qr[256 * b + 5 * i + j] = (int8_t)((int)(v % 3) - 1);
-                    v /= 3;
-                }
-            }
-            qr[256 * b + 255] = (int8_t)((int)(blk[53] % 3) - 1);
-        }
-        break;
-    }
-    case JKB_Q4_1: {  // repack.rs:1814-1826: scale d, min -m (0.0 when m == 0), unsigned codes
-        const float dd = f16_finite_dev(rd16(blk)), m = f16_finite_dev(rd16(blk + 2));
-        sr[b] = dd;
-        mr[b] = m == 0.0f ? 0.0f : -m;
-        for (int i = 0; i < 16; i++) {
-            qr[32 * b + i] = (int8_t)(blk[4 + i] & 0x0F);
-            qr[32 * b + 16 + i] = (int8_t)(blk[4 + i] >> 4);
-        }
-        break;
-    }
-    case JKB_Q5_1: {  // repack.rs:1841-1855 with unpack_q5_1_block_i8 (quant.rs:169-190)
-        const float dd = f16_finite_dev(rd16(blk)), m = f16_finite_dev(rd16(blk + 2));
-        sr[b] = dd;
-        mr[b] = m == 0.0f ? 0.0f : -m;
-        const uint32_t qh = (uint32_t)blk[4] | ((uint32_t)blk[5] << 8) |
-                            ((uint32_t)blk[6] << 16) | ((uint32_t)blk[7] << 24);
-        for (int i = 0; i < 16; i++) {
-            qr[32 * b + i] = (int8_t)((blk[8 + i] & 0x0F) | (((qh >> i) & 1) << 4));
-            qr[32 * b + 16 + i] = (int8_t)((blk[8 + i] >> 4) | (((qh >> (i + 16)) & 1) << 4));
-        }
-        break;
-    }
-    case JKB_IQ4_NL: {  // repack.rs:1856-1873: the code book values, left 0 when d == 0
-        // KVALUES_IQ4NL (quant.rs:80-82)
-        constexpr int8_t kv[16] = {-127, -104, -83, -65, -49, -35, -22, -10,
-                                   1,    13,   25,  38,  53,  69,  89,  113};
-        const float dd = f16_finite_dev(rd16(blk));
-        sr[b] = dd;
-        for (int i = 0; i < 16; i++) {
-            qr[32 * b + i] = dd != 0.0f ? kv[blk[2 + i] & 0x0F] : 0;
-            qr[32 * b + 16 + i] = dd != 0.0f ? kv[blk[2 + i] >> 4] : 0;
-        }
-        break;
-    }
-    case JKB_Q2_K: {  // repack.rs:1874-1892 with unpack_q2_k_block_i8 (quant.rs:198-246)
-        // sub-block s (16 elements) takes the 2-bit field 2 * ((s % 8) / 2) of
-        // qs[32 (s / 8) + 16 (s % 2) + l]; scale d * (sc & 15), min dmin * (sc >> 4)
-        const float dd = f16_finite_dev(rd16(blk + 80)), dmin = f16_finite_dev(rd16(blk + 82));
-        for (int s = 0; s < 16; s++) {
-            sr[16 * b + s] = __fmul_rn(dd, (float)(blk[s] & 0x0F));
-            mr[16 * b + s] = __fmul_rn(dmin, (float)(blk[s] >> 4));
-            const int sh = 2 * ((s % 8) / 2);
-            const uint8_t *qs = blk + 16 + 32 * (s / 8) + 16 * (s % 2);
-            for (int l = 0; l < 16; l++) qr[256 * b + 16 * s + l] = (int8_t)((qs[l] >> sh) & 3);
-        }
-        break;
-    }
-    case JKB_Q3_K: {  // repack.rs:1893-1908 with unpack_q3_k_block_i8 (quant.rs:255-330)
-        // 6-bit scale s: low 4 bits from byte s (s < 8, low nibble) or s - 8 (high nibble),
-        // top 2 bits from byte 8 + s % 4 at bit 2 (s / 4); codes minus 4 where the hmask bit
-        // s / 2 of hmask[16 (s % 2) + l] is clear
-        const uint8_t *hm = blk, *raw6 = blk + 96;
-        const float dd = f16_finite_dev(rd16(blk + 108));
-        for (int s = 0; s < 16; s++) {
-            const int lo = s < 8 ? raw6[s] & 0x0F : raw6[s - 8] >> 4;
-            const int hi = (raw6[8 + s % 4] >> (2 * (s / 4))) & 3;
-            sr[16 * b + s] = __fmul_rn(dd, (float)((lo | (hi << 4)) - 32));
-            const int sh = 2 * ((s % 8) / 2);
-            const uint8_t *qs = blk + 32 + 32 * (s / 8) + 16 * (s % 2);
-            for (int l = 0; l < 16; l++) {
-                const int code = (qs[l] >> sh) & 3;
-                const int high = (hm[16 * (s % 2) + l] >> (s / 2)) & 1;
-                qr[256 * b + 16 * s + l] = (int8_t)(code - (high ? 0 : 4));
-            }
-        }
-        break;
-    }
-    case JKB_I2_S: {
-        for (int s = 0; s < 4; s++) sr[b * 4 + s] = i2s;
-        for (int g = 0; g < 32; g++) {
-            uint8_t v = blk[g];
-            bool z = i2s == 0.0f;
-            qr[128 * b + g] = z ? 0 : (int8_t)(((v >> 6) & 3) - 1);
-            qr[128 * b + 32 + g] = z ? 0 : (int8_t)(((v >> 4) & 3) - 1);
-            qr[128 * b + 64 + g] = z ? 0 : (int8_t)(((v >> 2) & 3) - 1);
-            qr[128 * b + 96 + g] = z ? 0 : (int8_t)((v & 3) - 1);
-        }
-        break;
-    }
-    default: break;
-    }
+    const int be = repack_block_elems(quant), gpb = be / repack_group_elems(quant);
+    repack_block_i8(quant, raw + r * raw_row + b * (size_t)bb, q + r * k_pad + b * (size_t)be,
+                    scales + r * groups + b * (size_t)gpb,
+                    mins ? mins + r * groups + b * (size_t)gpb : nullptr, i2s);
 }
 
 // validate_matrix_shape + validate_matrix_view (repack.rs:1151-1284).
@@ -596,6 +393,118 @@ static int repacked_upload(const jkb_tensor_view *v, size_t rows, size_t cols, c
     return JKB_OK;
 }
 
+
+// ---- parallel load path: BlockScaledTileLayout, repack_into_tile_range, from_tile_buffers ----
+// The reference tile layout (repack.rs:1286-1449): tiles [n_tile][k_chunk] of 128 bytes, each
+// 8 weight rows x 16 K values (row j of the tile at bytes 16j .. 16j + 16); scales and mins
+// [n_tile][scale_group][8] f32. These host buffers are what a loader fills on worker threads;
+// from_tile_buffers uploads them and converts them to the device layout above.
+constexpr size_t TILE_N = 8, TILE_K = 16, TILE_BYTES = 128;
+
+// BlockScaledTileLayout::for_tensor (repack.rs:1308-1336) and from_validated_dims
+// (:1338-1366) for an explicit [rows, cols] interpretation.
+static int block_layout(const jkb_tensor_view *v, size_t rows, size_t cols, const char *fn,
+                        jkb_block_scaled_tile_layout *L) {
+    const char *nm = v->name ? v->name : "";
+    const Fmt *f = fmt_of(v->quant);
+    if (!f)
+        return fail(JKB_E_CAPABILITY, nm, v->offset, v->byte_len, v->byte_len,
+                    "%s: unsupported tensor quant %s", fn, quant_name(v->quant));
+    int rc = validate_matrix_view(v, f, rows, cols);
+    if (rc) return rc;
+    memset(L, 0, sizeof(*L));
+    L->quant = v->quant;
+    L->rows = rows;
+    L->cols = cols;
+    L->row_bytes = cols / (size_t)f->block_elems * (size_t)f->block_bytes;
+    L->k_padded = (cols + 31) / 32 * 32;
+    L->n_tiles = (rows + TILE_N - 1) / TILE_N;
+    L->k_chunks = L->k_padded / TILE_K;
+    L->chunks_per_scale = repack_group_elems(v->quant) == 16 ? 1 : 2;
+    L->scale_groups = L->k_chunks / L->chunks_per_scale;
+    L->has_mins = repack_has_mins(v->quant) ? 1 : 0;
+    L->total_tiles = L->n_tiles * L->k_chunks;
+    L->total_scales = L->n_tiles * L->scale_groups * TILE_N;
+    L->total_mins = L->has_mins ? L->total_scales : 0;
+    return JKB_OK;
+}
+
+// repack_block_scaled_range_into_i8 (repack.rs:1724-2103) on the host for tiles [t0, t1):
+// zero-fills the outputs, then expands every block of every row of those tiles with the shared
+// decoder and scatters its values into the tile layout. No heap allocation.
+static void repack_tiles_host(const jkb_block_scaled_tile_layout &L, const uint8_t *raw, float i2s,
+                              size_t t0, size_t t1, int8_t *tiles, float *scales, float *mins) {
+    const size_t tile_stride = L.k_chunks * TILE_BYTES, sc_stride = L.scale_groups * TILE_N;
+    memset(tiles, 0, (t1 - t0) * tile_stride);
+    memset(scales, 0, (t1 - t0) * sc_stride * 4);
+    if (mins) memset(mins, 0, (t1 - t0) * sc_stride * 4);
+    const Fmt *f = fmt_of(L.quant);
+    const int be = repack_block_elems(L.quant), ge = repack_group_elems(L.quant), gpb = be / ge;
+    const size_t nb = L.cols / (size_t)be;
+    int8_t qb[256];
+    float sb[16], mb[16];
+    for (size_t nt = t0; nt < t1; nt++) {
+        int8_t *tb = tiles + (nt - t0) * tile_stride;
+        float *st = scales + (nt - t0) * sc_stride;
+        float *mt = mins ? mins + (nt - t0) * sc_stride : nullptr;
+        for (size_t j = 0; j < TILE_N; j++) {
+            const size_t row = nt * TILE_N + j;
+            if (row >= L.rows) break;
+            const uint8_t *rr = raw + row * L.row_bytes;
+            for (size_t b = 0; b < nb; b++) {
+                repack_block_i8(L.quant, rr + b * (size_t)f->block_bytes, qb, sb, mb, i2s);
+                for (int e = 0; e < be; e++) {
+                    const size_t k = b * (size_t)be + (size_t)e;
+                    tb[(k / TILE_K) * TILE_BYTES + j * TILE_K + k % TILE_K] = qb[e];
+                }
+                for (int g = 0; g < gpb; g++) {
+                    st[(b * (size_t)gpb + (size_t)g) * TILE_N + j] = sb[g];
+                    if (mt) mt[(b * (size_t)gpb + (size_t)g) * TILE_N + j] = mb[g];
+                }
+            }
+        }
+    }
+}
+
+// The reference tile layout -> the device layout: one thread per (row, 16-byte K chunk) and per
+// (row, scale group).
+__global__ void detile_kernel(const uint8_t *__restrict__ tiles, const float *__restrict__ sc,
+                              const float *__restrict__ mn, size_t rows, size_t k_chunks,
+                              size_t groups, int8_t *__restrict__ q, size_t k_pad,
+                              float *__restrict__ scales, float *__restrict__ mins) {
+    const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const size_t nq = rows * k_chunks;
+    if (idx < nq) {
+        const size_t r = idx / k_chunks, ch = idx % k_chunks;
+        const uint4 *src = reinterpret_cast<const uint4 *>(
+            tiles + (r / TILE_N) * k_chunks * TILE_BYTES + ch * TILE_BYTES + (r % TILE_N) * TILE_K);
+        *reinterpret_cast<uint4 *>(q + r * k_pad + ch * TILE_K) = *src;
+        return;
+    }
+    const size_t i = idx - nq;
+    if (i >= rows * groups) return;
+    const size_t r = i / groups, g = i % groups;
+    const size_t at = (r / TILE_N) * groups * TILE_N + g * TILE_N + r % TILE_N;
+    scales[r * groups + g] = sc[at];
+    if (mins) mins[r * groups + g] = mn[at];
+}
+
+static int check_tile_range(const jkb_tensor_view *v, const jkb_block_scaled_tile_layout &L,
+                            size_t t0, size_t t1) {
+    if (t0 > t1 || t1 > L.n_tiles)
+        return fail(JKB_E_BOUNDS, v->name ? v->name : "", t0, t1 > t0 ? t1 - t0 : 0, L.n_tiles,
+                    "tile_range %zu..%zu exceeds n_tiles (%zu)", t0, t1, L.n_tiles);
+    return JKB_OK;
+}
+
+static int host_raw(const jkb_tensor_view *v, const char *fn, const uint8_t **raw) {
+    if (!v->data || v->data_on_device)
+        return fail(JKB_E_INVALID, v->name ? v->name : "", v->offset, v->byte_len, v->byte_len,
+                    "%s reads host bytes", fn);
+    *raw = (const uint8_t *)v->data;
+    return JKB_OK;
+}
+
 }  // namespace jkb
 
 using namespace jkb;
@@ -698,6 +607,170 @@ int jkb_repacked_weight_buffers(const jkb_repacked_weight *w, size_t *rows, size
     if (q) *q = w->q;
     if (scales) *scales = w->scales;
     if (mins) *mins = w->mins;
+    return JKB_OK;
+}
+
+
+int jkb_block_scaled_layout(const jkb_tensor_view *view, size_t rows, size_t cols,
+                            jkb_block_scaled_tile_layout *out) {
+    if (!view || !out) return fail(JKB_E_INVALID, "block_scaled_layout", 0, 0, 0, "null argument");
+    return block_layout(view, rows, cols, "block_scaled_layout", out);
+}
+
+int jkb_repack_into_tile_range(const jkb_tensor_view *view, size_t rows, size_t cols,
+                               size_t tile_begin, size_t tile_end, uint8_t *out_tiles,
+                               size_t n_out_tiles, float *out_scales, size_t n_scales,
+                               float *out_mins, size_t n_mins) {
+    static const char *fn = "repack_into_tile_range";
+    if (!view) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null view");
+    jkb_block_scaled_tile_layout L;
+    int rc = block_layout(view, rows, cols, fn, &L);
+    if (rc || (rc = check_tile_range(view, L, tile_begin, tile_end))) return rc;
+    const char *nm = view->name ? view->name : "";
+    const size_t sub = tile_end - tile_begin, exp_tiles = sub * L.k_chunks,
+                 exp_scales = sub * L.scale_groups * TILE_N;
+    if (n_out_tiles != exp_tiles || n_scales != exp_scales ||
+        (exp_tiles && (!out_tiles || !out_scales)))
+        return fail(JKB_E_BOUNDS, nm, tile_begin, n_out_tiles, exp_tiles,
+                    "tile/scale slice lengths (%zu, %zu) != expected (%zu, %zu)", n_out_tiles,
+                    n_scales, exp_tiles, exp_scales);
+    if (L.has_mins) {
+        if (!out_mins)
+            return fail(JKB_E_BOUNDS, nm, tile_begin, 0, exp_scales, "%s requires out_mins slice",
+                        quant_name(L.quant));
+        if (n_mins != exp_scales)
+            return fail(JKB_E_BOUNDS, nm, tile_begin, n_mins, exp_scales,
+                        "out_mins length %zu != expected %zu", n_mins, exp_scales);
+    }
+    const uint8_t *raw = nullptr;
+    if ((rc = host_raw(view, fn, &raw))) return rc;
+    if (sub == 0) return JKB_OK;
+    const float i2s = L.quant == JKB_I2_S ? read_i2s_trailer(view, L.rows * L.row_bytes) : 0.0f;
+    repack_tiles_host(L, raw, i2s, tile_begin, tile_end, (int8_t *)out_tiles, out_scales,
+                      L.has_mins ? out_mins : nullptr);
+    return JKB_OK;
+}
+
+int jkb_repack_q4_k_m_parallel_slices(const jkb_tensor_view *view, size_t rows, size_t cols,
+                                      size_t tile_begin, size_t tile_end, int8_t *out_tiles_i8,
+                                      size_t tiles_len, float *out_scales, size_t n_scales,
+                                      float *out_mins, size_t n_mins) {
+    static const char *fn = "repack_q4_k_m_parallel_slices";
+    if (!view) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null view");
+    const char *nm = view->name ? view->name : "";
+    if (view->quant != JKB_Q4_K_M)
+        return fail(JKB_E_CAPABILITY, nm, view->offset, view->byte_len, view->byte_len,
+                    "%s: unsupported tensor quant %s", fn, quant_name(view->quant));
+    jkb_block_scaled_tile_layout L;
+    int rc = block_layout(view, rows, cols, fn, &L);
+    if (rc || (rc = check_tile_range(view, L, tile_begin, tile_end))) return rc;
+    const size_t sub = tile_end - tile_begin, exp_bytes = sub * L.k_chunks * TILE_BYTES,
+                 exp_scales = sub * L.scale_groups * TILE_N;
+    if (tiles_len != exp_bytes || n_scales != exp_scales || n_mins != exp_scales ||
+        (exp_bytes && (!out_tiles_i8 || !out_scales || !out_mins)))
+        return fail(JKB_E_BOUNDS, nm, tile_begin, tiles_len, exp_bytes,
+                    "parallel slice lengths (%zu, %zu, %zu) != expected (%zu, %zu, %zu)",
+                    tiles_len, n_scales, n_mins, exp_bytes, exp_scales, exp_scales);
+    const uint8_t *raw = nullptr;
+    if ((rc = host_raw(view, fn, &raw))) return rc;
+    if (sub == 0) return JKB_OK;
+    repack_tiles_host(L, raw, 0.0f, tile_begin, tile_end, out_tiles_i8, out_scales, out_mins);
+    return JKB_OK;
+}
+
+int jkb_repacked_weight_from_tile_buffers(const jkb_block_scaled_tile_layout *layout,
+                                          const uint8_t *tiles, size_t n_tiles,
+                                          const float *scales, size_t n_scales,
+                                          const float *mins, size_t n_mins, void *stream,
+                                          jkb_repacked_weight **out) {
+    static const char *fn = "RepackedWeight::from_tile_buffers";
+    if (!layout || !out) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null argument");
+    *out = nullptr;
+    const jkb_block_scaled_tile_layout &L = *layout;
+    // the layout must be one block_scaled_layout produced (its fields follow from quant, rows
+    // and cols)
+    const Fmt *f = fmt_of(L.quant);
+    if (!f) return fail(JKB_E_CAPABILITY, fn, 0, 0, 0, "unsupported tensor quant %s",
+                        quant_name(L.quant));
+    const size_t kp = (L.cols + 31) / 32 * 32, ge = (size_t)repack_group_elems(L.quant);
+    if (L.rows == 0 || L.cols == 0 || L.cols % (size_t)f->block_elems || L.k_padded != kp ||
+        L.n_tiles != (L.rows + TILE_N - 1) / TILE_N || L.k_chunks != kp / TILE_K ||
+        L.chunks_per_scale != ge / TILE_K || L.scale_groups != kp / ge ||
+        L.has_mins != (repack_has_mins(L.quant) ? 1 : 0) ||
+        L.row_bytes != L.cols / (size_t)f->block_elems * (size_t)f->block_bytes ||
+        L.total_tiles != L.n_tiles * L.k_chunks ||
+        L.total_scales != L.n_tiles * L.scale_groups * TILE_N ||
+        L.total_mins != (L.has_mins ? L.total_scales : 0))
+        return fail(JKB_E_BOUNDS, fn, 0, 0, 0,
+                    "layout fields do not describe a %s [%zu, %zu] block-scaled layout",
+                    quant_name(L.quant), L.rows, L.cols);
+    if (n_tiles != L.total_tiles || n_scales != L.total_scales)
+        return fail(JKB_E_BOUNDS, fn, 0, n_tiles, L.total_tiles,
+                    "buffer lengths (%zu, %zu) != expected (%zu, %zu)", n_tiles, n_scales,
+                    L.total_tiles, L.total_scales);
+    if (L.has_mins) {
+        if (!mins || n_mins != L.total_mins)
+            return fail(JKB_E_BOUNDS, fn, 0, mins ? n_mins : 0, L.total_mins,
+                        "%s requires mins buffer of length %zu", quant_name(L.quant),
+                        L.total_mins);
+    } else if (mins) {
+        return fail(JKB_E_BOUNDS, fn, 0, n_mins, 0, "%s does not use mins buffer",
+                    quant_name(L.quant));
+    }
+    if (!tiles || !scales) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null buffer");
+    cudaStream_t st = as_stream(stream);
+    jkb_repacked_weight *w = new jkb_repacked_weight();
+    memset(w, 0, sizeof(*w));
+    w->magic = REPACKED_MAGIC;
+    w->quant = L.quant;
+    w->rows = L.rows;
+    w->cols = L.cols;
+    w->k_pad = kp;
+    w->group_elems = ge;
+    w->scale_groups = L.scale_groups;
+    snprintf(w->name, sizeof(w->name), "%s", "from_tile_buffers");
+    Arena a;
+    const size_t qb = L.rows * kp, sb = L.rows * L.scale_groups * 4;
+    a.cap = Arena::round(qb) + Arena::round(sb) * (L.has_mins ? 2 : 1);
+    // staging of the host tiles (freed before returning): tiles, scales, mins
+    const size_t tb = L.total_tiles * TILE_BYTES, ssb = L.total_scales * 4;
+    Arena s;
+    s.cap = Arena::round(tb) + Arena::round(ssb) * (L.has_mins ? 2 : 1);
+    cudaError_t e = cudaMalloc(&a.base, a.cap);
+    if (e != cudaSuccess) {
+        delete w;
+        return fail_cuda(e, "from_tile_buffers (device buffers)");
+    }
+    e = cudaMalloc(&s.base, s.cap);
+    if (e != cudaSuccess) {
+        cudaFree(a.base);
+        delete w;
+        return fail_cuda(e, "from_tile_buffers (staging)");
+    }
+    w->base = a.base;
+    w->device_bytes = a.cap;
+    w->q = (int8_t *)a.take(qb);
+    w->scales = (float *)a.take(sb);
+    w->mins = L.has_mins ? (float *)a.take(sb) : nullptr;
+    uint8_t *d_tiles = s.take(tb);
+    float *d_sc = (float *)s.take(ssb), *d_mn = L.has_mins ? (float *)s.take(ssb) : nullptr;
+    cudaMemcpyAsync(d_tiles, tiles, tb, cudaMemcpyHostToDevice, st);
+    cudaMemcpyAsync(d_sc, scales, ssb, cudaMemcpyHostToDevice, st);
+    if (d_mn) cudaMemcpyAsync(d_mn, mins, ssb, cudaMemcpyHostToDevice, st);
+    const size_t n = L.rows * (L.k_chunks + L.scale_groups);
+    detile_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(d_tiles, d_sc, d_mn, L.rows,
+                                                               L.k_chunks, L.scale_groups, w->q,
+                                                               kp, w->scales, w->mins);
+    int rc = check_launch("detile_kernel");
+    e = cudaStreamSynchronize(st);
+    cudaFree(s.base);
+    if (!rc && e != cudaSuccess) rc = fail_cuda(e, "from_tile_buffers");
+    if (rc) {
+        cudaFree(a.base);
+        delete w;
+        return rc;
+    }
+    *out = w;
     return JKB_OK;
 }
 

@@ -45,6 +45,37 @@ class jkb_error_info(C.Structure):
     ]
 
 
+class jkb_block_scaled_tile_layout(C.Structure):
+    _fields_ = [
+        ("quant", C.c_int32),
+        ("has_mins", C.c_int32),
+        ("rows", C.c_size_t),
+        ("cols", C.c_size_t),
+        ("row_bytes", C.c_size_t),
+        ("k_padded", C.c_size_t),
+        ("n_tiles", C.c_size_t),
+        ("k_chunks", C.c_size_t),
+        ("chunks_per_scale", C.c_size_t),
+        ("scale_groups", C.c_size_t),
+        ("total_tiles", C.c_size_t),
+        ("total_scales", C.c_size_t),
+        ("total_mins", C.c_size_t),
+    ]
+
+
+class jkb_act_q8_view(C.Structure):
+    _fields_ = [
+        ("m", C.c_size_t),
+        ("k", C.c_size_t),
+        ("k_padded", C.c_size_t),
+        ("q", C.c_void_p),
+        ("x_scales", C.c_void_p),
+        ("x_sums", C.c_void_p),
+        ("x_sums_16", C.c_void_p),
+        ("super_scales", C.c_void_p),
+    ]
+
+
 P, S, I, F = C.c_void_p, C.c_size_t, C.c_int, C.c_float
 PP = C.POINTER(C.c_void_p)
 PS = C.POINTER(C.c_size_t)
@@ -154,8 +185,39 @@ SIGNATURES = {
     "jkb_packed_nibble_matrix_dequantize_row": [P, S, P, S, P],
     "jkb_gemm_q4_0_ime": [P, S, P, P, P],
     "jkb_gemm_q4_k_ime": [P, S, P, P, P],
+    "jkb_quantize_row_f32_to_q8_32": [P, S, P, S, P, S, P, S, P],
+    "jkb_scratch_create": [S, PP],
+    "jkb_scratch_wrap": [P, S, PP],
+    "jkb_scratch_destroy": [P],
+    "jkb_scratch_reset": [P],
+    "jkb_scratch_used_bytes": [P, PS],
+    "jkb_scratch_remaining_bytes": [P, PS],
+    "jkb_scratch_alloc": [P, S, PP],
+    "jkb_scratch_scope_begin": [P, PS],
+    "jkb_scratch_scope_end": [P, S],
+    "jkb_quantize_row_q8_0_in_scratch": [P, S, P, PP, P],
+    "jkb_quantize_row_q8_0_in_scope": [P, S, P, PP, P],
+    "jkb_quantize_row_q8_k_in_scratch": [P, S, P, PP, P],
+    "jkb_quantize_row_q8_k_in_scope": [P, S, P, PP, P],
+    "jkb_act_q8_view_scratch_bytes_for_row": [S],
+    "jkb_act_q8_view_quantize_row_in_scratch": [P, S, P, C.POINTER(jkb_act_q8_view), P],
+    "jkb_act_q8_view_quantize_row_in_scope": [P, S, P, C.POINTER(jkb_act_q8_view), P],
+    "jkb_act_q8_as_view": [P, C.POINTER(jkb_act_q8_view)],
+    "jkb_gemv_repacked_view": [P, S, P, C.POINTER(jkb_act_q8_view), P],
+    "jkb_gemv_repacked_view_rows": [P, S, P, C.POINTER(jkb_act_q8_view), S, S, P],
+    "jkb_gemv_repacked_f32": [P, S, P, P, S, P, P],
+    "jkb_gemv_repacked_f32_rows": [P, S, P, P, S, S, S, P, P],
+    "jkb_gemm_repacked_f32_rows": [P, S, P, P, S, S, S, S, P, P],
+    "jkb_block_scaled_layout": [C.POINTER(jkb_tensor_view), S, S,
+                                C.POINTER(jkb_block_scaled_tile_layout)],
+    "jkb_repack_into_tile_range": [C.POINTER(jkb_tensor_view), S, S, S, S, P, S, P, S, P, S],
+    "jkb_repack_q4_k_m_parallel_slices": [C.POINTER(jkb_tensor_view), S, S, S, S, P, S, P, S, P,
+                                          S],
+    "jkb_repacked_weight_from_tile_buffers": [C.POINTER(jkb_block_scaled_tile_layout), P, S, P, S,
+                                              P, S, P, PP],
 }
-_RESTYPE = {"jkb_last_error": C.c_char_p, "jkb_clear_error": None}
+_RESTYPE = {"jkb_last_error": C.c_char_p, "jkb_clear_error": None,
+            "jkb_act_q8_view_scratch_bytes_for_row": C.c_size_t}
 
 _lib = None
 

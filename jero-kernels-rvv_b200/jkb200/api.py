@@ -36,6 +36,12 @@ __all__ = [
     "gemv_q5_0_q8_0", "gemv_q5_0_q8_0_4x", "gemv_q5_k_q8_k", "vec_dot_q5_0", "vec_dot_q5_k",
     "vec_dot_q5_0_rvv", "vec_dot_q5_k_rvv", "relu_squared_gate_f32",
     "relu_squared_subln_quantize_i8_rows", "BitNetFFN", "bitlinear_i8_gemm",
+    "quantize_row_f32_to_q8_32", "ScratchWorkspace", "ScratchScope",
+    "quantize_row_q8_0_in_scratch", "quantize_row_q8_0_in_scope", "quantize_row_q8_k_in_scratch",
+    "quantize_row_q8_k_in_scope", "QuantizedActQ8View", "gemv_repacked_view",
+    "gemv_repacked_view_rows", "gemv_repacked_f32", "gemv_repacked_f32_rows",
+    "gemm_repacked_f32_rows", "BlockScaledTileLayout", "block_scaled_layout",
+    "repack_into_tile_range", "repack_q4_k_m_parallel_slices",
 ]
 
 
@@ -319,6 +325,12 @@ class QuantizedActQ8:
                 device_view(ptrs[3].value, (m, kp // 16), "<f4"),
                 device_view(ptrs[4].value, (m, (k + 255) // 256), "<f4"))
 
+    def as_view(self) -> "QuantizedActQ8View":
+        """repack.rs:708 QuantizedActQ8::as_view: the current batch as a borrowed view."""
+        v = _lib.jkb_act_q8_view()
+        _check(_L().jkb_act_q8_as_view(self._h, C.byref(v)))
+        return QuantizedActQ8View(v, owner=self)
+
     def destroy(self):
         if getattr(self, "_h", None):
             _L().jkb_act_q8_destroy(self._h)
@@ -390,6 +402,34 @@ class RepackedWeight:
 
     def gemm_rows(self, out, act, row_range, stream=None):
         gemm_repacked_rows(out, self, act, row_range, stream)
+
+    def gemv_view(self, out, act: "QuantizedActQ8View", stream=None):
+        """repack.rs:2628 RepackedWeight::gemv_view."""
+        gemv_repacked_view(out, self, act, stream)
+
+    def gemv_view_rows(self, out, act: "QuantizedActQ8View", row_range, stream=None):
+        """repack.rs:2638 RepackedWeight::gemv_view_rows."""
+        gemv_repacked_view_rows(out, self, act, row_range, stream)
+
+    @classmethod
+    def block_scaled_layout(cls, view: TensorView, rows: int, cols: int):
+        """repack.rs:2372 RepackedWeight::block_scaled_layout."""
+        return block_scaled_layout(view, rows, cols)
+
+    @classmethod
+    def from_tile_buffers(cls, layout: "BlockScaledTileLayout", tiles, scales, mins=None,
+                          stream=None):
+        """repack.rs:2386 RepackedWeight::from_tile_buffers: host numpy buffers in the
+        reference tile layout (tiles: total_tiles x 128 bytes, scales / mins: f32)."""
+        t = np.ascontiguousarray(tiles).view(np.uint8).reshape(-1)
+        s = np.ascontiguousarray(scales, np.float32).reshape(-1)
+        mn = None if mins is None else np.ascontiguousarray(mins, np.float32).reshape(-1)
+        h = C.c_void_p()
+        _check(_L().jkb_repacked_weight_from_tile_buffers(
+            C.byref(layout._c), t.ctypes.data, t.size // 128, s.ctypes.data, s.size,
+            None if mn is None else mn.ctypes.data, 0 if mn is None else mn.size,
+            _stream(stream), C.byref(h)))
+        return cls(h.value, "from_tile_buffers")
 
     def destroy(self):
         if getattr(self, "_h", None):
@@ -1003,3 +1043,246 @@ def gemm_repacked_f32_noalloc(out, weights, x, m, stream=None):
     and race, so serialize them. No counterpart in the reference."""
     _check(_L().jkb_gemm_repacked_f32_noalloc(_dptr(out), out.numel(), weights._h, _dptr(x),
                                               x.numel(), m, _stream(stream)))
+
+
+# ------------------------------------------------------------------------------- row quantizer
+
+def quantize_row_f32_to_q8_32(x, out_quants, out_scales, out_sums, stream=None):
+    """repack.rs:441 quantize_row_f32_to_q8_32: device f32 x -> i8 quants (round_up(len, 32)),
+    per-32 scales and sequential f32 sums (device tensors)."""
+    _check(_L().jkb_quantize_row_f32_to_q8_32(_dptr(x), x.numel(), _dptr(out_quants),
+                                              out_quants.numel(), _dptr(out_scales),
+                                              out_scales.numel(), _dptr(out_sums),
+                                              out_sums.numel(), _stream(stream)))
+
+
+# ------------------------------------------------------------------------------- scratch arenas
+
+class ScratchWorkspace:
+    """jero_core::ScratchWorkspace on the device: a bump arena of `nbytes` (allocated here), or
+    over a caller-owned CUDA tensor (`wrap`, nothing allocated). Carves start at 128 bytes."""
+
+    def __init__(self, nbytes: int = None, *, wrap: torch.Tensor = None):
+        h = C.c_void_p()
+        if wrap is not None:
+            self._keep = wrap
+            _check(_L().jkb_scratch_wrap(_dptr(wrap), wrap.numel() * wrap.element_size(),
+                                         C.byref(h)))
+        else:
+            _check(_L().jkb_scratch_create(nbytes, C.byref(h)))
+        self._h = h.value
+
+    @property
+    def handle(self):
+        if self._h is None:
+            raise InvalidHandle(6, "ScratchWorkspace", 0, 0, 0, "scratch destroyed")
+        return self._h
+
+    def reset(self):
+        _check(_L().jkb_scratch_reset(self.handle))
+
+    def used_bytes(self) -> int:
+        v = C.c_size_t()
+        _check(_L().jkb_scratch_used_bytes(self.handle, C.byref(v)))
+        return v.value
+
+    def remaining_bytes(self) -> int:
+        v = C.c_size_t()
+        _check(_L().jkb_scratch_remaining_bytes(self.handle, C.byref(v)))
+        return v.value
+
+    def alloc(self, nbytes: int) -> int:
+        """Carves nbytes; returns the device address."""
+        p = C.c_void_p()
+        _check(_L().jkb_scratch_alloc(self.handle, nbytes, C.byref(p)))
+        return p.value
+
+    def scope(self) -> "ScratchScope":
+        """ScratchWorkspace::scope: carves inside the `with` block are released at its end."""
+        return ScratchScope(self)
+
+    def destroy(self):
+        if getattr(self, "_h", None):
+            _L().jkb_scratch_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+class ScratchScope:
+    """jero_core::ScratchScope: a saved cursor of a workspace, rewound on exit."""
+
+    def __init__(self, ws: ScratchWorkspace):
+        self.ws = ws
+        self.handle = ws.handle
+
+    def __enter__(self):
+        m = C.c_size_t()
+        _check(_L().jkb_scratch_scope_begin(self.ws.handle, C.byref(m)))
+        self.mark = m.value
+        return self
+
+    def __exit__(self, *exc):
+        _check(_L().jkb_scratch_scope_end(self.ws.handle, self.mark))
+        return False
+
+
+def _in_scratch(fn, x, ws, bb, stream):
+    p = C.c_void_p()
+    _check(getattr(_L(), fn)(_dptr(x), x.numel(), ws.handle, C.byref(p), _stream(stream)))
+    n = x.numel() // (32 if bb == BLOCK_Q8_0_BYTES else 256)
+    return device_view(p.value, (n * bb,), "u1")
+
+
+def quantize_row_q8_0_in_scratch(x, ws: ScratchWorkspace, stream=None) -> torch.Tensor:
+    """quant_q8.rs:405: BlockQ8_0 blocks carved from the arena (a uint8 device view)."""
+    return _in_scratch("jkb_quantize_row_q8_0_in_scratch", x, ws, BLOCK_Q8_0_BYTES, stream)
+
+
+def quantize_row_q8_0_in_scope(x, scope: ScratchScope, stream=None) -> torch.Tensor:
+    """quant_q8.rs:429."""
+    return _in_scratch("jkb_quantize_row_q8_0_in_scope", x, scope, BLOCK_Q8_0_BYTES, stream)
+
+
+def quantize_row_q8_k_in_scratch(x, ws: ScratchWorkspace, stream=None) -> torch.Tensor:
+    """quant_q8.rs:602: BlockQ8K blocks carved from the arena (a uint8 device view)."""
+    return _in_scratch("jkb_quantize_row_q8_k_in_scratch", x, ws, BLOCK_Q8_K_BYTES, stream)
+
+
+def quantize_row_q8_k_in_scope(x, scope: ScratchScope, stream=None) -> torch.Tensor:
+    """quant_q8.rs:626."""
+    return _in_scratch("jkb_quantize_row_q8_k_in_scope", x, scope, BLOCK_Q8_K_BYTES, stream)
+
+
+class QuantizedActQ8View:
+    """QuantizedActQ8View (repack.rs:806-1090): quantized activations in device memory the
+    library does not own (an arena's planes or a QuantizedActQ8's)."""
+
+    def __init__(self, c_view, owner=None):
+        self._c = c_view
+        self._owner = owner  # keeps the arena or handle alive
+        self.m, self.k, self.k_padded = c_view.m, c_view.k, c_view.k_padded
+
+    @staticmethod
+    def scratch_bytes_for_row(k: int) -> int:
+        """repack.rs:824."""
+        return int(_L().jkb_act_q8_view_scratch_bytes_for_row(k))
+
+    @classmethod
+    def quantize_row_in_scratch(cls, act, ws: ScratchWorkspace, stream=None):
+        """repack.rs:870."""
+        v = _lib.jkb_act_q8_view()
+        _check(_L().jkb_act_q8_view_quantize_row_in_scratch(_dptr(act), act.numel(), ws.handle,
+                                                            C.byref(v), _stream(stream)))
+        return cls(v, ws)
+
+    @classmethod
+    def quantize_row_in_scope(cls, act, scope: ScratchScope, stream=None):
+        """repack.rs:969."""
+        v = _lib.jkb_act_q8_view()
+        _check(_L().jkb_act_q8_view_quantize_row_in_scope(_dptr(act), act.numel(),
+                                                          scope.handle, C.byref(v),
+                                                          _stream(stream)))
+        return cls(v, scope)
+
+    def buffers(self):
+        """Zero-copy device views: q, x_scales, x_sums, x_sums_16, super_scales."""
+        c, m, kp = self._c, self.m, self.k_padded
+        return (device_view(c.q, (m, kp), "i1"), device_view(c.x_scales, (m, kp // 32), "<f4"),
+                device_view(c.x_sums, (m, kp // 32), "<f4"),
+                device_view(c.x_sums_16, (m, kp // 16), "<f4"),
+                device_view(c.super_scales, (m, (self.k + 255) // 256), "<f4"))
+
+
+def gemv_repacked_view(out, weights: RepackedWeight, act: QuantizedActQ8View, stream=None):
+    """repack.rs:4030 gemv_repacked_view."""
+    _check(_L().jkb_gemv_repacked_view(_dptr(out), out.numel(), weights._h, C.byref(act._c),
+                                       _stream(stream)))
+
+
+def gemv_repacked_view_rows(out, weights: RepackedWeight, act: QuantizedActQ8View, row_range,
+                            stream=None):
+    """repack.rs:4045 gemv_repacked_view_rows."""
+    _check(_L().jkb_gemv_repacked_view_rows(_dptr(out), out.numel(), weights._h,
+                                            C.byref(act._c), row_range.start, row_range.stop,
+                                            _stream(stream)))
+
+
+def gemv_repacked_f32(out, weights: RepackedWeight, x, scratch: QuantizedActQ8, stream=None):
+    """repack.rs:4101 gemv_repacked_f32 (the quantized row goes to the caller's handle)."""
+    _check(_L().jkb_gemv_repacked_f32(_dptr(out), out.numel(), weights._h, _dptr(x), x.numel(),
+                                      scratch._h, _stream(stream)))
+
+
+def gemv_repacked_f32_rows(out, weights: RepackedWeight, x, row_range, scratch: QuantizedActQ8,
+                           stream=None):
+    """repack.rs:4114 gemv_repacked_f32_rows."""
+    _check(_L().jkb_gemv_repacked_f32_rows(_dptr(out), out.numel(), weights._h, _dptr(x),
+                                           x.numel(), row_range.start, row_range.stop,
+                                           scratch._h, _stream(stream)))
+
+
+def gemm_repacked_f32_rows(out, weights: RepackedWeight, x, m, row_range,
+                           scratch: QuantizedActQ8, stream=None):
+    """repack.rs:4143 gemm_repacked_f32_rows."""
+    _check(_L().jkb_gemm_repacked_f32_rows(_dptr(out), out.numel(), weights._h, _dptr(x),
+                                           x.numel(), m, row_range.start, row_range.stop,
+                                           scratch._h, _stream(stream)))
+
+
+# ------------------------------------------------------------------------------- load path
+
+class BlockScaledTileLayout:
+    """BlockScaledTileLayout (repack.rs:1286-1449) as block_scaled_layout fills it."""
+
+    def __init__(self, c_layout):
+        self._c = c_layout
+        for name, _ in _lib.jkb_block_scaled_tile_layout._fields_:
+            setattr(self, name, getattr(c_layout, name))
+        self.quant = QuantType(self.quant)
+        self.has_mins = bool(self.has_mins)
+
+
+def block_scaled_layout(view: TensorView, rows: int, cols: int) -> BlockScaledTileLayout:
+    """repack.rs:2372 RepackedWeight::block_scaled_layout (host only)."""
+    L = _lib.jkb_block_scaled_tile_layout()
+    v = view._c()
+    _check(_L().jkb_block_scaled_layout(C.byref(v), rows, cols, C.byref(L)))
+    return BlockScaledTileLayout(L)
+
+
+def repack_into_tile_range(view: TensorView, rows: int, cols: int, tile_range, out_tiles=None,
+                           out_scales=None, out_mins=None):
+    """repack.rs:1579 repack_into_tile_range on host buffers (allocated here when not given):
+    returns (tiles [tiles * k_chunks][128] u8, scales f32, mins f32 or None)."""
+    L = block_scaled_layout(view, rows, cols)
+    n = len(tile_range)
+    if out_tiles is None:
+        out_tiles = np.zeros((n * L.k_chunks, 128), np.uint8)
+    if out_scales is None:
+        out_scales = np.zeros(n * L.scale_groups * 8, np.float32)
+    if out_mins is None and L.has_mins:
+        out_mins = np.zeros(n * L.scale_groups * 8, np.float32)
+    v = view._c()
+
+    def ptr(a):
+        return None if a is None else a.ctypes.data
+    _check(_L().jkb_repack_into_tile_range(
+        C.byref(v), rows, cols, tile_range.start, tile_range.stop, ptr(out_tiles),
+        out_tiles.size // 128, ptr(out_scales), out_scales.size, ptr(out_mins),
+        0 if out_mins is None else out_mins.size))
+    return out_tiles, out_scales, out_mins
+
+
+def repack_q4_k_m_parallel_slices(view: TensorView, rows: int, cols: int, tile_range,
+                                  out_tiles_i8, out_scales, out_mins):
+    """repack.rs:1659 repack_q4_k_m_parallel_slices (host numpy buffers)."""
+    v = view._c()
+    _check(_L().jkb_repack_q4_k_m_parallel_slices(
+        C.byref(v), rows, cols, tile_range.start, tile_range.stop, out_tiles_i8.ctypes.data,
+        out_tiles_i8.size, out_scales.ctypes.data, out_scales.size, out_mins.ctypes.data,
+        out_mins.size))
