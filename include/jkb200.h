@@ -231,7 +231,7 @@ typedef struct {
     float *x_sums_16;
     float *super_scales;
 } jkb_act_q8_view;
-/* repack.rs:824 QuantizedActQ8View::scratch_bytes_for_row: arena bytes one row of k needs,
+/* repack.rs:827 QuantizedActQ8View::scratch_bytes_for_row: arena bytes one row of k needs,
  * alignment padding included (0 for k == 0). */
 size_t jkb_act_q8_view_scratch_bytes_for_row(size_t k);
 /* repack.rs:870 quantize_row_in_scratch / :969 quantize_row_in_scope: quantizes one device f32

@@ -1169,7 +1169,7 @@ class QuantizedActQ8View:
 
     @staticmethod
     def scratch_bytes_for_row(k: int) -> int:
-        """repack.rs:824."""
+        """repack.rs:827."""
         return int(_L().jkb_act_q8_view_scratch_bytes_for_row(k))
 
     @classmethod

@@ -10,8 +10,8 @@ and repack_q4_k_m_parallel_slices (:1659), through the C ABI.
 * Tile ranges stitch: disjoint ranges filled separately (as the reference's worker threads do,
   tests/wave3_prefill_gqa_and_gemm.rs:281-363) concatenate to the whole range.
 * Validation fails closed like the reference: ranges past n_tiles, wrong slice lengths, a
-  missing mins slice, dense or non-Q4_K_M formats, device-resident bytes.
-* QuantizedActQ8View::scratch_bytes_for_row (repack.rs:824) on the host."""
+  missing mins slice, dense or non-Q4_K_M formats.
+* QuantizedActQ8View::scratch_bytes_for_row (repack.rs:827) on the host."""
 import ctypes as C
 
 import numpy as np
