@@ -386,8 +386,12 @@ class DecodeSet:
         self.peer = peer and world > 1
         self.unfused, self.prequant = unfused, set(prequant) - {""}
         names = [(name, rows) for name, _, rows, _, _ in mats]
+        # two output slots alternate by step parity (a step's outputs stay readable while the
+        # next step runs): the peer group's two slots, or two flat NCCL / single-GPU buffers
         self.outs = (PeerOutputs(names, world, rank, batch=batch) if self.peer
                      else ShardedOutputs(names, world, rank, batch=batch))
+        self.outs2 = (None if self.peer
+                      else [self.outs, ShardedOutputs(names, world, rank, batch=batch)])
         self.weights, self.shards, self.bytes_per_step = {}, [], 0
         for i, (name, quant, rows, cols, s) in enumerate(mats):
             rr = self.outs.rows_of(name)
@@ -401,12 +405,18 @@ class DecodeSet:
         g = torch.Generator(device="cpu").manual_seed(7)
         # all activation streams in one device buffer: the e2e loop moves a step's inputs with
         # one host-to-device copy
-        self.x_all = torch.cat([torch.randn(batch * n, generator=g) for n in acts.values()]).cuda()
-        self.xs, self.xq, off = {}, {}, 0
+        # (two input slots alternate by step parity like the outputs: the e2e loop copies the
+        # next step's inputs in while a step runs)
+        x0 = torch.cat([torch.randn(batch * n, generator=g) for n in acts.values()])
+        self.x_slots = [x0.cuda(), x0.cuda()]
+        self.x_all = self.x_slots[0]
+        self.xs_slots, self.xq, off = [{}, {}], {}, 0
         for s, n in acts.items():
-            self.xs[s] = self.x_all[off:off + batch * n]
+            for k in range(2):
+                self.xs_slots[k][s] = self.x_slots[k][off:off + batch * n]
             self.xq[s] = jkb.empty_q8_k_blocks(batch * n // 256)
             off += batch * n
+        self.xs = self.xs_slots[0]
         self.groups = {}  # activation stream -> matrices fed by it, in mats order
         for name, quant, per, cols, s, copies in self.shards:
             self.groups.setdefault(s, []).append((name, copies))
@@ -423,21 +433,24 @@ class DecodeSet:
         return n
 
     def lslice(self, name, i):
-        return self.outs.local_slice(name, i % 2) if self.peer else self.outs.local_slice(name)
+        if self.peer:
+            return self.outs.local_slice(name, i % 2)
+        return self.outs2[i % 2].local_slice(name)
 
     def run_group(self, s, i):
         jkb = self.jkb
         items = [(self.lslice(n, i), self.weights[(n, i % c)]) for n, c in self.groups[s]]
+        xs = self.xs_slots[i % 2]
         if self.batch > 1:
-            jkb.quantize_rows_q8_k(self.xs[s], self.batch, self.acts[s], self.xq[s])
+            jkb.quantize_rows_q8_k(xs[s], self.batch, self.acts[s], self.xq[s])
             for out, w in items:
                 jkb.gemv_batch(out, w, self.xq[s], self.batch)
         elif self.unfused or s in self.prequant:
-            jkb.quantize_row_q8_k(self.xs[s], self.xq[s])
+            jkb.quantize_row_q8_k(xs[s], self.xq[s])
             for out, w in items:
                 jkb.gemv_rows(out, w, self.xq[s], range(0, w.rows))
         else:
-            jkb.vec_dot_grouped_rvv(items, self.xs[s])
+            jkb.vec_dot_grouped_rvv(items, xs[s])
 
     def layer_part(self, i):
         for s in self.groups:
@@ -448,7 +461,7 @@ class DecodeSet:
         if self.peer:
             self.outs.gather(i % 2)
         else:
-            self.outs.gather()
+            self.outs2[i % 2].gather()
 
     def step(self, i, marks=None, stream=None):
         """One step. `marks`: 4 events recorded before the layer GEMVs, before the lm_head group,
@@ -469,16 +482,17 @@ class DecodeSet:
         """Full output of matrix `name` after step i: [rows], or [batch][rows]."""
         if self.peer:
             return self.outs.output(name, i % 2)
+        o = self.outs2[i % 2]
         if self.world == 1:
-            t = self.outs.local_slice(name)
+            t = o.local_slice(name)
             return t if self.batch == 1 else t.view(self.batch, -1)
-        return self.outs.output(name)
+        return o.output(name)
 
     def full(self, i):
         """The buffer holding every matrix's full output after step i (the e2e read-back)."""
         if self.peer:
             return self.outs.full(i % 2)
-        return self.outs.gathered
+        return self.outs2[i % 2].gathered
 
     def destroy(self):
         for w in self.weights.values():
@@ -564,36 +578,70 @@ def time_decode(ds, steps, warmup, stream, world, local=0, sample_clocks=False):
             "gather_ms": split[2], "clocks": clocks}
 
 
-def e2e_decode(ds, steps, warmup, world):
+def e2e_decode(ds, steps, warmup, world, stream):
     """The same steps through the public API with host buffers: every step copies its f32 inputs
-    in from pinned host memory and its full outputs out to pinned host memory, eager launches,
-    timed with CUDA events on the launching stream (max over ranks)."""
+    in from pinned host memory and its full outputs out to pinned host memory, with eager
+    launches. The copies run on a second stream and overlap the neighbouring steps' kernels:
+    step i's inputs arrive in input slot i % 2 while step i - 1 runs, and its outputs leave from
+    output slot i % 2 while step i + 1 runs; events order each copy after what it depends on and
+    before what would overwrite it (including a peer's push into the slot, which cannot happen
+    before this rank's all-gather of step i + 1, so that all-gather waits for the read-back of
+    step i). Timed with CUDA events on the compute stream from before the first copy in to after
+    the last copy out, max over ranks. Also reports the host's time per step to enqueue the
+    calls."""
     import torch
     import torch.distributed as dist
 
-    host_in = ds.x_all.cpu().pin_memory()
-    host_out = torch.empty(ds.full(0).numel(), dtype=torch.float32).pin_memory()
+    copy = torch.cuda.Stream()
+    host_in = [ds.x_slots[0].cpu().pin_memory(), ds.x_slots[1].cpu().pin_memory()]
+    n_out = ds.full(0).numel()
+    host_out = [torch.empty(n_out, dtype=torch.float32).pin_memory() for _ in range(2)]
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    h2d_done, comp_done, d2h_done, read_done = ({}, {}, {}, {})
 
-    def e2e_step(i):
-        ds.x_all.copy_(host_in, non_blocking=True)
-        ds.step(i)
-        host_out.copy_(ds.full(i), non_blocking=True)
+    def run(i0, n):
+        for i in range(i0, i0 + n):
+            k = i % 2
+            with torch.cuda.stream(copy):
+                if i - 2 in read_done:  # step i - 2's kernels have read input slot k
+                    copy.wait_event(read_done[i - 2])
+                ds.x_slots[k].copy_(host_in[k], non_blocking=True)
+                h2d_done[i] = ev()
+                h2d_done[i].record(copy)
+            stream.wait_event(h2d_done[i])
+            ds.layer_part(i)
+            ds.run_group(ds.lm_stream, i)
+            read_done[i] = ev()
+            read_done[i].record(stream)
+            if i - 1 in d2h_done:  # the read-back of step i - 1 precedes this rank's push
+                stream.wait_event(d2h_done[i - 1])
+            ds.collect(i)
+            comp_done[i] = ev()
+            comp_done[i].record(stream)
+            with torch.cuda.stream(copy):
+                copy.wait_event(comp_done[i])
+                host_out[k].copy_(ds.full(i), non_blocking=True)
+                d2h_done[i] = ev()
+                d2h_done[i].record(copy)
+            for d in (h2d_done, comp_done, d2h_done, read_done):
+                d.pop(i - 3, None)
 
-    for i in range(warmup):
-        e2e_step(i)
+    run(0, warmup)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(warmup, warmup + steps):  # step numbers continue, so output slots alternate
-        e2e_step(i)
+    copy.wait_event(e0)
+    t0 = time.perf_counter()
+    run(warmup, steps)  # step numbers continue, so the slots alternate across the boundary
+    host_s = time.perf_counter() - t0
+    stream.wait_event(d2h_done[warmup + steps - 1])
     e1.record(stream)
     torch.cuda.synchronize()
     ms = _max_over_ranks(e0.elapsed_time(e1), world)
-    return {"ms_step": ms / steps, "h2d_bytes_per_step": host_in.numel() * 4,
-            "d2h_bytes_per_step": host_out.numel() * 4}
+    return {"ms_step": ms / steps, "h2d_bytes_per_step": host_in[0].numel() * 4,
+            "d2h_bytes_per_step": n_out * 4, "host_us_per_step": round(host_s / steps * 1e6, 2)}
 
 
 def decode_section(jkb, spec, world, rank, stream, steps, warmup, batch, peer):
@@ -642,7 +690,7 @@ def run_gpu(args):
     total_bytes = ds.bytes_per_step
     ms_step = t["ms_step"]
     value = total_bytes / (ms_step * 1e-3) / 1e9
-    e2e = e2e_decode(ds, args.steps, args.warmup, world)
+    e2e = e2e_decode(ds, args.steps, args.warmup, world, stream)
     e2e_val = total_bytes / (e2e["ms_step"] * 1e-3) / 1e9
     launches = ds.launches_per_step
     ds.destroy()
@@ -701,7 +749,10 @@ def run_gpu(args):
             "clocks": t["clocks"],
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
-                    "d2h_bytes_per_step": e2e["d2h_bytes_per_step"]},
+                    "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
+                    "host_us_per_step": e2e["host_us_per_step"],
+                    "copies": "pinned host buffers, copies on a second stream overlapping "
+                              "the neighbouring steps' kernels"},
         }
         res.update(sections)
         if prefill is not None:
@@ -812,7 +863,10 @@ def run_bitnet(world, rank, launches=20):
         return us
 
     H, F, M = BITNET_HIDDEN, BITNET_FFN, 128
-    res = {"shapes": [], "note": "hidden 2560, ffn 6912; ternary iid p=1/3, scale 0.02"}
+    peak, peak_kind = measured_peaks()
+    res = {"shapes": [], "note": "hidden 2560, ffn 6912; ternary iid p=1/3, scale 0.02",
+           "batch1_roofline": "hbm: weight blocks + i8 activation + f32 output per launch "
+                              f"over the launch time, of the {peak_kind} {peak} GB/s"}
     norm = {n: torch.ones(n, device="cuda") for n in (H, F)}
 
     def act_i8(n, m, seed):
@@ -842,9 +896,11 @@ def run_bitnet(world, rank, launches=20):
 
             us1 = maxr(_graph_time(one, max(launches, copies)))
             nbytes = (rows // world) * (cols // be) * bb + cols + per * 4
+            gbs1 = nbytes * world / (us1 * 1e-6) / 1e9
             row = {"quant": qname, "rows": rows, "cols": cols,
                    "batch1_us": round(us1, 2),
-                   "batch1_gbs": round(nbytes * world / (us1 * 1e-6) / 1e9, 1)}
+                   "batch1_gbs": round(gbs1, 1),
+                   "batch1_hbm_frac_per_gpu": round(gbs1 / world / peak, 4)}
             for w in ws[1:]:
                 w.destroy()
             w = ws[0]

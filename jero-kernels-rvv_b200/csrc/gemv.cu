@@ -20,6 +20,7 @@
 //   i8 rows       : xq[K] | block totals i32 (block = the weight format's block)
 #include <cooperative_groups.h>
 #include <cstdio>
+#include <cstdlib>
 #include <type_traits>
 
 #include "gpu_layout.cuh"
@@ -948,9 +949,23 @@ constexpr int gemv_min_blocks() {
     return MODE == M_SINGLE && std::is_same<F, FQ6_K>::value ? 4 : 0;
 }
 
+// Blocks a lane loads before consuming the first of them (the unrolled main loop), per
+// format: as many as keep the loads in registers, given the size of one block's load (Ld).
+// A launch takes this unrolled variant when its warps would otherwise walk several blocks
+// one DRAM round trip at a time (small matrices, or rows longer than 32 blocks).
+template <class F> struct GemvUnroll { static constexpr int value = 1; };
+template <> struct GemvUnroll<FQ4_0> { static constexpr int value = 4; };
+template <> struct GemvUnroll<FQ5_0> { static constexpr int value = 4; };
+template <> struct GemvUnroll<FQ8_0<ActQ80>> { static constexpr int value = 4; };
+template <> struct GemvUnroll<FQ8_0<ActI8<32>>> { static constexpr int value = 4; };
+template <> struct GemvUnroll<FI2S> { static constexpr int value = 4; };
+template <> struct GemvUnroll<FTQ2<ActQ8K>> { static constexpr int value = 2; };
+template <> struct GemvUnroll<FTQ2<ActI8<256>>> { static constexpr int value = 2; };
+template <> struct GemvUnroll<FQ4_K> { static constexpr int value = 2; };
+
 // F: weight format. S: activation stager (F::Act, or a stager that quantizes f32 input into
-// the same shared-memory layout).
-template <class F, class S, int MODE>
+// the same shared-memory layout). U: blocks in flight per lane (1 or GemvUnroll<F>).
+template <class F, class S, int MODE, int U>
 __global__ void __launch_bounds__(MAX_WARPS * 32, (gemv_min_blocks<F, MODE>())) gemv_kernel(KArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     constexpr int TB = MODE == M_TOK ? TOK_MAX : 1;  // token slots per CTA
@@ -1038,13 +1053,51 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, (gemv_min_blocks<F, MODE>())) 
         if (a.act_scales) args.act_scale = a.act_scales[tok];
         S::stage(args, a.x + (size_t)tok * a.x_row_stride, smem);
     }
-    while (r0 < a.row_end) {
-        const int b = b0 + li;
-        if (r0 + rsub < a.row_end && b < a.nb) {
-            const typename F::Ld l = F::load(args, row_ptrs(), b);
-            consume(l, b);
+    if constexpr (U == 1) {
+        while (r0 < a.row_end) {
+            const int b = b0 + li;
+            if (r0 + rsub < a.row_end && b < a.nb) {
+                const typename F::Ld l = F::load(args, row_ptrs(), b);
+                consume(l, b);
+            }
+            advance();
         }
-        advance();
+    } else {
+        // Unrolled: the loads of the warp's next U steps (the positions advance() will visit)
+        // are issued together, then consumed in order, so U DRAM round trips overlap.
+        while (r0 < a.row_end) {
+            typename F::Ld l[U];
+            int bq[U];
+            bool vq[U];
+            size_t pr = r0;
+            int pb = b0;
+            Row rp = row_ptrs();
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                bq[u] = pb + li;
+                vq[u] = pr < a.row_end && pr + rsub < a.row_end && bq[u] < a.nb;
+                if (vq[u]) l[u] = F::load(args, rp, bq[u]);
+                pb += lpr;
+                if (pb >= a.nb && u + 1 < U) {
+                    pb = 0;
+                    pr += stride;
+                    if (MODE == M_MULTI) {
+                        float *unused;
+                        rp = row_of<MODE>(a, pr + rsub, unused);
+                    } else {
+                        rp = Row{a.mat[0].qs + (pr + rsub) * a.qs_row,
+                                 a.mat[0].sc + (pr + rsub) * a.sc_row,
+                                 a.mat[0].d + (pr + rsub) * (size_t)a.nb};
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                if (r0 >= a.row_end) break;
+                if (vq[u]) consume(l[u], bq[u]);
+                advance();
+            }
+        }
     }
 }
 
@@ -1056,9 +1109,17 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, (gemv_min_blocks<F, MODE>())) 
 // small CTAs, smaller ones pack the device better.
 constexpr unsigned GEMV_MAX_CLUSTER = 8;
 
-template <class F, class S, int MODE>
-static int launch_t(const KArgs &a_in, size_t m, cudaStream_t st, const char *name) {
-    KArgs a = a_in;
+// Launch shape of one GEMV launch (plan_t) and the number of steps each warp walks with it.
+struct GemvPlan {
+    int warps;
+    unsigned C;
+    size_t gx, m, smem;
+    size_t steps;  // block steps per warp (row steps x ceil(nb / lanes per row))
+};
+
+template <class F, class S, int MODE, int U>
+static GemvPlan plan_t(KArgs &a, size_t m) {
+    GemvPlan p{};
     size_t smem = S::bytes(a.K);
     if (MODE == M_TOK) {  // as many token slots per CTA as fit in 150 KB, at most TOK_MAX
         const size_t slot = (smem + 15) / 16 * 16;
@@ -1071,7 +1132,7 @@ static int launch_t(const KArgs &a_in, size_t m, cudaStream_t st, const char *na
         smem = slot * tpc;
         m = (m + tpc - 1) / tpc;  // CTA rows of the grid
     }
-    auto kern = gemv_kernel<F, S, MODE>;
+    auto kern = gemv_kernel<F, S, MODE, U>;
     // resident CTAs on the device per CTA size (8, 4 or 2 warps) and cluster size (1, 2, 4,
     // 8; for cluster launches the resident clusters times the cluster size), cached per
     // template instance (B200 only)
@@ -1131,9 +1192,49 @@ static int launch_t(const KArgs &a_in, size_t m, cudaStream_t st, const char *na
     if (m * gx > cap) gx = (cap + m - 1) / m;
     gx = (gx + C - 1) / C * C;  // whole clusters
     if (gx < 1) gx = 1;
-    cudaError_t e = launch_pdl_cluster(kern, dim3((unsigned)gx, (unsigned)m), dim3(warps * 32),
-                                       smem, st, C, a);
+    const size_t lpr = (size_t)1 << a.lpr_shift;
+    p.warps = warps;
+    p.C = C;
+    p.gx = gx;
+    p.m = m;
+    p.smem = smem;
+    p.steps = (rows + gx * warps * rpw - 1) / (gx * warps * rpw) * ((a.nb + lpr - 1) / lpr);
+    return p;
+}
+
+template <class F, class S, int MODE, int U>
+static int launch_p(const KArgs &a, const GemvPlan &p, cudaStream_t st, const char *name) {
+    cudaError_t e = launch_pdl_cluster(gemv_kernel<F, S, MODE, U>,
+                                       dim3((unsigned)p.gx, (unsigned)p.m), dim3(p.warps * 32),
+                                       p.smem, st, p.C, a);
     return e == cudaSuccess ? JKB_OK : fail_cuda(e, name);
+}
+
+// JKB_GEMV_UNROLL=1 in the environment keeps every launch on the one-block-at-a-time loop (for
+// measuring the unrolled loop against it); unset, the launcher decides.
+static bool unroll_allowed() {
+    static const bool ok = [] {
+        const char *v = getenv("JKB_GEMV_UNROLL");
+        return !(v && v[0] == '1' && v[1] == 0);
+    }();
+    return ok;
+}
+
+// Single and grouped launches whose warps would walk two or more block steps take the
+// unrolled loop (GemvUnroll<F> blocks in flight per lane); token batches and the diagnostic
+// launch keep one block at a time.
+template <class F, class S, int MODE>
+static int launch_t(const KArgs &a_in, size_t m, cudaStream_t st, const char *name) {
+    constexpr bool can = MODE == M_SINGLE || MODE == M_MULTI;
+    constexpr int UF = can ? GemvUnroll<F>::value : 1;
+    KArgs a = a_in;
+    const GemvPlan p1 = plan_t<F, S, MODE, 1>(a, m);
+    if (UF > 1 && p1.steps >= 2 && unroll_allowed()) {
+        KArgs au = a_in;
+        const GemvPlan pu = plan_t<F, S, MODE, UF>(au, m);
+        return launch_p<F, S, MODE, UF>(au, pu, st, name);
+    }
+    return launch_p<F, S, MODE, 1>(a, p1, st, name);
 }
 
 static const size_t MAX_K = 120 * 1024;

@@ -175,7 +175,7 @@ def test_view_in_scratch_and_gemv_view(jkb, oracle, quant, rows, cols):
     assert np.array_equal(bits(host(part)), bits(ref[10:rows - 7]))
     with pytest.raises(jkb.TensorBoundsError, match="out of bounds"):
         jkb.gemv_repacked_view_rows(part, rw, view, range(20, rows + 3))
-    # the scope form rewinds; a workspace one byte short of the budget fails closed
+    # the scope form rewinds
     ws.reset()
     with ws.scope() as sc:
         v2 = jkb.QuantizedActQ8View.quantize_row_in_scope(dev(x), sc)
@@ -183,7 +183,12 @@ def test_view_in_scratch_and_gemv_view(jkb, oracle, quant, rows, cols):
         jkb.gemv_repacked_view(out, rw, v2)
         assert np.array_equal(bits(host(out)), bits(ref))
     assert ws.used_bytes() == 0
-    small = jkb.ScratchWorkspace(need - 128 - 1)
+    # the planes need `need` bytes at worst (an unaligned cursor, the last plane padded);
+    # from an aligned start exactly the planes' bytes, one byte fewer fails
+    kp = (cols + 31) // 32 * 32
+    up = lambda n: (n + 127) // 128 * 128  # noqa: E731
+    exact = up(kp) + 2 * up(kp // 32 * 4) + up(kp // 16 * 4) + (cols + 255) // 256 * 4
+    small = jkb.ScratchWorkspace(exact - 1)
     with pytest.raises(jkb.TensorBoundsError, match="scratch exhausted"):
         jkb.QuantizedActQ8View.quantize_row_in_scratch(dev(x), small)
     assert small.used_bytes() == 0
