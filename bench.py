@@ -478,6 +478,62 @@ class DecodeSet:
         if marks is not None:
             marks[3].record(stream)
 
+    def c_calls(self, k, stream):
+        """Step calls of output/input slot k (steps i with i % 2 == k) as C-ABI function +
+        argument tuples with every pointer resolved, for a caller that replays them each step
+        (the e2e loop): the same calls layer_part / run_group / collect make, validated by a
+        first eager step. Returns (compute calls before the collection, collection calls);
+        a call is (cfunc, args) or a Python callable (the NCCL all-gather)."""
+        import ctypes as C
+        from jkb200 import _lib
+
+        L = _lib.load()
+        xs = self.xs_slots[k]
+        keep = []  # ctypes arrays referenced by the argument tuples
+        calls = []
+
+        def group(s):
+            items = [(self.lslice(n, k), self.weights[(n, k % c)]) for n, c in self.groups[s]]
+            if self.batch > 1:
+                calls.append((L.jkb_quantize_rows_q8_k, (xs[s].data_ptr(), self.batch,
+                              self.acts[s], self.xq[s].data_ptr(), self.xq[s].numel() // 292,
+                              stream)))
+                for out, w in items:
+                    calls.append((L.jkb_gemv_batch, (out.data_ptr(), out.numel(), w.handle,
+                                  self.xq[s].data_ptr(), self.xq[s].numel() // 292, self.batch,
+                                  stream)))
+            elif self.unfused or s in self.prequant:
+                calls.append((L.jkb_quantize_row_q8_k, (xs[s].data_ptr(), xs[s].numel(),
+                              self.xq[s].data_ptr(), self.xq[s].numel() // 292, stream)))
+                for out, w in items:
+                    calls.append((L.jkb_gemv_rows, (out.data_ptr(), out.numel(), w.handle,
+                                  self.xq[s].data_ptr(), self.xq[s].numel() // 292, 0, w.rows,
+                                  stream)))
+            else:
+                arr = (_lib.jkb_vec_dot_item * len(items))()
+                for j, (out, w) in enumerate(items):
+                    arr[j].out, arr[j].out_len, arr[j].w = out.data_ptr(), out.numel(), w.handle
+                keep.append(arr)
+                calls.append((L.jkb_vec_dot_grouped_rvv, (arr, len(items), xs[s].data_ptr(),
+                                                          xs[s].numel(), stream)))
+
+        for s in self.groups:
+            if s != self.lm_stream:
+                group(s)
+        group(self.lm_stream)
+        coll = []
+        if self.peer:
+            if not hasattr(self.outs, "_chunks"):
+                self.outs._chunks = [self.outs.group.chunk_arrays(self.outs.chunks(j))
+                                     for j in range(self.outs.SLOTS)]
+            offs, lens, n = self.outs._chunks[k]
+            coll.append((L.jkb_peer_group_allgather, (self.outs.group.handle, offs, lens, n,
+                                                      stream)))
+        elif self.world > 1:
+            coll.append(lambda: self.outs2[k].gather())
+        self._keep_c = getattr(self, "_keep_c", []) + keep
+        return calls, coll
+
     def output(self, name, i):
         """Full output of matrix `name` after step i: [rows], or [batch][rows]."""
         if self.peer:
@@ -579,54 +635,75 @@ def time_decode(ds, steps, warmup, stream, world, local=0, sample_clocks=False):
 
 
 def e2e_decode(ds, steps, warmup, world, stream):
-    """The same steps through the public API with host buffers: every step copies its f32 inputs
-    in from pinned host memory and its full outputs out to pinned host memory, with eager
-    launches. The copies run on a second stream and overlap the neighbouring steps' kernels:
-    step i's inputs arrive in input slot i % 2 while step i - 1 runs, and its outputs leave from
+    """The same steps through the public C ABI with host buffers, the way a compiled caller
+    drives it: each step's calls are prebuilt once per slot as ctypes function and argument
+    tuples (DecodeSet.c_calls: validation and pointer lookup happen once, as an engine holding
+    handles would do), and the copies and events go straight to the CUDA runtime. Every step
+    copies its f32 inputs in from pinned host memory and its full outputs out to pinned host
+    memory. The copies run on a second stream and overlap the neighbouring steps' kernels: step
+    i's inputs arrive in input slot i % 2 while step i - 1 runs, and its outputs leave from
     output slot i % 2 while step i + 1 runs; events order each copy after what it depends on and
     before what would overwrite it (including a peer's push into the slot, which cannot happen
     before this rank's all-gather of step i + 1, so that all-gather waits for the read-back of
     step i). Timed with CUDA events on the compute stream from before the first copy in to after
-    the last copy out, max over ranks. Also reports the host's time per step to enqueue the
-    calls."""
+    the last copy out, max over ranks. Also reports the host's time per step to enqueue."""
+    import ctypes as C
+
     import torch
     import torch.distributed as dist
 
+    rt = C.CDLL("libcudart.so.12")  # the CUDA runtime torch has loaded
+    rt.cudaMemcpyAsync.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.c_int, C.c_void_p]
+    rt.cudaEventRecord.argtypes = [C.c_void_p, C.c_void_p]
+    rt.cudaStreamWaitEvent.argtypes = [C.c_void_p, C.c_void_p, C.c_uint]
+    rt.cudaEventCreateWithFlags.argtypes = [C.POINTER(C.c_void_p), C.c_uint]
     copy = torch.cuda.Stream()
+    cs, ks = stream.cuda_stream, copy.cuda_stream
     host_in = [ds.x_slots[0].cpu().pin_memory(), ds.x_slots[1].cpu().pin_memory()]
     n_out = ds.full(0).numel()
     host_out = [torch.empty(n_out, dtype=torch.float32).pin_memory() for _ in range(2)]
-    ev = lambda: torch.cuda.Event()  # noqa: E731
-    h2d_done, comp_done, d2h_done, read_done = ({}, {}, {}, {})
+    in_bytes, out_bytes = host_in[0].numel() * 4, n_out * 4
+
+    def event():
+        e = C.c_void_p()
+        assert rt.cudaEventCreateWithFlags(C.byref(e), 2) == 0  # cudaEventDisableTiming
+        return e
+    # per slot: inputs copied in, inputs read by the step, step done, outputs copied out
+    ev = {name: [event(), event()] for name in ("h2d", "read", "comp", "d2h")}
+    plan = [ds.c_calls(k, cs) for k in range(2)]
+    slot_io = [(ds.x_slots[k].data_ptr(), host_in[k].data_ptr(), ds.full(k).data_ptr(),
+                host_out[k].data_ptr()) for k in range(2)]
+
+    def call(c):
+        if callable(c):
+            c()
+            return
+        rc = c[0](*c[1])
+        if rc:
+            raise RuntimeError(f"{c[0].__name__} failed ({rc}): {ds.jkb._lib.load().jkb_last_error()}")
 
     def run(i0, n):
         for i in range(i0, i0 + n):
             k = i % 2
-            with torch.cuda.stream(copy):
-                if i - 2 in read_done:  # step i - 2's kernels have read input slot k
-                    copy.wait_event(read_done[i - 2])
-                ds.x_slots[k].copy_(host_in[k], non_blocking=True)
-                h2d_done[i] = ev()
-                h2d_done[i].record(copy)
-            stream.wait_event(h2d_done[i])
-            ds.layer_part(i)
-            ds.run_group(ds.lm_stream, i)
-            read_done[i] = ev()
-            read_done[i].record(stream)
-            if i - 1 in d2h_done:  # the read-back of step i - 1 precedes this rank's push
-                stream.wait_event(d2h_done[i - 1])
-            ds.collect(i)
-            comp_done[i] = ev()
-            comp_done[i].record(stream)
-            with torch.cuda.stream(copy):
-                copy.wait_event(comp_done[i])
-                host_out[k].copy_(ds.full(i), non_blocking=True)
-                d2h_done[i] = ev()
-                d2h_done[i].record(copy)
-            for d in (h2d_done, comp_done, d2h_done, read_done):
-                d.pop(i - 3, None)
+            dx, hx, dy, hy = slot_io[k]
+            rt.cudaStreamWaitEvent(ks, ev["read"][k], 0)  # step i - 2 has read input slot k
+            rt.cudaMemcpyAsync(dx, hx, in_bytes, 1, ks)
+            rt.cudaEventRecord(ev["h2d"][k], ks)
+            rt.cudaStreamWaitEvent(cs, ev["h2d"][k], 0)
+            calls, coll = plan[k]
+            for c in calls:
+                call(c)
+            rt.cudaEventRecord(ev["read"][k], cs)
+            rt.cudaStreamWaitEvent(cs, ev["d2h"][1 - k], 0)  # read-back of step i - 1 first
+            for c in coll:
+                call(c)
+            rt.cudaEventRecord(ev["comp"][k], cs)
+            rt.cudaStreamWaitEvent(ks, ev["comp"][k], 0)
+            rt.cudaMemcpyAsync(hy, dy, out_bytes, 2, ks)
+            rt.cudaEventRecord(ev["d2h"][k], ks)
 
-    run(0, warmup)
+    ds.step(0)  # one eager step through the checked API first
+    run(1, warmup)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -634,14 +711,14 @@ def e2e_decode(ds, steps, warmup, world, stream):
     e0.record(stream)
     copy.wait_event(e0)
     t0 = time.perf_counter()
-    run(warmup, steps)  # step numbers continue, so the slots alternate across the boundary
+    run(1 + warmup, steps)  # step numbers continue, so the slots alternate across the boundary
     host_s = time.perf_counter() - t0
-    stream.wait_event(d2h_done[warmup + steps - 1])
+    rt.cudaStreamWaitEvent(cs, ev["d2h"][(warmup + steps) % 2], 0)
     e1.record(stream)
     torch.cuda.synchronize()
     ms = _max_over_ranks(e0.elapsed_time(e1), world)
-    return {"ms_step": ms / steps, "h2d_bytes_per_step": host_in[0].numel() * 4,
-            "d2h_bytes_per_step": n_out * 4, "host_us_per_step": round(host_s / steps * 1e6, 2)}
+    return {"ms_step": ms / steps, "h2d_bytes_per_step": in_bytes,
+            "d2h_bytes_per_step": out_bytes, "host_us_per_step": round(host_s / steps * 1e6, 2)}
 
 
 def decode_section(jkb, spec, world, rank, stream, steps, warmup, batch, peer):
@@ -752,7 +829,8 @@ def run_gpu(args):
                     "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
                     "host_us_per_step": e2e["host_us_per_step"],
                     "copies": "pinned host buffers, copies on a second stream overlapping "
-                              "the neighbouring steps' kernels"},
+                              "the neighbouring steps' kernels",
+                    "calls": "the C ABI through prebuilt ctypes call tuples"},
         }
         res.update(sections)
         if prefill is not None:

@@ -110,50 +110,19 @@ __device__ __forceinline__ int sbyte(uint32_t w, int k) { return (int)(int8_t)(w
 
 // ---------------------------------------------------------------- activation staging
 
-// Copies `nwords` 32-bit words of x into shared memory through scatter(word_index, value).
-// With a 16-byte aligned x it uses 16-byte loads, and each thread issues a round of up to 4
-// loads before any store, so staging costs about one memory round trip.
-template <class Scatter>
-__device__ __forceinline__ void stage_words(const uint8_t *x, int nwords, Scatter scatter) {
-    constexpr int R = 4;
-    const int nt = blockDim.x;
-    if ((((uintptr_t)x) & 15) == 0) {
-        const int nvec = nwords >> 2;
-        for (int base = 0; base < nvec; base += R * nt) {
-            uint4 v[R];
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                const int i = base + r * nt + threadIdx.x;
-                if (i < nvec) v[r] = __ldg(reinterpret_cast<const uint4 *>(x) + i);
-            }
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                const int i = base + r * nt + threadIdx.x;
-                if (i < nvec) {
-                    scatter(4 * i, v[r].x);
-                    scatter(4 * i + 1, v[r].y);
-                    scatter(4 * i + 2, v[r].z);
-                    scatter(4 * i + 3, v[r].w);
-                }
-            }
-        }
-        for (int wi = 4 * nvec + threadIdx.x; wi < nwords; wi += nt)
-            scatter(wi, __ldg(reinterpret_cast<const uint32_t *>(x) + wi));
-    } else {
-        for (int base = 0; base < nwords; base += R * nt) {
-            uint32_t v[R];
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                const int i = base + r * nt + threadIdx.x;
-                if (i < nwords) v[r] = __ldg(reinterpret_cast<const uint32_t *>(x) + i);
-            }
-#pragma unroll
-            for (int r = 0; r < R; r++) {
-                const int i = base + r * nt + threadIdx.x;
-                if (i < nwords) scatter(i, v[r]);
-            }
-        }
+// Copies `nwords` 32-bit words of x (4-byte aligned) into shared memory, word wi to dst(wi),
+// with asynchronous global-to-shared copies: no registers hold the data, every copy of the
+// thread is in flight at once, so staging costs one memory round trip whatever the CTA size.
+// The caller synchronizes the CTA afterwards.
+template <class Dst>
+__device__ __forceinline__ void stage_words(const uint8_t *x, int nwords, Dst dst) {
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(x);
+    for (int wi = threadIdx.x; wi < nwords; wi += blockDim.x) {
+        const uint32_t sa = (uint32_t)__cvta_generic_to_shared(dst(wi));
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sa), "l"(src + wi)
+                     : "memory");
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
 }
 
 // BlockQ8K activations (quant_q8.rs:62-71). Superblock s: 256 i8 at s*256 with chunk j at
@@ -179,17 +148,15 @@ struct ActQ8K {
     static __device__ void stage(const KArgs &a, const uint8_t *x, uint8_t *s) {
         const int nb = a.K / 256, K = a.K;  // 292-byte BlockQ8K = 73 words
         float *xd_ = (float *)(s + K + nb * 32);
-        stage_words(x, nb * 73, [&](int wi, uint32_t v) {
+        stage_words(x, nb * 73, [&](int wi) -> uint8_t * {
             const int blk = wi / 73, w = wi - blk * 73;
-            if (w == 0) {
-                xd_[blk] = __uint_as_float(v);
-            } else if (w <= 64) {
+            if (w == 0) return reinterpret_cast<uint8_t *>(xd_ + blk);
+            if (w <= 64) {
                 const int ww = w - 1, j = ww >> 2;
-                *(uint32_t *)(s + blk * 256 + 16 * (j ^ (blk & 7)) + 4 * (ww & 3)) = v;
-            } else {
-                const int ww = w - 65, h = ww >> 2;
-                *(uint32_t *)(s + K + blk * 32 + 16 * (h ^ ((blk >> 2) & 1)) + 4 * (ww & 3)) = v;
+                return s + blk * 256 + 16 * (j ^ (blk & 7)) + 4 * (ww & 3);
             }
+            const int ww = w - 65, h = ww >> 2;
+            return s + K + blk * 32 + 16 * (h ^ ((blk >> 2) & 1)) + 4 * (ww & 3);
         });
         __syncthreads();
         int *tot_ = (int *)(s + a.K + nb * 36);
@@ -223,14 +190,11 @@ struct ActQ80 {
     static __device__ void stage(const KArgs &a, const uint8_t *x, uint8_t *s) {
         const int nb = a.K / 32;  // 36-byte BlockQ8_0 = 9 words
         float *xd_ = (float *)(s + a.K);
-        stage_words(x, nb * 9, [&](int wi, uint32_t v) {
+        stage_words(x, nb * 9, [&](int wi) -> uint8_t * {
             const int blk = wi / 9, w = wi - blk * 9;
-            if (w == 0) {
-                xd_[blk] = __uint_as_float(v);
-            } else {
-                const int ww = w - 1, j = ww >> 2;
-                *(uint32_t *)(s + blk * 32 + 16 * (j ^ ((blk >> 2) & 1)) + 4 * (ww & 3)) = v;
-            }
+            if (w == 0) return reinterpret_cast<uint8_t *>(xd_ + blk);
+            const int ww = w - 1, j = ww >> 2;
+            return s + blk * 32 + 16 * (j ^ ((blk >> 2) & 1)) + 4 * (ww & 3);
         });
         __syncthreads();
         int *tot_ = (int *)(s + a.K + nb * 4);
@@ -267,16 +231,17 @@ struct ActI8 {
     }
     static __device__ void stage(const KArgs &a, const uint8_t *x, uint8_t *s) {
         if (threadIdx.x == 0) *reinterpret_cast<float *>(s + a.K + (a.K / BE) * 4) = a.act_scale;
-        auto put = [&](int wi, uint32_t v) {
+        auto at = [&](int wi) -> uint8_t * {
             const int e = 4 * wi, b = e / BE, off = e - b * BE, j = off >> 4;
-            *(uint32_t *)(s + b * BE + 16 * (j ^ swz(b)) + (off & 15)) = v;
+            return s + b * BE + 16 * (j ^ swz(b)) + (off & 15);
         };
         if ((((uintptr_t)x) & 3) == 0) {
-            stage_words(x, a.K / 4, put);
+            stage_words(x, a.K / 4, at);
         } else {
             for (int i = threadIdx.x; i < a.K / 4; i += blockDim.x)
-                put(i, (uint32_t)x[4 * i] | ((uint32_t)x[4 * i + 1] << 8) |
-                           ((uint32_t)x[4 * i + 2] << 16) | ((uint32_t)x[4 * i + 3] << 24));
+                *(uint32_t *)at(i) = (uint32_t)x[4 * i] | ((uint32_t)x[4 * i + 1] << 8) |
+                                     ((uint32_t)x[4 * i + 2] << 16) |
+                                     ((uint32_t)x[4 * i + 3] << 24);
         }
         __syncthreads();
         int *tot_ = (int *)(s + a.K);
@@ -1038,10 +1003,45 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, (gemv_min_blocks<F, MODE>())) 
             if (MODE == M_MULTI) rpm = row_of<MODE>(a, r0 + rsub, outp);
         }
     };
-    // Weights never depend on the previous kernel in the stream; the activation may. Start
-    // pulling this warp's first blocks into L2, then wait for the previous grid (programmatic
-    // dependent launch) before staging the activation.
-    if (r0 + rsub < a.row_end && li < a.nb) F::prefetch(args, row_ptrs(), li);
+    // The unrolled variant's next U steps (the positions advance() will visit): their loads
+    // are issued together and consumed in order, so U DRAM round trips overlap.
+    typename F::Ld l[U];
+    int bq[U];
+    bool vq[U];
+    auto issue = [&]() {
+        size_t pr = r0;
+        int pb = b0;
+        Row rp = row_ptrs();
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            bq[u] = pb + li;
+            vq[u] = pr < a.row_end && pr + rsub < a.row_end && bq[u] < a.nb;
+            if (vq[u]) l[u] = F::load(args, rp, bq[u]);
+            pb += lpr;
+            if (pb >= a.nb && u + 1 < U) {
+                pb = 0;
+                pr += stride;
+                if (MODE == M_MULTI) {
+                    float *unused;
+                    rp = row_of<MODE>(a, pr + rsub, unused);
+                } else {
+                    rp = Row{a.mat[0].qs + (pr + rsub) * a.qs_row,
+                             a.mat[0].sc + (pr + rsub) * a.sc_row,
+                             a.mat[0].d + (pr + rsub) * (size_t)a.nb};
+                }
+            }
+        }
+    };
+    // Weights never depend on the previous kernel in the stream; the activation may. Before
+    // waiting for the previous grid (programmatic dependent launch), the unrolled variant
+    // loads the warp's first U blocks into registers and the one-block loop pulls the first
+    // block into L2; the activation is staged after the wait. (Weight handles are complete
+    // when their upload returns, so no earlier kernel writes them.)
+    if constexpr (U == 1) {
+        if (r0 + rsub < a.row_end && li < a.nb) F::prefetch(args, row_ptrs(), li);
+    } else {
+        issue();
+    }
     pdl_wait();
     pdl_launch_dependents();
     if (MODE == M_TOK) {
@@ -1057,46 +1057,20 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, (gemv_min_blocks<F, MODE>())) 
         while (r0 < a.row_end) {
             const int b = b0 + li;
             if (r0 + rsub < a.row_end && b < a.nb) {
-                const typename F::Ld l = F::load(args, row_ptrs(), b);
-                consume(l, b);
+                const typename F::Ld ld = F::load(args, row_ptrs(), b);
+                consume(ld, b);
             }
             advance();
         }
     } else {
-        // Unrolled: the loads of the warp's next U steps (the positions advance() will visit)
-        // are issued together, then consumed in order, so U DRAM round trips overlap.
         while (r0 < a.row_end) {
-            typename F::Ld l[U];
-            int bq[U];
-            bool vq[U];
-            size_t pr = r0;
-            int pb = b0;
-            Row rp = row_ptrs();
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                bq[u] = pb + li;
-                vq[u] = pr < a.row_end && pr + rsub < a.row_end && bq[u] < a.nb;
-                if (vq[u]) l[u] = F::load(args, rp, bq[u]);
-                pb += lpr;
-                if (pb >= a.nb && u + 1 < U) {
-                    pb = 0;
-                    pr += stride;
-                    if (MODE == M_MULTI) {
-                        float *unused;
-                        rp = row_of<MODE>(a, pr + rsub, unused);
-                    } else {
-                        rp = Row{a.mat[0].qs + (pr + rsub) * a.qs_row,
-                                 a.mat[0].sc + (pr + rsub) * a.sc_row,
-                                 a.mat[0].d + (pr + rsub) * (size_t)a.nb};
-                    }
-                }
-            }
 #pragma unroll
             for (int u = 0; u < U; u++) {
                 if (r0 >= a.row_end) break;
                 if (vq[u]) consume(l[u], bq[u]);
                 advance();
             }
+            if (r0 < a.row_end) issue();
         }
     }
 }
@@ -1220,20 +1194,19 @@ static bool unroll_allowed() {
     return ok;
 }
 
-// Single and grouped launches whose warps would walk two or more block steps take the
-// unrolled loop (GemvUnroll<F> blocks in flight per lane); token batches and the diagnostic
-// launch keep one block at a time.
+// Single and grouped launches of the formats with GemvUnroll<F> > 1 take the unrolled loop
+// (its first loads also go ahead of the programmatic-launch wait); the Q6_K / Q5_K kernels,
+// token batches and the diagnostic launch keep one block at a time.
 template <class F, class S, int MODE>
 static int launch_t(const KArgs &a_in, size_t m, cudaStream_t st, const char *name) {
     constexpr bool can = MODE == M_SINGLE || MODE == M_MULTI;
     constexpr int UF = can ? GemvUnroll<F>::value : 1;
     KArgs a = a_in;
-    const GemvPlan p1 = plan_t<F, S, MODE, 1>(a, m);
-    if (UF > 1 && p1.steps >= 2 && unroll_allowed()) {
-        KArgs au = a_in;
-        const GemvPlan pu = plan_t<F, S, MODE, UF>(au, m);
-        return launch_p<F, S, MODE, UF>(au, pu, st, name);
+    if (UF > 1 && unroll_allowed()) {
+        const GemvPlan pu = plan_t<F, S, MODE, UF>(a, m);
+        return launch_p<F, S, MODE, UF>(a, pu, st, name);
     }
+    const GemvPlan p1 = plan_t<F, S, MODE, 1>(a, m);
     return launch_p<F, S, MODE, 1>(a, p1, st, name);
 }
 

@@ -295,10 +295,12 @@ static int weight_upload(const jkb_tensor_view *v, size_t rows, size_t cols, cud
         v->quant, w->gpu_format, raw, rows, w->nb, w->nb * (size_t)f->block_bytes,
         f->block_bytes, qs, w->p.qs_row, sc, w->p.sc_row, d);
     rc = check_launch("relayout_kernel");
-    if (owned) {
-        cudaStreamSynchronize(st);
-        cudaFree(raw);
-    }
+    // The GEMV kernels may issue their first weight loads before their programmatic-launch
+    // wait (weights never depend on the kernel before them), so a handle is returned only once
+    // its planes are written.
+    const cudaError_t se = cudaStreamSynchronize(st);
+    if (!rc && se != cudaSuccess) rc = fail_cuda(se, "jkb_weight_upload");
+    if (owned) cudaFree(raw);
     if (rc) {
         cudaFree(a.base);
         delete w;
