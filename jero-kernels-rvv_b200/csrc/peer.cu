@@ -73,6 +73,11 @@ __device__ void bounded_arrival_wait(unsigned long long *cnt, unsigned long long
 }
 
 __global__ void __launch_bounds__(AG_THREADS) peer_allgather_kernel(AgArgs a) {
+    // Launched as a programmatic dependent of the kernel before it (the step's last GEMV): wait
+    // for that grid's rows, then let the next step's first kernel launch and load its weights
+    // while this one pushes rows and waits for the peers' (its activations wait for this grid).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
     const uint8_t *src = a.data[a.rank];
     const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const size_t nthr = (size_t)gridDim.x * blockDim.x;
@@ -226,7 +231,9 @@ int jkb_peer_group_allgather(jkb_peer_group *pg, const size_t *offset, const siz
     a.expected = reinterpret_cast<unsigned long long *>(pg->base) + 1;
     a.arrivals = (unsigned long long)(pg->world - 1) * AG_CTAS;
     a.err = err;
-    peer_allgather_kernel<<<AG_CTAS, AG_THREADS, 0, as_stream(stream)>>>(a);
+    const cudaError_t le =
+        launch_pdl(peer_allgather_kernel, dim3(AG_CTAS), dim3(AG_THREADS), 0, as_stream(stream), a);
+    if (le != cudaSuccess) return fail_cuda(le, "peer_allgather_kernel");
     return check_launch("peer_allgather_kernel");
 }
 
