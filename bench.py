@@ -668,8 +668,12 @@ def e2e_decode(ds, steps, warmup, world, stream):
         e = C.c_void_p()
         assert rt.cudaEventCreateWithFlags(C.byref(e), 2) == 0  # cudaEventDisableTiming
         return e
-    # per slot: inputs copied in, inputs read by the step, step done, outputs copied out
-    ev = {name: [event(), event()] for name in ("h2d", "read", "comp", "d2h")}
+    # Events (one per slot): comp[k] after a step of slot k; inp[k] on the copy stream after the
+    # read-back of step j - 2 and the copy-in of step j (slot k = j % 2); back[k] after the
+    # read-back of a step of slot k. The compute stream takes one wait and one record a step
+    # (two with peers, whose pushes into a slot must follow its read-back): every stream
+    # operation between two kernels ends their programmatic launch overlap.
+    ev = {name: [event(), event()] for name in ("comp", "inp", "back")}
     plan = [ds.c_calls(k, cs) for k in range(2)]
     slot_io = [(ds.x_slots[k].data_ptr(), host_in[k].data_ptr(), ds.full(k).data_ptr(),
                 host_out[k].data_ptr()) for k in range(2)]
@@ -682,27 +686,38 @@ def e2e_decode(ds, steps, warmup, world, stream):
         if rc:
             raise RuntimeError(f"{c[0].__name__} failed ({rc}): {ds.jkb._lib.load().jkb_last_error()}")
 
+    def copy_in(j):
+        """Copy stream: the inputs of step j into slot j % 2, after step j - 2 (same slot) has
+        finished and its outputs have been read back."""
+        k = j % 2
+        dx, hx, _, _ = slot_io[k]
+        rt.cudaStreamWaitEvent(ks, ev["comp"][k], 0)
+        rt.cudaMemcpyAsync(dx, hx, in_bytes, 1, ks)
+        rt.cudaEventRecord(ev["inp"][k], ks)
+
     def run(i0, n):
         for i in range(i0, i0 + n):
             k = i % 2
-            dx, hx, dy, hy = slot_io[k]
-            rt.cudaStreamWaitEvent(ks, ev["read"][k], 0)  # step i - 2 has read input slot k
-            rt.cudaMemcpyAsync(dx, hx, in_bytes, 1, ks)
-            rt.cudaEventRecord(ev["h2d"][k], ks)
-            rt.cudaStreamWaitEvent(cs, ev["h2d"][k], 0)
+            _, _, dy, hy = slot_io[k]
+            rt.cudaStreamWaitEvent(cs, ev["inp"][k], 0)
             calls, coll = plan[k]
             for c in calls:
                 call(c)
-            rt.cudaEventRecord(ev["read"][k], cs)
-            rt.cudaStreamWaitEvent(cs, ev["d2h"][1 - k], 0)  # read-back of step i - 1 first
-            for c in coll:
-                call(c)
+            if coll:
+                rt.cudaStreamWaitEvent(cs, ev["back"][1 - k], 0)  # read-back of step i - 1
+                for c in coll:
+                    call(c)
             rt.cudaEventRecord(ev["comp"][k], cs)
+            # copy stream: this step's outputs out, then the inputs of step i + 2 (same slot)
             rt.cudaStreamWaitEvent(ks, ev["comp"][k], 0)
             rt.cudaMemcpyAsync(hy, dy, out_bytes, 2, ks)
-            rt.cudaEventRecord(ev["d2h"][k], ks)
+            rt.cudaEventRecord(ev["back"][k], ks)
+            copy_in(i + 2)
 
     ds.step(0)  # one eager step through the checked API first
+    torch.cuda.synchronize()
+    copy_in(1)
+    copy_in(2)
     run(1, warmup)
     torch.cuda.synchronize()
     if world > 1:
@@ -713,7 +728,7 @@ def e2e_decode(ds, steps, warmup, world, stream):
     t0 = time.perf_counter()
     run(1 + warmup, steps)  # step numbers continue, so the slots alternate across the boundary
     host_s = time.perf_counter() - t0
-    rt.cudaStreamWaitEvent(cs, ev["d2h"][(warmup + steps) % 2], 0)
+    rt.cudaStreamWaitEvent(cs, ev["back"][(warmup + steps) % 2], 0)
     e1.record(stream)
     torch.cuda.synchronize()
     ms = _max_over_ranks(e0.elapsed_time(e1), world)
