@@ -801,6 +801,7 @@ def run_gpu(args):
                 sec["batch16"] = decode_section(jkb, sp, world, rank, stream,
                                                 max(4, args.steps // 4), args.warmup, 16, peer)
         sections["q4_0_gemv_4096"] = run_q4_0_gemv(jkb, world)
+        sections["per_shape_" + spec["key"]] = run_decode_shapes(jkb, spec, world, rank)
     prefill = None if args.no_gemm else run_prefill_gemm(world, rank)
     bitnet = None if args.no_bitnet else run_bitnet(world, rank)
 
@@ -869,6 +870,65 @@ def decode_config(spec, world, peer):
                 "" if world == 1 else
                 " + one-kernel all-gather over NVLink peer memory" if peer
                 else " + NCCL all-gather")}
+
+
+def run_decode_shapes(jkb, spec, world, rank, launches=40):
+    """Each activation group of a decode set on its own (this rank's row shards), with the step's
+    own calls -- the grouped f32-input launch for the layer groups, quantize_row_q8_k + the
+    pre-quantized GEMV for the lm_head -- over weight copies rotating past 2x the L2: us per
+    group and GB/s of its algorithmic bytes (max over ranks for the time, whole-job bytes)."""
+    import torch
+    from jkb200.shard import shard_rows
+
+    peak, _ = measured_peaks()
+    groups = {}
+    for i, (name, quant, rows, cols, st) in enumerate(spec["mats"]):
+        groups.setdefault(st, []).append((i, name, quant, rows, cols))
+    res = {}
+    for st, mats in groups.items():
+        nbytes = sum(algorithmic_bytes(q, r, c) for _, _, q, r, c in mats)
+        shard_bytes = max(1, nbytes // world)
+        copies = max(1, min(64, -(-260_000_000 // shard_bytes)))
+        cols = mats[0][4]
+        raws = {}
+        for i, name, quant, rows, _ in mats:
+            rr = shard_rows(rows, world, rank)
+            raws[name] = (rr, synth_matrix(quant, rows, cols, 1000 + i, rr.start, rr.stop,
+                                           spec["sigma"]))
+        sets = []
+        for c in range(copies):  # copies of the same bytes (GEMV time does not depend on them)
+            items = []
+            for i, name, quant, rows, _ in mats:
+                rr, raw = raws[name]
+                w = jkb.Weight(jkb.TensorView(name, quant, [len(rr), cols], raw), len(rr), cols)
+                items.append((torch.empty(len(rr), dtype=torch.float32, device="cuda"), w))
+            sets.append(items)
+        x = torch.randn(cols, generator=torch.Generator().manual_seed(9)).cuda()
+        xq = jkb.empty_q8_k_blocks(cols // 256)
+        lm = st == spec["mats"][-1][4]
+        it = [0]
+
+        def one():
+            items = sets[it[0] % copies]
+            if lm:
+                jkb.quantize_row_q8_k(x, xq)
+                for out, w in items:
+                    jkb.gemv_rows(out, w, xq, range(0, w.rows))
+            else:
+                jkb.vec_dot_grouped_rvv(items, x)
+            it[0] += 1
+
+        us = _max_over_ranks(_graph_time(one, max(launches, copies)), world)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res["+".join(n for _, n, _, _, _ in mats)] = {
+            "us": round(us, 2), "gbs": round(gbs, 1),
+            "hbm_frac_per_gpu": round(gbs / world / peak, 4), "bytes": nbytes}
+        for items in sets:
+            for _, w in items:
+                w.destroy()
+        del sets
+        torch.cuda.empty_cache()
+    return res
 
 
 def run_q4_0_gemv(jkb, world, launches=60):
