@@ -47,7 +47,6 @@
 
 #include <atomic>
 #include <cstdio>
-#include <cstdlib>
 
 #include "jkb_internal.h"
 #include "nibble.cuh"
@@ -62,13 +61,9 @@ constexpr int GPS = 4;    // scale groups per stage
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
 template <int BN_, int WPQ_, int GPR_, bool EXACT_, bool MINS_ = false, bool H16_ = false,
-          int NIB_ = NIB_NONE, int AB_ = 1, int CTAS_ = 1>
+          int NIB_ = NIB_NONE, int AB_ = 1>
 struct TcCfg {
     static constexpr int BN = BN_, WPQ = WPQ_, GPR = GPR_;
-    // CTAS: resident CTAs per SM. Two halve each CTA's TMEM, shared memory and registers so that
-    // twice the epilogue warps share an SM's issue slots (more independent work to hide the
-    // epilogue's fixed-latency dependencies).
-    static constexpr int CTAS = CTAS_;
     static constexpr bool EXACT = EXACT_;
     // MINS: groups carry a min term (Q4_K_M, Q4_1): acc += c * (xs * ws) - x_sum * wm
     static constexpr bool MINS = MINS_;
@@ -108,7 +103,7 @@ struct TcCfg {
     static constexpr int EPI = 4 * WPQ;    // epilogue warps
     static constexpr int THREADS = (2 + EPI + (H16 ? 1 : 0) + CONV) * 32;
     // TMEM: two round buffers of GPR group accumulators (BN int32 columns each)
-    static constexpr int TMEM_COLS = 512 / CTAS_;
+    static constexpr int TMEM_COLS = 512;
     static constexpr int SA = BMW * BK, SB = BN * BK;  // operand bytes per stage
     static constexpr int SAN = NIB ? BMW * BK / 2 : 0;  // 4-bit weight tile bytes per stage
     static constexpr int SMT = NIB ? BMW * 16 : 0;       // scale words: 16 bytes per row
@@ -119,7 +114,7 @@ struct TcCfg {
             : SA + SB + BMW * NG * 4 + GPS * BN * 4 + (MINS ? BMW * NG * 4 + NG * BN * 4 : 0);
     static constexpr int STAGE_SMEM =
         STAGE_TX + (H16 ? 2 * SB : 0) + (NIB ? SA + BMW * NG * 4 + (MINS ? BMW * GPS * 4 : 0) : 0);
-    static constexpr int STAGES_FIT = ((NEG8 ? 184 : 200) * 1024) / CTAS_ / STAGE_SMEM;
+    static constexpr int STAGES_FIT = ((NEG8 ? 184 : 200) * 1024) / STAGE_SMEM;
     // BitLinear blocks run on small batches, where a CTA's time is its stages' load latency:
     // they keep up to eight stages in flight, the block-scaled GEMM six
     static constexpr int STAGES_MAX = AB_ > 1 ? 8 : 6;
@@ -394,7 +389,7 @@ __device__ __forceinline__ void nib_convert(TcSmem<C> &sm, int s, int ks, int e)
 }
 
 template <class C>
-__global__ void __launch_bounds__(C::THREADS, C::CTAS)
+__global__ void __launch_bounds__(C::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    const __grid_constant__ CUtensorMap tmWS, const __grid_constant__ CUtensorMap tmXS,
                    const __grid_constant__ CUtensorMap tmWM, const __grid_constant__ CUtensorMap tmXN,
@@ -868,8 +863,7 @@ int launch_tc_common(const TcWeight &wt, const jkb_act_q8 *act, float *out, size
         if (e != cudaSuccess) return fail_cuda(e, "gemm_repacked (tensor-core kernel attribute)");
         attr_set[dev] = true;
     }
-    const size_t slots = (size_t)num_sms() * C::CTAS;
-    const size_t grid = ntiles < slots ? ntiles : slots;
+    const size_t grid = ntiles < (size_t)num_sms() ? ntiles : (size_t)num_sms();
     gemm_tc_kernel<C><<<(unsigned)grid, C::THREADS, smem, st>>>(
         wt.tmW, tmX, wt.tmWS, tmXS, wt.tmWM, tmXN, (int)act->m, (int)G, (int)row_begin,
         (int)sub_n, tiles_w, tiles_t, out, err);
@@ -949,18 +943,6 @@ int choose_tile(size_t m, size_t sub_n, bool mins) {
 template <bool E, bool MN, bool H> using TC64 = TcCfg<64, 2, H ? 2 : 4, E, MN, H>;
 template <bool E, bool MN, bool H> using TC96 = TcCfg<96, 3, H ? 1 : 2, E, MN, H>;
 template <bool E, bool MN, bool H> using TC128 = TcCfg<128, 2, H ? 1 : 2, E, MN, H>;
-// 64 tokens, one group a round, two CTAs per SM (256 TMEM columns and half the stages each).
-template <bool E, bool MN> using TC64X2 = TcCfg<64, 2, 1, E, MN, false, NIB_NONE, 1, 2>;
-
-// JKB_GEMM_2CTA=1 in the environment runs the 32-element-group GEMMs on TC64X2 (for measuring
-// it against the one-CTA configurations).
-static bool two_cta_selected() {
-    static const bool on = [] {
-        const char *v = getenv("JKB_GEMM_2CTA");
-        return v && v[0] == '1' && v[1] == 0;
-    }();
-    return on;
-}
 
 // The nibble GEMM's configurations: the repacked GEMM's three with two converter warps; with
 // IQ4_NL's four (14 warps and more leave 144 registers a thread or fewer) only the 64-token
@@ -986,10 +968,6 @@ int launch_tc_bn(int bn, const jkb_repacked_weight *w, const jkb_act_q8 *act, fl
     if constexpr (MINS && H16) {
         return launch_tc<TC64_H16_MINS<EXACT>>(w, act, out, row_begin, row_end, st, err);
     } else {
-        if constexpr (!H16) {
-            if (two_cta_selected())
-                return launch_tc<TC64X2<EXACT, MINS>>(w, act, out, row_begin, row_end, st, err);
-        }
         switch (bn) {
             case 64:
                 return launch_tc<TC64<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
