@@ -18,8 +18,9 @@ the lm_head is 431 MB, so every step streams 554 MB (> 4x the 126 MB L2).
 
 With --gpus N (torchrun, one rank per GPU) every matrix is sharded by output rows; each rank
 runs its slices, and one launch of this library's all-gather kernel per step pushes the output
-slices to every peer over NVLink (--collective nccl: one NCCL all-gather instead). Strong
-scaling: the same total work at every N.
+slices to every peer over NVLink (--collective push: the GEMV kernels store every row into
+every peer's buffer as they compute it, and one signal kernel completes the step; nccl: one
+NCCL all-gather). Strong scaling: the same total work at every N.
 
 Sections of the same JSON line: the Llama-3-70B decode set at batch 1 and 16, the
 Q4_0 GEMV, the Q8_0 prefill GEMM and BitNet BitLinear.
@@ -329,7 +330,7 @@ def run_reference(args):
         "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8 dot / f32 scale", "data": "synthetic",
-        "config": decode_config(spec, args.gpus, args.collective == "peer"),
+        "config": decode_config(spec, args.gpus, args.collective),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores,
                          "kind": "port", "sample": sample, "cpu_model": cpu_model()},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -376,19 +377,20 @@ class DecodeSet:
     Layer matrices can exist in `layer_copies` copies used on alternate steps, so that a step
     never finds its weights in the L2."""
 
-    def __init__(self, jkb, mats, acts, world, rank, *, peer=True, batch=1, layer_copies=1,
-                 prequant=("f",), unfused=False, seed=1000, sigma=0.02):
+    def __init__(self, jkb, mats, acts, world, rank, *, peer=True, push=False, batch=1,
+                 layer_copies=1, prequant=("f",), unfused=False, seed=1000, sigma=0.02):
         import torch
         from jkb200.shard import PeerOutputs, ShardedOutputs
 
         self.jkb, self.mats, self.acts = jkb, mats, acts
         self.world, self.rank, self.batch = world, rank, batch
         self.peer = peer and world > 1
+        self.push = push and self.peer
         self.unfused, self.prequant = unfused, set(prequant) - {""}
         names = [(name, rows) for name, _, rows, _, _ in mats]
         # two output slots alternate by step parity (a step's outputs stay readable while the
         # next step runs): the peer group's two slots, or two flat NCCL / single-GPU buffers
-        self.outs = (PeerOutputs(names, world, rank, batch=batch) if self.peer
+        self.outs = (PeerOutputs(names, world, rank, batch=batch, push=self.push) if self.peer
                      else ShardedOutputs(names, world, rank, batch=batch))
         self.outs2 = (None if self.peer
                       else [self.outs, ShardedOutputs(names, world, rank, batch=batch)])
@@ -522,7 +524,9 @@ class DecodeSet:
                 group(s)
         group(self.lm_stream)
         coll = []
-        if self.peer:
+        if self.push:
+            coll.append((L.jkb_peer_group_signal, (self.outs.group.handle, stream)))
+        elif self.peer:
             if not hasattr(self.outs, "_chunks"):
                 self.outs._chunks = [self.outs.group.chunk_arrays(self.outs.chunks(j))
                                      for j in range(self.outs.SLOTS)]
@@ -605,7 +609,9 @@ def time_decode(ds, steps, warmup, stream, world, local=0, sample_clocks=False):
         # nvidia-smi samples every 100 ms and the timed replay lasts milliseconds: about 0.5 s of
         # untimed replays of the same graph run right before it, so the clock samples are taken
         # under this workload.
-        n_load = max(1, int(500.0 / max(t_start.elapsed_time(t_end), 1e-3)))
+        # the same count on every rank (each replay holds one exchange per step)
+        n_load = max(1, int(500.0 / max(_max_over_ranks(t_start.elapsed_time(t_end), world),
+                                        1e-3)))
         sampler = ClockSampler(local)
         sampler.start()
         time.sleep(0.2)
@@ -736,12 +742,12 @@ def e2e_decode(ds, steps, warmup, world, stream):
             "d2h_bytes_per_step": out_bytes, "host_us_per_step": round(host_s / steps * 1e6, 2)}
 
 
-def decode_section(jkb, spec, world, rank, stream, steps, warmup, batch, peer):
+def decode_section(jkb, spec, world, rank, stream, steps, warmup, batch, peer, push):
     """configs[4]-style numbers for one decode set and batch: GB/s of the whole job, the
     fraction of measured HBM per GPU, and the per-step split (max over ranks)."""
     mats, acts, copies, sigma = spec["mats"], spec["acts"], spec["copies"], spec["sigma"]
-    ds = DecodeSet(jkb, mats, acts, world, rank, peer=peer, batch=batch, layer_copies=copies,
-                   sigma=sigma)
+    ds = DecodeSet(jkb, mats, acts, world, rank, peer=peer, push=push, batch=batch,
+                   layer_copies=copies, sigma=sigma)
     t = time_decode(ds, steps, warmup, stream, world)
     peak, _ = measured_peaks()
     gbs = ds.bytes_per_step / (t["ms_step"] * 1e-3) / 1e9
@@ -772,10 +778,10 @@ def run_gpu(args):
 
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
-    peer = args.collective == "peer"
+    peer, push = args.collective in ("push", "peer"), args.collective == "push"
     spec = DECODE_SETS[args.workload]
     # --- the headline: this rank's row shard of every matrix of the decode set
-    ds = DecodeSet(jkb, spec["mats"], spec["acts"], world, rank, peer=peer,
+    ds = DecodeSet(jkb, spec["mats"], spec["acts"], world, rank, peer=peer, push=push,
                    layer_copies=spec["copies"], prequant=args.prequant.split(","),
                    unfused=args.unfused, sigma=spec["sigma"])
     t = time_decode(ds, args.steps, args.warmup, stream, world, local, sample_clocks=True)
@@ -794,12 +800,13 @@ def run_gpu(args):
         sections[DECODE_SETS[other]["key"]] = {
             "config": DECODE_SETS[other]["config"],
             "batch1": decode_section(jkb, DECODE_SETS[other], world, rank, stream, args.steps,
-                                     args.warmup, 1, peer)}
+                                     args.warmup, 1, peer, push)}
         for key, sp in DECODE_SETS.items():
             if sp.get("batch16"):
                 sec = sections.setdefault(sp["key"], {"config": sp["config"]})
                 sec["batch16"] = decode_section(jkb, sp, world, rank, stream,
-                                                max(4, args.steps // 4), args.warmup, 16, peer)
+                                                max(4, args.steps // 4), args.warmup, 16, peer,
+                                                push)
         sections["q4_0_gemv_4096"] = run_q4_0_gemv(jkb, world)
         sections["per_shape_" + spec["key"]] = run_decode_shapes(jkb, spec, world, rank)
     prefill = None if args.no_gemm else run_prefill_gemm(world, rank)
@@ -823,7 +830,7 @@ def run_gpu(args):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "int8 dot / f32 scale", "data": "synthetic",
-            "config": decode_config(spec, world, peer),
+            "config": decode_config(spec, world, args.collective),
             "split_us": {"layer_gemvs": round(t["layer_ms"] * 1e3, 2),
                          "lm_head": round(t["lm_head_ms"] * 1e3, 2),
                          "gather": round(t["gather_ms"] * 1e3, 2),
@@ -862,13 +869,15 @@ def run_gpu(args):
         dist.destroy_process_group()
 
 
-def decode_config(spec, world, peer):
+def decode_config(spec, world, collective):
     return {"workload": f"{spec['workload']} (BASELINE {spec['config']})", "batch": 1,
             "weights": "Q4_K_M layers + Q6_K lm_head",
             "l2": spec["l2"],
             "parallelism": f"row-shard x{world}" + (
                 "" if world == 1 else
-                " + one-kernel all-gather over NVLink peer memory" if peer
+                " + rows pushed to the peers by the GEMVs over NVLink, one signal kernel"
+                if collective == "push" else
+                " + one-kernel all-gather over NVLink peer memory" if collective == "peer"
                 else " + NCCL all-gather")}
 
 
@@ -1306,8 +1315,9 @@ def run_gemm_case(args):
     x = torch.randn(M * K, generator=torch.Generator().manual_seed(2)).cuda()
     act = jkb.QuantizedActQ8.quantize(x, M, K)
     out = torch.empty(M * N, dtype=torch.float32, device="cuda")
-    us = _graph_time(lambda: rw.gemm(out, act), args.launches)
-    print(json.dumps({"kernel": args.kernel, "m": M, "rows": N, "cols": K,
+    with jkb.gemm_exact(args.exact):
+        us = _graph_time(lambda: rw.gemm(out, act), args.launches)
+    print(json.dumps({"kernel": args.kernel, "m": M, "rows": N, "cols": K, "exact": args.exact,
                       "us_per_launch": round(us, 2),
                       "tops": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 2)}))
 
@@ -1334,6 +1344,37 @@ def run_bitlinear_case(args):
                       "tops": round(2.0 * M * N * K / (us * 1e-6) / 1e12, 2)}))
 
 
+def run_bitlinear_gemv_case(args):
+    """bitlinear_i8 at batch 1 on TQ2_0 (--kernel bitlinear) or I2_S (bitlinear_i2s) weights,
+    --rows x --cols, i8 activation from the SubLN quantizer, weight copies rotating past 2x the
+    L2, `--launches` calls in a CUDA graph (the profiling case of the BitNet batch-1 path)."""
+    import torch
+    import jkb200 as jkb
+
+    quant = I2_S if args.kernel == "bitlinear_i2s" else TQ2_0
+    N, K = args.rows, args.cols
+    be, bb = BLOCK[quant]
+    nbytes = N * (K // be) * bb + K + 4 * N
+    copies = max(1, min(128, -(-260_000_000 // nbytes)))
+    raw = synth_ternary(quant, N, K, 77)
+    ws = [jkb.Weight(jkb.TensorView("w", quant, [N, K], raw), N, K) for _ in range(copies)]
+    x = torch.randn(K, generator=torch.Generator().manual_seed(6)).cuda()
+    q = torch.empty(K, dtype=torch.int8, device="cuda")
+    sc = torch.empty(1, dtype=torch.float32, device="cuda")
+    jkb.subln_quantize_absmax_i8_rows(q, x, torch.ones(K, device="cuda"), 1, K, 1e-5, sc)
+    scale = float(sc.item())
+    out = torch.empty(N, dtype=torch.float32, device="cuda")
+    it = [0]
+
+    def one():
+        jkb.bitlinear_i8(out, ws[it[0] % copies], q, scale)
+        it[0] += 1
+
+    us = _graph_time(one, max(args.launches, copies) if args.launches > 3 else args.launches)
+    print(json.dumps({"kernel": args.kernel, "rows": N, "cols": K, "copies": copies,
+                      "us_per_launch": round(us, 3), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}))
+
+
 def run_int8_peak(args):
     """cuBLAS int8 GEMM throughput through torch._int_mm (the int8 roofline denominator)."""
     import torch
@@ -1355,10 +1396,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="jkb", choices=["jkb", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--collective", choices=["peer", "nccl"], default="peer",
-                    help="N > 1: collect the output-row shards with this library's one-kernel "
-                         "all-gather over NVLink peer memory (peer) or one NCCL all-gather per "
-                         "step (nccl)")
+    ap.add_argument("--collective", choices=["push", "peer", "nccl"], default="peer",
+                    help="N > 1: collect the output-row shards by pushing them to the peers "
+                         "from the GEMV kernels over NVLink plus one signal kernel (push), by "
+                         "this library's one-kernel all-gather over NVLink peer memory (peer) "
+                         "or by one NCCL all-gather per step (nccl)"),
     ap.add_argument("--prequant", default="f",
                     help="comma list of activation streams (x, attn, h, a, f) quantized by their "
                          "own quantize_row_q8_k launch ahead of pre-quantized GEMVs instead of "
@@ -1377,11 +1419,14 @@ def main():
     ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0", "gemm_q8_0", "gemm_q4_k",
                                          "gemm_q6_k", "gemm_nib_q4_k", "gemm_q4_1", "gemm_q5_1",
                                          "gemm_iq4_nl", "gemm_q2_k", "gemm_q3_k", "int8_peak",
-                                         "bitlinear_tc"],
+                                         "bitlinear_tc", "bitlinear", "bitlinear_i2s"],
                     help="run one GEMV shape (profiling case) instead of the benchmark")
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--cols", type=int, default=4096)
     ap.add_argument("--launches", type=int, default=3)
+    ap.add_argument("--exact", action="store_true",
+                    help="--kernel gemm_*: the bit-exact epilogue (gemm_exact) instead of the "
+                         "default fused multiply-add")
     ap.add_argument("--unfused", action="store_true",
                     help="quantize each activation in its own launch and run one GEMV launch "
                          "per matrix (jkb_quantize_row_q8_k + jkb_gemv_*) instead of the "
@@ -1391,6 +1436,8 @@ def main():
         args.warmup = 3
     if args.kernel == "bitlinear_tc":
         run_bitlinear_case(args)
+    elif args.kernel in ("bitlinear", "bitlinear_i2s"):
+        run_bitlinear_gemv_case(args)
     elif args.kernel and args.kernel.startswith("gemm_"):
         run_gemm_case(args)
     elif args.kernel == "int8_peak":

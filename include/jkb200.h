@@ -676,8 +676,27 @@ int jkb_peer_group_buffer(const jkb_peer_group *pg, void **local, size_t *bytes)
 int jkb_peer_group_allgather(jkb_peer_group *pg, const size_t *offset, const size_t *len,
                              size_t n, void *stream);
 /* Low-level: make `stream` wait until `arrivals` more peer signals have reached this rank than
- * at its previous wait (each allgather delivers one per pushing CTA of every peer). */
+ * at its previous wait (each allgather or signal call delivers one from every peer). */
 int jkb_peer_group_wait(jkb_peer_group *pg, uint64_t arrivals, void *stream);
+/* Pushed outputs: the all-gather fused into the GEMVs. While push is enabled on a group (an
+ * opened group; at most 8 groups at a time), every launch of the single-token, grouped and
+ * token-batch GEMV entry points (jkb_gemv_q*_q8_*, jkb_gemv_tq*_q8_k, jkb_gemv_rows,
+ * jkb_gemv_batch, jkb_vec_dot_<fmt>_rvv, jkb_vec_dot_grouped_rvv, jkb_bitlinear_i8, its _rvv /
+ * _ime forms and jkb_bitlinear_i8_batch) whose outputs lie
+ * in the group's buffer also stores each output element to the same offset in every peer's
+ * buffer, from the kernel that computes it (NVLink stores), and fences those stores at system
+ * scope before the kernel ends. jkb_peer_group_signal then completes the exchange: one small
+ * kernel signals every peer and makes `stream` wait until every peer's signal of the same call
+ * has arrived (bounded like the all-gather). All ranks call it once per step, after their
+ * pushing launches; the two-slot rule of the all-gather applies. An output range that crosses
+ * the edge of a pushing buffer fails with JKB_E_BOUNDS. The repacked and nibble products
+ * (jkb_gemm_repacked*, jkb_gemv_repacked*, jkb_bitlinear_i8_gemm, the PackedNibbleMatrix
+ * GEMMs), the scalar block dots jkb_vec_dot_<fmt>_q8_* and the f32 jkb_vec_dot_<fmt> do not
+ * push and fail with JKB_E_CAPABILITY on an output in a pushing buffer; other entry points do
+ * not push either (their outputs belong outside pushing buffers). With one rank both calls are
+ * no-ops. */
+int jkb_peer_group_set_push(jkb_peer_group *pg, int enable);
+int jkb_peer_group_signal(jkb_peer_group *pg, void *stream);
 int jkb_peer_group_destroy(jkb_peer_group *pg);
 
 #if defined(__GNUC__)

@@ -169,7 +169,8 @@ static int vec_dot_raw(const char *fn, int quant, const uint8_t *w, size_t w_len
                     x_len * (size_t)f->block_bytes, x_len, w_len);
     if (!w || !x || !result) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
     int rc;
-    if ((rc = check_align(x, 4, fn, "x_blocks")) || (rc = check_align(result, 4, fn, "result")))
+    if ((rc = check_align(x, 4, fn, "x_blocks")) || (rc = check_align(result, 4, fn, "result")) ||
+        (rc = push_reject(result, result + 1, fn)))
         return rc;
     if (x_len > 16384)
         return fail(JKB_E_BOUNDS, fn, 0, x_len, 16384, "%s: %zu blocks exceed the 16384-block row "
@@ -358,7 +359,8 @@ static int vec_dot_f32_call(const char *fn, int quant, float *out, size_t out_le
     int rc = validate_weight_call(fn, w, quant, out_len, in_len);
     if (rc) return rc;
     if (!out || !input) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
-    if ((rc = check_align(out, 4, fn, "output")) || (rc = check_align(input, 4, fn, "input")))
+    if ((rc = check_align(out, 4, fn, "output")) || (rc = check_align(input, 4, fn, "input")) ||
+        (rc = push_reject(out, out + out_len, fn)))
         return rc;
     DqArgs a;
     a.qs = w->p.qs;

@@ -133,6 +133,7 @@ static int gemm_rows(const char *fn, float *out, size_t out_len, const jkb_repac
     if (sub_n == 0 || act->m == 0) return JKB_OK;
     if (!out) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null output");
     int arc = check_align(out, 4, fn, "output");
+    if (!arc) arc = push_reject(out, out + out_len, fn);
     if (arc) return arc;
     bool used = false;
     int rc = gemm_tc_launch(w, act, out, row_begin, row_end, st, &used);
@@ -324,7 +325,8 @@ int jkb_bitlinear_i8_gemm(float *out, size_t out_len, const jkb_repacked_weight 
     if (!out || !act_i8 || !act_scales) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null pointer");
     int rc;
     if ((rc = check_align(out, 4, fn, "output")) ||
-        (rc = check_align(act_scales, 4, fn, "act_scales")))
+        (rc = check_align(act_scales, 4, fn, "act_scales")) ||
+        (rc = push_reject(out, out + out_len, fn)))
         return rc;
     cudaStream_t st = as_stream(stream);
     if ((rc = act_q8_from_i8(scratch, act_i8, act_scales, m, st))) return rc;

@@ -61,6 +61,10 @@ struct KArgs {
     int tpc;        // M_TOK: tokens per CTA (1..TOK_MAX), each staged in its own smem slot
     int32_t *dbg_sumi, *dbg_mins;
     float *dbg_val;
+    // pushed outputs: every output element is also stored at these byte offsets from its
+    // address (the same position in each peer's mapping of a pushing peer group's buffer)
+    int npush;
+    long long push_delta[JKB_PEER_MAX_RANKS - 1];
 };
 
 // Row pointers of one weight row: quant plane, scale plane, f16 block scales.
@@ -284,6 +288,14 @@ __device__ __forceinline__ void load_group(const float *x, bool vec, int e, floa
 // BlockQ8K (quantize_row_q8_k, quant_q8.rs:447-475), into the ActQ8K layout: lane l of the warp
 // takes elements 8l..8l+8 of the superblock; absmax by shuffles; lane l writes its 8 bytes, even
 // lanes the 16-element bsums, lane 0 the scale and the block total.
+// Every CTA of the cluster has started, so its shared memory may be written through the
+// cluster window. Only execution is ordered (nothing has been written yet), so the arrive is
+// relaxed: a release here would wait for the weight loads already in flight.
+__device__ __forceinline__ void cluster_started() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" :::
+                     "memory");
+}
+
 struct ActQ8KF32 : ActQ8K {
     static constexpr bool kCluster = true;  // launched as thread-block clusters
     static int units(int K) { return K / 256; }
@@ -295,7 +307,7 @@ struct ActQ8KF32 : ActQ8K {
         const int K = a.K, nsb = K / 256;
         const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
         const int gw = (int)rank * nw + (threadIdx.x >> 5), gstride = (int)C * nw;
-        cl.sync();
+        cluster_started();
         // two superblocks per warp and round: both loads are issued before the arithmetic
         for (int sb0 = gw; sb0 < nsb; sb0 += 2 * gstride) {  // warp-uniform
             float vv[2][8];
@@ -366,7 +378,7 @@ struct ActQ80F32 : ActQ80 {
         const int K = a.K, nbk = K / 32, nunit = (nbk + 3) / 4;
         const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
         const int gw = (int)rank * nw + (threadIdx.x >> 5), gstride = (int)C * nw;
-        cl.sync();
+        cluster_started();
         const int sub = lane & 7;
         // two units per warp and round: both loads are issued before the arithmetic
         for (int u0 = gw; u0 < nunit; u0 += 2 * gstride) {  // warp-uniform
@@ -992,7 +1004,13 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, (gemv_min_blocks<F, MODE>())) 
                     if (li == 0 && r0 + rsub < a.row_end) {
                         float *o =
                             MODE == M_MULTI ? outp : a.mat[0].out + (r0 + rsub - a.row_begin);
-                        o[tok_off + (size_t)t * a.out_ld] = acc[t];
+                        float *dst = o + tok_off + (size_t)t * a.out_ld;
+                        *dst = acc[t];
+#pragma unroll
+                        for (int q = 0; q < JKB_PEER_MAX_RANKS - 1; q++)
+                            if (q < a.npush)
+                                *reinterpret_cast<float *>(reinterpret_cast<char *>(dst) +
+                                                           a.push_delta[q]) = acc[t];
                     }
                 }
             }
@@ -1073,6 +1091,9 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, (gemv_min_blocks<F, MODE>())) 
             if (r0 < a.row_end) issue();
         }
     }
+    // pushed outputs are performed at system scope before the grid completes, so a peer that
+    // sees the signal sent after it (jkb_peer_group_signal) sees them
+    if (a.npush) __threadfence_system();
 }
 
 // ---------------------------------------------------------------- launch
@@ -1288,6 +1309,26 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
                     "no GEMV kernel for this combination of grouped/diagnostic launch and "
                     "activation kind %d",
                     L.act_kind);
+    if (!diag) {
+        // outputs in a pushing peer group's buffer: every matrix of the launch in the same one
+        PushTarget pt;
+        for (int i = 0; i < a.nmat; i++) {
+            const size_t n = multi ? L.ws[i]->rows : a.row_end - a.row_begin;
+            const float *lo = a.mat[i].out;
+            PushTarget ti;
+            const int rc = push_lookup(lo, lo + (m - 1) * a.out_ld + n, &ti, w->name);
+            if (rc) return rc;
+            if (i == 0)
+                pt = ti;
+            else if (ti.group != pt.group)
+                return fail(JKB_E_INVALID, w->name, 0, (size_t)i, (size_t)a.nmat,
+                            "grouped GEMV: outputs 0 and %d are not in the same pushing peer "
+                            "group's buffer (one launch pushes to one group or none)",
+                            i);
+        }
+        a.npush = pt.n;
+        for (int q = 0; q < pt.n; q++) a.push_delta[q] = pt.delta[q];
+    }
     // pre-quantized or i8 activations: single or diagnostic launches
 #define JKB_LAUNCH(F)                                                                   \
     return diag  ? launch_t<F, F::Act, M_DIAG>(a, m, st, "gemv_kernel<diag>")           \

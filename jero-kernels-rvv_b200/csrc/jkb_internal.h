@@ -216,6 +216,21 @@ struct GemvLaunch {
 };
 int launch_gemv(const GemvLaunch &L, cudaStream_t st);
 
+// Output pushing (peer.cu): the peers of a peer group with push enabled, as byte offsets from an
+// address in this rank's buffer to the same position in each peer's mapping of its buffer.
+struct PushTarget {
+    int n = 0;  // peers to store to (0: the range is in no pushing group)
+    long long delta[JKB_PEER_MAX_RANKS - 1] = {};
+    const void *group = nullptr;
+};
+// Looks up the byte range [lo, hi) among the buffers of this device's pushing peer groups:
+// JKB_OK with t->n = 0 when it is in none, filled in when it lies inside one, JKB_E_BOUNDS when
+// it crosses the edge of one. `who` names the caller in the error.
+int push_lookup(const void *lo, const void *hi, PushTarget *t, const char *who);
+// JKB_E_CAPABILITY when [lo, hi) overlaps a pushing group's buffer: for the entry points whose
+// kernels write outputs without pushing them (the repacked GEMMs).
+int push_reject(const void *lo, const void *hi, const char *who);
+
 // Fills a jkb_act_q8 from i8 BitLinear activations with per-token scales (quantize.cu).
 int act_q8_from_i8(jkb_act_q8 *a, const int8_t *act_i8, const float *scales, size_t m,
                    cudaStream_t st);

@@ -260,6 +260,7 @@ int nibble_gemm_rows(const char *fn, float *out, size_t out_len, const jkb_nibbl
     if (sub_n == 0 || act->m == 0) return JKB_OK;
     if (!out) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null output");
     rc = check_align(out, 4, fn, "output");
+    if (!rc) rc = push_reject(out, out + out_len, fn);
     if (rc) return rc;
     bool used = false;
     rc = gemm_tc_nibble_launch(w, act, out, row_begin, row_end, st, &used);

@@ -1,18 +1,27 @@
 // Peer groups: a one-kernel all-gather of output-row shards over NVLink.
 //
 // One process per GPU. Each rank's group owns one cudaMalloc allocation:
-//   [0, 8)      arrival counter (u64): signals received from peers, one per pushing CTA
+//   [0, 8)      arrival counter (u64): signals received from peers, one per peer and call
 //   [8, 16)     expected count (u64): advanced by each wait
+//   [16, 24)    CTA counter (u64) of this rank's all-gather launches
 //   [256, ...)  the output buffer handed to callers (`bytes` long), identical layout on every rank
 // The ranks exchange CUDA IPC handles of these allocations and map each other's. The all-gather
 // kernel (a fixed grid of AG_CTAS CTAs on every rank) copies this rank's chunks of the buffer to
 // the same offsets in every peer's buffer with coalesced 16-byte stores over NVLink (plain
-// stores; no multicast). Each CTA then passes a CTA barrier, fences at system scope and adds 1
-// to every peer's arrival counter with release semantics; CTA 0 advances this rank's expected
-// count by (world - 1) * AG_CTAS and spins, with an acquire load and a 2 s bound, until the
-// arrivals reach it. Both counts live on the device, so a captured CUDA graph stays correct
-// across replays.
+// stores; no multicast). Each CTA then passes a CTA barrier, fences at system scope and counts
+// itself; the last CTA of the launch adds 1 to every peer's arrival counter with release
+// semantics, advances this rank's expected count by world - 1 and spins, with an acquire load
+// and a 2 s bound, until the arrivals reach it. The counts live on the device, so a captured
+// CUDA graph stays correct across replays.
+//
+// Pushing groups: with push enabled, the GEMV kernels whose outputs lie in the group's buffer
+// store every output element to the same offset in each peer's buffer as well (4-byte stores
+// over NVLink, spread over the kernel's run) and fence them at system scope before they exit.
+// The step then ends with jkb_peer_group_signal: the all-gather kernel with no chunks and one
+// CTA, which only signals every peer and waits for their signals.
+#include <atomic>
 #include <cstring>
+#include <mutex>
 
 #include "jkb_internal.h"
 
@@ -25,6 +34,7 @@ struct jkb_peer_group {
     bool opened;
     cudaIpcMemHandle_t handle;
     int device;
+    bool push;  // registered in the pushing-group table
 };
 
 namespace jkb {
@@ -32,19 +42,76 @@ namespace jkb {
 constexpr uint32_t PEER_MAGIC = 0x4A4B5031u;  // "JKP1"
 constexpr size_t PEER_HDR = 256;              // counters and padding
 constexpr unsigned long long PEER_WAIT_NS = 2000000000ull;
-constexpr int AG_CTAS = 16;                   // CTAs of every rank's all-gather launch
+constexpr int AG_CTAS = 128;                  // CTAs of every rank's all-gather launch
 constexpr int AG_THREADS = 256;
+constexpr int AG_VEC = 4;                     // 16-byte loads in flight per thread
 
 static bool check_pg(const jkb_peer_group *pg) { return pg && pg->magic == PEER_MAGIC; }
 
+// The groups with push enabled, looked up by every GEMV launch while the count is non-zero.
+constexpr int PUSH_MAX_GROUPS = 8;
+std::mutex g_push_mu;
+std::atomic<int> g_push_count{0};
+jkb_peer_group *g_push[PUSH_MAX_GROUPS];
+
+static void push_unregister(jkb_peer_group *pg) {
+    std::lock_guard<std::mutex> lk(g_push_mu);
+    for (int i = 0; i < PUSH_MAX_GROUPS; i++)
+        if (g_push[i] == pg) {
+            g_push[i] = nullptr;
+            g_push_count.fetch_sub(1, std::memory_order_release);
+        }
+    pg->push = false;
+}
+
+int push_lookup(const void *lo, const void *hi, PushTarget *t, const char *who) {
+    *t = PushTarget{};
+    if (g_push_count.load(std::memory_order_acquire) == 0 || hi <= lo) return JKB_OK;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess) return fail_cuda(cudaGetLastError(), who);
+    const uint8_t *l = static_cast<const uint8_t *>(lo), *h = static_cast<const uint8_t *>(hi);
+    std::lock_guard<std::mutex> lk(g_push_mu);
+    for (int i = 0; i < PUSH_MAX_GROUPS; i++) {
+        const jkb_peer_group *pg = g_push[i];
+        if (!pg || pg->device != dev) continue;
+        const uint8_t *b = pg->base + PEER_HDR, *e = b + pg->bytes;
+        if (h <= b || l >= e) continue;
+        if (l < b || h > e)
+            return fail(JKB_E_BOUNDS, who, (size_t)(l - b), (size_t)(h - l), pg->bytes,
+                        "output range crosses the edge of a pushing peer group's %zu-byte buffer",
+                        pg->bytes);
+        for (int p = 0; p < pg->world; p++)
+            if (p != pg->rank) t->delta[t->n++] = (long long)(pg->peer_base[p] - pg->base);
+        t->group = pg;
+        return JKB_OK;
+    }
+    return JKB_OK;
+}
+
+int push_reject(const void *lo, const void *hi, const char *who) {
+    PushTarget t;
+    int rc = push_lookup(lo, hi, &t, who);
+    if (rc == JKB_OK && t.group)
+        rc = fail(JKB_E_CAPABILITY, who, 0, 0, 0,
+                  "output inside a pushing peer group's buffer: this entry point does not push "
+                  "its outputs (use jkb_peer_group_allgather, or disable push)");
+    return rc;
+}
+
 namespace {
 
+// One all-gather launch. The chunks' 16-byte aligned bodies form one index space of 16-byte
+// words (body_pre: prefix counts); their 4-byte heads and tails (up to 3 words each) are listed
+// in w4. Both are laid out on the host.
 struct AgArgs {
-    int world, rank, nchunk;
-    unsigned long long off[JKB_PEER_MAX_CHUNKS], len[JKB_PEER_MAX_CHUNKS];  // bytes
+    int world, rank, nchunk, n4;
+    unsigned long long body_off[JKB_PEER_MAX_CHUNKS];      // byte offset of chunk c's body
+    unsigned long long body_pre[JKB_PEER_MAX_CHUNKS + 1];  // 16-byte words before chunk c's body
+    unsigned long long w4[6 * JKB_PEER_MAX_CHUNKS];        // byte offsets of 4-byte words
     uint8_t *data[JKB_PEER_MAX_RANKS];                 // every rank's buffer (data region)
     unsigned long long *cnt[JKB_PEER_MAX_RANKS];       // every rank's arrival counter
     unsigned long long *expected;                      // this rank's expected count
+    unsigned long long *done;                          // this rank's CTA counter of launches
     unsigned long long arrivals;                       // added to it by this launch's wait
     int *err;
 };
@@ -81,35 +148,61 @@ __global__ void __launch_bounds__(AG_THREADS) peer_allgather_kernel(AgArgs a) {
     const uint8_t *src = a.data[a.rank];
     const size_t tid = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     const size_t nthr = (size_t)gridDim.x * blockDim.x;
-    for (int c = 0; c < a.nchunk; c++) {
-        const size_t off = a.off[c], len = a.len[c];
-        // 4-byte head up to a 16-byte boundary, 16-byte body, 4-byte tail
-        const size_t head = ((16 - (off & 15)) & 15) < len ? ((16 - (off & 15)) & 15) : len;
-        const size_t body = (len - head) & ~(size_t)15;
-        for (size_t i = tid; i < (body >> 4); i += nthr) {
-            const size_t o = off + head + (i << 4);
-            const uint4 v = *reinterpret_cast<const uint4 *>(src + o);
-            for (int p = 0; p < a.world; p++)
-                if (p != a.rank) *reinterpret_cast<uint4 *>(a.data[p] + o) = v;
+    const unsigned long long nbody = a.body_pre[a.nchunk];
+    // each thread loads up to AG_VEC words of the flat body index before storing any, so a
+    // launch's L2 round trips overlap instead of following one another chunk by chunk
+    for (size_t base = tid; base < nbody; base += AG_VEC * nthr) {
+        uint4 v[AG_VEC];
+        size_t o[AG_VEC];
+#pragma unroll
+        for (int u = 0; u < AG_VEC; u++) {
+            const size_t i = base + (size_t)u * nthr;
+            o[u] = ~(size_t)0;
+            if (i < nbody) {
+                int c = 0;
+                while (c + 1 < a.nchunk && a.body_pre[c + 1] <= i) c++;
+                o[u] = a.body_off[c] + ((i - a.body_pre[c]) << 4);
+                v[u] = *reinterpret_cast<const uint4 *>(src + o[u]);
+            }
         }
-        const size_t tail = len - head - body;
-        for (size_t i = tid; i < ((head + tail) >> 2); i += nthr) {
-            const size_t o = i < (head >> 2) ? off + (i << 2) : off + head + body + ((i - (head >> 2)) << 2);
-            const uint32_t v = *reinterpret_cast<const uint32_t *>(src + o);
-            for (int p = 0; p < a.world; p++)
-                if (p != a.rank) *reinterpret_cast<uint32_t *>(a.data[p] + o) = v;
-        }
+#pragma unroll
+        for (int u = 0; u < AG_VEC; u++)
+            if (o[u] != ~(size_t)0)
+                for (int p = 0; p < a.world; p++)
+                    if (p != a.rank) *reinterpret_cast<uint4 *>(a.data[p] + o[u]) = v[u];
     }
-    // The CTA barrier orders every thread's stores before thread 0's system-scope fence and
-    // release, which are cumulative over them; the peer's acquire in its wait sees the data.
+    for (size_t i = tid; i < (size_t)a.n4; i += nthr) {
+        const size_t o = a.w4[i];
+        const uint32_t v = *reinterpret_cast<const uint32_t *>(src + o);
+        for (int p = 0; p < a.world; p++)
+            if (p != a.rank) *reinterpret_cast<uint32_t *>(a.data[p] + o) = v;
+    }
+    // The CTA barrier orders every thread's stores before thread 0's system-scope fence, which
+    // is cumulative over them. The CTAs then count themselves on this rank's launch counter;
+    // the last one (whose acquire-release add follows every other CTA's fence) fences again,
+    // signals each peer once with a release and waits for the peers' signals. A one-CTA launch
+    // (jkb_peer_group_signal) is its own last CTA and leaves the counter alone, so the counter
+    // stays a multiple of AG_CTAS between all-gather launches.
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence_system();
-        for (int p = 0; p < a.world; p++)
-            if (p != a.rank)
-                asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(a.cnt[p]) : "memory");
-        if (blockIdx.x == 0)
+        bool last = gridDim.x == 1;
+        if (!last) {
+            unsigned long long old;
+            asm volatile("atom.add.acq_rel.gpu.global.u64 %0, [%1], 1;"
+                         : "=l"(old)
+                         : "l"(a.done)
+                         : "memory");
+            last = (old + 1) % gridDim.x == 0;
+        }
+        if (last) {
+            __threadfence_system();
+            for (int p = 0; p < a.world; p++)
+                if (p != a.rank)
+                    asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(a.cnt[p])
+                                 : "memory");
             bounded_arrival_wait(a.cnt[a.rank], a.expected, a.arrivals, a.err);
+        }
     }
 }
 
@@ -122,6 +215,30 @@ __global__ void peer_wait_kernel(unsigned long long *cnt, unsigned long long *ex
 }  // namespace jkb
 
 using namespace jkb;
+
+// The all-gather kernel on `ctas` CTAs, each of which signals every peer once after its share
+// of a's chunks (none for jkb_peer_group_signal).
+static int launch_allgather(jkb_peer_group *pg, AgArgs &a, int ctas, void *stream,
+                            const char *fn) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != pg->device)
+        return fail(JKB_E_INVALID, fn, 0, 0, 0, "peer group created on device %d, current %d",
+                    pg->device, dev);
+    int *err = device_error_word();
+    if (!err) return fail(JKB_E_CUDA, fn, 0, 0, 0, "no device error word");
+    for (int p = 0; p < pg->world; p++) {
+        a.data[p] = pg->peer_base[p] + PEER_HDR;
+        a.cnt[p] = reinterpret_cast<unsigned long long *>(pg->peer_base[p]);
+    }
+    a.expected = reinterpret_cast<unsigned long long *>(pg->base) + 1;
+    a.done = reinterpret_cast<unsigned long long *>(pg->base) + 2;
+    a.arrivals = (unsigned long long)(pg->world - 1);  // one signal from each peer
+    a.err = err;
+    const cudaError_t le =
+        launch_pdl(peer_allgather_kernel, dim3(ctas), dim3(AG_THREADS), 0, as_stream(stream), a);
+    if (le != cudaSuccess) return fail_cuda(le, "peer_allgather_kernel");
+    return check_launch("peer_allgather_kernel");
+}
 
 extern "C" {
 
@@ -214,27 +331,50 @@ int jkb_peer_group_allgather(jkb_peer_group *pg, const size_t *offset, const siz
             return fail(JKB_E_BOUNDS, fn, offset[i], len[i], pg->bytes,
                         "chunk %zu [%zu, +%zu) not 4-byte aligned or outside the %zu-byte buffer",
                         i, offset[i], len[i], pg->bytes);
-        a.off[i] = offset[i];
-        a.len[i] = len[i];
+        // 4-byte head up to a 16-byte boundary, 16-byte body, 4-byte tail
+        const size_t off = offset[i], l = len[i];
+        const size_t head = ((16 - (off & 15)) & 15) < l ? ((16 - (off & 15)) & 15) : l;
+        const size_t body = (l - head) & ~(size_t)15;
+        for (size_t o = off; o < off + head; o += 4) a.w4[a.n4++] = o;
+        for (size_t o = off + head + body; o < off + l; o += 4) a.w4[a.n4++] = o;
+        a.body_off[i] = off + head;
+        a.body_pre[i + 1] = a.body_pre[i] + (body >> 4);
     }
     if (pg->world == 1) return JKB_OK;  // every chunk is already in place
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev != pg->device)
-        return fail(JKB_E_INVALID, fn, 0, 0, 0, "peer group created on device %d, current %d",
-                    pg->device, dev);
-    int *err = device_error_word();
-    if (!err) return fail(JKB_E_CUDA, fn, 0, 0, 0, "no device error word");
-    for (int p = 0; p < pg->world; p++) {
-        a.data[p] = pg->peer_base[p] + PEER_HDR;
-        a.cnt[p] = reinterpret_cast<unsigned long long *>(pg->peer_base[p]);
+    return launch_allgather(pg, a, AG_CTAS, stream, fn);
+}
+
+int jkb_peer_group_set_push(jkb_peer_group *pg, int enable) {
+    static const char *fn = "peer_group_set_push";
+    if (!check_pg(pg)) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null or destroyed group");
+    if (!pg->opened) return fail(JKB_E_INVALID, fn, 0, 0, 0, "peer group not opened");
+    if (!enable) {
+        if (pg->push) push_unregister(pg);
+        return JKB_OK;
     }
-    a.expected = reinterpret_cast<unsigned long long *>(pg->base) + 1;
-    a.arrivals = (unsigned long long)(pg->world - 1) * AG_CTAS;
-    a.err = err;
-    const cudaError_t le =
-        launch_pdl(peer_allgather_kernel, dim3(AG_CTAS), dim3(AG_THREADS), 0, as_stream(stream), a);
-    if (le != cudaSuccess) return fail_cuda(le, "peer_allgather_kernel");
-    return check_launch("peer_allgather_kernel");
+    std::lock_guard<std::mutex> lk(g_push_mu);
+    if (pg->push) return JKB_OK;
+    for (int i = 0; i < PUSH_MAX_GROUPS; i++)
+        if (!g_push[i]) {
+            g_push[i] = pg;
+            pg->push = true;
+            g_push_count.fetch_add(1, std::memory_order_release);
+            return JKB_OK;
+        }
+    return fail(JKB_E_BOUNDS, fn, 0, PUSH_MAX_GROUPS, PUSH_MAX_GROUPS,
+                "%d peer groups already push their outputs (limit)", PUSH_MAX_GROUPS);
+}
+
+int jkb_peer_group_signal(jkb_peer_group *pg, void *stream) {
+    static const char *fn = "peer_group_signal";
+    if (!check_pg(pg)) return fail(JKB_E_INVALID, fn, 0, 0, 0, "null or destroyed group");
+    if (!pg->opened) return fail(JKB_E_INVALID, fn, 0, 0, 0, "peer group not opened");
+    if (pg->world == 1) return JKB_OK;
+    AgArgs a = {};
+    a.world = pg->world;
+    a.rank = pg->rank;
+    a.nchunk = 0;
+    return launch_allgather(pg, a, 1, stream, fn);
 }
 
 int jkb_peer_group_wait(jkb_peer_group *pg, uint64_t arrivals, void *stream) {
@@ -251,6 +391,7 @@ int jkb_peer_group_wait(jkb_peer_group *pg, uint64_t arrivals, void *stream) {
 
 int jkb_peer_group_destroy(jkb_peer_group *pg) {
     if (!check_pg(pg)) return fail(JKB_E_INVALID, "peer_group_destroy", 0, 0, 0, "null group");
+    if (pg->push) push_unregister(pg);
     pg->magic = 0;
     for (int p = 0; p < pg->world; p++)
         if (p != pg->rank && pg->peer_base[p]) cudaIpcCloseMemHandle(pg->peer_base[p]);

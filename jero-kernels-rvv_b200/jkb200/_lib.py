@@ -155,6 +155,8 @@ SIGNATURES = {
     "jkb_peer_group_buffer": [P, PP, PS],
     "jkb_peer_group_allgather": [P, PS, PS, S, P],
     "jkb_peer_group_wait": [P, C.c_uint64, P],
+    "jkb_peer_group_set_push": [P, I],
+    "jkb_peer_group_signal": [P, P],
     "jkb_peer_group_destroy": [P],
     "jkb_bitlinear_i8": [P, S, P, P, S, F, P],
     "jkb_bitlinear_i8_rvv": [P, S, P, P, S, F, P],

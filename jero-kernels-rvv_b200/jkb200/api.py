@@ -974,6 +974,17 @@ class PeerGroup:
         """Low level: make the stream wait for `arrivals` more peer signals (bounded)."""
         _check(_L().jkb_peer_group_wait(self.handle, arrivals, _stream(stream)))
 
+    def set_push(self, enable: bool = True):
+        """While enabled, the GEMV entry points store every output element that lands in this
+        group's buffer into each peer's buffer too, from the kernel that computes it; signal()
+        then completes the exchange (jkb_peer_group_set_push)."""
+        _check(_L().jkb_peer_group_set_push(self.handle, 1 if enable else 0))
+
+    def signal(self, stream=None):
+        """Signal every peer that this rank's pushed outputs are complete and make the stream
+        wait for every peer's signal of the same call (bounded: bit 1 of device_status())."""
+        _check(_L().jkb_peer_group_signal(self.handle, _stream(stream)))
+
     def destroy(self):
         if getattr(self, "handle", None):
             _L().jkb_peer_group_destroy(self.handle)

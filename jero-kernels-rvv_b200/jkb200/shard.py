@@ -119,14 +119,19 @@ class PeerOutputs:
     slot)``; after ``gather(slot)`` every rank holds all rows of every matrix in
     ``output(name, slot)``. With a batch of m tokens a matrix takes m * rows floats of a slot,
     rank p's part being its [m][rows of the shard] block at offset m * (first row of the shard),
-    so each rank still pushes one contiguous chunk per matrix."""
+    so each rank still pushes one contiguous chunk per matrix.
+
+    push=True: the GEMVs that write ``local_slice`` store their rows into every peer's buffer
+    as they compute them (PeerGroup.set_push), and ``gather`` only signals and waits
+    (PeerGroup.signal); outputs must then come from the GEMV entry points."""
 
     SLOTS = 2
 
-    def __init__(self, mats, world: int, rank: int, group=None, batch: int = 1):
+    def __init__(self, mats, world: int, rank: int, group=None, batch: int = 1,
+                 push: bool = False):
         from .api import PeerGroup
 
-        self.world, self.rank, self.batch = world, rank, batch
+        self.world, self.rank, self.batch, self.push = world, rank, batch, push
         self.offs, self.rows = {}, {}
         total = 0
         for name, rows in mats:
@@ -135,6 +140,8 @@ class PeerOutputs:
         self.total = total
         self.pitch = (total + 3) // 4 * 4  # floats per slot (16-byte multiple)
         self.group = PeerGroup(self.SLOTS * self.pitch * 4, world, rank, group)
+        if push:
+            self.group.set_push(True)
         self.slots = self.group.buffer[:self.SLOTS * self.pitch].view(self.SLOTS, self.pitch)
 
     def rows_of(self, name: str) -> range:
@@ -171,7 +178,11 @@ class PeerOutputs:
         return out
 
     def gather(self, slot: int, stream=None):
-        """One kernel: this rank's rows of the slot to every peer, then wait for theirs."""
+        """One kernel: this rank's rows of the slot to every peer (already there with push),
+        then wait for theirs."""
+        if self.push:
+            self.group.signal(stream)
+            return
         if not hasattr(self, "_chunks"):
             self._chunks = [self.group.chunk_arrays(self.chunks(s)) for s in range(self.SLOTS)]
         self.group.allgather_arrays(self._chunks[slot], stream)

@@ -9,7 +9,9 @@ are independent, so sharding by rows changes no arithmetic (gemv_repacked_rows, 
 The same shapes then go through the library's one-kernel all-gather (jkb200.shard.PeerOutputs:
 every rank pushes its rows into every peer's buffer over NVLink): over three steps alternating
 the two output slots, every rank's full outputs must equal its own single-GPU results bit for
-bit. Prints one JSON line per rank and exits non-zero on a mismatch.
+bit. Then the same with pushed outputs (the GEMV kernels store each row into every peer's
+buffer, one signal kernel a step): single, grouped f32-input and token-batch launches. Prints
+one JSON line per rank and exits non-zero on a mismatch.
 """
 import json
 import os
@@ -133,6 +135,57 @@ def main():
     torch.cuda.synchronize()
     dist.barrier()  # no rank still writes into a peer's buffer
     pouts.destroy()
+
+    # pushed outputs: the GEMVs store their rows into every peer's buffer as they compute them
+    # and one signal kernel a step completes the exchange. ffn_gate through the grouped
+    # f32-input launch, ffn_down and lm_head through pre-quantized gemv_rows; then a batch of
+    # four tokens through gemv_batch. Every rank checks every row.
+    push = PeerOutputs([(nm, r) for nm, _, r, _, _ in MATS], world, rank, push=True)
+    push_ok = True
+    for step in range(3):
+        slot = step % 2
+        gs = torch.Generator().manual_seed(200 + step)
+        x_s = {s_: torch.randn(n_, generator=gs).cuda() for s_, n_ in ACTS.items()}
+        xq_s = {}
+        for s_, n_ in ACTS.items():
+            xq_s[s_] = jkb.empty_q8_k_blocks(n_ // 256)
+            jkb.quantize_row_q8_k(x_s[s_], xq_s[s_])
+        for name, quant, rows, cols, s in MATS:
+            if name == "ffn_gate":
+                jkb.vec_dot_grouped_rvv([(push.local_slice(name, slot), shard_w[name])], x_s[s])
+            else:
+                jkb.gemv_rows(push.local_slice(name, slot), shard_w[name], xq_s[s],
+                              range(0, len(push.rows_of(name))))
+        push.gather(slot)
+        for name, quant, rows, cols, s in MATS:
+            ref = torch.empty(rows, dtype=torch.float32, device="cuda")
+            if name == "ffn_gate":
+                jkb.vec_dot_grouped_rvv([(ref, full_w[name])], x_s[s])
+            else:
+                jkb.gemv_rows(ref, full_w[name], xq_s[s], range(0, rows))
+            push_ok &= torch.equal(push.output(name, slot).view(torch.int32),
+                                   ref.view(torch.int32))
+        torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    dist.barrier()
+    push.destroy()
+    name, quant, rows, cols, s = MATS[2]
+    pb = PeerOutputs([(name, rows)], world, rank, batch=4, push=True)
+    xb = torch.randn(4 * cols, generator=torch.Generator().manual_seed(300)).cuda()
+    xqb = jkb.empty_q8_k_blocks(4 * cols // 256)
+    jkb.quantize_rows_q8_k(xb, 4, cols, xqb)
+    jkb.gemv_batch(pb.local_slice(name, 0), shard_w[name], xqb, 4)
+    pb.gather(0)
+    ref = torch.empty(4 * rows, dtype=torch.float32, device="cuda")
+    jkb.gemv_batch(ref, full_w[name], xqb, 4)
+    push_ok &= torch.equal(pb.output(name, 0).reshape(-1).view(torch.int32),
+                           ref.view(torch.int32))
+    res["peer_push"] = "bit-exact" if push_ok else "MISMATCH"
+    res["push_status"] = jkb.device_status()
+    ok &= push_ok and res["push_status"] == 0
+    torch.cuda.synchronize()
+    dist.barrier()
+    pb.destroy()
 
     res["ok"] = bool(ok)
     print(json.dumps(res), flush=True)

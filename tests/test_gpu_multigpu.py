@@ -3,7 +3,7 @@ tests/mgpu_worker.py under torchrun on every visible GPU (at most 8) and checks 
 reports bit-exact reassembled outputs (Q4_K_M 8192 -> 28672 and 28672 -> 8192, Q6_K
 8192 -> 128256 GEMVs and a Q8_0 prefill GEMM, each against the single-GPU call on rank 0),
 both with the NCCL all-gather and with the library's one-kernel all-gather over NVLink peer
-memory (checked on every rank).
+memory, and with rows pushed to the peers by the GEMV kernels (both checked on every rank).
 Needs at least 2 GPUs; with one GPU the sharded host logic is covered by test_shard_gloo.py."""
 import json
 import os
@@ -36,3 +36,5 @@ def test_row_sharded_outputs_match_single_gpu():
     assert r0["device_status"] == 0
     for r in lines:  # the NVLink all-gather kernel: every rank holds every row
         assert r["peer_allgather"] == "bit-exact" and r["peer_status"] == 0, r
+        # rows pushed by the GEMV kernels themselves, one signal kernel a step
+        assert r["peer_push"] == "bit-exact" and r["push_status"] == 0, r

@@ -79,3 +79,70 @@ def test_allgather_chunk_validation(jkb):
     pg.allgather([(0, 1024)])
     assert jkb.device_status() == 0
     pg.destroy()
+
+
+def test_single_rank_push_and_signal(jkb, oracle):
+    """Push mode with one rank: the GEMVs into the group's buffer have no peer to store to and
+    stay bit-identical to the plain calls (single, grouped and token-batch launches); signal()
+    returns without a wait."""
+    from jkb200.shard import PeerOutputs
+
+    w1, w3 = _weights(oracle)
+    W1, W3 = upload(jkb, Q4_K, w1, 300, 1024), upload(jkb, Q6_K, w3, 130, 1024)
+    outs = PeerOutputs([("a", 300), ("b", 130)], 1, 0, push=True)
+    xq = jkb.empty_q8_k_blocks(4 * 4)
+    for step in range(3):
+        slot = step % 2
+        x = dev(oracle.normal(1024, 20 + step, 1.0))
+        jkb.vec_dot_grouped_rvv([(outs.local_slice("a", slot), W1)], x)
+        jkb.quantize_row_q8_k(x, xq[:4 * 292])
+        jkb.gemv_rows(outs.local_slice("b", slot), W3, xq[:4 * 292], range(0, 130))
+        outs.gather(slot)
+        assert jkb.device_status() == 0
+        ra, rb = torch.empty(300, device="cuda"), torch.empty(130, device="cuda")
+        jkb.vec_dot_grouped_rvv([(ra, W1)], x)
+        jkb.gemv_rows(rb, W3, xq[:4 * 292], range(0, 130))
+        assert np.array_equal(bits(host(outs.output("a", slot))), bits(host(ra)))
+        assert np.array_equal(bits(host(outs.output("b", slot))), bits(host(rb)))
+    outs.destroy()
+    # token batch: four tokens through gemv_batch into a pushing buffer
+    outs = PeerOutputs([("b", 130)], 1, 0, batch=4, push=True)
+    xb = dev(oracle.normal(4 * 1024, 31, 1.0))
+    jkb.quantize_rows_q8_k(xb, 4, 1024, xq)
+    jkb.gemv_batch(outs.local_slice("b", 0), W3, xq, 4)
+    outs.gather(0)
+    rb = torch.empty(4 * 130, device="cuda")
+    jkb.gemv_batch(rb, W3, xq, 4)
+    assert np.array_equal(bits(host(outs.output("b", 0))).reshape(-1), bits(host(rb)))
+    assert jkb.device_status() == 0
+    outs.destroy()
+
+
+def test_push_boundaries_fail_closed(jkb, oracle):
+    """An output range that crosses the edge of a pushing buffer is rejected before any launch;
+    the entry points that do not push (the repacked GEMM) refuse outputs inside one; with push
+    disabled again both work."""
+    w1, _ = _weights(oracle)
+    W1 = upload(jkb, Q4_K, w1, 300, 1024)
+    x = dev(oracle.normal(1024, 9, 1.0))
+    from jkb200 import _lib
+    from jkb200.api import _check
+
+    pg = jkb.PeerGroup(4 * 400, world=1, rank=0)
+    pg.set_push(True)
+    jkb.vec_dot_q4_k_m_rvv(pg.buffer[:300], W1, x)  # inside: fine
+    # 300 outputs starting 200 bytes before the buffer (in the group's own 256-byte header, so
+    # the range stays inside the allocation): rejected before any launch
+    lo = pg.buffer.data_ptr() - 200
+    with pytest.raises(jkb.TensorBoundsError, match="crosses the edge"):
+        _check(_lib.load().jkb_vec_dot_q4_k_m_rvv(lo, 300, W1.handle, x.data_ptr(), 1024, None))
+    raw = oracle.quantize_weights(8, oracle.normal(64 * 256, 4, 0.02), 64, 256)
+    rw = jkb.RepackedWeight.from_tensor(jkb.TensorView("w", 8, [64, 256], raw), 64, 256)
+    act = jkb.QuantizedActQ8.quantize(dev(oracle.normal(2 * 256, 5, 1.0)), 2, 256)
+    with pytest.raises(jkb.CapabilityMismatch, match="does not push"):
+        rw.gemm(pg.buffer[:128], act)
+    pg.set_push(False)
+    rw.gemm(pg.buffer[:128], act)
+    assert jkb.device_status() == 0
+    rw.destroy()
+    pg.destroy()
