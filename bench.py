@@ -1419,7 +1419,8 @@ def main():
     ap.add_argument("--kernel", choices=["q4_k", "q6_k", "q8_0", "gemm_q8_0", "gemm_q4_k",
                                          "gemm_q6_k", "gemm_nib_q4_k", "gemm_q4_1", "gemm_q5_1",
                                          "gemm_iq4_nl", "gemm_q2_k", "gemm_q3_k", "int8_peak",
-                                         "bitlinear_tc", "bitlinear", "bitlinear_i2s"],
+                                         "bitlinear_tc", "bitlinear", "bitlinear_i2s",
+                                         "per_shape"],
                     help="run one GEMV shape (profiling case) instead of the benchmark")
     ap.add_argument("--rows", type=int, default=65536)
     ap.add_argument("--cols", type=int, default=4096)
@@ -1438,6 +1439,12 @@ def main():
         run_bitlinear_case(args)
     elif args.kernel in ("bitlinear", "bitlinear_i2s"):
         run_bitlinear_gemv_case(args)
+    elif args.kernel == "per_shape":  # each group of the --workload decode set on its own
+        import torch
+        import jkb200 as jkb
+
+        torch.cuda.set_device(0)
+        print(json.dumps(run_decode_shapes(jkb, DECODE_SETS[args.workload], 1, 0)))
     elif args.kernel and args.kernel.startswith("gemm_"):
         run_gemm_case(args)
     elif args.kernel == "int8_peak":

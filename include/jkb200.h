@@ -254,7 +254,6 @@ int jkb_weight_upload_infer(const jkb_tensor_view *view, void *stream, jkb_weigh
 int jkb_weight_destroy(jkb_weight *w);
 int jkb_weight_info(const jkb_weight *w, size_t *rows, size_t *cols, int32_t *quant,
                     size_t *device_bytes, size_t *gguf_bytes);
-
 /* ---- direct-integer single-row block dots (raw GGUF row bytes on the device) ---- */
 /* quant_q8.rs:1463 vec_dot_q4_0_q8_0 -> *result (device f32) */
 int jkb_vec_dot_q4_0_q8_0(const uint8_t *w_blocks, size_t w_len, const jkb_block_q8_0 *x,

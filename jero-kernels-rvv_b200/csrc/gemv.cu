@@ -248,12 +248,16 @@ struct ActI8 {
                                      ((uint32_t)x[4 * i + 3] << 24);
         }
         __syncthreads();
+        // block totals, one warp per block (integer sums: exact in any order)
         int *tot_ = (int *)(s + a.K);
-        for (int b = threadIdx.x; b < a.K / BE; b += blockDim.x) {
+        const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+        for (int b = threadIdx.x >> 5; b < a.K / BE; b += nw) {
             const int *q = (const int *)(s + b * BE);
             int t = 0;
-            for (int w = 0; w < BE / 4; w++) t = __dp4a(q[w], 0x01010101, t);
-            tot_[b] = t;
+            for (int w = lane; w < BE / 4; w += 32) t = __dp4a(q[w], 0x01010101, t);
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1) t += __shfl_xor_sync(0xffffffffu, t, m);
+            if (lane == 0) tot_[b] = t;
         }
         __syncthreads();
     }
@@ -290,10 +294,20 @@ __device__ __forceinline__ void load_group(const float *x, bool vec, int e, floa
 // lanes the 16-element bsums, lane 0 the scale and the block total.
 // Every CTA of the cluster has started, so its shared memory may be written through the
 // cluster window. Only execution is ordered (nothing has been written yet), so the arrive is
-// relaxed: a release here would wait for the weight loads already in flight.
-__device__ __forceinline__ void cluster_started() {
-    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" :::
-                     "memory");
+// relaxed: a release here would wait for the weight loads already in flight. A CTA alone (C = 1)
+// writes only its own shared memory and needs no barrier here.
+__device__ __forceinline__ void cluster_started(unsigned C) {
+    if (C > 1)
+        asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" :::
+                         "memory");
+}
+// The staged activation is complete in every CTA of the cluster. A CTA alone takes the CTA
+// barrier, which (unlike the cluster barrier's release) does not wait for its weight loads.
+__device__ __forceinline__ void cluster_staged(cg::cluster_group &cl, unsigned C) {
+    if (C > 1)
+        cl.sync();
+    else
+        __syncthreads();
 }
 
 struct ActQ8KF32 : ActQ8K {
@@ -307,7 +321,7 @@ struct ActQ8KF32 : ActQ8K {
         const int K = a.K, nsb = K / 256;
         const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
         const int gw = (int)rank * nw + (threadIdx.x >> 5), gstride = (int)C * nw;
-        cluster_started();
+        cluster_started(C);
         // two superblocks per warp and round: both loads are issued before the arithmetic
         for (int sb0 = gw; sb0 < nsb; sb0 += 2 * gstride) {  // warp-uniform
             float vv[2][8];
@@ -361,7 +375,7 @@ struct ActQ8KF32 : ActQ8K {
                 }
             }
         }
-        cl.sync();
+        cluster_staged(cl, C);
     }
 };
 
@@ -378,7 +392,7 @@ struct ActQ80F32 : ActQ80 {
         const int K = a.K, nbk = K / 32, nunit = (nbk + 3) / 4;
         const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
         const int gw = (int)rank * nw + (threadIdx.x >> 5), gstride = (int)C * nw;
-        cluster_started();
+        cluster_started(C);
         const int sub = lane & 7;
         // two units per warp and round: both loads are issued before the arithmetic
         for (int u0 = gw; u0 < nunit; u0 += 2 * gstride) {  // warp-uniform
@@ -434,7 +448,7 @@ struct ActQ80F32 : ActQ80 {
                 }
             }
         }
-        cl.sync();
+        cluster_staged(cl, C);
     }
 };
 
@@ -1103,6 +1117,16 @@ __global__ void __launch_bounds__(MAX_WARPS * 32, (gemv_min_blocks<F, MODE>())) 
 // quantization units: larger clusters cut the repeated quantization of wide inputs and of
 // small CTAs, smaller ones pack the device better.
 constexpr unsigned GEMV_MAX_CLUSTER = 8;
+// JKB_GEMV_MAX_CLUSTER=1, 2 or 4 in the environment caps the cluster of the f32-input stagers
+// (for measuring the cluster-shared quantization against one per CTA); unset, up to 8.
+static unsigned max_cluster() {
+    static const unsigned c = [] {
+        const char *v = getenv("JKB_GEMV_MAX_CLUSTER");
+        const int n = v ? atoi(v) : 0;
+        return (n == 1 || n == 2 || n == 4) ? (unsigned)n : GEMV_MAX_CLUSTER;
+    }();
+    return c;
+}
 
 // Launch shape of one GEMV launch (plan_t) and the number of steps each warp walks with it.
 struct GemvPlan {
@@ -1154,7 +1178,7 @@ static GemvPlan plan_t(KArgs &a, size_t m) {
     unsigned C = 1;
     int cs = 0;
     if (S::kCluster)
-        while (C < GEMV_MAX_CLUSTER && S::units(a.K) > 2 * warps * (int)C) {
+        while (C < max_cluster() && S::units(a.K) > 2 * warps * (int)C) {
             C <<= 1;
             cs++;
         }

@@ -258,3 +258,4 @@ def test_gemv_batch16_70b_shapes(jkb, oracle, quant, rows, cols):
             ok, worst = R.gemv_tolerance_ok(got[t, r:r + 1], y_ref, v_ref, REL)
             assert ok, f"token {t} row {r}: worst {worst:.3g} of bound"
     w.destroy()
+
