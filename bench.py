@@ -378,7 +378,8 @@ class DecodeSet:
     never finds its weights in the L2."""
 
     def __init__(self, jkb, mats, acts, world, rank, *, peer=True, push=False, batch=1,
-                 layer_copies=1, prequant=("f",), unfused=False, seed=1000, sigma=0.02):
+                 layer_copies=1, prequant=("f",), unfused=False, seed=1000, sigma=0.02,
+                 tc=False):
         import torch
         from jkb200.shard import PeerOutputs, ShardedOutputs
 
@@ -387,6 +388,9 @@ class DecodeSet:
         self.peer = peer and world > 1
         self.push = push and self.peer
         self.unfused, self.prequant = unfused, set(prequant) - {""}
+        # token batches on the tensor cores: i8 RepackedWeights and one QuantizedActQ8 per
+        # activation stream (gemm_repacked) instead of GGUF-layout weights and gemv_batch
+        self.tc = tc and batch > 1
         names = [(name, rows) for name, _, rows, _, _ in mats]
         # two output slots alternate by step parity (a step's outputs stay readable while the
         # next step runs): the peer group's two slots, or two flat NCCL / single-GPU buffers
@@ -401,8 +405,9 @@ class DecodeSet:
             copies = 1 if name == "lm_head" else layer_copies
             for c in range(copies):
                 raw = synth_matrix(quant, rows, cols, seed + i + 97 * c, rr.start, rr.stop, sigma)
-                self.weights[(name, c)] = jkb.Weight(
-                    jkb.TensorView(f"{name}.{c}", quant, [len(rr), cols], raw), len(rr), cols)
+                view = jkb.TensorView(f"{name}.{c}", quant, [len(rr), cols], raw)
+                self.weights[(name, c)] = (jkb.RepackedWeight.from_tensor(view, len(rr), cols)
+                                           if self.tc else jkb.Weight(view, len(rr), cols))
             self.shards.append((name, quant, len(rr), cols, s, copies))
         g = torch.Generator(device="cpu").manual_seed(7)
         # all activation streams in one device buffer: the e2e loop moves a step's inputs with
@@ -416,7 +421,8 @@ class DecodeSet:
         for s, n in acts.items():
             for k in range(2):
                 self.xs_slots[k][s] = self.x_slots[k][off:off + batch * n]
-            self.xq[s] = jkb.empty_q8_k_blocks(batch * n // 256)
+            self.xq[s] = (jkb.QuantizedActQ8(batch, n) if self.tc
+                          else jkb.empty_q8_k_blocks(batch * n // 256))
             off += batch * n
         self.xs = self.xs_slots[0]
         self.groups = {}  # activation stream -> matrices fed by it, in mats order
@@ -443,7 +449,11 @@ class DecodeSet:
         jkb = self.jkb
         items = [(self.lslice(n, i), self.weights[(n, i % c)]) for n, c in self.groups[s]]
         xs = self.xs_slots[i % 2]
-        if self.batch > 1:
+        if self.tc:
+            self.xq[s].quantize_into(xs[s], self.batch, self.acts[s])
+            for out, w in items:
+                w.gemm(out, self.xq[s])
+        elif self.batch > 1:
             jkb.quantize_rows_q8_k(xs[s], self.batch, self.acts[s], self.xq[s])
             for out, w in items:
                 jkb.gemv_batch(out, w, self.xq[s], self.batch)
@@ -496,7 +506,13 @@ class DecodeSet:
 
         def group(s):
             items = [(self.lslice(n, k), self.weights[(n, k % c)]) for n, c in self.groups[s]]
-            if self.batch > 1:
+            if self.tc:
+                calls.append((L.jkb_act_q8_quantize, (self.xq[s]._h, xs[s].data_ptr(),
+                              xs[s].numel(), self.batch, self.acts[s], stream)))
+                for out, w in items:
+                    calls.append((L.jkb_gemm_repacked, (out.data_ptr(), out.numel(), w._h,
+                                  self.xq[s]._h, stream)))
+            elif self.batch > 1:
                 calls.append((L.jkb_quantize_rows_q8_k, (xs[s].data_ptr(), self.batch,
                               self.acts[s], self.xq[s].data_ptr(), self.xq[s].numel() // 292,
                               stream)))
@@ -557,6 +573,9 @@ class DecodeSet:
     def destroy(self):
         for w in self.weights.values():
             w.destroy()
+        if self.tc:
+            for a in self.xq.values():
+                a.destroy()
         if self.peer:
             self.outs.destroy()
 
@@ -742,12 +761,12 @@ def e2e_decode(ds, steps, warmup, world, stream):
             "d2h_bytes_per_step": out_bytes, "host_us_per_step": round(host_s / steps * 1e6, 2)}
 
 
-def decode_section(jkb, spec, world, rank, stream, steps, warmup, batch, peer, push):
+def decode_section(jkb, spec, world, rank, stream, steps, warmup, batch, peer, push, tc=False):
     """configs[4]-style numbers for one decode set and batch: GB/s of the whole job, the
     fraction of measured HBM per GPU, and the per-step split (max over ranks)."""
     mats, acts, copies, sigma = spec["mats"], spec["acts"], spec["copies"], spec["sigma"]
     ds = DecodeSet(jkb, mats, acts, world, rank, peer=peer, push=push, batch=batch,
-                   layer_copies=copies, sigma=sigma)
+                   layer_copies=copies, sigma=sigma, tc=tc)
     t = time_decode(ds, steps, warmup, stream, world)
     peak, _ = measured_peaks()
     gbs = ds.bytes_per_step / (t["ms_step"] * 1e-3) / 1e9
@@ -757,7 +776,10 @@ def decode_section(jkb, spec, world, rank, stream, steps, warmup, batch, peer, p
            "split_us": {"layer_gemvs": round(t["layer_ms"] * 1e3, 2),
                         "lm_head": round(t["lm_head_ms"] * 1e3, 2),
                         "gather": round(t["gather_ms"] * 1e3, 2)},
-           "launches_per_step": ds.launches_per_step}
+           "launches_per_step": ds.launches_per_step,
+           "weights": ("i8 RepackedWeight, gemm_repacked (tensor cores); GB/s counts the GGUF "
+                       "bytes of the same matrices" if ds.tc else
+                       "GGUF blocks, " + ("gemv_batch" if batch > 1 else "f32-input GEMV"))}
     ds.destroy()
     return res
 
@@ -807,6 +829,10 @@ def run_gpu(args):
                 sec["batch16"] = decode_section(jkb, sp, world, rank, stream,
                                                 max(4, args.steps // 4), args.warmup, 16, peer,
                                                 push)
+                # the same batch on the tensor cores: i8 RepackedWeights + gemm_repacked
+                sec["batch16_tc"] = decode_section(jkb, sp, world, rank, stream,
+                                                   max(4, args.steps // 4), args.warmup, 16,
+                                                   peer, push, tc=True)
         sections["q4_0_gemv_4096"] = run_q4_0_gemv(jkb, world)
         sections["per_shape_" + spec["key"]] = run_decode_shapes(jkb, spec, world, rank)
     prefill = None if args.no_gemm else run_prefill_gemm(world, rank)

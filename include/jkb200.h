@@ -119,8 +119,8 @@ void jkb_clear_error(void);
  * wait expired). Synchronizes `stream`, copies the word to *flags, clears it, and returns
  * JKB_E_TIMEOUT when it was non-zero, JKB_OK otherwise. */
 int jkb_device_status(int32_t *flags, void *stream);
-/* No reference counterpart: the f32 epilogue of the tensor-core repacked GEMM (32-element
- * scale groups, batches of at least 32 tokens). 0 (the default): acc = fma((f32)c, xs * ws, acc)
+/* No reference counterpart: the f32 epilogue of the tensor-core repacked GEMM (scale groups
+ * of 32 or 16 elements, batches of at least 16 tokens; Q2_K from 32). 0 (the default): acc = fma((f32)c, xs * ws, acc)
  * per group, within one rounding per group of the reference and far inside its 1e-5 relative
  * tolerance; the integer group sums c are exact either way. 1: the reference's separately
  * rounded product and sum (accumulate_scaled_tile_scalar, repack.rs:3045-3093), bit-identical

@@ -943,6 +943,8 @@ int choose_tile(size_t m, size_t sub_n, bool mins) {
 template <bool E, bool MN, bool H> using TC64 = TcCfg<64, 2, H ? 2 : 4, E, MN, H>;
 template <bool E, bool MN, bool H> using TC96 = TcCfg<96, 3, H ? 1 : 2, E, MN, H>;
 template <bool E, bool MN, bool H> using TC128 = TcCfg<128, 2, H ? 1 : 2, E, MN, H>;
+// Small batches (16 to 32 tokens): a 32-token tile with one epilogue warp per lane quarter.
+template <bool E, bool MN, bool H> using TC32 = TcCfg<32, 1, H ? 2 : 4, E, MN, H>;
 
 // The nibble GEMM's configurations: the repacked GEMM's three with two converter warps; with
 // IQ4_NL's four (14 warps and more leave 144 registers a thread or fewer) only the 64-token
@@ -955,8 +957,11 @@ template <bool E, int NB> using TN128 = TcCfg<128, 2, 2, E, NMINS<NB>, false, NB
 
 std::atomic<int> g_gemm_exact{0};
 
-// Smallest batch the tensor-core path takes (one 128-row MMA tile is mostly padding below it).
+// Smallest batch the tensor-core path takes (one 128-row MMA tile is mostly padding below it);
+// the repacked GEMM takes batches from TC_SMALL_M tokens on its 32-token tile (measured against
+// the dp4a token-batch kernels at 16 tokens on the Llama-3-70B shapes).
 constexpr size_t TC_MIN_M = 32;
+constexpr size_t TC_SMALL_M = 16;
 
 // 16-element groups with min terms (Q2_K): the 64-token tile at one group a round, the only
 // configuration that keeps its scales, mins and token sums in registers without spilling.
@@ -969,6 +974,8 @@ int launch_tc_bn(int bn, const jkb_repacked_weight *w, const jkb_act_q8 *act, fl
         return launch_tc<TC64_H16_MINS<EXACT>>(w, act, out, row_begin, row_end, st, err);
     } else {
         switch (bn) {
+            case 32:
+                return launch_tc<TC32<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
             case 64:
                 return launch_tc<TC64<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
             case 128:
@@ -986,7 +993,9 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
     const size_t kp = w->k_pad;
     const bool mins = w->mins != nullptr, h16 = w->group_elems == 16;
     const float *xn = h16 ? act->x_nsums16_t : act->x_nsums_t;  // min terms' token sums
-    if ((w->group_elems != 32 && !h16) || kp % BK != 0 || act->m < TC_MIN_M ||
+    // the 16-element groups with min terms (Q2_K) have only the 64-token tile
+    const size_t min_m = (h16 && mins) ? TC_MIN_M : TC_SMALL_M;
+    if ((w->group_elems != 32 && !h16) || kp % BK != 0 || act->m < min_m ||
         act->k_pad != kp ||
         act->m > (size_t)INT32_MAX || w->rows > (size_t)INT32_MAX || act->x_scales_t == nullptr ||
         (mins && xn == nullptr))
@@ -998,7 +1007,7 @@ int gemm_tc_launch(const jkb_repacked_weight *w, const jkb_act_q8 *act, float *o
     int *err = device_error_word();
     if (!err) return JKB_OK;
     *used = true;
-    const int bn = choose_tile(act->m, row_end - row_begin, mins || h16);
+    const int bn = act->m <= 32 ? 32 : choose_tile(act->m, row_end - row_begin, mins || h16);
     const bool exact = g_gemm_exact.load(std::memory_order_relaxed);
     if (h16 && mins)  // Q2_K: 16-element groups with min terms
         return exact ? launch_tc_bn<true, true, true>(bn, w, act, out, row_begin, row_end, st, err)

@@ -248,16 +248,12 @@ struct ActI8 {
                                      ((uint32_t)x[4 * i + 3] << 24);
         }
         __syncthreads();
-        // block totals, one warp per block (integer sums: exact in any order)
         int *tot_ = (int *)(s + a.K);
-        const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-        for (int b = threadIdx.x >> 5; b < a.K / BE; b += nw) {
+        for (int b = threadIdx.x; b < a.K / BE; b += blockDim.x) {
             const int *q = (const int *)(s + b * BE);
             int t = 0;
-            for (int w = lane; w < BE / 4; w += 32) t = __dp4a(q[w], 0x01010101, t);
-#pragma unroll
-            for (int m = 16; m > 0; m >>= 1) t += __shfl_xor_sync(0xffffffffu, t, m);
-            if (lane == 0) tot_[b] = t;
+            for (int w = 0; w < BE / 4; w++) t = __dp4a(q[w], 0x01010101, t);
+            tot_[b] = t;
         }
         __syncthreads();
     }

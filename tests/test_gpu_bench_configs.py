@@ -8,7 +8,8 @@ with (BASELINE configs[0] to configs[4]).
   and last eight, the rest seeded) against the oracle GEMV within the row tolerance, and the
   lm_head's Q8_K input bit for bit.
 * configs[4], the Llama-3-70B set at batch 1 (f32-input launches) and batch 16
-  (quantize_rows_q8_k + gemv_batch), sampled rows of every token against the oracle; and its
+  (quantize_rows_q8_k + gemv_batch; and on the tensor cores, QuantizedActQ8 + gemm_repacked),
+  sampled rows of every token against the oracle; and its
   row sharding over 8 ranks emulated on one GPU: each rank's slice uploaded on its own, the
   stitched outputs equal to the single-GPU call bit for bit (the multi-GPU run is in
   test_gpu_multigpu.py).
@@ -29,7 +30,7 @@ import pytest
 import torch
 
 import refgen as R
-from gpuutil import assert_gemm_close, bits, dev, host
+from gpuutil import assert_gemm_close, bits, dev, gemm_abs_bound, host
 
 pytestmark = pytest.mark.gpu
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -89,6 +90,34 @@ def test_decode_70b_step_matches_oracle(jkb, oracle, batch):
     """configs[4] at its full size on one GPU, batch 1 (f32-input grouped launches) and batch 16
     (gemv_batch)."""
     _decode_parity(jkb, oracle, "70b", batch, 1)
+
+
+def test_decode_70b_batch16_tensor_cores_match_oracle(jkb, oracle):
+    """configs[4] at batch 16 on the tensor cores (the bench's batch16_tc section): i8
+    RepackedWeights, the 16 tokens quantized by QuantizedActQ8 and one gemm_repacked per matrix
+    on the 32-token tile. Three 32-row ranges per matrix (first, middle, last) for every token
+    against oracle.gemm_repacked within the GEMM tolerance (repack.rs:3045-3093 semantics)."""
+    spec = bench.DECODE_SETS["70b"]
+    batch = 16
+    ds = bench.DecodeSet(jkb, spec["mats"], spec["acts"], 1, 0, peer=False, batch=batch,
+                         layer_copies=spec["copies"], sigma=spec["sigma"], tc=True)
+    xs = {s: ds.xs[s].cpu().numpy() for s in spec["acts"]}
+    ds.step(0)
+    torch.cuda.synchronize()
+    assert jkb.device_status() == 0
+    for j, (name, quant, rows, cols, s) in enumerate(spec["mats"]):
+        raw = bench.synth_matrix(quant, rows, cols, 1000 + j, sigma=spec["sigma"])
+        row_bytes = raw.size // rows
+        got = host(ds.output(name, 0)).reshape(batch, rows)
+        for r0 in (0, rows // 2 - 16, rows - 32):
+            sub = raw[r0 * row_bytes:(r0 + 32) * row_bytes]
+            q, sc, mn = oracle.repack_block_scaled(quant, sub, 32, cols)
+            xq, xsc, xsum, xs16, _ = oracle.act_q8_quantize(xs[s], batch, cols)
+            ref = oracle.gemm_repacked(quant, q, sc, mn, 32, cols, xq, xsc, xsum, xs16, batch,
+                                       nthreads=os.cpu_count() or 8)
+            bound = gemm_abs_bound(oracle, quant, sub, 32, cols, xs[s], batch)
+            assert_gemm_close(got[:, r0:r0 + 32], ref, bound)
+    ds.destroy()
 
 
 @pytest.mark.parametrize("name", ["ffn_gate", "ffn_down", "lm_head"])

@@ -1,6 +1,6 @@
 """The tcgen05 tensor-core path of the repacked GEMM (32-element scale groups: Q8_0, Q4_0,
 TQ2_0, I2_S and Q4_K_M weights, the last with their min terms; 16-element groups: Q6_K;
-batches of at least 32 tokens;
+batches of at least 16 tokens, 16 to 32 of them on the 32-token tile;
 K a multiple of 128) vs the CPU oracle. Every output accumulates its groups in K order as
 accumulate_scaled_tile_scalar does (repack.rs:3045-3093), acc += (f32)c * (xs * ws)
 [- x_sum * wm]:
@@ -12,7 +12,8 @@ accumulate_scaled_tile_scalar does (repack.rs:3045-3093), acc += (f32)c * (xs * 
 
 Shapes cover one tile (32 x 128 x 128: one K stage, a partial token tile), ragged token and
 weight-row tiles, K = 14336 (448 groups), a row range that starts inside a tile, batches that
-select each of the three tile widths (64, 96, 128 tokens), and every format the path takes.
+select each of the four tile widths (32, 64, 96, 128 tokens; the 32-token one with 16 and 24
+tokens, half or a quarter of it padding), and every format the path takes.
 The device error word (bounded waits inside the kernel) must stay clear."""
 import numpy as np
 import pytest
@@ -56,6 +57,11 @@ SHAPES = [
     (36, 40, 384, 2560),    # I2_S (per-tensor scale)
     (6, 200, 300, 4096),    # Q5_0
     (13, 200, 300, 4096),   # Q5_K (min terms)
+    (8, 16, 300, 4096),     # 16 tokens: the 32-token tile, half of it padding
+    (8, 24, 1100, 512),     # 24 tokens, 9 weight tiles
+    (12, 16, 300, 4096),    # Q4_K_M, 16 tokens
+    (14, 16, 300, 4096),    # Q6_K, 16 tokens
+    (12, 16, 28672, 256),   # Q4_K_M, 16 tokens over 224 weight tiles (two waves)
 ]
 
 
