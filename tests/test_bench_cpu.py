@@ -55,4 +55,15 @@ def test_reference_arm_prints_one_json_line():
     assert d["e2e"]["h2d_bytes_per_step"] == 0
     assert d["cpu_baseline"]["cpu_model"]
     # the same config dict the GPU arm prints at N=1
-    assert d["config"] == bench.decode_config(bench.DECODE_SETS["8b"], 1, True)
+    assert d["config"] == bench.decode_config(bench.DECODE_SETS["8b"], 1, "peer")
+
+
+def test_decode_config_names_the_collective():
+    """N > 1: the config line says how the output shards are collected (the driver's scaling
+    runs use the default, the one-kernel all-gather)."""
+    sp = bench.DECODE_SETS["8b"]
+    par = {c: bench.decode_config(sp, 2, c)["parallelism"] for c in ("peer", "push", "nccl")}
+    assert par["peer"] == "row-shard x2 + one-kernel all-gather over NVLink peer memory"
+    assert "pushed to the peers by the GEMVs" in par["push"]
+    assert par["nccl"].endswith("NCCL all-gather")
+    assert bench.decode_config(sp, 1, "push")["parallelism"] == "row-shard x1"
