@@ -46,6 +46,7 @@ def _weights(oracle, quant, rows, cols, seed):
     (14, 384, 2048, 64),    # tensor cores, 16-element groups
     (10, 384, 2048, 64),    # Q2_K: the dp4a kernel on this entry point
     (8, 96, 2048, 9),       # a small batch: the dp4a kernel
+    (12, 384, 2048, 16),    # 16 tokens: the tensor cores' 32-token tile
     (8, 40, 163840, 4),     # K too long for the transposed planes (they are not written)
 ])
 def test_noalloc_matches_allocating_entry_point_twice(jkb, oracle, quant, rows, cols, m):
