@@ -1124,6 +1124,23 @@ static unsigned max_cluster() {
     return c;
 }
 
+// Smallest CTA (in warps) the launcher shrinks to for small matrices. Every CTA stages the
+// whole activation (or, with f32 input, its cluster quantizes it), so small CTAs leave each
+// thread several staging copies or quantization rounds: launches keep 8-warp CTAs even when
+// fewer CTAs than SMs result (measured, Q4_K_M, 2-warp floor -> 8: f32 input 512 x 14336
+// 6.91 -> 4.53 us, 512 x 4096 3.76 -> 3.20 us, 1024 x 14336 5.74 -> 5.22 us; pre-quantized
+// 512 x 14336 9.26 -> 5.03 us, 1024 x 4096 4.22 -> 3.01 us; 2048 rows and up unchanged).
+// JKB_GEMV_MIN_WARPS=2 or 4 in the environment lets the launcher shrink CTAs that far when a
+// matrix has fewer rows than the SMs' 8-warp CTAs take (for measuring the launch shapes).
+static int min_warps() {
+    static const int w = [] {
+        const char *v = getenv("JKB_GEMV_MIN_WARPS");
+        const int n = v ? atoi(v) : 0;
+        return (n == 2 || n == 4) ? n : 8;
+    }();
+    return w;
+}
+
 // Launch shape of one GEMV launch (plan_t) and the number of steps each warp walks with it.
 struct GemvPlan {
     int warps;
@@ -1166,9 +1183,10 @@ static GemvPlan plan_t(KArgs &a, size_t m) {
     const int rpw = 32 >> a.lpr_shift;
     const size_t rows = a.row_end - a.row_begin;
     const size_t sms = (size_t)num_sms();
-    // Fewer warps per CTA when the matrix is small, so that every SM gets work.
+    // Fewer warps per CTA when the matrix is small, down to min_warps() (8 unless set).
     int warps = MAX_WARPS;
-    while (warps > 2 && m * ((rows + (size_t)warps * rpw - 1) / ((size_t)warps * rpw)) < sms)
+    while (warps > min_warps() &&
+           m * ((rows + (size_t)warps * rpw - 1) / ((size_t)warps * rpw)) < sms)
         warps >>= 1;
     const int slot = warps == 8 ? 0 : warps == 4 ? 1 : 2;
     unsigned C = 1;

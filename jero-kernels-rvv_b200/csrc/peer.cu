@@ -1,18 +1,22 @@
 // Peer groups: a one-kernel all-gather of output-row shards over NVLink.
 //
 // One process per GPU. Each rank's group owns one cudaMalloc allocation:
-//   [0, 8)      arrival counter (u64): signals received from peers, one per peer and call
-//   [8, 16)     expected count (u64): advanced by each wait
-//   [16, 24)    CTA counter (u64) of this rank's all-gather launches
+//   [0, 8)      arrival counter (u64): call signals received from peers, one per peer and call
+//   [8, 16)     expected count (u64) of the arrival counter, advanced by each wait
+//   [16, 24)    expected CTA signals per peer (u64), advanced by each all-gather or signal call
+//   [64, 128)   CTA arrival counters (u64 per rank): entry p counts the CTA signals from rank p
 //   [256, ...)  the output buffer handed to callers (`bytes` long), identical layout on every rank
 // The ranks exchange CUDA IPC handles of these allocations and map each other's. The all-gather
-// kernel (a fixed grid of AG_CTAS CTAs on every rank) copies this rank's chunks of the buffer to
-// the same offsets in every peer's buffer with coalesced 16-byte stores over NVLink (plain
-// stores; no multicast). Each CTA then passes a CTA barrier, fences at system scope and counts
-// itself; the last CTA of the launch adds 1 to every peer's arrival counter with release
-// semantics, advances this rank's expected count by world - 1 and spins, with an acquire load
-// and a 2 s bound, until the arrivals reach it. The counts live on the device, so a captured
-// CUDA graph stays correct across replays.
+// kernel copies this rank's chunks of the buffer to the same offsets in every peer's buffer with
+// coalesced 16-byte stores over NVLink (plain stores; no multicast). Its CTA count follows the
+// buffer size and the world size, so every rank launches the same grid. Each CTA then passes a
+// CTA barrier, fences at system scope once and adds 1 to its own entry of every peer's CTA
+// arrival counters (a release pattern: the fence, then relaxed adds); CTA 0 also adds 1 to
+// every peer's arrival counter (the call's signal). CTA 0 then spins, with acquire loads and a
+// 2 s bound, until every peer's entry has counted this call's CTAs and the call signals have
+// arrived. Per-peer entries keep a fast peer's signals of the next call from standing in for a
+// slow peer's signals of this one. The counts live on the device, so a captured CUDA graph
+// stays correct across replays.
 //
 // Pushing groups: with push enabled, the GEMV kernels whose outputs lie in the group's buffer
 // store every output element to the same offset in each peer's buffer as well (4-byte stores
@@ -42,7 +46,7 @@ namespace jkb {
 constexpr uint32_t PEER_MAGIC = 0x4A4B5031u;  // "JKP1"
 constexpr size_t PEER_HDR = 256;              // counters and padding
 constexpr unsigned long long PEER_WAIT_NS = 2000000000ull;
-constexpr int AG_CTAS = 128;                  // CTAs of every rank's all-gather launch
+constexpr int AG_CTAS = 128;                  // most CTAs of an all-gather launch
 constexpr int AG_THREADS = 256;
 constexpr int AG_VEC = 4;                     // 16-byte loads in flight per thread
 
@@ -110,8 +114,9 @@ struct AgArgs {
     unsigned long long w4[6 * JKB_PEER_MAX_CHUNKS];        // byte offsets of 4-byte words
     uint8_t *data[JKB_PEER_MAX_RANKS];                 // every rank's buffer (data region)
     unsigned long long *cnt[JKB_PEER_MAX_RANKS];       // every rank's arrival counter
+    unsigned long long *ccnt[JKB_PEER_MAX_RANKS];      // every rank's CTA arrival counters
     unsigned long long *expected;                      // this rank's expected count
-    unsigned long long *done;                          // this rank's CTA counter of launches
+    unsigned long long *cexpected;                     // this rank's expected CTA signals
     unsigned long long arrivals;                       // added to it by this launch's wait
     int *err;
 };
@@ -136,6 +141,34 @@ __device__ void bounded_arrival_wait(unsigned long long *cnt, unsigned long long
             }
         }
         __nanosleep(64);
+    }
+}
+
+// Spins (thread 0 of the calling CTA) until every peer's entry of this rank's CTA arrival
+// counters reaches *cexpected + add (which it stores back); bounded by PEER_WAIT_NS in total.
+__device__ void bounded_cta_wait(const unsigned long long *entries, int world, int rank,
+                                 unsigned long long *cexpected, unsigned long long add, int *err) {
+    const unsigned long long target = *cexpected + add;
+    *cexpected = target;
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (int p = 0; p < world; p++) {
+        if (p == rank) continue;
+        for (uint32_t i = 0;; i++) {
+            unsigned long long v;
+            asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(entries + p)
+                         : "memory");
+            if (v >= target) break;
+            if ((i & 63) == 63) {
+                unsigned long long t;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                if (t - t0 > PEER_WAIT_NS) {
+                    atomicOr(err, 2);
+                    return;
+                }
+            }
+            __nanosleep(64);
+        }
     }
 }
 
@@ -178,29 +211,23 @@ __global__ void __launch_bounds__(AG_THREADS) peer_allgather_kernel(AgArgs a) {
             if (p != a.rank) *reinterpret_cast<uint32_t *>(a.data[p] + o) = v;
     }
     // The CTA barrier orders every thread's stores before thread 0's system-scope fence, which
-    // is cumulative over them. The CTAs then count themselves on this rank's launch counter;
-    // the last one (whose acquire-release add follows every other CTA's fence) fences again,
-    // signals each peer once with a release and waits for the peers' signals. A one-CTA launch
-    // (jkb_peer_group_signal) is its own last CTA and leaves the counter alone, so the counter
-    // stays a multiple of AG_CTAS between all-gather launches.
+    // is cumulative over them; the fence followed by each relaxed add is a release pattern for
+    // the peer that reads the count. (A release add per peer would fence before each add, and
+    // each fence waits for the previous add's NVLink round trip: with release adds from one CTA
+    // the step's collection grew by about 2 us per added peer.)
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence_system();
-        bool last = gridDim.x == 1;
-        if (!last) {
-            unsigned long long old;
-            asm volatile("atom.add.acq_rel.gpu.global.u64 %0, [%1], 1;"
-                         : "=l"(old)
-                         : "l"(a.done)
-                         : "memory");
-            last = (old + 1) % gridDim.x == 0;
-        }
-        if (last) {
-            __threadfence_system();
+        for (int p = 0; p < a.world; p++)
+            if (p != a.rank)
+                asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(a.ccnt[p] + a.rank)
+                             : "memory");
+        if (blockIdx.x == 0) {
             for (int p = 0; p < a.world; p++)
                 if (p != a.rank)
-                    asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(a.cnt[p])
+                    asm volatile("red.relaxed.sys.global.add.u64 [%0], 1;" ::"l"(a.cnt[p])
                                  : "memory");
+            bounded_cta_wait(a.ccnt[a.rank], a.world, a.rank, a.cexpected, gridDim.x, a.err);
             bounded_arrival_wait(a.cnt[a.rank], a.expected, a.arrivals, a.err);
         }
     }
@@ -216,6 +243,18 @@ __global__ void peer_wait_kernel(unsigned long long *cnt, unsigned long long *ex
 
 using namespace jkb;
 
+// CTAs of an all-gather launch: enough for one pass over a rank's share of the whole buffer
+// (AG_VEC words a thread), 8 to AG_CTAS. It depends only on the buffer size and the world size,
+// so every rank launches the same grid and expects as many CTA signals as it sends.
+static int ag_ctas(const jkb_peer_group *pg) {
+    const size_t words = pg->bytes / 16 / (size_t)pg->world;
+    const size_t per_cta = (size_t)AG_THREADS * AG_VEC;
+    size_t n = (words + per_cta - 1) / per_cta;
+    if (n < 8) n = 8;
+    if (n > (size_t)AG_CTAS) n = AG_CTAS;
+    return (int)n;
+}
+
 // The all-gather kernel on `ctas` CTAs, each of which signals every peer once after its share
 // of a's chunks (none for jkb_peer_group_signal).
 static int launch_allgather(jkb_peer_group *pg, AgArgs &a, int ctas, void *stream,
@@ -229,10 +268,11 @@ static int launch_allgather(jkb_peer_group *pg, AgArgs &a, int ctas, void *strea
     for (int p = 0; p < pg->world; p++) {
         a.data[p] = pg->peer_base[p] + PEER_HDR;
         a.cnt[p] = reinterpret_cast<unsigned long long *>(pg->peer_base[p]);
+        a.ccnt[p] = reinterpret_cast<unsigned long long *>(pg->peer_base[p]) + 8;
     }
     a.expected = reinterpret_cast<unsigned long long *>(pg->base) + 1;
-    a.done = reinterpret_cast<unsigned long long *>(pg->base) + 2;
-    a.arrivals = (unsigned long long)(pg->world - 1);  // one signal from each peer
+    a.cexpected = reinterpret_cast<unsigned long long *>(pg->base) + 2;
+    a.arrivals = (unsigned long long)(pg->world - 1);  // one call signal from each peer
     a.err = err;
     const cudaError_t le =
         launch_pdl(peer_allgather_kernel, dim3(ctas), dim3(AG_THREADS), 0, as_stream(stream), a);
@@ -341,7 +381,7 @@ int jkb_peer_group_allgather(jkb_peer_group *pg, const size_t *offset, const siz
         a.body_pre[i + 1] = a.body_pre[i] + (body >> 4);
     }
     if (pg->world == 1) return JKB_OK;  // every chunk is already in place
-    return launch_allgather(pg, a, AG_CTAS, stream, fn);
+    return launch_allgather(pg, a, ag_ctas(pg), stream, fn);
 }
 
 int jkb_peer_group_set_push(jkb_peer_group *pg, int enable) {
