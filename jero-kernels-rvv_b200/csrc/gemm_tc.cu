@@ -47,6 +47,7 @@
 
 #include <atomic>
 #include <cstdio>
+#include <cstdlib>
 
 #include "jkb_internal.h"
 #include "nibble.cuh"
@@ -61,9 +62,12 @@ constexpr int GPS = 4;    // scale groups per stage
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // bounded waits: 2 s
 
 template <int BN_, int WPQ_, int GPR_, bool EXACT_, bool MINS_ = false, bool H16_ = false,
-          int NIB_ = NIB_NONE, int AB_ = 1>
+          int NIB_ = NIB_NONE, int AB_ = 1, int CTAS_ = 1>
 struct TcCfg {
     static constexpr int BN = BN_, WPQ = WPQ_, GPR = GPR_;
+    // CTAS: resident CTAs per SM. Two halve each CTA's TMEM and shared memory so that an SM runs
+    // two tiles' pipelines and twice the epilogue warps at once.
+    static constexpr int CTAS = CTAS_;
     static constexpr bool EXACT = EXACT_;
     // MINS: groups carry a min term (Q4_K_M, Q4_1): acc += c * (xs * ws) - x_sum * wm
     static constexpr bool MINS = MINS_;
@@ -103,7 +107,7 @@ struct TcCfg {
     static constexpr int EPI = 4 * WPQ;    // epilogue warps
     static constexpr int THREADS = (2 + EPI + (H16 ? 1 : 0) + CONV) * 32;
     // TMEM: two round buffers of GPR group accumulators (BN int32 columns each)
-    static constexpr int TMEM_COLS = 512;
+    static constexpr int TMEM_COLS = 512 / CTAS_;
     static constexpr int SA = BMW * BK, SB = BN * BK;  // operand bytes per stage
     static constexpr int SAN = NIB ? BMW * BK / 2 : 0;  // 4-bit weight tile bytes per stage
     static constexpr int SMT = NIB ? BMW * 16 : 0;       // scale words: 16 bytes per row
@@ -114,7 +118,7 @@ struct TcCfg {
             : SA + SB + BMW * NG * 4 + GPS * BN * 4 + (MINS ? BMW * NG * 4 + NG * BN * 4 : 0);
     static constexpr int STAGE_SMEM =
         STAGE_TX + (H16 ? 2 * SB : 0) + (NIB ? SA + BMW * NG * 4 + (MINS ? BMW * GPS * 4 : 0) : 0);
-    static constexpr int STAGES_FIT = ((NEG8 ? 184 : 200) * 1024) / STAGE_SMEM;
+    static constexpr int STAGES_FIT = ((NEG8 ? 184 : 200) * 1024) / CTAS_ / STAGE_SMEM;
     // BitLinear blocks run on small batches, where a CTA's time is its stages' load latency:
     // they keep up to eight stages in flight, the block-scaled GEMM six
     static constexpr int STAGES_MAX = AB_ > 1 ? 8 : 6;
@@ -389,7 +393,7 @@ __device__ __forceinline__ void nib_convert(TcSmem<C> &sm, int s, int ks, int e)
 }
 
 template <class C>
-__global__ void __launch_bounds__(C::THREADS, 1)
+__global__ void __launch_bounds__(C::THREADS, C::CTAS)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    const __grid_constant__ CUtensorMap tmWS, const __grid_constant__ CUtensorMap tmXS,
                    const __grid_constant__ CUtensorMap tmWM, const __grid_constant__ CUtensorMap tmXN,
@@ -863,7 +867,8 @@ int launch_tc_common(const TcWeight &wt, const jkb_act_q8 *act, float *out, size
         if (e != cudaSuccess) return fail_cuda(e, "gemm_repacked (tensor-core kernel attribute)");
         attr_set[dev] = true;
     }
-    const size_t grid = ntiles < (size_t)num_sms() ? ntiles : (size_t)num_sms();
+    const size_t slots = (size_t)num_sms() * C::CTAS;
+    const size_t grid = ntiles < slots ? ntiles : slots;
     gemm_tc_kernel<C><<<(unsigned)grid, C::THREADS, smem, st>>>(
         wt.tmW, tmX, wt.tmWS, tmXS, wt.tmWM, tmXN, (int)act->m, (int)G, (int)row_begin,
         (int)sub_n, tiles_w, tiles_t, out, err);
@@ -945,6 +950,23 @@ template <bool E, bool MN, bool H> using TC96 = TcCfg<96, 3, H ? 1 : 2, E, MN, H
 template <bool E, bool MN, bool H> using TC128 = TcCfg<128, 2, H ? 1 : 2, E, MN, H>;
 // Small batches (16 to 32 tokens): a 32-token tile with one epilogue warp per lane quarter.
 template <bool E, bool MN, bool H> using TC32 = TcCfg<32, 1, H ? 2 : 4, E, MN, H>;
+// The same tile at two CTAs per SM (256 TMEM columns and half the stages each), for launches
+// with more tiles than SMs: an SM then runs two tiles' pipelines and twice the epilogue warps
+// at once. Measured at 16 tokens (FMA epilogue): 28672 x 8192 Q4_K_M 98.2 -> 82.9 us, Q8_0
+// 80.9 -> 58.1 us. With fewer tiles than SMs the halved stages only slow each tile (8192 x
+// 28672 Q4_K_M, 64 tiles: 162.5 -> 188.0 us), so those keep one CTA per SM. Not for 16-element
+// groups, whose masking warp leaves two CTAs too few registers (they spill).
+template <bool E, bool MN>
+using TC32X2 = TcCfg<32, 1, 4, E, MN, false, NIB_NONE, 1, 2>;
+// JKB_GEMM_SMALL2=0 or 1 in the environment forces the 32-token tile to one or two CTAs per SM
+// (for measuring one against the other); unset, the tile count decides.
+static int small_two_cta() {
+    static const int v = [] {
+        const char *e = getenv("JKB_GEMM_SMALL2");
+        return (e && (e[0] == '0' || e[0] == '1') && e[1] == 0) ? e[0] - '0' : -1;
+    }();
+    return v;
+}
 
 // The nibble GEMM's configurations: the repacked GEMM's three with two converter warps; with
 // IQ4_NL's four (14 warps and more leave 144 registers a thread or fewer) only the 64-token
@@ -975,6 +997,14 @@ int launch_tc_bn(int bn, const jkb_repacked_weight *w, const jkb_act_q8 *act, fl
     } else {
         switch (bn) {
             case 32:
+                if constexpr (!H16) {
+                    const size_t tiles = (row_end - row_begin + BMW - 1) / BMW *
+                                         ((act->m + 31) / 32);
+                    const int forced = small_two_cta();
+                    if (forced == 1 || (forced < 0 && tiles > (size_t)num_sms()))
+                        return launch_tc<TC32X2<EXACT, MINS>>(w, act, out, row_begin, row_end,
+                                                              st, err);
+                }
                 return launch_tc<TC32<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
             case 64:
                 return launch_tc<TC64<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
