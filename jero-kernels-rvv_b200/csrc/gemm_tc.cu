@@ -953,11 +953,14 @@ template <bool E, bool MN, bool H> using TC32 = TcCfg<32, 1, H ? 2 : 4, E, MN, H
 // The same tile at two CTAs per SM (256 TMEM columns and half the stages each), for launches
 // with more tiles than SMs: an SM then runs two tiles' pipelines and twice the epilogue warps
 // at once. Measured at 16 tokens (FMA epilogue): 28672 x 8192 Q4_K_M 98.2 -> 82.9 us, Q8_0
-// 80.9 -> 58.1 us. With fewer tiles than SMs the halved stages only slow each tile (8192 x
-// 28672 Q4_K_M, 64 tiles: 162.5 -> 188.0 us), so those keep one CTA per SM. Not for 16-element
-// groups, whose masking warp leaves two CTAs too few registers (they spill).
+// 80.9 -> 58.1 us; 128256 x 8192 Q6_K (16-element groups, one group a round so that the
+// masking warp's CTA fits two to an SM) 539.8 -> 421.5 us. With fewer tiles than SMs the halved
+// stages only slow each tile (8192 x 28672 Q4_K_M, 64 tiles: 162.5 -> 188.0 us), so those keep
+// one CTA per SM.
 template <bool E, bool MN>
 using TC32X2 = TcCfg<32, 1, 4, E, MN, false, NIB_NONE, 1, 2>;
+template <bool E, bool MN>
+using TC32X2H = TcCfg<32, 1, 1, E, MN, true, NIB_NONE, 1, 2>;
 // JKB_GEMM_SMALL2=0 or 1 in the environment forces the 32-token tile to one or two CTAs per SM
 // (for measuring one against the other); unset, the tile count decides.
 static int small_two_cta() {
@@ -997,13 +1000,18 @@ int launch_tc_bn(int bn, const jkb_repacked_weight *w, const jkb_act_q8 *act, fl
     } else {
         switch (bn) {
             case 32:
-                if constexpr (!H16) {
+                {
                     const size_t tiles = (row_end - row_begin + BMW - 1) / BMW *
                                          ((act->m + 31) / 32);
                     const int forced = small_two_cta();
-                    if (forced == 1 || (forced < 0 && tiles > (size_t)num_sms()))
-                        return launch_tc<TC32X2<EXACT, MINS>>(w, act, out, row_begin, row_end,
-                                                              st, err);
+                    if (forced == 1 || (forced < 0 && tiles > (size_t)num_sms())) {
+                        if constexpr (H16)
+                            return launch_tc<TC32X2H<EXACT, MINS>>(w, act, out, row_begin,
+                                                                   row_end, st, err);
+                        else
+                            return launch_tc<TC32X2<EXACT, MINS>>(w, act, out, row_begin,
+                                                                  row_end, st, err);
+                    }
                 }
                 return launch_tc<TC32<EXACT, MINS, H16>>(w, act, out, row_begin, row_end, st, err);
             case 64:

@@ -1141,6 +1141,20 @@ static int min_warps() {
     return w;
 }
 
+// Smallest cluster of the f32-input stagers: 2, so that even inputs one CTA's warps quantize in
+// one round are quantized once per CTA pair (measured on the Llama-3-8B decode shapes, K = 4096:
+// q/k/v 6.35 -> 5.94 us, o 4.55 -> 4.20 us, gate/up 14.77 -> 14.50 us; clusters of at least 4
+// made gate/up slower, 18.6 us). JKB_GEMV_MIN_CLUSTER=1, 2 or 4 in the environment sets it (for
+// measuring).
+static unsigned min_cluster() {
+    static const unsigned c = [] {
+        const char *v = getenv("JKB_GEMV_MIN_CLUSTER");
+        const int n = v ? atoi(v) : 0;
+        return (n == 1 || n == 2 || n == 4) ? (unsigned)n : 2u;
+    }();
+    return c;
+}
+
 // Launch shape of one GEMV launch (plan_t) and the number of steps each warp walks with it.
 struct GemvPlan {
     int warps;
@@ -1192,7 +1206,8 @@ static GemvPlan plan_t(KArgs &a, size_t m) {
     unsigned C = 1;
     int cs = 0;
     if (S::kCluster)
-        while (C < max_cluster() && S::units(a.K) > 2 * warps * (int)C) {
+        while (C < max_cluster() &&
+               (S::units(a.K) > 2 * warps * (int)C || C < min_cluster())) {
             C <<= 1;
             cs++;
         }
