@@ -123,7 +123,14 @@ struct TcCfg {
     // they keep up to eight stages in flight, the block-scaled GEMM six
     static constexpr int STAGES_MAX = AB_ > 1 ? 8 : 6;
     static constexpr int STAGES = STAGES_FIT > STAGES_MAX ? STAGES_MAX : STAGES_FIT;
+    // KSPLIT_MAX: the most CTAs (a cluster) that may share one tile by splitting its K stages,
+    // for launches with few tiles. The 32-token tile of the FMA epilogue only: its accumulators
+    // (16 KB a CTA) fit beside the stages for the partial sums' exchange, and the exact
+    // epilogue's single sequential sum per output cannot be split.
+    static constexpr int KSPLIT_MAX =
+        (BN == 32 && CTAS_ == 1 && !EXACT_ && !H16_ && NIB_ == NIB_NONE && AB_ == 1) ? 4 : 1;
     static_assert((COLS == 32 || COLS == 64) && BN % 32 == 0 && BN <= 256, "tile shape");
+    static_assert(KSPLIT_MAX == 1 || COLS == 32, "K split: one 32-token column block a thread");
     static_assert(GPS % GPR == 0 && 2 * NA * BN <= TMEM_COLS, "two rounds of NA buffers");
     static_assert(!(H16 && NIB), "nibble formats use 32-element groups");
     static_assert((BMW * NG * 4) % 128 == 0 && (GPS * BN * 4) % 128 == 0 &&
@@ -149,7 +156,11 @@ struct TcSmem {
     // -x_sums (-x_sums_16 for 16-element groups), permuted like xs
     alignas(128) float xn[C::MINS ? C::STAGES : 1][C::NG][C::BN];
     alignas(1024) uint8_t neg8[C::NEG8 ? C::SA : 1024];  // NEG8: a weight tile of -8
+    // K split: the other CTAs' accumulators, [CTA rank - 1][f32 pair][epilogue thread]
+    alignas(16) uint64_t xch[C::KSPLIT_MAX > 1 ? C::KSPLIT_MAX - 1 : 1]
+                            [C::KSPLIT_MAX > 1 ? C::EPI * 32 * 16 : 1];
     uint64_t full[C::STAGES], empty[C::STAGES], masked[C::STAGES], tfull[2], tempty[2], done;
+    uint64_t xfull;  // K split: the other CTAs' partial sums have landed in xch
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -313,6 +324,54 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
     return r;
 }
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// Distributed shared memory of a thread-block cluster: the address of this CTA's shared
+// location p in CTA `rank` of the cluster, a store there, and a release arrival (cluster
+// scope) on an mbarrier there; and a wait on a local mbarrier that acquires at cluster scope.
+__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_u64(uint32_t addr, uint64_t v) {
+    asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_cluster(uint64_t *b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded like mbar_wait_slow (about 2 s; false on expiry or when another role has aborted).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *b, uint32_t parity,
+                                                  volatile int *abort_flag, int *err) {
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t i = 1;; i++) {
+        if (mbar_try_cluster(b, parity)) return true;
+        if ((i & 255) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer() - t0 > WAIT_NS) {
+                *abort_flag = 1;
+                atomicOr(err, 1);
+                return false;
+            }
+        }
+    }
+}
 
 // NIB: converts stage s (K stage ks of its tile): the 4-bit codes in an[s] to int8 values in
 // a[s], in the layout the TMA's 128-byte swizzle gives (16-byte unit u of row r at
@@ -398,7 +457,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
                    const __grid_constant__ CUtensorMap tmWS, const __grid_constant__ CUtensorMap tmXS,
                    const __grid_constant__ CUtensorMap tmWM, const __grid_constant__ CUtensorMap tmXN,
                    int M, int G, int row_begin, int sub_n, int tiles_w, int tiles_t,
-                   float *__restrict__ out, int *err) {
+                   int ksplit, float *__restrict__ out, int *err) {
     constexpr int BN = C::BN, STAGES = C::STAGES, GPR = C::GPR, EPI = C::EPI, COLS = C::COLS;
     constexpr int NA = C::NA, SPL = C::SPL;
     extern __shared__ uint8_t smem_raw[];
@@ -408,6 +467,13 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
     const int kstages = G / GPS;
     const int ntiles = tiles_w * tiles_t;
     volatile int *abort_flag = &sm.abort_flag;
+    // K split: a cluster of nsplit CTAs shares each tile, CTA rank r (= blockIdx.x % nsplit,
+    // its rank in the one-dimensional cluster) taking K stages [k_begin, k_end); rank 0 adds
+    // the others' accumulators to its own in rank order and stores the tile.
+    const int nsplit = C::KSPLIT_MAX > 1 ? ksplit : 1;
+    const int krank = (int)blockIdx.x % nsplit;
+    const int tile0 = (int)blockIdx.x / nsplit, tstride = (int)gridDim.x / nsplit;
+    const int k_begin = kstages * krank / nsplit, k_end = kstages * (krank + 1) / nsplit;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; i++) {
@@ -421,6 +487,8 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
             mbar_init(&sm.tempty[i], EPI);
         }
         mbar_init(&sm.done, 1);
+        // one arrival per epilogue warp of every other CTA of the cluster
+        mbar_init(&sm.xfull, nsplit > 1 ? EPI * (nsplit - 1) : 1);
         sm.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -441,6 +509,9 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = sm.tmem_base;
+    if (nsplit > 1)  // every CTA of the cluster runs, barriers initialized, before any DSMEM access
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                         "memory");
 
     // epilogue geometry: TMEM lane quarter, token-column slice
     const int quarter = warp & 3, slice = (warp - 2) >> 2;
@@ -450,10 +521,10 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
         if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            for (int t = tile0; t < ntiles && ok; t += tstride) {
                 const int tt = t % tiles_t, tw = t / tiles_t;
                 const int wrow = row_begin + tw * BMW, tok = tt * BN;
-                for (int ks = 0; ks < kstages; ks++, it++) {
+                for (int ks = k_begin; ks < k_end; ks++, it++) {
                     const int s = it % STAGES;
                     if (!mbar_wait(&sm.empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, err)) {
                         ok = false;
@@ -500,8 +571,8 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
             const uint64_t nd = smem_desc(sm.neg8);
             uint32_t it = 0, rc = 0;  // stage and round counters
             bool ok = true;
-            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-                for (int ks = 0; ks < kstages && ok; ks++, it++) {
+            for (int t = tile0; t < ntiles && ok; t += tstride) {
+                for (int ks = k_begin; ks < k_end && ok; ks++, it++) {
                     const int s = it % STAGES;
                     if (!mbar_wait((C::H16 || C::NIB) ? &sm.masked[s] : &sm.full[s],
                                    (it / STAGES) & 1, abort_flag, err)) {
@@ -576,8 +647,8 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
         // position p of row r holds logical unit p ^ (r & 7).
         uint32_t it = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-            for (int ks = 0; ks < kstages; ks++, it++) {
+        for (int t = tile0; t < ntiles && ok; t += tstride) {
+            for (int ks = k_begin; ks < k_end; ks++, it++) {
                 const int s = it % STAGES;
                 if (!mbar_wait(&sm.full[s], (it / STAGES) & 1, abort_flag, err)) {
                     ok = false;
@@ -605,8 +676,8 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
         const int e = (warp - 2 - EPI) * 32 + lane;
         uint32_t it = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-            for (int ks = 0; ks < kstages; ks++, it++) {
+        for (int t = tile0; t < ntiles && ok; t += tstride) {
+            for (int ks = k_begin; ks < k_end; ks++, it++) {
                 const int s = it % STAGES;
                 if (!mbar_wait_sleepy(&sm.full[s], (it / STAGES) & 1, abort_flag, err)) {
                     ok = false;
@@ -627,8 +698,9 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
         // each token pair is one f32x2 operand.
         const int r0 = quarter * 32 + (lane >> 2), kq = lane & 3;
         uint32_t it = 0, rc = 0;
+        [[maybe_unused]] uint32_t xphase = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        for (int t = tile0; t < ntiles && ok; t += tstride) {
             const int tt = t % tiles_t, tw = t / tiles_t;
             // acc[cb][h][r][i]: column block cb (32 tokens), half h, repeat r, row R_{2h+i}
             uint64_t acc[COLS / 32][2][4][2];
@@ -638,7 +710,7 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
                 for (int h = 0; h < 2; h++)
 #pragma unroll
                     for (int r = 0; r < 4; r++) acc[cb][h][r][0] = acc[cb][h][r][1] = 0ull;
-            for (int ks = 0; ks < kstages && ok; ks++, it++) {
+            for (int ks = k_begin; ks < k_end && ok; ks++, it++) {
                 const int s = it % STAGES;
                 // NIB: the token scales come with the TMA (full), the weight scales from the
                 // converter warps (masked)
@@ -761,6 +833,43 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
                 if (lane == 0) mbar_arrive(&sm.empty[s]);
             }
             if (!ok) break;
+            if constexpr (C::KSPLIT_MAX > 1) {
+                if (nsplit > 1) {
+                    // K split: ranks 1.. store their accumulators into rank 0's exchange slots
+                    // (pair k of epilogue thread et at k * 32 * EPI + et) and arrive on its
+                    // barrier; rank 0 waits and adds them in rank order, then stores the tile.
+                    constexpr int ET = 32 * EPI;
+                    const int et = (warp - 2) * 32 + lane;
+                    if (krank > 0) {
+                        const uint32_t dst = cluster_addr(&sm.xch[krank - 1][et], 0);
+#pragma unroll
+                        for (int h = 0; h < 2; h++)
+#pragma unroll
+                            for (int r = 0; r < 4; r++)
+#pragma unroll
+                                for (int i = 0; i < 2; i++)
+                                    st_cluster_u64(dst + 8u * (uint32_t)(((h * 4 + r) * 2 + i) * ET),
+                                                   acc[0][h][r][i]);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive_cluster(cluster_addr(&sm.xfull, 0));
+                        continue;
+                    }
+                    if (!mbar_wait_cluster(&sm.xfull, xphase, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    xphase ^= 1u;
+                    for (int q = 0; q < nsplit - 1; q++)
+#pragma unroll
+                        for (int h = 0; h < 2; h++)
+#pragma unroll
+                            for (int r = 0; r < 4; r++)
+#pragma unroll
+                                for (int i = 0; i < 2; i++)
+                                    acc[0][h][r][i] = add2(
+                                        acc[0][h][r][i], sm.xch[q][((h * 4 + r) * 2 + i) * ET + et]);
+                }
+            }
             const int m0 = tt * BN + slice * COLS + 2 * kq;
 #pragma unroll
             for (int h = 0; h < 2; h++)
@@ -791,6 +900,16 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
 }
 
 // ---------------------------------------------------------------- host side
+
+// JKB_GEMM_KSPLIT=0 in the environment keeps every tile on one CTA (for measuring the K split
+// against it); unset, launches with few tiles split K.
+static bool k_split_allowed() {
+    static const bool on = [] {
+        const char *v = getenv("JKB_GEMM_KSPLIT");
+        return !(v && v[0] == '0' && v[1] == 0);
+    }();
+    return on;
+}
 
 // cuTensorMapEncodeTiled, resolved through the runtime's driver entry point so that the library
 // does not link the driver library (it still loads on machines without a GPU driver).
@@ -867,11 +986,40 @@ int launch_tc_common(const TcWeight &wt, const jkb_act_q8 *act, float *out, size
         if (e != cudaSuccess) return fail_cuda(e, "gemm_repacked (tensor-core kernel attribute)");
         attr_set[dev] = true;
     }
+    // K split: with few tiles, clusters of 2 or 4 CTAs share each tile (one tile a cluster, at
+    // least two K stages a CTA), so that more SMs stream weights and run epilogues.
+    int nsplit = 1;
+    if (C::KSPLIT_MAX > 1 && k_split_allowed()) {
+        for (int c = C::KSPLIT_MAX; c >= 2; c >>= 1)
+            if ((size_t)c * ntiles <= (size_t)num_sms() && G / GPS >= (size_t)(2 * c)) {
+                nsplit = c;
+                break;
+            }
+    }
+    if (nsplit > 1) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(nsplit * ntiles));
+        cfg.blockDim = dim3(C::THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)nsplit;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<C>, wt.tmW, tmX, wt.tmWS, tmXS, wt.tmWM, tmXN,
+                               (int)act->m, (int)G, (int)row_begin, (int)sub_n, tiles_w, tiles_t,
+                               nsplit, out, err);
+        if (e != cudaSuccess) return fail_cuda(e, "gemm_tc_kernel (K-split cluster launch)");
+        return check_launch("gemm_tc_kernel");
+    }
     const size_t slots = (size_t)num_sms() * C::CTAS;
     const size_t grid = ntiles < slots ? ntiles : slots;
     gemm_tc_kernel<C><<<(unsigned)grid, C::THREADS, smem, st>>>(
         wt.tmW, tmX, wt.tmWS, tmXS, wt.tmWM, tmXN, (int)act->m, (int)G, (int)row_begin,
-        (int)sub_n, tiles_w, tiles_t, out, err);
+        (int)sub_n, tiles_w, tiles_t, 1, out, err);
     return check_launch("gemm_tc_kernel");
 }
 
