@@ -646,7 +646,8 @@ int jkb_gemm_q4_k_ime(float *out, size_t out_len, const jkb_nibble_matrix *w,
 
 /* ---- multi-GPU output-row sharding: a one-kernel all-gather over NVLink (no reference
  * counterpart; the reference splits work by row ranges, gemv_repacked_rows repack.rs:4014) ----
- * One process per GPU. Every rank creates a peer group holding a device buffer of `bytes`, the
+ * One process per GPU. Every rank creates a peer group holding a device buffer of `bytes` (the
+ * same on every rank: it fixes the all-gather's grid, whose CTAs each signal every peer), the
  * ranks exchange the group handles (JKB_PEER_HANDLE_BYTES each, over any host channel) and
  * open them (CUDA IPC: each rank maps every peer's buffer). Each rank computes its output-row
  * shards into its own buffer at their global offsets (the buffer holds the full output
