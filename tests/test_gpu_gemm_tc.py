@@ -62,6 +62,9 @@ SHAPES = [
     (12, 16, 300, 4096),    # Q4_K_M, 16 tokens
     (14, 16, 300, 4096),    # Q6_K, 16 tokens
     (12, 16, 28672, 256),   # Q4_K_M, 16 tokens over 224 weight tiles (two waves)
+    (8, 16, 300, 4224),     # 3 tiles: K split over clusters of 4, 33 K stages split 8/8/8/9
+    (12, 20, 1000, 2304),   # Q4_K_M, 8 tiles: K split over clusters of 4, ragged tokens
+    (8, 32, 8192, 1024),    # 64 tiles: K split over clusters of 2
 ]
 
 
