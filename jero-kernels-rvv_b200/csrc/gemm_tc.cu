@@ -25,7 +25,9 @@
 //
 // Layout. The MMA's M side is 128 weight rows (TMEM lane = weight row), its N side BN tokens
 // (TMEM column = token); one persistent CTA per SM walks (weight tile, token tile) pairs, token
-// tiles fastest. Warp roles:
+// tiles fastest. The 32-token tile of small batches also runs at two CTAs per SM (more tiles
+// than SMs) or, in the FMA epilogue, with each tile's K stages split over a cluster of 2 or 4
+// CTAs (few tiles; see KSPLIT_MAX). Warp roles:
 //   warp 0     TMA producer: per stage 128 bytes of K (4 groups) of the weight tile and of the
 //              token tile (128-byte swizzle), the weight scales [128 rows][4 groups] and the
 //              token scales [4 groups][BN tokens] (from the transposed activation-scale plane);
