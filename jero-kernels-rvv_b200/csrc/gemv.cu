@@ -59,6 +59,7 @@ struct KArgs {
     int lpr_shift;  // log2(lanes per row)
     int ntok;       // M_TOK: tokens of the launch
     int tpc;        // M_TOK: tokens per CTA (1..TOK_MAX), each staged in its own smem slot
+    int stage16;    // ActI8: 16-byte staging copies when the activation is 16-byte aligned
     int32_t *dbg_sumi, *dbg_mins;
     float *dbg_val;
     // pushed outputs: every output element is also stored at these byte offsets from its
@@ -213,6 +214,16 @@ struct ActQ80 {
     }
 };
 
+// JKB_GEMV_STAGE16=0 in the environment stages 16-byte aligned i8 activations with 4-byte
+// copies too (for measuring the 16-byte copies against them); unset, 16-byte copies.
+static bool stage16_host() {
+    static const bool on = [] {
+        const char *v = getenv("JKB_GEMV_STAGE16");
+        return !(v && v[0] == '0' && v[1] == 0);
+    }();
+    return on;
+}
+
 // Plain i8 activations (BitLinear, ime.rs:882): blocks of the weight format's BE elements,
 // chunk j at 16*(j ^ swz(b)); integer total per block.
 template <int BE>
@@ -239,7 +250,18 @@ struct ActI8 {
             const int e = 4 * wi, b = e / BE, off = e - b * BE, j = off >> 4;
             return s + b * BE + 16 * (j ^ swz(b)) + (off & 15);
         };
-        if ((((uintptr_t)x) & 3) == 0) {
+        if ((((uintptr_t)x) & 15) == 0 && a.stage16) {
+            // 16-byte copies: a block's 16-byte chunk lands whole at its swizzled position, a
+            // quarter of the 4-byte copies' requests
+            for (int ci = threadIdx.x; ci < a.K / 16; ci += blockDim.x) {
+                const int e = 16 * ci, b = e / BE, j = (e - b * BE) >> 4;
+                const uint32_t sa =
+                    (uint32_t)__cvta_generic_to_shared(s + b * BE + 16 * (j ^ swz(b)));
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(x + e)
+                             : "memory");
+            }
+            asm volatile("cp.async.wait_all;" ::: "memory");
+        } else if ((((uintptr_t)x) & 3) == 0) {
             stage_words(x, a.K / 4, at);
         } else {
             for (int i = threadIdx.x; i < a.K / 4; i += blockDim.x)
@@ -1325,6 +1347,7 @@ int launch_gemv(const GemvLaunch &L, cudaStream_t st) {
     }
     a.qs_row = w->p.qs_row;
     a.sc_row = w->p.sc_row;
+    a.stage16 = stage16_host() ? 1 : 0;
     a.x = (const uint8_t *)L.x;
     a.x_row_stride = L.x_row_stride;
     a.act_scales = L.act_scales;
