@@ -489,8 +489,8 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
             mbar_init(&sm.tempty[i], EPI);
         }
         mbar_init(&sm.done, 1);
-        // one arrival per epilogue warp of every other CTA of the cluster
-        mbar_init(&sm.xfull, nsplit > 1 ? EPI * (nsplit - 1) : 1);
+        // one arrival per epilogue thread of every other CTA of the cluster
+        mbar_init(&sm.xfull, nsplit > 1 ? EPI * 32 * (nsplit - 1) : 1);
         sm.abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -838,8 +838,9 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
             if constexpr (C::KSPLIT_MAX > 1) {
                 if (nsplit > 1) {
                     // K split: ranks 1.. store their accumulators into rank 0's exchange slots
-                    // (pair k of epilogue thread et at k * 32 * EPI + et) and arrive on its
-                    // barrier; rank 0 waits and adds them in rank order, then stores the tile.
+                    // (pair k of epilogue thread et at k * 32 * EPI + et) and every thread
+                    // arrives on its barrier; rank 0 waits and adds them in rank order, then
+                    // stores the tile.
                     constexpr int ET = 32 * EPI;
                     const int et = (warp - 2) * 32 + lane;
                     if (krank > 0) {
@@ -852,8 +853,8 @@ __global__ void __launch_bounds__(C::THREADS, C::CTAS)
                                 for (int i = 0; i < 2; i++)
                                     st_cluster_u64(dst + 8u * (uint32_t)(((h * 4 + r) * 2 + i) * ET),
                                                    acc[0][h][r][i]);
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive_cluster(cluster_addr(&sm.xfull, 0));
+                        // each thread's release arrival orders its own stores before it
+                        mbar_arrive_cluster(cluster_addr(&sm.xfull, 0));
                         continue;
                     }
                     if (!mbar_wait_cluster(&sm.xfull, xphase, abort_flag, err)) {
