@@ -777,8 +777,9 @@ def decode_section(jkb, spec, world, rank, stream, steps, warmup, batch, peer, p
                         "lm_head": round(t["lm_head_ms"] * 1e3, 2),
                         "gather": round(t["gather_ms"] * 1e3, 2)},
            "launches_per_step": ds.launches_per_step,
-           "weights": ("i8 RepackedWeight, gemm_repacked (tensor cores); GB/s counts the GGUF "
-                       "bytes of the same matrices" if ds.tc else
+           "weights": ("i8 RepackedWeight, gemm_repacked (tensor cores, 32-token tile: two "
+                       "CTAs per SM with more tiles than SMs, K split over a cluster with few); "
+                       "GB/s counts the GGUF bytes of the same matrices" if ds.tc else
                        "GGUF blocks, " + ("gemv_batch" if batch > 1 else "f32-input GEMV"))}
     ds.destroy()
     return res
